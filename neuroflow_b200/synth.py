@@ -1,0 +1,137 @@
+"""Seeded synthetic inputs and random-init models with the shapes of the benchmark
+configurations (no dataset or checkpoint is available offline).
+
+* Gaussian random fields: periodic, spectrum ~ (|k|^2 + tau^2)^-2, unit std.
+* Weights: spectral U(-1, 1)/(in*out); Linear Kaiming-uniform as PyTorch's default
+  init (U(+-1/sqrt(fan_in)) for weight and bias).
+* Calibration: forward hooks on every Linear output of the float32 model, min/max over
+  a separate calibration batch, as the reference's `calibrate`
+  (neuroflow/quant/static_quant.py:609-741) does.  The float32 forward here follows
+  neuroflow/nn/fno2d.py:150-180 (torch.fft, exact GELU as torch's F.gelu).
+This module is a fixture producer for tests and bench.py, not part of the inference
+path.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from . import ir, quant
+
+
+def grf2d(rng: np.random.Generator, n: int, H: int, W: int, tau: float = 3.0) -> np.ndarray:
+    """(n, H, W) periodic GRF with spectrum (|k|^2 + tau^2)^-2, normalised to unit std."""
+    kh = np.fft.fftfreq(H, d=1.0 / H)[:, None]
+    kw = np.fft.rfftfreq(W, d=1.0 / W)[None, :]
+    amp = (kh ** 2 + kw ** 2 + tau ** 2) ** -1.0  # sqrt of the (.)^-2 power spectrum
+    out = np.empty((n, H, W), np.float32)
+    for i in range(n):
+        z = rng.standard_normal((H, W // 2 + 1)) + 1j * rng.standard_normal((H, W // 2 + 1))
+        f = np.fft.irfft2(z * amp, s=(H, W))
+        f = (f - f.mean()) / (f.std() + 1e-12)
+        out[i] = f.astype(np.float32)
+    return out
+
+
+def grf3d(rng: np.random.Generator, n: int, S: int, tau: float = 2.0) -> np.ndarray:
+    k0 = np.fft.fftfreq(S, d=1.0 / S)
+    kd = np.fft.rfftfreq(S, d=1.0 / S)
+    amp = (k0[:, None, None] ** 2 + k0[None, :, None] ** 2 + kd[None, None, :] ** 2
+           + tau ** 2) ** -1.0
+    out = np.empty((n, S, S, S), np.float32)
+    for i in range(n):
+        z = rng.standard_normal(amp.shape) + 1j * rng.standard_normal(amp.shape)
+        f = np.fft.irfftn(z * amp, s=(S, S, S))
+        f = (f - f.mean()) / (f.std() + 1e-12)
+        out[i] = f.astype(np.float32)
+    return out
+
+
+def fno2d_inputs(rng: np.random.Generator, n: int, H: int, W: int, in_ch: int = 3) -> np.ndarray:
+    """(n, H, W, in_ch): field + grid coordinates in [0, 1) (+ extra GRFs if in_ch > 3)."""
+    x = np.empty((n, H, W, in_ch), np.float32)
+    x[..., 0] = grf2d(rng, n, H, W)
+    if in_ch >= 2:
+        x[..., 1] = (np.arange(H, dtype=np.float32) / H)[None, :, None]
+    if in_ch >= 3:
+        x[..., 2] = (np.arange(W, dtype=np.float32) / W)[None, None, :]
+    for c in range(3, in_ch):
+        x[..., c] = grf2d(rng, n, H, W)
+    return x
+
+
+def _kaiming_linear(rng, out_f: int, in_f: int):
+    bound = 1.0 / math.sqrt(in_f)
+    w = rng.uniform(-bound, bound, size=(out_f, in_f)).astype(np.float32)
+    b = rng.uniform(-bound, bound, size=(out_f,)).astype(np.float32)
+    return w, b
+
+
+def fno2d_weights(rng, in_ch, out_ch, width, mh, mw, L):
+    wts = {}
+    wts["lift.weight"], wts["lift.bias"] = _kaiming_linear(rng, width, in_ch)
+    s = 1.0 / (width * width)
+    for i in range(L):
+        wts[f"specs.{i}.weights_real"] = (s * rng.uniform(-1, 1, (width, width, mh, mw))).astype(np.float32)
+        wts[f"specs.{i}.weights_imag"] = (s * rng.uniform(-1, 1, (width, width, mh, mw))).astype(np.float32)
+        wts[f"locs.{i}.weight"], wts[f"locs.{i}.bias"] = _kaiming_linear(rng, width, width)
+    wts["proj_q.weight"], wts["proj_q.bias"] = _kaiming_linear(rng, width, width)
+    wts["proj_out.weight"], wts["proj_out.bias"] = _kaiming_linear(rng, out_ch, width)
+    return wts
+
+
+def fno2d_linear_outputs(wts: dict, x: np.ndarray, L: int, mh: int, mw: int) -> dict:
+    """Float32 FNO2d forward (neuroflow/nn/fno2d.py:150-180) returning every Linear's
+    output, the statistics `calibrate` hooks."""
+    import torch
+    import torch.nn.functional as F
+
+    def lin(t, name):
+        return t @ torch.from_numpy(wts[name + ".weight"]).T + torch.from_numpy(wts[name + ".bias"])
+
+    obs = {}
+    with torch.no_grad():
+        h = lin(torch.from_numpy(x), "lift")
+        obs["lift.output"] = h.numpy().copy()
+        h = h.permute(0, 3, 1, 2)
+        Hh, Ww = h.shape[-2], h.shape[-1]
+        for i in range(L):
+            xf = torch.fft.rfftn(h, dim=(-2, -1))[..., :mh, :mw]
+            wgt = torch.complex(torch.from_numpy(wts[f"specs.{i}.weights_real"]),
+                                torch.from_numpy(wts[f"specs.{i}.weights_imag"]))
+            of = torch.einsum("bimn,iomn->bomn", xf, wgt)
+            of = F.pad(of, (0, (Ww // 2 + 1) - mw, 0, Hh - mh))
+            x1 = torch.fft.irfftn(of, s=(Hh, Ww), dim=(-2, -1))
+            x2 = lin(h.permute(0, 2, 3, 1), f"locs.{i}")
+            obs[f"locs.{i}.output"] = x2.numpy().copy()
+            h = F.gelu(x1 + x2.permute(0, 3, 1, 2))
+        q = lin(h.permute(0, 2, 3, 1), "proj_q")
+        obs["proj_q.output"] = q.numpy().copy()
+        y = lin(F.gelu(q), "proj_out")
+        obs["proj_out.output"] = y.numpy().copy()
+    return obs
+
+
+def fno2d_model(seed: int, in_ch=3, out_ch=1, width=64, mh=12, mw=12, L=4, H=128, W=128,
+                n_calib=32, per_channel=True, calib_chunk=8) -> ir.Model:
+    """A random-init FNO2d with a calibrated NIRQ block (per-channel weights,
+    per-tensor activations), ready for ir.write."""
+    rng = np.random.default_rng(seed)
+    wts = fno2d_weights(rng, in_ch, out_ch, width, mh, mw, L)
+    crng = np.random.default_rng(seed + 1)
+    mins, maxs = {}, {}
+    done = 0
+    while done < n_calib:
+        nb = min(calib_chunk, n_calib - done)
+        xc = fno2d_inputs(crng, nb, H, W, in_ch)
+        for k, v in fno2d_linear_outputs(wts, xc, L, mh, mw).items():
+            mins[k] = min(mins.get(k, np.inf), float(v.min()))
+            maxs[k] = max(maxs.get(k, -np.inf), float(v.max()))
+        done += nb
+    qp = quant.weight_qparams(wts, per_channel=per_channel)
+    for k in mins:
+        qp[k] = quant.tensor_qparams(np.array([mins[k], maxs[k]], np.float32))
+    cfg = dict(in_channels=in_ch, out_channels=out_ch, width=width, modes_h=mh, modes_w=mw,
+               n_layers=L, pad_factor=1)
+    return ir.Model(op="FNO2d", config=cfg, weights=wts, qparams=qp, quant_enabled=True)

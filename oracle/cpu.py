@@ -1,0 +1,360 @@
+"""ctypes front-end for the CPU parity checkers.
+
+TEST INFRASTRUCTURE ONLY.  `Oracle` wraps oracle/liboracle.so (the C restatement in
+nfo_oracle.c); `Reference` wraps oracle/_ref/libnflow_ref.so (the reference sources
+compiled by oracle/Makefile).  Only tests/, __graft_entry__.smoke() and bench.py's
+CPU legs use this module, as the checker or the timed CPU baseline.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libnflow_ref.so")
+MAX_LAYERS = 8
+
+_f32p = C.POINTER(C.c_float)
+_i32p = C.POINTER(C.c_int32)
+_i8p = C.POINTER(C.c_int8)
+_i64p = C.POINTER(C.c_int64)
+
+
+def _p(a, t=_f32p):
+    return None if a is None else a.ctypes.data_as(t)
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+class _WQ(C.Structure):
+    _fields_ = [("pc_scales", _f32p), ("pc_zps", _i32p), ("pc_n", C.c_int64),
+                ("pc_axis", C.c_int32), ("has_pc", C.c_int32), ("pt_scale", C.c_float),
+                ("pt_zp", C.c_int32), ("has_pt", C.c_int32)]
+
+
+class _AQ(C.Structure):
+    _fields_ = [("scale", C.c_float), ("zp", C.c_int32), ("has", C.c_int32),
+                ("fp8_scale", C.c_float), ("has_fp8", C.c_int32)]
+
+
+class _FNO2d(C.Structure):
+    _fields_ = ([(n, C.c_int32) for n in ("in_ch", "out_ch", "width", "modes_h", "modes_w",
+                                          "n_layers", "pad_factor", "relu", "quant_enabled")]
+                + [(n, _f32p) for n in ("lift_w", "lift_b", "proj_q_w", "proj_q_b",
+                                        "proj_out_w", "proj_out_b")]
+                + [(n, _f32p * MAX_LAYERS) for n in ("spec_wr", "spec_wi", "loc_w", "loc_b")]
+                + [(n, _WQ) for n in ("q_lift_w", "q_lift_b", "q_proj_q_w", "q_proj_q_b",
+                                      "q_proj_out_w", "q_proj_out_b")]
+                + [(n, _WQ * MAX_LAYERS) for n in ("q_spec_wr", "q_spec_wi", "q_loc_w",
+                                                   "q_loc_b")]
+                + [(n, _AQ) for n in ("a_lift", "a_proj_q", "a_proj_out")]
+                + [("a_locs", _AQ * MAX_LAYERS)])
+
+
+class _Taps(C.Structure):
+    _fields_ = [("codes_in", _i8p * (MAX_LAYERS + 1)), ("x1_out", _f32p * MAX_LAYERS),
+                ("h_out", _f32p * MAX_LAYERS)]
+
+
+class Oracle:
+    """The C restatement (nfo_oracle.c)."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle`")
+        self.lib = C.CDLL(path)
+        L = self.lib
+        L.nfo_fno2d_forward.restype = C.c_int
+        L.nfo_fno2d_forward.argtypes = [C.POINTER(_FNO2d), C.c_int, _f32p, C.c_int, C.c_int,
+                                        C.c_int, _f32p, C.POINTER(_Taps)]
+
+    # -- primitives ---------------------------------------------------------
+    def quantise_activation(self, A, scale, zp):
+        A = _c(A, np.float32)
+        out = np.empty(A.shape, np.int8)
+        self.lib.nfo_quantise_activation(_p(A), _p(out, _i8p), C.c_int64(A.size),
+                                         C.c_float(scale), C.c_int32(zp))
+        return out
+
+    def fake_quant(self, x, scale, zp):
+        x = _c(x, np.float32).copy()
+        self.lib.nfo_fake_quant(_p(x), C.c_int64(x.size), C.c_float(scale), C.c_int32(zp))
+        return x
+
+    def quantise_weight_2d(self, W, scales, zps):
+        W = _c(W, np.float32)
+        n, k = W.shape
+        q = np.empty((n, k), np.int8)
+        s = np.empty(n, np.int32)
+        self.lib.nfo_quantise_weight_2d(_p(W), n, k, _p(_c(scales, np.float32)),
+                                        _p(_c(zps, np.int32), _i32p), _p(q, _i8p), _p(s, _i32p))
+        return q, s
+
+    def linear_forward_batched(self, Wq, sW, zpW, sumW, bias, sA, zpA, A):
+        A = _c(A, np.float32)
+        M, K = A.shape
+        N = Wq.shape[0]
+        out = np.empty((M, N), np.float32)
+        acc = np.empty((M, N), np.int32)
+        codes = np.empty((M, K), np.int8)
+        bias_c = None if bias is None else _c(bias, np.float32)
+        self.lib.nfo_linear_forward_batched(
+            _p(_c(Wq, np.int8), _i8p), _p(_c(sW, np.float32)), _p(_c(zpW, np.int32), _i32p),
+            _p(_c(sumW, np.int32), _i32p), _p(bias_c), K, N, C.c_float(sA), C.c_int32(zpA),
+            M, _p(A), _p(out), _p(acc, _i32p), _p(codes, _i8p))
+        return out, acc, codes
+
+    def int8_gemm_rows(self, Aq, sA, zpA, Wq, sW, zpW, sumW, bias, gelu):
+        Aq = _c(Aq, np.int8)
+        M, K = Aq.shape
+        N = Wq.shape[0]
+        out = np.empty((M, N), np.float32)
+        acc = np.empty((M, N), np.int32)
+        bias_c = None if bias is None else _c(bias, np.float32)
+        self.lib.nfo_int8_gemm_rows(
+            _p(Aq, _i8p), _p(_c(sA, np.float32)), _p(_c(zpA, np.int32), _i32p), M, K,
+            _p(_c(Wq, np.int8), _i8p), _p(_c(sW, np.float32)), _p(_c(zpW, np.int32), _i32p),
+            _p(_c(sumW, np.int32), _i32p), N, _p(bias_c), int(bool(gelu)), _p(out),
+            _p(acc, _i32p))
+        return out, acc
+
+    def linear(self, x, W, b):
+        x = _c(x, np.float32)
+        M, K = x.shape
+        N = W.shape[0]
+        y = np.empty((M, N), np.float32)
+        self.lib.nfo_linear(_p(x), _p(_c(W, np.float32)),
+                            None if b is None else _p(_c(b, np.float32)), M, K, N, _p(y))
+        return y
+
+    def activation(self, x, relu=False):
+        x = _c(x, np.float32).copy()
+        self.lib.nfo_apply_activation(_p(x), C.c_int64(x.size), int(relu))
+        return x
+
+    def rfft2(self, x):
+        x = _c(x, np.float32)
+        H, W = x.shape
+        out = np.empty((H, W // 2 + 1, 2), np.float32)
+        self.lib.nfo_rfft2(_p(x), H, W, _p(out))
+        return out
+
+    def irfft2(self, xc, H, W):
+        xc = _c(xc, np.float32)
+        out = np.empty((H, W), np.float32)
+        self.lib.nfo_irfft2(_p(xc), H, W, _p(out))
+        return out
+
+    def rfft(self, x):
+        x = _c(x, np.float32)
+        out = np.empty((x.size // 2 + 1, 2), np.float32)
+        self.lib.nfo_rfft(_p(x), x.size, _p(out))
+        return out
+
+    def irfft(self, xc, n):
+        out = np.empty(n, np.float32)
+        self.lib.nfo_irfft(_p(_c(xc, np.float32)), n, _p(out))
+        return out
+
+    def spectral_conv2d(self, h, wr, wi):
+        h = _c(h, np.float32)
+        b, w, H, W = h.shape
+        mh, mw = wr.shape[2], wr.shape[3]
+        out = np.empty_like(h)
+        self.lib.nfo_spectral_conv2d(_p(h), b, w, H, W, mh, mw, _p(_c(wr, np.float32)),
+                                     _p(_c(wi, np.float32)), _p(out))
+        return out
+
+    # -- FNO2d -----------------------------------------------------------------
+    def fno2d_forward(self, model, x, mode: int, taps: bool = False):
+        """mode 0: reference fake-quant FNO2d; mode 1: INT8 composition.
+        Returns y, or (y, taps_dict) when taps=True."""
+        x = _c(x, np.float32)
+        B, H, W, _ = x.shape
+        st, keep = build_fno2d_struct(model)
+        cfg = model.config
+        y = np.empty((B, H, W, cfg["out_channels"]), np.float32)
+        tp = None
+        tap_arrays = {}
+        if taps:
+            tp = _Taps()
+            L, w = cfg["n_layers"], cfg["width"]
+            for i in range(L + 1):
+                a = np.zeros((B, H, W, w), np.int8)
+                tap_arrays[f"codes_in.{i}"] = a
+                tp.codes_in[i] = _p(a, _i8p)
+            for i in range(L):
+                a = np.zeros((B, w, H, W), np.float32)
+                tap_arrays[f"x1.{i}"] = a
+                tp.x1_out[i] = _p(a)
+                a = np.zeros((B, H, W, w), np.float32)
+                tap_arrays[f"h.{i}"] = a
+                tp.h_out[i] = _p(a)
+        rc = self.lib.nfo_fno2d_forward(C.byref(st), int(mode), _p(x), B, H, W, _p(y),
+                                        C.byref(tp) if tp is not None else None)
+        if rc != 0:
+            raise RuntimeError(f"nfo_fno2d_forward failed: {rc}")
+        del keep
+        return (y, tap_arrays) if taps else y
+
+
+def _wq(qp, keep):
+    from neuroflow_b200 import ir
+    s = _WQ()
+    if isinstance(qp, ir.PerChannel):
+        sc = _c(qp.scales, np.float32)
+        zp = _c(qp.zero_points, np.int32)
+        keep += [sc, zp]
+        s.pc_scales, s.pc_zps, s.pc_n = _p(sc), _p(zp, _i32p), sc.size
+        s.pc_axis, s.has_pc = int(qp.channel_axis), 1
+    elif isinstance(qp, ir.PerTensor):
+        s.pt_scale, s.pt_zp, s.has_pt = float(qp.scale), int(qp.zero_point), 1
+    return s
+
+
+def _aq(model, key):
+    from neuroflow_b200 import ir
+    a = _AQ()
+    qp = model.qparams.get(key)
+    if isinstance(qp, ir.PerTensor):
+        a.scale, a.zp, a.has = float(qp.scale), int(qp.zero_point), 1
+    elif isinstance(qp, ir.FP8):
+        a.fp8_scale, a.has_fp8 = float(qp.scale), 1
+    return a
+
+
+def build_fno2d_struct(model):
+    """Fill the C model struct from an ir.Model (FNO2d)."""
+    cfg, w = model.config, model.weights
+    keep = []
+    st = _FNO2d()
+    st.in_ch, st.out_ch, st.width = cfg["in_channels"], cfg["out_channels"], cfg["width"]
+    st.modes_h, st.modes_w, st.n_layers = cfg["modes_h"], cfg["modes_w"], cfg["n_layers"]
+    st.pad_factor = cfg.get("pad_factor", 1)
+    st.relu = 1 if model.activation == "relu" else 0
+    st.quant_enabled = 1 if model.quant_enabled else 0
+
+    def arr(name):
+        a = _c(w[name], np.float32)
+        keep.append(a)
+        return _p(a)
+
+    for fld, nm in (("lift_w", "lift.weight"), ("lift_b", "lift.bias"),
+                    ("proj_q_w", "proj_q.weight"), ("proj_q_b", "proj_q.bias"),
+                    ("proj_out_w", "proj_out.weight"), ("proj_out_b", "proj_out.bias")):
+        setattr(st, fld, arr(nm))
+        setattr(st, "q_" + fld, _wq(model.qparams.get(nm), keep))
+    for i in range(cfg["n_layers"]):
+        for fld, nm in (("spec_wr", f"specs.{i}.weights_real"), ("spec_wi", f"specs.{i}.weights_imag"),
+                        ("loc_w", f"locs.{i}.weight"), ("loc_b", f"locs.{i}.bias")):
+            getattr(st, fld)[i] = arr(nm)
+            getattr(st, "q_" + fld)[i] = _wq(model.qparams.get(nm), keep)
+        st.a_locs[i] = _aq(model, f"locs.{i}.output")
+    st.a_lift = _aq(model, "lift.output")
+    st.a_proj_q = _aq(model, "proj_q.output")
+    st.a_proj_out = _aq(model, "proj_out.output")
+    return st, keep
+
+
+class Reference:
+    """The reference runtime compiled from its sources (oracle/_ref)."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle ref`")
+        self.lib = C.CDLL(path)
+        self.lib.ref_last_error.restype = C.c_char_p
+        self.lib.ref_bench_run.restype = C.c_double
+
+    def run(self, path, x, out_ch, enable_int8=False, tokenmixer2d=False):
+        x = _c(x, np.float32)
+        h = C.c_void_p()
+        rc = self.lib.ref_runtime_create(path.encode(), C.byref(h))
+        if rc != 0:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        try:
+            if enable_int8:
+                self.lib.ref_runtime_enable_int8(h)
+            ys = list(x.shape[:-1]) + [out_ch]
+            y = np.zeros(ys, np.float32)
+            xs = (C.c_int64 * x.ndim)(*x.shape)
+            yv = (C.c_int64 * y.ndim)(*y.shape)
+            fn = self.lib.ref_runtime_run_tokenmixer2d if tokenmixer2d else self.lib.ref_runtime_run
+            rc = fn(h, _p(x), xs, x.ndim, _p(y), yv, y.ndim)
+            if rc != 0:
+                raise RuntimeError(self.lib.ref_last_error().decode())
+            return y
+        finally:
+            self.lib.ref_runtime_destroy(h)
+
+    def bench(self, path, x, out_ch, nthreads, reps=1, enable_int8=False, tokenmixer2d=False):
+        """Wall seconds for `reps` passes over x split across `nthreads` runtimes."""
+        x = _c(x, np.float32)
+        xs = (C.c_int64 * x.ndim)(*x.shape)
+        ys = (C.c_int64 * x.ndim)(*(list(x.shape[:-1]) + [out_ch]))
+        t = self.lib.ref_bench_run(path.encode(), int(tokenmixer2d), int(enable_int8), _p(x),
+                                   xs, x.ndim, ys, int(nthreads), int(reps))
+        if t < 0:
+            raise RuntimeError(f"ref_bench_run failed ({t})")
+        return t
+
+    def linear(self, x, W, b):
+        x = _c(x, np.float32)
+        M, K = x.shape
+        N = W.shape[0]
+        y = np.empty((M, N), np.float32)
+        self.lib.ref_linear(_p(x), _p(_c(W, np.float32)),
+                            None if b is None else _p(_c(b, np.float32)), M, K, N, _p(y))
+        return y
+
+    def activation(self, x, relu=False):
+        x = _c(x, np.float32).copy()
+        self.lib.ref_apply_activation(_p(x), C.c_int64(x.size), int(relu))
+        return x
+
+    def rfft2(self, x):
+        x = _c(x, np.float32)
+        H, W = x.shape
+        out = np.empty((H, W // 2 + 1, 2), np.float32)
+        self.lib.ref_rfft2(_p(x), H, W, _p(out))
+        return out
+
+    def irfft2(self, xc, H, W):
+        out = np.empty((H, W), np.float32)
+        self.lib.ref_irfft2(_p(_c(xc, np.float32)), H, W, _p(out))
+        return out
+
+    def spectral_conv2d(self, h, wr, wi):
+        h = _c(h, np.float32)
+        b, w, H, W = h.shape
+        out = np.empty_like(h)
+        self.lib.ref_spectral_conv2d(_p(h), b, w, H, W, wr.shape[2], wr.shape[3],
+                                     _p(_c(wr, np.float32)), _p(_c(wi, np.float32)), _p(out))
+        return out
+
+    def quantise_activation(self, A, scale, zp):
+        A = _c(A, np.float32)
+        M, K = A.reshape(-1, A.shape[-1]).shape
+        out = np.empty(A.shape, np.int8)
+        self.lib.ref_quantise_activation(_p(A), _p(out, _i8p), M, K, C.c_float(scale),
+                                         C.c_int32(zp))
+        return out
+
+    def linear_forward_batched(self, Wq, sW, zpW, sumW, bias, sA, zpA, A):
+        A = _c(A, np.float32)
+        M, K = A.shape
+        N = Wq.shape[0]
+        out = np.empty((M, N), np.float32)
+        bias_c = None if bias is None else _c(bias, np.float32)
+        rc = self.lib.ref_linear_forward_batched(
+            _p(_c(Wq, np.int8), _i8p), _p(_c(sW, np.float32)), _p(_c(zpW, np.int32), _i32p),
+            _p(_c(sumW, np.int32), _i32p), _p(bias_c), K, N, C.c_float(sA), C.c_int32(zpA),
+            M, _p(A), _p(out))
+        if rc != 0:
+            raise RuntimeError("ref_linear_forward_batched failed")
+        return out

@@ -1,0 +1,828 @@
+/*
+ * nfo_oracle.c -- CPU restatement of the NeuroFlow reference arithmetic for the
+ * quantized neural-operator inference path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity checker for the CUDA path in
+ * neuroflow_b200/csrc.  Only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline leg may load it.  It is never linked into the product library.
+ *
+ * Every function below restates one piece of the reference C++ runtime
+ * (cpp/src/*.cpp of AITree69/neuroflow) and names the file:line it follows.  The
+ * expression shapes are kept identical to the reference so that, compiled with the
+ * same compiler and the same flags as the reference build (-O3 -mavx2 -mfma, GCC's
+ * default floating-point contraction), the results are bit-identical.  That claim is
+ * checked by tests/test_oracle_pin.py against the reference sources compiled from
+ * their original location (oracle/Makefile, target `ref`).
+ *
+ * Two FNO2d modes exist:
+ *   mode 0  "fake-quant fp32": the reference FNO2d::Forward (cpp/src/fno.cpp:777-995)
+ *           with the runtime's load-time weight fake-quant (cpp/src/fno.cpp:217-290).
+ *           Pinned bit-exact against the reference runtime.
+ *   mode 1  "int8": the reference has no INT8 GEMM for FNO2d.  This mode applies the
+ *           reference FNO1d INT8 convention (cpp/src/fno.cpp:125-159, :360-406,
+ *           :475-549) to FNO2d's layer structure: the layer input is snapped with the
+ *           previous layer's ".output" qparams, the 1x1 layers (locs.i, proj_q) run
+ *           through LinearForwardBatched (cpp/src/int8_gemm.cpp:530-580) with the
+ *           per-channel weight codes of QuantiseWeight2D (cpp/src/fno.cpp:325-358),
+ *           and the FNO2d output fake-quant boundaries are kept.  Each piece is pinned
+ *           separately; the composition has no reference counterpart.
+ */
+#include <complex.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifndef M_PI
+#define M_PI 3.14159265358979323846
+#endif
+
+#define NFO_MAX_LAYERS 8
+
+/* ------------------------------------------------------------------------- */
+/* Quantisation primitives                                                    */
+/* ------------------------------------------------------------------------- */
+
+/* int8_gemm.cpp:507-520 QuantiseActivation: q = (int)round(v/s) + zp, clamp. */
+void nfo_quantise_activation(const float* A, int8_t* A_q, int64_t n, float scale_A,
+                             int32_t zp_A) {
+    for (int64_t i = 0; i < n; ++i) {
+        int32_t q = (int32_t)(roundf(A[i] / scale_A)) + zp_A;
+        if (q < -128) q = -128;
+        if (q > 127) q = 127;
+        A_q[i] = (int8_t)q;
+    }
+}
+
+/* fno.cpp:830-842 (and :497-505, :629-640): float fake-quant round trip. */
+void nfo_fake_quant(float* data, int64_t numel, float scale, int32_t zero_point) {
+    const float zp = (float)zero_point;
+    for (int64_t k = 0; k < numel; ++k) {
+        float v = data[k];
+        float q = roundf(v / scale) + zp;
+        if (q < -128.0f) q = -128.0f;
+        if (q > 127.0f) q = 127.0f;
+        data[k] = (q - zp) * scale;
+    }
+}
+
+/* fno.cpp:813-828 FNO2d FP8 branch of apply_fake_quant: a log2 snap.  The exponent
+ * passed to std::ldexp is a float converted to int (truncation toward zero), which
+ * is what the reference computes. */
+void nfo_fake_quant_fp8_log2(float* data, int64_t numel, float scale) {
+    if (!(scale > 0.0f)) return;
+    for (int64_t k = 0; k < numel; ++k) {
+        const float v = data[k] / scale;
+        const float abs_v = fabsf(v);
+        const float sign = v < 0.0f ? -1.0f : 1.0f;
+        const float quant_v = (abs_v < 0.015625f)
+            ? abs_v
+            : ldexpf(1.0f, (int)(roundf(log2f(abs_v) * 8.0f) / 8.0f));
+        const float clamped = fminf(quant_v, 448.0f);
+        data[k] = sign * clamped * scale;
+    }
+}
+
+/* fno.cpp:236-241 fake_quant_pt (per element, zp given as float). */
+static inline float fake_quant_pt(float v, float s, float zp) {
+    float q = roundf(v / s) + zp;
+    if (q < -128.0f) q = -128.0f;
+    if (q > 127.0f) q = 127.0f;
+    return (q - zp) * s;
+}
+
+/* fno.cpp:217-290 DequantiseWeight.  Per-channel qparams are applied for 2-D tensors
+ * with axis 0 and 3-D tensors with axis 1; any other layout falls through to the
+ * per-tensor qparams when those exist.  Returns 1 if the tensor was modified. */
+int nfo_dequantise_weight(float* t, const int64_t* shape, int ndim,
+                          const float* pc_scales, const int32_t* pc_zps, int64_t pc_n,
+                          int pc_axis, int has_pc, float pt_scale, int32_t pt_zp,
+                          int has_pt) {
+    if (has_pc) {
+        if (ndim == 2 && pc_axis == 0) {
+            for (int64_t c = 0; c < pc_n; ++c) {
+                const float s = pc_scales[c];
+                const float zp = (float)pc_zps[c];
+                for (int64_t i = 0; i < shape[1]; ++i) {
+                    const int64_t off = c * shape[1] + i;
+                    t[off] = fake_quant_pt(t[off], s, zp);
+                }
+            }
+            return 1;
+        } else if (ndim == 3 && pc_axis == 1) {
+            const int64_t in_dim = shape[0], out_dim = shape[1], modes_dim = shape[2];
+            for (int64_t i = 0; i < in_dim; ++i)
+                for (int64_t c = 0; c < out_dim; ++c) {
+                    const float s = pc_scales[c];
+                    const float zp = (float)pc_zps[c];
+                    for (int64_t k = 0; k < modes_dim; ++k) {
+                        const int64_t off = i * (out_dim * modes_dim) + c * modes_dim + k;
+                        t[off] = fake_quant_pt(t[off], s, zp);
+                    }
+                }
+            return 1;
+        }
+    }
+    if (has_pt) {
+        const float s = pt_scale;
+        const float zp = (float)pt_zp;
+        int64_t numel = 1;
+        for (int d = 0; d < ndim; ++d) numel *= shape[d];
+        for (int64_t i = 0; i < numel; ++i) t[i] = fake_quant_pt(t[i], s, zp);
+        return 1;
+    }
+    return 0;
+}
+
+/* fno.cpp:325-358 QuantiseWeight2D: per-output-row codes and the cached
+ * sum_W_per_row[o] = sum_i (W_q[o,i] - zp[o]). */
+void nfo_quantise_weight_2d(const float* W, int n_out, int k, const float* scales,
+                            const int32_t* zps, int8_t* W_q, int32_t* sum_w) {
+    for (int64_t c = 0; c < n_out; ++c) {
+        const float s = scales[c];
+        const float zp = (float)zps[c];
+        int32_t row_sum = 0;
+        for (int64_t i = 0; i < k; ++i) {
+            const int64_t off = c * k + i;
+            float q = roundf(W[off] / s) + zp;
+            if (q < -128.0f) q = -128.0f;
+            if (q > 127.0f) q = 127.0f;
+            const int8_t q8 = (int8_t)q;
+            W_q[off] = q8;
+            row_sum += (int32_t)q8 - zps[c];
+        }
+        sum_w[c] = row_sum;
+    }
+}
+
+/* int8_gemm.cpp:479-496 PrecomputeSumW. */
+void nfo_precompute_sum_w(const int8_t* W_q, const int32_t* zp_w, int in_f, int out_f,
+                          int32_t* out) {
+    for (int o = 0; o < out_f; ++o) {
+        int32_t acc = 0;
+        const int8_t* w_row = W_q + (int64_t)o * in_f;
+        for (int i = 0; i < in_f; ++i) acc += (int32_t)w_row[i] - zp_w[o];
+        out[o] = acc;
+    }
+}
+
+/* int8_gemm.cpp:530-580 LinearForwardBatched: bulk quantise, per-row Sum a, scalar
+ * int32 GEMM with acc = sum a*(w - zp_w), and the reference epilogue
+ *   y = sW*sA*float(acc - zp_w*sum_a - zp_A*sum_w + (int64)K*zp_w*zp_A)
+ * followed by y + (bias or 0).  The optional acc_out / codes_out taps expose the
+ * int32 accumulator and the int8 activation codes for bit-exact checks. */
+void nfo_linear_forward_batched(const int8_t* W_q, const float* scale_W,
+                                const int32_t* zp_W, const int32_t* sum_W,
+                                const float* bias, int in_f, int out_f, float scale_A,
+                                int32_t zp_A, int bsz, const float* A, float* C,
+                                int32_t* acc_out, int8_t* codes_out) {
+    if (bsz <= 0) return;
+    int8_t* A_q = codes_out ? codes_out : (int8_t*)malloc((size_t)bsz * in_f);
+    nfo_quantise_activation(A, A_q, (int64_t)bsz * in_f, scale_A, zp_A);
+    for (int r = 0; r < bsz; ++r) {
+        const int8_t* a_row = A_q + (int64_t)r * in_f;
+        int32_t sum_a = 0;
+        for (int i = 0; i < in_f; ++i) sum_a += a_row[i];
+        float* c_row = C + (int64_t)r * out_f;
+        for (int o = 0; o < out_f; ++o) {
+            const int8_t* w_row = W_q + (int64_t)o * in_f;
+            const int32_t zp_w_o = zp_W[o];
+            int32_t acc = 0;
+            for (int i = 0; i < in_f; ++i)
+                acc += (int32_t)a_row[i] * ((int32_t)w_row[i] - zp_w_o);
+            if (acc_out) acc_out[(int64_t)r * out_f + o] = acc;
+            const int32_t sum_w = sum_W ? sum_W[o] : 0;
+            const float y = scale_W[o] * scale_A *
+                (float)(acc - zp_w_o * sum_a - zp_A * sum_w + (int64_t)in_f * zp_w_o * zp_A);
+            c_row[o] = y + (bias ? bias[o] : 0.0f);
+        }
+    }
+    if (!codes_out) free(A_q);
+}
+
+/* fno.cpp:36-48 ApplyActivation: GELU (tanh approximation) or ReLU. */
+void nfo_apply_activation(float* data, int64_t n, int relu) {
+    if (relu) {
+        for (int64_t i = 0; i < n; ++i)
+            if (data[i] < 0.0f) data[i] = 0.0f;
+    } else {
+        const float c = sqrtf(2.0f / (float)M_PI);
+        for (int64_t i = 0; i < n; ++i) {
+            float z = data[i];
+            data[i] = 0.5f * z * (1.0f + tanhf(c * (z + 0.044715f * z * z * z)));
+        }
+    }
+}
+
+/* Per-token INT8 GEMM used by the standalone GEMM sweep: activation codes with one
+ * (scale, zero point) per row, per-channel weight codes, and the reference epilogue
+ * of int8_gemm.cpp:574-577 evaluated with the row's own (scale_A, zp_A); then
+ * bias (fno.cpp:541-548 adds it as a separate float add) and optional GELU
+ * (fno.cpp:36-48).  The per-row form has no reference entry point; its arithmetic is
+ * the reference formula with scale_A/zp_A indexed by row. */
+void nfo_int8_gemm_rows(const int8_t* A_q, const float* scale_A, const int32_t* zp_A,
+                        int M, int K, const int8_t* W_q, const float* scale_W,
+                        const int32_t* zp_W, const int32_t* sum_W, int N,
+                        const float* bias, int gelu, float* C, int32_t* acc_out) {
+    const float c = sqrtf(2.0f / (float)M_PI);
+    for (int64_t r = 0; r < M; ++r) {
+        const int8_t* a_row = A_q + r * K;
+        int32_t sum_a = 0;
+        for (int i = 0; i < K; ++i) sum_a += a_row[i];
+        const float sA = scale_A[r];
+        const int32_t zA = zp_A[r];
+        for (int o = 0; o < N; ++o) {
+            const int8_t* w_row = W_q + (int64_t)o * K;
+            const int32_t zp_w_o = zp_W[o];
+            int32_t acc = 0;
+            for (int i = 0; i < K; ++i) acc += (int32_t)a_row[i] * ((int32_t)w_row[i] - zp_w_o);
+            if (acc_out) acc_out[r * N + o] = acc;
+            const float y = scale_W[o] * sA *
+                (float)(acc - zp_w_o * sum_a - zA * sum_W[o] + (int64_t)K * zp_w_o * zA);
+            float out = y + 0.0f;
+            if (bias) out = out + bias[o];
+            if (gelu) {
+                float z = out;
+                out = 0.5f * z * (1.0f + tanhf(c * (z + 0.044715f * z * z * z)));
+            }
+            C[r * N + o] = out;
+        }
+    }
+}
+
+/* fno.cpp:51-80 Linear, the hand-rolled loop (the reference is built without Eigen). */
+void nfo_linear(const float* x, const float* W, const float* b, int bsz, int k, int n,
+                float* y) {
+    for (int i = 0; i < bsz; ++i) {
+        const float* xi = x + (int64_t)i * k;
+        float* yi = y + (int64_t)i * n;
+        for (int j = 0; j < n; ++j) {
+            float acc = b ? b[j] : 0.0f;
+            const float* wj = W + (int64_t)j * k;
+            for (int p = 0; p < k; ++p) acc += xi[p] * wj[p];
+            yi[j] = acc;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------- */
+/* FFT: radix-2 Cooley-Tukey with the twiddle recurrence w *= wlen             */
+/* ------------------------------------------------------------------------- */
+
+/* fft.cpp:36-46 bit reversal. */
+static void bit_reverse(float complex* a, int n) {
+    int j = 0;
+    for (int i = 1; i < n; ++i) {
+        int bit = n >> 1;
+        for (; j & bit; bit >>= 1) j ^= bit;
+        j ^= bit;
+        if (i < j) {
+            float complex t = a[i];
+            a[i] = a[j];
+            a[j] = t;
+        }
+    }
+}
+
+/* Complex products as the reference build evaluates them.  With -O3 -mavx2 -mfma
+ * (with or without the -mavx512* flags) GCC emits two code paths for
+ * ComplexFftInPlace (fft.cpp:49-69):
+ *   forward butterfly  v = a*w : packed multiplies + addsub, no fusion
+ *                                re = ar*wr - ai*wi,  im = ai*wr + ar*wi
+ *   inverse butterfly  v = a*w : re = fma(ar, wr, -(ai*wi)),  im = fma(ar, wi, ai*wr)
+ *   twiddle update  w *= wlen  : same fused form as the inverse butterfly.
+ * The helpers below spell those forms out so that the restatement does not depend
+ * on the C compiler's own contraction choices. */
+__attribute__((optimize("fp-contract=off")))
+static float complex cmul_plain(float complex a, float complex b) {
+    const float ar = crealf(a), ai = cimagf(a), br = crealf(b), bi = cimagf(b);
+    const float p0 = ar * br, p1 = ai * bi, p2 = ai * br, p3 = ar * bi;
+    return CMPLXF(p0 - p1, p2 + p3);
+}
+
+__attribute__((optimize("fp-contract=off")))
+static float complex cmul_fused(float complex a, float complex b) {
+    const float ar = crealf(a), ai = cimagf(a), br = crealf(b), bi = cimagf(b);
+    const float p1 = ai * bi, p2 = ai * br;
+    return CMPLXF(fmaf(ar, br, -p1), fmaf(ar, bi, p2));
+}
+
+/* fft.cpp:49-69 in-place complex FFT; the inverse scales by 1/n. */
+static void complex_fft(float complex* a, int n, int inverse) {
+    bit_reverse(a, n);
+    for (int len = 2; len <= n; len <<= 1) {
+        const float ang = (inverse ? 2.0f : -2.0f) * (float)M_PI / (float)len;
+        const float complex wlen = CMPLXF(cosf(ang), sinf(ang));
+        for (int i = 0; i < n; i += len) {
+            float complex w = CMPLXF(1.0f, 0.0f);
+            for (int k = 0; k < len / 2; ++k) {
+                float complex u = a[i + k];
+                float complex v = inverse ? cmul_fused(a[i + k + len / 2], w)
+                                          : cmul_plain(a[i + k + len / 2], w);
+                a[i + k] = u + v;
+                a[i + k + len / 2] = u - v;
+                w = cmul_fused(w, wlen);
+            }
+        }
+    }
+    if (inverse) {
+        const float inv = 1.0f / (float)n;
+        for (int i = 0; i < n; ++i) a[i] *= inv;
+    }
+}
+
+/* fft.cpp:73-84 Rfft: out has n/2+1 interleaved complex values. */
+void nfo_rfft(const float* x, int n, float* out_complex) {
+    float complex* buf = (float complex*)malloc(sizeof(float complex) * n);
+    for (int i = 0; i < n; ++i) buf[i] = CMPLXF(x[i], 0.0f);
+    complex_fft(buf, n, 0);
+    const int half = n / 2 + 1;
+    for (int i = 0; i < half; ++i) {
+        out_complex[2 * i] = crealf(buf[i]);
+        out_complex[2 * i + 1] = cimagf(buf[i]);
+    }
+    free(buf);
+}
+
+/* fft.cpp:86-99 Irfft: mirror conjugates of bins 1..n/2-1, complex inverse, real part. */
+void nfo_irfft(const float* x_complex, int n, float* out) {
+    float complex* buf = (float complex*)malloc(sizeof(float complex) * n);
+    const int half = n / 2 + 1;
+    for (int i = 0; i < half; ++i) buf[i] = CMPLXF(x_complex[2 * i], x_complex[2 * i + 1]);
+    for (int i = 1; i < n - half + 1; ++i) buf[n - i] = conjf(buf[i]);
+    complex_fft(buf, n, 1);
+    for (int i = 0; i < n; ++i) out[i] = crealf(buf[i]);
+    free(buf);
+}
+
+/* fft.cpp:101-124 Rfft2: row rfft, then column complex FFT over the W/2+1 columns. */
+void nfo_rfft2(const float* x, int H, int W, float* out_complex) {
+    const int half_w = W / 2 + 1;
+    float complex* scratch = (float complex*)malloc(sizeof(float complex) * (size_t)H * half_w);
+    for (int i = 0; i < H; ++i)
+        nfo_rfft(x + (int64_t)i * W, W, (float*)(scratch + (int64_t)i * half_w));
+    float complex* col = (float complex*)malloc(sizeof(float complex) * H);
+    for (int j = 0; j < half_w; ++j) {
+        for (int i = 0; i < H; ++i) col[i] = scratch[(int64_t)i * half_w + j];
+        complex_fft(col, H, 0);
+        for (int i = 0; i < H; ++i) {
+            out_complex[((int64_t)i * half_w + j) * 2] = crealf(col[i]);
+            out_complex[((int64_t)i * half_w + j) * 2 + 1] = cimagf(col[i]);
+        }
+    }
+    free(col);
+    free(scratch);
+}
+
+/* fft.cpp:126-149 Irfft2: column inverse complex FFT, then row irfft. */
+void nfo_irfft2(const float* x_complex, int H, int W, float* out) {
+    const int half_w = W / 2 + 1;
+    float complex* col = (float complex*)malloc(sizeof(float complex) * H);
+    float complex* scratch = (float complex*)malloc(sizeof(float complex) * (size_t)H * half_w);
+    for (int j = 0; j < half_w; ++j) {
+        for (int i = 0; i < H; ++i)
+            col[i] = CMPLXF(x_complex[((int64_t)i * half_w + j) * 2],
+                            x_complex[((int64_t)i * half_w + j) * 2 + 1]);
+        complex_fft(col, H, 1);
+        for (int i = 0; i < H; ++i) scratch[(int64_t)i * half_w + j] = col[i];
+    }
+    for (int i = 0; i < H; ++i)
+        nfo_irfft((const float*)(scratch + (int64_t)i * half_w), W, out + (int64_t)i * W);
+    free(scratch);
+    free(col);
+}
+
+/* fft.cpp:151-194 Rfft3: D-axis rfft, W-axis cfft, H-axis cfft. */
+void nfo_rfft3(const float* x, int H, int W, int D, float* out_complex) {
+    const int half_d = D / 2 + 1;
+    const size_t tot = (size_t)H * W * half_d;
+    float complex* scratch = (float complex*)malloc(sizeof(float complex) * tot);
+    for (int i = 0; i < H; ++i)
+        for (int j = 0; j < W; ++j)
+            nfo_rfft(x + ((int64_t)i * W + j) * D, D,
+                     (float*)(scratch + ((int64_t)i * W + j) * half_d));
+    float complex* col_w = (float complex*)malloc(sizeof(float complex) * W);
+    for (int i = 0; i < H; ++i)
+        for (int k = 0; k < half_d; ++k) {
+            for (int j = 0; j < W; ++j) col_w[j] = scratch[((int64_t)i * W + j) * half_d + k];
+            complex_fft(col_w, W, 0);
+            for (int j = 0; j < W; ++j) scratch[((int64_t)i * W + j) * half_d + k] = col_w[j];
+        }
+    float complex* col_h = (float complex*)malloc(sizeof(float complex) * H);
+    for (int j = 0; j < W; ++j)
+        for (int k = 0; k < half_d; ++k) {
+            for (int i = 0; i < H; ++i) col_h[i] = scratch[((int64_t)i * W + j) * half_d + k];
+            complex_fft(col_h, H, 0);
+            for (int i = 0; i < H; ++i) {
+                out_complex[(((int64_t)i * W + j) * half_d + k) * 2] = crealf(col_h[i]);
+                out_complex[(((int64_t)i * W + j) * half_d + k) * 2 + 1] = cimagf(col_h[i]);
+            }
+        }
+    free(col_h);
+    free(col_w);
+    free(scratch);
+}
+
+/* fft.cpp:196-243 Irfft3: H-axis inverse, W-axis inverse, D-axis irfft. */
+void nfo_irfft3(const float* x_complex, int H, int W, int D, float* out) {
+    const int half_d = D / 2 + 1;
+    const size_t tot = (size_t)H * W * half_d;
+    float complex* col_h = (float complex*)malloc(sizeof(float complex) * H);
+    float complex* scratch = (float complex*)malloc(sizeof(float complex) * tot);
+    for (int j = 0; j < W; ++j)
+        for (int k = 0; k < half_d; ++k) {
+            for (int i = 0; i < H; ++i)
+                col_h[i] = CMPLXF(x_complex[(((int64_t)i * W + j) * half_d + k) * 2],
+                                  x_complex[(((int64_t)i * W + j) * half_d + k) * 2 + 1]);
+            complex_fft(col_h, H, 1);
+            for (int i = 0; i < H; ++i) scratch[((int64_t)i * W + j) * half_d + k] = col_h[i];
+        }
+    float complex* col_w = (float complex*)malloc(sizeof(float complex) * W);
+    for (int i = 0; i < H; ++i)
+        for (int k = 0; k < half_d; ++k) {
+            for (int j = 0; j < W; ++j) col_w[j] = scratch[((int64_t)i * W + j) * half_d + k];
+            complex_fft(col_w, W, 1);
+            for (int j = 0; j < W; ++j) scratch[((int64_t)i * W + j) * half_d + k] = col_w[j];
+        }
+    for (int i = 0; i < H; ++i)
+        for (int j = 0; j < W; ++j)
+            nfo_irfft((const float*)(scratch + ((int64_t)i * W + j) * half_d), D,
+                      out + ((int64_t)i * W + j) * D);
+    free(col_w);
+    free(scratch);
+    free(col_h);
+}
+
+/* ------------------------------------------------------------------------- */
+/* Spectral convolutions                                                      */
+/* ------------------------------------------------------------------------- */
+
+/* fno.cpp:164-207 SpectralConv1d on h (b, w, n). */
+void nfo_spectral_conv1d(const float* h, int bsz, int w, int n, int modes,
+                         const float* w_real, const float* w_imag, float* out) {
+    const int half = n / 2 + 1;
+    float* Hs = (float*)malloc(sizeof(float) * (size_t)w * half * 2);
+    float* Out_ft = (float*)malloc(sizeof(float) * (size_t)w * half * 2);
+    float* time_scratch = (float*)malloc(sizeof(float) * n);
+    for (int bi = 0; bi < bsz; ++bi) {
+        memset(Out_ft, 0, sizeof(float) * (size_t)w * half * 2);
+        for (int wi = 0; wi < w; ++wi)
+            nfo_rfft(h + (int64_t)bi * w * n + (int64_t)wi * n, n, Hs + (int64_t)wi * half * 2);
+        for (int mi = 0; mi < modes; ++mi)
+            for (int wo = 0; wo < w; ++wo) {
+                float sum_re = 0.0f, sum_im = 0.0f;
+                for (int wi2 = 0; wi2 < w; ++wi2) {
+                    float hr = Hs[wi2 * half * 2 + 2 * mi];
+                    float hi = Hs[wi2 * half * 2 + 2 * mi + 1];
+                    float wr = w_real[((wi2 * w) + wo) * modes + mi];
+                    float wi3 = w_imag[((wi2 * w) + wo) * modes + mi];
+                    sum_re += hr * wr - hi * wi3;
+                    sum_im += hr * wi3 + hi * wr;
+                }
+                Out_ft[wo * half * 2 + 2 * mi] = sum_re;
+                Out_ft[wo * half * 2 + 2 * mi + 1] = sum_im;
+            }
+        for (int wo = 0; wo < w; ++wo) {
+            nfo_irfft(Out_ft + (int64_t)wo * half * 2, n, time_scratch);
+            memcpy(out + (int64_t)bi * w * n + (int64_t)wo * n, time_scratch, sizeof(float) * n);
+        }
+    }
+    free(time_scratch);
+    free(Out_ft);
+    free(Hs);
+}
+
+/* fno.cpp:717-771 SpectralConv2d on h (b, w, H, W). */
+void nfo_spectral_conv2d(const float* h, int bsz, int w, int H, int W, int modes_h,
+                         int modes_w, const float* w_real, const float* w_imag, float* out) {
+    const int half_w = W / 2 + 1;
+    const size_t spec = (size_t)w * H * half_w * 2;
+    float* H_spec = (float*)malloc(sizeof(float) * spec);
+    float* Out_ft = (float*)malloc(sizeof(float) * spec);
+    for (int bi = 0; bi < bsz; ++bi) {
+        memset(Out_ft, 0, sizeof(float) * spec);
+        for (int wi = 0; wi < w; ++wi)
+            nfo_rfft2(h + ((int64_t)bi * w + wi) * H * W, H, W,
+                      H_spec + ((int64_t)wi * H) * half_w * 2);
+        for (int mi = 0; mi < modes_h; ++mi)
+            for (int mj = 0; mj < modes_w; ++mj)
+                for (int wo = 0; wo < w; ++wo) {
+                    float sum_re = 0.0f, sum_im = 0.0f;
+                    for (int wi = 0; wi < w; ++wi) {
+                        const float* H_wi = H_spec + (((int64_t)wi * H + mi) * half_w + mj) * 2;
+                        float hr = H_wi[0];
+                        float hi = H_wi[1];
+                        const float* w_wi =
+                            w_real + ((((int64_t)wi * w) + wo) * modes_h + mi) * modes_w + mj;
+                        const float* wi_wi =
+                            w_imag + ((((int64_t)wi * w) + wo) * modes_h + mi) * modes_w + mj;
+                        float wr = w_wi[0];
+                        float wii = wi_wi[0];
+                        sum_re += hr * wr - hi * wii;
+                        sum_im += hr * wii + hi * wr;
+                    }
+                    float* Out_wo = Out_ft + (((int64_t)wo * H + mi) * half_w + mj) * 2;
+                    Out_wo[0] = sum_re;
+                    Out_wo[1] = sum_im;
+                }
+        for (int wo = 0; wo < w; ++wo)
+            nfo_irfft2(Out_ft + (int64_t)wo * H * half_w * 2, H, W,
+                       out + (((int64_t)bi * w + wo) * H) * W);
+    }
+    free(Out_ft);
+    free(H_spec);
+}
+
+/* ------------------------------------------------------------------------- */
+/* FNO2d forward                                                              */
+/* ------------------------------------------------------------------------- */
+
+/* Weight qparams attached to one weight tensor (per-channel and/or per-tensor). */
+typedef struct {
+    const float* pc_scales;
+    const int32_t* pc_zps;
+    int64_t pc_n;
+    int32_t pc_axis;
+    int32_t has_pc;
+    float pt_scale;
+    int32_t pt_zp;
+    int32_t has_pt;
+} nfo_wq;
+
+/* Activation qparams for one ".output" key: INT8 per-tensor and/or FP8 scale. */
+typedef struct {
+    float scale;
+    int32_t zp;
+    int32_t has;
+    float fp8_scale;
+    int32_t has_fp8;
+} nfo_aq;
+
+typedef struct {
+    int32_t in_ch, out_ch, width, modes_h, modes_w, n_layers, pad_factor, relu;
+    int32_t quant_enabled;
+    const float* lift_w;
+    const float* lift_b;
+    const float* proj_q_w;
+    const float* proj_q_b;
+    const float* proj_out_w;
+    const float* proj_out_b;
+    const float* spec_wr[NFO_MAX_LAYERS];
+    const float* spec_wi[NFO_MAX_LAYERS];
+    const float* loc_w[NFO_MAX_LAYERS];
+    const float* loc_b[NFO_MAX_LAYERS];
+    nfo_wq q_lift_w, q_lift_b, q_proj_q_w, q_proj_q_b, q_proj_out_w, q_proj_out_b;
+    nfo_wq q_spec_wr[NFO_MAX_LAYERS];
+    nfo_wq q_spec_wi[NFO_MAX_LAYERS];
+    nfo_wq q_loc_w[NFO_MAX_LAYERS];
+    nfo_wq q_loc_b[NFO_MAX_LAYERS];
+    nfo_aq a_lift, a_proj_q, a_proj_out;
+    nfo_aq a_locs[NFO_MAX_LAYERS];
+} nfo_fno2d;
+
+static float* dup_floats(const float* src, int64_t n) {
+    float* d = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+    memcpy(d, src, sizeof(float) * (size_t)n);
+    return d;
+}
+
+static void dq_weight(float* t, int64_t d0, int64_t d1, int64_t d2, int64_t d3, int ndim,
+                      const nfo_wq* q) {
+    int64_t shape[4] = {d0, d1, d2, d3};
+    nfo_dequantise_weight(t, shape, ndim, q->pc_scales, q->pc_zps, q->pc_n, q->pc_axis,
+                          q->has_pc, q->pt_scale, q->pt_zp, q->has_pt);
+}
+
+/* fno.cpp:810-844 apply_fake_quant: FP8 log2 snap takes precedence over INT8. */
+static void apply_fq(float* data, int64_t numel, const nfo_aq* a, int quant_enabled) {
+    if (!quant_enabled) return;
+    if (a->has_fp8) {
+        nfo_fake_quant_fp8_log2(data, numel, a->fp8_scale);
+    } else if (a->has) {
+        nfo_fake_quant(data, numel, a->scale, a->zp);
+    }
+}
+
+/* The layer-input snap of the FNO1d INT8 convention (fno.cpp:475-508): INT8
+ * per-tensor only (the FP8 table is not consulted for the input snap). */
+static void apply_input_fq(float* data, int64_t numel, const nfo_aq* a, int quant_enabled) {
+    if (quant_enabled && a->has) nfo_fake_quant(data, numel, a->scale, a->zp);
+}
+
+/* Optional per-layer taps for layer-wise parity checks (may be NULL):
+ * codes_in[i]  : int8 codes of the layer-i input (channel-last), int8 mode only
+ * x1_out[i]    : spectral branch output, channel-first (b, w, H, W)
+ * h_out[i]     : layer-i output after the activation, channel-last (b, H, W, w) */
+typedef struct {
+    int8_t* codes_in[NFO_MAX_LAYERS + 1];
+    float* x1_out[NFO_MAX_LAYERS];
+    float* h_out[NFO_MAX_LAYERS];
+} nfo_taps;
+
+/* mode 0: fno.cpp:777-995 with the Create-time weight fake-quant (fno.cpp:997-1020).
+ * mode 1: the INT8 composition described in the file header.
+ * x (b, H, W, in_ch) -> y (b, H, W, out_ch).  Returns 0, or a StatusCode value on
+ * a rejected shape (tensor.h:31-37). */
+int nfo_fno2d_forward(const nfo_fno2d* m, int mode, const float* x, int bsz, int H0,
+                      int W0, float* y, nfo_taps* taps) {
+    const int w = m->width, mh = m->modes_h, mw = m->modes_w, L = m->n_layers;
+    const int in_ch = m->in_ch, out_ch = m->out_ch;
+    if (L > NFO_MAX_LAYERS) return 1;
+    if (H0 <= 0 || W0 <= 0 || (H0 & (H0 - 1)) || (W0 & (W0 - 1))) return 1;
+
+    /* Create-time weight copies + fake-quant (fno.cpp:997-1020). */
+    float* lift_w = dup_floats(m->lift_w, (int64_t)w * in_ch);
+    float* lift_b = dup_floats(m->lift_b, w);
+    float* pq_w = dup_floats(m->proj_q_w, (int64_t)w * w);
+    float* pq_b = dup_floats(m->proj_q_b, w);
+    float* po_w = dup_floats(m->proj_out_w, (int64_t)out_ch * w);
+    float* po_b = dup_floats(m->proj_out_b, out_ch);
+    float* swr[NFO_MAX_LAYERS];
+    float* swi[NFO_MAX_LAYERS];
+    float* lw[NFO_MAX_LAYERS];
+    float* lb[NFO_MAX_LAYERS];
+    const int64_t nspec = (int64_t)w * w * mh * mw;
+    for (int i = 0; i < L; ++i) {
+        swr[i] = dup_floats(m->spec_wr[i], nspec);
+        swi[i] = dup_floats(m->spec_wi[i], nspec);
+        lw[i] = dup_floats(m->loc_w[i], (int64_t)w * w);
+        lb[i] = dup_floats(m->loc_b[i], w);
+    }
+    if (m->quant_enabled) {
+        dq_weight(lift_w, w, in_ch, 0, 0, 2, &m->q_lift_w);
+        dq_weight(lift_b, w, 0, 0, 0, 1, &m->q_lift_b);
+        dq_weight(pq_w, w, w, 0, 0, 2, &m->q_proj_q_w);
+        dq_weight(pq_b, w, 0, 0, 0, 1, &m->q_proj_q_b);
+        dq_weight(po_w, out_ch, w, 0, 0, 2, &m->q_proj_out_w);
+        dq_weight(po_b, out_ch, 0, 0, 0, 1, &m->q_proj_out_b);
+        for (int i = 0; i < L; ++i) {
+            dq_weight(swr[i], w, w, mh, mw, 4, &m->q_spec_wr[i]);
+            dq_weight(swi[i], w, w, mh, mw, 4, &m->q_spec_wi[i]);
+            dq_weight(lw[i], w, w, 0, 0, 2, &m->q_loc_w[i]);
+            dq_weight(lb[i], w, 0, 0, 0, 1, &m->q_loc_b[i]);
+        }
+    }
+
+    /* INT8 caches (fno.cpp:325-406 applied to locs.i and proj_q). */
+    int8_t* lq[NFO_MAX_LAYERS + 1];
+    int32_t* lsum[NFO_MAX_LAYERS + 1];
+    int use_int8[NFO_MAX_LAYERS + 1];
+    for (int i = 0; i <= L; ++i) {
+        const nfo_wq* q = (i < L) ? &m->q_loc_w[i] : &m->q_proj_q_w;
+        const float* W = (i < L) ? lw[i] : pq_w;
+        const nfo_aq* a_in = (i == 0) ? &m->a_lift : &m->a_locs[i - 1];
+        use_int8[i] = (mode == 1) && q->has_pc && q->pc_axis == 0 && a_in->has &&
+                      m->quant_enabled;
+        lq[i] = NULL;
+        lsum[i] = NULL;
+        if (use_int8[i]) {
+            lq[i] = (int8_t*)malloc((size_t)w * w);
+            lsum[i] = (int32_t*)malloc(sizeof(int32_t) * w);
+            nfo_quantise_weight_2d(W, w, w, q->pc_scales, q->pc_zps, lq[i], lsum[i]);
+        }
+    }
+
+    int64_t H = H0, W = W0;
+    const int64_t P = H * W;
+    const int64_t M = (int64_t)bsz * P;
+
+    float* h = (float*)calloc((size_t)(M * w), sizeof(float));        /* (b,H,W,w) */
+    nfo_linear(x, lift_w, lift_b, (int)M, in_ch, w, h);
+    apply_fq(h, M * w, &m->a_lift, m->quant_enabled);
+
+    float* h_perm = (float*)calloc((size_t)(M * w), sizeof(float));   /* (b,w,H,W) */
+    for (int64_t bi = 0; bi < bsz; ++bi)
+        for (int wi = 0; wi < w; ++wi)
+            for (int64_t hi = 0; hi < H; ++hi)
+                for (int64_t wj = 0; wj < W; ++wj)
+                    h_perm[((bi * w + wi) * H + hi) * W + wj] = h[((bi * H + hi) * W + wj) * w + wi];
+
+    /* fno.cpp:867-892 padding */
+    int64_t pad_h = 0, pad_w = 0;
+    if (m->pad_factor > 1) {
+        const int pf = m->pad_factor;
+        pad_h = (pf - (H % pf)) % pf;
+        pad_w = (pf - (W % pf)) % pf;
+        if (pad_h > 0 || pad_w > 0) {
+            const int64_t Hp = H + pad_h, Wp = W + pad_w;
+            float* padded = (float*)calloc((size_t)(bsz * w * Hp * Wp), sizeof(float));
+            for (int64_t bi = 0; bi < bsz; ++bi)
+                for (int wi = 0; wi < w; ++wi)
+                    for (int64_t hi = 0; hi < H; ++hi)
+                        memcpy(padded + ((bi * w + wi) * Hp + hi) * Wp,
+                               h_perm + ((bi * w + wi) * H + hi) * W, sizeof(float) * W);
+            free(h_perm);
+            h_perm = padded;
+            H += pad_h;
+            W += pad_w;
+        }
+    }
+    const int64_t Mp = (int64_t)bsz * H * W;
+    float* x1 = (float*)calloc((size_t)(Mp * w), sizeof(float));
+    float* x2 = (float*)calloc((size_t)(Mp * w), sizeof(float));
+    float* pin = (float*)calloc((size_t)(Mp * w), sizeof(float));
+    float* pout = (float*)calloc((size_t)(Mp * w), sizeof(float));
+    float* add = (float*)calloc((size_t)(Mp * w), sizeof(float));
+
+    for (int i = 0; i < L; ++i) {
+        const nfo_aq* a_in = (i == 0) ? &m->a_lift : &m->a_locs[i - 1];
+        if (mode == 1) apply_input_fq(h_perm, Mp * w, a_in, m->quant_enabled);
+        nfo_spectral_conv2d(h_perm, bsz, w, (int)H, (int)W, mh, mw, swr[i], swi[i], x1);
+        if (taps && taps->x1_out[i]) memcpy(taps->x1_out[i], x1, sizeof(float) * Mp * w);
+        for (int64_t bi = 0; bi < bsz; ++bi)
+            for (int64_t hi = 0; hi < H; ++hi)
+                for (int64_t wj = 0; wj < W; ++wj)
+                    for (int wi = 0; wi < w; ++wi)
+                        pin[((bi * H + hi) * W + wj) * w + wi] = h_perm[((bi * w + wi) * H + hi) * W + wj];
+        if (use_int8[i]) {
+            nfo_linear_forward_batched(lq[i], m->q_loc_w[i].pc_scales, m->q_loc_w[i].pc_zps,
+                                       lsum[i], NULL, w, w, a_in->scale, a_in->zp, (int)Mp, pin,
+                                       pout, NULL, taps ? taps->codes_in[i] : NULL);
+            for (int64_t r = 0; r < Mp; ++r)
+                for (int j = 0; j < w; ++j) pout[r * w + j] += lb[i][j];
+        } else {
+            nfo_linear(pin, lw[i], lb[i], (int)Mp, w, w, pout);
+        }
+        for (int64_t bi = 0; bi < bsz; ++bi)
+            for (int wi = 0; wi < w; ++wi)
+                for (int64_t hi = 0; hi < H; ++hi)
+                    for (int64_t wj = 0; wj < W; ++wj)
+                        x2[((bi * w + wi) * H + hi) * W + wj] = pout[((bi * H + hi) * W + wj) * w + wi];
+        apply_fq(x2, Mp * w, &m->a_locs[i], m->quant_enabled);
+        for (int64_t k = 0; k < Mp * w; ++k) add[k] = x1[k] + x2[k];
+        nfo_apply_activation(add, Mp * w, m->relu);
+        memcpy(h_perm, add, sizeof(float) * Mp * w);
+        if (taps && taps->h_out[i]) {
+            for (int64_t bi = 0; bi < bsz; ++bi)
+                for (int64_t hi = 0; hi < H; ++hi)
+                    for (int64_t wj = 0; wj < W; ++wj)
+                        for (int wi = 0; wi < w; ++wi)
+                            taps->h_out[i][((bi * H + hi) * W + wj) * w + wi] =
+                                h_perm[((bi * w + wi) * H + hi) * W + wj];
+        }
+    }
+
+    if (pad_h > 0 || pad_w > 0) {
+        const int64_t oh = H - pad_h, ow = W - pad_w;
+        float* trimmed = (float*)calloc((size_t)(bsz * w * oh * ow), sizeof(float));
+        for (int64_t bi = 0; bi < bsz; ++bi)
+            for (int wi = 0; wi < w; ++wi)
+                for (int64_t hi = 0; hi < oh; ++hi)
+                    memcpy(trimmed + ((bi * w + wi) * oh + hi) * ow,
+                           h_perm + ((bi * w + wi) * H + hi) * W, sizeof(float) * ow);
+        free(h_perm);
+        h_perm = trimmed;
+        H = oh;
+        W = ow;
+    }
+
+    float* h_back = (float*)calloc((size_t)(M * w), sizeof(float));
+    for (int64_t bi = 0; bi < bsz; ++bi)
+        for (int64_t hi = 0; hi < H; ++hi)
+            for (int64_t wj = 0; wj < W; ++wj)
+                for (int wi = 0; wi < w; ++wi)
+                    h_back[((bi * H + hi) * W + wj) * w + wi] = h_perm[((bi * w + wi) * H + hi) * W + wj];
+
+    float* q = (float*)calloc((size_t)(M * w), sizeof(float));
+    if (use_int8[L]) {
+        const nfo_aq* a_in = (L == 0) ? &m->a_lift : &m->a_locs[L - 1];
+        nfo_linear_forward_batched(lq[L], m->q_proj_q_w.pc_scales, m->q_proj_q_w.pc_zps,
+                                   lsum[L], NULL, w, w, a_in->scale, a_in->zp, (int)M, h_back, q,
+                                   NULL, taps ? taps->codes_in[L] : NULL);
+        for (int64_t r = 0; r < M; ++r)
+            for (int j = 0; j < w; ++j) q[r * w + j] += pq_b[j];
+    } else {
+        nfo_linear(h_back, pq_w, pq_b, (int)M, w, w, q);
+    }
+    apply_fq(q, M * w, &m->a_proj_q, m->quant_enabled);
+    nfo_apply_activation(q, M * w, m->relu);
+    nfo_linear(q, po_w, po_b, (int)M, w, out_ch, y);
+    apply_fq(y, M * out_ch, &m->a_proj_out, m->quant_enabled);
+
+    free(q);
+    free(h_back);
+    free(add);
+    free(pout);
+    free(pin);
+    free(x2);
+    free(x1);
+    free(h_perm);
+    free(h);
+    for (int i = 0; i <= L; ++i) {
+        free(lq[i]);
+        free(lsum[i]);
+    }
+    for (int i = 0; i < L; ++i) {
+        free(swr[i]);
+        free(swi[i]);
+        free(lw[i]);
+        free(lb[i]);
+    }
+    free(lift_w);
+    free(lift_b);
+    free(pq_w);
+    free(pq_b);
+    free(po_w);
+    free(po_b);
+    return 0;
+}
