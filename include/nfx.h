@@ -1,0 +1,111 @@
+/*
+ * nfx.h -- C-ABI of the B200 (sm_100a) quantized neural-operator inference library
+ * (libnfx.so).  Plain pointers, sizes and status codes; no C++ or torch types.
+ *
+ * Every entry point replaces one interface of the reference NeuroFlow C++ runtime
+ * (AITree69/neuroflow, paths relative to that project) and is cited beside it.  The
+ * return value of every int-returning function is a reference StatusCode
+ * (cpp/include/neuroflow/tensor.h:29-37): 0 Ok, 1 InvalidArg, 2 FileNotFound,
+ * 3 ParseError, 4 ShapeMismatch, 5 UnsupportedOp, 99 Internal (CUDA failures and
+ * device-side timeouts are reported as Internal with a message).
+ *
+ * Threading: a runtime handle is single-threaded, like the reference runtime
+ * (cpp/include/neuroflow/fno.h:192-209).  Different handles may be used from
+ * different threads.  Each handle is bound to one CUDA device chosen at creation.
+ */
+#ifndef NFX_H_
+#define NFX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    NFX_OK = 0,
+    NFX_INVALID_ARG = 1,
+    NFX_FILE_NOT_FOUND = 2,
+    NFX_PARSE_ERROR = 3,
+    NFX_SHAPE_MISMATCH = 4,
+    NFX_UNSUPPORTED_OP = 5,
+    NFX_INTERNAL = 99
+};
+
+typedef struct nfx_runtime nfx_runtime;
+
+/* ---- InferenceRuntime (cpp/include/neuroflow/runtime.h:69-135) ---------------- */
+
+/* InferenceRuntime::Create (runtime.h:72-74, runtime.cpp:79-83): load a NeuroIR v0
+ * binary (.nneuroir, with the optional NIRQ block) and upload the weights to
+ * `device`.  On failure *out is NULL and nfx_last_error() holds the message. */
+int nfx_runtime_create(const char* ir_path, int device, nfx_runtime** out);
+
+/* Destructor of InferenceRuntime. */
+void nfx_runtime_destroy(nfx_runtime* rt);
+
+/* InferenceRuntime::op (runtime.h:114): "FNO1d", "FNO2d", ... */
+const char* nfx_runtime_op(const nfx_runtime* rt);
+
+/* InferenceRuntime::EnableInt8Gemm (runtime.h:116-124, runtime.cpp:155-166).  On this
+ * runtime the INT8 path covers FNO2d as well as FNO1d (see DESIGN.md for the exact
+ * semantics); it needs per-channel weight qparams and per-tensor activation qparams
+ * in the NIRQ block, otherwise it is a no-op like the reference. */
+void nfx_runtime_enable_int8_gemm(nfx_runtime* rt);
+
+/* InferenceRuntime::IsInt8GemmEnabled (runtime.h:126-128). */
+int nfx_runtime_is_int8_gemm_enabled(const nfx_runtime* rt);
+
+/* InferenceRuntime::Run (runtime.h:76-79, runtime.cpp:85-101).  x and y are HOST
+ * float32 row-major buffers owned by the caller; shapes as the reference's
+ * FNO*::Forward checks them (batch first, channels last).  Synchronous. */
+int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
+                    float* y, const int64_t* y_shape, int y_rank);
+
+/* Device-resident variant of Run: x and y are DEVICE pointers on the runtime's device;
+ * the work is enqueued on `stream` (a cudaStream_t, NULL = legacy default stream)
+ * and the call returns without synchronising.  Device-side errors surface at the
+ * next nfx_runtime_check() or synchronous call.  No counterpart in the reference
+ * (its runtime is host-only); it is the timing/multi-GPU entry of the same work. */
+int nfx_runtime_run_device(nfx_runtime* rt, const float* x, const int64_t* x_shape,
+                           int x_rank, float* y, const int64_t* y_shape, int y_rank,
+                           void* stream);
+
+/* Synchronise the runtime's work and report device-side errors (bounded waits that
+ * timed out inside a kernel) as NFX_INTERNAL. */
+int nfx_runtime_check(nfx_runtime* rt);
+
+/* Message of the last failing call on this handle ("" when none). */
+const char* nfx_runtime_last_error(const nfx_runtime* rt);
+
+/* Message of the last failing handle-less call of this thread. */
+const char* nfx_last_error(void);
+
+/* ---- nflow-quant GEMM (cpp/include/neuroflow/int8_gemm.h) ----------------------- */
+
+/* W8A8 GEMM over activation CODES with one (scale, zero point) per row, per-channel
+ * weight codes, and the reference LinearForwardBatched epilogue
+ * (int8_gemm.cpp:559-578) evaluated with the row's qparams, then + bias[o]
+ * (fno.cpp:541-548) and an optional activation (act: 0 none, 1 GELU tanh form,
+ * 2 ReLU; fno.cpp:36-48).  Replaces int8_gemm::LinearForwardBatched
+ * (int8_gemm.h:95-97) for inputs that are already quantised per token.
+ * All pointers are DEVICE pointers on the current device:
+ *   A (M,K) int8; scale_a/zp_a (M,) or NULL to use scale_a_t/zp_a_t for every row;
+ *   W (N,K) int8 in (out, in) layout; scale_w, zp_w, sum_w, bias (N,) (bias may be
+ *   NULL); C (M,N) float32.  sum_w[o] = sum_k (W[o,k] - zp_w[o]) (int8_gemm.h:67-77).
+ * K, N in {32, 64, 128, 256}; M >= 0.  Asynchronous on `stream`. */
+int nfx_int8_gemm(const int8_t* A, const float* scale_a, const int32_t* zp_a, float scale_a_t,
+                  int32_t zp_a_t, int M, int K, const int8_t* W, const float* scale_w,
+                  const int32_t* zp_w, const int32_t* sum_w, const float* bias, int N, int act,
+                  float* C, void* stream);
+
+/* Read and clear the device error word of the current device (bit flags of waits
+ * that timed out inside kernels).  Synchronises the device. */
+int nfx_device_errors(unsigned* flags_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NFX_H_ */

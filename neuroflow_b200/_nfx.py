@@ -1,0 +1,89 @@
+"""ctypes binding of libnfx.so (the C-ABI in include/nfx.h).
+
+The product path: every call goes to the CUDA library; there is no CPU fallback.
+Importing this module fails loudly when the library has not been built.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libnfx.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(
+        f"{LIB_PATH} is missing: build the CUDA library first "
+        "(python -m neuroflow_b200.build, or __graft_entry__.build())")
+
+lib = C.CDLL(LIB_PATH)
+
+_vp = C.c_void_p
+_i64p = C.POINTER(C.c_int64)
+
+lib.nfx_last_error.restype = C.c_char_p
+lib.nfx_int8_gemm.restype = C.c_int
+lib.nfx_int8_gemm.argtypes = [_vp, _vp, _vp, C.c_float, C.c_int32, C.c_int, C.c_int, _vp, _vp,
+                              _vp, _vp, _vp, C.c_int, C.c_int, _vp, _vp]
+lib.nfx_device_errors.restype = C.c_int
+lib.nfx_device_errors.argtypes = [C.POINTER(C.c_uint)]
+
+if hasattr(lib, "nfx_runtime_create"):
+    lib.nfx_runtime_create.restype = C.c_int
+    lib.nfx_runtime_create.argtypes = [C.c_char_p, C.c_int, C.POINTER(_vp)]
+    lib.nfx_runtime_destroy.restype = None
+    lib.nfx_runtime_destroy.argtypes = [_vp]
+    lib.nfx_runtime_op.restype = C.c_char_p
+    lib.nfx_runtime_op.argtypes = [_vp]
+    lib.nfx_runtime_enable_int8_gemm.restype = None
+    lib.nfx_runtime_enable_int8_gemm.argtypes = [_vp]
+    lib.nfx_runtime_is_int8_gemm_enabled.restype = C.c_int
+    lib.nfx_runtime_is_int8_gemm_enabled.argtypes = [_vp]
+    lib.nfx_runtime_run.restype = C.c_int
+    lib.nfx_runtime_run.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int]
+    lib.nfx_runtime_run_device.restype = C.c_int
+    lib.nfx_runtime_run_device.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int, _vp]
+    lib.nfx_runtime_check.restype = C.c_int
+    lib.nfx_runtime_check.argtypes = [_vp]
+    lib.nfx_runtime_last_error.restype = C.c_char_p
+    lib.nfx_runtime_last_error.argtypes = [_vp]
+
+
+class NfxError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[status {code}] {msg}")
+        self.code = code
+
+
+def check(rc: int, handle=None) -> None:
+    if rc != 0:
+        if handle is not None:
+            msg = lib.nfx_runtime_last_error(handle)
+        else:
+            msg = lib.nfx_last_error()
+        raise NfxError(rc, (msg or b"").decode())
+
+
+def device_errors() -> int:
+    v = C.c_uint(0)
+    check(lib.nfx_device_errors(C.byref(v)))
+    return int(v.value)
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def int8_gemm(A, W, scale_w, zp_w, sum_w, bias=None, scale_a=None, zp_a=None, scale_a_t=1.0,
+              zp_a_t=0, act=0, out=None, stream=None):
+    """torch-tensor front-end of nfx_int8_gemm (device tensors, current device)."""
+    import torch
+    M, K = A.shape
+    N = W.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    s = stream if stream is not None else torch.cuda.current_stream(A.device).cuda_stream
+    check(lib.nfx_int8_gemm(_ptr(A), _ptr(scale_a), _ptr(zp_a), float(scale_a_t), int(zp_a_t),
+                            M, K, _ptr(W), _ptr(scale_w), _ptr(zp_w), _ptr(sum_w), _ptr(bias), N,
+                            int(act), _ptr(out), C.c_void_p(s)))
+    return out

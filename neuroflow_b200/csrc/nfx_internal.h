@@ -1,0 +1,42 @@
+// nfx_internal.h -- declarations shared by the CUDA translation units and the C-ABI
+// layer (not part of the public interface; the public one is include/nfx.h).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace nfx {
+
+// Arguments of the INT8 GEMM kernel (gemm_i8.cu).  Device pointers.
+struct GemmArgs {
+    const int8_t* A;          // (M, K) activation codes
+    const float* scale_a;     // (M,) per-row scale, or nullptr -> scale_a_t
+    const int32_t* zp_a;      // (M,) per-row zero point, or nullptr -> zp_a_t
+    float scale_a_t;
+    int zp_a_t;
+    const int8_t* W;          // (N, K) weight codes, (out, in) layout
+    const float* scale_w;     // (N,)
+    const int32_t* zp_w;      // (N,)
+    const int32_t* sum_w;     // (N,) sum_k (W[o,k] - zp_w[o])
+    const float* bias;        // (N,) or nullptr
+    int act;                  // 0 none, 1 GELU (tanh form), 2 ReLU
+    float* C;                 // (M, N) fp32 output
+    int M;
+    unsigned* err;            // device error word
+};
+
+bool gemm_i8_supported(int K, int N);
+cudaError_t gemm_i8_launch(const GemmArgs& p, int K, int N, cudaStream_t stream);
+
+// Host helpers (nfx_host.cpp)
+int current_device();
+int device_sm_count();
+unsigned* device_error_word();  // per current device, allocated once
+// Encode a 2-D row-major tensor map (inner dimension first).  Returns false on error.
+bool encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+               uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+               int swizzle_bytes);
+
+}  // namespace nfx

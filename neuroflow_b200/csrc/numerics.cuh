@@ -1,0 +1,64 @@
+// numerics.cuh -- device restatements of the reference runtime's scalar arithmetic,
+// written with explicit IEEE intrinsics so that nvcc cannot re-associate or contract
+// them differently from the reference build (GCC -O3 -mfma, whose contraction choices
+// are spelled out per function below).
+#pragma once
+
+#include <climits>
+#include <cstdint>
+
+namespace nfx {
+
+// int8_gemm.cpp:514-518 QuantiseActivation for one element:
+//   q = (int32)std::round(v / s) + zp, clamped to [-128, 127].
+// std::round is half-away-from-zero (CUDA roundf); the division is IEEE.  The
+// float->int conversion follows x86 cvttss2si, which the reference executes: values
+// outside int32 range and NaN become INT_MIN, and the following `+ zp` wraps.
+__device__ __forceinline__ int quantise_i8(float v, float s, int zp) {
+    const float r = roundf(__fdiv_rn(v, s));
+    int q = (fabsf(r) < 2147483648.0f) ? __float2int_rz(r) : INT_MIN;
+    q = static_cast<int>(static_cast<unsigned>(q) + static_cast<unsigned>(zp));
+    return q < -128 ? -128 : (q > 127 ? 127 : q);
+}
+
+// fno.cpp:497-505 / :830-842: the float form of the same code,
+//   q = std::round(v / s) + zp (float), clamped with ordered compares (NaN passes).
+__device__ __forceinline__ float fq_code(float v, float s, float zp) {
+    float q = __fadd_rn(roundf(__fdiv_rn(v, s)), zp);
+    if (q < -128.0f) q = -128.0f;
+    if (q > 127.0f) q = 127.0f;
+    return q;
+}
+
+// fake-quant round trip: (q - zp) * s.
+__device__ __forceinline__ float fake_quant(float v, float s, float zp) {
+    return __fmul_rn(__fsub_rn(fq_code(v, s, zp), zp), s);
+}
+
+// fno.cpp:36-48 GELU (tanh form).  The reference build evaluates
+//   z + 0.044715f*z*z*z   as   fma(z, (0.044715f*z)*z, z)
+// and 0.5f*z*(1+t) as (0.5f*z)*(1+t).  tanhf is CUDA's (the reference uses glibc's;
+// the two differ by at most a couple of ulps, which the parity tolerance states).
+__device__ __forceinline__ float gelu_tanh(float z) {
+    const float c = __fsqrt_rn(__fdiv_rn(2.0f, 3.14159265358979323846f));
+    const float t = __fmul_rn(__fmul_rn(0.044715f, z), z);
+    const float inner = __fmaf_rn(z, t, z);
+    const float th = tanhf(__fmul_rn(c, inner));
+    return __fmul_rn(__fmul_rn(0.5f, z), __fadd_rn(1.0f, th));
+}
+
+__device__ __forceinline__ float relu_ref(float z) { return z < 0.0f ? 0.0f : z; }
+
+// int8_gemm.cpp:574-577 epilogue of LinearForwardBatched for one output:
+//   v = acc - zp_w*sum_a - zp_A*sum_w + K*zp_w*zp_A,  acc = sum a*(w - zp_w)
+// Given raw = sum a*w (the tensor-core product) and sum_a, acc = raw - zp_w*sum_a, so
+//   v = raw + zp_w*(K*zp_A - 2*sum_a) - zp_A*sum_w.
+// Every term stays inside int32 for K <= 256, so int32 arithmetic gives the same
+// value as the reference's int32/int64 mix.  y = (sW*sA)*float(v), then y + 0.0f.
+__device__ __forceinline__ float dequant_ref(int raw, int zp_w, int rconst, int zpA_sumw,
+                                             float sWsA) {
+    const int v = raw + zp_w * rconst - zpA_sumw;
+    return __fadd_rn(__fmul_rn(sWsA, __int2float_rn(v)), 0.0f);
+}
+
+}  // namespace nfx

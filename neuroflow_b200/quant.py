@@ -104,3 +104,33 @@ def quantise_rows(a: np.ndarray):
     q = np.sign(quo) * np.floor(np.abs(quo) + 0.5)
     q = np.clip(q.astype(np.int64) + zp[:, None], -128, 127).astype(np.int8)
     return q, scale, zp
+
+
+def quantise_weight_2d(W: np.ndarray, qp: PerChannel):
+    """Per-output-row weight codes and sum_w[o] = sum_i (W_q[o,i] - zp[o]) (the rule of
+    the reference's QuantiseWeight2D, cpp/src/fno.cpp:325-358)."""
+    W = np.asarray(W, np.float32)
+    s = np.asarray(qp.scales, np.float32)[:, None]
+    zp = np.asarray(qp.zero_points, np.int32)
+    quo = (W / s).astype(np.float32).astype(np.float64)
+    q = np.sign(quo) * np.floor(np.abs(quo) + 0.5)
+    q = (q.astype(np.float32) + zp[:, None].astype(np.float32))
+    q = np.clip(q, -128, 127).astype(np.int8)
+    sum_w = (q.astype(np.int32) - zp[:, None]).sum(axis=1).astype(np.int32)
+    return q, sum_w
+
+
+def gemm_case(seed: int, M: int, K: int, N: int):
+    """Synthetic INT8 GEMM operands of the GEMM sweep: per-token (per-row) codes of
+    N(0,1) activations, per-channel codes of Kaiming-uniform weights, fp32 bias."""
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    Aq, sA, zA = quantise_rows(a) if M > 0 else (np.zeros((0, K), np.int8),
+                                                 np.zeros(0, np.float32), np.zeros(0, np.int32))
+    bound = 1.0 / np.sqrt(K)
+    W = rng.uniform(-bound, bound, (N, K)).astype(np.float32)
+    bias = rng.uniform(-bound, bound, N).astype(np.float32)
+    qp = per_channel_qparams(W, 0)
+    Wq, sum_w = quantise_weight_2d(W, qp)
+    return dict(Aq=Aq, sA=sA, zA=zA, Wq=Wq, sW=np.asarray(qp.scales, np.float32),
+                zW=np.asarray(qp.zero_points, np.int32), sum_w=sum_w, bias=bias)
