@@ -1,0 +1,658 @@
+// fno2d.cu -- FNO2d INT8 layer executor kernels (sm_100a).
+//
+// Activations between layers live in HBM only as int8 codes, channel-last
+// (b, h, w, c), quantised with the layer-input qparams (the reference FNO1d INT8
+// convention, cpp/src/fno.cpp:475-549, applied to FNO2d's structure,
+// cpp/src/fno.cpp:777-995).  One layer is three kernels:
+//
+//   spec_fwd   codes -> per-row-block partial spectra of the truncated 2D rFFT
+//              (rows: W-axis DFT restricted to kw < MW; then the H-axis DFT
+//              restricted to kh < MH, accumulated over the block's rows).
+//   spec_mix   sum of the partials, then the per-mode complex (in x out) contraction
+//              (fno.cpp:740-764) -> Y (b, kh, kw, o).
+//   layer      tcgen05 kind::i8 GEMM of the local 1x1 layer (codes x locs.i codes),
+//              fused with: inverse truncated 2D transform of Y evaluated at the
+//              tile's points (x1), the LinearForwardBatched dequant epilogue + bias,
+//              locs.i.output fake-quant (x2), x1 + x2, activation, and quantisation
+//              to the next layer's codes (TMA store).
+//
+// lift (K = in_ch, CUDA cores) and the projection (tcgen05 GEMM for proj_q, the
+// out_ch-wide proj_out dot product in the epilogue) close the network.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "fno2d.h"
+#include "nfx_internal.h"
+#include "numerics.cuh"
+#include "sm100.cuh"
+
+namespace nfx {
+namespace {
+
+constexpr int pow2ceil(int v) {
+    int p = 32;
+    while (p < v) p <<= 1;
+    return p;
+}
+
+// ---------------------------------------------------------------------------
+// fake-quant variants selected at run time (fno.cpp:810-844)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float apply_fq(float v, const FqParam& q) {
+    if (q.kind == 1) return fake_quant(v, q.scale, static_cast<float>(q.zp));
+    if (q.kind == 2) {
+        // FP8 log2 snap of the reference FNO2d (fno.cpp:813-828)
+        if (!(q.scale > 0.0f)) return v;
+        const float u = __fdiv_rn(v, q.scale);
+        const float a = fabsf(u);
+        const float sign = u < 0.0f ? -1.0f : 1.0f;
+        const float qv = (a < 0.015625f)
+                             ? a
+                             : ldexpf(1.0f, static_cast<int>(__fdiv_rn(
+                                                roundf(__fmul_rn(log2f(a), 8.0f)), 8.0f)));
+        const float c = fminf(qv, 448.0f);
+        return __fmul_rn(__fmul_rn(sign, c), q.scale);
+    }
+    return v;
+}
+
+__device__ __forceinline__ float activation(float z, int act) {
+    return act == 1 ? relu_ref(z) : gelu_tanh(z);
+}
+
+// ---------------------------------------------------------------------------
+// lift: x (M, in_ch) fp32 -> codes (M, C) with the lift.output qparams.
+// fno.cpp:848-853 (Linear + fake-quant), fno.cpp:51-80 (the fma chain from the bias).
+// ---------------------------------------------------------------------------
+template <int C>
+__global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, int64_t M,
+                                                   int in_ch, const float* __restrict__ w,
+                                                   const float* __restrict__ b, float s, int zp,
+                                                   int8_t* __restrict__ codes) {
+    __shared__ float sw[C * 8];
+    __shared__ float sb[C];
+    for (int i = threadIdx.x; i < C * in_ch; i += blockDim.x) sw[i] = w[i];
+    for (int i = threadIdx.x; i < C; i += blockDim.x) sb[i] = b[i];
+    __syncthreads();
+    const float zpf = static_cast<float>(zp);
+    for (int64_t m = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; m < M;
+         m += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float xi[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) xi[k] = k < in_ch ? x[m * in_ch + k] : 0.0f;
+        uint32_t words[C / 4];
+#pragma unroll
+        for (int o = 0; o < C; ++o) {
+            float acc = sb[o];
+            for (int k = 0; k < in_ch; ++k) acc = __fmaf_rn(xi[k], sw[o * in_ch + k], acc);
+            const uint32_t byte = static_cast<uint32_t>(static_cast<int>(fq_code(acc, s, zpf))) & 0xFFu;
+            if ((o & 3) == 0) words[o >> 2] = byte;
+            else words[o >> 2] |= byte << (8 * (o & 3));
+        }
+        uint4* dst = reinterpret_cast<uint4*>(codes + m * C);
+#pragma unroll
+        for (int v = 0; v < C / 16; ++v)
+            dst[v] = make_uint4(words[4 * v], words[4 * v + 1], words[4 * v + 2], words[4 * v + 3]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// spec_fwd: grid (H / HB, B), C*MW threads.  Thread (c, kw) = (tid % C, tid / C)
+// accumulates  X[kh][kw][c] += F[h][kw][c] * e^{-2 pi i kh h / H}  over the block's
+// rows, with F[h][kw][c] = sum_w x[h][w][c] e^{-2 pi i kw w / W} and
+// x = (code - zp) * s, the snapped activation (fno.cpp:497-505).
+// ---------------------------------------------------------------------------
+template <int C, int MH, int MW>
+__global__ void __launch_bounds__(C * MW) spec_fwd_kernel(const int8_t* __restrict__ codes, int H,
+                                                          int W, int HB, float s, int zp,
+                                                          const float2* __restrict__ twf_w,
+                                                          const float2* __restrict__ twf_h,
+                                                          float2* __restrict__ xpart) {
+    constexpr int kThr = C * MW;
+    extern __shared__ float smem_f[];
+    float* sx = smem_f;                                          // [W][C]
+    float2* stw = reinterpret_cast<float2*>(smem_f + W * C);     // [MW][W]
+    const int hb = blockIdx.x, b = blockIdx.y;
+    const int nHB = gridDim.x;
+    for (int i = threadIdx.x; i < MW * W; i += kThr) stw[i] = twf_w[i];
+    const int c = threadIdx.x % C, kw = threadIdx.x / C;
+    float2 acc[MH];
+#pragma unroll
+    for (int kh = 0; kh < MH; ++kh) acc[kh] = make_float2(0.f, 0.f);
+    const float zpf = static_cast<float>(zp);
+    const int8_t* src_b = codes + static_cast<int64_t>(b) * H * W * C;
+    for (int r = 0; r < HB; ++r) {
+        const int h = hb * HB + r;
+        __syncthreads();
+        const int4* row = reinterpret_cast<const int4*>(src_b + static_cast<int64_t>(h) * W * C);
+        for (int i = threadIdx.x; i < W * C / 16; i += kThr) {
+            int4 v = row[i];
+            const int8_t* q = reinterpret_cast<const int8_t*>(&v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                sx[i * 16 + j] = __fmul_rn(__fsub_rn(static_cast<float>(q[j]), zpf), s);
+        }
+        __syncthreads();
+        float fr = 0.f, fi = 0.f;
+        const float2* t = stw + kw * W;
+        for (int w = 0; w < W; ++w) {
+            const float xv = sx[w * C + c];
+            const float2 tw = t[w];
+            fr = fmaf(xv, tw.x, fr);
+            fi = fmaf(xv, tw.y, fi);
+        }
+        const float2* eh = twf_h + h * MH;
+#pragma unroll
+        for (int kh = 0; kh < MH; ++kh) {
+            const float2 e = __ldg(eh + kh);
+            acc[kh].x = fmaf(fr, e.x, fmaf(-fi, e.y, acc[kh].x));
+            acc[kh].y = fmaf(fr, e.y, fmaf(fi, e.x, acc[kh].y));
+        }
+    }
+    // xpart[b][hb][kh][kw][c]
+    float2* dst = xpart + (static_cast<int64_t>(b) * nHB + hb) * (MH * MW * C);
+#pragma unroll
+    for (int kh = 0; kh < MH; ++kh) dst[(kh * MW + kw) * C + c] = acc[kh];
+}
+
+// ---------------------------------------------------------------------------
+// spec_mix: grid (MH*MW, ceil(B / SB)), 256 threads.  Y[b][m][o] = sum_i X[b][m][i] W[m][i][o]
+// with X = sum over the row-block partials (fixed order) and W re-laid as [m][i][o].
+// ---------------------------------------------------------------------------
+template <int C, int MH, int MW>
+__global__ void __launch_bounds__(256) spec_mix_kernel(const float2* __restrict__ xpart, int nHB,
+                                                       int B, int SB,
+                                                       const float2* __restrict__ wspec,
+                                                       float2* __restrict__ Y) {
+    constexpr int M = MH * MW;
+    __shared__ float2 sw[C * C];
+    __shared__ float2 sx[256 / C][C];
+    const int m = blockIdx.x;
+    for (int i = threadIdx.x; i < C * C; i += 256) sw[i] = wspec[static_cast<int64_t>(m) * C * C + i];
+    constexpr int kLanes = 256 / C;  // samples processed at once
+    const int o = threadIdx.x % C, sl = threadIdx.x / C;
+    const int b0 = blockIdx.y * SB;
+    const int b1 = min(B, b0 + SB);
+    for (int bb = b0; bb < b1; bb += kLanes) {
+        __syncthreads();
+        const int b = bb + sl;
+        if (b < b1) {
+            float2 s = make_float2(0.f, 0.f);
+            for (int hb = 0; hb < nHB; ++hb) {
+                const float2 v = xpart[((static_cast<int64_t>(b) * nHB + hb) * M + m) * C + o];
+                s.x += v.x;
+                s.y += v.y;
+            }
+            sx[sl][o] = s;
+        }
+        __syncthreads();
+        if (b < b1) {
+            float yr = 0.f, yi = 0.f;
+            for (int i = 0; i < C; ++i) {
+                const float2 xv = sx[sl][i];
+                const float2 wv = sw[i * C + o];
+                yr = fmaf(xv.x, wv.x, fmaf(-xv.y, wv.y, yr));
+                yi = fmaf(xv.x, wv.y, fmaf(xv.y, wv.x, yi));
+            }
+            Y[(static_cast<int64_t>(b) * M + m) * C + o] = make_float2(yr, yi);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// layer / projection: tcgen05 GEMM over 128-point tiles with fused epilogues.
+// ---------------------------------------------------------------------------
+constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA/TMEM, warps 4..11 epilogue
+constexpr int kEpiWarp0 = 4;
+
+template <int C, int MH, int MW, bool PROJ>
+struct LCfg {
+    static constexpr int kEpiWarps = PROJ ? 4 : 8;
+    static constexpr int kRowBytes = C;                   // 32 or 64 (SW32 / SW64)
+    static constexpr int kABytes = 128 * C;
+    static constexpr int kStages = 4;
+    static constexpr int kAccCols = ((C + 16 + 31) / 32) * 32;
+    static constexpr int kAccStages = 2;
+    static constexpr int kTmemCols = pow2ceil(kAccStages * kAccCols);
+    static constexpr int kCols = PROJ ? C : C / 2;        // columns per epilogue warp
+    static constexpr int kCh = kCols < 32 ? kCols : 32;   // columns per TMEM load
+    static constexpr int kRmax = 4;                       // rows per tile (W >= 32)
+    static constexpr int kOffW = 0;
+    static constexpr int kOffOnes = 4096 > C * C ? 4096 : C * C;
+    static constexpr int kOffA = kOffOnes + 1024;
+    static constexpr int kOffStage = kOffA + kStages * kABytes;
+    static constexpr int kStageBytes = 32 * (C / 2);      // one warp's half tile of codes
+    static constexpr int kOffY = kOffStage + 8 * 2 * 1024;
+    static constexpr int kYBytes = PROJ ? 0 : MH * MW * C * 8;
+    static constexpr int kOffT = kOffY + kYBytes;
+    static constexpr int kTBytes = PROJ ? 0 : kRmax * MW * C * 8;
+    static constexpr int kOffTw = kOffT + kTBytes;
+    static constexpr int kTwBytes = PROJ ? 0 : MW * 128 * 8;
+    static constexpr int kOffCol = kOffTw + kTwBytes;
+    static constexpr int kColBytes = 8 * C * 4 + 4 * 8 * C * 4;  // params + proj_out weights
+    static constexpr int kOffBars = kOffCol + kColBytes;
+    static constexpr int kSmemBytes = kOffBars + 8 * (2 * kStages + 2 * kAccStages + 1) + 16 + 1024;
+    static_assert(kSmemBytes <= 227 * 1024, "smem");
+};
+
+template <int C, int MH, int MW, bool PROJ>
+__global__ void __launch_bounds__(kThreads, 1)
+layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmOut,
+             const LayerArgs p) {
+    using L = LCfg<C, MH, MW, PROJ>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sW = smem + L::kOffW;
+    uint8_t* sOnes = smem + L::kOffOnes;
+    uint8_t* sA = smem + L::kOffA;
+    uint8_t* sStage = smem + L::kOffStage;
+    float2* sY = reinterpret_cast<float2*>(smem + L::kOffY);
+    float2* sT = reinterpret_cast<float2*>(smem + L::kOffT);
+    float2* sTw = reinterpret_cast<float2*>(smem + L::kOffTw);
+    float* sSWSA = reinterpret_cast<float*>(smem + L::kOffCol);  // sW[o] * s_in
+    int* sZpW = reinterpret_cast<int*>(sSWSA + C);
+    int* sZs = sZpW + C;                                          // zp_in * sum_w[o]
+    float* sBias = reinterpret_cast<float*>(sZs + C);
+    float* sWout = sBias + C;                                     // [out_ch][C] (PROJ)
+    float* sBout = sWout + 4 * C;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBars);
+    uint64_t* empty = full + L::kStages;
+    uint64_t* accFull = empty + L::kStages;
+    uint64_t* accEmpty = accFull + L::kAccStages;
+    uint64_t* epiBar = accEmpty + L::kAccStages;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(epiBar + 1);
+    volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int num_tiles = static_cast<int>((p.M + 127) / 128);
+    const int t_begin = static_cast<int>(static_cast<int64_t>(num_tiles) * blockIdx.x / gridDim.x);
+    const int t_end = static_cast<int>(static_cast<int64_t>(num_tiles) * (blockIdx.x + 1) / gridDim.x);
+
+    // ---- set-up
+    {
+        constexpr int kChunks = C / 16;
+        for (int idx = threadIdx.x; idx < C * kChunks; idx += kThreads) {
+            const int o = idx / kChunks, c = idx % kChunks;
+            const uint4 v = *reinterpret_cast<const uint4*>(p.Wq + o * C + c * 16);
+            *reinterpret_cast<uint4*>(sW + swz_offset(o * C + c * 16, C)) = v;
+        }
+        for (int idx = threadIdx.x; idx < 1024 / 16; idx += kThreads) {
+            const uint32_t one = (idx * 16 < C) ? 0x01010101u : 0u;  // row 0 = ones
+            *reinterpret_cast<uint4*>(sOnes + idx * 16) = make_uint4(one, one, one, one);
+        }
+        for (int o = threadIdx.x; o < C; o += kThreads) {
+            sSWSA[o] = __fmul_rn(p.scale_w[o], p.s_in);
+            sZpW[o] = p.zp_w[o];
+            sZs[o] = p.zp_in * p.sum_w[o];
+            sBias[o] = p.bias[o];
+        }
+        if (PROJ) {
+            for (int i = threadIdx.x; i < p.out_ch * C; i += kThreads) sWout[i] = p.w_out[i];
+            for (int i = threadIdx.x; i < p.out_ch; i += kThreads) sBout[i] = p.b_out[i];
+        } else {
+            for (int i = threadIdx.x; i < MW * p.W; i += kThreads) sTw[i] = p.twi_w[i];
+        }
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < L::kStages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            for (int s = 0; s < L::kAccStages; ++s) {
+                mbar_init(&accFull[s], 1);
+                mbar_init(&accEmpty[s], L::kEpiWarps);
+            }
+            mbar_init(epiBar, L::kEpiWarps * 32);
+            *sAbort = 0;
+            fence_mbar_init();
+        }
+        if (warp == 1) tmem_alloc(sTmem, L::kTmemCols);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    const uint32_t tmem_base = *sTmem;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            prefetch_tmap(&tmIn);
+            int it = 0;
+            for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+                const int s = it % L::kStages;
+                const uint32_t ph = (it / L::kStages) & 1;
+                if (!mbar_wait(&empty[s], ph ^ 1, sAbort)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitSlotFree);
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], L::kABytes);
+                tma_load_2d(sA + s * L::kABytes, &tmIn, &full[s], 0, tile * 128);
+            }
+            for (int j = (it > L::kStages ? it - L::kStages : 0); j < it; ++j)
+                if (!mbar_wait(&full[j % L::kStages], (j / L::kStages) & 1, sAbort)) break;
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (elect_one()) {
+            int it = 0;
+            for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+                const int s = it % L::kStages;
+                const uint32_t ph = (it / L::kStages) & 1;
+                const int a = it % L::kAccStages;
+                const uint32_t aph = (it / L::kAccStages) & 1;
+                if (!mbar_wait(&accEmpty[a], aph ^ 1, sAbort)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitAccFree);
+                    break;
+                }
+                if (!mbar_wait(&full[s], ph, sAbort)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitTmaFull);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + a * L::kAccCols;
+                const uint32_t aBase = smem_u32(sA + s * L::kABytes);
+#pragma unroll
+                for (int kk = 0; kk < C / 32; ++kk) {
+                    const uint64_t ad = umma_desc(aBase + kk * 32, C);
+                    const uint64_t wd = umma_desc(smem_u32(sW) + kk * 32, C);
+                    const uint64_t od = umma_desc(smem_u32(sOnes) + kk * 32, C);
+                    mma_i8(d, ad, wd, idesc_i8(C), kk > 0 ? 1u : 0u);
+                    mma_i8(d + C, ad, od, idesc_i8(16), kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&empty[s]);
+                mma_commit(&accFull[a]);
+            }
+            if (it > 0) {
+                const int j = it - 1;
+                mbar_wait(&accFull[j % L::kAccStages], (j / L::kAccStages) & 1, sAbort);
+            }
+        }
+        __syncwarp();
+    } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + L::kEpiWarps) {
+        const int ew = warp - kEpiWarp0;
+        const int etid = ew * 32 + lane;
+        constexpr int kEpiThreads = L::kEpiWarps * 32;
+        const int quad = warp & 3;
+        const int col0 = PROJ ? 0 : (ew >> 2) * L::kCols;
+        const int row = quad * 32 + lane;  // row of the 128-point tile
+        const int P = p.H * p.W;
+        const int R = 128 / p.W > 0 ? 128 / p.W : 1;
+        const float zpo = static_cast<float>(p.fq_out.zp);
+        int cached_b = -1;
+        int it = 0, nstore = 0;
+        uint32_t nsync = 0;
+        // all epilogue threads meet here; bounded, so a missing peer turns into an abort
+        auto epi_sync = [&]() -> bool {
+            mbar_arrive(epiBar);
+            const bool ok = mbar_wait(epiBar, nsync & 1u, sAbort);
+            ++nsync;
+            return ok;
+        };
+        bool epi_ok = true;
+        for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+            const int64_t g0 = static_cast<int64_t>(tile) * 128;
+            const int b = static_cast<int>(g0 / P);
+            const int p0 = static_cast<int>(g0 % P);
+            if (!PROJ) {
+                // inverse transform along H for this tile's rows: T[r][kw][o]
+                if (b != cached_b) {
+                    const float4* src = reinterpret_cast<const float4*>(
+                        p.Y + static_cast<int64_t>(b) * MH * MW * C);
+                    float4* dst = reinterpret_cast<float4*>(sY);
+                    for (int i = etid; i < MH * MW * C / 2; i += kEpiThreads) dst[i] = src[i];
+                    cached_b = b;
+                    if (!epi_sync()) {
+                        epi_ok = false;
+                        break;
+                    }
+                }
+                const int h0 = p0 / p.W;
+                for (int idx = etid; idx < R * MW * C; idx += kEpiThreads) {
+                    const int r = idx / (MW * C), rem = idx % (MW * C);
+                    const int kw = rem / C, o = rem % C;
+                    const float2* eh = p.twi_h + (h0 + r) * MH;
+                    float tr = 0.f, ti = 0.f;
+#pragma unroll
+                    for (int kh = 0; kh < MH; ++kh) {
+                        const float2 y = sY[(kh * MW + kw) * C + o];
+                        const float2 e = __ldg(eh + kh);
+                        tr = fmaf(y.x, e.x, fmaf(-y.y, e.y, tr));
+                        ti = fmaf(y.x, e.y, fmaf(y.y, e.x, ti));
+                    }
+                    sT[idx] = make_float2(tr, ti);
+                }
+                if (!epi_sync()) {
+                    epi_ok = false;
+                    break;
+                }
+            }
+            const int a = it % L::kAccStages;
+            const uint32_t aph = (it / L::kAccStages) & 1;
+            if (!mbar_wait(&accFull[a], aph, sAbort)) {
+                *sAbort = 1;
+                atomicOr(p.err, kErrWaitAccFull);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * L::kAccCols;
+            uint32_t sum_u;
+            tmem_ld1(tbase + C, sum_u);
+            tmem_wait_ld();
+            const int rconst = C * p.zp_in - 2 * static_cast<int>(sum_u);
+            // this point's position inside the tile's rows and its W twiddles
+            const int pr = (p0 % p.W + row) / p.W;           // local row index
+            const int pw = (p0 + row) % p.W;
+            float2 ew_reg[MW];
+            if (!PROJ) {
+#pragma unroll
+                for (int kw = 0; kw < MW; ++kw) ew_reg[kw] = sTw[kw * p.W + pw];
+            }
+            float acc_out[4] = {0.f, 0.f, 0.f, 0.f};
+            if (PROJ) {
+                for (int j = 0; j < p.out_ch; ++j) acc_out[j] = sBout[j];
+            }
+#pragma unroll 1
+            for (int c0 = col0; c0 < col0 + L::kCols; c0 += L::kCh) {
+                uint32_t raw[32];
+                if constexpr (L::kCh == 32) {
+                    tmem_ld32(tbase + c0, raw);
+                } else {
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                        : "=r"(raw[0]), "=r"(raw[1]), "=r"(raw[2]), "=r"(raw[3]), "=r"(raw[4]),
+                          "=r"(raw[5]), "=r"(raw[6]), "=r"(raw[7]), "=r"(raw[8]), "=r"(raw[9]),
+                          "=r"(raw[10]), "=r"(raw[11]), "=r"(raw[12]), "=r"(raw[13]),
+                          "=r"(raw[14]), "=r"(raw[15])
+                        : "r"(tbase + c0));
+                }
+                tmem_wait_ld();
+                if (c0 + L::kCh >= col0 + L::kCols) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&accEmpty[a]);
+                }
+                if constexpr (PROJ) {
+#pragma unroll
+                    for (int j = 0; j < L::kCh; ++j) {
+                        const int o = c0 + j;
+                        float v = dequant_ref(static_cast<int>(raw[j]), sZpW[o], rconst, sZs[o], sSWSA[o]);
+                        v = __fadd_rn(v, sBias[o]);
+                        v = apply_fq(v, p.fq_out);
+                        v = activation(v, p.act);
+                        for (int jj = 0; jj < p.out_ch; ++jj)
+                            acc_out[jj] = __fmaf_rn(v, sWout[jj * C + o], acc_out[jj]);
+                    }
+                } else {
+                    uint32_t packed[8];
+#pragma unroll
+                    for (int j = 0; j < L::kCh; ++j) {
+                        const int o = c0 + j;
+                        // x1: inverse W-axis transform of T at this point
+                        const float2* trow = sT + (pr * MW) * C + o;
+                        float x1 = 0.f;
+#pragma unroll
+                        for (int kw = 0; kw < MW; ++kw) {
+                            const float2 t = trow[kw * C];
+                            x1 = fmaf(t.x, ew_reg[kw].x, fmaf(-t.y, ew_reg[kw].y, x1));
+                        }
+                        float v = dequant_ref(static_cast<int>(raw[j]), sZpW[o], rconst, sZs[o], sSWSA[o]);
+                        v = __fadd_rn(v, sBias[o]);
+                        const float x2 = fake_quant(v, p.fq_out.scale, zpo);
+                        const float z = __fadd_rn(x1, x2);
+                        const float hval = activation(z, p.act);
+                        const int code = static_cast<int>(fq_code(hval, p.fq_out.scale, zpo));
+                        const uint32_t byte = static_cast<uint32_t>(code) & 0xFFu;
+                        if ((j & 3) == 0) packed[j >> 2] = byte;
+                        else packed[j >> 2] |= byte << (8 * (j & 3));
+                    }
+                    uint8_t* buf = sStage + (ew * 2 + (nstore & 1)) * 1024;
+                    if (nstore >= 2) {
+                        if (lane == 0) tma_store_wait_read<1>();
+                        __syncwarp();
+                    }
+                    constexpr int kRow = L::kCh;  // bytes per row of this warp's half tile
+#pragma unroll
+                    for (int j16 = 0; j16 < kRow / 16; ++j16) {
+                        const uint32_t off = (kRow == 32) ? swz_offset(lane * 32 + j16 * 16, 32)
+                                                          : static_cast<uint32_t>(lane * 16);
+                        *reinterpret_cast<uint4*>(buf + off) =
+                            make_uint4(packed[4 * j16], packed[4 * j16 + 1], packed[4 * j16 + 2],
+                                       packed[4 * j16 + 3]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmOut, buf, c0, static_cast<int>(g0) + quad * 32);
+                        tma_store_commit();
+                    }
+                    ++nstore;
+                }
+            }
+            if (PROJ) {
+                const int64_t m = g0 + row;
+                if (m < p.M) {
+                    for (int j = 0; j < p.out_ch; ++j)
+                        p.y[m * p.out_ch + j] = apply_fq(acc_out[j], p.fq_final);
+                }
+            } else {
+                // every epilogue thread is done with sT before the next tile rewrites it
+                if (!epi_sync()) {
+                    epi_ok = false;
+                    break;
+                }
+            }
+        }
+        if (!epi_ok) {
+            *sAbort = 1;
+            atomicOr(p.err, kErrWaitDrain);
+        }
+        if (lane == 0) tma_store_wait_all<0>();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, L::kTmemCols);
+    }
+}
+
+template <typename Kern>
+cudaError_t set_smem(Kern k, int bytes) {
+    return set_max_dynamic_smem(reinterpret_cast<const void*>(k), bytes);
+}
+
+template <int C, int MH, int MW>
+cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
+    cudaError_t e;
+    const int64_t M = static_cast<int64_t>(pl.B) * pl.H * pl.W;
+    // lift
+    {
+        const int64_t blocks64 = (M + 255) / 256;
+        const int grid = static_cast<int>(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
+        lift_kernel<C><<<grid, 256, 0, st>>>(pl.x, M, pl.in_ch, pl.lift_w, pl.lift_b,
+                                             pl.lift_s, pl.lift_zp, pl.codes[0]);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    const int sms = device_sm_count();
+    const int num_tiles = static_cast<int>((M + 127) / 128);
+    const int grid_l = num_tiles < sms ? num_tiles : sms;
+    int cur = 0;
+    for (int i = 0; i < pl.L; ++i) {
+        const int nHB = pl.H / pl.HB;
+        const int sm_fwd = (pl.W * C + MW * pl.W * 2) * 4;
+        {
+            auto k = spec_fwd_kernel<C, MH, MW>;
+            if ((e = set_smem(k, sm_fwd)) != cudaSuccess) return e;
+            k<<<dim3(nHB, pl.B), C * MW, sm_fwd, st>>>(pl.codes[cur], pl.H, pl.W, pl.HB,
+                                                    pl.layer[i].s_in, pl.layer[i].zp_in,
+                                                    pl.twf_w, pl.twf_h, pl.xpart);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        }
+        {
+            const int SB = 32;
+            spec_mix_kernel<C, MH, MW><<<dim3(MH * MW, (pl.B + SB - 1) / SB), 256, 0, st>>>(
+                pl.xpart, nHB, pl.B, SB, pl.layer[i].wspec, pl.Y);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        }
+        {
+            using LC = LCfg<C, MH, MW, false>;
+            auto k = layer_kernel<C, MH, MW, false>;
+            if ((e = set_smem(k, LC::kSmemBytes)) != cudaSuccess) return e;
+            CUtensorMap tin, tout;
+            if (!encode_2d(&tin, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur], C, M, C, C, 128, C) ||
+                !encode_2d(&tout, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur ^ 1], C, M, C, C / 2,
+                           32, C / 2 == 32 ? 32 : 0))
+                return cudaErrorInvalidValue;
+            LayerArgs a = pl.layer[i].args;
+            a.M = M;
+            a.H = pl.H;
+            a.W = pl.W;
+            a.Y = pl.Y;
+            a.twi_w = pl.twi_w;
+            a.twi_h = pl.twi_h;
+            a.err = pl.err;
+            k<<<grid_l, kThreads, LC::kSmemBytes, st>>>(tin, tout, a);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        }
+        cur ^= 1;
+    }
+    {
+        using LC = LCfg<C, MH, MW, true>;
+        auto k = layer_kernel<C, MH, MW, true>;
+        if ((e = set_smem(k, LC::kSmemBytes)) != cudaSuccess) return e;
+        CUtensorMap tin;
+        if (!encode_2d(&tin, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur], C, M, C, C, 128, C))
+            return cudaErrorInvalidValue;
+        LayerArgs a = pl.proj;
+        a.M = M;
+        a.H = pl.H;
+        a.W = pl.W;
+        a.err = pl.err;
+        a.y = pl.y;
+        k<<<grid_l, kThreads, LC::kSmemBytes, st>>>(tin, tin, a);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace
+
+bool fno2d_supported(int C, int MH, int MW) {
+    return C == 64 && MH == 12 && MW == 12;
+}
+
+cudaError_t fno2d_run(const Fno2dPlan& pl, cudaStream_t st) {
+    if (pl.C == 64 && pl.MH == 12 && pl.MW == 12) return run_layers<64, 12, 12>(pl, st);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace nfx

@@ -1,0 +1,79 @@
+// fno2d.h -- host/device interface of the FNO2d INT8 executor (fno2d.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace nfx {
+
+// Fake-quant applied at an ".output" boundary: kind 0 none, 1 INT8 per-tensor,
+// 2 the reference FNO2d FP8 log2 snap (fno.cpp:813-828).
+struct FqParam {
+    int kind;
+    float scale;
+    int zp;
+};
+
+// Arguments of one tcgen05 layer launch (local 1x1 layer or the projection).
+struct LayerArgs {
+    // GEMM operands: weight codes (C, C), per-channel params
+    const int8_t* Wq;
+    const float* scale_w;
+    const int32_t* zp_w;
+    const int32_t* sum_w;
+    const float* bias;
+    float s_in;       // input activation qparams (the layer-input key)
+    int zp_in;
+    FqParam fq_out;   // locs.i.output (layer) / proj_q.output (projection)
+    FqParam fq_final; // proj_out.output (projection only)
+    int act;          // 0 GELU (tanh form), 1 ReLU
+    // spectral branch (layer only)
+    const float2* Y;      // (B, MH*MW, C) mixed spectrum
+    const float2* twi_w;  // (MW, W)  f_kw * e^{+2 pi i kw w / W} / W
+    const float2* twi_h;  // (H, MH)  e^{+2 pi i kh h / H} / H
+    // projection only
+    const float* w_out;   // (out_ch, C) proj_out weight (fake-quantised at load)
+    const float* b_out;   // (out_ch,)
+    int out_ch;
+    float* y;             // (M, out_ch)
+    // geometry
+    int64_t M;
+    int H, W;
+    unsigned* err;
+};
+
+struct Fno2dLayerPlan {
+    float s_in;
+    int zp_in;
+    const float2* wspec;  // (MH*MW, C, C) complex, [mode][in][out]
+    LayerArgs args;
+};
+
+constexpr int kFno2dMaxLayers = 8;
+
+// Everything one forward pass needs (device pointers).
+struct Fno2dPlan {
+    int B, H, W, C, MH, MW, L, in_ch, HB;
+    const float* x;        // (B, H, W, in_ch)
+    float* y;              // (B, H, W, out_ch)
+    const float* lift_w;   // (C, in_ch)
+    const float* lift_b;   // (C,)
+    float lift_s;
+    int lift_zp;
+    int8_t* codes[2];      // ping-pong (B*H*W, C)
+    float2* xpart;         // (B, H/HB, MH*MW, C)
+    float2* Y;             // (B, MH*MW, C)
+    const float2* twf_w;   // (MW, W)  e^{-2 pi i kw w / W}
+    const float2* twf_h;   // (H, MH)  e^{-2 pi i kh h / H}
+    const float2* twi_w;
+    const float2* twi_h;
+    Fno2dLayerPlan layer[kFno2dMaxLayers];
+    LayerArgs proj;
+    unsigned* err;
+};
+
+bool fno2d_supported(int C, int MH, int MW);
+cudaError_t fno2d_run(const Fno2dPlan& plan, cudaStream_t stream);
+
+}  // namespace nfx

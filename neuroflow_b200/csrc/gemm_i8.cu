@@ -320,15 +320,8 @@ cudaError_t launch(const GemmArgs& p, const CUtensorMap& tmA, const CUtensorMap&
                    cudaStream_t stream) {
     using C = Cfg<K, N>;
     auto kern = gemm_i8_kernel<K, N>;
-    static unsigned attr_set = 0;  // one bit per device ordinal (< 32)
-    const int dev = current_device();
-    if (dev < 0 || dev >= 32) return cudaErrorInvalidDevice;
-    if (!(attr_set & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             C::kSmemBytes);
-        if (e != cudaSuccess) return e;
-        attr_set |= 1u << dev;
-    }
+    cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(kern), C::kSmemBytes);
+    if (e != cudaSuccess) return e;
     const int tiles = (p.M + 127) / 128;
     const int grid = tiles < num_sms ? tiles : num_sms;
     kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tmA, tmC, p);

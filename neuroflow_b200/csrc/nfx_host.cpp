@@ -4,7 +4,9 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "nfx_internal.h"
 
@@ -65,6 +67,19 @@ unsigned* device_error_word() {
         g_err[d] = static_cast<unsigned*>(p);
     }
     return g_err[d];
+}
+
+cudaError_t set_max_dynamic_smem(const void* kernel, int bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> done;
+    const int d = current_device();
+    std::lock_guard<std::mutex> lk(mu);
+    auto key = std::make_pair(kernel, d);
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= bytes) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done[key] = bytes;
+    return e;
 }
 
 bool encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,

@@ -34,6 +34,8 @@ cudaError_t gemm_i8_launch(const GemmArgs& p, int K, int N, cudaStream_t stream)
 int current_device();
 int device_sm_count();
 unsigned* device_error_word();  // per current device, allocated once
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device).
+cudaError_t set_max_dynamic_smem(const void* kernel, int bytes);
 // Encode a 2-D row-major tensor map (inner dimension first).  Returns false on error.
 bool encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
                uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,

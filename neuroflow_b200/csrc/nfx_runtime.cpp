@@ -1,0 +1,453 @@
+// nfx_runtime.cpp -- the runtime handle behind nfx_runtime_* (include/nfx.h): the
+// device-side counterpart of the reference InferenceRuntime (runtime.cpp:21-171).
+//
+// Create loads the IR on the host, applies the load-time weight fake-quant
+// (fno.cpp:997-1020 -> DequantiseWeight), and uploads the weights once.
+// EnableInt8Gemm builds the per-channel weight codes (QuantiseWeight2D) and enables
+// the INT8 executor.  Run/RunDevice validate shapes like FNO2d::Forward
+// (fno.cpp:778-794) and launch the executor on the handle's device.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/nfx.h"
+#include "fno2d.h"
+#include "nfx_internal.h"
+#include "nfx_ir.h"
+
+namespace nfx {
+int set_thread_error(int code, const std::string& msg);
+}
+
+struct nfx_runtime {
+    int device = 0;
+    nfx::IrModel model;
+    std::string err;
+    bool int8_enabled = false;
+    cudaStream_t stream = nullptr;  // used by the synchronous host-buffer Run
+    std::vector<void*> allocs;      // weights and tables (freed at destroy)
+    // FNO2d state
+    nfx::Fno2dPlan plan{};
+    int max_B = 0;                  // capacity of the activation buffers
+    int buf_H = 0, buf_W = 0;
+    void* act_bufs[4] = {nullptr, nullptr, nullptr, nullptr};
+    float* dx = nullptr;            // host-Run staging (device side)
+    float* dy = nullptr;
+    size_t dx_cap = 0, dy_cap = 0;
+    float2* tw[4] = {nullptr, nullptr, nullptr, nullptr};  // twf_w, twf_h, twi_w, twi_h
+    int tw_H = 0, tw_W = 0;
+};
+
+namespace {
+
+int rt_fail(nfx_runtime* rt, int code, const std::string& m) {
+    if (rt) rt->err = m;
+    return code;
+}
+
+bool cuda_ok(nfx_runtime* rt, cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return true;
+    rt->err = std::string(what) + ": " + cudaGetErrorString(e);
+    return false;
+}
+
+template <typename T>
+T* upload(nfx_runtime* rt, const T* host, size_t count) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, count * sizeof(T) + 16) != cudaSuccess) return nullptr;
+    rt->allocs.push_back(p);
+    if (count && cudaMemcpy(p, host, count * sizeof(T), cudaMemcpyHostToDevice) != cudaSuccess)
+        return nullptr;
+    return static_cast<T*>(p);
+}
+
+nfx::FqParam fq_for(const nfx::IrModel& m, const std::string& key) {
+    nfx::FqParam f{0, 1.0f, 0};
+    if (!m.quant_enabled) return f;
+    auto it8 = m.activation_fp8_qparams.find(key);
+    if (it8 != m.activation_fp8_qparams.end()) {
+        f.kind = 2;
+        f.scale = it8->second;
+        return f;
+    }
+    auto it = m.activation_qparams.find(key);
+    if (it != m.activation_qparams.end()) {
+        f.kind = 1;
+        f.scale = it->second.scale;
+        f.zp = it->second.zero_point;
+    }
+    return f;
+}
+
+const float* wptr(nfx_runtime* rt, const std::string& name) {
+    const auto& t = rt->model.weights.at(name);
+    return upload(rt, t.data.data(), t.data.size());
+}
+
+// FNO2d config block (ir_loader.h:147-155)
+struct F2 {
+    int in_ch, out_ch, width, mh, mw, L, pad;
+};
+F2 fno2d_cfg(const nfx::IrModel& m) {
+    return F2{m.cfg[0], m.cfg[1], m.cfg[2], m.cfg[3], m.cfg[4], m.cfg[5], m.cfg[6]};
+}
+
+int fno2d_create(nfx_runtime* rt) {
+    auto& m = rt->model;
+    const F2 c = fno2d_cfg(m);
+    if (m.quant_enabled) {
+        for (const auto& name : m.weight_order) nfx::dequantise_weight(m.weights[name], m, name);
+    }
+    if (!nfx::fno2d_supported(c.width, c.mh, c.mw)) return NFX_OK;  // Run reports UnsupportedOp
+    auto& pl = rt->plan;
+    pl.C = c.width;
+    pl.MH = c.mh;
+    pl.MW = c.mw;
+    pl.L = c.L;
+    pl.in_ch = c.in_ch;
+    pl.lift_w = wptr(rt, "lift.weight");
+    pl.lift_b = wptr(rt, "lift.bias");
+    if (!pl.lift_w || !pl.lift_b) return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+    for (int i = 0; i < c.L && i < nfx::kFno2dMaxLayers; ++i) {
+        // spectral weights (in, out, mh, mw) real/imag -> [mode][in][out] complex
+        const auto& wr = m.weights.at("specs." + std::to_string(i) + ".weights_real");
+        const auto& wi = m.weights.at("specs." + std::to_string(i) + ".weights_imag");
+        const int C = c.width, M = c.mh * c.mw;
+        std::vector<float> packed(static_cast<size_t>(M) * C * C * 2);
+        for (int in = 0; in < C; ++in)
+            for (int o = 0; o < C; ++o)
+                for (int md = 0; md < M; ++md) {
+                    const size_t src = (static_cast<size_t>(in) * C + o) * M + md;
+                    const size_t dst = ((static_cast<size_t>(md) * C + in) * C + o) * 2;
+                    packed[dst] = wr.data[src];
+                    packed[dst + 1] = wi.data[src];
+                }
+        pl.layer[i].wspec = reinterpret_cast<const float2*>(upload(rt, packed.data(), packed.size()));
+        auto& a = pl.layer[i].args;
+        a.bias = wptr(rt, "locs." + std::to_string(i) + ".bias");
+        if (!pl.layer[i].wspec || !a.bias) return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+    }
+    pl.proj.bias = wptr(rt, "proj_q.bias");
+    pl.proj.w_out = wptr(rt, "proj_out.weight");
+    pl.proj.b_out = wptr(rt, "proj_out.bias");
+    pl.proj.out_ch = c.out_ch;
+    if (!pl.proj.bias || !pl.proj.w_out || !pl.proj.b_out)
+        return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+    return NFX_OK;
+}
+
+// EnableInt8Gemm for FNO2d: every locs.i and proj_q needs per-channel (axis 0) weight
+// qparams, and every layer input key needs per-tensor INT8 activation qparams.
+void fno2d_enable_int8(nfx_runtime* rt) {
+    auto& m = rt->model;
+    const F2 c = fno2d_cfg(m);
+    if (!m.quant_enabled || !nfx::fno2d_supported(c.width, c.mh, c.mw) || c.L > nfx::kFno2dMaxLayers)
+        return;
+    if (c.out_ch < 1 || c.out_ch > 4 || c.in_ch < 1 || c.in_ch > 8) return;
+    auto act_key = [](int i) { return i == 0 ? std::string("lift.output")
+                                             : "locs." + std::to_string(i - 1) + ".output"; };
+    for (int i = 0; i <= c.L; ++i) {
+        if (!m.activation_qparams.count(act_key(i))) return;
+        if (m.activation_fp8_qparams.count(act_key(i))) return;
+    }
+    auto& pl = rt->plan;
+    for (int i = 0; i <= c.L; ++i) {
+        const std::string wname = i < c.L ? "locs." + std::to_string(i) + ".weight" : "proj_q.weight";
+        auto pc = m.weight_per_channel_qparams.find(wname);
+        if (pc == m.weight_per_channel_qparams.end()) return;
+        std::vector<int8_t> codes;
+        std::vector<int32_t> sum_w;
+        if (!nfx::quantise_weight_2d(m.weights.at(wname), pc->second, codes, sum_w)) return;
+        if (static_cast<int>(codes.size()) != c.width * c.width) return;
+        nfx::LayerArgs& a = i < c.L ? pl.layer[i].args : pl.proj;
+        a.Wq = upload(rt, codes.data(), codes.size());
+        a.scale_w = upload(rt, pc->second.scales.data(), static_cast<size_t>(c.width));
+        a.zp_w = upload(rt, pc->second.zero_points.data(), static_cast<size_t>(c.width));
+        a.sum_w = upload(rt, sum_w.data(), sum_w.size());
+        if (!a.Wq || !a.scale_w || !a.zp_w || !a.sum_w) return;
+        const nfx::QP in = m.activation_qparams.at(act_key(i));
+        a.s_in = in.scale;
+        a.zp_in = in.zero_point;
+        a.act = m.activation == "relu" ? 1 : 0;
+        if (i < c.L) {
+            pl.layer[i].s_in = in.scale;
+            pl.layer[i].zp_in = in.zero_point;
+            a.fq_out = fq_for(m, "locs." + std::to_string(i) + ".output");
+        } else {
+            a.fq_out = fq_for(m, "proj_q.output");
+            a.fq_final = fq_for(m, "proj_out.output");
+        }
+    }
+    const nfx::QP lq = m.activation_qparams.at("lift.output");
+    pl.lift_s = lq.scale;
+    pl.lift_zp = lq.zero_point;
+    rt->int8_enabled = true;
+}
+
+// Twiddle tables in double precision, rounded once to float.
+int ensure_twiddles(nfx_runtime* rt, int H, int W) {
+    if (rt->tw_H == H && rt->tw_W == W) return NFX_OK;
+    const int MH = rt->plan.MH, MW = rt->plan.MW;
+    std::vector<float> fw(2 * MW * W), fh(2 * H * MH), iw(2 * MW * W), ih(2 * H * MH);
+    const double two_pi = 6.283185307179586476925286766559;
+    for (int k = 0; k < MW; ++k)
+        for (int w = 0; w < W; ++w) {
+            const double a = two_pi * static_cast<double>((static_cast<int64_t>(k) * w) % W) / W;
+            const double f = (k == 0 || 2 * k == W) ? 1.0 : 2.0;
+            fw[2 * (k * W + w)] = static_cast<float>(std::cos(a));
+            fw[2 * (k * W + w) + 1] = static_cast<float>(-std::sin(a));
+            iw[2 * (k * W + w)] = static_cast<float>(f * std::cos(a) / W);
+            iw[2 * (k * W + w) + 1] = static_cast<float>(f * std::sin(a) / W);
+        }
+    for (int h = 0; h < H; ++h)
+        for (int k = 0; k < MH; ++k) {
+            const double a = two_pi * static_cast<double>((static_cast<int64_t>(k) * h) % H) / H;
+            fh[2 * (h * MH + k)] = static_cast<float>(std::cos(a));
+            fh[2 * (h * MH + k) + 1] = static_cast<float>(-std::sin(a));
+            ih[2 * (h * MH + k)] = static_cast<float>(std::cos(a) / H);
+            ih[2 * (h * MH + k) + 1] = static_cast<float>(std::sin(a) / H);
+        }
+    for (auto*& p : rt->tw) {
+        if (p) cudaFree(p);
+        p = nullptr;
+    }
+    const std::vector<float>* src[4] = {&fw, &fh, &iw, &ih};
+    for (int i = 0; i < 4; ++i) {
+        void* p = nullptr;
+        if (!cuda_ok(rt, cudaMalloc(&p, src[i]->size() * 4), "cudaMalloc")) return NFX_INTERNAL;
+        rt->tw[i] = static_cast<float2*>(p);
+        if (!cuda_ok(rt, cudaMemcpy(p, src[i]->data(), src[i]->size() * 4, cudaMemcpyHostToDevice),
+                     "cudaMemcpy"))
+            return NFX_INTERNAL;
+    }
+    rt->tw_H = H;
+    rt->tw_W = W;
+    return NFX_OK;
+}
+
+int ensure_buffers(nfx_runtime* rt, int B, int H, int W) {
+    if (B <= rt->max_B && H == rt->buf_H && W == rt->buf_W) return NFX_OK;
+    for (auto*& p : rt->act_bufs) {
+        if (p) cudaFree(p);
+        p = nullptr;
+    }
+    const auto& pl = rt->plan;
+    const size_t M = static_cast<size_t>(B) * H * W;
+    const int nHB = H < 8 ? H : 8;
+    const size_t sizes[4] = {M * pl.C, M * pl.C,
+                             static_cast<size_t>(B) * nHB * pl.MH * pl.MW * pl.C * sizeof(float2),
+                             static_cast<size_t>(B) * pl.MH * pl.MW * pl.C * sizeof(float2)};
+    for (int i = 0; i < 4; ++i)
+        if (!cuda_ok(rt, cudaMalloc(&rt->act_bufs[i], sizes[i] + 256), "cudaMalloc activations"))
+            return NFX_INTERNAL;
+    rt->max_B = B;
+    rt->buf_H = H;
+    rt->buf_W = W;
+    return NFX_OK;
+}
+
+int check_fno2d_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t* ys, int yr) {
+    const F2 c = fno2d_cfg(rt->model);
+    if (xr != 4) return rt_fail(rt, NFX_SHAPE_MISMATCH, "expected 4D input (batch, h, w, in_ch)");
+    if (xs[3] != c.in_ch) return rt_fail(rt, NFX_SHAPE_MISMATCH, "input channels mismatch");
+    if (yr != 4 || ys[0] != xs[0] || ys[1] != xs[1] || ys[2] != xs[2] || ys[3] != c.out_ch)
+        return rt_fail(rt, NFX_SHAPE_MISMATCH, "output buffer shape mismatch");
+    auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
+    if (!pow2(xs[1]) || !pow2(xs[2]))
+        return rt_fail(rt, NFX_INVALID_ARG, "FNO2d: H and W must each be a power of two");
+    return NFX_OK;
+}
+
+int fno2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
+    const F2 c = fno2d_cfg(rt->model);
+    if (!nfx::fno2d_supported(c.width, c.mh, c.mw))
+        return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                       "FNO2d on the GPU runtime supports width 64 with 12x12 modes");
+    if (!rt->int8_enabled)
+        return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                       "FNO2d on the GPU runtime runs the INT8 path: call EnableInt8Gemm() on an "
+                       "IR with per-channel weight and per-tensor activation qparams");
+    const int B = static_cast<int>(xs[0]), H = static_cast<int>(xs[1]), W = static_cast<int>(xs[2]);
+    if (B == 0) return NFX_OK;
+    if (W < 32 || W > 128 || H < 8 || H > 4096 || c.mh > H || c.mw > W / 2 + 1)
+        return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                       "FNO2d GPU executor: needs 32 <= W <= 128, H >= 8, modes within the grid");
+    if (c.pad > 1 && ((H % c.pad) || (W % c.pad)))
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, "FNO2d GPU executor: padding is not supported");
+    int s = ensure_twiddles(rt, H, W);
+    if (s != NFX_OK) return s;
+    s = ensure_buffers(rt, B, H, W);
+    if (s != NFX_OK) return s;
+    nfx::Fno2dPlan pl = rt->plan;
+    pl.B = B;
+    pl.H = H;
+    pl.W = W;
+    pl.HB = H / (H < 8 ? H : 8);
+    pl.x = dx;
+    pl.y = dy;
+    pl.codes[0] = static_cast<int8_t*>(rt->act_bufs[0]);
+    pl.codes[1] = static_cast<int8_t*>(rt->act_bufs[1]);
+    pl.xpart = static_cast<float2*>(rt->act_bufs[2]);
+    pl.Y = static_cast<float2*>(rt->act_bufs[3]);
+    pl.twf_w = rt->tw[0];
+    pl.twf_h = rt->tw[1];
+    pl.twi_w = rt->tw[2];
+    pl.twi_h = rt->tw[3];
+    pl.err = nfx::device_error_word();
+    if (!pl.err) return rt_fail(rt, NFX_INTERNAL, "no device error word");
+    const cudaError_t e = nfx::fno2d_run(pl, st);
+    if (e != cudaSuccess)
+        return rt_fail(rt, NFX_INTERNAL, std::string("FNO2d launch failed: ") + cudaGetErrorString(e));
+    return NFX_OK;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int d) {
+        cudaGetDevice(&prev);
+        if (prev != d) cudaSetDevice(d);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int64_t numel(const int64_t* s, int r) {
+    int64_t n = 1;
+    for (int i = 0; i < r; ++i) n *= s[i];
+    return n;
+}
+
+}  // namespace
+
+extern "C" {
+
+int nfx_runtime_create(const char* ir_path, int device, nfx_runtime** out) {
+    if (!out) return nfx::set_thread_error(NFX_INVALID_ARG, "nfx_runtime_create: out is NULL");
+    *out = nullptr;
+    if (!ir_path) return nfx::set_thread_error(NFX_INVALID_ARG, "nfx_runtime_create: path is NULL");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+        return nfx::set_thread_error(NFX_INVALID_ARG, "nfx_runtime_create: no such CUDA device");
+    std::unique_ptr<nfx_runtime> rt(new nfx_runtime());
+    rt->device = device;
+    std::string msg;
+    int s = nfx::load_ir(ir_path, rt->model, msg);
+    if (s != NFX_OK) return nfx::set_thread_error(s, msg);
+    const auto& op = rt->model.op;
+    if (op != "FNO1d" && op != "FNO2d" && op != "FNO3d" && op != "DeepONet" && op != "TokenMixer" &&
+        op != "GraphOp" && op != "TokenMixer2D" && op != "GraphOp2D")
+        return nfx::set_thread_error(NFX_UNSUPPORTED_OP, "runtime does not support op: " + op);
+    DeviceGuard g(device);
+    if (cudaStreamCreateWithFlags(&rt->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return nfx::set_thread_error(NFX_INTERNAL, "cudaStreamCreate failed");
+    if (op == "FNO2d") {
+        s = fno2d_create(rt.get());
+        if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
+    }
+    if (!nfx::device_error_word())
+        return nfx::set_thread_error(NFX_INTERNAL, "cannot allocate the device error word");
+    *out = rt.release();
+    return NFX_OK;
+}
+
+void nfx_runtime_destroy(nfx_runtime* rt) {
+    if (!rt) return;
+    DeviceGuard g(rt->device);
+    cudaDeviceSynchronize();
+    for (void* p : rt->allocs) cudaFree(p);
+    for (void* p : rt->act_bufs)
+        if (p) cudaFree(p);
+    for (auto* p : rt->tw)
+        if (p) cudaFree(p);
+    if (rt->dx) cudaFree(rt->dx);
+    if (rt->dy) cudaFree(rt->dy);
+    if (rt->stream) cudaStreamDestroy(rt->stream);
+    delete rt;
+}
+
+const char* nfx_runtime_op(const nfx_runtime* rt) { return rt ? rt->model.op.c_str() : ""; }
+
+void nfx_runtime_enable_int8_gemm(nfx_runtime* rt) {
+    if (!rt) return;
+    DeviceGuard g(rt->device);
+    if (rt->model.op == "FNO2d") fno2d_enable_int8(rt);
+}
+
+int nfx_runtime_is_int8_gemm_enabled(const nfx_runtime* rt) { return rt && rt->int8_enabled ? 1 : 0; }
+
+const char* nfx_runtime_last_error(const nfx_runtime* rt) { return rt ? rt->err.c_str() : ""; }
+
+int nfx_runtime_run_device(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
+                           float* y, const int64_t* y_shape, int y_rank, void* stream) {
+    if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
+    if (!x_shape || !y_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
+    DeviceGuard g(rt->device);
+    if (rt->model.op != "FNO2d")
+        return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                       "the GPU runtime executes FNO2d in this release; op is " + rt->model.op);
+    int s = check_fno2d_shapes(rt, x_shape, x_rank, y_shape, y_rank);
+    if (s != NFX_OK) return s;
+    if (numel(x_shape, x_rank) > 0 && (!x || !y)) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
+    return fno2d_launch(rt, x, x_shape, y, static_cast<cudaStream_t>(stream));
+}
+
+int nfx_runtime_check(nfx_runtime* rt) {
+    if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
+    DeviceGuard g(rt->device);
+    if (!cuda_ok(rt, cudaDeviceSynchronize(), "device error")) return NFX_INTERNAL;
+    unsigned* w = nfx::device_error_word();
+    unsigned v = 0;
+    if (!w || !cuda_ok(rt, cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost), "error word read"))
+        return NFX_INTERNAL;
+    if (v) {
+        cudaMemset(w, 0, 4);
+        return rt_fail(rt, NFX_INTERNAL,
+                       "a kernel gave up waiting (device error flags 0x" + std::to_string(v) + ")");
+    }
+    return NFX_OK;
+}
+
+int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank, float* y,
+                    const int64_t* y_shape, int y_rank) {
+    if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
+    if (!x_shape || !y_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
+    DeviceGuard g(rt->device);
+    if (rt->model.op != "FNO2d")
+        return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                       "the GPU runtime executes FNO2d in this release; op is " + rt->model.op);
+    int s = check_fno2d_shapes(rt, x_shape, x_rank, y_shape, y_rank);
+    if (s != NFX_OK) return s;
+    const size_t nx = static_cast<size_t>(numel(x_shape, x_rank));
+    const size_t ny = static_cast<size_t>(numel(y_shape, y_rank));
+    if (nx == 0) return NFX_OK;
+    if (!x || !y) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
+    if (nx > rt->dx_cap) {
+        if (rt->dx) cudaFree(rt->dx);
+        rt->dx = nullptr;
+        if (!cuda_ok(rt, cudaMalloc(&rt->dx, nx * 4), "cudaMalloc input")) return NFX_INTERNAL;
+        rt->dx_cap = nx;
+    }
+    if (ny > rt->dy_cap) {
+        if (rt->dy) cudaFree(rt->dy);
+        rt->dy = nullptr;
+        if (!cuda_ok(rt, cudaMalloc(&rt->dy, ny * 4), "cudaMalloc output")) return NFX_INTERNAL;
+        rt->dy_cap = ny;
+    }
+    if (!cuda_ok(rt, cudaMemcpyAsync(rt->dx, x, nx * 4, cudaMemcpyHostToDevice, rt->stream), "H2D"))
+        return NFX_INTERNAL;
+    s = fno2d_launch(rt, rt->dx, x_shape, rt->dy, rt->stream);
+    if (s != NFX_OK) return s;
+    if (!cuda_ok(rt, cudaMemcpyAsync(y, rt->dy, ny * 4, cudaMemcpyDeviceToHost, rt->stream), "D2H"))
+        return NFX_INTERNAL;
+    if (!cuda_ok(rt, cudaStreamSynchronize(rt->stream), "FNO2d execution")) return NFX_INTERNAL;
+    return nfx_runtime_check(rt);
+}
+
+}  // extern "C"

@@ -1,0 +1,27 @@
+"""CPU-side checks of the C-ABI library: it loads and exports every symbol that
+include/nfx.h declares (no GPU calls)."""
+import ctypes
+import os
+import re
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    src = open(os.path.join(ROOT, "include", "nfx.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(nfx_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_declared_symbols():
+    from neuroflow_b200 import _nfx
+    names = _declared()
+    assert len(names) >= 10
+    missing = [n for n in names if not hasattr(_nfx.lib, n)]
+    assert not missing, missing
+
+
+def test_library_is_sm100a_only():
+    # the build targets sm_100a exclusively
+    from neuroflow_b200 import build
+    assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]

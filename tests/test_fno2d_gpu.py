@@ -1,0 +1,74 @@
+"""FNO2d INT8 executor on the GPU vs the CPU restatement (oracle mode 1)."""
+import os
+
+import numpy as np
+import pytest
+
+from neuroflow_b200 import ir, synth
+from oracle.cpu import Oracle
+
+
+def _model(tmp_path, seed=3, L=4, H=32, W=32, in_ch=3, out_ch=1):
+    m = synth.fno2d_model(seed, in_ch=in_ch, out_ch=out_ch, width=64, mh=12, mw=12, L=L, H=H,
+                          W=W, n_calib=4, calib_chunk=4)
+    p = os.path.join(str(tmp_path), "fno2d.nneuroir")
+    ir.write(p, m)
+    return m, p
+
+
+def _stats(got, want, step):
+    d = np.abs(got - want)
+    return dict(max_abs=float(d.max()), frac_diff=float(np.mean(d > 0)),
+                max_steps=float(d.max() / step), rel_l2=float(np.linalg.norm(got - want) /
+                                                             (np.linalg.norm(want) + 1e-30)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,W", [(32, 32), (64, 128)])
+def test_fno2d_int8_end_to_end(tmp_path, H, W):
+    from neuroflow_b200.runtime import InferenceRuntime
+    m, path = _model(tmp_path, H=H, W=W)
+    x = synth.fno2d_inputs(np.random.default_rng(11), 3, H, W)
+    want = Oracle().fno2d_forward(m, x, mode=1)
+    rt = InferenceRuntime(path)
+    rt.enable_int8_gemm()
+    assert rt.is_int8_gemm_enabled()
+    got = np.zeros_like(want)
+    rt.run(x, got)
+    step = m.qparams["proj_out.output"].scale
+    st = _stats(got, want, step)
+    print(H, W, st)
+    assert np.all(np.isfinite(got))
+    assert st["rel_l2"] < 2e-2, st
+    assert st["frac_diff"] < 0.05, st
+
+
+@pytest.mark.gpu
+def test_fno2d_shape_errors(tmp_path):
+    from neuroflow_b200.runtime import InferenceRuntime
+    m, path = _model(tmp_path, L=1)
+    rt = InferenceRuntime(path)
+    rt.enable_int8_gemm()
+    x = np.zeros((1, 32, 32, 3), np.float32)
+    with pytest.raises(RuntimeError, match="input channels mismatch"):
+        rt.run(np.zeros((1, 32, 32, 2), np.float32), np.zeros((1, 32, 32, 1), np.float32))
+    with pytest.raises(RuntimeError, match="output buffer shape mismatch"):
+        rt.run(x, np.zeros((1, 32, 16, 1), np.float32))
+    with pytest.raises(RuntimeError, match="power of two"):
+        rt.run(np.zeros((1, 24, 32, 3), np.float32), np.zeros((1, 24, 32, 1), np.float32))
+    with pytest.raises(RuntimeError, match="expected 4D"):
+        rt.run(np.zeros((32, 32, 3), np.float32), np.zeros((32, 32, 1), np.float32))
+
+
+@pytest.mark.gpu
+def test_fno2d_without_nirq_is_not_int8(tmp_path):
+    from neuroflow_b200.runtime import InferenceRuntime
+    m, _ = _model(tmp_path, L=1)
+    m.quant_enabled = False
+    p = os.path.join(str(tmp_path), "plain.nneuroir")
+    ir.write(p, m)
+    rt = InferenceRuntime(p)
+    rt.enable_int8_gemm()
+    assert not rt.is_int8_gemm_enabled()
+    with pytest.raises(RuntimeError, match="INT8"):
+        rt.run(np.zeros((1, 32, 32, 3), np.float32), np.zeros((1, 32, 32, 1), np.float32))
