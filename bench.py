@@ -1,0 +1,378 @@
+"""Benchmark: FNO2d INT8 inference on 1..8 B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nfx|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (one process per GPU)
+
+One step = one forward pass of the FNO2d INT8 executor over a batch of 256 samples
+(128x128 grid, 3 input channels, width 64, 12x12 modes, 4 layers, out_ch 1) per GPU
+(weak scaling: every rank runs its own 256-sample batch; rank 0 gathers all outputs
+over NCCL, the only collective).  Inputs are seeded synthetic Gaussian random fields;
+weights are random-init and calibrated on a separate 32-sample batch (no dataset or
+checkpoint is available offline).  The per-step working set (268 MB of int8 codes
+per layer boundary + 50 MB of input) is larger than the 126 MB L2, so no L2 flush is
+needed between steps.
+
+`value`: samples/s of the whole job with inputs resident in HBM, device-timed with
+CUDA events, max over ranks.  `e2e`: the same metric through the public host-buffer
+API (InferenceRuntime.run: pinned host x -> device -> host y every step).
+`--impl reference`: the reference's own CPU runtime (compiled from its sources into
+oracle/_ref) on all host cores, one InferenceRuntime per thread.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(in_channels=3, out_channels=1, width=64, modes_h=12, modes_w=12, n_layers=4,
+           H=128, W=128, batch=256, n_calib=32)
+METRIC = "FNO2d INT8 samples/s"
+UNIT = "samples/s"
+WORKLOAD = "configs[2] FNO2d INT8 per-channel, 128x128, width 64, 12x12 modes, 4 layers"
+# algorithmic bytes per sample of the whole network (int8 codes at each layer boundary,
+# read twice per layer, written once; fp32 input and output): 16 P + 14 P C
+P = CFG["H"] * CFG["W"]
+BYTES_PER_SAMPLE = 16 * P + 14 * P * CFG["width"]
+
+
+def model_path(seed: int = 0) -> str:
+    from neuroflow_b200 import ir, synth
+    key = hashlib.sha1(json.dumps([CFG, seed, "v1"], sort_keys=True).encode()).hexdigest()[:12]
+    path = os.path.join(tempfile.gettempdir(), f"nfx_bench_fno2d_{key}.nneuroir")
+    if not os.path.exists(path):
+        m = synth.fno2d_model(seed, in_ch=CFG["in_channels"], out_ch=CFG["out_channels"],
+                              width=CFG["width"], mh=CFG["modes_h"], mw=CFG["modes_w"],
+                              L=CFG["n_layers"], H=CFG["H"], W=CFG["W"], n_calib=CFG["n_calib"])
+        tmp = path + f".{os.getpid()}"
+        ir.write(tmp, m)
+        os.replace(tmp, path)
+    return path
+
+
+def inputs(seed: int, n: int) -> np.ndarray:
+    from neuroflow_b200 import synth
+    return synth.fno2d_inputs(np.random.default_rng(seed), n, CFG["H"], CFG["W"],
+                              CFG["in_channels"])
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def cpu_reference(path: str, x: np.ndarray, nthreads: int, target_s: float = 8.0):
+    """Reference runtime on the host cores: returns (samples/s, sample description)."""
+    from oracle.cpu import Reference
+    ref = Reference()
+    t1 = ref.bench(path, x[:1], CFG["out_channels"], 1, 1)          # one sample, one thread
+    reps = max(1, int(round(target_s / max(t1, 1e-3))))
+    n = min(len(x), nthreads)
+    wall = ref.bench(path, x[:n], CFG["out_channels"], n, reps)
+    return n * reps / wall, n, reps, t1
+
+
+def gemm_sweep(device):
+    """configs[1] GEMM at M = 1,048,576 rows: achieved HBM GB/s of nfx_int8_gemm."""
+    import torch
+    from neuroflow_b200 import _nfx, quant
+    hbm, src = peaks()
+    out = []
+    M = 1 << 20
+    for K in (32, 64, 128, 256):
+        N = K
+        c = quant.gemm_case(K, 4096, K, N)     # weights + qparams; rows tiled below
+        rng = np.random.default_rng(K)
+        A = torch.from_numpy(rng.integers(-128, 128, (M, K), dtype=np.int8)).to(device)
+        sA = torch.from_numpy(rng.uniform(0.005, 0.02, M).astype(np.float32)).to(device)
+        zA = torch.from_numpy(rng.integers(-20, 20, M).astype(np.int32)).to(device)
+        t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(device)
+             for k, v in c.items() if k in ("Wq", "sW", "zW", "sum_w", "bias")}
+        C_ = torch.empty((M, N), dtype=torch.float32, device=device)
+        for act in (0, 1):
+            for _ in range(3):
+                _nfx.int8_gemm(A, t["Wq"], t["sW"], t["zW"], t["sum_w"], bias=t["bias"],
+                               scale_a=sA, zp_a=zA, act=act, out=C_)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 20
+            e0.record()
+            for _ in range(reps):
+                _nfx.int8_gemm(A, t["Wq"], t["sW"], t["zW"], t["sum_w"], bias=t["bias"],
+                               scale_a=sA, zp_a=zA, act=act, out=C_)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            byts = M * K + N * K + 4 * M * N + 16 * N + 8 * M
+            gbs = byts / (ms * 1e-3) / 1e9
+            out.append({"M": M, "K": K, "N": N, "epilogue": "bias+GELU" if act else "bias",
+                        "us": round(ms * 1e3, 2), "GBps": round(gbs, 1),
+                        "frac": round(gbs / hbm, 3)})
+        del A, sA, zA, C_
+    return out
+
+
+def run_nfx(args, ws, rank, local):
+    import torch
+    from neuroflow_b200.runtime import InferenceRuntime
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    B = CFG["batch"]
+    path = model_path(0)
+    x_host = inputs(100 + rank, B)
+    rt = InferenceRuntime(path, local)
+    rt.enable_int8_gemm()
+    if not rt.is_int8_gemm_enabled():
+        raise RuntimeError("INT8 path not enabled for the bench model")
+    dx = torch.from_numpy(x_host).to(device)
+    dy = torch.empty((B, CFG["H"], CFG["W"], CFG["out_channels"]), dtype=torch.float32,
+                     device=device)
+    stream = torch.cuda.Stream(device)
+    gathered = None
+    if ws > 1:
+        import torch.distributed as dist
+        gathered = torch.empty((ws,) + tuple(dy.shape), dtype=torch.float32, device=device)
+
+    def step():
+        rt.run_device(dx, dy, stream)
+        if ws > 1:
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(gathered, dy)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    rt.check()
+
+    rt.profile(True)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    prof = rt.profile_read()
+    rt.profile(False)
+    rt.check()
+    if ws > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = ws * B * args.steps / (ms * 1e-3)
+
+    # end-to-end through the host-buffer API (pinned host memory)
+    xp = torch.from_numpy(x_host).pin_memory()
+    yp = torch.empty(tuple(dy.shape), dtype=torch.float32).pin_memory()
+    xn, yn = xp.numpy(), yp.numpy()
+    for _ in range(max(1, args.warmup)):
+        rt.run(xn, yn)
+    if ws > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    e2e_steps = max(3, args.steps // 2)
+    for _ in range(e2e_steps):
+        rt.run(xn, yn)
+    e2e_s = time.perf_counter() - t0
+    if ws > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = ws * B * e2e_steps / e2e_s
+
+    result = None
+    if rank == 0:
+        hbm, src = peaks()
+        # dominant kernel of the step
+        top = max(prof.items(), key=lambda kv: kv[1][1])
+        name, (launches, tot_ms) = top
+        per_launch_s = tot_ms / launches * 1e-3
+        M = B * P
+        C = CFG["width"]
+        alg = {  # algorithmic bytes per launch of each kernel
+            "fno2d_layer": 2 * M * C,                      # codes in + codes out
+            "fno2d_spec_fwd": M * C,                       # codes in
+            "fno2d_proj": M * C + 4 * M * CFG["out_channels"],
+            "fno2d_lift": 4 * M * CFG["in_channels"] + M * C,
+            "fno2d_spec_mix": 0,
+        }[name]
+        achieved = alg / per_launch_s / 1e9
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tp):
+            traffic = json.load(open(tp)).get(name)
+        share = {k: round(v[1] / sum(vv[1] for vv in prof.values()), 3) for k, v in prof.items()}
+        total_launches = sum(v[0] for v in prof.values())
+        result = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": B, "global_batch": B * ws,
+                       "grid": [CFG["H"], CFG["W"]], "in_channels": CFG["in_channels"],
+                       "out_channels": CFG["out_channels"], "width": C, "modes": [12, 12],
+                       "n_layers": CFG["n_layers"], "parallelism": f"batch x{ws}",
+                       "l2": "working set > L2 (268 MB codes per layer boundary)"},
+            "e2e": {"value": round(e2e, 1), "unit": UNIT,
+                    "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(4 * B * P)},
+            "roofline": {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 3),
+                         "peak_source": src, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": alg,
+                         "launch_us": round(per_launch_s * 1e6, 1)},
+            "network_roofline": {"bytes_per_sample": BYTES_PER_SAMPLE,
+                                 "achieved_GBps": round(value / ws * BYTES_PER_SAMPLE / 1e9, 1),
+                                 "frac": round(value / ws * BYTES_PER_SAMPLE / 1e9 / hbm, 3)},
+            "kernel_share": share,
+            "gpu_launches": total_launches,
+            "clocks": clk.summary(),
+        }
+    return result, rt, x_host, path
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="nfx", choices=["nfx", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true")
+    args = ap.parse_args()
+    ws, rank, local = dist_setup(args.gpus)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        path = model_path(0)
+        n = os.cpu_count() or 1
+        x = inputs(100, max(1, n))
+        from oracle.cpu import Reference
+        ref = Reference()
+        for _ in range(args.warmup):
+            ref.bench(path, x[:1], CFG["out_channels"], 1, 1)
+        t = 0.0
+        for _ in range(args.steps):
+            t += ref.bench(path, x, CFG["out_channels"], n, 1)
+        v = n * args.steps / t
+        line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT,
+                "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": True, "dtype": "fp32",
+                "config": {"workload": WORKLOAD, "batch_per_step": n},
+                "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": n,
+                                 "kind": "reference",
+                                 "sample": f"{n} samples per step through the reference "
+                                           "InferenceRuntime::Run (FNO2d fake-quant fp32 path; "
+                                           "the reference has no INT8 FNO2d), one runtime per "
+                                           "thread"},
+                "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    result, rt, x_host, path = run_nfx(args, ws, rank, local)
+    if rank == 0:
+        if ws == 1 and not args.no_gemm:
+            import torch
+            result["gemm_sweep"] = gemm_sweep(torch.device("cuda", local))
+        if ws == 1 and not args.no_cpu_baseline:
+            n = os.cpu_count() or 1
+            v, nthr, reps, t1 = cpu_reference(path, x_host, n)
+            result["cpu_baseline"] = {
+                "value": round(v, 3), "unit": UNIT, "cores": nthr, "kind": "reference",
+                "sample": f"{nthr * reps} samples ({nthr} threads x {reps}) of the same "
+                          "workload through the reference InferenceRuntime::Run (fake-quant "
+                          "fp32 FNO2d; the reference has no INT8 FNO2d); single-thread "
+                          f"{t1:.2f} s/sample"}
+        print(json.dumps(result), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

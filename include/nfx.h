@@ -76,6 +76,17 @@ int nfx_runtime_run_device(nfx_runtime* rt, const float* x, const int64_t* x_sha
  * timed out inside a kernel) as NFX_INTERNAL. */
 int nfx_runtime_check(nfx_runtime* rt);
 
+/* Per-kernel device timing (tracing): when enabled, every kernel the executor launches
+ * is bracketed by CUDA events recorded on its launch stream.  profile_count returns
+ * the number of distinct kernels seen since enabling (waiting for the recorded events);
+ * profile_entry returns a kernel's name, launch count and summed device time in ms.
+ * Enabling again resets the totals.  No counterpart in the reference, whose only
+ * timing is ad-hoc std::chrono in cpp/tests/bench_int8_gemm.cpp:144-178. */
+int nfx_runtime_profile_enable(nfx_runtime* rt, int enable);
+int nfx_runtime_profile_count(nfx_runtime* rt);
+int nfx_runtime_profile_entry(nfx_runtime* rt, int index, const char** name, int* launches,
+                              double* total_ms);
+
 /* Message of the last failing call on this handle ("" when none). */
 const char* nfx_runtime_last_error(const nfx_runtime* rt);
 

@@ -47,6 +47,13 @@ if hasattr(lib, "nfx_runtime_create"):
     lib.nfx_runtime_check.argtypes = [_vp]
     lib.nfx_runtime_last_error.restype = C.c_char_p
     lib.nfx_runtime_last_error.argtypes = [_vp]
+    lib.nfx_runtime_profile_enable.restype = C.c_int
+    lib.nfx_runtime_profile_enable.argtypes = [_vp, C.c_int]
+    lib.nfx_runtime_profile_count.restype = C.c_int
+    lib.nfx_runtime_profile_count.argtypes = [_vp]
+    lib.nfx_runtime_profile_entry.restype = C.c_int
+    lib.nfx_runtime_profile_entry.argtypes = [_vp, C.c_int, C.POINTER(C.c_char_p),
+                                              C.POINTER(C.c_int), C.POINTER(C.c_double)]
 
 
 class NfxError(RuntimeError):

@@ -578,8 +578,10 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
     {
         const int64_t blocks64 = (M + 255) / 256;
         const int grid = static_cast<int>(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
+        if (pl.timer) pl.timer->begin("fno2d_lift", st);
         lift_kernel<C><<<grid, 256, 0, st>>>(pl.x, M, pl.in_ch, pl.lift_w, pl.lift_b,
                                              pl.lift_s, pl.lift_zp, pl.codes[0]);
+        if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
     const int sms = device_sm_count();
@@ -592,15 +594,19 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
         {
             auto k = spec_fwd_kernel<C, MH, MW>;
             if ((e = set_smem(k, sm_fwd)) != cudaSuccess) return e;
+            if (pl.timer) pl.timer->begin("fno2d_spec_fwd", st);
             k<<<dim3(nHB, pl.B), C * MW, sm_fwd, st>>>(pl.codes[cur], pl.H, pl.W, pl.HB,
                                                     pl.layer[i].s_in, pl.layer[i].zp_in,
                                                     pl.twf_w, pl.twf_h, pl.xpart);
+            if (pl.timer) pl.timer->end(st);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
         {
             const int SB = 32;
+            if (pl.timer) pl.timer->begin("fno2d_spec_mix", st);
             spec_mix_kernel<C, MH, MW><<<dim3(MH * MW, (pl.B + SB - 1) / SB), 256, 0, st>>>(
                 pl.xpart, nHB, pl.B, SB, pl.layer[i].wspec, pl.Y);
+            if (pl.timer) pl.timer->end(st);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
         {
@@ -620,7 +626,9 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
             a.twi_w = pl.twi_w;
             a.twi_h = pl.twi_h;
             a.err = pl.err;
+            if (pl.timer) pl.timer->begin("fno2d_layer", st);
             k<<<grid_l, kThreads, LC::kSmemBytes, st>>>(tin, tout, a);
+            if (pl.timer) pl.timer->end(st);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
         cur ^= 1;
@@ -638,7 +646,9 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
         a.W = pl.W;
         a.err = pl.err;
         a.y = pl.y;
+        if (pl.timer) pl.timer->begin("fno2d_proj", st);
         k<<<grid_l, kThreads, LC::kSmemBytes, st>>>(tin, tin, a);
+        if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -5,6 +5,8 @@
 
 #include <cstdint>
 
+#include "nfx_internal.h"
+
 namespace nfx {
 
 // Fake-quant applied at an ".output" boundary: kind 0 none, 1 INT8 per-tensor,
@@ -71,6 +73,7 @@ struct Fno2dPlan {
     Fno2dLayerPlan layer[kFno2dMaxLayers];
     LayerArgs proj;
     unsigned* err;
+    KernelTimer* timer;    // nullptr unless profiling is enabled
 };
 
 bool fno2d_supported(int C, int MH, int MW);

@@ -30,6 +30,13 @@ struct GemmArgs {
 bool gemm_i8_supported(int K, int N);
 cudaError_t gemm_i8_launch(const GemmArgs& p, int K, int N, cudaStream_t stream);
 
+// Optional per-kernel device timing (CUDA events on the launch stream).
+struct KernelTimer {
+    virtual void begin(const char* name, cudaStream_t s) = 0;
+    virtual void end(cudaStream_t s) = 0;
+    virtual ~KernelTimer() = default;
+};
+
 // Host helpers (nfx_host.cpp)
 int current_device();
 int device_sm_count();

@@ -23,6 +23,72 @@ namespace nfx {
 int set_thread_error(int code, const std::string& msg);
 }
 
+namespace nfx {
+// Event-pair timer: begin/end record events on the launch stream; read() waits for
+// them and folds the elapsed times into per-kernel totals.
+struct EventTimer : KernelTimer {
+    struct Pending {
+        std::string name;
+        cudaEvent_t a, b;
+    };
+    std::vector<Pending> pending;
+    std::vector<cudaEvent_t> pool;
+    std::vector<std::string> names;
+    std::vector<int> launches;
+    std::vector<double> total_ms;
+    cudaEvent_t take() {
+        if (!pool.empty()) {
+            cudaEvent_t e = pool.back();
+            pool.pop_back();
+            return e;
+        }
+        cudaEvent_t e = nullptr;
+        cudaEventCreate(&e);
+        return e;
+    }
+    void begin(const char* name, cudaStream_t s) override {
+        Pending p{name, take(), take()};
+        cudaEventRecord(p.a, s);
+        pending.push_back(p);
+    }
+    void end(cudaStream_t s) override {
+        if (!pending.empty()) cudaEventRecord(pending.back().b, s);
+    }
+    void collect() {
+        for (auto& p : pending) {
+            cudaEventSynchronize(p.b);
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, p.a, p.b);
+            size_t i = 0;
+            while (i < names.size() && names[i] != p.name) ++i;
+            if (i == names.size()) {
+                names.push_back(p.name);
+                launches.push_back(0);
+                total_ms.push_back(0.0);
+            }
+            launches[i] += 1;
+            total_ms[i] += ms;
+            pool.push_back(p.a);
+            pool.push_back(p.b);
+        }
+        pending.clear();
+    }
+    void reset() {
+        collect();
+        names.clear();
+        launches.clear();
+        total_ms.clear();
+    }
+    ~EventTimer() override {
+        for (auto& p : pending) {
+            cudaEventDestroy(p.a);
+            cudaEventDestroy(p.b);
+        }
+        for (auto e : pool) cudaEventDestroy(e);
+    }
+};
+}  // namespace nfx
+
 struct nfx_runtime {
     int device = 0;
     nfx::IrModel model;
@@ -40,6 +106,7 @@ struct nfx_runtime {
     size_t dx_cap = 0, dy_cap = 0;
     float2* tw[4] = {nullptr, nullptr, nullptr, nullptr};  // twf_w, twf_h, twi_w, twi_h
     int tw_H = 0, tw_W = 0;
+    std::unique_ptr<nfx::EventTimer> timer;  // per-kernel timing when enabled
 };
 
 namespace {
@@ -299,6 +366,7 @@ int fno2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
     pl.twi_h = rt->tw[3];
     pl.err = nfx::device_error_word();
     if (!pl.err) return rt_fail(rt, NFX_INTERNAL, "no device error word");
+    pl.timer = rt->timer.get();
     const cudaError_t e = nfx::fno2d_run(pl, st);
     if (e != cudaSuccess)
         return rt_fail(rt, NFX_INTERNAL, std::string("FNO2d launch failed: ") + cudaGetErrorString(e));
@@ -369,7 +437,40 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
     if (rt->dx) cudaFree(rt->dx);
     if (rt->dy) cudaFree(rt->dy);
     if (rt->stream) cudaStreamDestroy(rt->stream);
+    rt->timer.reset();
     delete rt;
+}
+
+int nfx_runtime_profile_enable(nfx_runtime* rt, int enable) {
+    if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
+    DeviceGuard g(rt->device);
+    if (enable) {
+        if (!rt->timer) rt->timer.reset(new nfx::EventTimer());
+        rt->timer->reset();
+    } else {
+        rt->timer.reset();
+    }
+    return NFX_OK;
+}
+
+int nfx_runtime_profile_count(nfx_runtime* rt) {
+    if (!rt || !rt->timer) return 0;
+    DeviceGuard g(rt->device);
+    rt->timer->collect();
+    return static_cast<int>(rt->timer->names.size());
+}
+
+int nfx_runtime_profile_entry(nfx_runtime* rt, int i, const char** name, int* launches,
+                              double* total_ms) {
+    if (!rt || !rt->timer) return rt_fail(rt, NFX_INVALID_ARG, "profiling is not enabled");
+    DeviceGuard g(rt->device);
+    rt->timer->collect();
+    if (i < 0 || i >= static_cast<int>(rt->timer->names.size()))
+        return rt_fail(rt, NFX_INVALID_ARG, "profile entry out of range");
+    if (name) *name = rt->timer->names[i].c_str();
+    if (launches) *launches = rt->timer->launches[i];
+    if (total_ms) *total_ms = rt->timer->total_ms[i];
+    return NFX_OK;
 }
 
 const char* nfx_runtime_op(const nfx_runtime* rt) { return rt ? rt->model.op.c_str() : ""; }

@@ -76,6 +76,25 @@ class InferenceRuntime:
         if rc != 0:
             raise RuntimeError("Run failed: " + self._err())
 
+    def profile(self, enable: bool = True) -> None:
+        """Enable (and reset) or disable per-kernel CUDA-event timing."""
+        rc = _lib.nfx_runtime_profile_enable(self._h, int(bool(enable)))
+        if rc != 0:
+            raise RuntimeError(self._err())
+
+    def profile_read(self) -> dict:
+        """{kernel name: (launches, total device ms)} since profiling was enabled."""
+        out = {}
+        for i in range(_lib.nfx_runtime_profile_count(self._h)):
+            name = C.c_char_p()
+            n = C.c_int()
+            ms = C.c_double()
+            rc = _lib.nfx_runtime_profile_entry(self._h, i, C.byref(name), C.byref(n), C.byref(ms))
+            if rc != 0:
+                raise RuntimeError(self._err())
+            out[name.value.decode()] = (n.value, ms.value)
+        return out
+
     def check(self) -> None:
         rc = _lib.nfx_runtime_check(self._h)
         if rc != 0:
