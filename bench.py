@@ -193,7 +193,7 @@ def run_nfx(args, ws, rank, local):
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    B = CFG["batch"]
+    B = args.batch
     path = model_path(0)
     x_host = inputs(100 + rank, B)
     rt = InferenceRuntime(path, local)
@@ -245,23 +245,25 @@ def run_nfx(args, ws, rank, local):
     value = ws * B * args.steps / (ms * 1e-3)
 
     # end-to-end through the host-buffer API (pinned host memory)
+    if args.no_e2e:
+        e2e_steps = 0
     xp = torch.from_numpy(x_host).pin_memory()
     yp = torch.empty(tuple(dy.shape), dtype=torch.float32).pin_memory()
     xn, yn = xp.numpy(), yp.numpy()
-    for _ in range(max(1, args.warmup)):
+    e2e_steps = 0 if args.no_e2e else max(3, args.steps // 2)
+    for _ in range(max(1, args.warmup) if e2e_steps else 0):
         rt.run(xn, yn)
     if ws > 1:
         dist.barrier()
     t0 = time.perf_counter()
-    e2e_steps = max(3, args.steps // 2)
     for _ in range(e2e_steps):
         rt.run(xn, yn)
-    e2e_s = time.perf_counter() - t0
+    e2e_s = max(time.perf_counter() - t0, 1e-9)
     if ws > 1:
         t = torch.tensor([e2e_s], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = ws * B * e2e_steps / e2e_s
+    e2e = ws * B * e2e_steps / e2e_s if e2e_steps else None
 
     result = None
     if rank == 0:
@@ -296,7 +298,7 @@ def run_nfx(args, ws, rank, local):
                        "out_channels": CFG["out_channels"], "width": C, "modes": [12, 12],
                        "n_layers": CFG["n_layers"], "parallelism": f"batch x{ws}",
                        "l2": "working set > L2 (268 MB codes per layer boundary)"},
-            "e2e": {"value": round(e2e, 1), "unit": UNIT,
+            "e2e": {"value": round(e2e, 1) if e2e else None, "unit": UNIT,
                     "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(4 * B * P)},
             "roofline": {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 3),
@@ -321,6 +323,10 @@ def main():
     ap.add_argument("--impl", default="nfx", choices=["nfx", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=CFG["batch"],
+                    help="samples per GPU (default: the configs[2] batch of 256; smaller "
+                         "values only for profiling captures)")
     args = ap.parse_args()
     ws, rank, local = dist_setup(args.gpus)
 
