@@ -72,6 +72,23 @@ int nfx_runtime_run_device(nfx_runtime* rt, const float* x, const int64_t* x_sha
                            int x_rank, float* y, const int64_t* y_shape, int y_rank,
                            void* stream);
 
+/* Allocation-free variant of nfx_runtime_run_device, for callers that cannot call
+ * cudaMalloc while they run inference (their device memory belongs to another
+ * allocator, or allocation is forbidden or too slow on their inference path).  It
+ * runs the same FNO2d INT8 kernels but keeps all scratch (activation codes, spectra,
+ * transform tables, error word) in one fixed 32 MiB device array inside libnfx.so,
+ * held on every GPU that loads the library until exit; a batch that needs more
+ * returns NFX_INVALID_ARG (about 11 samples of 128x128 at width 64).  The first call
+ * on a device looks up the array's device address (and registers the kernels'
+ * shared-memory limits), so make it before any stream capture; later calls allocate
+ * nothing on the device or the host.  Calls share the array: calls that overlap on
+ * the GPU race and must be serialised by the caller.  x and y are device pointers;
+ * the call returns after the work on `stream` has finished.  No counterpart in the
+ * reference. */
+int nfx_runtime_run_device_noalloc(nfx_runtime* rt, const float* x, const int64_t* x_shape,
+                                   int x_rank, float* y, const int64_t* y_shape, int y_rank,
+                                   void* stream);
+
 /* Synchronise the runtime's work and report device-side errors (bounded waits that
  * timed out inside a kernel) as NFX_INTERNAL. */
 int nfx_runtime_check(nfx_runtime* rt);

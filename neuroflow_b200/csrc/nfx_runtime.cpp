@@ -394,6 +394,50 @@ int64_t numel(const int64_t* s, int r) {
 
 }  // namespace
 
+namespace nfx {
+
+// Helpers of the allocation-free entry point (noalloc.cu).  They validate the call
+// exactly as nfx_runtime_run_device does and copy the handle's weight plan, without
+// touching the handle's on-demand buffers.
+int runtime_device(const nfx_runtime* rt) { return rt->device; }
+
+int runtime_fail(nfx_runtime* rt, int code, const char* msg) { return rt_fail(rt, code, msg); }
+
+int fno2d_noalloc_plan(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
+                       float* y, const int64_t* y_shape, int y_rank, Fno2dPlan* plan) {
+    if (!x_shape || !y_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
+    if (rt->model.op != "FNO2d")
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, "the allocation-free entry point runs FNO2d");
+    int s = check_fno2d_shapes(rt, x_shape, x_rank, y_shape, y_rank);
+    if (s != NFX_OK) return s;
+    const F2 c = fno2d_cfg(rt->model);
+    if (!fno2d_supported(c.width, c.mh, c.mw))
+        return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                       "FNO2d on the GPU runtime supports width 64 with 12x12 modes");
+    if (!rt->int8_enabled)
+        return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                       "FNO2d on the GPU runtime runs the INT8 path: call EnableInt8Gemm() first");
+    const int B = static_cast<int>(x_shape[0]), H = static_cast<int>(x_shape[1]),
+              W = static_cast<int>(x_shape[2]);
+    if (W < 32 || W > 128 || H < 8 || H > 4096 || c.mh > H || c.mw > W / 2 + 1)
+        return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                       "FNO2d GPU executor: needs 32 <= W <= 128, H >= 8, modes within the grid");
+    if (c.pad > 1 && ((H % c.pad) || (W % c.pad)))
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, "FNO2d GPU executor: padding is not supported");
+    if (B > 0 && (!x || !y)) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
+    *plan = rt->plan;
+    plan->B = B;
+    plan->H = H;
+    plan->W = W;
+    plan->HB = H / (H < 8 ? H : 8);
+    plan->x = x;
+    plan->y = y;
+    plan->timer = nullptr;
+    return NFX_OK;
+}
+
+}  // namespace nfx
+
 extern "C" {
 
 int nfx_runtime_create(const char* ir_path, int device, nfx_runtime** out) {
