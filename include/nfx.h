@@ -42,6 +42,13 @@ typedef struct nfx_runtime nfx_runtime;
  * `device`.  On failure *out is NULL and nfx_last_error() holds the message. */
 int nfx_runtime_create(const char* ir_path, int device, nfx_runtime** out);
 
+/* LoadNeuroIr (runtime.h:66, runtime.cpp:16-19): parse a NeuroIR v0 binary on the
+ * host only (no device work).  Writes the op name (NUL-terminated, truncated to
+ * op_cap), the 8-int32 config block (unused slots 0), the number of weight tensors
+ * read, and whether a NIRQ block was present.  Any output pointer may be NULL. */
+int nfx_load_neuroir(const char* ir_path, char* op_out, int op_cap, int32_t* cfg_out8,
+                     int* n_weights_out, int* quant_enabled_out);
+
 /* Destructor of InferenceRuntime. */
 void nfx_runtime_destroy(nfx_runtime* rt);
 

@@ -25,6 +25,9 @@ lib.nfx_last_error.restype = C.c_char_p
 lib.nfx_int8_gemm.restype = C.c_int
 lib.nfx_int8_gemm.argtypes = [_vp, _vp, _vp, C.c_float, C.c_int32, C.c_int, C.c_int, _vp, _vp,
                               _vp, _vp, _vp, C.c_int, C.c_int, _vp, _vp]
+lib.nfx_load_neuroir.restype = C.c_int
+lib.nfx_load_neuroir.argtypes = [C.c_char_p, C.c_char_p, C.c_int, C.POINTER(C.c_int32),
+                                 C.POINTER(C.c_int), C.POINTER(C.c_int)]
 lib.nfx_device_errors.restype = C.c_int
 lib.nfx_device_errors.argtypes = [C.POINTER(C.c_uint)]
 
@@ -94,3 +97,14 @@ def int8_gemm(A, W, scale_w, zp_w, sum_w, bias=None, scale_a=None, zp_a=None, sc
                             M, K, _ptr(W), _ptr(scale_w), _ptr(zp_w), _ptr(sum_w), _ptr(bias), N,
                             int(act), _ptr(out), C.c_void_p(s)))
     return out
+
+
+def load_neuroir(path: str):
+    """LoadNeuroIr on the host: (op, config ints, n_weights, quant_enabled); raises
+    NfxError with the reference StatusCode on failure."""
+    op = C.create_string_buffer(32)
+    cfg = (C.c_int32 * 8)()
+    nw = C.c_int()
+    q = C.c_int()
+    check(lib.nfx_load_neuroir(str(path).encode(), op, 32, cfg, C.byref(nw), C.byref(q)))
+    return op.value.decode(), list(cfg), nw.value, bool(q.value)

@@ -8,6 +8,7 @@
 // (fno.cpp:778-794) and launch the executor on the handle's device.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -466,6 +467,25 @@ int nfx_runtime_create(const char* ir_path, int device, nfx_runtime** out) {
     if (!nfx::device_error_word())
         return nfx::set_thread_error(NFX_INTERNAL, "cannot allocate the device error word");
     *out = rt.release();
+    return NFX_OK;
+}
+
+int nfx_load_neuroir(const char* ir_path, char* op_out, int op_cap, int32_t* cfg_out8,
+                     int* n_weights_out, int* quant_enabled_out) {
+    if (!ir_path) return nfx::set_thread_error(NFX_INVALID_ARG, "nfx_load_neuroir: path is NULL");
+    nfx::IrModel m;
+    std::string msg;
+    const int s = nfx::load_ir(ir_path, m, msg);
+    if (s != NFX_OK) return nfx::set_thread_error(s, msg);
+    if (op_out && op_cap > 0) {
+        const size_t n = std::min(static_cast<size_t>(op_cap - 1), m.op.size());
+        std::memcpy(op_out, m.op.data(), n);
+        op_out[n] = 0;
+    }
+    if (cfg_out8)
+        for (int i = 0; i < 8; ++i) cfg_out8[i] = m.cfg[i];
+    if (n_weights_out) *n_weights_out = static_cast<int>(m.weight_order.size());
+    if (quant_enabled_out) *quant_enabled_out = m.quant_enabled ? 1 : 0;
     return NFX_OK;
 }
 

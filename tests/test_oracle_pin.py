@@ -1,0 +1,193 @@
+"""CPU: the C restatement (oracle/) pinned against the reference.
+
+1. Against the committed golden fixtures (tests/golden/, made by make_golden.py from the
+   reference's own Python exporter/quantiser and its C++ runtime): bit-exact.
+2. Against the reference sources compiled in place (oracle/_ref) on fresh random
+   inputs, when that library is present (it is built by __graft_entry__.build() where
+   the reference tree exists): bit-exact.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from neuroflow_b200 import ir, quant, synth
+from oracle.cpu import REF_SO, Oracle, Reference
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+needs_ref = pytest.mark.skipif(not os.path.exists(REF_SO),
+                               reason="oracle/_ref not built (needs the reference tree)")
+
+
+def _g(name):
+    return np.load(os.path.join(GOLD, name))
+
+
+def _bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+# ---------------------------------------------------------------- golden fixtures
+def test_golden_fno2d_fake_quant_network():
+    d = _g("fno2d_q.npz")
+    m = ir.read(os.path.join(GOLD, "fno2d_q.nneuroir"))
+    assert m.op == "FNO2d" and m.quant_enabled
+    y = Oracle().fno2d_forward(m, d["x"], mode=0)
+    assert np.array_equal(_bits(y), _bits(d["y_q"]))
+
+
+def test_golden_fno2d_plain_network():
+    d = _g("fno2d_q.npz")
+    m = ir.read(os.path.join(GOLD, "fno2d_plain.nneuroir"))
+    assert not m.quant_enabled
+    y = Oracle().fno2d_forward(m, d["x"], mode=0)
+    assert np.array_equal(_bits(y), _bits(d["y_plain"]))
+
+
+def test_golden_linear_forward_batched_and_quantiser():
+    d = _g("int8_gemm.npz")
+    o = Oracle()
+    c, acc, codes = o.linear_forward_batched(d["Wq"], d["sW"], d["zW"], d["sumW"], None,
+                                             float(d["sA"]), int(d["zA"]), d["A"])
+    assert np.array_equal(_bits(c), _bits(d["C"]))
+    assert np.array_equal(codes, d["Aq"])
+    cb, _, _ = o.linear_forward_batched(d["Wq"], d["sW"], d["zW"], d["sumW"], d["bias"],
+                                        float(d["sA"]), int(d["zA"]), d["A"])
+    assert np.array_equal(_bits(cb), _bits(d["Cb"]))
+    # the precomputed row sums of the fixture equal the restated rule
+    assert np.array_equal(d["sumW"],
+                          (d["Wq"].astype(np.int32) - d["zW"][:, None]).sum(axis=1))
+
+
+def test_golden_fft_and_gelu():
+    d = _g("fft.npz")
+    o = Oracle()
+    assert np.array_equal(_bits(o.rfft2(d["x"])), _bits(d["rfft2"]))
+    assert np.array_equal(_bits(o.irfft2(d["rfft2"], 16, 32)), _bits(d["irfft2"]))
+    g = _g("gelu.npz")
+    assert np.array_equal(_bits(o.activation(g["z"])), _bits(g["gelu"]))
+
+
+def test_golden_qparam_rules():
+    d = _g("qparams.npz")
+    for i in range(5):
+        q = quant.tensor_qparams(d[f"case{i}"])
+        assert np.float32(q.scale) == np.float32(d["t_scale"][i])
+        assert q.zero_point == d["t_zp"][i]
+    pc = quant.per_channel_qparams(d["W"], 0)
+    assert np.array_equal(_bits(pc.scales), _bits(d["pc_scale"]))
+    assert np.array_equal(pc.zero_points, d["pc_zp"])
+
+
+def test_golden_ir_bytes_roundtrip():
+    for name in ("fno2d_q.nneuroir", "fno2d_plain.nneuroir"):
+        raw = open(os.path.join(GOLD, name), "rb").read()
+        m = ir.read_bytes(raw)
+        assert ir.write_bytes(m) == raw
+        assert m.config["width"] == 16 and m.config["n_layers"] == 2
+
+
+def test_golden_ir_through_the_cpp_loader():
+    from neuroflow_b200 import _nfx
+    op, cfg, nw, q = _nfx.load_neuroir(os.path.join(GOLD, "fno2d_q.nneuroir"))
+    assert op == "FNO2d" and cfg[:7] == [3, 1, 16, 4, 4, 2, 1] and nw == 14 and q
+
+
+def test_cpp_loader_error_codes(tmp_path):
+    from neuroflow_b200 import _nfx
+    raw = open(os.path.join(GOLD, "fno2d_q.nneuroir"), "rb").read()
+    cases = {
+        "missing": (None, 2, "cannot open IR file"),
+        "magic": (b"NIRX" + raw[4:], 3, "bad magic"),
+        "version": (raw[:4] + b"\x04\x00" + raw[6:], 3, "unsupported IR binary version"),
+        "opcode": (raw[:6] + b"\x09" + raw[7:], 5, "unknown op_code"),
+        "truncated": (raw[:5000], 3, "truncated"),
+        "name": (raw.replace(b"locs.1.weight", b"locs.1.weighX"), 3, "weight name mismatch"),
+        "nirq_kind": (raw[:raw.index(b"NIRQ") + 9] + b"\x07" + raw[raw.index(b"NIRQ") + 10:], 3,
+                      "unsupported qparam kind"),
+    }
+    for key, (blob, code, msg) in cases.items():
+        p = tmp_path / f"{key}.nneuroir"
+        if blob is not None:
+            p.write_bytes(blob)
+        with pytest.raises(_nfx.NfxError) as ei:
+            _nfx.load_neuroir(str(p))
+        assert ei.value.code == code, key
+        assert msg in str(ei.value), key
+    # a file without NIRQ ends right after the weights and loads fine
+    p = tmp_path / "plain.nneuroir"
+    p.write_bytes(raw[:raw.index(b"NIRQ")])
+    assert _nfx.load_neuroir(str(p))[3] is False
+
+
+# ---------------------------------------------------------- compiled reference sources
+@needs_ref
+def test_ref_fft_all_sizes_bitexact():
+    o, r = Oracle(), Reference()
+    rng = np.random.default_rng(0)
+    for H, W in [(2, 2), (4, 8), (8, 64), (32, 32), (128, 128), (256, 16)]:
+        x = (rng.standard_normal((H, W)) * 10 ** rng.uniform(-2, 2)).astype(np.float32)
+        a, b = o.rfft2(x), r.rfft2(x)
+        assert np.array_equal(_bits(a), _bits(b)), (H, W)
+        assert np.array_equal(_bits(o.irfft2(a, H, W)), _bits(r.irfft2(a, H, W))), (H, W)
+
+
+@needs_ref
+def test_ref_spectral_conv_linear_gelu_bitexact():
+    o, r = Oracle(), Reference()
+    rng = np.random.default_rng(1)
+    h = rng.standard_normal((2, 16, 32, 16)).astype(np.float32)
+    wr = rng.standard_normal((16, 16, 12, 6)).astype(np.float32) / 256
+    wi = rng.standard_normal((16, 16, 12, 6)).astype(np.float32) / 256
+    assert np.array_equal(_bits(o.spectral_conv2d(h, wr, wi)), _bits(r.spectral_conv2d(h, wr, wi)))
+    x = rng.standard_normal((100, 64)).astype(np.float32)
+    W = rng.standard_normal((33, 64)).astype(np.float32)
+    b = rng.standard_normal(33).astype(np.float32)
+    assert np.array_equal(_bits(o.linear(x, W, b)), _bits(r.linear(x, W, b)))
+    z = (rng.standard_normal(100000) * 4).astype(np.float32)
+    assert np.array_equal(_bits(o.activation(z)), _bits(r.activation(z)))
+    assert np.array_equal(_bits(o.activation(z, relu=True)), _bits(r.activation(z, relu=True)))
+
+
+@needs_ref
+def test_ref_linear_forward_batched_bitexact():
+    o, r = Oracle(), Reference()
+    for K, N in [(32, 32), (64, 64), (128, 64), (256, 256)]:
+        c = quant.gemm_case(K * 7 + N, 257, K, N)
+        A = (np.random.default_rng(K).standard_normal((257, K)) * 2).astype(np.float32)
+        qa = quant.tensor_qparams(A)
+        for bias in (None, c["bias"]):
+            want = r.linear_forward_batched(c["Wq"], c["sW"], c["zW"], c["sum_w"], bias,
+                                            qa.scale, qa.zero_point, A)
+            got, _, _ = o.linear_forward_batched(c["Wq"], c["sW"], c["zW"], c["sum_w"], bias,
+                                                 qa.scale, qa.zero_point, A)
+            assert np.array_equal(_bits(got), _bits(want)), (K, N)
+
+
+@needs_ref
+@pytest.mark.parametrize("per_channel", [True, False])
+def test_ref_fno2d_network_bitexact(tmp_path, per_channel):
+    m = synth.fno2d_model(9, width=16, mh=5, mw=4, L=3, H=16, W=32, n_calib=2,
+                          per_channel=per_channel)
+    p = str(tmp_path / "m.nneuroir")
+    ir.write(p, m)
+    x = synth.fno2d_inputs(np.random.default_rng(3), 2, 16, 32)
+    want = Reference().run(p, x, 1)
+    got = Oracle().fno2d_forward(m, x, mode=0)
+    assert np.array_equal(_bits(got), _bits(want))
+
+
+# ------------------------------------------------------------- INT8 composition
+def test_int8_mode_close_to_fake_quant_network():
+    """The INT8 path differs from the FP32 fake-quant network only by the activation
+    quantisation of the layer inputs: outputs agree to a few output steps."""
+    m = synth.fno2d_model(4, width=16, mh=4, mw=4, L=2, H=16, W=16, n_calib=2)
+    x = synth.fno2d_inputs(np.random.default_rng(8), 2, 16, 16)
+    o = Oracle()
+    y0 = o.fno2d_forward(m, x, mode=0)
+    y1, taps = o.fno2d_forward(m, x, mode=1, taps=True)
+    step = m.qparams["proj_out.output"].scale
+    assert np.abs(y1 - y0).max() <= 16 * step
+    # layer-0 codes are the lift output's codes
+    assert taps["codes_in.0"].min() >= -128 and taps["codes_in.0"].max() <= 127
+    assert len(np.unique(taps["codes_in.1"])) > 20
