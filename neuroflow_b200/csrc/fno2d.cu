@@ -70,7 +70,7 @@ template <int C>
 __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, int64_t M,
                                                    int in_ch, const float* __restrict__ w,
                                                    const float* __restrict__ b, float s, int zp,
-                                                   int8_t* __restrict__ codes) {
+                                                   float inv_s, int8_t* __restrict__ codes) {
     __shared__ float sw[C * 8];
     __shared__ float sb[C];
     for (int i = threadIdx.x; i < C * in_ch; i += blockDim.x) sw[i] = w[i];
@@ -87,7 +87,8 @@ __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, 
         for (int o = 0; o < C; ++o) {
             float acc = sb[o];
             for (int k = 0; k < in_ch; ++k) acc = __fmaf_rn(xi[k], sw[o * in_ch + k], acc);
-            const uint32_t byte = static_cast<uint32_t>(static_cast<int>(fq_code(acc, s, zpf))) & 0xFFu;
+            const uint32_t byte =
+                static_cast<uint32_t>(static_cast<int>(fq_code_fast(acc, s, inv_s, zpf))) & 0xFFu;
             if ((o & 3) == 0) words[o >> 2] = byte;
             else words[o >> 2] |= byte << (8 * (o & 3));
         }
@@ -203,45 +204,84 @@ __global__ void __launch_bounds__(256) spec_mix_kernel(const float2* __restrict_
 
 // ---------------------------------------------------------------------------
 // layer / projection: tcgen05 GEMM over 128-point tiles with fused epilogues.
+//
+// TMEM per accumulator stage: [0, C) int32 local-layer accumulator, [C, C+16)
+// int32 sum_a (ones block), and with TCX [kX1Col, kX1Col + C) the fp32 spectral
+// branch x1, produced by 3xTF32 tcgen05 MMAs:
+//   x1[p][o] = sum_j Binv[p][j] * T[o][j],  j = 2 kw + {re, im},
+//   Binv[p][2kw] = f cos(2 pi kw w/W)/W,  Binv[p][2kw+1] = -f sin(2 pi kw w/W)/W,
+//   T[o][2kw] + i T[o][2kw+1] = sum_kh Y[kh][kw][o] e^{2 pi i kh h/H}/H,
+// with each fp32 operand split into a tf32 "hi" part and the remainder "lo" and the
+// product accumulated as hi*hi + lo*hi + hi*lo (error ~2^-21 relative).  TCX needs the
+// tile to be one grid row (W == 128); narrower grids evaluate x1 on CUDA cores.
 // ---------------------------------------------------------------------------
 constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA/TMEM, warps 4..11 epilogue
 constexpr int kEpiWarp0 = 4;
+constexpr int kLutMaxCells = 1536;
 
-template <int C, int MH, int MW, bool PROJ>
+template <int C, int MH, int MW, bool PROJ, bool TCX>
 struct LCfg {
     static constexpr int kEpiWarps = PROJ ? 4 : 8;
-    static constexpr int kRowBytes = C;                   // 32 or 64 (SW32 / SW64)
     static constexpr int kABytes = 128 * C;
-    static constexpr int kStages = 4;
-    static constexpr int kAccCols = ((C + 16 + 31) / 32) * 32;
+    static constexpr int kStages = 3;
+    static constexpr int kOnesCol = C;
+    static constexpr int kX1Col = ((C + 16 + 31) / 32) * 32;
+    static constexpr int kAccCols = TCX ? kX1Col + C : kX1Col;
     static constexpr int kAccStages = 2;
     static constexpr int kTmemCols = pow2ceil(kAccStages * kAccCols);
     static constexpr int kCols = PROJ ? C : C / 2;        // columns per epilogue warp
     static constexpr int kCh = kCols < 32 ? kCols : 32;   // columns per TMEM load
     static constexpr int kRmax = 4;                       // rows per tile (W >= 32)
+    static constexpr int kKx = 32;                        // padded K of the x1 MMA (fp32)
+    static_assert(!TCX || 2 * MW <= kKx, "x1 MMA K");
+    static constexpr int up1k(int v) { return (v + 1023) / 1024 * 1024; }
     static constexpr int kOffW = 0;
-    static constexpr int kOffOnes = 4096 > C * C ? 4096 : C * C;
+    static constexpr int kOffOnes = up1k(C * C);
     static constexpr int kOffA = kOffOnes + 1024;
     static constexpr int kOffStage = kOffA + kStages * kABytes;
-    static constexpr int kStageBytes = 32 * (C / 2);      // one warp's half tile of codes
-    static constexpr int kOffY = kOffStage + 8 * 2 * 1024;
+    static constexpr int kOffY = kOffStage + (PROJ ? 0 : 8 * 2 * 1024);
     static constexpr int kYBytes = PROJ ? 0 : MH * MW * C * 8;
-    static constexpr int kOffT = kOffY + kYBytes;
-    static constexpr int kTBytes = PROJ ? 0 : kRmax * MW * C * 8;
+    static constexpr int kOffBinv = up1k(kOffY + kYBytes);
+    static constexpr int kBinvBytes = TCX ? 2 * 128 * kKx * 4 : 0;        // hi, lo
+    static constexpr int kOffTop = kOffBinv + kBinvBytes;
+    static constexpr int kTopBytes = TCX ? 2 * 2 * C * kKx * 4 : 0;       // 2 buffers x (hi, lo)
+    static constexpr int kOffT = kOffTop + kTopBytes;
+    static constexpr int kTBytes = (PROJ || TCX) ? 0 : kRmax * MW * C * 8;
     static constexpr int kOffTw = kOffT + kTBytes;
-    static constexpr int kTwBytes = PROJ ? 0 : MW * 128 * 8;
-    static constexpr int kOffCol = kOffTw + kTwBytes;
-    static constexpr int kColBytes = 8 * C * 4 + 4 * 8 * C * 4;  // params + proj_out weights
+    static constexpr int kTwBytes = (PROJ || TCX) ? 0 : MW * 128 * 8;
+    static constexpr int kOffLut = kOffTw + kTwBytes;
+    static constexpr int kLutBytes = PROJ ? 256 * 4 : kLutMaxCells * 16;  // code cells / act table
+    static constexpr int kOffCol = kOffLut + kLutBytes;
+    static constexpr int kColBytes = C * 16 + 4 * C * 4 + 16;           // params, proj_out w, b
     static constexpr int kOffBars = kOffCol + kColBytes;
-    static constexpr int kSmemBytes = kOffBars + 8 * (2 * kStages + 2 * kAccStages + 1) + 16 + 1024;
+    static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2 + 1;
+    static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
     static_assert(kSmemBytes <= 227 * 1024, "smem");
 };
 
-template <int C, int MH, int MW, bool PROJ>
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+    hi = __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+    lo = __fsub_rn(x, hi);
+}
+
+// the next layer's code from z via the host-built table (nfx_lut.h)
+__device__ __forceinline__ int code_from_lut(float z, const int4* lut, int ncells, float zlo,
+                                             float inv_delta) {
+    const float fi = __fmul_rn(__fsub_rn(z, zlo), inv_delta);
+    int idx = __float2int_rz(fi);
+    idx = idx < 0 ? 0 : (idx > ncells - 1 ? ncells - 1 : idx);
+    const int4 c = lut[idx];
+    const int base = (c.z << 24) >> 24;
+    const int d1 = (c.z << 16) >> 24;
+    const int d2 = (c.z << 8) >> 24;
+    return base + (z >= __int_as_float(c.x) ? d1 : 0) + (z >= __int_as_float(c.y) ? d2 : 0);
+}
+
+template <int C, int MH, int MW, bool PROJ, bool TCX>
 __global__ void __launch_bounds__(kThreads, 1)
 layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmOut,
              const LayerArgs p) {
-    using L = LCfg<C, MH, MW, PROJ>;
+    using L = LCfg<C, MH, MW, PROJ, TCX>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -250,19 +290,21 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
     uint8_t* sA = smem + L::kOffA;
     uint8_t* sStage = smem + L::kOffStage;
     float2* sY = reinterpret_cast<float2*>(smem + L::kOffY);
+    uint8_t* sBinv = smem + L::kOffBinv;
+    uint8_t* sTop = smem + L::kOffTop;
     float2* sT = reinterpret_cast<float2*>(smem + L::kOffT);
     float2* sTw = reinterpret_cast<float2*>(smem + L::kOffTw);
-    float* sSWSA = reinterpret_cast<float*>(smem + L::kOffCol);  // sW[o] * s_in
-    int* sZpW = reinterpret_cast<int*>(sSWSA + C);
-    int* sZs = sZpW + C;                                          // zp_in * sum_w[o]
-    float* sBias = reinterpret_cast<float*>(sZs + C);
-    float* sWout = sBias + C;                                     // [out_ch][C] (PROJ)
+    int4* sLut = reinterpret_cast<int4*>(smem + L::kOffLut);
+    float* sAct = reinterpret_cast<float*>(smem + L::kOffLut);
+    float4* sCol = reinterpret_cast<float4*>(smem + L::kOffCol);  // {sW*s_in, zp_w, zp_in*sum_w, bias}
+    float* sWout = reinterpret_cast<float*>(sCol + C);            // [out_ch][C] (PROJ)
     float* sBout = sWout + 4 * C;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBars);
     uint64_t* empty = full + L::kStages;
     uint64_t* accFull = empty + L::kStages;
     uint64_t* accEmpty = accFull + L::kAccStages;
-    uint64_t* epiBar = accEmpty + L::kAccStages;
+    uint64_t* tReady = accEmpty + L::kAccStages;
+    uint64_t* epiBar = tReady + 2;
     uint32_t* sTmem = reinterpret_cast<uint32_t*>(epiBar + 1);
     volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
 
@@ -271,6 +313,8 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
     const int num_tiles = static_cast<int>((p.M + 127) / 128);
     const int t_begin = static_cast<int>(static_cast<int64_t>(num_tiles) * blockIdx.x / gridDim.x);
     const int t_end = static_cast<int>(static_cast<int64_t>(num_tiles) * (blockIdx.x + 1) / gridDim.x);
+    const bool use_lut = !PROJ && p.lut_cells > 0;
+    const bool use_act = PROJ && p.act_table != nullptr && p.fq_out.kind == 1;
 
     // ---- set-up
     {
@@ -284,17 +328,38 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
             const uint32_t one = (idx * 16 < C) ? 0x01010101u : 0u;  // row 0 = ones
             *reinterpret_cast<uint4*>(sOnes + idx * 16) = make_uint4(one, one, one, one);
         }
-        for (int o = threadIdx.x; o < C; o += kThreads) {
-            sSWSA[o] = __fmul_rn(p.scale_w[o], p.s_in);
-            sZpW[o] = p.zp_w[o];
-            sZs[o] = p.zp_in * p.sum_w[o];
-            sBias[o] = p.bias[o];
-        }
+        for (int o = threadIdx.x; o < C; o += kThreads)
+            sCol[o] = make_float4(__fmul_rn(p.scale_w[o], p.s_in), __int_as_float(p.zp_w[o]),
+                                  __int_as_float(p.zp_in * p.sum_w[o]), p.bias[o]);
         if (PROJ) {
             for (int i = threadIdx.x; i < p.out_ch * C; i += kThreads) sWout[i] = p.w_out[i];
             for (int i = threadIdx.x; i < p.out_ch; i += kThreads) sBout[i] = p.b_out[i];
+            if (use_act)
+                for (int i = threadIdx.x; i < 256; i += kThreads) sAct[i] = p.act_table[i];
         } else {
-            for (int i = threadIdx.x; i < MW * p.W; i += kThreads) sTw[i] = p.twi_w[i];
+            if (use_lut)
+                for (int i = threadIdx.x; i < p.lut_cells; i += kThreads) sLut[i] = p.code_lut[i];
+            if constexpr (TCX) {
+                // Binv (A operand, 128 points x 32, SW128 K-major), hi and lo
+                for (int idx = threadIdx.x; idx < 128 * L::kKx; idx += kThreads) {
+                    const int w = idx / L::kKx, j = idx % L::kKx;
+                    float v = 0.0f;
+                    if (j < 2 * MW) {
+                        const float2 t = p.twi_w[(j >> 1) * p.W + w];
+                        v = (j & 1) ? -t.y : t.x;
+                    }
+                    float hi, lo;
+                    split_tf32(v, hi, lo);
+                    const uint32_t off = swz_offset(w * 128 + j * 4, 128);
+                    *reinterpret_cast<float*>(sBinv + off) = hi;
+                    *reinterpret_cast<float*>(sBinv + 128 * 128 + off) = lo;
+                }
+                // T operand buffers: zero (the K padding columns stay zero)
+                for (int idx = threadIdx.x; idx < L::kTopBytes / 16; idx += kThreads)
+                    reinterpret_cast<uint4*>(sTop)[idx] = make_uint4(0, 0, 0, 0);
+            } else {
+                for (int i = threadIdx.x; i < MW * p.W; i += kThreads) sTw[i] = p.twi_w[i];
+            }
         }
         if (threadIdx.x == 0) {
             for (int s = 0; s < L::kStages; ++s) {
@@ -305,6 +370,8 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                 mbar_init(&accFull[s], 1);
                 mbar_init(&accEmpty[s], L::kEpiWarps);
             }
+            mbar_init(&tReady[0], L::kEpiWarps * 32);
+            mbar_init(&tReady[1], L::kEpiWarps * 32);
             mbar_init(epiBar, L::kEpiWarps * 32);
             *sAbort = 0;
             fence_mbar_init();
@@ -354,6 +421,13 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                     atomicOr(p.err, kErrWaitTmaFull);
                     break;
                 }
+                if constexpr (TCX && !PROJ) {
+                    if (!mbar_wait(&tReady[it & 1], (it >> 1) & 1, sAbort)) {
+                        *sAbort = 1;
+                        atomicOr(p.err, kErrWaitDrain);
+                        break;
+                    }
+                }
                 tc_fence_after();
                 const uint32_t d = tmem_base + a * L::kAccCols;
                 const uint32_t aBase = smem_u32(sA + s * L::kABytes);
@@ -363,7 +437,26 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                     const uint64_t wd = umma_desc(smem_u32(sW) + kk * 32, C);
                     const uint64_t od = umma_desc(smem_u32(sOnes) + kk * 32, C);
                     mma_i8(d, ad, wd, idesc_i8(C), kk > 0 ? 1u : 0u);
-                    mma_i8(d + C, ad, od, idesc_i8(16), kk > 0 ? 1u : 0u);
+                    mma_i8(d + L::kOnesCol, ad, od, idesc_i8(16), kk > 0 ? 1u : 0u);
+                }
+                if constexpr (TCX && !PROJ) {
+                    const uint32_t dx = d + L::kX1Col;
+                    const uint32_t bhi = smem_u32(sBinv), blo = bhi + 128 * 128;
+                    const uint32_t thi = smem_u32(sTop) + (it & 1) * (2 * C * 128);
+                    const uint32_t tlo = thi + C * 128;
+                    constexpr uint32_t idx1 = idesc_tf32(C);
+#pragma unroll
+                    for (int kk = 0; kk < L::kKx / 8; ++kk)
+                        mma_tf32(dx, umma_desc(bhi + kk * 32, 128), umma_desc(thi + kk * 32, 128),
+                                 idx1, kk > 0 ? 1u : 0u);
+#pragma unroll
+                    for (int kk = 0; kk < L::kKx / 8; ++kk)
+                        mma_tf32(dx, umma_desc(blo + kk * 32, 128), umma_desc(thi + kk * 32, 128),
+                                 idx1, 1u);
+#pragma unroll
+                    for (int kk = 0; kk < L::kKx / 8; ++kk)
+                        mma_tf32(dx, umma_desc(bhi + kk * 32, 128), umma_desc(tlo + kk * 32, 128),
+                                 idx1, 1u);
                 }
                 mma_commit(&empty[s]);
                 mma_commit(&accFull[a]);
@@ -383,6 +476,7 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
         const int row = quad * 32 + lane;  // row of the 128-point tile
         const int P = p.H * p.W;
         const int R = 128 / p.W > 0 ? 128 / p.W : 1;
+        const float s_out = p.fq_out.scale, inv_out = p.fq_out.inv_scale;
         const float zpo = static_cast<float>(p.fq_out.zp);
         int cached_b = -1;
         int it = 0, nstore = 0;
@@ -395,41 +489,90 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
             return ok;
         };
         bool epi_ok = true;
-        for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+        // reload the cached spectrum when tile `tile` belongs to another sample
+        auto ensure_y = [&](int tile) -> bool {
+            const int b = static_cast<int>(static_cast<int64_t>(tile) * 128 / P);
+            if (b == cached_b) return true;
+            if (!epi_sync()) return false;
+            const float4* src = reinterpret_cast<const float4*>(p.Y + static_cast<int64_t>(b) * MH * MW * C);
+            float4* dst = reinterpret_cast<float4*>(sY);
+            for (int i = etid; i < MH * MW * C / 2; i += kEpiThreads) dst[i] = src[i];
+            cached_b = b;
+            return epi_sync();
+        };
+        // TCX: T of tile `tile` into operand buffer `buf` (hi/lo tf32 split, SW128 rows o)
+        auto compute_top = [&](int tile, int buf) {
             const int64_t g0 = static_cast<int64_t>(tile) * 128;
-            const int b = static_cast<int>(g0 / P);
+            const int h = static_cast<int>((g0 % P) / p.W);
+            const float2* eh = p.twi_h + h * MH;
+            uint8_t* thi = sTop + buf * (2 * C * 128);
+            uint8_t* tlo = thi + C * 128;
+            for (int idx = etid; idx < MW * C; idx += kEpiThreads) {
+                const int kw = idx / C, o = idx % C;
+                float tr = 0.f, ti = 0.f;
+#pragma unroll
+                for (int kh = 0; kh < MH; ++kh) {
+                    const float2 y = sY[(kh * MW + kw) * C + o];
+                    const float2 e = __ldg(eh + kh);
+                    tr = fmaf(y.x, e.x, fmaf(-y.y, e.y, tr));
+                    ti = fmaf(y.x, e.y, fmaf(y.y, e.x, ti));
+                }
+                float h0, l0, h1, l1;
+                split_tf32(tr, h0, l0);
+                split_tf32(ti, h1, l1);
+                const uint32_t o0 = swz_offset(o * 128 + (2 * kw) * 4, 128);
+                const uint32_t o1 = swz_offset(o * 128 + (2 * kw + 1) * 4, 128);
+                *reinterpret_cast<float*>(thi + o0) = h0;
+                *reinterpret_cast<float*>(thi + o1) = h1;
+                *reinterpret_cast<float*>(tlo + o0) = l0;
+                *reinterpret_cast<float*>(tlo + o1) = l1;
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&tReady[buf]);
+        };
+        if constexpr (TCX && !PROJ) {
+            if (t_begin < t_end) {
+                if (!ensure_y(t_begin)) epi_ok = false;
+                else compute_top(t_begin, 0);
+            }
+        }
+        for (int tile = t_begin; tile < t_end && epi_ok; ++tile, ++it) {
+            const int64_t g0 = static_cast<int64_t>(tile) * 128;
             const int p0 = static_cast<int>(g0 % P);
-            if (!PROJ) {
-                // inverse transform along H for this tile's rows: T[r][kw][o]
-                if (b != cached_b) {
-                    const float4* src = reinterpret_cast<const float4*>(
-                        p.Y + static_cast<int64_t>(b) * MH * MW * C);
-                    float4* dst = reinterpret_cast<float4*>(sY);
-                    for (int i = etid; i < MH * MW * C / 2; i += kEpiThreads) dst[i] = src[i];
-                    cached_b = b;
+            if constexpr (!PROJ) {
+                if constexpr (TCX) {
+                    if (tile + 1 < t_end) {
+                        if (!ensure_y(tile + 1)) {
+                            epi_ok = false;
+                            break;
+                        }
+                        compute_top(tile + 1, (it + 1) & 1);
+                    }
+                } else {
+                    // inverse transform along H for this tile's rows: T[r][kw][o]
+                    if (!ensure_y(tile)) {
+                        epi_ok = false;
+                        break;
+                    }
+                    const int h0 = p0 / p.W;
+                    for (int idx = etid; idx < R * MW * C; idx += kEpiThreads) {
+                        const int r = idx / (MW * C), rem = idx % (MW * C);
+                        const int kw = rem / C, o = rem % C;
+                        const float2* eh = p.twi_h + (h0 + r) * MH;
+                        float tr = 0.f, ti = 0.f;
+#pragma unroll
+                        for (int kh = 0; kh < MH; ++kh) {
+                            const float2 y = sY[(kh * MW + kw) * C + o];
+                            const float2 e = __ldg(eh + kh);
+                            tr = fmaf(y.x, e.x, fmaf(-y.y, e.y, tr));
+                            ti = fmaf(y.x, e.y, fmaf(y.y, e.x, ti));
+                        }
+                        sT[idx] = make_float2(tr, ti);
+                    }
                     if (!epi_sync()) {
                         epi_ok = false;
                         break;
                     }
-                }
-                const int h0 = p0 / p.W;
-                for (int idx = etid; idx < R * MW * C; idx += kEpiThreads) {
-                    const int r = idx / (MW * C), rem = idx % (MW * C);
-                    const int kw = rem / C, o = rem % C;
-                    const float2* eh = p.twi_h + (h0 + r) * MH;
-                    float tr = 0.f, ti = 0.f;
-#pragma unroll
-                    for (int kh = 0; kh < MH; ++kh) {
-                        const float2 y = sY[(kh * MW + kw) * C + o];
-                        const float2 e = __ldg(eh + kh);
-                        tr = fmaf(y.x, e.x, fmaf(-y.y, e.y, tr));
-                        ti = fmaf(y.x, e.y, fmaf(y.y, e.x, ti));
-                    }
-                    sT[idx] = make_float2(tr, ti);
-                }
-                if (!epi_sync()) {
-                    epi_ok = false;
-                    break;
                 }
             }
             const int a = it % L::kAccStages;
@@ -442,26 +585,29 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
             tc_fence_after();
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * L::kAccCols;
             uint32_t sum_u;
-            tmem_ld1(tbase + C, sum_u);
+            tmem_ld1(tbase + L::kOnesCol, sum_u);
             tmem_wait_ld();
             const int rconst = C * p.zp_in - 2 * static_cast<int>(sum_u);
-            // this point's position inside the tile's rows and its W twiddles
-            const int pr = (p0 % p.W + row) / p.W;           // local row index
+            // this point's position inside the tile's rows and its W twiddles (CUDA-core x1)
+            const int pr = (p0 % p.W + row) / p.W;
             const int pw = (p0 + row) % p.W;
             float2 ew_reg[MW];
-            if (!PROJ) {
+            if constexpr (!PROJ && !TCX) {
 #pragma unroll
                 for (int kw = 0; kw < MW; ++kw) ew_reg[kw] = sTw[kw * p.W + pw];
             }
-            float acc_out[4] = {0.f, 0.f, 0.f, 0.f};
-            if (PROJ) {
-                for (int j = 0; j < p.out_ch; ++j) acc_out[j] = sBout[j];
+            float acc_out[4];
+            if constexpr (PROJ) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc_out[j] = j < p.out_ch ? sBout[j] : 0.0f;
             }
 #pragma unroll 1
             for (int c0 = col0; c0 < col0 + L::kCols; c0 += L::kCh) {
                 uint32_t raw[32];
+                uint32_t x1r[32];
                 if constexpr (L::kCh == 32) {
                     tmem_ld32(tbase + c0, raw);
+                    if constexpr (TCX && !PROJ) tmem_ld32(tbase + L::kX1Col + c0, x1r);
                 } else {
                     asm volatile(
                         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -482,32 +628,51 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
 #pragma unroll
                     for (int j = 0; j < L::kCh; ++j) {
                         const int o = c0 + j;
-                        float v = dequant_ref(static_cast<int>(raw[j]), sZpW[o], rconst, sZs[o], sSWSA[o]);
-                        v = __fadd_rn(v, sBias[o]);
-                        v = apply_fq(v, p.fq_out);
-                        v = activation(v, p.act);
-                        for (int jj = 0; jj < p.out_ch; ++jj)
-                            acc_out[jj] = __fmaf_rn(v, sWout[jj * C + o], acc_out[jj]);
+                        const float4 cp = sCol[o];
+                        const int vint = static_cast<int>(raw[j]) + __float_as_int(cp.y) * rconst -
+                                         __float_as_int(cp.z);
+                        float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
+                        float g;
+                        if (use_act) {
+                            const float q = fq_code_fast(v, s_out, inv_out, zpo);
+                            g = sAct[static_cast<int>(q) + 128];
+                        } else {
+                            g = activation(apply_fq(v, p.fq_out), p.act);
+                        }
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj)
+                            if (jj < p.out_ch) acc_out[jj] = __fmaf_rn(g, sWout[jj * C + o], acc_out[jj]);
                     }
                 } else {
                     uint32_t packed[8];
 #pragma unroll
                     for (int j = 0; j < L::kCh; ++j) {
                         const int o = c0 + j;
-                        // x1: inverse W-axis transform of T at this point
-                        const float2* trow = sT + (pr * MW) * C + o;
-                        float x1 = 0.f;
+                        float x1;
+                        if constexpr (TCX) {
+                            x1 = __uint_as_float(x1r[j]);
+                        } else {
+                            const float2* trow = sT + (pr * MW) * C + o;
+                            x1 = 0.f;
 #pragma unroll
-                        for (int kw = 0; kw < MW; ++kw) {
-                            const float2 t = trow[kw * C];
-                            x1 = fmaf(t.x, ew_reg[kw].x, fmaf(-t.y, ew_reg[kw].y, x1));
+                            for (int kw = 0; kw < MW; ++kw) {
+                                const float2 t = trow[kw * C];
+                                x1 = fmaf(t.x, ew_reg[kw].x, fmaf(-t.y, ew_reg[kw].y, x1));
+                            }
                         }
-                        float v = dequant_ref(static_cast<int>(raw[j]), sZpW[o], rconst, sZs[o], sSWSA[o]);
-                        v = __fadd_rn(v, sBias[o]);
-                        const float x2 = fake_quant(v, p.fq_out.scale, zpo);
+                        const float4 cp = sCol[o];
+                        const int vint = static_cast<int>(raw[j]) + __float_as_int(cp.y) * rconst -
+                                         __float_as_int(cp.z);
+                        const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
+                        const float q2 = fq_code_fast(v, s_out, inv_out, zpo);
+                        const float x2 = __fmul_rn(__fsub_rn(q2, zpo), s_out);
                         const float z = __fadd_rn(x1, x2);
-                        const float hval = activation(z, p.act);
-                        const int code = static_cast<int>(fq_code(hval, p.fq_out.scale, zpo));
+                        int code;
+                        if (use_lut) {
+                            code = code_from_lut(z, sLut, p.lut_cells, p.lut_zlo, p.lut_inv_delta);
+                        } else {
+                            code = static_cast<int>(fq_code(activation(z, p.act), s_out, zpo));
+                        }
                         const uint32_t byte = static_cast<uint32_t>(code) & 0xFFu;
                         if ((j & 3) == 0) packed[j >> 2] = byte;
                         else packed[j >> 2] |= byte << (8 * (j & 3));
@@ -535,13 +700,24 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                     ++nstore;
                 }
             }
-            if (PROJ) {
+            if constexpr (PROJ) {
                 const int64_t m = g0 + row;
                 if (m < p.M) {
-                    for (int j = 0; j < p.out_ch; ++j)
-                        p.y[m * p.out_ch + j] = apply_fq(acc_out[j], p.fq_final);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (j >= p.out_ch) break;
+                        float yv = acc_out[j];
+                        if (p.fq_final.kind == 1) {
+                            const float zf = static_cast<float>(p.fq_final.zp);
+                            const float q = fq_code_fast(yv, p.fq_final.scale, p.fq_final.inv_scale, zf);
+                            yv = __fmul_rn(__fsub_rn(q, zf), p.fq_final.scale);
+                        } else {
+                            yv = apply_fq(yv, p.fq_final);
+                        }
+                        p.y[m * p.out_ch + j] = yv;
+                    }
                 }
-            } else {
+            } else if constexpr (!TCX) {
                 // every epilogue thread is done with sT before the next tile rewrites it
                 if (!epi_sync()) {
                     epi_ok = false;
@@ -580,7 +756,7 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
         const int grid = static_cast<int>(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
         if (pl.timer) pl.timer->begin("fno2d_lift", st);
         lift_kernel<C><<<grid, 256, 0, st>>>(pl.x, M, pl.in_ch, pl.lift_w, pl.lift_b,
-                                             pl.lift_s, pl.lift_zp, pl.codes[0]);
+                                             pl.lift_s, pl.lift_zp, pl.lift_inv_s, pl.codes[0]);
         if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
@@ -610,14 +786,6 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
         {
-            using LC = LCfg<C, MH, MW, false>;
-            auto k = layer_kernel<C, MH, MW, false>;
-            if ((e = set_smem(k, LC::kSmemBytes)) != cudaSuccess) return e;
-            CUtensorMap tin, tout;
-            if (!encode_2d(&tin, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur], C, M, C, C, 128, C) ||
-                !encode_2d(&tout, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur ^ 1], C, M, C, C / 2,
-                           32, C / 2 == 32 ? 32 : 0))
-                return cudaErrorInvalidValue;
             LayerArgs a = pl.layer[i].args;
             a.M = M;
             a.H = pl.H;
@@ -626,16 +794,31 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
             a.twi_w = pl.twi_w;
             a.twi_h = pl.twi_h;
             a.err = pl.err;
+            CUtensorMap tin, tout;
+            if (!encode_2d(&tin, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur], C, M, C, C, 128, C) ||
+                !encode_2d(&tout, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur ^ 1], C, M, C, C / 2,
+                           32, C / 2 == 32 ? 32 : 0))
+                return cudaErrorInvalidValue;
             if (pl.timer) pl.timer->begin("fno2d_layer", st);
-            k<<<grid_l, kThreads, LC::kSmemBytes, st>>>(tin, tout, a);
+            if (pl.W == 128) {
+                using LC = LCfg<C, MH, MW, false, true>;
+                auto k = layer_kernel<C, MH, MW, false, true>;
+                if ((e = set_smem(k, LC::kSmemBytes)) != cudaSuccess) return e;
+                k<<<grid_l, kThreads, LC::kSmemBytes, st>>>(tin, tout, a);
+            } else {
+                using LC = LCfg<C, MH, MW, false, false>;
+                auto k = layer_kernel<C, MH, MW, false, false>;
+                if ((e = set_smem(k, LC::kSmemBytes)) != cudaSuccess) return e;
+                k<<<grid_l, kThreads, LC::kSmemBytes, st>>>(tin, tout, a);
+            }
             if (pl.timer) pl.timer->end(st);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
         cur ^= 1;
     }
     {
-        using LC = LCfg<C, MH, MW, true>;
-        auto k = layer_kernel<C, MH, MW, true>;
+        using LC = LCfg<C, MH, MW, true, false>;
+        auto k = layer_kernel<C, MH, MW, true, false>;
         if ((e = set_smem(k, LC::kSmemBytes)) != cudaSuccess) return e;
         CUtensorMap tin;
         if (!encode_2d(&tin, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur], C, M, C, C, 128, C))

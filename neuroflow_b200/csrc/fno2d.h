@@ -15,6 +15,7 @@ struct FqParam {
     int kind;
     float scale;
     int zp;
+    float inv_scale;  // 1/scale (IEEE), for the division-free fast path
 };
 
 // Arguments of one tcgen05 layer launch (local 1x1 layer or the projection).
@@ -34,6 +35,12 @@ struct LayerArgs {
     const float2* Y;      // (B, MH*MW, C) mixed spectrum
     const float2* twi_w;  // (MW, W)  f_kw * e^{+2 pi i kw w / W} / W
     const float2* twi_h;  // (H, MH)  e^{+2 pi i kh h / H} / H
+    // z -> next-layer code table (layer; lut_cells == 0: evaluate directly)
+    const int4* code_lut;  // CodeCell[lut_cells]
+    int lut_cells;
+    float lut_zlo, lut_inv_delta;
+    // activation of the 256 fake-quantised proj_q values (projection; nullptr: direct)
+    const float* act_table;
     // projection only
     const float* w_out;   // (out_ch, C) proj_out weight (fake-quantised at load)
     const float* b_out;   // (out_ch,)
@@ -63,6 +70,7 @@ struct Fno2dPlan {
     const float* lift_b;   // (C,)
     float lift_s;
     int lift_zp;
+    float lift_inv_s;
     int8_t* codes[2];      // ping-pong (B*H*W, C)
     float2* xpart;         // (B, H/HB, MH*MW, C)
     float2* Y;             // (B, MH*MW, C)

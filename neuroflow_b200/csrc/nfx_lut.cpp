@@ -1,0 +1,188 @@
+// nfx_lut.cpp -- construction of the exact activation/quantisation tables.
+//
+// This file is compiled for the host without FMA contraction (x86-64 baseline), so
+// every float operation below rounds exactly where written.  The reference build
+// (GCC -O3 -mfma) contracts one product of its GELU, z + 0.044715f*z*z*z, into
+// fma(z, (0.044715f*z)*z, z); std::fma reproduces that.  tanh is the C library's
+// tanhf, the function the reference calls.
+#include "nfx_lut.h"
+
+#include <cmath>
+#include <cstring>
+#include <limits>
+
+namespace nfx {
+namespace {
+
+float next_up(float x) { return std::nextafter(x, std::numeric_limits<float>::infinity()); }
+
+// order-preserving map of finite floats to integers, and back
+int64_t f2o(float f) {
+    int32_t i;
+    std::memcpy(&i, &f, 4);
+    return i >= 0 ? static_cast<int64_t>(i) : -static_cast<int64_t>(i & 0x7FFFFFFF);
+}
+float o2f(int64_t o) {
+    int32_t i = o >= 0 ? static_cast<int32_t>(o) : static_cast<int32_t>((-o) | 0x80000000u);
+    float f;
+    std::memcpy(&f, &i, 4);
+    return f;
+}
+
+struct Transition {
+    float t;         // smallest float with the new code (bisection result)
+    int before, after;
+};
+
+}  // namespace
+
+float act_ref(float z, int act) {
+    if (act == 1) return z < 0.0f ? 0.0f : z;
+    const float c = std::sqrt(2.0f / static_cast<float>(3.14159265358979323846));
+    const float t = (0.044715f * z) * z;
+    const float inner = std::fma(z, t, z);
+    const float th = std::tanh(c * inner);
+    return (0.5f * z) * (1.0f + th);
+}
+
+float fq_code_ref(float v, float s, float zp) {
+    float q = std::round(v / s) + zp;
+    if (q < -128.0f) q = -128.0f;
+    if (q > 127.0f) q = 127.0f;
+    return q;
+}
+
+std::vector<float> build_act_table(float s, int zp, int act) {
+    std::vector<float> t(256);
+    const float zpf = static_cast<float>(zp);
+    for (int k = -128; k <= 127; ++k) t[k + 128] = act_ref((static_cast<float>(k) - zpf) * s, act);
+    return t;
+}
+
+bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::string& why) {
+    if (!(s > 0.0f) || !std::isfinite(s)) {
+        why = "scale must be positive and finite";
+        return false;
+    }
+    const float zpf = static_cast<float>(zp);
+    auto code = [&](float z) { return static_cast<int>(fq_code_ref(act_ref(z, act), s, zpf)); };
+
+    // scan range: the negative branch of GELU is bounded below by -0.17, so every
+    // breakpoint with z < 0 lies above -64; on the positive side codes saturate by
+    // z = (128 - zp) * s (act(z) <= z there).
+    const float zmin = -64.0f;
+    const float zmax = std::fmax(64.0f, (129.0f - zpf) * s * 1.01f);
+    if (code(zmin) != code(-1.0e30f)) {
+        why = "activation does not settle below z = -64";
+        return false;
+    }
+    const double h = std::fmin(0.25, 0.5 * s) / 64.0;  // far below the breakpoint spacing
+    std::vector<Transition> tr;
+    float prev_z = zmin;
+    int prev_c = code(zmin);
+    const int64_t nsteps = static_cast<int64_t>(std::ceil((zmax - zmin) / h));
+    for (int64_t i = 1; i <= nsteps; ++i) {
+        const float z = i == nsteps ? zmax : static_cast<float>(zmin + h * i);
+        const int c = code(z);
+        if (c != prev_c) {
+            // bisection over consecutive floats: smallest z' in (prev_z, z] with code != prev_c
+            int64_t lo = f2o(prev_z), hi = f2o(z);
+            while (hi - lo > 1) {
+                const int64_t mid = lo + (hi - lo) / 2;
+                if (code(o2f(mid)) == prev_c) lo = mid;
+                else hi = mid;
+            }
+            tr.push_back({o2f(hi), prev_c, c});
+        }
+        prev_z = z;
+        prev_c = c;
+    }
+    if (code(zmax) != code(1.0e30f)) {
+        why = "activation does not saturate within the scan range";
+        return false;
+    }
+    for (const auto& t : tr) {
+        if (std::abs(t.after - t.before) != 1) {
+            why = "code jumps by more than one step between scan points";
+            return false;
+        }
+    }
+    if (tr.empty()) {
+        out.zlo = 0.0f;
+        out.inv_delta = 1.0f;
+        out.cells.assign(1, CodeCell{std::numeric_limits<float>::infinity(),
+                                     std::numeric_limits<float>::infinity(),
+                                     code(0.0f) & 0xFF, 0});
+        return true;
+    }
+    double delta = std::fmin(0.25, 0.5 * s);
+    const double lo_z = tr.front().t, hi_z = tr.back().t;
+    for (int attempt = 0; attempt < 8; ++attempt, delta *= 0.5) {
+        const double zlo = lo_z - 2.0 * delta;
+        const int ncells = static_cast<int>(std::ceil((hi_z - zlo) / delta)) + 2;
+        if (ncells > max_cells) {
+            why = "code table would need more than the allowed number of cells";
+            return false;
+        }
+        const double margin = delta / 64.0;
+        std::vector<CodeCell> cells(static_cast<size_t>(ncells));
+        bool ok = true;
+        size_t first = 0;  // first transition not left of the current cell's range
+        for (int j = 0; j < ncells && ok; ++j) {
+            const double a = zlo + delta * j - margin;
+            const double b = (j == ncells - 1) ? 1e30 : zlo + delta * (j + 1) + margin;
+            while (first < tr.size() && tr[first].t < a) ++first;
+            const int base = first == 0 ? tr.front().before : tr[first - 1].after;
+            CodeCell c{std::numeric_limits<float>::infinity(), std::numeric_limits<float>::infinity(),
+                       0, 0};
+            int d[2] = {0, 0};
+            int n = 0;
+            for (size_t k = first; k < tr.size() && tr[k].t < b; ++k) {
+                if (n == 2) {
+                    ok = false;
+                    break;
+                }
+                (n == 0 ? c.t1 : c.t2) = tr[k].t;
+                d[n++] = tr[k].after - tr[k].before;
+            }
+            c.packed = (base & 0xFF) | ((d[0] & 0xFF) << 8) | ((d[1] & 0xFF) << 16);
+            cells[j] = c;
+        }
+        if (!ok) continue;
+        out.zlo = static_cast<float>(zlo);
+        out.inv_delta = static_cast<float>(1.0 / delta);
+        out.cells = std::move(cells);
+        // self-check on random points against the direct evaluation
+        uint32_t st = 12345u;
+        for (int k = 0; k < 20000; ++k) {
+            st = st * 1664525u + 1013904223u;
+            const float z = static_cast<float>(lo_z - 1.0 + (hi_z - lo_z + 2.0) * (st >> 8) / 16777216.0);
+            float fi = (z - out.zlo) * out.inv_delta;
+            int idx = static_cast<int>(fi);
+            if (fi < 0.0f) idx = 0;
+            if (idx > ncells - 1) idx = ncells - 1;
+            const CodeCell& cc = out.cells[idx];
+            const int base = static_cast<int8_t>(cc.packed & 0xFF);
+            const int d1 = static_cast<int8_t>((cc.packed >> 8) & 0xFF);
+            const int d2 = static_cast<int8_t>((cc.packed >> 16) & 0xFF);
+            const int got = base + (z >= cc.t1 ? d1 : 0) + (z >= cc.t2 ? d2 : 0);
+            const int want = code(z);
+            if (got != want) {
+                // accept only the flip windows of a few ulps around a breakpoint
+                bool near = false;
+                for (const auto& t : tr)
+                    if (std::fabs(static_cast<double>(z) - t.t) <= 64.0 * std::fabs(next_up(t.t) - t.t))
+                        near = true;
+                if (!near) {
+                    why = "code table self-check failed";
+                    return false;
+                }
+            }
+        }
+        return true;
+    }
+    why = "no cell size gives at most two breakpoints per cell";
+    return false;
+}
+
+}  // namespace nfx

@@ -19,6 +19,7 @@
 #include "fno2d.h"
 #include "nfx_internal.h"
 #include "nfx_ir.h"
+#include "nfx_lut.h"
 
 namespace nfx {
 int set_thread_error(int code, const std::string& msg);
@@ -134,7 +135,7 @@ T* upload(nfx_runtime* rt, const T* host, size_t count) {
 }
 
 nfx::FqParam fq_for(const nfx::IrModel& m, const std::string& key) {
-    nfx::FqParam f{0, 1.0f, 0};
+    nfx::FqParam f{0, 1.0f, 0, 1.0f};
     if (!m.quant_enabled) return f;
     auto it8 = m.activation_fp8_qparams.find(key);
     if (it8 != m.activation_fp8_qparams.end()) {
@@ -147,6 +148,7 @@ nfx::FqParam fq_for(const nfx::IrModel& m, const std::string& key) {
         f.kind = 1;
         f.scale = it->second.scale;
         f.zp = it->second.zero_point;
+        f.inv_scale = 1.0f / f.scale;
     }
     return f;
 }
@@ -245,14 +247,33 @@ void fno2d_enable_int8(nfx_runtime* rt) {
             pl.layer[i].s_in = in.scale;
             pl.layer[i].zp_in = in.zero_point;
             a.fq_out = fq_for(m, "locs." + std::to_string(i) + ".output");
+            // exact z -> next-code table (falls back to direct evaluation when absent)
+            nfx::CodeLut lut;
+            std::string why;
+            a.code_lut = nullptr;
+            a.lut_cells = 0;
+            if (nfx::build_code_lut(a.fq_out.scale, a.fq_out.zp, a.act, 1536, lut, why)) {
+                a.code_lut = reinterpret_cast<const int4*>(upload(rt, lut.cells.data(), lut.cells.size()));
+                if (a.code_lut) {
+                    a.lut_cells = static_cast<int>(lut.cells.size());
+                    a.lut_zlo = lut.zlo;
+                    a.lut_inv_delta = lut.inv_delta;
+                }
+            }
         } else {
             a.fq_out = fq_for(m, "proj_q.output");
             a.fq_final = fq_for(m, "proj_out.output");
+            a.act_table = nullptr;
+            if (a.fq_out.kind == 1) {
+                const std::vector<float> t = nfx::build_act_table(a.fq_out.scale, a.fq_out.zp, a.act);
+                a.act_table = upload(rt, t.data(), t.size());
+            }
         }
     }
     const nfx::QP lq = m.activation_qparams.at("lift.output");
     pl.lift_s = lq.scale;
     pl.lift_zp = lq.zero_point;
+    pl.lift_inv_s = 1.0f / lq.scale;
     rt->int8_enabled = true;
 }
 

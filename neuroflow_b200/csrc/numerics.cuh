@@ -30,6 +30,21 @@ __device__ __forceinline__ float fq_code(float v, float s, float zp) {
     return q;
 }
 
+// The same code without a division on the common path.  r = v * (1/s) differs from
+// the correctly rounded quotient v / s by less than 2^-12 while |v/s| < 2^10, so
+// rounding r to the nearest integer gives the quotient's rounding whenever r is not
+// within 2^-11 of a half-integer (there round-half-away and round-half-even agree
+// too).  Inputs near a half-integer, |r| >= 2^10, and NaN take the exact path.
+__device__ __forceinline__ float fq_code_fast(float v, float s, float inv_s, float zp) {
+    const float r = __fmul_rn(v, inv_s);
+    const float k = rintf(r);
+    if (!(fabsf(__fsub_rn(r, k)) < 0.49951171875f) || !(fabsf(r) < 1024.0f))
+        return fq_code(v, s, zp);
+    float q = __fadd_rn(k, zp);
+    q = fminf(fmaxf(q, -128.0f), 127.0f);
+    return q;
+}
+
 // fake-quant round trip: (q - zp) * s.
 __device__ __forceinline__ float fake_quant(float v, float s, float zp) {
     return __fmul_rn(__fsub_rn(fq_code(v, s, zp), zp), s);
