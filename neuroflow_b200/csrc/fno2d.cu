@@ -71,31 +71,47 @@ __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, 
                                                    int in_ch, const float* __restrict__ w,
                                                    const float* __restrict__ b, float s, int zp,
                                                    float inv_s, int8_t* __restrict__ codes) {
+    // one thread per (point, group of 16 channels)
+    constexpr int kG = C / 16;
     __shared__ float sw[C * 8];
     __shared__ float sb[C];
     for (int i = threadIdx.x; i < C * in_ch; i += blockDim.x) sw[i] = w[i];
     for (int i = threadIdx.x; i < C; i += blockDim.x) sb[i] = b[i];
     __syncthreads();
     const float zpf = static_cast<float>(zp);
-    for (int64_t m = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; m < M;
-         m += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        float xi[8];
+    const int64_t n = M * kG;
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < n;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t m = t / kG;
+        const int o0 = static_cast<int>(t % kG) * 16;
+        float acc[16];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) xi[k] = k < in_ch ? x[m * in_ch + k] : 0.0f;
-        uint32_t words[C / 4];
+        for (int j = 0; j < 16; ++j) acc[j] = sb[o0 + j];
+        for (int k = 0; k < in_ch; ++k) {
+            const float xv = __ldg(x + m * in_ch + k);
 #pragma unroll
-        for (int o = 0; o < C; ++o) {
-            float acc = sb[o];
-            for (int k = 0; k < in_ch; ++k) acc = __fmaf_rn(xi[k], sw[o * in_ch + k], acc);
-            const uint32_t byte =
-                static_cast<uint32_t>(static_cast<int>(fq_code_fast(acc, s, inv_s, zpf))) & 0xFFu;
-            if ((o & 3) == 0) words[o >> 2] = byte;
-            else words[o >> 2] |= byte << (8 * (o & 3));
+            for (int j = 0; j < 16; ++j) acc[j] = __fmaf_rn(xv, sw[(o0 + j) * in_ch + k], acc[j]);
         }
-        uint4* dst = reinterpret_cast<uint4*>(codes + m * C);
+        uint32_t words[4];
+        uint32_t badmask = 0;
 #pragma unroll
-        for (int v = 0; v < C / 16; ++v)
-            dst[v] = make_uint4(words[4 * v], words[4 * v + 1], words[4 * v + 2], words[4 * v + 3]);
+        for (int j = 0; j < 16; ++j) {
+            bool bad;
+            const float q = fq_code_try(acc[j], inv_s, zpf, bad);
+            badmask |= static_cast<uint32_t>(bad) << j;
+            const uint32_t byte = static_cast<uint32_t>(static_cast<int>(q)) & 0xFFu;
+            if ((j & 3) == 0) words[j >> 2] = byte;
+            else words[j >> 2] |= byte << (8 * (j & 3));
+        }
+        while (badmask) {  // rare: quotient near a half-integer, huge or NaN
+            const int j = __ffs(badmask) - 1;
+            badmask &= badmask - 1;
+            float a = sb[o0 + j];
+            for (int k = 0; k < in_ch; ++k) a = __fmaf_rn(__ldg(x + m * in_ch + k), sw[(o0 + j) * in_ch + k], a);
+            const uint32_t byte = static_cast<uint32_t>(static_cast<int>(fq_code(a, s, zpf))) & 0xFFu;
+            words[j >> 2] = (words[j >> 2] & ~(0xFFu << (8 * (j & 3)))) | (byte << (8 * (j & 3)));
+        }
+        *reinterpret_cast<uint4*>(codes + m * C + o0) = make_uint4(words[0], words[1], words[2], words[3]);
     }
 }
 
@@ -217,7 +233,7 @@ __global__ void __launch_bounds__(256) spec_mix_kernel(const float2* __restrict_
 // ---------------------------------------------------------------------------
 constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA/TMEM, warps 4..11 epilogue
 constexpr int kEpiWarp0 = 4;
-constexpr int kLutMaxCells = 1536;
+constexpr int kLutMaxCells = 3072;
 
 template <int C, int MH, int MW, bool PROJ, bool TCX>
 struct LCfg {
@@ -250,7 +266,7 @@ struct LCfg {
     static constexpr int kOffTw = kOffT + kTBytes;
     static constexpr int kTwBytes = (PROJ || TCX) ? 0 : MW * 128 * 8;
     static constexpr int kOffLut = kOffTw + kTwBytes;
-    static constexpr int kLutBytes = PROJ ? 256 * 4 : kLutMaxCells * 16;  // code cells / act table
+    static constexpr int kLutBytes = PROJ ? 256 * 4 : kLutMaxCells * 8;   // code cells / act table
     static constexpr int kOffCol = kOffLut + kLutBytes;
     static constexpr int kColBytes = C * 16 + 4 * C * 4 + 16;           // params, proj_out w, b
     static constexpr int kOffBars = kOffCol + kColBytes;
@@ -265,16 +281,15 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
 }
 
 // the next layer's code from z via the host-built table (nfx_lut.h)
-__device__ __forceinline__ int code_from_lut(float z, const int4* lut, int ncells, float zlo,
+__device__ __forceinline__ int code_from_lut(float z, const int2* lut, int ncells, float zlo,
                                              float inv_delta) {
     const float fi = __fmul_rn(__fsub_rn(z, zlo), inv_delta);
     int idx = __float2int_rz(fi);
     idx = idx < 0 ? 0 : (idx > ncells - 1 ? ncells - 1 : idx);
-    const int4 c = lut[idx];
-    const int base = (c.z << 24) >> 24;
-    const int d1 = (c.z << 16) >> 24;
-    const int d2 = (c.z << 8) >> 24;
-    return base + (z >= __int_as_float(c.x) ? d1 : 0) + (z >= __int_as_float(c.y) ? d2 : 0);
+    const int2 c = lut[idx];
+    const int base = (c.y << 24) >> 24;
+    const int d = (c.y << 16) >> 24;
+    return base + (z >= __int_as_float(c.x) ? d : 0);
 }
 
 template <int C, int MH, int MW, bool PROJ, bool TCX>
@@ -294,7 +309,7 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
     uint8_t* sTop = smem + L::kOffTop;
     float2* sT = reinterpret_cast<float2*>(smem + L::kOffT);
     float2* sTw = reinterpret_cast<float2*>(smem + L::kOffTw);
-    int4* sLut = reinterpret_cast<int4*>(smem + L::kOffLut);
+    int2* sLut = reinterpret_cast<int2*>(smem + L::kOffLut);
     float* sAct = reinterpret_cast<float*>(smem + L::kOffLut);
     float4* sCol = reinterpret_cast<float4*>(smem + L::kOffCol);  // {sW*s_in, zp_w, zp_in*sum_w, bias}
     float* sWout = reinterpret_cast<float*>(sCol + C);            // [out_ch][C] (PROJ)
@@ -504,7 +519,9 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
         auto compute_top = [&](int tile, int buf) {
             const int64_t g0 = static_cast<int64_t>(tile) * 128;
             const int h = static_cast<int>((g0 % P) / p.W);
-            const float2* eh = p.twi_h + h * MH;
+            float2 eh[MH];
+#pragma unroll
+            for (int kh = 0; kh < MH; ++kh) eh[kh] = __ldg(p.twi_h + h * MH + kh);
             uint8_t* thi = sTop + buf * (2 * C * 128);
             uint8_t* tlo = thi + C * 128;
             for (int idx = etid; idx < MW * C; idx += kEpiThreads) {
@@ -513,9 +530,8 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
 #pragma unroll
                 for (int kh = 0; kh < MH; ++kh) {
                     const float2 y = sY[(kh * MW + kw) * C + o];
-                    const float2 e = __ldg(eh + kh);
-                    tr = fmaf(y.x, e.x, fmaf(-y.y, e.y, tr));
-                    ti = fmaf(y.x, e.y, fmaf(y.y, e.x, ti));
+                    tr = fmaf(y.x, eh[kh].x, fmaf(-y.y, eh[kh].y, tr));
+                    ti = fmaf(y.x, eh[kh].y, fmaf(y.y, eh[kh].x, ti));
                 }
                 float h0, l0, h1, l1;
                 split_tf32(tr, h0, l0);
@@ -619,60 +635,91 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                         : "r"(tbase + c0));
                 }
                 tmem_wait_ld();
-                if (c0 + L::kCh >= col0 + L::kCols) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&accEmpty[a]);
-                }
+                const bool last_chunk = c0 + L::kCh >= col0 + L::kCols;
+                // The fast, branch-free pass over the chunk; elements whose fake-quant
+                // quotient lies next to a half-integer are fixed afterwards with the
+                // exact division (their accumulators are re-read from TMEM).
+                uint32_t bad = 0;
                 if constexpr (PROJ) {
+                    float g[32];
 #pragma unroll
                     for (int j = 0; j < L::kCh; ++j) {
-                        const int o = c0 + j;
-                        const float4 cp = sCol[o];
+                        const float4 cp = sCol[c0 + j];
                         const int vint = static_cast<int>(raw[j]) + __float_as_int(cp.y) * rconst -
                                          __float_as_int(cp.z);
-                        float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
-                        float g;
+                        const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
                         if (use_act) {
-                            const float q = fq_code_fast(v, s_out, inv_out, zpo);
-                            g = sAct[static_cast<int>(q) + 128];
+                            bool b;
+                            const float q = fq_code_try(v, inv_out, zpo, b);
+                            bad |= static_cast<uint32_t>(b) << j;
+                            g[j] = sAct[static_cast<int>(q) + 128];
                         } else {
-                            g = activation(apply_fq(v, p.fq_out), p.act);
+                            g[j] = activation(apply_fq(v, p.fq_out), p.act);
                         }
-#pragma unroll
-                        for (int jj = 0; jj < 4; ++jj)
-                            if (jj < p.out_ch) acc_out[jj] = __fmaf_rn(g, sWout[jj * C + o], acc_out[jj]);
                     }
-                } else {
-                    uint32_t packed[8];
+                    uint32_t any = __reduce_or_sync(0xffffffffu, bad);
+                    while (any) {
+                        const int j = __ffs(any) - 1;
+                        any &= any - 1;
+                        uint32_t rj;
+                        tmem_ld1(tbase + c0 + j, rj);
+                        tmem_wait_ld();
+                        if (bad & (1u << j)) {
+                            const float4 cp = sCol[c0 + j];
+                            const int vint = static_cast<int>(rj) + __float_as_int(cp.y) * rconst -
+                                             __float_as_int(cp.z);
+                            const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
+                            const float gj = sAct[static_cast<int>(fq_code(v, s_out, zpo)) + 128];
+#pragma unroll
+                            for (int k = 0; k < 32; ++k)
+                                if (k == j) g[k] = gj;
+                        }
+                    }
+                    if (last_chunk) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&accEmpty[a]);
+                    }
 #pragma unroll
                     for (int j = 0; j < L::kCh; ++j) {
-                        const int o = c0 + j;
-                        float x1;
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj)
+                            if (jj < p.out_ch)
+                                acc_out[jj] = __fmaf_rn(g[j], sWout[jj * C + c0 + j], acc_out[jj]);
+                    }
+                } else {
+                    // x1 of element j (tensor-core result, or CUDA-core inverse W-DFT)
+                    auto x1_of = [&](int j, uint32_t xbits) -> float {
                         if constexpr (TCX) {
-                            x1 = __uint_as_float(x1r[j]);
+                            return __uint_as_float(xbits);
                         } else {
-                            const float2* trow = sT + (pr * MW) * C + o;
-                            x1 = 0.f;
+                            const float2* trow = sT + (pr * MW) * C + c0 + j;
+                            float x1 = 0.f;
 #pragma unroll
                             for (int kw = 0; kw < MW; ++kw) {
                                 const float2 t = trow[kw * C];
                                 x1 = fmaf(t.x, ew_reg[kw].x, fmaf(-t.y, ew_reg[kw].y, x1));
                             }
+                            return x1;
                         }
-                        const float4 cp = sCol[o];
+                    };
+                    auto code_of = [&](float z) -> int {
+                        if (use_lut) return code_from_lut(z, sLut, p.lut_cells, p.lut_zlo, p.lut_inv_delta);
+                        return static_cast<int>(fq_code(activation(z, p.act), s_out, zpo));
+                    };
+                    uint32_t packed[8];
+#pragma unroll
+                    for (int j = 0; j < L::kCh; ++j) {
+                        const float x1 = x1_of(j, x1r[j]);
+                        const float4 cp = sCol[c0 + j];
                         const int vint = static_cast<int>(raw[j]) + __float_as_int(cp.y) * rconst -
                                          __float_as_int(cp.z);
                         const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
-                        const float q2 = fq_code_fast(v, s_out, inv_out, zpo);
+                        bool b;
+                        const float q2 = fq_code_try(v, inv_out, zpo, b);
+                        bad |= static_cast<uint32_t>(b) << j;
                         const float x2 = __fmul_rn(__fsub_rn(q2, zpo), s_out);
-                        const float z = __fadd_rn(x1, x2);
-                        int code;
-                        if (use_lut) {
-                            code = code_from_lut(z, sLut, p.lut_cells, p.lut_zlo, p.lut_inv_delta);
-                        } else {
-                            code = static_cast<int>(fq_code(activation(z, p.act), s_out, zpo));
-                        }
+                        const int code = code_of(__fadd_rn(x1, x2));
                         const uint32_t byte = static_cast<uint32_t>(code) & 0xFFu;
                         if ((j & 3) == 0) packed[j >> 2] = byte;
                         else packed[j >> 2] |= byte << (8 * (j & 3));
@@ -690,6 +737,32 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                         *reinterpret_cast<uint4*>(buf + off) =
                             make_uint4(packed[4 * j16], packed[4 * j16 + 1], packed[4 * j16 + 2],
                                        packed[4 * j16 + 3]);
+                    }
+                    uint32_t any = __reduce_or_sync(0xffffffffu, bad);
+                    while (any) {
+                        const int j = __ffs(any) - 1;
+                        any &= any - 1;
+                        uint32_t rj, xj = 0;
+                        tmem_ld1(tbase + c0 + j, rj);
+                        if constexpr (TCX) tmem_ld1(tbase + L::kX1Col + c0 + j, xj);
+                        tmem_wait_ld();
+                        if (bad & (1u << j)) {
+                            const float4 cp = sCol[c0 + j];
+                            const int vint = static_cast<int>(rj) + __float_as_int(cp.y) * rconst -
+                                             __float_as_int(cp.z);
+                            const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
+                            const float x2 = __fmul_rn(__fsub_rn(fq_code(v, s_out, zpo), zpo), s_out);
+                            const int code = code_of(__fadd_rn(x1_of(j, xj), x2));
+                            const uint32_t off = (kRow == 32)
+                                                     ? swz_offset(lane * 32 + (j >> 4) * 16, 32) + (j & 15)
+                                                     : static_cast<uint32_t>(lane * 16 + j);
+                            buf[off] = static_cast<uint8_t>(code & 0xFF);
+                        }
+                    }
+                    if (last_chunk) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&accEmpty[a]);
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
@@ -752,7 +825,7 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
     const int64_t M = static_cast<int64_t>(pl.B) * pl.H * pl.W;
     // lift
     {
-        const int64_t blocks64 = (M + 255) / 256;
+        const int64_t blocks64 = (M * (C / 16) + 255) / 256;
         const int grid = static_cast<int>(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
         if (pl.timer) pl.timer->begin("fno2d_lift", st);
         lift_kernel<C><<<grid, 256, 0, st>>>(pl.x, M, pl.in_ch, pl.lift_w, pl.lift_b,

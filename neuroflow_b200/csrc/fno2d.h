@@ -36,7 +36,7 @@ struct LayerArgs {
     const float2* twi_w;  // (MW, W)  f_kw * e^{+2 pi i kw w / W} / W
     const float2* twi_h;  // (H, MH)  e^{+2 pi i kh h / H} / H
     // z -> next-layer code table (layer; lut_cells == 0: evaluate directly)
-    const int4* code_lut;  // CodeCell[lut_cells]
+    const int2* code_lut;  // CodeCell[lut_cells] {breakpoint, base | d << 8}
     int lut_cells;
     float lut_zlo, lut_inv_delta;
     // activation of the 256 fake-quantised proj_q values (projection; nullptr: direct)

@@ -110,14 +110,12 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
     if (tr.empty()) {
         out.zlo = 0.0f;
         out.inv_delta = 1.0f;
-        out.cells.assign(1, CodeCell{std::numeric_limits<float>::infinity(),
-                                     std::numeric_limits<float>::infinity(),
-                                     code(0.0f) & 0xFF, 0});
+        out.cells.assign(1, CodeCell{std::numeric_limits<float>::infinity(), code(0.0f) & 0xFF});
         return true;
     }
     double delta = std::fmin(0.25, 0.5 * s);
     const double lo_z = tr.front().t, hi_z = tr.back().t;
-    for (int attempt = 0; attempt < 8; ++attempt, delta *= 0.5) {
+    for (int attempt = 0; attempt < 10; ++attempt, delta *= 0.5) {
         const double zlo = lo_z - 2.0 * delta;
         const int ncells = static_cast<int>(std::ceil((hi_z - zlo) / delta)) + 2;
         if (ncells > max_cells) {
@@ -133,19 +131,19 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
             const double b = (j == ncells - 1) ? 1e30 : zlo + delta * (j + 1) + margin;
             while (first < tr.size() && tr[first].t < a) ++first;
             const int base = first == 0 ? tr.front().before : tr[first - 1].after;
-            CodeCell c{std::numeric_limits<float>::infinity(), std::numeric_limits<float>::infinity(),
-                       0, 0};
-            int d[2] = {0, 0};
+            CodeCell c{std::numeric_limits<float>::infinity(), 0};
+            int d = 0;
             int n = 0;
             for (size_t k = first; k < tr.size() && tr[k].t < b; ++k) {
-                if (n == 2) {
+                if (n == 1) {
                     ok = false;
                     break;
                 }
-                (n == 0 ? c.t1 : c.t2) = tr[k].t;
-                d[n++] = tr[k].after - tr[k].before;
+                c.t = tr[k].t;
+                d = tr[k].after - tr[k].before;
+                ++n;
             }
-            c.packed = (base & 0xFF) | ((d[0] & 0xFF) << 8) | ((d[1] & 0xFF) << 16);
+            c.packed = (base & 0xFF) | ((d & 0xFF) << 8);
             cells[j] = c;
         }
         if (!ok) continue;
@@ -163,9 +161,8 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
             if (idx > ncells - 1) idx = ncells - 1;
             const CodeCell& cc = out.cells[idx];
             const int base = static_cast<int8_t>(cc.packed & 0xFF);
-            const int d1 = static_cast<int8_t>((cc.packed >> 8) & 0xFF);
-            const int d2 = static_cast<int8_t>((cc.packed >> 16) & 0xFF);
-            const int got = base + (z >= cc.t1 ? d1 : 0) + (z >= cc.t2 ? d2 : 0);
+            const int dd = static_cast<int8_t>((cc.packed >> 8) & 0xFF);
+            const int got = base + (z >= cc.t ? dd : 0);
             const int want = code(z);
             if (got != want) {
                 // accept only the flip windows of a few ulps around a breakpoint
@@ -181,7 +178,7 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
         }
         return true;
     }
-    why = "no cell size gives at most two breakpoints per cell";
+    why = "no cell size gives at most one breakpoint per cell";
     return false;
 }
 

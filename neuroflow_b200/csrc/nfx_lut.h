@@ -6,10 +6,10 @@
 //    with act the reference GELU (fno.cpp:36-48, glibc tanhf) or ReLU and fq_code the
 //    reference float quantiser (fno.cpp:497-505).  code(z) is a step function of the
 //    float z = x1 + x2.  The table splits z into uniform cells; each cell stores the
-//    code at its (slightly extended) left edge and at most two breakpoints inside,
+//    code at its (slightly extended) left edge and at most one breakpoint inside,
 //    found exactly by bisection over consecutive float values using the host's
 //    reference-equivalent arithmetic.  The GPU evaluates
-//        code = base + d1*(z >= t1) + d2*(z >= t2)
+//        code = base + d*(z >= t)
 //    for the cell of z.  Where float rounding makes code(z) flip back and forth within
 //    a few ulps of a breakpoint, the table keeps one breakpoint of that window.
 // 2. Activation table.  The projection applies the activation to a fake-quantised
@@ -24,9 +24,8 @@
 namespace nfx {
 
 struct CodeCell {
-    float t1, t2;   // breakpoints (+inf when unused)
-    int32_t packed; // base code (int8) | d1 (int8) << 8 | d2 (int8) << 16
-    int32_t pad;
+    float t;        // breakpoint (+inf when unused)
+    int32_t packed; // base code (int8) | d (int8) << 8
 };
 
 struct CodeLut {
@@ -41,7 +40,7 @@ float act_ref(float z, int act);
 float fq_code_ref(float v, float s, float zp);
 
 // Build the z -> code table for (s, zp, act).  Returns false (with a reason) if no
-// table with at most `max_cells` cells and two breakpoints per cell exists.
+// table with at most `max_cells` cells and one breakpoint per cell exists.
 bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::string& why);
 
 // act_ref((k - zp) * s) for k = -128..127 (index k + 128).

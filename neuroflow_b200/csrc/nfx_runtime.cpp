@@ -252,8 +252,8 @@ void fno2d_enable_int8(nfx_runtime* rt) {
             std::string why;
             a.code_lut = nullptr;
             a.lut_cells = 0;
-            if (nfx::build_code_lut(a.fq_out.scale, a.fq_out.zp, a.act, 1536, lut, why)) {
-                a.code_lut = reinterpret_cast<const int4*>(upload(rt, lut.cells.data(), lut.cells.size()));
+            if (nfx::build_code_lut(a.fq_out.scale, a.fq_out.zp, a.act, 3072, lut, why)) {
+                a.code_lut = reinterpret_cast<const int2*>(upload(rt, lut.cells.data(), lut.cells.size()));
                 if (a.code_lut) {
                     a.lut_cells = static_cast<int>(lut.cells.size());
                     a.lut_zlo = lut.zlo;

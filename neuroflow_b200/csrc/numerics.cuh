@@ -45,6 +45,16 @@ __device__ __forceinline__ float fq_code_fast(float v, float s, float inv_s, flo
     return q;
 }
 
+// Branch-free form of the fast path for unrolled epilogues: returns the fast code and
+// reports in `bad` whether the element needs the exact path (the caller fixes those
+// elements afterwards, outside the unrolled loop).
+__device__ __forceinline__ float fq_code_try(float v, float inv_s, float zp, bool& bad) {
+    const float r = __fmul_rn(v, inv_s);
+    const float k = rintf(r);
+    bad = !(fabsf(__fsub_rn(r, k)) < 0.49951171875f) || !(fabsf(r) < 1024.0f);
+    return fminf(fmaxf(__fadd_rn(k, zp), -128.0f), 127.0f);
+}
+
 // fake-quant round trip: (q - zp) * s.
 __device__ __forceinline__ float fake_quant(float v, float s, float zp) {
     return __fmul_rn(__fsub_rn(fq_code(v, s, zp), zp), s);
