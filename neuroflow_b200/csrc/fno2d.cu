@@ -814,6 +814,280 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
     }
 }
 
+// ---------------------------------------------------------------------------
+// spec_fwd_tc: the forward transform of a layer on tensor cores (W == 128).
+//
+// Row DFT (along W) as an exact integer GEMM: for a pair of grid rows,
+//   D_l[(r, c)][n] = sum_w code[h+r][w][c] * Blimb_l[n][w]      (tcgen05 kind::i8)
+// where the DFT basis B[j][w] (cos / -sin of 2 pi kw w / W, j = 2 kw + {0, 1}) is
+// scaled by 2^27, rounded to an integer and split into four balanced base-256
+// digits Blimb_0..3.  The codes are the MMA's A operand in MN-major layout (two
+// TMA-loaded [w][c] tiles, one per row, as the two 64-wide M atoms); the digit
+// matrices are the K-major B operand.  Recombined exactly in int64,
+//   F[h][j][c] = s * (sum_l D_l 256^(3-l) - zp * sum_w Bint[j][w]) / 2^27
+// is the row DFT of the snapped activation (code - zp) * s.  The H-axis DFT is then
+// accumulated on CUDA cores over the unit's rows:
+//   X[kh][kw][c] += F[h][kw][c] * e^{-2 pi i kh h / H}.
+// A work unit is (sample, block of HB rows); CTAs loop over units.
+// ---------------------------------------------------------------------------
+template <int C, int MH, int MW>
+struct FCfg {
+    static constexpr int kTile = 128 * C;                   // one grid row of codes
+    static constexpr int kStages = 4;                       // row-pair ring
+    static constexpr int kStageBytes = 2 * kTile;
+    static constexpr int kN = 32;                           // basis rows per digit (padded)
+    static constexpr int kLimbBytes = kN * 128;             // [32][128] int8, SW128
+    static constexpr int kOffA = 0;
+    static constexpr int kOffB = kOffA + kStages * kStageBytes;
+    static constexpr int kOffF = kOffB + 4 * kLimbBytes;    // 2 x [2][MW][C] float2
+    static constexpr int kFBytes = 2 * 2 * MW * C * 8;
+    static constexpr int kOffE = kOffF + kFBytes;           // twf_h [H][MH] float2 (H <= 512)
+    static constexpr int kEBytes = 512 * MH * 8;
+    static constexpr int kOffBars = kOffE + kEBytes;
+    static constexpr int kSmemBytes = kOffBars + 8 * (2 * kStages + 4 + 1) + 16 + 1024;
+    static constexpr int kTmemCols = 256;                   // 2 stages x 4 digits x 32
+    static_assert(kSmemBytes <= 227 * 1024, "smem");
+    static_assert(2 * MW <= 24, "basis rows");
+};
+
+// MN-major descriptor: SW64 atoms of 64 bytes along M, `lbo` between M atoms,
+// `sbo` between groups of 8 K rows.
+__device__ __forceinline__ uint64_t umma_desc_mn64(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) |
+           (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) |
+           (static_cast<uint64_t>(4u) << 61);
+}
+
+template <int C, int MH, int MW>
+__global__ void __launch_bounds__(kThreads, 1)
+spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArgs p) {
+    using F = FCfg<C, MH, MW>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sA = smem + F::kOffA;
+    uint8_t* sB = smem + F::kOffB;
+    float2* sF = reinterpret_cast<float2*>(smem + F::kOffF);
+    float2* sE = reinterpret_cast<float2*>(smem + F::kOffE);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + F::kOffBars);
+    uint64_t* empty = full + F::kStages;
+    uint64_t* accFull = empty + F::kStages;
+    uint64_t* accEmpty = accFull + 2;
+    uint64_t* epiBar = accEmpty + 2;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(epiBar + 1);
+    volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int pairs_per_unit = p.HB / 2;
+    const int nHB = p.H / p.HB;
+    const int num_units = p.B * nHB;
+
+    {
+        // digit matrices -> shared memory (K-major, 128-byte swizzle)
+        for (int idx = threadIdx.x; idx < 4 * F::kN * 8; idx += kThreads) {
+            const int l = idx / (F::kN * 8), rem = idx % (F::kN * 8);
+            const int n = rem / 8, ch = rem % 8;
+            const uint4 v = *reinterpret_cast<const uint4*>(p.limbs + (l * F::kN + n) * 128 + ch * 16);
+            *reinterpret_cast<uint4*>(sB + l * F::kLimbBytes + swz_offset(n * 128 + ch * 16, 128)) = v;
+        }
+        for (int i = threadIdx.x; i < p.H * MH; i += kThreads) sE[i] = p.twf_h[i];
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < F::kStages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            for (int s = 0; s < 2; ++s) {
+                mbar_init(&accFull[s], 1);
+                mbar_init(&accEmpty[s], 8);
+            }
+            mbar_init(epiBar, 256);
+            *sAbort = 0;
+            fence_mbar_init();
+        }
+        if (warp == 1) tmem_alloc(sTmem, F::kTmemCols);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    const uint32_t tmem_base = *sTmem;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            prefetch_tmap(&tmCodes);
+            int it = 0;
+            for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+                const int b = u / nHB, hb = u % nHB;
+                for (int k = 0; k < pairs_per_unit; ++k, ++it) {
+                    const int s = it % F::kStages;
+                    const uint32_t ph = (it / F::kStages) & 1;
+                    if (!mbar_wait(&empty[s], ph ^ 1, sAbort)) {
+                        *sAbort = 1;
+                        atomicOr(p.err, kErrWaitSlotFree);
+                        goto producer_done;
+                    }
+                    mbar_arrive_expect_tx(&full[s], F::kStageBytes);
+                    const int row = b * p.H + hb * p.HB + 2 * k;   // tile index of grid row h
+                    tma_load_2d(sA + s * F::kStageBytes, &tmCodes, &full[s], 0, row * 128);
+                    tma_load_2d(sA + s * F::kStageBytes + F::kTile, &tmCodes, &full[s], 0, (row + 1) * 128);
+                }
+            }
+        producer_done:
+            for (int j = (it > F::kStages ? it - F::kStages : 0); j < it; ++j)
+                if (!mbar_wait(&full[j % F::kStages], (j / F::kStages) & 1, sAbort)) break;
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (elect_one()) {
+            // kind::i8, signed, int32 D, A MN-major, B K-major, M = 128, N = 32
+            constexpr uint32_t idesc = idesc_i8(F::kN) | (1u << 15);
+            int it = 0;
+            const int total = ((num_units - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                               static_cast<int>(gridDim.x)) * pairs_per_unit;
+            for (; it < total; ++it) {
+                const int s = it % F::kStages;
+                const uint32_t ph = (it / F::kStages) & 1;
+                const int a = it & 1;
+                const uint32_t aph = (it >> 1) & 1;
+                if (!mbar_wait(&accEmpty[a], aph ^ 1, sAbort)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitAccFree);
+                    break;
+                }
+                if (!mbar_wait(&full[s], ph, sAbort)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitTmaFull);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t aBase = smem_u32(sA + s * F::kStageBytes);
+#pragma unroll
+                for (int l = 0; l < 4; ++l) {
+                    const uint32_t d = tmem_base + a * 128 + l * 32;
+                    const uint32_t bBase = smem_u32(sB + l * F::kLimbBytes);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_i8(d, umma_desc_mn64(aBase + kk * 2048, F::kTile, 512),
+                               umma_desc(bBase + kk * 32, 128), idesc, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&empty[s]);
+                mma_commit(&accFull[a]);
+            }
+            if (it > 0) mbar_wait(&accFull[(it - 1) & 1], ((it - 1) >> 1) & 1, sAbort);
+        }
+        __syncwarp();
+    } else if (warp >= 4) {
+        const int ew = warp - 4;            // 0..7
+        const int etid = ew * 32 + lane;    // 0..255
+        const int quad = warp & 3;
+        const int half = ew >> 2;           // basis columns [16 half, 16 half + 12)
+        const int m = quad * 32 + lane;     // TMEM lane = (r, c)
+        const int r = m / C, c = m % C;
+        constexpr int kPairs = C * MW;
+        constexpr int kPer = (kPairs + 255) / 256;
+        const double scale = static_cast<double>(p.s) * 7.450580596923828125e-9;  // s / 2^27
+        uint32_t nsync = 0;
+        bool ok = true;
+        int it = 0;
+        for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+            const int b = u / nHB, hb = u % nHB;
+            float2 acc[kPer][MH];
+#pragma unroll
+            for (int i = 0; i < kPer; ++i)
+#pragma unroll
+                for (int kh = 0; kh < MH; ++kh) acc[i][kh] = make_float2(0.f, 0.f);
+            for (int k = 0; k < pairs_per_unit; ++k, ++it) {
+                const int a = it & 1;
+                if (!mbar_wait(&accFull[a], (it >> 1) & 1, sAbort)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t tb = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * 128 + 16 * half;
+                uint32_t d[4][16];
+#pragma unroll
+                for (int l = 0; l < 4; ++l) {
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                        : "=r"(d[l][0]), "=r"(d[l][1]), "=r"(d[l][2]), "=r"(d[l][3]), "=r"(d[l][4]),
+                          "=r"(d[l][5]), "=r"(d[l][6]), "=r"(d[l][7]), "=r"(d[l][8]), "=r"(d[l][9]),
+                          "=r"(d[l][10]), "=r"(d[l][11]), "=r"(d[l][12]), "=r"(d[l][13]),
+                          "=r"(d[l][14]), "=r"(d[l][15])
+                        : "r"(tb + l * 32));
+                }
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&accEmpty[a]);
+                float2* f = sF + (it & 1) * (2 * MW * C);
+#pragma unroll
+                for (int t = 0; t < 12; ++t) {
+                    const int j = 12 * half + t;
+                    const long long v = ((static_cast<long long>(static_cast<int>(d[0][t])) * 256 +
+                                          static_cast<int>(d[1][t])) * 256 +
+                                         static_cast<int>(d[2][t])) * 256 +
+                                        static_cast<int>(d[3][t]) -
+                                        static_cast<long long>(p.zp) * p.sum_b[j];
+                    const float fv = static_cast<float>(static_cast<double>(v) * scale);
+                    float* dst = reinterpret_cast<float*>(f + (r * MW + (j >> 1)) * C + c);
+                    dst[j & 1] = fv;
+                }
+                // everyone's row DFT of this row pair is in sF before the H accumulation
+                mbar_arrive(epiBar);
+                if (!mbar_wait(epiBar, nsync & 1u, sAbort)) {
+                    ok = false;
+                    break;
+                }
+                ++nsync;
+                const int h0 = hb * p.HB + 2 * k;
+#pragma unroll
+                for (int i = 0; i < kPer; ++i) {
+                    const int q = etid + 256 * i;
+                    if (q < kPairs) {
+                        const int kw = q / C, cc = q % C;
+#pragma unroll
+                        for (int rr = 0; rr < 2; ++rr) {
+                            const float2 fv = f[(rr * MW + kw) * C + cc];
+                            const float2* e = sE + (h0 + rr) * MH;
+#pragma unroll
+                            for (int kh = 0; kh < MH; ++kh) {
+                                const float2 ev = e[kh];
+                                acc[i][kh].x = fmaf(fv.x, ev.x, fmaf(-fv.y, ev.y, acc[i][kh].x));
+                                acc[i][kh].y = fmaf(fv.x, ev.y, fmaf(fv.y, ev.x, acc[i][kh].y));
+                            }
+                        }
+                    }
+                }
+            }
+            if (!ok) break;
+            float2* dst = p.xpart + (static_cast<int64_t>(b) * nHB + hb) * (MH * MW * C);
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) {
+                const int q = etid + 256 * i;
+                if (q < kPairs) {
+                    const int kw = q / C, cc = q % C;
+#pragma unroll
+                    for (int kh = 0; kh < MH; ++kh) dst[(kh * MW + kw) * C + cc] = acc[i][kh];
+                }
+            }
+        }
+        if (!ok) {
+            *sAbort = 1;
+            atomicOr(p.err, kErrWaitAccFull);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, F::kTmemCols);
+    }
+}
+
 template <typename Kern>
 cudaError_t set_smem(Kern k, int bytes) {
     return set_max_dynamic_smem(reinterpret_cast<const void*>(k), bytes);
@@ -840,7 +1114,21 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
     for (int i = 0; i < pl.L; ++i) {
         const int nHB = pl.H / pl.HB;
         const int sm_fwd = (pl.W * C + MW * pl.W * 2) * 4;
-        {
+        if (pl.W == 128 && pl.fwd_limbs && pl.H <= 512 && (pl.HB % 2) == 0) {
+            using FC = FCfg<C, MH, MW>;
+            auto k = spec_fwd_tc_kernel<C, MH, MW>;
+            if ((e = set_smem(k, FC::kSmemBytes)) != cudaSuccess) return e;
+            CUtensorMap tc;
+            if (!encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur], C, M, C, C, 128, C))
+                return cudaErrorInvalidValue;
+            SpecFwdArgs fa{pl.fwd_limbs, pl.fwd_sum_b, pl.twf_h, pl.xpart, pl.layer[i].s_in,
+                           pl.layer[i].zp_in, pl.B, pl.H, pl.HB, pl.err};
+            const int units = pl.B * nHB;
+            if (pl.timer) pl.timer->begin("fno2d_spec_fwd", st);
+            k<<<units < sms ? units : sms, kThreads, FC::kSmemBytes, st>>>(tc, fa);
+            if (pl.timer) pl.timer->end(st);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        } else {
             auto k = spec_fwd_kernel<C, MH, MW>;
             if ((e = set_smem(k, sm_fwd)) != cudaSuccess) return e;
             if (pl.timer) pl.timer->begin("fno2d_spec_fwd", st);

@@ -52,6 +52,18 @@ struct LayerArgs {
     unsigned* err;
 };
 
+// Arguments of the tensor-core forward transform (spec_fwd_tc_kernel, W == 128).
+struct SpecFwdArgs {
+    const int8_t* limbs;      // [4][32][128] int8: base-256 digits of the scaled DFT basis
+    const long long* sum_b;   // [2*MW] sum over w of the scaled basis (for the zero point)
+    const float2* twf_h;      // (H, MH)
+    float2* xpart;            // (B, H/HB, MH*MW, C)
+    float s;                  // layer-input scale and zero point
+    int zp;
+    int B, H, HB;
+    unsigned* err;
+};
+
 struct Fno2dLayerPlan {
     float s_in;
     int zp_in;
@@ -75,6 +87,8 @@ struct Fno2dPlan {
     float2* xpart;         // (B, H/HB, MH*MW, C)
     float2* Y;             // (B, MH*MW, C)
     const float2* twf_w;   // (MW, W)  e^{-2 pi i kw w / W}
+    const int8_t* fwd_limbs;    // tensor-core forward basis (W == 128), see SpecFwdArgs
+    const long long* fwd_sum_b;
     const float2* twf_h;   // (H, MH)  e^{-2 pi i kh h / H}
     const float2* twi_w;
     const float2* twi_h;

@@ -108,6 +108,8 @@ struct nfx_runtime {
     size_t dx_cap = 0, dy_cap = 0;
     float2* tw[4] = {nullptr, nullptr, nullptr, nullptr};  // twf_w, twf_h, twi_w, twi_h
     int tw_H = 0, tw_W = 0;
+    int8_t* fwd_limbs = nullptr;      // tensor-core forward basis digits (W == 128)
+    long long* fwd_sum_b = nullptr;
     std::unique_ptr<nfx::EventTimer> timer;  // per-kernel timing when enabled
 };
 
@@ -313,6 +315,44 @@ int ensure_twiddles(nfx_runtime* rt, int H, int W) {
                      "cudaMemcpy"))
             return NFX_INTERNAL;
     }
+    // integer DFT basis for the tensor-core forward transform (W == 128): the basis
+    // scaled by 2^27 and rounded, split into four balanced base-256 digits
+    if (rt->fwd_limbs) cudaFree(rt->fwd_limbs);
+    if (rt->fwd_sum_b) cudaFree(rt->fwd_sum_b);
+    rt->fwd_limbs = nullptr;
+    rt->fwd_sum_b = nullptr;
+    if (W == 128 && 2 * MW <= 24) {
+        std::vector<int8_t> limbs(4 * 32 * 128, 0);
+        std::vector<long long> sum_b(2 * MW, 0);
+        for (int j = 0; j < 2 * MW; ++j) {
+            const int kw = j / 2, n = j < 12 ? j : j + 4;
+            for (int w = 0; w < W; ++w) {
+                const double a = two_pi * static_cast<double>((static_cast<int64_t>(kw) * w) % W) / W;
+                const double v = (j & 1) ? -std::sin(a) : std::cos(a);
+                long long r = std::llround(v * 134217728.0);
+                sum_b[j] += r;
+                int dig[4];
+                for (int l = 3; l >= 1; --l) {
+                    const long long d = ((r + 128) & 255) - 128;
+                    dig[l] = static_cast<int>(d);
+                    r = (r - d) / 256;
+                }
+                dig[0] = static_cast<int>(r);
+                for (int l = 0; l < 4; ++l) limbs[(l * 32 + n) * 128 + w] = static_cast<int8_t>(dig[l]);
+            }
+        }
+        void* p1 = nullptr;
+        void* p2 = nullptr;
+        if (!cuda_ok(rt, cudaMalloc(&p1, limbs.size()), "cudaMalloc") ||
+            !cuda_ok(rt, cudaMalloc(&p2, sum_b.size() * sizeof(long long)), "cudaMalloc"))
+            return NFX_INTERNAL;
+        rt->fwd_limbs = static_cast<int8_t*>(p1);
+        rt->fwd_sum_b = static_cast<long long*>(p2);
+        if (!cuda_ok(rt, cudaMemcpy(p1, limbs.data(), limbs.size(), cudaMemcpyHostToDevice), "cudaMemcpy") ||
+            !cuda_ok(rt, cudaMemcpy(p2, sum_b.data(), sum_b.size() * sizeof(long long),
+                                    cudaMemcpyHostToDevice), "cudaMemcpy"))
+            return NFX_INTERNAL;
+    }
     rt->tw_H = H;
     rt->tw_W = W;
     return NFX_OK;
@@ -386,6 +426,8 @@ int fno2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
     pl.twf_h = rt->tw[1];
     pl.twi_w = rt->tw[2];
     pl.twi_h = rt->tw[3];
+    pl.fwd_limbs = rt->fwd_limbs;
+    pl.fwd_sum_b = rt->fwd_sum_b;
     pl.err = nfx::device_error_word();
     if (!pl.err) return rt_fail(rt, NFX_INTERNAL, "no device error word");
     pl.timer = rt->timer.get();
@@ -454,6 +496,8 @@ int fno2d_noalloc_plan(nfx_runtime* rt, const float* x, const int64_t* x_shape, 
     plan->HB = H / (H < 8 ? H : 8);
     plan->x = x;
     plan->y = y;
+    plan->fwd_limbs = nullptr;
+    plan->fwd_sum_b = nullptr;
     plan->timer = nullptr;
     return NFX_OK;
 }
@@ -519,6 +563,8 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
         if (p) cudaFree(p);
     for (auto* p : rt->tw)
         if (p) cudaFree(p);
+    if (rt->fwd_limbs) cudaFree(rt->fwd_limbs);
+    if (rt->fwd_sum_b) cudaFree(rt->fwd_sum_b);
     if (rt->dx) cudaFree(rt->dx);
     if (rt->dy) cudaFree(rt->dy);
     if (rt->stream) cudaStreamDestroy(rt->stream);
@@ -615,7 +661,9 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
     if (nx == 0) return NFX_OK;
     if (!x || !y) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
     if (nx > rt->dx_cap) {
-        if (rt->dx) cudaFree(rt->dx);
+        if (rt->fwd_limbs) cudaFree(rt->fwd_limbs);
+    if (rt->fwd_sum_b) cudaFree(rt->fwd_sum_b);
+    if (rt->dx) cudaFree(rt->dx);
         rt->dx = nullptr;
         if (!cuda_ok(rt, cudaMalloc(&rt->dx, nx * 4), "cudaMalloc input")) return NFX_INTERNAL;
         rt->dx_cap = nx;
