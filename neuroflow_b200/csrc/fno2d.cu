@@ -237,7 +237,9 @@ constexpr int kLutMaxCells = 3072;
 
 template <int C, int MH, int MW, bool PROJ, bool TCX>
 struct LCfg {
-    static constexpr int kEpiWarps = PROJ ? 4 : 8;
+    // 16 epilogue warps: 4 per TMEM lane quadrant, each owning C/4 columns
+    static constexpr int kEpiWarps = 16;
+    static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
     static constexpr int kABytes = 128 * C;
     static constexpr int kStages = 3;
     static constexpr int kOnesCol = C;
@@ -245,8 +247,9 @@ struct LCfg {
     static constexpr int kAccCols = TCX ? kX1Col + C : kX1Col;
     static constexpr int kAccStages = 2;
     static constexpr int kTmemCols = pow2ceil(kAccStages * kAccCols);
-    static constexpr int kCols = PROJ ? C : C / 2;        // columns per epilogue warp
-    static constexpr int kCh = kCols < 32 ? kCols : 32;   // columns per TMEM load
+    static constexpr int kCols = C / 4;                   // columns per epilogue warp
+    static constexpr int kCh = kCols;                     // columns per TMEM load
+    static_assert(kCols == 16, "the epilogue is laid out for width 64");
     static constexpr int kRmax = 4;                       // rows per tile (W >= 32)
     static constexpr int kKx = 32;                        // padded K of the x1 MMA (fp32)
     static_assert(!TCX || 2 * MW <= kKx, "x1 MMA K");
@@ -255,8 +258,9 @@ struct LCfg {
     static constexpr int kOffOnes = up1k(C * C);
     static constexpr int kOffA = kOffOnes + 1024;
     static constexpr int kOffStage = kOffA + kStages * kABytes;
-    static constexpr int kOffY = kOffStage + (PROJ ? 0 : 8 * 2 * 1024);
-    static constexpr int kYBytes = PROJ ? 0 : MH * MW * C * 8;
+    static constexpr int kOffY = kOffStage + (PROJ ? 0 : kEpiWarps * 2 * 512);
+    // layer: cached spectrum Y of the current sample; projection: 2 x [128][C+1] activations
+    static constexpr int kYBytes = PROJ ? 2 * 128 * (C + 1) * 4 : MH * MW * C * 8;
     static constexpr int kOffBinv = up1k(kOffY + kYBytes);
     static constexpr int kBinvBytes = TCX ? 2 * 128 * kKx * 4 : 0;        // hi, lo
     static constexpr int kOffTop = kOffBinv + kBinvBytes;
@@ -274,6 +278,16 @@ struct LCfg {
     static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
     static_assert(kSmemBytes <= 227 * 1024, "smem");
 };
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
 
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     hi = __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
@@ -293,7 +307,7 @@ __device__ __forceinline__ int code_from_lut(float z, const int2* lut, int ncell
 }
 
 template <int C, int MH, int MW, bool PROJ, bool TCX>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(LCfg<C, MH, MW, PROJ, TCX>::kThreads, 1)
 layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmOut,
              const LayerArgs p) {
     using L = LCfg<C, MH, MW, PROJ, TCX>;
@@ -311,6 +325,7 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
     float2* sTw = reinterpret_cast<float2*>(smem + L::kOffTw);
     int2* sLut = reinterpret_cast<int2*>(smem + L::kOffLut);
     float* sAct = reinterpret_cast<float*>(smem + L::kOffLut);
+    float* sG = reinterpret_cast<float*>(smem + L::kOffY);       // PROJ: [2][128][C+1]
     float4* sCol = reinterpret_cast<float4*>(smem + L::kOffCol);  // {sW*s_in, zp_w, zp_in*sum_w, bias}
     float* sWout = reinterpret_cast<float*>(sCol + C);            // [out_ch][C] (PROJ)
     float* sBout = sWout + 4 * C;
@@ -334,29 +349,29 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
     // ---- set-up
     {
         constexpr int kChunks = C / 16;
-        for (int idx = threadIdx.x; idx < C * kChunks; idx += kThreads) {
+        for (int idx = threadIdx.x; idx < C * kChunks; idx += L::kThreads) {
             const int o = idx / kChunks, c = idx % kChunks;
             const uint4 v = *reinterpret_cast<const uint4*>(p.Wq + o * C + c * 16);
             *reinterpret_cast<uint4*>(sW + swz_offset(o * C + c * 16, C)) = v;
         }
-        for (int idx = threadIdx.x; idx < 1024 / 16; idx += kThreads) {
+        for (int idx = threadIdx.x; idx < 1024 / 16; idx += L::kThreads) {
             const uint32_t one = (idx * 16 < C) ? 0x01010101u : 0u;  // row 0 = ones
             *reinterpret_cast<uint4*>(sOnes + idx * 16) = make_uint4(one, one, one, one);
         }
-        for (int o = threadIdx.x; o < C; o += kThreads)
+        for (int o = threadIdx.x; o < C; o += L::kThreads)
             sCol[o] = make_float4(__fmul_rn(p.scale_w[o], p.s_in), __int_as_float(p.zp_w[o]),
                                   __int_as_float(p.zp_in * p.sum_w[o]), p.bias[o]);
         if (PROJ) {
-            for (int i = threadIdx.x; i < p.out_ch * C; i += kThreads) sWout[i] = p.w_out[i];
-            for (int i = threadIdx.x; i < p.out_ch; i += kThreads) sBout[i] = p.b_out[i];
+            for (int i = threadIdx.x; i < p.out_ch * C; i += L::kThreads) sWout[i] = p.w_out[i];
+            for (int i = threadIdx.x; i < p.out_ch; i += L::kThreads) sBout[i] = p.b_out[i];
             if (use_act)
-                for (int i = threadIdx.x; i < 256; i += kThreads) sAct[i] = p.act_table[i];
+                for (int i = threadIdx.x; i < 256; i += L::kThreads) sAct[i] = p.act_table[i];
         } else {
             if (use_lut)
-                for (int i = threadIdx.x; i < p.lut_cells; i += kThreads) sLut[i] = p.code_lut[i];
+                for (int i = threadIdx.x; i < p.lut_cells; i += L::kThreads) sLut[i] = p.code_lut[i];
             if constexpr (TCX) {
                 // Binv (A operand, 128 points x 32, SW128 K-major), hi and lo
-                for (int idx = threadIdx.x; idx < 128 * L::kKx; idx += kThreads) {
+                for (int idx = threadIdx.x; idx < 128 * L::kKx; idx += L::kThreads) {
                     const int w = idx / L::kKx, j = idx % L::kKx;
                     float v = 0.0f;
                     if (j < 2 * MW) {
@@ -370,10 +385,10 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                     *reinterpret_cast<float*>(sBinv + 128 * 128 + off) = lo;
                 }
                 // T operand buffers: zero (the K padding columns stay zero)
-                for (int idx = threadIdx.x; idx < L::kTopBytes / 16; idx += kThreads)
+                for (int idx = threadIdx.x; idx < L::kTopBytes / 16; idx += L::kThreads)
                     reinterpret_cast<uint4*>(sTop)[idx] = make_uint4(0, 0, 0, 0);
             } else {
-                for (int i = threadIdx.x; i < MW * p.W; i += kThreads) sTw[i] = p.twi_w[i];
+                for (int i = threadIdx.x; i < MW * p.W; i += L::kThreads) sTw[i] = p.twi_w[i];
             }
         }
         if (threadIdx.x == 0) {
@@ -487,7 +502,7 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
         const int etid = ew * 32 + lane;
         constexpr int kEpiThreads = L::kEpiWarps * 32;
         const int quad = warp & 3;
-        const int col0 = PROJ ? 0 : (ew >> 2) * L::kCols;
+        const int col0 = (ew >> 2) * L::kCols;  // this warp's 16 columns
         const int row = quad * 32 + lane;  // row of the 128-point tile
         const int P = p.H * p.W;
         const int R = 128 / p.W > 0 ? 128 / p.W : 1;
@@ -621,19 +636,8 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
             for (int c0 = col0; c0 < col0 + L::kCols; c0 += L::kCh) {
                 uint32_t raw[32];
                 uint32_t x1r[32];
-                if constexpr (L::kCh == 32) {
-                    tmem_ld32(tbase + c0, raw);
-                    if constexpr (TCX && !PROJ) tmem_ld32(tbase + L::kX1Col + c0, x1r);
-                } else {
-                    asm volatile(
-                        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-                        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-                        : "=r"(raw[0]), "=r"(raw[1]), "=r"(raw[2]), "=r"(raw[3]), "=r"(raw[4]),
-                          "=r"(raw[5]), "=r"(raw[6]), "=r"(raw[7]), "=r"(raw[8]), "=r"(raw[9]),
-                          "=r"(raw[10]), "=r"(raw[11]), "=r"(raw[12]), "=r"(raw[13]),
-                          "=r"(raw[14]), "=r"(raw[15])
-                        : "r"(tbase + c0));
-                }
+                tmem_ld16(tbase + c0, raw);
+                if constexpr (TCX && !PROJ) tmem_ld16(tbase + L::kX1Col + c0, x1r);
                 tmem_wait_ld();
                 const bool last_chunk = c0 + L::kCh >= col0 + L::kCols;
                 // The fast, branch-free pass over the chunk; elements whose fake-quant
@@ -680,13 +684,9 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&accEmpty[a]);
                     }
+                    float* grow = sG + (it & 1) * (128 * (C + 1)) + row * (C + 1) + c0;
 #pragma unroll
-                    for (int j = 0; j < L::kCh; ++j) {
-#pragma unroll
-                        for (int jj = 0; jj < 4; ++jj)
-                            if (jj < p.out_ch)
-                                acc_out[jj] = __fmaf_rn(g[j], sWout[jj * C + c0 + j], acc_out[jj]);
-                    }
+                    for (int j = 0; j < L::kCh; ++j) grow[j] = g[j];
                 } else {
                     // x1 of element j (tensor-core result, or CUDA-core inverse W-DFT)
                     auto x1_of = [&](int j, uint32_t xbits) -> float {
@@ -724,7 +724,7 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                         if ((j & 3) == 0) packed[j >> 2] = byte;
                         else packed[j >> 2] |= byte << (8 * (j & 3));
                     }
-                    uint8_t* buf = sStage + (ew * 2 + (nstore & 1)) * 1024;
+                    uint8_t* buf = sStage + (ew * 2 + (nstore & 1)) * 512;
                     if (nstore >= 2) {
                         if (lane == 0) tma_store_wait_read<1>();
                         __syncwarp();
@@ -774,6 +774,20 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                 }
             }
             if constexpr (PROJ) {
+                // the 64 activations of every row are in shared memory; the first warp of
+                // each lane quadrant runs the reference's sequential proj_out fma chain
+                if (!epi_sync()) {
+                    epi_ok = false;
+                    break;
+                }
+                if (ew >= 4) continue;
+                const float* grow = sG + (it & 1) * (128 * (C + 1)) + row * (C + 1);
+#pragma unroll
+                for (int o = 0; o < C; ++o) {
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj)
+                        if (jj < p.out_ch) acc_out[jj] = __fmaf_rn(grow[o], sWout[jj * C + o], acc_out[jj]);
+                }
                 const int64_t m = g0 + row;
                 if (m < p.M) {
 #pragma unroll
@@ -1157,20 +1171,20 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
             a.err = pl.err;
             CUtensorMap tin, tout;
             if (!encode_2d(&tin, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur], C, M, C, C, 128, C) ||
-                !encode_2d(&tout, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur ^ 1], C, M, C, C / 2,
-                           32, C / 2 == 32 ? 32 : 0))
+                !encode_2d(&tout, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur ^ 1], C, M, C, C / 4,
+                           32, 0))
                 return cudaErrorInvalidValue;
             if (pl.timer) pl.timer->begin("fno2d_layer", st);
             if (pl.W == 128) {
                 using LC = LCfg<C, MH, MW, false, true>;
                 auto k = layer_kernel<C, MH, MW, false, true>;
                 if ((e = set_smem(k, LC::kSmemBytes)) != cudaSuccess) return e;
-                k<<<grid_l, kThreads, LC::kSmemBytes, st>>>(tin, tout, a);
+                k<<<grid_l, LC::kThreads, LC::kSmemBytes, st>>>(tin, tout, a);
             } else {
                 using LC = LCfg<C, MH, MW, false, false>;
                 auto k = layer_kernel<C, MH, MW, false, false>;
                 if ((e = set_smem(k, LC::kSmemBytes)) != cudaSuccess) return e;
-                k<<<grid_l, kThreads, LC::kSmemBytes, st>>>(tin, tout, a);
+                k<<<grid_l, LC::kThreads, LC::kSmemBytes, st>>>(tin, tout, a);
             }
             if (pl.timer) pl.timer->end(st);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -1191,7 +1205,7 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
         a.err = pl.err;
         a.y = pl.y;
         if (pl.timer) pl.timer->begin("fno2d_proj", st);
-        k<<<grid_l, kThreads, LC::kSmemBytes, st>>>(tin, tin, a);
+        k<<<grid_l, LC::kThreads, LC::kSmemBytes, st>>>(tin, tin, a);
         if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
