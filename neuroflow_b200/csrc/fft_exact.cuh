@@ -1,0 +1,54 @@
+// fft_exact.cuh -- the reference radix-2 FFT (fft.cpp:36-99) on the GPU with the
+// reference build's rounding, so that spectra and inverse transforms are bit-identical
+// to the CPU runtime's.
+//
+// The reference FFT is iterative Cooley-Tukey on a bit-reversed copy.  What fixes its
+// rounding is (a) the order of stages and butterflies, which is a tree and therefore
+// independent of how the butterflies of one stage are scheduled, (b) the twiddle of
+// butterfly k at stage len, which is the k-th value of the recurrence w *= wlen
+// (host-built table, nfx_lut.h), and (c) the expression shape of each complex product
+// in the reference's GCC -O3 -mfma build:
+//   forward butterfly  v = a*w:  re = ar*wr - ai*wi,         im = ai*wr + ar*wi
+//   inverse butterfly  v = a*w:  re = fma(ar, wr, -(ai*wi)), im = fma(ar, wi, ai*wr)
+// All arithmetic below uses the _rn intrinsics, which nvcc never contracts.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace nfx {
+
+__device__ __forceinline__ int bit_reverse(int i, int log2n) {
+    return log2n == 0 ? 0 : static_cast<int>(__brev(static_cast<unsigned>(i)) >> (32 - log2n));
+}
+
+// In-place transform of one row of n complex values in shared memory, already in
+// bit-reversed order, by one warp.  `tw` is the stage-concatenated twiddle table
+// (n - 1 entries).  INV selects the inverse butterflies (the caller applies the 1/n).
+template <bool INV>
+__device__ __forceinline__ void warp_fft_row(float2* a, int n, const float2* __restrict__ tw,
+                                             int lane) {
+    for (int half = 1; half < n; half <<= 1) {
+        const float2* t = tw + (half - 1);
+        for (int b = lane; b < n / 2; b += 32) {
+            const int k = b & (half - 1);
+            const int i0 = (b - k) * 2 + k;
+            const int i1 = i0 + half;
+            const float2 w = __ldg(t + k);
+            const float2 u = a[i0];
+            const float2 x = a[i1];
+            float2 v;
+            if (INV) {
+                v.x = __fmaf_rn(x.x, w.x, -__fmul_rn(x.y, w.y));
+                v.y = __fmaf_rn(x.x, w.y, __fmul_rn(x.y, w.x));
+            } else {
+                v.x = __fsub_rn(__fmul_rn(x.x, w.x), __fmul_rn(x.y, w.y));
+                v.y = __fadd_rn(__fmul_rn(x.y, w.x), __fmul_rn(x.x, w.y));
+            }
+            a[i0] = make_float2(__fadd_rn(u.x, v.x), __fadd_rn(u.y, v.y));
+            a[i1] = make_float2(__fsub_rn(u.x, v.x), __fsub_rn(u.y, v.y));
+        }
+        __syncwarp();
+    }
+}
+
+}  // namespace nfx

@@ -1,0 +1,383 @@
+// fno1d.cu -- FNO1d executor (sm_100a): the reference FNO1d::Forward
+// (cpp/src/fno.cpp:408-706) with the reference's rounding.
+//
+// Activations between layers stay channel-last (b, p, c) in HBM, as int8 codes when the
+// next layer snaps its input with per-tensor qparams (the snap is then exact and free:
+// the previous layer's epilogue emits the code through the host-built z -> code table)
+// and as fp32 otherwise.  One layer is
+//
+//   fft1d_fwd   per (b, c) row: the reference radix-2 rFFT (fft.cpp:73-84) of the
+//               layer input, bit-identical, truncated to `modes` bins -> Xs (b, c, m)
+//   [gemm_i8]   INT8 path only: tcgen05 LinearForwardBatched of the input codes
+//               (fno.cpp:125-159) -> x2raw (b*N, C)
+//   layer1d     per (b, group of G output channels): the spectral contraction
+//               (fno.cpp:181-196), the inverse transform (fft.cpp:86-99) of each
+//               output row, the local Linear (FP32 dot product, or x2raw + bias), the
+//               output fake-quant, x1 + x2 and the activation -> next activation
+//
+// lift1d (fno.cpp:438-466) and proj1d (fno.cpp:683-702) close the network.  The only
+// operation that is not bit-identical to the reference is tanhf inside GELU where its
+// result is consumed as fp32 (CUDA's tanhf vs glibc's differ by at most a few ulps);
+// wherever GELU feeds a per-tensor snap the exact table is used instead.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "fft_exact.cuh"
+#include "fno1d.h"
+#include "nfx_internal.h"
+#include "numerics.cuh"
+
+namespace nfx {
+namespace {
+
+__device__ __forceinline__ float act_f(float z, int act) {
+    return act == 1 ? relu_ref(z) : gelu_tanh(z);
+}
+
+// fno.cpp:585-603 FP8 branch: log2 snap of v / scale (the std::ldexp exponent is the
+// float truncated to int, as the reference computes it).
+__device__ __forceinline__ float fp8_log2_snap(float v, float scale) {
+    if (!(scale > 0.0f)) return v;
+    const float u = __fdiv_rn(v, scale);
+    const float a = fabsf(u);
+    const float sign = u < 0.0f ? -1.0f : 1.0f;
+    const float qv = (a < 0.015625f)
+                         ? a
+                         : ldexpf(1.0f, static_cast<int>(__fdiv_rn(
+                                            roundf(__fmul_rn(log2f(a), 8.0f)), 8.0f)));
+    return __fmul_rn(__fmul_rn(sign, fminf(qv, 448.0f)), scale);
+}
+
+// value of activation element idx: a code snapped back, (q - zp) * s, or the fp32 value
+__device__ __forceinline__ float act_value(const void* h, int64_t idx, int codes, float s,
+                                           float zpf) {
+    if (codes)
+        return __fmul_rn(__fsub_rn(static_cast<float>(static_cast<const int8_t*>(h)[idx]), zpf), s);
+    return static_cast<const float*>(h)[idx];
+}
+
+// ---------------------------------------------------------------------------
+// lift: h[b, p, c] = Linear from lift_b[c] over x[b, p, :] (fno.cpp:51-80); zero in
+// the padded tail (fno.cpp:450-466); then the layer-0 snap as a code, when it exists.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) lift1d_kernel(const float* __restrict__ x, int n, int N,
+                                                     int C, int in_ch, int64_t total,
+                                                     const float* __restrict__ w,
+                                                     const float* __restrict__ bias, int codes,
+                                                     float s, int zp, void* out) {
+    const float zpf = static_cast<float>(zp);
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(t % C);
+        const int64_t bp = t / C;
+        const int p = static_cast<int>(bp % N);
+        const int64_t b = bp / N;
+        float acc = 0.0f;
+        if (p < n) {
+            acc = __ldg(bias + c);
+            const float* xr = x + (b * n + p) * in_ch;
+            const int nu = linear_unfused_len(in_ch);
+            for (int k = 0; k < in_ch; ++k)
+                acc = linear_step(acc, __ldg(xr + k), __ldg(w + c * in_ch + k), k >= nu);
+        }
+        if (codes)
+            static_cast<int8_t*>(out)[t] = static_cast<int8_t>(static_cast<int>(fq_code(acc, s, zpf)));
+        else
+            static_cast<float*>(out)[t] = acc;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// forward transform: grid (C / R, B), R warps, one row (b, c) per warp.
+// Dynamic shared memory R * N float2.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) fft1d_fwd_kernel(const void* __restrict__ h, int codes,
+                                                        float s, int zp, int N, int log2N, int C,
+                                                        int modes,
+                                                        const float2* __restrict__ tw,
+                                                        float2* __restrict__ Xs) {
+    extern __shared__ float2 sa[];
+    const int R = blockDim.x >> 5;
+    const int b = blockIdx.y, c0 = blockIdx.x * R;
+    const float zpf = static_cast<float>(zp);
+    for (int t = threadIdx.x; t < N * R; t += blockDim.x) {
+        const int p = t / R, r = t - (t / R) * R;
+        const float v = act_value(h, (static_cast<int64_t>(b) * N + p) * C + c0 + r, codes, s, zpf);
+        sa[r * N + bit_reverse(p, log2N)] = make_float2(v, 0.0f);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float2* row = sa + warp * N;
+    warp_fft_row<false>(row, N, tw, lane);
+    for (int m = lane; m < modes; m += 32)
+        Xs[(static_cast<int64_t>(b) * C + c0 + warp) * modes + m] = row[m];
+}
+
+// ---------------------------------------------------------------------------
+// layer: grid (C / G, B), 256 threads.  Dynamic shared memory:
+//   sRow [G][N] float2 (inverse transforms, then x1), sY [G][modes] float2,
+//   sW [G][C] float (local weights of the group, FP32 path)
+// ---------------------------------------------------------------------------
+struct Layer1dArgs {
+    const void* h_in;
+    void* h_out;
+    const float2* Xs;
+    const float* x2raw;
+    const float2* tw_inv;
+    Fno1dLayer L;
+    int N, log2N, C, G, modes, act;
+};
+
+__global__ void __launch_bounds__(256) layer1d_kernel(Layer1dArgs a) {
+    extern __shared__ float2 smem[];
+    const int G = a.G, N = a.N, C = a.C, modes = a.modes;
+    float2* sRow = smem;
+    float2* sY = sRow + static_cast<size_t>(G) * N;
+    float* sW = reinterpret_cast<float*>(sY + static_cast<size_t>(G) * modes);
+    const int b = blockIdx.y, o0 = blockIdx.x * G;
+    const Fno1dLayer& L = a.L;
+
+    // spectral contraction (fno.cpp:181-196), sum over input channels in order:
+    //   re += fma(hr, wr, -(hi*wi)),  im += fma(hr, wi, hi*wr)
+    for (int t = threadIdx.x; t < G * modes; t += blockDim.x) {
+        const int r = t / modes, m = t - (t / modes) * modes;
+        const int o = o0 + r;
+        float sr = 0.0f, si = 0.0f;
+        const float2* xb = a.Xs + static_cast<int64_t>(b) * C * modes + m;
+        for (int c = 0; c < C; ++c) {
+            const float2 hv = xb[static_cast<int64_t>(c) * modes];
+            const int64_t wi = (static_cast<int64_t>(c) * C + o) * modes + m;
+            const float wr = __ldg(L.wr + wi), wim = __ldg(L.wi + wi);
+            sr = __fadd_rn(sr, __fmaf_rn(hv.x, wr, -__fmul_rn(hv.y, wim)));
+            si = __fadd_rn(si, __fmaf_rn(hv.x, wim, __fmul_rn(hv.y, wr)));
+        }
+        sY[r * modes + m] = make_float2(sr, si);
+    }
+    if (!L.use_int8)
+        for (int t = threadIdx.x; t < G * C; t += blockDim.x) sW[t] = __ldg(L.loc_w + static_cast<int64_t>(o0) * C + t);
+    __syncthreads();
+
+    // inverse transform of each output row (Irfft, fft.cpp:86-99): bins [0, half) from
+    // the contraction (zero past `modes`), the upper half mirrored as conjugates
+    const int half = N / 2 + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int r = warp; r < G; r += blockDim.x >> 5) {
+        float2* row = sRow + static_cast<size_t>(r) * N;
+        for (int j = lane; j < N; j += 32) {
+            float2 v;
+            if (j < half) {
+                v = j < modes ? sY[r * modes + j] : make_float2(0.0f, 0.0f);
+            } else {
+                const int i = N - j;
+                const float2 u = i < modes ? sY[r * modes + i] : make_float2(0.0f, 0.0f);
+                v = make_float2(u.x, -u.y);
+            }
+            row[bit_reverse(j, a.log2N)] = v;
+        }
+        __syncwarp();
+        warp_fft_row<true>(row, N, a.tw_inv, lane);
+    }
+    __syncthreads();
+
+    // local layer + epilogue, one point per thread iteration
+    const float inv_n = __fdiv_rn(1.0f, static_cast<float>(N));
+    const float zpf_in = static_cast<float>(L.in_zp);
+    const float zpf_fq = static_cast<float>(L.fq_zp);
+    const float zpf_out = static_cast<float>(L.out_zp);
+    for (int p = threadIdx.x; p < N; p += blockDim.x) {
+        const int64_t row = static_cast<int64_t>(b) * N + p;
+        float x2[8];
+        if (L.use_int8) {
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+                if (r < G) x2[r] = __fadd_rn(a.x2raw[row * C + o0 + r], __ldg(L.loc_b + o0 + r));
+        } else {
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+                if (r < G) x2[r] = __ldg(L.loc_b + o0 + r);
+            const int nu = linear_unfused_len(C);
+            for (int k = 0; k < C; ++k) {
+                const float hv = act_value(a.h_in, row * C + k, L.in_codes, L.in_s, zpf_in);
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+                    if (r < G) x2[r] = linear_step(x2[r], hv, sW[r * C + k], k >= nu);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            if (r >= G) break;
+            const int o = o0 + r;
+            float v = x2[r];
+            if (L.fq_kind == 1) {
+                v = fake_quant(v, L.fq_s, zpf_fq);
+            } else if (L.fq_kind == 2) {
+                const int64_t qi = static_cast<int64_t>(o) * N + p;
+                v = fake_quant(v, __ldg(L.pt_s + qi), static_cast<float>(__ldg(L.pt_zp + qi)));
+            } else if (L.fq_kind == 3) {
+                v = fp8_log2_snap(v, L.fq_s);
+            }
+            const float x1 = __fmul_rn(sRow[static_cast<size_t>(r) * N + p].x, inv_n);
+            const float z = __fadd_rn(x1, v);
+            if (L.out_codes) {
+                const int q = L.lut_cells > 0
+                                  ? code_from_lut(z, L.code_lut, L.lut_cells, L.lut_zlo, L.lut_inv_delta)
+                                  : static_cast<int>(fq_code(act_f(z, a.act), L.out_s, zpf_out));
+                static_cast<int8_t*>(a.h_out)[row * C + o] = static_cast<int8_t>(q);
+            } else {
+                static_cast<float*>(a.h_out)[row * C + o] = act_f(z, a.act);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// projection (fno.cpp:683-702): q = Linear(h, proj_q) -> act -> y = Linear(q, proj_out),
+// both the reference's sequential dot product from the bias (linear_step), the proj_out
+// sum interleaved with the production of q[c] in increasing c (the same operation
+// sequence per output).  One point per
+// thread; the point's activation row is staged in shared memory [threads][C + 1].
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) proj1d_kernel(const float* __restrict__ h, int n, int N,
+                                                     int C, int out_ch, int64_t total,
+                                                     const float* __restrict__ pq_w,
+                                                     const float* __restrict__ pq_b,
+                                                     const float* __restrict__ po_w,
+                                                     const float* __restrict__ po_b, int act,
+                                                     float* __restrict__ y) {
+    extern __shared__ float sh[];
+    float* mine = sh + static_cast<size_t>(threadIdx.x) * (C + 1);
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b = t / n;
+        const int p = static_cast<int>(t - b * n);
+        const float* hr = h + (b * N + p) * C;
+        for (int k = 0; k < C; ++k) mine[k] = hr[k];
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = j < out_ch ? __ldg(po_b + j) : 0.0f;
+        const int nu = linear_unfused_len(C);
+        for (int c = 0; c < C; ++c) {
+            float q = __ldg(pq_b + c);
+            const float* wr = pq_w + static_cast<int64_t>(c) * C;
+            for (int k = 0; k < C; ++k) q = linear_step(q, mine[k], __ldg(wr + k), k >= nu);
+            q = act_f(q, act);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (j < out_ch)
+                    acc[j] = linear_step(acc[j], q, __ldg(po_w + static_cast<int64_t>(j) * C + c), c >= nu);
+        }
+        float* yr = y + t * out_ch;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (j < out_ch) yr[j] = acc[j];
+    }
+}
+
+int ilog2(int v) {
+    int l = 0;
+    while ((1 << l) < v) ++l;
+    return l;
+}
+
+// rows per CTA: the largest of 8, 4, 2, 1 that divides C with R * N float2 <= 64 KB
+int rows_per_cta(int C, int N) {
+    for (int R = 8; R > 1; R >>= 1)
+        if (C % R == 0 && static_cast<size_t>(R) * N * sizeof(float2) <= 65536) return R;
+    return 1;
+}
+
+}  // namespace
+
+cudaError_t fno1d_run(const Fno1dPlan& pl, cudaStream_t st) {
+    if (pl.B == 0) return cudaSuccess;
+    const int N = pl.N, C = pl.C, log2N = ilog2(N);
+    const int sms = device_sm_count();
+    const int R = rows_per_cta(C, N);
+    cudaError_t e;
+    {
+        const int64_t total = static_cast<int64_t>(pl.B) * N * C;
+        const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, sms * 16));
+        const Fno1dLayer& L0 = pl.layer[0];
+        if (pl.timer) pl.timer->begin("fno1d_lift", st);
+        lift1d_kernel<<<grid, 256, 0, st>>>(pl.x, pl.n, N, C, pl.in_ch, total, pl.lift_w, pl.lift_b,
+                                            L0.in_codes, L0.in_s, L0.in_zp, pl.h[0]);
+        if (pl.timer) pl.timer->end(st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    const size_t fwd_smem = static_cast<size_t>(R) * N * sizeof(float2);
+    if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(fft1d_fwd_kernel),
+                                  static_cast<int>(fwd_smem))) != cudaSuccess)
+        return e;
+    const size_t layer_smem = static_cast<size_t>(R) * N * sizeof(float2) +
+                              static_cast<size_t>(R) * pl.modes * sizeof(float2) +
+                              static_cast<size_t>(R) * C * sizeof(float);
+    if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(layer1d_kernel),
+                                  static_cast<int>(layer_smem))) != cudaSuccess)
+        return e;
+    for (int i = 0; i < pl.L; ++i) {
+        const Fno1dLayer& L = pl.layer[i];
+        const void* hin = pl.h[i & 1];
+        void* hout = pl.h[(i + 1) & 1];
+        if (pl.timer) pl.timer->begin("fno1d_fft_fwd", st);
+        fft1d_fwd_kernel<<<dim3(C / R, pl.B), 32 * R, fwd_smem, st>>>(
+            hin, L.in_codes, L.in_s, L.in_zp, N, log2N, C, pl.modes, pl.tw_fwd, pl.Xs);
+        if (pl.timer) pl.timer->end(st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if (L.use_int8) {
+            GemmArgs g{};
+            g.A = static_cast<const int8_t*>(hin);
+            g.scale_a_t = L.in_s;
+            g.zp_a_t = L.in_zp;
+            g.W = L.Wq;
+            g.scale_w = L.scale_w;
+            g.zp_w = L.zp_w;
+            g.sum_w = L.sum_w;
+            g.bias = nullptr;
+            g.act = 0;
+            g.C = pl.x2raw;
+            g.M = pl.B * N;
+            g.err = pl.err;
+            if (pl.timer) pl.timer->begin("fno1d_gemm_i8", st);
+            e = gemm_i8_launch(g, C, C, st);
+            if (pl.timer) pl.timer->end(st);
+            if (e != cudaSuccess) return e;
+        }
+        Layer1dArgs a;
+        a.h_in = hin;
+        a.h_out = hout;
+        a.Xs = pl.Xs;
+        a.x2raw = pl.x2raw;
+        a.tw_inv = pl.tw_inv;
+        a.L = L;
+        a.N = N;
+        a.log2N = log2N;
+        a.C = C;
+        a.G = R;
+        a.modes = pl.modes;
+        a.act = pl.act;
+        if (pl.timer) pl.timer->begin("fno1d_layer", st);
+        layer1d_kernel<<<dim3(C / R, pl.B), 256, layer_smem, st>>>(a);
+        if (pl.timer) pl.timer->end(st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    {
+        const int64_t total = static_cast<int64_t>(pl.B) * pl.n;
+        const int threads = C > 128 ? 64 : 128;
+        const size_t smem = static_cast<size_t>(threads) * (C + 1) * sizeof(float);
+        if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(proj1d_kernel),
+                                      static_cast<int>(smem))) != cudaSuccess)
+            return e;
+        const int grid = static_cast<int>(std::min<int64_t>((total + threads - 1) / threads, sms * 8));
+        if (pl.timer) pl.timer->begin("fno1d_proj", st);
+        proj1d_kernel<<<grid, threads, smem, st>>>(static_cast<const float*>(pl.h[pl.L & 1]), pl.n, N, C,
+                                                   pl.out_ch, total, pl.pq_w, pl.pq_b, pl.po_w,
+                                                   pl.po_b, pl.act, pl.y);
+        if (pl.timer) pl.timer->end(st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace nfx

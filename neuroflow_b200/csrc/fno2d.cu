@@ -64,7 +64,7 @@ __device__ __forceinline__ float activation(float z, int act) {
 
 // ---------------------------------------------------------------------------
 // lift: x (M, in_ch) fp32 -> codes (M, C) with the lift.output qparams.
-// fno.cpp:848-853 (Linear + fake-quant), fno.cpp:51-80 (the fma chain from the bias).
+// fno.cpp:848-853 (Linear + fake-quant), fno.cpp:51-80 (the dot product from the bias).
 // ---------------------------------------------------------------------------
 template <int C>
 __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, int64_t M,
@@ -87,10 +87,11 @@ __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, 
         float acc[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) acc[j] = sb[o0 + j];
+        const int nu = linear_unfused_len(in_ch);
         for (int k = 0; k < in_ch; ++k) {
             const float xv = __ldg(x + m * in_ch + k);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) acc[j] = __fmaf_rn(xv, sw[(o0 + j) * in_ch + k], acc[j]);
+            for (int j = 0; j < 16; ++j) acc[j] = linear_step(acc[j], xv, sw[(o0 + j) * in_ch + k], k >= nu);
         }
         uint32_t words[4];
         uint32_t badmask = 0;
@@ -107,7 +108,8 @@ __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, 
             const int j = __ffs(badmask) - 1;
             badmask &= badmask - 1;
             float a = sb[o0 + j];
-            for (int k = 0; k < in_ch; ++k) a = __fmaf_rn(__ldg(x + m * in_ch + k), sw[(o0 + j) * in_ch + k], a);
+            for (int k = 0; k < in_ch; ++k)
+                a = linear_step(a, __ldg(x + m * in_ch + k), sw[(o0 + j) * in_ch + k], k >= nu);
             const uint32_t byte = static_cast<uint32_t>(static_cast<int>(fq_code(a, s, zpf))) & 0xFFu;
             words[j >> 2] = (words[j >> 2] & ~(0xFFu << (8 * (j & 3)))) | (byte << (8 * (j & 3)));
         }
@@ -292,18 +294,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     hi = __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
     lo = __fsub_rn(x, hi);
-}
-
-// the next layer's code from z via the host-built table (nfx_lut.h)
-__device__ __forceinline__ int code_from_lut(float z, const int2* lut, int ncells, float zlo,
-                                             float inv_delta) {
-    const float fi = __fmul_rn(__fsub_rn(z, zlo), inv_delta);
-    int idx = __float2int_rz(fi);
-    idx = idx < 0 ? 0 : (idx > ncells - 1 ? ncells - 1 : idx);
-    const int2 c = lut[idx];
-    const int base = (c.y << 24) >> 24;
-    const int d = (c.y << 16) >> 24;
-    return base + (z >= __int_as_float(c.x) ? d : 0);
 }
 
 template <int C, int MH, int MW, bool PROJ, bool TCX>
@@ -775,7 +765,7 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
             }
             if constexpr (PROJ) {
                 // the 64 activations of every row are in shared memory; the first warp of
-                // each lane quadrant runs the reference's sequential proj_out fma chain
+                // each lane quadrant runs the reference's sequential proj_out dot product
                 if (!epi_sync()) {
                     epi_ok = false;
                     break;
@@ -786,7 +776,9 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                 for (int o = 0; o < C; ++o) {
 #pragma unroll
                     for (int jj = 0; jj < 4; ++jj)
-                        if (jj < p.out_ch) acc_out[jj] = __fmaf_rn(grow[o], sWout[jj * C + o], acc_out[jj]);
+                        if (jj < p.out_ch)
+                            acc_out[jj] = linear_step(acc_out[jj], grow[o], sWout[jj * C + o],
+                                                      o >= linear_unfused_len(C));
                 }
                 const int64_t m = g0 + row;
                 if (m < p.M) {

@@ -182,4 +182,24 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
     return false;
 }
 
+std::vector<float> build_fft_twiddles(int n, bool inverse) {
+    std::vector<float> t(2 * static_cast<size_t>(n > 1 ? n - 1 : 0));
+    const float pi = static_cast<float>(3.14159265358979323846);
+    for (int len = 2; len <= n; len <<= 1) {
+        const float ang = (inverse ? 2.0f : -2.0f) * pi / static_cast<float>(len);
+        const float lr = std::cos(ang), li = std::sin(ang);
+        float wr = 1.0f, wi = 0.0f;
+        for (int k = 0; k < len / 2; ++k) {
+            const size_t e = static_cast<size_t>(len / 2 - 1 + k);
+            t[2 * e] = wr;
+            t[2 * e + 1] = wi;
+            const float nr = std::fma(wr, lr, -(wi * li));
+            const float ni = std::fma(wr, li, wi * lr);
+            wr = nr;
+            wi = ni;
+        }
+    }
+    return t;
+}
+
 }  // namespace nfx

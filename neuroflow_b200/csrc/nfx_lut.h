@@ -46,4 +46,14 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
 // act_ref((k - zp) * s) for k = -128..127 (index k + 128).
 std::vector<float> build_act_table(float s, int zp, int act);
 
+// 3. FFT twiddles.  The reference radix-2 FFT (fft.cpp:49-69) does not evaluate
+//    e^{-+2 pi i k/len}; it starts each butterfly group at w = 1 and updates
+//    w *= wlen after every butterfly, with wlen = (cosf(ang), sinf(ang)),
+//    ang = (-+2.0f * (float)M_PI) / (float)len, and the product in the fused form
+//    the reference build emits (re = fma(wr, lr, -(wi*li)), im = fma(wr, li, wi*lr)).
+//    The table holds those rounded values, stage after stage: entry (len/2 - 1 + k)
+//    is the w of butterfly k at stage len, for len = 2, 4, ..., n (n - 1 entries,
+//    interleaved re, im).
+std::vector<float> build_fft_twiddles(int n, bool inverse);
+
 }  // namespace nfx

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "../../include/nfx.h"
+#include "fno1d.h"
 #include "fno2d.h"
 #include "nfx_internal.h"
 #include "nfx_ir.h"
@@ -110,6 +111,14 @@ struct nfx_runtime {
     int tw_H = 0, tw_W = 0;
     int8_t* fwd_limbs = nullptr;      // tensor-core forward basis digits (W == 128)
     long long* fwd_sum_b = nullptr;
+    // FNO1d state
+    nfx::Fno1dPlan plan1{};
+    int pt_n[nfx::kFno1dMaxLayers] = {};   // per-token table sizes (locs.i.output)
+    int pt_w[nfx::kFno1dMaxLayers] = {};
+    void* f1_bufs[4] = {nullptr, nullptr, nullptr, nullptr};  // h0, h1, Xs, x2raw
+    int64_t f1_cap_BN = 0;                // B * N the buffers hold
+    float2* f1_tw[2] = {nullptr, nullptr};
+    int f1_tw_N = 0;
     std::unique_ptr<nfx::EventTimer> timer;  // per-kernel timing when enabled
 };
 
@@ -437,6 +446,241 @@ int fno2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
     return NFX_OK;
 }
 
+// ---------------------------------------------------------------------------
+// FNO1d (fno.cpp:408-706)
+// ---------------------------------------------------------------------------
+struct F1 {
+    int in_ch, out_ch, width, modes, L, pad;
+};
+F1 fno1d_cfg(const nfx::IrModel& m) {
+    return F1{m.cfg[0], m.cfg[1], m.cfg[2], m.cfg[3], m.cfg[4], m.cfg[5]};
+}
+
+std::string in_key(int i) {
+    return i == 0 ? std::string("lift.output") : "locs." + std::to_string(i - 1) + ".output";
+}
+
+// Create: load-time weight fake-quant (fno.cpp:293-315), uploads, and the per-layer
+// branch decisions of FNO1d::Forward that depend only on the IR.
+int fno1d_create(nfx_runtime* rt) {
+    auto& m = rt->model;
+    const F1 c = fno1d_cfg(m);
+    if (m.quant_enabled)
+        for (const auto& name : m.weight_order) nfx::dequantise_weight(m.weights[name], m, name);
+    if (c.L > nfx::kFno1dMaxLayers || c.width > nfx::kFno1dMaxC || c.width < 1 || c.out_ch > 16 ||
+        c.out_ch < 1 || c.in_ch < 1 || c.modes < 0)
+        return NFX_OK;  // Run reports UnsupportedOp
+    auto& pl = rt->plan1;
+    pl.C = c.width;
+    pl.in_ch = c.in_ch;
+    pl.out_ch = c.out_ch;
+    pl.modes = c.modes;
+    pl.L = c.L;
+    pl.act = m.activation == "relu" ? 1 : 0;
+    pl.lift_w = wptr(rt, "lift.weight");
+    pl.lift_b = wptr(rt, "lift.bias");
+    pl.pq_w = wptr(rt, "proj_q.weight");
+    pl.pq_b = wptr(rt, "proj_q.bias");
+    pl.po_w = wptr(rt, "proj_out.weight");
+    pl.po_b = wptr(rt, "proj_out.bias");
+    if (!pl.lift_w || !pl.lift_b || !pl.pq_w || !pl.pq_b || !pl.po_w || !pl.po_b)
+        return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+    const bool q = m.quant_enabled;
+    for (int i = 0; i < c.L; ++i) {
+        nfx::Fno1dLayer& L = pl.layer[i];
+        L = nfx::Fno1dLayer{};
+        const std::string s = std::to_string(i);
+        L.wr = wptr(rt, "specs." + s + ".weights_real");
+        L.wi = wptr(rt, "specs." + s + ".weights_imag");
+        L.loc_w = wptr(rt, "locs." + s + ".weight");
+        L.loc_b = wptr(rt, "locs." + s + ".bias");
+        if (!L.wr || !L.wi || !L.loc_w || !L.loc_b) return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+        // input snap: the per-tensor map only (fno.cpp:488-508)
+        auto it = m.activation_qparams.find(in_key(i));
+        if (q && it != m.activation_qparams.end()) {
+            L.in_codes = 1;
+            L.in_s = it->second.scale;
+            L.in_zp = it->second.zero_point;
+        }
+        // output fake-quant: FP8, else per-token, else per-tensor (fno.cpp:572-654)
+        const std::string ok = "locs." + s + ".output";
+        if (q) {
+            auto i8 = m.activation_fp8_qparams.find(ok);
+            auto ipt = m.activation_per_token_qparams.find(ok);
+            auto ipx = m.activation_qparams.find(ok);
+            if (i8 != m.activation_fp8_qparams.end()) {
+                L.fq_kind = 3;
+                L.fq_s = i8->second;
+            } else if (ipt != m.activation_per_token_qparams.end()) {
+                L.fq_kind = 2;
+                L.pt_s = upload(rt, ipt->second.scales.data(), ipt->second.scales.size());
+                L.pt_zp = upload(rt, ipt->second.zero_points.data(), ipt->second.zero_points.size());
+                if (!L.pt_s || !L.pt_zp) return rt_fail(rt, NFX_INTERNAL, "qparam upload failed");
+                rt->pt_n[i] = static_cast<int>(std::min(ipt->second.scales.size(), ipt->second.zero_points.size()));
+                rt->pt_w[i] = ipt->second.width;
+            } else if (ipx != m.activation_qparams.end()) {
+                L.fq_kind = 1;
+                L.fq_s = ipx->second.scale;
+                L.fq_zp = ipx->second.zero_point;
+            }
+        }
+    }
+    // each layer's output is the next layer's input: codes when that layer snaps
+    for (int i = 0; i + 1 < c.L; ++i) {
+        nfx::Fno1dLayer& L = pl.layer[i];
+        const nfx::Fno1dLayer& Ln = pl.layer[i + 1];
+        if (!Ln.in_codes) continue;
+        L.out_codes = 1;
+        L.out_s = Ln.in_s;
+        L.out_zp = Ln.in_zp;
+        nfx::CodeLut lut;
+        std::string why;
+        if (nfx::build_code_lut(L.out_s, L.out_zp, pl.act, 4096, lut, why)) {
+            L.code_lut = reinterpret_cast<const int2*>(upload(rt, lut.cells.data(), lut.cells.size()));
+            if (!L.code_lut) return rt_fail(rt, NFX_INTERNAL, "table upload failed");
+            L.lut_cells = static_cast<int>(lut.cells.size());
+            L.lut_zlo = lut.zlo;
+            L.lut_inv_delta = lut.inv_delta;
+        }
+    }
+    return NFX_OK;
+}
+
+// EnableInt8Gemm (runtime.cpp:155-166 -> fno.cpp:360-406): the flag is set whatever
+// the IR holds; a layer dispatches through the INT8 GEMM when LinearDispatchTryInt8
+// would (per-channel axis-0 weight codes, a per-tensor input qparam, no per-token or
+// FP8 qparam for the input key).
+void fno1d_enable_int8(nfx_runtime* rt) {
+    auto& m = rt->model;
+    const F1 c = fno1d_cfg(m);
+    rt->int8_enabled = true;
+    if (!m.quant_enabled || c.L > nfx::kFno1dMaxLayers) return;
+    auto& pl = rt->plan1;
+    if (!pl.lift_w) return;  // unsupported geometry; Run reports it
+    for (int i = 0; i < c.L; ++i) {
+        nfx::Fno1dLayer& L = pl.layer[i];
+        const std::string k = in_key(i);
+        if (m.activation_per_token_qparams.count(k) || m.activation_fp8_qparams.count(k)) continue;
+        if (!m.activation_qparams.count(k)) continue;
+        const std::string wname = "locs." + std::to_string(i) + ".weight";
+        auto pc = m.weight_per_channel_qparams.find(wname);
+        if (pc == m.weight_per_channel_qparams.end()) continue;
+        std::vector<int8_t> codes;
+        std::vector<int32_t> sum_w;
+        if (!nfx::quantise_weight_2d(m.weights.at(wname), pc->second, codes, sum_w)) continue;
+        L.Wq = upload(rt, codes.data(), codes.size());
+        L.scale_w = upload(rt, pc->second.scales.data(), pc->second.scales.size());
+        L.zp_w = upload(rt, pc->second.zero_points.data(), pc->second.zero_points.size());
+        L.sum_w = upload(rt, sum_w.data(), sum_w.size());
+        if (!L.Wq || !L.scale_w || !L.zp_w || !L.sum_w) continue;
+        L.use_int8 = 1;
+    }
+}
+
+int check_fno1d_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t* ys, int yr) {
+    const F1 c = fno1d_cfg(rt->model);
+    if (xr != 3) return rt_fail(rt, NFX_SHAPE_MISMATCH, "expected 3D input (batch, n, in_ch)");
+    if (xs[2] != c.in_ch) return rt_fail(rt, NFX_SHAPE_MISMATCH, "input channels mismatch");
+    if (yr != 3 || ys[0] != xs[0] || ys[1] != xs[1] || ys[2] != c.out_ch)
+        return rt_fail(rt, NFX_SHAPE_MISMATCH, "output buffer shape mismatch");
+    if (!(xs[1] > 0 && (xs[1] & (xs[1] - 1)) == 0))
+        return rt_fail(rt, NFX_INVALID_ARG, "Stage 1: input length n must be a power of two");
+    return NFX_OK;
+}
+
+int fno1d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
+    const F1 c = fno1d_cfg(rt->model);
+    auto& pl0 = rt->plan1;
+    if (!pl0.lift_w)
+        return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                       "FNO1d GPU executor: needs width <= 256, out_channels <= 16, <= 8 layers");
+    const int B = static_cast<int>(xs[0]), n = static_cast<int>(xs[1]);
+    int N = n;
+    if (c.pad > 1 && n % c.pad) N = n + (c.pad - n % c.pad);
+    if (N & (N - 1))
+        return rt_fail(rt, NFX_INVALID_ARG, "FNO1d: padded length must be a power of two");
+    if (N > nfx::kFno1dMaxN)
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, "FNO1d GPU executor: padded length above 8192");
+    if (c.modes > N / 2 + 1)
+        return rt_fail(rt, NFX_INVALID_ARG, "FNO1d: modes exceed n/2 + 1");
+    for (int i = 0; i < c.L; ++i) {
+        const auto& L = pl0.layer[i];
+        if (L.fq_kind == 2 && (rt->pt_w[i] != c.width || static_cast<int64_t>(rt->pt_n[i]) <
+                                                            static_cast<int64_t>(N) * c.width))
+            return rt_fail(rt, NFX_INVALID_ARG,
+                           "FNO1d: per-token qparams of locs." + std::to_string(i) +
+                               ".output do not cover (n, width)");
+        if (L.use_int8 && !nfx::gemm_i8_supported(c.width, c.width))
+            return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                           "FNO1d INT8 GEMM: width must be 32, 64, 128 or 256");
+    }
+    if (B == 0) return NFX_OK;
+    // twiddles for N
+    if (rt->f1_tw_N != N) {
+        for (int inv = 0; inv < 2; ++inv) {
+            const std::vector<float> t = nfx::build_fft_twiddles(N, inv == 1);
+            if (rt->f1_tw[inv]) cudaFree(rt->f1_tw[inv]);
+            rt->f1_tw[inv] = nullptr;
+            void* p = nullptr;
+            if (!cuda_ok(rt, cudaMalloc(&p, t.size() * 4 + 16), "cudaMalloc twiddles")) return NFX_INTERNAL;
+            rt->f1_tw[inv] = static_cast<float2*>(p);
+            if (!t.empty() && !cuda_ok(rt, cudaMemcpy(p, t.data(), t.size() * 4, cudaMemcpyHostToDevice),
+                                       "cudaMemcpy twiddles"))
+                return NFX_INTERNAL;
+        }
+        rt->f1_tw_N = N;
+    }
+    const int64_t BN = static_cast<int64_t>(B) * N;
+    if (BN > rt->f1_cap_BN) {
+        for (auto*& p : rt->f1_bufs) {
+            if (p) cudaFree(p);
+            p = nullptr;
+        }
+        const size_t sizes[4] = {static_cast<size_t>(BN) * c.width * 4, static_cast<size_t>(BN) * c.width * 4,
+                                 static_cast<size_t>(B) * c.width * (c.modes > 0 ? c.modes : 1) * sizeof(float2),
+                                 static_cast<size_t>(BN) * c.width * 4};
+        for (int i = 0; i < 4; ++i)
+            if (!cuda_ok(rt, cudaMalloc(&rt->f1_bufs[i], sizes[i] + 256), "cudaMalloc activations"))
+                return NFX_INTERNAL;
+        rt->f1_cap_BN = BN;
+    }
+    nfx::Fno1dPlan pl = pl0;
+    pl.B = B;
+    pl.n = n;
+    pl.N = N;
+    pl.x = dx;
+    pl.y = dy;
+    pl.tw_fwd = rt->f1_tw[0];
+    pl.tw_inv = rt->f1_tw[1];
+    pl.h[0] = rt->f1_bufs[0];
+    pl.h[1] = rt->f1_bufs[1];
+    pl.Xs = static_cast<float2*>(rt->f1_bufs[2]);
+    pl.x2raw = static_cast<float*>(rt->f1_bufs[3]);
+    if (c.L == 0) pl.layer[0] = nfx::Fno1dLayer{};
+    pl.err = nfx::device_error_word();
+    if (!pl.err) return rt_fail(rt, NFX_INTERNAL, "no device error word");
+    pl.timer = rt->timer.get();
+    const cudaError_t e = nfx::fno1d_run(pl, st);
+    if (e != cudaSuccess)
+        return rt_fail(rt, NFX_INTERNAL, std::string("FNO1d launch failed: ") + cudaGetErrorString(e));
+    return NFX_OK;
+}
+
+// ---------------------------------------------------------------------------
+// op dispatch of Run / RunDevice
+// ---------------------------------------------------------------------------
+int check_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t* ys, int yr) {
+    if (rt->model.op == "FNO2d") return check_fno2d_shapes(rt, xs, xr, ys, yr);
+    if (rt->model.op == "FNO1d") return check_fno1d_shapes(rt, xs, xr, ys, yr);
+    return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                   "the GPU runtime executes FNO1d and FNO2d through Run; op is " + rt->model.op);
+}
+
+int launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
+    if (rt->model.op == "FNO1d") return fno1d_launch(rt, dx, xs, dy, st);
+    return fno2d_launch(rt, dx, xs, dy, st);
+}
+
 struct DeviceGuard {
     int prev = -1;
     explicit DeviceGuard(int d) {
@@ -528,6 +772,9 @@ int nfx_runtime_create(const char* ir_path, int device, nfx_runtime** out) {
     if (op == "FNO2d") {
         s = fno2d_create(rt.get());
         if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
+    } else if (op == "FNO1d") {
+        s = fno1d_create(rt.get());
+        if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
     }
     if (!nfx::device_error_word())
         return nfx::set_thread_error(NFX_INTERNAL, "cannot allocate the device error word");
@@ -562,6 +809,10 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
     for (void* p : rt->act_bufs)
         if (p) cudaFree(p);
     for (auto* p : rt->tw)
+        if (p) cudaFree(p);
+    for (void* p : rt->f1_bufs)
+        if (p) cudaFree(p);
+    for (auto* p : rt->f1_tw)
         if (p) cudaFree(p);
     if (rt->fwd_limbs) cudaFree(rt->fwd_limbs);
     if (rt->fwd_sum_b) cudaFree(rt->fwd_sum_b);
@@ -610,6 +861,7 @@ void nfx_runtime_enable_int8_gemm(nfx_runtime* rt) {
     if (!rt) return;
     DeviceGuard g(rt->device);
     if (rt->model.op == "FNO2d") fno2d_enable_int8(rt);
+    if (rt->model.op == "FNO1d") fno1d_enable_int8(rt);
 }
 
 int nfx_runtime_is_int8_gemm_enabled(const nfx_runtime* rt) { return rt && rt->int8_enabled ? 1 : 0; }
@@ -621,13 +873,10 @@ int nfx_runtime_run_device(nfx_runtime* rt, const float* x, const int64_t* x_sha
     if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
     if (!x_shape || !y_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
     DeviceGuard g(rt->device);
-    if (rt->model.op != "FNO2d")
-        return rt_fail(rt, NFX_UNSUPPORTED_OP,
-                       "the GPU runtime executes FNO2d in this release; op is " + rt->model.op);
-    int s = check_fno2d_shapes(rt, x_shape, x_rank, y_shape, y_rank);
+    int s = check_shapes(rt, x_shape, x_rank, y_shape, y_rank);
     if (s != NFX_OK) return s;
     if (numel(x_shape, x_rank) > 0 && (!x || !y)) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
-    return fno2d_launch(rt, x, x_shape, y, static_cast<cudaStream_t>(stream));
+    return launch(rt, x, x_shape, y, static_cast<cudaStream_t>(stream));
 }
 
 int nfx_runtime_check(nfx_runtime* rt) {
@@ -651,19 +900,14 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
     if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
     if (!x_shape || !y_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
     DeviceGuard g(rt->device);
-    if (rt->model.op != "FNO2d")
-        return rt_fail(rt, NFX_UNSUPPORTED_OP,
-                       "the GPU runtime executes FNO2d in this release; op is " + rt->model.op);
-    int s = check_fno2d_shapes(rt, x_shape, x_rank, y_shape, y_rank);
+    int s = check_shapes(rt, x_shape, x_rank, y_shape, y_rank);
     if (s != NFX_OK) return s;
     const size_t nx = static_cast<size_t>(numel(x_shape, x_rank));
     const size_t ny = static_cast<size_t>(numel(y_shape, y_rank));
     if (nx == 0) return NFX_OK;
     if (!x || !y) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
     if (nx > rt->dx_cap) {
-        if (rt->fwd_limbs) cudaFree(rt->fwd_limbs);
-    if (rt->fwd_sum_b) cudaFree(rt->fwd_sum_b);
-    if (rt->dx) cudaFree(rt->dx);
+        if (rt->dx) cudaFree(rt->dx);
         rt->dx = nullptr;
         if (!cuda_ok(rt, cudaMalloc(&rt->dx, nx * 4), "cudaMalloc input")) return NFX_INTERNAL;
         rt->dx_cap = nx;
@@ -676,11 +920,11 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
     }
     if (!cuda_ok(rt, cudaMemcpyAsync(rt->dx, x, nx * 4, cudaMemcpyHostToDevice, rt->stream), "H2D"))
         return NFX_INTERNAL;
-    s = fno2d_launch(rt, rt->dx, x_shape, rt->dy, rt->stream);
+    s = launch(rt, rt->dx, x_shape, rt->dy, rt->stream);
     if (s != NFX_OK) return s;
     if (!cuda_ok(rt, cudaMemcpyAsync(y, rt->dy, ny * 4, cudaMemcpyDeviceToHost, rt->stream), "D2H"))
         return NFX_INTERNAL;
-    if (!cuda_ok(rt, cudaStreamSynchronize(rt->stream), "FNO2d execution")) return NFX_INTERNAL;
+    if (!cuda_ok(rt, cudaStreamSynchronize(rt->stream), "execution")) return NFX_INTERNAL;
     return nfx_runtime_check(rt);
 }
 

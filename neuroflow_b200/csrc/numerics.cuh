@@ -74,6 +74,31 @@ __device__ __forceinline__ float gelu_tanh(float z) {
 
 __device__ __forceinline__ float relu_ref(float z) { return z < 0.0f ? 0.0f : z; }
 
+// fno.cpp:51-80 Linear (acc = b; acc += x[p]*w[p] for p = 0..k-1) as the reference
+// build (GCC -O3 with the AVX-512 flags of cpp/CMakeLists.txt:78) evaluates it: the
+// sum is sequential, but the first linear_unfused_len(k) products come from 16- and
+// 8-wide vector multiplies and are added rounded; the scalar tail (k mod 8 terms) is
+// fused.
+__host__ __device__ constexpr int linear_unfused_len(int k) {
+    return (k - (k / 16) * 16 >= 8) ? (k / 16) * 16 + 8 : (k / 16) * 16;
+}
+__device__ __forceinline__ float linear_step(float acc, float x, float w, bool fused) {
+    return fused ? __fmaf_rn(x, w, acc) : __fadd_rn(acc, __fmul_rn(x, w));
+}
+
+// The next layer's code from z = x1 + x2 via the host-built exact table (nfx_lut.h):
+// cell of z, then base + d * (z >= breakpoint).
+__device__ __forceinline__ int code_from_lut(float z, const int2* lut, int ncells, float zlo,
+                                             float inv_delta) {
+    const float fi = __fmul_rn(__fsub_rn(z, zlo), inv_delta);
+    int idx = __float2int_rz(fi);
+    idx = idx < 0 ? 0 : (idx > ncells - 1 ? ncells - 1 : idx);
+    const int2 c = lut[idx];
+    const int base = (c.y << 24) >> 24;
+    const int d = (c.y << 16) >> 24;
+    return base + (z >= __int_as_float(c.x) ? d : 0);
+}
+
 // int8_gemm.cpp:574-577 epilogue of LinearForwardBatched for one output:
 //   v = acc - zp_w*sum_a - zp_A*sum_w + K*zp_w*zp_A,  acc = sum a*(w - zp_w)
 // Given raw = sum a*w (the tensor-core product) and sum_a, acc = raw - zp_w*sum_a, so

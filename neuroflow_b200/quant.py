@@ -6,13 +6,14 @@ tests and bench.py carry the same kind of qparams a reference user would export:
   * compute_per_channel_qparams neuroflow/quant/static_quant.py:536-589
   * _channel_axis_for_weight    neuroflow/quant/static_quant.py:837-852
   * compute_fp8_e4m3_qparams    neuroflow/quant/static_quant.py:338-352
+  * calibrate(per_token=True)   neuroflow/quant/static_quant.py:658-717
 The inference path never calls this module; it reads the qparams from the IR.
 """
 from __future__ import annotations
 
 import numpy as np
 
-from .ir import FP8, PerChannel, PerTensor
+from .ir import FP8, PerChannel, PerTensor, PerToken
 
 INT8_MIN, INT8_MAX = -128, 127
 
@@ -134,3 +135,22 @@ def gemm_case(seed: int, M: int, K: int, N: int):
     Wq, sum_w = quantise_weight_2d(W, qp)
     return dict(Aq=Aq, sA=sA, zA=zA, Wq=Wq, sW=np.asarray(qp.scales, np.float32),
                 zW=np.asarray(qp.zero_points, np.int32), sum_w=sum_w, bias=bias)
+
+
+def per_token_qparams(stacked: np.ndarray) -> PerToken:
+    """Per-token (per (n, w) element) INT8 qparams of a stacked (batch, n, w) Linear
+    output: min/max over the batch axis, the per-channel rule per element, flattened
+    row-major over (n, w)."""
+    t = np.asarray(stacked, dtype=np.float32)
+    _, n, w = t.shape
+    mins = t.min(axis=0)
+    maxs = t.max(axis=0)
+    spans = maxs - mins
+    scales = np.where(spans > 0, spans / (INT8_MAX - INT8_MIN), 1.0).astype(np.float32)
+    raw = np.round(INT8_MIN - mins / scales)
+    zps = np.clip(raw, INT8_MIN, INT8_MAX).astype(np.int32)
+    lo = zps == INT8_MIN
+    hi = zps == INT8_MAX
+    scales = np.where(lo & (maxs > 0), maxs / (INT8_MAX - INT8_MIN), scales).astype(np.float32)
+    scales = np.where(hi & (mins < 0), -mins / (INT8_MAX - INT8_MIN), scales).astype(np.float32)
+    return PerToken(scales.reshape(-1), zps.reshape(-1), w)

@@ -135,3 +135,111 @@ def fno2d_model(seed: int, in_ch=3, out_ch=1, width=64, mh=12, mw=12, L=4, H=128
     cfg = dict(in_channels=in_ch, out_channels=out_ch, width=width, modes_h=mh, modes_w=mw,
                n_layers=L, pad_factor=1)
     return ir.Model(op="FNO2d", config=cfg, weights=wts, qparams=qp, quant_enabled=True)
+
+
+# ------------------------------------------------------------------------- FNO1d
+def grf1d(rng: np.random.Generator, n_samples: int, n: int, n_modes: int = 32) -> np.ndarray:
+    """(n_samples, n) periodic field: sum of `n_modes` cos/sin pairs with coefficients
+    ~ N(0, k^-2), normalised to unit std."""
+    xs = np.arange(n, dtype=np.float64) / n
+    k = np.arange(1, n_modes + 1, dtype=np.float64)
+    basis_c = np.cos(2 * np.pi * k[:, None] * xs[None, :])
+    basis_s = np.sin(2 * np.pi * k[:, None] * xs[None, :])
+    out = np.empty((n_samples, n), np.float32)
+    for i in range(n_samples):
+        a = rng.standard_normal(n_modes) / k
+        b = rng.standard_normal(n_modes) / k
+        f = a @ basis_c + b @ basis_s
+        f = (f - f.mean()) / (f.std() + 1e-12)
+        out[i] = f.astype(np.float32)
+    return out
+
+
+def fno1d_inputs(rng: np.random.Generator, n_samples: int, n: int, in_ch: int = 2) -> np.ndarray:
+    """(n_samples, n, in_ch): field u0 + the grid x in [0, 1) (+ extra fields)."""
+    x = np.empty((n_samples, n, in_ch), np.float32)
+    x[..., 0] = grf1d(rng, n_samples, n)
+    if in_ch >= 2:
+        x[..., 1] = (np.arange(n, dtype=np.float32) / n)[None, :]
+    for c in range(2, in_ch):
+        x[..., c] = grf1d(rng, n_samples, n)
+    return x
+
+
+def fno1d_weights(rng, in_ch, out_ch, width, modes, L):
+    wts = {}
+    wts["lift.weight"], wts["lift.bias"] = _kaiming_linear(rng, width, in_ch)
+    s = 1.0 / (width * width)
+    for i in range(L):
+        wts[f"specs.{i}.weights_real"] = (s * rng.uniform(-1, 1, (width, width, modes))).astype(np.float32)
+        wts[f"specs.{i}.weights_imag"] = (s * rng.uniform(-1, 1, (width, width, modes))).astype(np.float32)
+        wts[f"locs.{i}.weight"], wts[f"locs.{i}.bias"] = _kaiming_linear(rng, width, width)
+    wts["proj_q.weight"], wts["proj_q.bias"] = _kaiming_linear(rng, width, width)
+    wts["proj_out.weight"], wts["proj_out.bias"] = _kaiming_linear(rng, out_ch, width)
+    return wts
+
+
+def fno1d_linear_outputs(wts: dict, x: np.ndarray, L: int, modes: int, pad_factor: int = 1) -> dict:
+    """Float32 FNO1d forward (neuroflow/nn/fno.py:126-150) returning every Linear's
+    output (batch, n, features), the tensors `calibrate` hooks."""
+    import torch
+    import torch.nn.functional as F
+
+    def lin(t, name):
+        return t @ torch.from_numpy(wts[name + ".weight"]).T + torch.from_numpy(wts[name + ".bias"])
+
+    obs = {}
+    with torch.no_grad():
+        h = lin(torch.from_numpy(x), "lift")
+        obs["lift.output"] = h.numpy().copy()
+        h = h.permute(0, 2, 1)
+        pad_len = 0
+        if pad_factor > 1:
+            pad_len = (pad_factor - (h.shape[-1] % pad_factor)) % pad_factor
+            h = F.pad(h, (0, pad_len))
+        n = h.shape[-1]
+        for i in range(L):
+            xf = torch.fft.rfft(h, dim=-1)[..., :modes]
+            wgt = torch.complex(torch.from_numpy(wts[f"specs.{i}.weights_real"]),
+                                torch.from_numpy(wts[f"specs.{i}.weights_imag"]))
+            of = F.pad(torch.einsum("bim,iom->bom", xf, wgt), (0, (n // 2 + 1) - modes))
+            x1 = torch.fft.irfft(of, n=n, dim=-1)
+            x2 = lin(h.permute(0, 2, 1), f"locs.{i}")
+            obs[f"locs.{i}.output"] = x2.numpy().copy()
+            h = F.gelu(x1 + x2.permute(0, 2, 1))
+        if pad_len > 0:
+            h = h[..., :-pad_len]
+        q = lin(h.permute(0, 2, 1), "proj_q")
+        obs["proj_q.output"] = q.numpy().copy()
+        y = lin(F.gelu(q), "proj_out")
+        obs["proj_out.output"] = y.numpy().copy()
+    return obs
+
+
+def fno1d_model(seed: int, in_ch=2, out_ch=1, width=64, modes=16, L=4, n=1024, n_calib=32,
+                per_token=True, per_channel=True, quantised=True, pad_factor=0,
+                calib_chunk=32) -> ir.Model:
+    """A random-init FNO1d (configs[0] shape by default).  With `quantised`, a calibrated
+    NIRQ block: per-channel (or per-tensor) weights and per-token (or per-tensor)
+    activations, as `quantise_model(per_channel_weights, per_token_activations)`
+    exports them."""
+    rng = np.random.default_rng(seed)
+    wts = fno1d_weights(rng, in_ch, out_ch, width, modes, L)
+    cfg = dict(in_channels=in_ch, out_channels=out_ch, width=width, modes=modes, n_layers=L,
+               pad_factor=pad_factor, _=0)
+    if not quantised:
+        return ir.Model(op="FNO1d", config=cfg, weights=wts, quant_enabled=False)
+    crng = np.random.default_rng(seed + 1)
+    obs = {}
+    done = 0
+    while done < n_calib:
+        nb = min(calib_chunk, n_calib - done)
+        xc = fno1d_inputs(crng, nb, n, in_ch)
+        for k, v in fno1d_linear_outputs(wts, xc, L, modes, pad_factor).items():
+            obs.setdefault(k, []).append(v)
+        done += nb
+    qp = quant.weight_qparams(wts, per_channel=per_channel)
+    for k, vs in obs.items():
+        st = np.concatenate(vs, axis=0)
+        qp[k] = quant.per_token_qparams(st) if per_token else quant.tensor_qparams(st)
+    return ir.Model(op="FNO1d", config=cfg, weights=wts, qparams=qp, quant_enabled=True)

@@ -56,6 +56,26 @@ class _FNO2d(C.Structure):
                 + [("a_locs", _AQ * MAX_LAYERS)])
 
 
+class _AQ1(C.Structure):
+    _fields_ = [("scale", C.c_float), ("zp", C.c_int32), ("has", C.c_int32),
+                ("fp8_scale", C.c_float), ("has_fp8", C.c_int32), ("pt_scales", _f32p),
+                ("pt_zps", _i32p), ("pt_n", C.c_int64), ("pt_width", C.c_int32),
+                ("has_pt", C.c_int32)]
+
+
+class _FNO1d(C.Structure):
+    _fields_ = ([(n, C.c_int32) for n in ("in_ch", "out_ch", "width", "modes", "n_layers",
+                                          "pad_factor", "relu", "quant_enabled", "int8_enabled")]
+                + [(n, _f32p) for n in ("lift_w", "lift_b", "proj_q_w", "proj_q_b",
+                                        "proj_out_w", "proj_out_b")]
+                + [(n, _f32p * MAX_LAYERS) for n in ("spec_wr", "spec_wi", "loc_w", "loc_b")]
+                + [(n, _WQ) for n in ("q_lift_w", "q_lift_b", "q_proj_q_w", "q_proj_q_b",
+                                      "q_proj_out_w", "q_proj_out_b")]
+                + [(n, _WQ * MAX_LAYERS) for n in ("q_spec_wr", "q_spec_wi", "q_loc_w",
+                                                   "q_loc_b")]
+                + [("a_lift", _AQ1), ("a_locs", _AQ1 * MAX_LAYERS)])
+
+
 class _Taps(C.Structure):
     _fields_ = [("codes_in", _i8p * (MAX_LAYERS + 1)), ("x1_out", _f32p * MAX_LAYERS),
                 ("h_out", _f32p * MAX_LAYERS)]
@@ -72,6 +92,8 @@ class Oracle:
         L.nfo_fno2d_forward.restype = C.c_int
         L.nfo_fno2d_forward.argtypes = [C.POINTER(_FNO2d), C.c_int, _f32p, C.c_int, C.c_int,
                                         C.c_int, _f32p, C.POINTER(_Taps)]
+        L.nfo_fno1d_forward.restype = C.c_int
+        L.nfo_fno1d_forward.argtypes = [C.POINTER(_FNO1d), _f32p, C.c_int, C.c_int, _f32p]
 
     # -- primitives ---------------------------------------------------------
     def quantise_activation(self, A, scale, zp):
@@ -201,6 +223,67 @@ class Oracle:
             raise RuntimeError(f"nfo_fno2d_forward failed: {rc}")
         del keep
         return (y, tap_arrays) if taps else y
+
+
+    # -- FNO1d -----------------------------------------------------------------
+    def fno1d_forward(self, model, x, int8: bool = False):
+        """The reference FNO1d::Forward after Create (and EnableInt8Gemm if `int8`)."""
+        x = _c(x, np.float32)
+        B, n, _ = x.shape
+        st, keep = build_fno1d_struct(model, int8)
+        y = np.empty((B, n, model.config["out_channels"]), np.float32)
+        rc = self.lib.nfo_fno1d_forward(C.byref(st), _p(x), B, n, _p(y))
+        if rc != 0:
+            raise RuntimeError(f"nfo_fno1d_forward failed: {rc}")
+        del keep
+        return y
+
+
+def _aq1(model, key, keep):
+    from neuroflow_b200 import ir
+    a = _AQ1()
+    qp = model.qparams.get(key) if model.quant_enabled else None
+    if isinstance(qp, ir.PerTensor):
+        a.scale, a.zp, a.has = float(qp.scale), int(qp.zero_point), 1
+    elif isinstance(qp, ir.FP8):
+        a.fp8_scale, a.has_fp8 = float(qp.scale), 1
+    elif isinstance(qp, ir.PerToken):
+        sc = _c(qp.scales, np.float32)
+        zp = _c(qp.zero_points, np.int32)
+        keep += [sc, zp]
+        a.pt_scales, a.pt_zps, a.pt_n = _p(sc), _p(zp, _i32p), sc.size
+        a.pt_width, a.has_pt = int(qp.width), 1
+    return a
+
+
+def build_fno1d_struct(model, int8: bool):
+    cfg, w = model.config, model.weights
+    keep = []
+    st = _FNO1d()
+    st.in_ch, st.out_ch, st.width = cfg["in_channels"], cfg["out_channels"], cfg["width"]
+    st.modes, st.n_layers, st.pad_factor = cfg["modes"], cfg["n_layers"], cfg.get("pad_factor", 0)
+    st.relu = 1 if model.activation == "relu" else 0
+    st.quant_enabled = 1 if model.quant_enabled else 0
+    st.int8_enabled = 1 if int8 else 0
+
+    def arr(name):
+        a = _c(w[name], np.float32)
+        keep.append(a)
+        return _p(a)
+
+    for fld, nm in (("lift_w", "lift.weight"), ("lift_b", "lift.bias"),
+                    ("proj_q_w", "proj_q.weight"), ("proj_q_b", "proj_q.bias"),
+                    ("proj_out_w", "proj_out.weight"), ("proj_out_b", "proj_out.bias")):
+        setattr(st, fld, arr(nm))
+        setattr(st, "q_" + fld, _wq(model.qparams.get(nm), keep))
+    for i in range(cfg["n_layers"]):
+        for fld, nm in (("spec_wr", f"specs.{i}.weights_real"), ("spec_wi", f"specs.{i}.weights_imag"),
+                        ("loc_w", f"locs.{i}.weight"), ("loc_b", f"locs.{i}.bias")):
+            getattr(st, fld)[i] = arr(nm)
+            getattr(st, "q_" + fld)[i] = _wq(model.qparams.get(nm), keep)
+        st.a_locs[i] = _aq1(model, f"locs.{i}.output", keep)
+    st.a_lift = _aq1(model, "lift.output", keep)
+    return st, keep
 
 
 def _wq(qp, keep):

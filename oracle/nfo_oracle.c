@@ -206,10 +206,12 @@ void nfo_apply_activation(float* data, int64_t n, int relu) {
         for (int64_t i = 0; i < n; ++i)
             if (data[i] < 0.0f) data[i] = 0.0f;
     } else {
+        /* the reference build contracts z + 0.044715f*z*z*z into one fma */
         const float c = sqrtf(2.0f / (float)M_PI);
         for (int64_t i = 0; i < n; ++i) {
             float z = data[i];
-            data[i] = 0.5f * z * (1.0f + tanhf(c * (z + 0.044715f * z * z * z)));
+            const float inner = fmaf(0.044715f * z * z, z, z);
+            data[i] = 0.5f * z * (1.0f + tanhf(c * inner));
         }
     }
 }
@@ -243,14 +245,24 @@ void nfo_int8_gemm_rows(const int8_t* A_q, const float* scale_A, const int32_t* 
             if (bias) out = out + bias[o];
             if (gelu) {
                 float z = out;
-                out = 0.5f * z * (1.0f + tanhf(c * (z + 0.044715f * z * z * z)));
+                out = 0.5f * z * (1.0f + tanhf(c * fmaf(0.044715f * z * z, z, z)));
             }
             C[r * N + o] = out;
         }
     }
 }
 
-/* fno.cpp:51-80 Linear, the hand-rolled loop (the reference is built without Eigen). */
+/* fno.cpp:51-80 Linear, the hand-rolled loop (the reference is built without Eigen).
+ * The reference build (GCC -O3, cpp/CMakeLists.txt:78 flags with AVX-512) vectorises
+ * the dot product as 16-wide blocks of products that are then added to the
+ * accumulator one by one in order (unfused), one 8-wide block when at least 8 terms
+ * remain, and a scalar tail of fused multiply-adds for the last k mod 8 terms.  The
+ * sum order is the plain sequential one throughout; only the fusion changes. */
+int nfo_linear_unfused_len(int k) {
+    const int a = (k / 16) * 16;
+    return (k - a >= 8) ? a + 8 : a;
+}
+
 void nfo_linear(const float* x, const float* W, const float* b, int bsz, int k, int n,
                 float* y) {
     for (int i = 0; i < bsz; ++i) {
@@ -259,7 +271,10 @@ void nfo_linear(const float* x, const float* W, const float* b, int bsz, int k, 
         for (int j = 0; j < n; ++j) {
             float acc = b ? b[j] : 0.0f;
             const float* wj = W + (int64_t)j * k;
-            for (int p = 0; p < k; ++p) acc += xi[p] * wj[p];
+            const int vec = nfo_linear_unfused_len(k);
+            int p = 0;
+            for (; p < vec; ++p) acc = acc + xi[p] * wj[p];
+            for (; p < k; ++p) acc = fmaf(xi[p], wj[p], acc);
             yi[j] = acc;
         }
     }
@@ -476,8 +491,8 @@ void nfo_spectral_conv1d(const float* h, int bsz, int w, int n, int modes,
                     float hi = Hs[wi2 * half * 2 + 2 * mi + 1];
                     float wr = w_real[((wi2 * w) + wo) * modes + mi];
                     float wi3 = w_imag[((wi2 * w) + wo) * modes + mi];
-                    sum_re += hr * wr - hi * wi3;
-                    sum_im += hr * wi3 + hi * wr;
+                    sum_re = sum_re + fmaf(hr, wr, -(hi * wi3));
+                    sum_im = sum_im + fmaf(hr, wi3, hi * wr);
                 }
                 Out_ft[wo * half * 2 + 2 * mi] = sum_re;
                 Out_ft[wo * half * 2 + 2 * mi + 1] = sum_im;
@@ -518,8 +533,8 @@ void nfo_spectral_conv2d(const float* h, int bsz, int w, int H, int W, int modes
                             w_imag + ((((int64_t)wi * w) + wo) * modes_h + mi) * modes_w + mj;
                         float wr = w_wi[0];
                         float wii = wi_wi[0];
-                        sum_re += hr * wr - hi * wii;
-                        sum_im += hr * wii + hi * wr;
+                        sum_re = sum_re + fmaf(hr, wr, -(hi * wii));
+                        sum_im = sum_im + fmaf(hr, wii, hi * wr);
                     }
                     float* Out_wo = Out_ft + (((int64_t)wo * H + mi) * half_w + mj) * 2;
                     Out_wo[0] = sum_re;
@@ -813,6 +828,244 @@ int nfo_fno2d_forward(const nfo_fno2d* m, int mode, const float* x, int bsz, int
         free(lsum[i]);
     }
     for (int i = 0; i < L; ++i) {
+        free(swr[i]);
+        free(swi[i]);
+        free(lw[i]);
+        free(lb[i]);
+    }
+    free(lift_w);
+    free(lift_b);
+    free(pq_w);
+    free(pq_b);
+    free(po_w);
+    free(po_b);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* FNO1d (fno.cpp:408-706)                                                    */
+/* ------------------------------------------------------------------------- */
+
+/* Activation qparams of one ".output" key as FNO1d consults them: the per-tensor
+ * INT8 map, the per-token map (fno.cpp:606-628) and the FP8 map (fno.cpp:580-603). */
+typedef struct {
+    float scale;
+    int32_t zp;
+    int32_t has;
+    float fp8_scale;
+    int32_t has_fp8;
+    const float* pt_scales;
+    const int32_t* pt_zps;
+    int64_t pt_n;
+    int32_t pt_width;
+    int32_t has_pt;
+} nfo_aq1;
+
+typedef struct {
+    int32_t in_ch, out_ch, width, modes, n_layers, pad_factor, relu;
+    int32_t quant_enabled;  /* the IR carried a NIRQ block (runtime.cpp:25-35) */
+    int32_t int8_enabled;   /* InferenceRuntime::EnableInt8Gemm was called */
+    const float* lift_w;
+    const float* lift_b;
+    const float* proj_q_w;
+    const float* proj_q_b;
+    const float* proj_out_w;
+    const float* proj_out_b;
+    const float* spec_wr[NFO_MAX_LAYERS];
+    const float* spec_wi[NFO_MAX_LAYERS];
+    const float* loc_w[NFO_MAX_LAYERS];
+    const float* loc_b[NFO_MAX_LAYERS];
+    nfo_wq q_lift_w, q_lift_b, q_proj_q_w, q_proj_q_b, q_proj_out_w, q_proj_out_b;
+    nfo_wq q_spec_wr[NFO_MAX_LAYERS];
+    nfo_wq q_spec_wi[NFO_MAX_LAYERS];
+    nfo_wq q_loc_w[NFO_MAX_LAYERS];
+    nfo_wq q_loc_b[NFO_MAX_LAYERS];
+    nfo_aq1 a_lift;
+    nfo_aq1 a_locs[NFO_MAX_LAYERS];
+} nfo_fno1d;
+
+/* FNO1d::Forward with the runtime's Create-time weight fake-quant (fno.cpp:293-315)
+ * and, when int8_enabled, EnableInt8Gemm's per-channel weight codes (fno.cpp:360-406)
+ * and the LinearDispatchTryInt8 rule (fno.cpp:125-159).  x (b, n, in_ch) ->
+ * y (b, n, out_ch).  Returns 0 or the StatusCode of a rejected call. */
+int nfo_fno1d_forward(const nfo_fno1d* m, const float* x, int bsz, int n0, float* y) {
+    const int w = m->width, modes = m->modes, L = m->n_layers;
+    const int in_ch = m->in_ch, out_ch = m->out_ch;
+    if (L > NFO_MAX_LAYERS) return 1;
+    if (n0 <= 0 || (n0 & (n0 - 1))) return 1;
+    {   /* per-token tables must cover the (padded) flat index range they are read at */
+        int64_t np = n0;
+        if (m->pad_factor > 1 && n0 % m->pad_factor) np += m->pad_factor - n0 % m->pad_factor;
+        for (int i = 0; i < L; ++i) {
+            const nfo_aq1* a = &m->a_locs[i];
+            if (m->quant_enabled && !a->has_fp8 && a->has_pt &&
+                (a->pt_width > w || np * a->pt_width > a->pt_n))
+                return 1;
+        }
+    }
+
+    float* lift_w = dup_floats(m->lift_w, (int64_t)w * in_ch);
+    float* lift_b = dup_floats(m->lift_b, w);
+    float* pq_w = dup_floats(m->proj_q_w, (int64_t)w * w);
+    float* pq_b = dup_floats(m->proj_q_b, w);
+    float* po_w = dup_floats(m->proj_out_w, (int64_t)out_ch * w);
+    float* po_b = dup_floats(m->proj_out_b, out_ch);
+    float* swr[NFO_MAX_LAYERS];
+    float* swi[NFO_MAX_LAYERS];
+    float* lw[NFO_MAX_LAYERS];
+    float* lb[NFO_MAX_LAYERS];
+    const int64_t nspec = (int64_t)w * w * modes;
+    for (int i = 0; i < L; ++i) {
+        swr[i] = dup_floats(m->spec_wr[i], nspec);
+        swi[i] = dup_floats(m->spec_wi[i], nspec);
+        lw[i] = dup_floats(m->loc_w[i], (int64_t)w * w);
+        lb[i] = dup_floats(m->loc_b[i], w);
+    }
+    if (m->quant_enabled) {
+        dq_weight(lift_w, w, in_ch, 0, 0, 2, &m->q_lift_w);
+        dq_weight(lift_b, w, 0, 0, 0, 1, &m->q_lift_b);
+        dq_weight(pq_w, w, w, 0, 0, 2, &m->q_proj_q_w);
+        dq_weight(pq_b, w, 0, 0, 0, 1, &m->q_proj_q_b);
+        dq_weight(po_w, out_ch, w, 0, 0, 2, &m->q_proj_out_w);
+        dq_weight(po_b, out_ch, 0, 0, 0, 1, &m->q_proj_out_b);
+        for (int i = 0; i < L; ++i) {
+            dq_weight(swr[i], w, w, modes, 0, 3, &m->q_spec_wr[i]);
+            dq_weight(swi[i], w, w, modes, 0, 3, &m->q_spec_wi[i]);
+            dq_weight(lw[i], w, w, 0, 0, 2, &m->q_loc_w[i]);
+            dq_weight(lb[i], w, 0, 0, 0, 1, &m->q_loc_b[i]);
+        }
+    }
+    /* EnableInt8Gemm cache for locs.i (lift/proj caches exist too but Forward never
+     * dispatches them) and the per-layer dispatch decision. */
+    int8_t* lq[NFO_MAX_LAYERS];
+    int32_t* lsum[NFO_MAX_LAYERS];
+    int use_int8[NFO_MAX_LAYERS];
+    for (int i = 0; i < L; ++i) {
+        const nfo_aq1* a_in = (i == 0) ? &m->a_lift : &m->a_locs[i - 1];
+        const nfo_wq* q = &m->q_loc_w[i];
+        lq[i] = NULL;
+        lsum[i] = NULL;
+        use_int8[i] = m->int8_enabled && m->quant_enabled && q->has_pc && q->pc_axis == 0 &&
+                      !a_in->has_pt && !a_in->has_fp8 && a_in->has;
+        if (use_int8[i]) {
+            lq[i] = (int8_t*)malloc((size_t)w * w);
+            lsum[i] = (int32_t*)malloc(sizeof(int32_t) * w);
+            nfo_quantise_weight_2d(lw[i], w, w, q->pc_scales, q->pc_zps, lq[i], lsum[i]);
+        }
+    }
+
+    int64_t n = n0;
+    float* h = (float*)calloc((size_t)bsz * n * w, sizeof(float));
+    nfo_linear(x, lift_w, lift_b, (int)(bsz * n), in_ch, w, h);
+    float* h_perm = (float*)calloc((size_t)bsz * w * n, sizeof(float));
+    for (int64_t bi = 0; bi < bsz; ++bi)
+        for (int wi = 0; wi < w; ++wi)
+            for (int64_t ni = 0; ni < n; ++ni)
+                h_perm[(bi * w + wi) * n + ni] = h[(bi * n + ni) * w + wi];
+    /* fno.cpp:450-466 padding */
+    int64_t pad_len = 0;
+    if (m->pad_factor > 1) {
+        const int64_t r = n % m->pad_factor;
+        pad_len = r == 0 ? 0 : m->pad_factor - r;
+        if (pad_len > 0) {
+            const int64_t np = n + pad_len;
+            float* padded = (float*)calloc((size_t)bsz * w * np, sizeof(float));
+            for (int64_t bi = 0; bi < bsz; ++bi)
+                for (int wi = 0; wi < w; ++wi)
+                    memcpy(padded + (bi * w + wi) * np, h_perm + (bi * w + wi) * n,
+                           sizeof(float) * n);
+            free(h_perm);
+            h_perm = padded;
+            n = np;
+        }
+    }
+    const int64_t numel = (int64_t)bsz * w * n;
+    float* x1 = (float*)calloc((size_t)numel, sizeof(float));
+    float* x2 = (float*)calloc((size_t)numel, sizeof(float));
+    float* pin = (float*)calloc((size_t)numel, sizeof(float));
+    float* pout = (float*)calloc((size_t)numel, sizeof(float));
+    float* add = (float*)calloc((size_t)numel, sizeof(float));
+
+    for (int i = 0; i < L; ++i) {
+        const nfo_aq1* a_in = (i == 0) ? &m->a_lift : &m->a_locs[i - 1];
+        const nfo_aq1* a_out = &m->a_locs[i];
+        /* fno.cpp:488-508 input snap (per-tensor map only) */
+        if (m->quant_enabled && a_in->has) nfo_fake_quant(h_perm, numel, a_in->scale, a_in->zp);
+        nfo_spectral_conv1d(h_perm, bsz, w, (int)n, modes, swr[i], swi[i], x1);
+        for (int64_t bi = 0; bi < bsz; ++bi)
+            for (int64_t ni = 0; ni < n; ++ni)
+                for (int wi = 0; wi < w; ++wi)
+                    pin[(bi * n + ni) * w + wi] = h_perm[(bi * w + wi) * n + ni];
+        if (use_int8[i]) {
+            nfo_linear_forward_batched(lq[i], m->q_loc_w[i].pc_scales, m->q_loc_w[i].pc_zps,
+                                       lsum[i], NULL, w, w, a_in->scale, a_in->zp,
+                                       (int)(bsz * n), pin, pout, NULL, NULL);
+            for (int64_t r = 0; r < bsz * n; ++r)
+                for (int j = 0; j < w; ++j) pout[r * w + j] += lb[i][j];
+        } else {
+            nfo_linear(pin, lw[i], lb[i], (int)(bsz * n), w, w, pout);
+        }
+        for (int64_t bi = 0; bi < bsz; ++bi)
+            for (int wi = 0; wi < w; ++wi)
+                for (int64_t ni = 0; ni < n; ++ni)
+                    x2[(bi * w + wi) * n + ni] = pout[(bi * n + ni) * w + wi];
+        if (m->quant_enabled) {
+            if (a_out->has_fp8) {
+                nfo_fake_quant_fp8_log2(x2, numel, a_out->fp8_scale);
+            } else if (a_out->has_pt) {
+                /* fno.cpp:606-628: the loop walks x2 with a flat (n, w_axis) index
+                 * although x2 is (b, w, n) here, so element k of a sample takes
+                 * scale k: element (channel c, position p) uses scales[c*n + p]. */
+                const int64_t wa = a_out->pt_width;
+                for (int64_t bi = 0; bi < bsz; ++bi)
+                    for (int64_t ni = 0; ni < n; ++ni)
+                        for (int64_t wi = 0; wi < wa; ++wi) {
+                            const int64_t qi = ni * wa + wi;
+                            const int64_t off = bi * n * wa + ni * wa + wi;
+                            x2[off] = fake_quant_pt(x2[off], a_out->pt_scales[qi],
+                                                    (float)a_out->pt_zps[qi]);
+                        }
+            } else if (a_out->has) {
+                nfo_fake_quant(x2, (int64_t)bsz * n * w, a_out->scale, a_out->zp);
+            }
+        }
+        for (int64_t k = 0; k < numel; ++k) add[k] = x1[k] + x2[k];
+        nfo_apply_activation(add, numel, m->relu);
+        memcpy(h_perm, add, sizeof(float) * numel);
+    }
+    if (pad_len > 0) {
+        const int64_t orig = n - pad_len;
+        float* trimmed = (float*)calloc((size_t)bsz * w * orig, sizeof(float));
+        for (int64_t bi = 0; bi < bsz; ++bi)
+            for (int wi = 0; wi < w; ++wi)
+                memcpy(trimmed + (bi * w + wi) * orig, h_perm + (bi * w + wi) * n,
+                       sizeof(float) * orig);
+        free(h_perm);
+        h_perm = trimmed;
+        n = orig;
+    }
+    float* h_back = (float*)calloc((size_t)bsz * n * w, sizeof(float));
+    for (int64_t bi = 0; bi < bsz; ++bi)
+        for (int64_t ni = 0; ni < n; ++ni)
+            for (int wi = 0; wi < w; ++wi)
+                h_back[(bi * n + ni) * w + wi] = h_perm[(bi * w + wi) * n + ni];
+    float* q = (float*)calloc((size_t)bsz * n * w, sizeof(float));
+    nfo_linear(h_back, pq_w, pq_b, (int)(bsz * n), w, w, q);
+    nfo_apply_activation(q, (int64_t)bsz * n * w, m->relu);
+    nfo_linear(q, po_w, po_b, (int)(bsz * n), w, out_ch, y);
+
+    free(q);
+    free(h_back);
+    free(add);
+    free(pout);
+    free(pin);
+    free(x2);
+    free(x1);
+    free(h_perm);
+    free(h);
+    for (int i = 0; i < L; ++i) {
+        free(lq[i]);
+        free(lsum[i]);
         free(swr[i]);
         free(swi[i]);
         free(lw[i]);

@@ -72,3 +72,21 @@ def test_fno2d_without_nirq_is_not_int8(tmp_path):
     assert not rt.is_int8_gemm_enabled()
     with pytest.raises(RuntimeError, match="INT8"):
         rt.run(np.zeros((1, 32, 32, 3), np.float32), np.zeros((1, 32, 32, 1), np.float32))
+
+
+@pytest.mark.gpu
+def test_fno2d_growing_batch_reuses_handle(tmp_path):
+    """Host-buffer Run with a growing batch re-allocates only the staging buffers; the
+    transform tables built for the grid stay valid."""
+    from neuroflow_b200.runtime import InferenceRuntime
+    m, path = _model(tmp_path, L=2, H=32, W=128)
+    rt = InferenceRuntime(path)
+    rt.enable_int8_gemm()
+    o = Oracle()
+    step = m.qparams["proj_out.output"].scale
+    for B in (1, 3, 2, 4):
+        x = synth.fno2d_inputs(np.random.default_rng(20 + B), B, 32, 128)
+        got = np.zeros((B, 32, 128, 1), np.float32)
+        rt.run(x, got)
+        st = _stats(got, o.fno2d_forward(m, x, mode=1), step)
+        assert st["rel_l2"] < 2e-2 and st["frac_diff"] < 0.05, (B, st)
