@@ -13,6 +13,13 @@ What it writes (small files, committed):
   fno2d_q.npz           input x, the reference C++ runtime's output y (fake-quant FP32
                         FNO2d, oracle/_ref), and the reference Python qparams
   fno2d_plain.nneuroir  the same model without NIRQ, with its runtime output
+  fno1d_pt.nneuroir     a tiny FNO1d (width 16, 6 modes, 2 layers, n = 64) calibrated with
+                        `quantise_model(per_channel_weights=True,
+                        per_token_activations=True)` (NIRQ kind 2) and exported by
+                        `export_all`
+  fno1d_pc.nneuroir     the same network calibrated with per-tensor activations
+  fno1d.npz             input x and the reference runtime's outputs for both files, with
+                        and without EnableInt8Gemm
   int8_gemm.npz         LinearForwardBatched vectors (reference C++): W codes, scales,
                         zero points, sum_w, A, C for K = N = 64, plus QuantiseActivation
   fft.npz               Rfft2/Irfft2 of a 16x32 field (reference C++)
@@ -39,6 +46,7 @@ sys.path.insert(0, ROOT)
 import torch  # noqa: E402
 
 from neuroflow.ir.export import export_all, export_to_binary, export_to_neuroir  # noqa: E402
+from neuroflow.nn.fno import FNO1d, FNO1dConfig  # noqa: E402
 from neuroflow.nn.fno2d import FNO2d, FNO2dConfig  # noqa: E402
 from neuroflow.quant import (compute_per_channel_qparams, compute_tensor_qparams,  # noqa: E402
                              quant_to_ir, quantise_model)
@@ -73,6 +81,26 @@ def main():
                         act_keys=np.array(sorted(act)),
                         act_scale=np.array([act[k][0] for k in sorted(act)], np.float32),
                         act_zp=np.array([act[k][1] for k in sorted(act)], np.int32))
+
+    # --- FNO1d, per-token and per-tensor activations ------------------------------
+    torch.manual_seed(1)
+    cfg1 = FNO1dConfig(in_channels=2, out_channels=1, width=16, modes=6, n_layers=2,
+                       activation="gelu", pad_factor=1)
+    m1 = FNO1d(cfg1).eval()
+    calib1 = torch.randn(4, 64, 2)
+    x1 = rng.standard_normal((3, 64, 2)).astype(np.float32)
+    outs = {"x": x1}
+    for tag, per_token in (("pt", True), ("pc", False)):
+        qm1 = quantise_model(m1, [calib1], per_channel_weights=True,
+                             per_token_activations=per_token)
+        with tempfile.TemporaryDirectory() as d:
+            _, p1 = export_all(m1, d, basename=f"fno1d_{tag}", quant=quant_to_ir(qm1))
+            blob1 = open(p1, "rb").read()
+        path1 = os.path.join(HERE, f"fno1d_{tag}.nneuroir")
+        open(path1, "wb").write(blob1)
+        outs[f"y_{tag}"] = ref.run(path1, x1, 1)
+        outs[f"y_{tag}_int8"] = ref.run(path1, x1, 1, enable_int8=True)
+    np.savez_compressed(os.path.join(HERE, "fno1d.npz"), **outs)
 
     # --- LinearForwardBatched ------------------------------------------------------
     K = N = 64

@@ -139,3 +139,19 @@ def test_fno1d_growing_batch_reuses_handle(tmp_path):
         y = np.zeros((B, 64, 1), np.float32)
         rt.run(x, y)
         assert np.array_equal(_bits(y), _bits(o.fno1d_forward(m, x, int8=True))), B
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tag", ["pt", "pc"])
+def test_fno1d_reference_exported_models(tag):
+    """Models calibrated and exported by the reference's Python package, against the
+    reference C++ runtime's own outputs (tests/golden, made by make_golden.py)."""
+    gold = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    d = np.load(os.path.join(gold, "fno1d.npz"))
+    path = os.path.join(gold, f"fno1d_{tag}.nneuroir")
+    for int8 in (False, True):
+        want = d[f"y_{tag}_int8" if int8 else f"y_{tag}"]
+        got = _run(path, d["x"], 1, int8)
+        diff = np.abs(got - want)
+        tol = 1e-5 * np.abs(want) + 1e-6 * np.abs(want).max()
+        assert np.mean(diff > tol) <= (0.02 if tag == "pt" else 0.0), (int8, float(diff.max()))

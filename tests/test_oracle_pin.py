@@ -2,9 +2,9 @@
 
 1. Against the committed golden fixtures (tests/golden/, made by make_golden.py from the
    reference's own Python exporter/quantiser and its C++ runtime): bit-exact.
-2. Against the reference sources compiled in place (oracle/_ref) on fresh random
-   inputs, when that library is present (it is built by __graft_entry__.build() where
-   the reference tree exists): bit-exact.
+2. Against the reference sources compiled in place (oracle/_ref, with the reference
+   build's own flags) on fresh random inputs, when that library is present (it is
+   built by __graft_entry__.build() where the reference tree exists): bit-exact.
 """
 import os
 
@@ -42,6 +42,21 @@ def test_golden_fno2d_plain_network():
     assert not m.quant_enabled
     y = Oracle().fno2d_forward(m, d["x"], mode=0)
     assert np.array_equal(_bits(y), _bits(d["y_plain"]))
+
+
+@pytest.mark.parametrize("tag", ["pt", "pc"])
+def test_golden_fno1d_networks(tag):
+    """FNO1d models calibrated and exported by the reference's own Python package
+    (per-token activations "pt", per-tensor "pc"), run by the reference runtime with
+    and without EnableInt8Gemm: the restatement reproduces every output bit."""
+    d = _g("fno1d.npz")
+    m = ir.read(os.path.join(GOLD, f"fno1d_{tag}.nneuroir"))
+    assert m.op == "FNO1d" and m.quant_enabled
+    kinds = {type(m.qparams[k]).__name__ for k in m.qparams if k.endswith(".output")}
+    assert kinds == ({"PerToken"} if tag == "pt" else {"PerTensor"})
+    o = Oracle()
+    assert np.array_equal(_bits(o.fno1d_forward(m, d["x"])), _bits(d[f"y_{tag}"]))
+    assert np.array_equal(_bits(o.fno1d_forward(m, d["x"], int8=True)), _bits(d[f"y_{tag}_int8"]))
 
 
 def test_golden_linear_forward_batched_and_quantiser():
@@ -150,6 +165,35 @@ def test_ref_spectral_conv_linear_gelu_bitexact():
 
 
 @needs_ref
+def test_ref_linear_every_length_bitexact():
+    """The vector-block / fused-tail split of the reference build's Linear, for every
+    dot-product length that occurs (in_ch, width, tails)."""
+    o, r = Oracle(), Reference()
+    rng = np.random.default_rng(5)
+    for K in list(range(1, 41)) + [48, 63, 64, 100, 128, 256]:
+        x = rng.standard_normal((64, K)).astype(np.float32)
+        W = rng.standard_normal((5, K)).astype(np.float32)
+        b = rng.standard_normal(5).astype(np.float32)
+        assert np.array_equal(_bits(o.linear(x, W, b)), _bits(r.linear(x, W, b))), K
+
+
+@needs_ref
+@pytest.mark.parametrize("variant", ["plain", "per_token", "per_tensor", "padded"])
+def test_ref_fno1d_network_bitexact(tmp_path, variant):
+    kw = {"plain": dict(quantised=False), "per_token": dict(per_token=True),
+          "per_tensor": dict(per_token=False), "padded": dict(per_token=True, pad_factor=32)}[variant]
+    n = 16 if variant == "padded" else 64
+    m = synth.fno1d_model(7, in_ch=5, width=20, modes=6, L=3, n=n, n_calib=4, **kw)
+    p = str(tmp_path / "m.nneuroir")
+    ir.write(p, m)
+    x = synth.fno1d_inputs(np.random.default_rng(4), 3, n, in_ch=5)
+    r, o = Reference(), Oracle()
+    for int8 in (False, True):
+        want = r.run(p, x, 1, enable_int8=int8)
+        assert np.array_equal(_bits(o.fno1d_forward(m, x, int8=int8)), _bits(want)), int8
+
+
+@needs_ref
 def test_ref_linear_forward_batched_bitexact():
     o, r = Oracle(), Reference()
     for K, N in [(32, 32), (64, 64), (128, 64), (256, 256)]:
@@ -167,11 +211,11 @@ def test_ref_linear_forward_batched_bitexact():
 @needs_ref
 @pytest.mark.parametrize("per_channel", [True, False])
 def test_ref_fno2d_network_bitexact(tmp_path, per_channel):
-    m = synth.fno2d_model(9, width=16, mh=5, mw=4, L=3, H=16, W=32, n_calib=2,
+    m = synth.fno2d_model(9, in_ch=5, width=20, mh=5, mw=4, L=3, H=16, W=32, n_calib=2,
                           per_channel=per_channel)
     p = str(tmp_path / "m.nneuroir")
     ir.write(p, m)
-    x = synth.fno2d_inputs(np.random.default_rng(3), 2, 16, 32)
+    x = synth.fno2d_inputs(np.random.default_rng(3), 2, 16, 32, in_ch=5)
     want = Reference().run(p, x, 1)
     got = Oracle().fno2d_forward(m, x, mode=0)
     assert np.array_equal(_bits(got), _bits(want))
