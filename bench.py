@@ -328,10 +328,11 @@ def main():
                     help="samples per GPU (default: the configs[2] batch of 256; smaller "
                          "values only for profiling captures)")
     args = ap.parse_args()
-    ws, rank, local = dist_setup(args.gpus)
 
     if args.impl == "reference":
-        if rank != 0:
+        # host-only arm: no process group; under torchrun rank 0 alone runs and prints
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        if int(os.environ.get("RANK", "0")) != 0:
             return
         path = model_path(0)
         n = os.cpu_count() or 1
@@ -359,6 +360,7 @@ def main():
         print(json.dumps(line), flush=True)
         return
 
+    ws, rank, local = dist_setup(args.gpus)
     result, rt, x_host, path = run_nfx(args, ws, rank, local)
     if rank == 0:
         if ws == 1 and not args.no_gemm:

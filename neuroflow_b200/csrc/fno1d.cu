@@ -9,7 +9,8 @@
 //   fft1d_fwd   per (b, c) row: the reference radix-2 rFFT (fft.cpp:73-84) of the
 //               layer input, bit-identical, truncated to `modes` bins -> Xs (b, c, m)
 //   [gemm_i8]   INT8 path only: tcgen05 LinearForwardBatched of the input codes
-//               (fno.cpp:125-159) -> x2raw (b*N, C)
+//               (fno.cpp:125-159) -> x2raw (b*N, C); widths the GEMM does not tile
+//               (not 32/64/128/256) compute the same integers inside layer1d
 //   layer1d     per (b, group of G output channels): the spectral contraction
 //               (fno.cpp:181-196), the inverse transform (fft.cpp:86-99) of each
 //               output row, the local Linear (FP32 dot product, or x2raw + bias), the
@@ -34,20 +35,6 @@ namespace {
 
 __device__ __forceinline__ float act_f(float z, int act) {
     return act == 1 ? relu_ref(z) : gelu_tanh(z);
-}
-
-// fno.cpp:585-603 FP8 branch: log2 snap of v / scale (the std::ldexp exponent is the
-// float truncated to int, as the reference computes it).
-__device__ __forceinline__ float fp8_log2_snap(float v, float scale) {
-    if (!(scale > 0.0f)) return v;
-    const float u = __fdiv_rn(v, scale);
-    const float a = fabsf(u);
-    const float sign = u < 0.0f ? -1.0f : 1.0f;
-    const float qv = (a < 0.015625f)
-                         ? a
-                         : ldexpf(1.0f, static_cast<int>(__fdiv_rn(
-                                            roundf(__fmul_rn(log2f(a), 8.0f)), 8.0f)));
-    return __fmul_rn(__fmul_rn(sign, fminf(qv, 448.0f)), scale);
 }
 
 // value of activation element idx: a code snapped back, (q - zp) * s, or the fp32 value
@@ -189,10 +176,34 @@ __global__ void __launch_bounds__(256) layer1d_kernel(Layer1dArgs a) {
     for (int p = threadIdx.x; p < N; p += blockDim.x) {
         const int64_t row = static_cast<int64_t>(b) * N + p;
         float x2[8];
-        if (L.use_int8) {
+        if (L.use_int8 && a.x2raw) {
 #pragma unroll
             for (int r = 0; r < 8; ++r)
                 if (r < G) x2[r] = __fadd_rn(a.x2raw[row * C + o0 + r], __ldg(L.loc_b + o0 + r));
+        } else if (L.use_int8) {
+            // widths the tcgen05 GEMM does not tile: the same LinearForwardBatched
+            // arithmetic on CUDA cores (int32 dot products, the reference epilogue)
+            const int8_t* arow = static_cast<const int8_t*>(a.h_in) + row * C;
+            int raw[8];
+            int sum_a = 0;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) raw[r] = 0;
+            for (int k = 0; k < C; ++k) {
+                const int av = arow[k];
+                sum_a += av;
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+                    if (r < G) raw[r] += av * static_cast<int>(__ldg(L.Wq + static_cast<int64_t>(o0 + r) * C + k));
+            }
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                if (r >= G) break;
+                const int o = o0 + r;
+                const int zw = __ldg(L.zp_w + o);
+                const float sWsA = __fmul_rn(__ldg(L.scale_w + o), L.in_s);
+                const float y = dequant_ref(raw[r], zw, C * L.in_zp - 2 * sum_a, L.in_zp * __ldg(L.sum_w + o), sWsA);
+                x2[r] = __fadd_rn(y, __ldg(L.loc_b + o));
+            }
         } else {
 #pragma unroll
             for (int r = 0; r < 8; ++r)
@@ -325,7 +336,7 @@ cudaError_t fno1d_run(const Fno1dPlan& pl, cudaStream_t st) {
             hin, L.in_codes, L.in_s, L.in_zp, N, log2N, C, pl.modes, pl.tw_fwd, pl.Xs);
         if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
-        if (L.use_int8) {
+        if (L.use_int8 && gemm_i8_supported(C, C)) {
             GemmArgs g{};
             g.A = static_cast<const int8_t*>(hin);
             g.scale_a_t = L.in_s;
@@ -348,7 +359,7 @@ cudaError_t fno1d_run(const Fno1dPlan& pl, cudaStream_t st) {
         a.h_in = hin;
         a.h_out = hout;
         a.Xs = pl.Xs;
-        a.x2raw = pl.x2raw;
+        a.x2raw = gemm_i8_supported(C, C) ? pl.x2raw : nullptr;
         a.tw_inv = pl.tw_inv;
         a.L = L;
         a.N = N;

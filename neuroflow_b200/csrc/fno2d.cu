@@ -37,27 +37,6 @@ constexpr int pow2ceil(int v) {
     return p;
 }
 
-// ---------------------------------------------------------------------------
-// fake-quant variants selected at run time (fno.cpp:810-844)
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ float apply_fq(float v, const FqParam& q) {
-    if (q.kind == 1) return fake_quant(v, q.scale, static_cast<float>(q.zp));
-    if (q.kind == 2) {
-        // FP8 log2 snap of the reference FNO2d (fno.cpp:813-828)
-        if (!(q.scale > 0.0f)) return v;
-        const float u = __fdiv_rn(v, q.scale);
-        const float a = fabsf(u);
-        const float sign = u < 0.0f ? -1.0f : 1.0f;
-        const float qv = (a < 0.015625f)
-                             ? a
-                             : ldexpf(1.0f, static_cast<int>(__fdiv_rn(
-                                                roundf(__fmul_rn(log2f(a), 8.0f)), 8.0f)));
-        const float c = fminf(qv, 448.0f);
-        return __fmul_rn(__fmul_rn(sign, c), q.scale);
-    }
-    return v;
-}
-
 __device__ __forceinline__ float activation(float z, int act) {
     return act == 1 ? relu_ref(z) : gelu_tanh(z);
 }

@@ -9,15 +9,6 @@
 
 namespace nfx {
 
-// Fake-quant applied at an ".output" boundary: kind 0 none, 1 INT8 per-tensor,
-// 2 the reference FNO2d FP8 log2 snap (fno.cpp:813-828).
-struct FqParam {
-    int kind;
-    float scale;
-    int zp;
-    float inv_scale;  // 1/scale (IEEE), for the division-free fast path
-};
-
 // Arguments of one tcgen05 layer launch (local 1x1 layer or the projection).
 struct LayerArgs {
     // GEMM operands: weight codes (C, C), per-channel params
@@ -100,5 +91,46 @@ struct Fno2dPlan {
 
 bool fno2d_supported(int C, int MH, int MW);
 cudaError_t fno2d_run(const Fno2dPlan& plan, cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// FP32 fake-quant executor (fno2d_fp32.cu): the reference FNO2d::Forward
+// (fno.cpp:777-995) as the runtime runs it without EnableInt8Gemm.  Activations are
+// fp32 channel-first (b, c, h, w) like the reference's h_perm.
+// ---------------------------------------------------------------------------
+struct Fno2dF32Layer {
+    const float* wr;      // (C, C, MH, MW) spectral weights (fake-quantised at load)
+    const float* wi;
+    const float* loc_w;   // (C, C)
+    const float* loc_b;
+    FqParam fq;           // locs.i.output
+};
+
+struct Fno2dF32Plan {
+    int B, H, W, Hp, Wp, C, MH, MW, L, in_ch, out_ch, act;
+    const float* x;       // (B, H, W, in_ch)
+    float* y;             // (B, H, W, out_ch)
+    const float* lift_w;
+    const float* lift_b;
+    FqParam fq_lift;
+    Fno2dF32Layer layer[kFno2dMaxLayers];
+    const float* pq_w;
+    const float* pq_b;
+    FqParam fq_pq;
+    const float* po_w;
+    const float* po_b;
+    FqParam fq_po;
+    const float2* twf_w;  // recurrence twiddles (nfx_lut.h) for Wp and Hp
+    const float2* twi_w;
+    const float2* twf_h;
+    const float2* twi_h;
+    float* h[2];          // (B, C, Hp, Wp)
+    float2* Xs;           // (B, C, MH, MW) truncated spectra
+    float2* colinv;       // (B, C, Hp, MW) column-inverse transforms
+    KernelTimer* timer;
+};
+
+// Geometry limits of the FP32 executor; returns nullptr or the reason it is unsupported.
+const char* fno2d_f32_unsupported(int C, int MH, int MW, int Hp, int Wp, int out_ch);
+cudaError_t fno2d_f32_run(const Fno2dF32Plan& plan, cudaStream_t stream);
 
 }  // namespace nfx

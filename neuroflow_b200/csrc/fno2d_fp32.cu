@@ -1,0 +1,360 @@
+// fno2d_fp32.cu -- FNO2d FP32 fake-quant executor (sm_100a): the reference
+// FNO2d::Forward (cpp/src/fno.cpp:777-995) as InferenceRuntime::Run executes it when
+// EnableInt8Gemm is not in effect, with the reference's rounding.
+//
+// Activations are fp32, channel-first (b, c, h, w), as the reference's h_perm: rows
+// of a channel are contiguous for the transforms, and a warp of consecutive points
+// reads one channel coalesced for the local layer.  One layer is
+//
+//   fwd2d    per (b, c): the reference Rfft2 (fft.cpp:101-124) restricted to what the
+//            truncation keeps -- every row transform (all of them feed the kept
+//            columns), then the column transforms of the MW kept columns -> Xs
+//   mix2d    per (b, group of output channels): the per-mode contraction
+//            (fno.cpp:740-764), then the column pass of Irfft2 (fft.cpp:126-149) for
+//            the MW nonzero columns -> colinv (b, o, h, kw)
+//   layer2d  per (b, row): the row pass of Irfft2 for every output channel (x1), the
+//            local Linear of the row's points, locs.i.output fake-quant, x1 + x2 and
+//            the activation -> next activation
+//
+// Every product, sum and transform follows the reference's expression shapes
+// (fft_exact.cuh, linear_step); the only approximate operation is CUDA's tanhf inside
+// GELU.  Columns of Irfft2 that the truncation leaves all-zero are taken as +0.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "fft_exact.cuh"
+#include "fno2d.h"
+#include "nfx_internal.h"
+#include "numerics.cuh"
+
+namespace nfx {
+namespace {
+
+constexpr int kChunk = 16;  // output channels per inverse-row chunk in layer2d
+constexpr int kMaxWp = 512;
+
+__device__ __forceinline__ float act_f(float z, int act) {
+    return act == 1 ? relu_ref(z) : gelu_tanh(z);
+}
+
+int ilog2(int v) {
+    int l = 0;
+    while ((1 << l) < v) ++l;
+    return l;
+}
+
+// lift (fno.cpp:848-865): Linear, lift.output fake-quant, permute to channel-first,
+// zero padding
+__global__ void __launch_bounds__(256) lift2d_f32_kernel(Fno2dF32Plan p) {
+    const int64_t total = static_cast<int64_t>(p.B) * p.C * p.Hp * p.Wp;
+    const int nu = linear_unfused_len(p.in_ch);
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int ww = static_cast<int>(t % p.Wp);
+        int64_t r = t / p.Wp;
+        const int hh = static_cast<int>(r % p.Hp);
+        r /= p.Hp;
+        const int c = static_cast<int>(r % p.C);
+        const int64_t b = r / p.C;
+        float v = 0.0f;
+        if (hh < p.H && ww < p.W) {
+            const float* xr = p.x + ((b * p.H + hh) * p.W + ww) * p.in_ch;
+            v = __ldg(p.lift_b + c);
+            for (int k = 0; k < p.in_ch; ++k)
+                v = linear_step(v, __ldg(xr + k), __ldg(p.lift_w + c * p.in_ch + k), k >= nu);
+            v = apply_fq(v, p.fq_lift);
+        }
+        p.h[0][t] = v;
+    }
+}
+
+// forward truncated Rfft2 of one (b, c) plane; 256 threads; shared memory
+// rowbuf [8][Wp] float2, colbuf [MW][Hp] float2 (columns stored bit-reversed)
+__global__ void __launch_bounds__(256) fwd2d_kernel(const float* __restrict__ hin, int Hp, int Wp,
+                                                    int C, int MH, int MW,
+                                                    const float2* __restrict__ twf_w,
+                                                    const float2* __restrict__ twf_h,
+                                                    float2* __restrict__ Xs) {
+    extern __shared__ float2 sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x, b = blockIdx.y;
+    const int lgW = 31 - __clz(Wp), lgH = 31 - __clz(Hp);
+    float2* row = sm + warp * Wp;
+    float2* col = sm + 8 * Wp;
+    const float* plane = hin + (static_cast<int64_t>(b) * C + c) * Hp * Wp;
+    for (int r = warp; r < Hp; r += 8) {
+        for (int j = lane; j < Wp; j += 32) row[bit_reverse(j, lgW)] = make_float2(plane[static_cast<int64_t>(r) * Wp + j], 0.0f);
+        __syncwarp();
+        warp_fft_row<false>(row, Wp, twf_w, lane);
+        const int rr = bit_reverse(r, lgH);
+        for (int kw = lane; kw < MW; kw += 32) col[kw * Hp + rr] = row[kw];
+        __syncwarp();
+    }
+    __syncthreads();
+    for (int kw = warp; kw < MW; kw += 8) {
+        warp_fft_row<false>(col + kw * Hp, Hp, twf_h, lane);
+        for (int kh = lane; kh < MH; kh += 32)
+            Xs[((static_cast<int64_t>(b) * C + c) * MH + kh) * MW + kw] = col[kw * Hp + kh];
+    }
+}
+
+// contraction + column inverse; grid (C / G, B), 256 threads; shared memory
+// sY [G][MH*MW] float2, colb [8][Hp] float2
+__global__ void __launch_bounds__(256) mix2d_kernel(const float2* __restrict__ Xs,
+                                                    const float* __restrict__ wr,
+                                                    const float* __restrict__ wi, int Hp, int C,
+                                                    int MH, int MW, int G,
+                                                    const float2* __restrict__ twi_h,
+                                                    float2* __restrict__ colinv) {
+    extern __shared__ float2 sm[];
+    const int M = MH * MW;
+    float2* sY = sm;
+    float2* colb = sm + G * M;
+    const int b = blockIdx.y, o0 = blockIdx.x * G;
+    for (int t = threadIdx.x; t < G * M; t += blockDim.x) {
+        const int r = t / M, md = t - (t / M) * M;
+        const int o = o0 + r;
+        float sr = 0.0f, si = 0.0f;
+        const float2* xb = Xs + static_cast<int64_t>(b) * C * M + md;
+        for (int c = 0; c < C; ++c) {
+            const float2 hv = xb[static_cast<int64_t>(c) * M];
+            const int64_t k = (static_cast<int64_t>(c) * C + o) * M + md;
+            const float a = __ldg(wr + k), bi = __ldg(wi + k);
+            sr = __fadd_rn(sr, __fmaf_rn(hv.x, a, -__fmul_rn(hv.y, bi)));
+            si = __fadd_rn(si, __fmaf_rn(hv.x, bi, __fmul_rn(hv.y, a)));
+        }
+        sY[t] = make_float2(sr, si);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int lgH = 31 - __clz(Hp);
+    const float invH = __fdiv_rn(1.0f, static_cast<float>(Hp));
+    float2* cb = colb + warp * Hp;
+    for (int q = warp; q < G * MW; q += 8) {
+        const int r = q / MW, kw = q - (q / MW) * MW;
+        for (int i = lane; i < Hp; i += 32)
+            cb[bit_reverse(i, lgH)] = i < MH ? sY[r * M + i * MW + kw] : make_float2(0.0f, 0.0f);
+        __syncwarp();
+        warp_fft_row<true>(cb, Hp, twi_h, lane);
+        float2* dst = colinv + ((static_cast<int64_t>(b) * C + o0 + r) * Hp) * MW + kw;
+        for (int i = lane; i < Hp; i += 32) {
+            const float2 v = cb[i];
+            dst[static_cast<int64_t>(i) * MW] = make_float2(__fmul_rn(v.x, invH), __fmul_rn(v.y, invH));
+        }
+        __syncwarp();
+    }
+}
+
+// row inverse + local layer + epilogue for one row of one sample; grid (Hp, B), 256
+// threads; shared memory sH [C][Wp] float, sX1 [kChunk][Wp] float2
+struct Layer2dArgs {
+    const float* hin;
+    float* hout;
+    const float2* colinv;
+    const float2* twi_w;
+    const float* loc_w;
+    const float* loc_b;
+    FqParam fq;
+    int Hp, Wp, C, MW, act;
+};
+
+__global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
+    extern __shared__ float2 sm[];
+    const int Wp = a.Wp, C = a.C, Hp = a.Hp;
+    float* sH = reinterpret_cast<float*>(sm);
+    float2* sX1 = sm + (static_cast<size_t>(C) * Wp + 1) / 2;
+    const int hh = blockIdx.x, b = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int lgW = 31 - __clz(Wp);
+    const int half = Wp / 2 + 1;
+    for (int t = threadIdx.x; t < C * Wp; t += blockDim.x) {
+        const int k = t / Wp, w = t - (t / Wp) * Wp;
+        sH[t] = a.hin[((static_cast<int64_t>(b) * C + k) * Hp + hh) * Wp + w];
+    }
+    const float invW = __fdiv_rn(1.0f, static_cast<float>(Wp));
+    const int nu = linear_unfused_len(C);
+    const int nj = Wp / 32 > 0 ? Wp / 32 : 1;
+    for (int o0 = 0; o0 < C; o0 += kChunk) {
+        // row pass of Irfft2 (fft.cpp:86-99) for kChunk output channels
+        for (int r = warp; r < kChunk && o0 + r < C; r += 8) {
+            float2* row = sX1 + static_cast<size_t>(r) * Wp;
+            const float2* ci = a.colinv + ((static_cast<int64_t>(b) * C + o0 + r) * Hp + hh) * a.MW;
+            for (int j = lane; j < Wp; j += 32) {
+                float2 v;
+                if (j < half) {
+                    v = j < a.MW ? ci[j] : make_float2(0.0f, 0.0f);
+                } else {
+                    const int i = Wp - j;
+                    const float2 u = i < a.MW ? ci[i] : make_float2(0.0f, 0.0f);
+                    v = make_float2(u.x, -u.y);
+                }
+                row[bit_reverse(j, lgW)] = v;
+            }
+            __syncwarp();
+            warp_fft_row<true>(row, Wp, a.twi_w, lane);
+        }
+        __syncthreads();
+        // local Linear of the row's points for this chunk: warp -> 2 output channels,
+        // lane -> points lane + 32 j
+        for (int rr = 0; rr < 2; ++rr) {
+            const int r = warp * 2 + rr;
+            const int o = o0 + r;
+            if (o >= C) break;
+            float acc[kMaxWp / 32];
+            const float bias = __ldg(a.loc_b + o);
+#pragma unroll
+            for (int j = 0; j < kMaxWp / 32; ++j) acc[j] = bias;
+            const float* wrow = a.loc_w + static_cast<int64_t>(o) * C;
+            for (int k = 0; k < C; ++k) {
+                const float wv = __ldg(wrow + k);
+                const float* hk = sH + static_cast<size_t>(k) * Wp;
+#pragma unroll
+                for (int j = 0; j < kMaxWp / 32; ++j)
+                    if (j < nj && lane + 32 * j < Wp) acc[j] = linear_step(acc[j], hk[lane + 32 * j], wv, k >= nu);
+            }
+            float* dst = a.hout + ((static_cast<int64_t>(b) * C + o) * Hp + hh) * Wp;
+#pragma unroll
+            for (int j = 0; j < kMaxWp / 32; ++j) {
+                const int w = lane + 32 * j;
+                if (j < nj && w < Wp) {
+                    const float x2 = apply_fq(acc[j], a.fq);
+                    const float x1 = __fmul_rn(sX1[static_cast<size_t>(r) * Wp + w].x, invW);
+                    dst[w] = act_f(__fadd_rn(x1, x2), a.act);
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// projection (fno.cpp:966-993): one unpadded point per thread, its channel column
+// staged in shared memory [threads][C + 1]
+__global__ void __launch_bounds__(128) proj2d_f32_kernel(Fno2dF32Plan p, const float* __restrict__ h) {
+    extern __shared__ float sh[];
+    float* mine = sh + static_cast<size_t>(threadIdx.x) * (p.C + 1);
+    const int64_t total = static_cast<int64_t>(p.B) * p.H * p.W;
+    const int C = p.C;
+    const int nu = linear_unfused_len(C);
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int ww = static_cast<int>(t % p.W);
+        const int64_t r = t / p.W;
+        const int hh = static_cast<int>(r % p.H);
+        const int64_t b = r / p.H;
+        for (int k = 0; k < C; ++k) mine[k] = h[((b * C + k) * p.Hp + hh) * p.Wp + ww];
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = j < p.out_ch ? __ldg(p.po_b + j) : 0.0f;
+        for (int c = 0; c < C; ++c) {
+            float q = __ldg(p.pq_b + c);
+            const float* wr = p.pq_w + static_cast<int64_t>(c) * C;
+            for (int k = 0; k < C; ++k) q = linear_step(q, mine[k], __ldg(wr + k), k >= nu);
+            q = act_f(apply_fq(q, p.fq_pq), p.act);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (j < p.out_ch)
+                    acc[j] = linear_step(acc[j], q, __ldg(p.po_w + static_cast<int64_t>(j) * C + c), c >= nu);
+        }
+        float* yr = p.y + t * p.out_ch;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (j < p.out_ch) yr[j] = apply_fq(acc[j], p.fq_po);
+    }
+}
+
+size_t fwd_smem(int Hp, int Wp, int MW) {
+    return (8 * static_cast<size_t>(Wp) + static_cast<size_t>(MW) * Hp) * sizeof(float2);
+}
+size_t layer_smem(int C, int Wp) {
+    return ((static_cast<size_t>(C) * Wp + 1) / 2 + static_cast<size_t>(kChunk) * Wp) * sizeof(float2);
+}
+int mix_group(int C) {
+    for (int G = 8; G > 1; G >>= 1)
+        if (C % G == 0) return G;
+    return 1;
+}
+
+}  // namespace
+
+const char* fno2d_f32_unsupported(int C, int MH, int MW, int Hp, int Wp, int out_ch) {
+    if (C < 1 || C > 256) return "FNO2d GPU executor: width must be in [1, 256]";
+    if (out_ch < 1 || out_ch > 16) return "FNO2d GPU executor: out_channels must be in [1, 16]";
+    if (Wp > kMaxWp || Hp > 4096) return "FNO2d GPU executor: padded W <= 512 and H <= 4096";
+    if (fwd_smem(Hp, Wp, MW) > 200 * 1024 || layer_smem(C, Wp) > 200 * 1024)
+        return "FNO2d GPU executor: grid too large for the shared-memory transforms";
+    if (static_cast<size_t>(mix_group(C)) * MH * MW * sizeof(float2) + 8 * static_cast<size_t>(Hp) * sizeof(float2) >
+        200 * 1024)
+        return "FNO2d GPU executor: too many modes";
+    return nullptr;
+}
+
+cudaError_t fno2d_f32_run(const Fno2dF32Plan& p, cudaStream_t st) {
+    if (p.B == 0) return cudaSuccess;
+    const int sms = device_sm_count();
+    cudaError_t e;
+    {
+        const int64_t total = static_cast<int64_t>(p.B) * p.C * p.Hp * p.Wp;
+        const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, sms * 32));
+        if (p.timer) p.timer->begin("fno2d_f32_lift", st);
+        lift2d_f32_kernel<<<grid, 256, 0, st>>>(p);
+        if (p.timer) p.timer->end(st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    const size_t sf = fwd_smem(p.Hp, p.Wp, p.MW);
+    const int G = mix_group(p.C);
+    const size_t sx = (static_cast<size_t>(G) * p.MH * p.MW + 8 * static_cast<size_t>(p.Hp)) * sizeof(float2);
+    const size_t sl = layer_smem(p.C, p.Wp);
+    if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(fwd2d_kernel), static_cast<int>(sf))) != cudaSuccess ||
+        (e = set_max_dynamic_smem(reinterpret_cast<const void*>(mix2d_kernel), static_cast<int>(sx))) != cudaSuccess ||
+        (e = set_max_dynamic_smem(reinterpret_cast<const void*>(layer2d_kernel), static_cast<int>(sl))) != cudaSuccess)
+        return e;
+    for (int i = 0; i < p.L; ++i) {
+        const float* hin = p.h[i & 1];
+        float* hout = p.h[(i + 1) & 1];
+        const Fno2dF32Layer& L = p.layer[i];
+        if (p.timer) p.timer->begin("fno2d_f32_fwd", st);
+        fwd2d_kernel<<<dim3(p.C, p.B), 256, sf, st>>>(hin, p.Hp, p.Wp, p.C, p.MH, p.MW, p.twf_w, p.twf_h, p.Xs);
+        if (p.timer) p.timer->end(st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if (p.timer) p.timer->begin("fno2d_f32_mix", st);
+        mix2d_kernel<<<dim3(p.C / G, p.B), 256, sx, st>>>(p.Xs, L.wr, L.wi, p.Hp, p.C, p.MH, p.MW, G, p.twi_h,
+                                                         p.colinv);
+        if (p.timer) p.timer->end(st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        Layer2dArgs a;
+        a.hin = hin;
+        a.hout = hout;
+        a.colinv = p.colinv;
+        a.twi_w = p.twi_w;
+        a.loc_w = L.loc_w;
+        a.loc_b = L.loc_b;
+        a.fq = L.fq;
+        a.Hp = p.Hp;
+        a.Wp = p.Wp;
+        a.C = p.C;
+        a.MW = p.MW;
+        a.act = p.act;
+        if (p.timer) p.timer->begin("fno2d_f32_layer", st);
+        layer2d_kernel<<<dim3(p.Hp, p.B), 256, sl, st>>>(a);
+        if (p.timer) p.timer->end(st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    {
+        const int64_t total = static_cast<int64_t>(p.B) * p.H * p.W;
+        const int threads = p.C > 128 ? 64 : 128;
+        const size_t smem = static_cast<size_t>(threads) * (p.C + 1) * sizeof(float);
+        if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(proj2d_f32_kernel), static_cast<int>(smem))) !=
+            cudaSuccess)
+            return e;
+        const int grid = static_cast<int>(std::min<int64_t>((total + threads - 1) / threads, sms * 8));
+        if (p.timer) p.timer->begin("fno2d_f32_proj", st);
+        proj2d_f32_kernel<<<grid, threads, smem, st>>>(p, p.h[p.L & 1]);
+        if (p.timer) p.timer->end(st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace nfx

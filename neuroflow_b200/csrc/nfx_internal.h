@@ -9,6 +9,15 @@
 
 namespace nfx {
 
+// Fake-quant applied at an ".output" boundary: kind 0 none, 1 INT8 per-tensor,
+// 2 the reference FNO2d FP8 log2 snap (fno.cpp:813-828).
+struct FqParam {
+    int kind;
+    float scale;
+    int zp;
+    float inv_scale;  // 1/scale (IEEE), for the division-free fast path
+};
+
 // Arguments of the INT8 GEMM kernel (gemm_i8.cu).  Device pointers.
 struct GemmArgs {
     const int8_t* A;          // (M, K) activation codes

@@ -111,6 +111,12 @@ struct nfx_runtime {
     int tw_H = 0, tw_W = 0;
     int8_t* fwd_limbs = nullptr;      // tensor-core forward basis digits (W == 128)
     long long* fwd_sum_b = nullptr;
+    // FNO2d FP32 (reference fake-quant) state
+    nfx::Fno2dF32Plan plan2f{};
+    void* f2_bufs[4] = {nullptr, nullptr, nullptr, nullptr};  // h0, h1, Xs, colinv
+    int64_t f2_cap[4] = {0, 0, 0, 0};
+    float2* f2_tw[4] = {nullptr, nullptr, nullptr, nullptr};   // fwd W, inv W, fwd H, inv H
+    int f2_tw_H = 0, f2_tw_W = 0;
     // FNO1d state
     nfx::Fno1dPlan plan1{};
     int pt_n[nfx::kFno1dMaxLayers] = {};   // per-token table sizes (locs.i.output)
@@ -177,13 +183,53 @@ F2 fno2d_cfg(const nfx::IrModel& m) {
     return F2{m.cfg[0], m.cfg[1], m.cfg[2], m.cfg[3], m.cfg[4], m.cfg[5], m.cfg[6]};
 }
 
+// The FP32 fake-quant plan (fno2d_fp32.cu): weights as the reference holds them after
+// Create, and the four ".output" fake-quant boundaries of FNO2d::Forward.
+int fno2d_f32_create(nfx_runtime* rt) {
+    auto& m = rt->model;
+    const F2 c = fno2d_cfg(m);
+    auto& pl = rt->plan2f;
+    if (c.L > nfx::kFno2dMaxLayers || c.in_ch < 1) return NFX_OK;  // Run reports it
+    pl.C = c.width;
+    pl.MH = c.mh;
+    pl.MW = c.mw;
+    pl.L = c.L;
+    pl.in_ch = c.in_ch;
+    pl.out_ch = c.out_ch;
+    pl.act = m.activation == "relu" ? 1 : 0;
+    pl.lift_w = wptr(rt, "lift.weight");
+    pl.lift_b = wptr(rt, "lift.bias");
+    pl.pq_w = wptr(rt, "proj_q.weight");
+    pl.pq_b = wptr(rt, "proj_q.bias");
+    pl.po_w = wptr(rt, "proj_out.weight");
+    pl.po_b = wptr(rt, "proj_out.bias");
+    pl.fq_lift = fq_for(m, "lift.output");
+    pl.fq_pq = fq_for(m, "proj_q.output");
+    pl.fq_po = fq_for(m, "proj_out.output");
+    if (!pl.lift_w || !pl.lift_b || !pl.pq_w || !pl.pq_b || !pl.po_w || !pl.po_b)
+        return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+    for (int i = 0; i < c.L; ++i) {
+        const std::string s = std::to_string(i);
+        auto& L = pl.layer[i];
+        L.wr = wptr(rt, "specs." + s + ".weights_real");
+        L.wi = wptr(rt, "specs." + s + ".weights_imag");
+        L.loc_w = wptr(rt, "locs." + s + ".weight");
+        L.loc_b = wptr(rt, "locs." + s + ".bias");
+        L.fq = fq_for(m, "locs." + s + ".output");
+        if (!L.wr || !L.wi || !L.loc_w || !L.loc_b) return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+    }
+    return NFX_OK;
+}
+
 int fno2d_create(nfx_runtime* rt) {
     auto& m = rt->model;
     const F2 c = fno2d_cfg(m);
     if (m.quant_enabled) {
         for (const auto& name : m.weight_order) nfx::dequantise_weight(m.weights[name], m, name);
     }
-    if (!nfx::fno2d_supported(c.width, c.mh, c.mw)) return NFX_OK;  // Run reports UnsupportedOp
+    int s0 = fno2d_f32_create(rt);
+    if (s0 != NFX_OK) return s0;
+    if (!nfx::fno2d_supported(c.width, c.mh, c.mw)) return NFX_OK;  // INT8 path unavailable
     auto& pl = rt->plan;
     pl.C = c.width;
     pl.MH = c.mh;
@@ -400,15 +446,87 @@ int check_fno2d_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t
     return NFX_OK;
 }
 
+int ensure_f2_buf(nfx_runtime* rt, int i, int64_t bytes) {
+    if (bytes <= rt->f2_cap[i]) return NFX_OK;
+    if (rt->f2_bufs[i]) cudaFree(rt->f2_bufs[i]);
+    rt->f2_bufs[i] = nullptr;
+    rt->f2_cap[i] = 0;
+    if (!cuda_ok(rt, cudaMalloc(&rt->f2_bufs[i], static_cast<size_t>(bytes) + 256), "cudaMalloc activations"))
+        return NFX_INTERNAL;
+    rt->f2_cap[i] = bytes;
+    return NFX_OK;
+}
+
+// FNO2d without EnableInt8Gemm: the reference's FP32 fake-quant network
+int fno2d_f32_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
+    const F2 c = fno2d_cfg(rt->model);
+    auto& pl0 = rt->plan2f;
+    if (!pl0.lift_w)
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, "FNO2d GPU executor: needs <= 8 layers");
+    const int B = static_cast<int>(xs[0]), H = static_cast<int>(xs[1]), W = static_cast<int>(xs[2]);
+    int Hp = H, Wp = W;
+    if (c.pad > 1) {
+        Hp = H + (c.pad - H % c.pad) % c.pad;
+        Wp = W + (c.pad - W % c.pad) % c.pad;
+    }
+    if ((Hp & (Hp - 1)) || (Wp & (Wp - 1)))
+        return rt_fail(rt, NFX_INVALID_ARG, "FNO2d: padded H and W must be powers of two");
+    if (c.mh > Hp || c.mw > Wp / 2 + 1)
+        return rt_fail(rt, NFX_INVALID_ARG, "FNO2d: modes exceed the (padded) grid");
+    if (const char* why = nfx::fno2d_f32_unsupported(c.width, c.mh, c.mw, Hp, Wp, c.out_ch))
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, why);
+    if (B == 0) return NFX_OK;
+    if (rt->f2_tw_H != Hp || rt->f2_tw_W != Wp) {
+        const int lens[4] = {Wp, Wp, Hp, Hp};
+        for (int i = 0; i < 4; ++i) {
+            const std::vector<float> t = nfx::build_fft_twiddles(lens[i], (i & 1) == 1);
+            if (rt->f2_tw[i]) cudaFree(rt->f2_tw[i]);
+            rt->f2_tw[i] = nullptr;
+            void* p = nullptr;
+            if (!cuda_ok(rt, cudaMalloc(&p, t.size() * 4 + 16), "cudaMalloc twiddles")) return NFX_INTERNAL;
+            rt->f2_tw[i] = static_cast<float2*>(p);
+            if (!t.empty() && !cuda_ok(rt, cudaMemcpy(p, t.data(), t.size() * 4, cudaMemcpyHostToDevice),
+                                       "cudaMemcpy twiddles"))
+                return NFX_INTERNAL;
+        }
+        rt->f2_tw_H = Hp;
+        rt->f2_tw_W = Wp;
+    }
+    const int64_t plane = static_cast<int64_t>(B) * c.width * Hp * Wp;
+    int s = ensure_f2_buf(rt, 0, plane * 4);
+    if (s == NFX_OK) s = ensure_f2_buf(rt, 1, plane * 4);
+    if (s == NFX_OK) s = ensure_f2_buf(rt, 2, static_cast<int64_t>(B) * c.width * c.mh * c.mw * 8);
+    if (s == NFX_OK) s = ensure_f2_buf(rt, 3, static_cast<int64_t>(B) * c.width * Hp * c.mw * 8);
+    if (s != NFX_OK) return s;
+    nfx::Fno2dF32Plan pl = pl0;
+    pl.B = B;
+    pl.H = H;
+    pl.W = W;
+    pl.Hp = Hp;
+    pl.Wp = Wp;
+    pl.x = dx;
+    pl.y = dy;
+    pl.twf_w = rt->f2_tw[0];
+    pl.twi_w = rt->f2_tw[1];
+    pl.twf_h = rt->f2_tw[2];
+    pl.twi_h = rt->f2_tw[3];
+    pl.h[0] = static_cast<float*>(rt->f2_bufs[0]);
+    pl.h[1] = static_cast<float*>(rt->f2_bufs[1]);
+    pl.Xs = static_cast<float2*>(rt->f2_bufs[2]);
+    pl.colinv = static_cast<float2*>(rt->f2_bufs[3]);
+    pl.timer = rt->timer.get();
+    const cudaError_t e = nfx::fno2d_f32_run(pl, st);
+    if (e != cudaSuccess)
+        return rt_fail(rt, NFX_INTERNAL, std::string("FNO2d launch failed: ") + cudaGetErrorString(e));
+    return NFX_OK;
+}
+
 int fno2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
     const F2 c = fno2d_cfg(rt->model);
+    if (!rt->int8_enabled) return fno2d_f32_launch(rt, dx, xs, dy, st);
     if (!nfx::fno2d_supported(c.width, c.mh, c.mw))
         return rt_fail(rt, NFX_UNSUPPORTED_OP,
-                       "FNO2d on the GPU runtime supports width 64 with 12x12 modes");
-    if (!rt->int8_enabled)
-        return rt_fail(rt, NFX_UNSUPPORTED_OP,
-                       "FNO2d on the GPU runtime runs the INT8 path: call EnableInt8Gemm() on an "
-                       "IR with per-channel weight and per-tensor activation qparams");
+                       "FNO2d INT8 executor supports width 64 with 12x12 modes");
     const int B = static_cast<int>(xs[0]), H = static_cast<int>(xs[1]), W = static_cast<int>(xs[2]);
     if (B == 0) return NFX_OK;
     if (W < 32 || W > 128 || H < 8 || H > 4096 || c.mh > H || c.mw > W / 2 + 1)
@@ -610,9 +728,6 @@ int fno1d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
             return rt_fail(rt, NFX_INVALID_ARG,
                            "FNO1d: per-token qparams of locs." + std::to_string(i) +
                                ".output do not cover (n, width)");
-        if (L.use_int8 && !nfx::gemm_i8_supported(c.width, c.width))
-            return rt_fail(rt, NFX_UNSUPPORTED_OP,
-                           "FNO1d INT8 GEMM: width must be 32, 64, 128 or 256");
     }
     if (B == 0) return NFX_OK;
     // twiddles for N
@@ -811,6 +926,10 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
     for (auto* p : rt->tw)
         if (p) cudaFree(p);
     for (void* p : rt->f1_bufs)
+        if (p) cudaFree(p);
+    for (void* p : rt->f2_bufs)
+        if (p) cudaFree(p);
+    for (auto* p : rt->f2_tw)
         if (p) cudaFree(p);
     for (auto* p : rt->f1_tw)
         if (p) cudaFree(p);

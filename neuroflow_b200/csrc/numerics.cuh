@@ -7,6 +7,8 @@
 #include <climits>
 #include <cstdint>
 
+#include "nfx_internal.h"
+
 namespace nfx {
 
 // int8_gemm.cpp:514-518 QuantiseActivation for one element:
@@ -73,6 +75,28 @@ __device__ __forceinline__ float gelu_tanh(float z) {
 }
 
 __device__ __forceinline__ float relu_ref(float z) { return z < 0.0f ? 0.0f : z; }
+
+// fno.cpp:585-603 / :813-828 FP8 branch: log2 snap of v / scale.  The std::ldexp
+// exponent is the float round(log2|u| * 8) / 8 truncated to int, as the reference
+// computes it.  log2f is CUDA's (glibc's may differ by an ulp next to a breakpoint).
+__device__ __forceinline__ float fp8_log2_snap(float v, float scale) {
+    if (!(scale > 0.0f)) return v;
+    const float u = __fdiv_rn(v, scale);
+    const float a = fabsf(u);
+    const float sign = u < 0.0f ? -1.0f : 1.0f;
+    const float qv = (a < 0.015625f)
+                         ? a
+                         : ldexpf(1.0f, static_cast<int>(__fdiv_rn(
+                                            roundf(__fmul_rn(log2f(a), 8.0f)), 8.0f)));
+    return __fmul_rn(__fmul_rn(sign, fminf(qv, 448.0f)), scale);
+}
+
+// fno.cpp:810-844 apply_fake_quant for one element: FP8 first, else INT8 per-tensor.
+__device__ __forceinline__ float apply_fq(float v, const FqParam& q) {
+    if (q.kind == 1) return fake_quant(v, q.scale, static_cast<float>(q.zp));
+    if (q.kind == 2) return fp8_log2_snap(v, q.scale);
+    return v;
+}
 
 // fno.cpp:51-80 Linear (acc = b; acc += x[p]*w[p] for p = 0..k-1) as the reference
 // build (GCC -O3 with the AVX-512 flags of cpp/CMakeLists.txt:78) evaluates it: the

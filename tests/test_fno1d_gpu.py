@@ -2,7 +2,7 @@
 pinned bit-exact against the reference runtime).
 
 * ReLU models: every operation on the path is reproduced with the reference's
-  rounding (radix-2 FFT with the recurrence twiddles, contraction, fma-chain Linear,
+  rounding (radix-2 FFT with the recurrence twiddles, contraction, Linear dot products,
   INT8 LinearForwardBatched, fake-quant), so the GPU output is BIT-IDENTICAL.
 * GELU models: tanhf is CUDA's where its result is consumed as fp32 (glibc's and
   CUDA's tanhf differ by a few ulps); where GELU feeds a per-tensor snap the exact
@@ -155,3 +155,16 @@ def test_fno1d_reference_exported_models(tag):
         diff = np.abs(got - want)
         tol = 1e-5 * np.abs(want) + 1e-6 * np.abs(want).max()
         assert np.mean(diff > tol) <= (0.02 if tag == "pt" else 0.0), (int8, float(diff.max()))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("width", [16, 20, 48])
+def test_fno1d_relu_bit_exact_untiled_widths(tmp_path, width):
+    """INT8 local layers at widths the tcgen05 GEMM does not tile run the same integer
+    arithmetic on CUDA cores; FP32 dot products with vector tails (width 20)."""
+    m, p = _model(tmp_path, "per_tensor", act="relu", width=width, modes=6, L=2, n=64)
+    x = synth.fno1d_inputs(np.random.default_rng(8), 2, 64)
+    for int8 in (False, True):
+        want = Oracle().fno1d_forward(m, x, int8=int8)
+        got = _run(p, x, 1, int8)
+        assert np.array_equal(_bits(got), _bits(want)), (int8, float(np.abs(got - want).max()))

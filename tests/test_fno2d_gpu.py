@@ -62,6 +62,8 @@ def test_fno2d_shape_errors(tmp_path):
 
 @pytest.mark.gpu
 def test_fno2d_without_nirq_is_not_int8(tmp_path):
+    """Without NIRQ, EnableInt8Gemm leaves the flag off (the reference's flag is
+    FNO1d-only) and Run executes the FP32 network."""
     from neuroflow_b200.runtime import InferenceRuntime
     m, _ = _model(tmp_path, L=1)
     m.quant_enabled = False
@@ -70,8 +72,11 @@ def test_fno2d_without_nirq_is_not_int8(tmp_path):
     rt = InferenceRuntime(p)
     rt.enable_int8_gemm()
     assert not rt.is_int8_gemm_enabled()
-    with pytest.raises(RuntimeError, match="INT8"):
-        rt.run(np.zeros((1, 32, 32, 3), np.float32), np.zeros((1, 32, 32, 1), np.float32))
+    x = synth.fno2d_inputs(np.random.default_rng(1), 1, 32, 32)
+    y = np.zeros((1, 32, 32, 1), np.float32)
+    rt.run(x, y)
+    want = Oracle().fno2d_forward(m, x, mode=0)
+    assert np.allclose(y, want, rtol=1e-4, atol=1e-5 * np.abs(want).max())
 
 
 @pytest.mark.gpu
