@@ -243,3 +243,44 @@ def fno1d_model(seed: int, in_ch=2, out_ch=1, width=64, modes=16, L=4, n=1024, n
         st = np.concatenate(vs, axis=0)
         qp[k] = quant.per_token_qparams(st) if per_token else quant.tensor_qparams(st)
     return ir.Model(op="FNO1d", config=cfg, weights=wts, qparams=qp, quant_enabled=True)
+
+
+# ------------------------------------------------------------------ TokenMixer2D
+TM2D_PARTS = ("ln1", "q_proj", "k_proj", "v_proj", "o_proj", "ln2", "ffn0", "ffn1")
+TM2D_INT8_PARTS = ("q_proj", "k_proj", "v_proj", "o_proj", "ffn0", "ffn1")
+
+
+def tm2d_model(seed: int, in_dim=3, out_dim=1, latent=128, h=64, w=64, n_patches=4096,
+               n_heads=4, n_layers=4, activation="gelu") -> ir.Model:
+    """A random-init TokenMixer2D (configs[4] shape by default): LayerNorm gamma = 1,
+    beta = 0, every Linear Kaiming-uniform.  The NIRQ block carries per-channel weight
+    qparams of the six INT8 layers (q, k, v, o, ffn0, ffn1); the reference runtime
+    ignores NIRQ for this op, the INT8 executor reads them."""
+    rng = np.random.default_rng(seed)
+    wts = {}
+    wts["slice_embed.proj.weight"], wts["slice_embed.proj.bias"] = _kaiming_linear(rng, latent, in_dim)
+    for i in range(n_layers):
+        pre = f"blocks.{i}."
+        for part in TM2D_PARTS:
+            if part.startswith("ln"):
+                wts[pre + part + ".weight"] = np.ones(latent, np.float32)
+                wts[pre + part + ".bias"] = np.zeros(latent, np.float32)
+            else:
+                o, k = {"ffn0": (2 * latent, latent), "ffn1": (latent, 2 * latent)}.get(part, (latent, latent))
+                wts[pre + part + ".weight"], wts[pre + part + ".bias"] = _kaiming_linear(rng, o, k)
+    wts["unslice.proj.weight"], wts["unslice.proj.bias"] = _kaiming_linear(rng, latent, in_dim + latent)
+    wts["head.weight"], wts["head.bias"] = _kaiming_linear(rng, out_dim, latent)
+    qp = {}
+    for i in range(n_layers):
+        for part in TM2D_INT8_PARTS:
+            name = f"blocks.{i}.{part}.weight"
+            qp[name] = quant.per_channel_qparams(wts[name], 0)
+    cfg = dict(in_dim=in_dim, out_dim=out_dim, latent_dim=latent, h=h, w=w, n_patches=n_patches,
+               n_heads=n_heads, n_layers=n_layers)
+    return ir.Model(op="TokenMixer2D", config=cfg, activation=activation, weights=wts, qparams=qp,
+                    quant_enabled=True)
+
+
+def tm2d_inputs(rng: np.random.Generator, n: int, h: int, w: int, in_dim: int = 3) -> np.ndarray:
+    """(n, h, w, in_dim): a GRF field (spectrum as configs[2]) + grid coordinates."""
+    return fno2d_inputs(rng, n, h, w, in_dim)

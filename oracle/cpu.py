@@ -76,6 +76,14 @@ class _FNO1d(C.Structure):
                 + [("a_lift", _AQ1), ("a_locs", _AQ1 * MAX_LAYERS)])
 
 
+class _TM2D(C.Structure):
+    _fields_ = ([(n, C.c_int32) for n in ("in_dim", "out_dim", "latent", "h", "w", "n_patches",
+                                          "n_heads", "n_layers", "relu")]
+                + [(n, _f32p) for n in ("se_w", "se_b", "un_w", "un_b", "head_w", "head_b")]
+                + [("blk_w", (_f32p * 8) * MAX_LAYERS), ("blk_b", (_f32p * 8) * MAX_LAYERS),
+                   ("pc_s", (_f32p * 8) * MAX_LAYERS), ("pc_zp", (_i32p * 8) * MAX_LAYERS)])
+
+
 class _Taps(C.Structure):
     _fields_ = [("codes_in", _i8p * (MAX_LAYERS + 1)), ("x1_out", _f32p * MAX_LAYERS),
                 ("h_out", _f32p * MAX_LAYERS)]
@@ -92,6 +100,8 @@ class Oracle:
         L.nfo_fno2d_forward.restype = C.c_int
         L.nfo_fno2d_forward.argtypes = [C.POINTER(_FNO2d), C.c_int, _f32p, C.c_int, C.c_int,
                                         C.c_int, _f32p, C.POINTER(_Taps)]
+        L.nfo_tm2d_forward.restype = C.c_int
+        L.nfo_tm2d_forward.argtypes = [C.POINTER(_TM2D), C.c_int, _f32p, C.c_int, _f32p]
         L.nfo_fno1d_forward.restype = C.c_int
         L.nfo_fno1d_forward.argtypes = [C.POINTER(_FNO1d), _f32p, C.c_int, C.c_int, _f32p]
 
@@ -237,6 +247,51 @@ class Oracle:
             raise RuntimeError(f"nfo_fno1d_forward failed: {rc}")
         del keep
         return y
+
+
+    # -- TokenMixer2D ---------------------------------------------------------------
+    def tm2d_forward(self, model, x, int8: bool = False):
+        """mode 0 (int8=False): the reference TokenMixer2D::Forward; int8=True: the INT8
+        variant (per-token activations, per-channel weight codes on q/k/v/o/ffn)."""
+        x = _c(x, np.float32)
+        st, keep = build_tm2d_struct(model)
+        cfg = model.config
+        y = np.empty(x.shape[:-1] + (cfg["out_dim"],), np.float32)
+        rc = self.lib.nfo_tm2d_forward(C.byref(st), 1 if int8 else 0, _p(x), x.shape[0], _p(y))
+        if rc != 0:
+            raise RuntimeError(f"nfo_tm2d_forward failed: {rc}")
+        del keep
+        return y
+
+
+def build_tm2d_struct(model):
+    from neuroflow_b200.synth import TM2D_PARTS
+    cfg, w = model.config, model.weights
+    keep = []
+    st = _TM2D()
+    for f, k in (("in_dim", "in_dim"), ("out_dim", "out_dim"), ("latent", "latent_dim"), ("h", "h"),
+                 ("w", "w"), ("n_patches", "n_patches"), ("n_heads", "n_heads"),
+                 ("n_layers", "n_layers")):
+        setattr(st, f, cfg[k])
+    st.relu = 1 if model.activation == "relu" else 0
+
+    def arr(a, dt=np.float32, t=_f32p):
+        a = _c(a, dt)
+        keep.append(a)
+        return _p(a, t)
+
+    st.se_w, st.se_b = arr(w["slice_embed.proj.weight"]), arr(w["slice_embed.proj.bias"])
+    st.un_w, st.un_b = arr(w["unslice.proj.weight"]), arr(w["unslice.proj.bias"])
+    st.head_w, st.head_b = arr(w["head.weight"]), arr(w["head.bias"])
+    for i in range(cfg["n_layers"]):
+        for j, part in enumerate(TM2D_PARTS):
+            st.blk_w[i][j] = arr(w[f"blocks.{i}.{part}.weight"])
+            st.blk_b[i][j] = arr(w[f"blocks.{i}.{part}.bias"])
+            qp = model.qparams.get(f"blocks.{i}.{part}.weight")
+            if qp is not None and hasattr(qp, "scales"):
+                st.pc_s[i][j] = arr(qp.scales)
+                st.pc_zp[i][j] = arr(qp.zero_points, np.int32, _i32p)
+    return st, keep
 
 
 def _aq1(model, key, keep):

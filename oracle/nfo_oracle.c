@@ -1079,3 +1079,230 @@ int nfo_fno1d_forward(const nfo_fno1d* m, const float* x, int bsz, int n0, float
     free(po_b);
     return 0;
 }
+
+/* ------------------------------------------------------------------------- */
+/* TokenMixer2D (fno.cpp:1418-1456, :1756-1956)                               */
+/* ------------------------------------------------------------------------- */
+
+/* A sequential dot-product reduction as the reference build evaluates it (the rule of
+ * nfo_linear): acc0 + sum_p a[p*sa] * b[p*sb]. */
+static float dot_ref(float acc, const float* a, int64_t sa, const float* b, int64_t sb, int k) {
+    const int vec = nfo_linear_unfused_len(k);
+    int p = 0;
+    for (; p < vec; ++p) acc = acc + a[p * sa] * b[p * sb];
+    for (; p < k; ++p) acc = fmaf(a[p * sa], b[p * sb], acc);
+    return acc;
+}
+
+/* fno.cpp:1418-1438 LayerNormLastDim: sequential mean, sequential sum of squared
+ * deviations (vector-block rule), y = fma((x - mean) * inv, gamma, beta). */
+void nfo_layer_norm(const float* x, int rows, int d, const float* gamma, const float* beta,
+                    float* y) {
+    const float eps = 1e-5f;
+    for (int r = 0; r < rows; ++r) {
+        const float* xr = x + (int64_t)r * d;
+        float* yr = y + (int64_t)r * d;
+        float mean = 0.0f;
+        for (int i = 0; i < d; ++i) mean += xr[i];
+        mean /= (float)d;
+        const int vec = nfo_linear_unfused_len(d);
+        float var = 0.0f;
+        for (int i = 0; i < d; ++i) {
+            const float diff = xr[i] - mean;
+            var = i < vec ? var + diff * diff : fmaf(diff, diff, var);
+        }
+        var /= (float)d;
+        const float inv = 1.0f / sqrtf(var + eps);
+        for (int i = 0; i < d; ++i) yr[i] = fmaf((xr[i] - mean) * inv, gamma[i], beta[i]);
+    }
+}
+
+/* Per-row (per-token) INT8 qparams of a row by the compute_tensor_qparams rule
+ * (neuroflow/quant/static_quant.py:480-533, Python floats = double): scale =
+ * (max - min) / 255, zp = clip(round_half_even(-128 - min / scale)), the clipped-zp
+ * scale fix-up, then the scale rounded to float32. */
+void nfo_row_qparams(const float* row, int n, float* scale_out, int32_t* zp_out) {
+    float mn = row[0], mx = row[0];
+    for (int i = 1; i < n; ++i) {
+        if (row[i] < mn) mn = row[i];
+        if (row[i] > mx) mx = row[i];
+    }
+    if (mx == mn || mn != mn || mx != mx) {
+        *scale_out = 1.0f;
+        *zp_out = 0;
+        return;
+    }
+    double scale = ((double)mx - (double)mn) / 255.0;
+    const double raw = nearbyint(-128.0 - (double)mn / scale);
+    double zp = raw < -128.0 ? -128.0 : (raw > 127.0 ? 127.0 : raw);
+    if (zp != raw) {
+        if (zp == -128.0) scale = ((double)mx - 0.0) / 255.0;
+        else scale = (0.0 - (double)mn) / 255.0;
+    }
+    *scale_out = (float)scale;
+    *zp_out = (int32_t)zp;
+}
+
+typedef struct {
+    int32_t in_dim, out_dim, latent, h, w, n_patches, n_heads, n_layers, relu;
+    const float* se_w;    /* slice_embed.proj (latent, in_dim) */
+    const float* se_b;
+    const float* un_w;    /* unslice.proj (latent, in_dim + latent) */
+    const float* un_b;
+    const float* head_w;  /* (out_dim, latent) */
+    const float* head_b;
+    /* per block: ln1, q, k, v, o, ln2, ffn0, ffn1 (weight, bias) */
+    const float* blk_w[NFO_MAX_LAYERS][8];
+    const float* blk_b[NFO_MAX_LAYERS][8];
+    /* INT8 variant: per-channel (axis 0) weight qparams of q, k, v, o, ffn0, ffn1
+     * (block slots 1, 2, 3, 4, 6, 7) */
+    const float* pc_s[NFO_MAX_LAYERS][8];
+    const int32_t* pc_zp[NFO_MAX_LAYERS][8];
+} nfo_tm2d;
+
+/* One Linear of the INT8 variant: per-token dynamic activation qparams, per-channel
+ * weight codes (QuantiseWeight2D), the LinearForwardBatched epilogue per row, then
+ * + bias as a separate add and the optional GELU (nfo_int8_gemm_rows). */
+static void tm2d_linear_int8(const float* A, int M, int K, const float* W, const float* b,
+                             const float* pcs, const int32_t* pczp, int N, int gelu, float* C) {
+    int8_t* Wq = (int8_t*)malloc((size_t)N * K);
+    int32_t* sw = (int32_t*)malloc(sizeof(int32_t) * N);
+    nfo_quantise_weight_2d(W, N, K, pcs, pczp, Wq, sw);
+    int8_t* Aq = (int8_t*)malloc((size_t)M * K);
+    float* sA = (float*)malloc(sizeof(float) * M);
+    int32_t* zA = (int32_t*)malloc(sizeof(int32_t) * M);
+    for (int r = 0; r < M; ++r) {
+        nfo_row_qparams(A + (int64_t)r * K, K, &sA[r], &zA[r]);
+        nfo_quantise_activation(A + (int64_t)r * K, Aq + (int64_t)r * K, K, sA[r], zA[r]);
+    }
+    nfo_int8_gemm_rows(Aq, sA, zA, M, K, Wq, pcs, pczp, sw, N, b, gelu, C, NULL);
+    free(zA);
+    free(sA);
+    free(Aq);
+    free(sw);
+    free(Wq);
+}
+
+/* mode 0: TokenMixer2D::Forward (fno.cpp:1756-1956), FP32, the reference's loops and
+ *         rounding (the AV sum uses the fused scalar form: its strided V operand keeps
+ *         the reference build from vectorising it).
+ * mode 1: the INT8 variant: q, k, v, o, ffn0, ffn1 through tm2d_linear_int8.
+ * x (b, h, w, in_dim) -> y (b, h, w, out_dim).  Returns 0 or a StatusCode. */
+int nfo_tm2d_forward(const nfo_tm2d* m, int mode, const float* x, int bsz, float* y) {
+    const int in_d = m->in_dim, out_d = m->out_dim, L = m->latent, np_ = m->n_patches;
+    const int nh = m->n_heads, nl = m->n_layers;
+    if (np_ <= 0 || (m->h * m->w) % np_ != 0 || L % nh != 0 || nl < 1 || nl > NFO_MAX_LAYERS)
+        return 1;
+    const int hd = L / nh;
+    const int n_points = m->h * m->w;
+    const int pp = n_points / np_;
+    const float scale = 1.0f / sqrtf((float)hd);
+    const int64_t bnp = (int64_t)bsz * np_;
+    float* xp = (float*)calloc((size_t)(bnp * in_d), sizeof(float));
+    for (int64_t bi = 0; bi < bsz; ++bi)
+        for (int pi = 0; pi < np_; ++pi)
+            for (int q = 0; q < pp; ++q) {
+                const float* src = x + ((bi * n_points) + (int64_t)pi * pp + q) * in_d;
+                float* dst = xp + (bi * np_ + pi) * in_d;
+                for (int d = 0; d < in_d; ++d) dst[d] += src[d] / (float)pp;
+            }
+    float* tok = (float*)malloc(sizeof(float) * (size_t)(bnp * L));
+    nfo_linear(xp, m->se_w, m->se_b, (int)bnp, in_d, L, tok);
+    float* ln = (float*)malloc(sizeof(float) * (size_t)(bnp * L));
+    float* Q = (float*)malloc(sizeof(float) * (size_t)(bnp * L));
+    float* Kb = (float*)malloc(sizeof(float) * (size_t)(bnp * L));
+    float* V = (float*)malloc(sizeof(float) * (size_t)(bnp * L));
+    float* ho = (float*)malloc(sizeof(float) * (size_t)(bnp * L));
+    float* f0 = (float*)malloc(sizeof(float) * (size_t)(bnp * 2 * L));
+    float* f1 = (float*)malloc(sizeof(float) * (size_t)(bnp * L));
+    float* attn = (float*)malloc(sizeof(float) * (size_t)np_ * np_);
+    for (int li = 0; li < nl; ++li) {
+        const float* const* Wt = m->blk_w[li];
+        const float* const* Bt = m->blk_b[li];
+        nfo_layer_norm(tok, (int)bnp, L, Wt[0], Bt[0], ln);
+        if (mode == 1) {
+            tm2d_linear_int8(ln, (int)bnp, L, Wt[1], Bt[1], m->pc_s[li][1], m->pc_zp[li][1], L, 0, Q);
+            tm2d_linear_int8(ln, (int)bnp, L, Wt[2], Bt[2], m->pc_s[li][2], m->pc_zp[li][2], L, 0, Kb);
+            tm2d_linear_int8(ln, (int)bnp, L, Wt[3], Bt[3], m->pc_s[li][3], m->pc_zp[li][3], L, 0, V);
+        } else {
+            nfo_linear(ln, Wt[1], Bt[1], (int)bnp, L, L, Q);
+            nfo_linear(ln, Wt[2], Bt[2], (int)bnp, L, L, Kb);
+            nfo_linear(ln, Wt[3], Bt[3], (int)bnp, L, L, V);
+        }
+        for (int64_t bi = 0; bi < bsz; ++bi)
+            for (int hi = 0; hi < nh; ++hi) {
+                for (int i = 0; i < np_; ++i)
+                    for (int j = 0; j < np_; ++j) {
+                        const float* q = Q + ((bi * np_ + i) * nh + hi) * hd;
+                        const float* k = Kb + ((bi * np_ + j) * nh + hi) * hd;
+                        attn[(int64_t)i * np_ + j] = dot_ref(0.0f, q, 1, k, 1, hd) * scale;
+                    }
+                for (int i = 0; i < np_; ++i) {  /* fno.cpp:1441-1456 */
+                    float* zr = attn + (int64_t)i * np_;
+                    float mx = zr[0];
+                    for (int j = 1; j < np_; ++j)
+                        if (zr[j] > mx) mx = zr[j];
+                    float sum = 0.0f;
+                    for (int j = 0; j < np_; ++j) {
+                        zr[j] = expf(zr[j] - mx);
+                        sum += zr[j];
+                    }
+                    const float inv = 1.0f / sum;
+                    for (int j = 0; j < np_; ++j) zr[j] *= inv;
+                }
+                const int av_vec = (np_ / 4) * 4;
+                for (int i = 0; i < np_; ++i)
+                    for (int dh = 0; dh < hd; ++dh) {
+                        float acc = 0.0f;
+                        for (int j = 0; j < np_; ++j) {
+                            const float a = attn[(int64_t)i * np_ + j];
+                            const float v = V[((bi * np_ + j) * nh + hi) * hd + dh];
+                            acc = j < av_vec ? acc + a * v : fmaf(a, v, acc);
+                        }
+                        ho[((bi * np_ + i) * nh + hi) * hd + dh] = acc;
+                    }
+            }
+        if (mode == 1)
+            tm2d_linear_int8(ho, (int)bnp, L, Wt[4], Bt[4], m->pc_s[li][4], m->pc_zp[li][4], L, 0, f1);
+        else
+            nfo_linear(ho, Wt[4], Bt[4], (int)bnp, L, L, f1);
+        for (int64_t i = 0; i < bnp * L; ++i) tok[i] += f1[i];
+        nfo_layer_norm(tok, (int)bnp, L, Wt[5], Bt[5], ln);
+        if (mode == 1) {
+            tm2d_linear_int8(ln, (int)bnp, L, Wt[6], Bt[6], m->pc_s[li][6], m->pc_zp[li][6], 2 * L,
+                             m->relu ? 0 : 1, f0);
+            if (m->relu)
+                for (int64_t i = 0; i < bnp * 2 * L; ++i) f0[i] = f0[i] < 0.0f ? 0.0f : f0[i];
+            tm2d_linear_int8(f0, (int)bnp, 2 * L, Wt[7], Bt[7], m->pc_s[li][7], m->pc_zp[li][7], L, 0, f1);
+        } else {
+            nfo_linear(ln, Wt[6], Bt[6], (int)bnp, L, 2 * L, f0);
+            nfo_apply_activation(f0, bnp * 2 * L, m->relu);
+            nfo_linear(f0, Wt[7], Bt[7], (int)bnp, 2 * L, L, f1);
+        }
+        for (int64_t i = 0; i < bnp * L; ++i) tok[i] += f1[i];
+    }
+    /* unslice: concat (x, token of the point's patch) -> Linear -> head */
+    const int ipl = in_d + L;
+    float* cat = (float*)malloc(sizeof(float) * (size_t)ipl);
+    float* feat = (float*)malloc(sizeof(float) * (size_t)L);
+    for (int64_t bi = 0; bi < bsz; ++bi)
+        for (int64_t ni = 0; ni < n_points; ++ni) {
+            memcpy(cat, x + (bi * n_points + ni) * in_d, sizeof(float) * in_d);
+            memcpy(cat + in_d, tok + (bi * np_ + ni / pp) * L, sizeof(float) * L);
+            nfo_linear(cat, m->un_w, m->un_b, 1, ipl, L, feat);
+            nfo_linear(feat, m->head_w, m->head_b, 1, L, out_d, y + (bi * n_points + ni) * out_d);
+        }
+    free(feat);
+    free(cat);
+    free(attn);
+    free(f1);
+    free(f0);
+    free(ho);
+    free(V);
+    free(Kb);
+    free(Q);
+    free(ln);
+    free(tok);
+    free(xp);
+    return 0;
+}

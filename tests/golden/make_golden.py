@@ -20,6 +20,10 @@ What it writes (small files, committed):
   fno1d_pc.nneuroir     the same network calibrated with per-tensor activations
   fno1d.npz             input x and the reference runtime's outputs for both files, with
                         and without EnableInt8Gemm
+  tm2d.nneuroir         a tiny TokenMixer2D (8x8 grid, 16 patches, latent 16, 2 heads,
+                        2 blocks) built by the reference's PyTorch model and exported by
+                        `export_all`
+  tm2d.npz              input x and the reference runtime's RunTokenMixer2D output
   int8_gemm.npz         LinearForwardBatched vectors (reference C++): W codes, scales,
                         zero points, sum_w, A, C for K = N = 64, plus QuantiseActivation
   fft.npz               Rfft2/Irfft2 of a 16x32 field (reference C++)
@@ -48,6 +52,7 @@ import torch  # noqa: E402
 from neuroflow.ir.export import export_all, export_to_binary, export_to_neuroir  # noqa: E402
 from neuroflow.nn.fno import FNO1d, FNO1dConfig  # noqa: E402
 from neuroflow.nn.fno2d import FNO2d, FNO2dConfig  # noqa: E402
+from neuroflow.nn.tokenmixer2d import TokenMixer2D, TokenMixer2DConfig  # noqa: E402
 from neuroflow.quant import (compute_per_channel_qparams, compute_tensor_qparams,  # noqa: E402
                              quant_to_ir, quantise_model)
 
@@ -151,6 +156,18 @@ def main():
                         t_scale=np.array(ts, np.float64), t_zp=np.array(tz, np.int32),
                         W=Wpc, pc_scale=np.asarray(pcq.scales, np.float32),
                         pc_zp=np.asarray(pcq.zero_points, np.int32))
+    # --- TokenMixer2D (appended last so the streams above are unchanged) ------------
+    torch.manual_seed(2)
+    tm = TokenMixer2D(TokenMixer2DConfig(in_dim=3, out_dim=1, h=8, w=8, n_patches=16,
+                                         latent_dim=16, n_heads=2, n_layers=2)).eval()
+    with tempfile.TemporaryDirectory() as d:
+        _, pt = export_all(tm, d, basename="tm2d")
+        blob_t = open(pt, "rb").read()
+    path_t = os.path.join(HERE, "tm2d.nneuroir")
+    open(path_t, "wb").write(blob_t)
+    xt = rng.standard_normal((2, 8, 8, 3)).astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "tm2d.npz"), x=xt,
+                        y=ref.run(path_t, xt, 1, tokenmixer2d=True))
     print("golden fixtures written to", HERE)
 
 

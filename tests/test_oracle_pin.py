@@ -59,6 +59,15 @@ def test_golden_fno1d_networks(tag):
     assert np.array_equal(_bits(o.fno1d_forward(m, d["x"], int8=True)), _bits(d[f"y_{tag}_int8"]))
 
 
+def test_golden_tm2d_network():
+    """A TokenMixer2D built by the reference's PyTorch model and exported by its
+    exporter; the reference runtime's RunTokenMixer2D output, every bit."""
+    d = _g("tm2d.npz")
+    m = ir.read(os.path.join(GOLD, "tm2d.nneuroir"))
+    assert m.op == "TokenMixer2D" and m.config["n_patches"] == 16
+    assert np.array_equal(_bits(Oracle().tm2d_forward(m, d["x"])), _bits(d["y"]))
+
+
 def test_golden_linear_forward_batched_and_quantiser():
     d = _g("int8_gemm.npz")
     o = Oracle()
@@ -191,6 +200,24 @@ def test_ref_fno1d_network_bitexact(tmp_path, variant):
     for int8 in (False, True):
         want = r.run(p, x, 1, enable_int8=int8)
         assert np.array_equal(_bits(o.fno1d_forward(m, x, int8=int8)), _bits(want)), int8
+
+
+@needs_ref
+@pytest.mark.parametrize("kw", [
+    dict(latent=16, n_heads=2, h=6, w=8, n_patches=12, n_layers=2),
+    dict(latent=24, n_heads=3, h=5, w=4, n_patches=20, n_layers=1, in_dim=5, out_dim=2),
+    dict(latent=16, n_heads=1, h=3, w=7, n_patches=21, n_layers=1),
+    dict(latent=32, n_heads=4, h=8, w=16, n_patches=128, n_layers=2)])
+def test_ref_tm2d_network_bitexact(tmp_path, kw):
+    """Ragged patch counts (the attention-times-V sum's fused tail), pooled patches
+    (pp > 1), odd latent widths (LayerNorm and Linear tails)."""
+    m = synth.tm2d_model(3, **kw)
+    p = str(tmp_path / "m.nneuroir")
+    ir.write(p, m)
+    x = np.random.default_rng(1).standard_normal(
+        (2, kw["h"], kw["w"], kw.get("in_dim", 3))).astype(np.float32)
+    want = Reference().run(p, x, kw.get("out_dim", 1), tokenmixer2d=True)
+    assert np.array_equal(_bits(Oracle().tm2d_forward(m, x)), _bits(want))
 
 
 @needs_ref
