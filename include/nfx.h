@@ -55,10 +55,13 @@ void nfx_runtime_destroy(nfx_runtime* rt);
 /* InferenceRuntime::op (runtime.h:114): "FNO1d", "FNO2d", ... */
 const char* nfx_runtime_op(const nfx_runtime* rt);
 
-/* InferenceRuntime::EnableInt8Gemm (runtime.h:116-124, runtime.cpp:155-166).  On this
- * runtime the INT8 path covers FNO2d as well as FNO1d (see DESIGN.md for the exact
- * semantics); it needs per-channel weight qparams and per-tensor activation qparams
- * in the NIRQ block, otherwise it is a no-op like the reference. */
+/* InferenceRuntime::EnableInt8Gemm (runtime.h:116-124, runtime.cpp:155-166).  FNO1d:
+ * the reference's semantics (the flag is set; layers whose input key has per-tensor
+ * qparams and whose weight has per-channel qparams run through the INT8 GEMM).  On
+ * this runtime it also enables INT8 executors the reference does not have: FNO2d
+ * (per-channel weight and per-tensor activation qparams needed) and TokenMixer2D
+ * (per-channel weight qparams of q/k/v/o/ffn0/ffn1, per-token activation qparams
+ * computed at run time); without those qparams it is a no-op like the reference. */
 void nfx_runtime_enable_int8_gemm(nfx_runtime* rt);
 
 /* InferenceRuntime::IsInt8GemmEnabled (runtime.h:126-128). */
@@ -78,6 +81,20 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
 int nfx_runtime_run_device(nfx_runtime* rt, const float* x, const int64_t* x_shape,
                            int x_rank, float* y, const int64_t* y_shape, int y_rank,
                            void* stream);
+
+/* InferenceRuntime::RunTokenMixer2D (runtime.h:98-101, runtime.cpp:142-151): x
+ * (batch, h, w, in_dim) -> y (batch, h, w, out_dim), HOST buffers, synchronous.  On a
+ * runtime whose op is not TokenMixer2D it returns NFX_INTERNAL "TokenMixer2D not
+ * initialized" as the reference does; nfx_runtime_run on a TokenMixer2D runtime returns
+ * NFX_INTERNAL "runtime does not support op" (runtime.cpp:97-100). */
+int nfx_runtime_run_tokenmixer2d(nfx_runtime* rt, const float* x, const int64_t* x_shape,
+                                 int x_rank, float* y, const int64_t* y_shape, int y_rank);
+
+/* Device-resident variant of nfx_runtime_run_tokenmixer2d (asynchronous on `stream`,
+ * like nfx_runtime_run_device).  No counterpart in the reference. */
+int nfx_runtime_run_tokenmixer2d_device(nfx_runtime* rt, const float* x,
+                                        const int64_t* x_shape, int x_rank, float* y,
+                                        const int64_t* y_shape, int y_rank, void* stream);
 
 /* Allocation-free variant of nfx_runtime_run_device, for callers that cannot call
  * cudaMalloc while they run inference (their device memory belongs to another

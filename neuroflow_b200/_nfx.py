@@ -46,6 +46,11 @@ if hasattr(lib, "nfx_runtime_create"):
     lib.nfx_runtime_run.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int]
     lib.nfx_runtime_run_device.restype = C.c_int
     lib.nfx_runtime_run_device.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int, _vp]
+    lib.nfx_runtime_run_tokenmixer2d.restype = C.c_int
+    lib.nfx_runtime_run_tokenmixer2d.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int]
+    lib.nfx_runtime_run_tokenmixer2d_device.restype = C.c_int
+    lib.nfx_runtime_run_tokenmixer2d_device.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p,
+                                                        C.c_int, _vp]
     lib.nfx_runtime_check.restype = C.c_int
     lib.nfx_runtime_check.argtypes = [_vp]
     lib.nfx_runtime_last_error.restype = C.c_char_p

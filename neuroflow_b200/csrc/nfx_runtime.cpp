@@ -21,6 +21,7 @@
 #include "nfx_internal.h"
 #include "nfx_ir.h"
 #include "nfx_lut.h"
+#include "tm2d.h"
 
 namespace nfx {
 int set_thread_error(int code, const std::string& msg);
@@ -117,6 +118,10 @@ struct nfx_runtime {
     int64_t f2_cap[4] = {0, 0, 0, 0};
     float2* f2_tw[4] = {nullptr, nullptr, nullptr, nullptr};   // fwd W, inv W, fwd H, inv H
     int f2_tw_H = 0, f2_tw_W = 0;
+    // TokenMixer2D state
+    nfx::Tm2dPlan plan_tm{};
+    void* tm_bufs[12] = {};
+    int64_t tm_cap_T = 0, tm_cap_P = 0;
     // FNO1d state
     nfx::Fno1dPlan plan1{};
     int pt_n[nfx::kFno1dMaxLayers] = {};   // per-token table sizes (locs.i.output)
@@ -782,13 +787,145 @@ int fno1d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
 }
 
 // ---------------------------------------------------------------------------
+// TokenMixer2D (fno.cpp:1756-1956)
+// ---------------------------------------------------------------------------
+const char* kTmParts[8] = {"ln1", "q_proj", "k_proj", "v_proj", "o_proj", "ln2", "ffn0", "ffn1"};
+
+int tm2d_create(nfx_runtime* rt) {
+    // the reference runtime builds TokenMixer2D from the raw weights and ignores NIRQ
+    // (runtime.cpp:61-64)
+    auto& m = rt->model;
+    auto& pl = rt->plan_tm;
+    const int* c = m.cfg;
+    pl.in_d = c[0];
+    pl.out_d = c[1];
+    pl.L = c[2];
+    pl.h = c[3];
+    pl.w = c[4];
+    pl.NP = c[5];
+    pl.heads = c[6];
+    pl.layers = c[7];
+    pl.act = m.activation == "relu" ? 1 : 0;
+    if (pl.layers < 1 || pl.layers > nfx::kTm2dMaxLayers) return NFX_OK;  // Run reports it
+    pl.se_w = wptr(rt, "slice_embed.proj.weight");
+    pl.se_b = wptr(rt, "slice_embed.proj.bias");
+    pl.un_w = wptr(rt, "unslice.proj.weight");
+    pl.un_b = wptr(rt, "unslice.proj.bias");
+    pl.head_w = wptr(rt, "head.weight");
+    pl.head_b = wptr(rt, "head.bias");
+    if (!pl.se_w || !pl.se_b || !pl.un_w || !pl.un_b || !pl.head_w || !pl.head_b)
+        return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+    for (int i = 0; i < pl.layers; ++i)
+        for (int j = 0; j < 8; ++j) {
+            const std::string pre = "blocks." + std::to_string(i) + "." + kTmParts[j];
+            pl.blk[i].w[j] = wptr(rt, pre + ".weight");
+            pl.blk[i].b[j] = wptr(rt, pre + ".bias");
+            if (!pl.blk[i].w[j] || !pl.blk[i].b[j]) return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+        }
+    return NFX_OK;
+}
+
+// EnableInt8Gemm for TokenMixer2D (no reference counterpart): q, k, v, o, ffn0, ffn1 of
+// every block need per-channel (axis 0) weight qparams in NIRQ; the weight codes follow
+// QuantiseWeight2D (fno.cpp:325-358) on the raw weights.
+void tm2d_enable_int8(nfx_runtime* rt) {
+    auto& m = rt->model;
+    auto& pl = rt->plan_tm;
+    if (!pl.se_w || !m.quant_enabled) return;
+    const int slots[6] = {1, 2, 3, 4, 6, 7};
+    for (int i = 0; i < pl.layers; ++i)
+        for (int j : slots) {
+            const std::string wn = "blocks." + std::to_string(i) + "." + kTmParts[j] + ".weight";
+            auto pc = m.weight_per_channel_qparams.find(wn);
+            if (pc == m.weight_per_channel_qparams.end()) return;
+            const auto& t = m.weights.at(wn);
+            if (!nfx::gemm_i8_supported(static_cast<int>(t.shape[1]), static_cast<int>(t.shape[0]))) return;
+        }
+    for (int i = 0; i < pl.layers; ++i)
+        for (int j : slots) {
+            const std::string wn = "blocks." + std::to_string(i) + "." + kTmParts[j] + ".weight";
+            const auto& pc = m.weight_per_channel_qparams.at(wn);
+            std::vector<int8_t> codes;
+            std::vector<int32_t> sum_w;
+            if (!nfx::quantise_weight_2d(m.weights.at(wn), pc, codes, sum_w)) return;
+            auto& q = pl.blk[i].q8[j];
+            q.Wq = upload(rt, codes.data(), codes.size());
+            q.scale_w = upload(rt, pc.scales.data(), pc.scales.size());
+            q.zp_w = upload(rt, pc.zero_points.data(), pc.zero_points.size());
+            q.sum_w = upload(rt, sum_w.data(), sum_w.size());
+            if (!q.Wq || !q.scale_w || !q.zp_w || !q.sum_w) return;
+        }
+    pl.int8 = 1;
+    rt->int8_enabled = true;
+}
+
+int check_tm2d_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t* ys, int yr) {
+    const auto& pl = rt->plan_tm;
+    if (xr != 4) return rt_fail(rt, NFX_SHAPE_MISMATCH, "TokenMixer2D: expected 4D x (batch, h, w, in_dim)");
+    if (xs[3] != pl.in_d) return rt_fail(rt, NFX_SHAPE_MISMATCH, "TokenMixer2D: input feature dim mismatch");
+    if (xs[1] != pl.h || xs[2] != pl.w) return rt_fail(rt, NFX_SHAPE_MISMATCH, "TokenMixer2D: h / w mismatch");
+    if (yr != 4 || ys[0] != xs[0] || ys[1] != xs[1] || ys[2] != xs[2] || ys[3] != pl.out_d)
+        return rt_fail(rt, NFX_SHAPE_MISMATCH, "TokenMixer2D: output buffer shape mismatch");
+    if (pl.NP <= 0 || (pl.h * pl.w) % pl.NP != 0)
+        return rt_fail(rt, NFX_INVALID_ARG, "TokenMixer2D: h*w must be a multiple of n_patches");
+    if (pl.heads <= 0 || pl.L % pl.heads != 0)
+        return rt_fail(rt, NFX_INVALID_ARG, "TokenMixer2D: latent_dim must be a multiple of n_heads");
+    if (pl.layers < 1) return rt_fail(rt, NFX_INVALID_ARG, "TokenMixer2D: n_layers must be >= 1");
+    if (pl.layers > nfx::kTm2dMaxLayers || !pl.se_w)
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, "TokenMixer2D GPU executor: at most 8 blocks");
+    if (const char* why = nfx::tm2d_unsupported(pl.L, pl.heads, pl.in_d, pl.out_d))
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, why);
+    return NFX_OK;
+}
+
+int tm2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
+    auto& pl0 = rt->plan_tm;
+    const int B = static_cast<int>(xs[0]);
+    if (B == 0) return NFX_OK;
+    const int64_t T = static_cast<int64_t>(B) * pl0.NP;
+    const int64_t P = static_cast<int64_t>(B) * pl0.h * pl0.w;
+    const int L = pl0.L;
+    if (T > rt->tm_cap_T || P > rt->tm_cap_P) {
+        for (auto*& p : rt->tm_bufs) {
+            if (p) cudaFree(p);
+            p = nullptr;
+        }
+        const int64_t sizes[12] = {T * pl0.in_d * 4, T * L * 4, T * L * 4, T * L * 4, T * L * 4, T * L * 4,
+                                   T * L * 4, T * 2 * L * 4, T * L * 4, P * L * 4, T * 2 * L, T * 8};
+        for (int i = 0; i < 12; ++i)
+            if (!cuda_ok(rt, cudaMalloc(&rt->tm_bufs[i], static_cast<size_t>(sizes[i]) + 256), "cudaMalloc activations"))
+                return NFX_INTERNAL;
+        rt->tm_cap_T = T;
+        rt->tm_cap_P = P;
+    }
+    nfx::Tm2dPlan pl = pl0;
+    pl.B = B;
+    pl.x = dx;
+    pl.y = dy;
+    float** f[10] = {&pl.pooled, &pl.tok, &pl.ln, &pl.q, &pl.k, &pl.v, &pl.ho, &pl.f0, &pl.f1, &pl.feat};
+    for (int i = 0; i < 10; ++i) *f[i] = static_cast<float*>(rt->tm_bufs[i]);
+    pl.codes = static_cast<int8_t*>(rt->tm_bufs[10]);
+    pl.row_s = static_cast<float*>(rt->tm_bufs[11]);
+    pl.row_zp = reinterpret_cast<int32_t*>(static_cast<char*>(rt->tm_bufs[11]) + T * 4);
+    pl.err = nfx::device_error_word();
+    if (!pl.err) return rt_fail(rt, NFX_INTERNAL, "no device error word");
+    pl.timer = rt->timer.get();
+    const cudaError_t e = nfx::tm2d_run(pl, st);
+    if (e != cudaSuccess)
+        return rt_fail(rt, NFX_INTERNAL, std::string("TokenMixer2D launch failed: ") + cudaGetErrorString(e));
+    return NFX_OK;
+}
+
+// ---------------------------------------------------------------------------
 // op dispatch of Run / RunDevice
 // ---------------------------------------------------------------------------
 int check_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t* ys, int yr) {
     if (rt->model.op == "FNO2d") return check_fno2d_shapes(rt, xs, xr, ys, yr);
     if (rt->model.op == "FNO1d") return check_fno1d_shapes(rt, xs, xr, ys, yr);
-    return rt_fail(rt, NFX_UNSUPPORTED_OP,
-                   "the GPU runtime executes FNO1d and FNO2d through Run; op is " + rt->model.op);
+    if (rt->model.op == "FNO3d")
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, "the GPU runtime does not execute FNO3d yet");
+    // runtime.cpp:97-100: Run serves the FNO family only
+    return rt_fail(rt, NFX_INTERNAL, "runtime does not support op: " + rt->model.op);
 }
 
 int launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
@@ -890,6 +1027,9 @@ int nfx_runtime_create(const char* ir_path, int device, nfx_runtime** out) {
     } else if (op == "FNO1d") {
         s = fno1d_create(rt.get());
         if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
+    } else if (op == "TokenMixer2D") {
+        s = tm2d_create(rt.get());
+        if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
     }
     if (!nfx::device_error_word())
         return nfx::set_thread_error(NFX_INTERNAL, "cannot allocate the device error word");
@@ -928,6 +1068,8 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
     for (void* p : rt->f1_bufs)
         if (p) cudaFree(p);
     for (void* p : rt->f2_bufs)
+        if (p) cudaFree(p);
+    for (void* p : rt->tm_bufs)
         if (p) cudaFree(p);
     for (auto* p : rt->f2_tw)
         if (p) cudaFree(p);
@@ -981,6 +1123,7 @@ void nfx_runtime_enable_int8_gemm(nfx_runtime* rt) {
     DeviceGuard g(rt->device);
     if (rt->model.op == "FNO2d") fno2d_enable_int8(rt);
     if (rt->model.op == "FNO1d") fno1d_enable_int8(rt);
+    if (rt->model.op == "TokenMixer2D") tm2d_enable_int8(rt);
 }
 
 int nfx_runtime_is_int8_gemm_enabled(const nfx_runtime* rt) { return rt && rt->int8_enabled ? 1 : 0; }
@@ -1040,6 +1183,53 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
     if (!cuda_ok(rt, cudaMemcpyAsync(rt->dx, x, nx * 4, cudaMemcpyHostToDevice, rt->stream), "H2D"))
         return NFX_INTERNAL;
     s = launch(rt, rt->dx, x_shape, rt->dy, rt->stream);
+    if (s != NFX_OK) return s;
+    if (!cuda_ok(rt, cudaMemcpyAsync(y, rt->dy, ny * 4, cudaMemcpyDeviceToHost, rt->stream), "D2H"))
+        return NFX_INTERNAL;
+    if (!cuda_ok(rt, cudaStreamSynchronize(rt->stream), "execution")) return NFX_INTERNAL;
+    return nfx_runtime_check(rt);
+}
+
+int nfx_runtime_run_tokenmixer2d_device(nfx_runtime* rt, const float* x, const int64_t* x_shape,
+                                        int x_rank, float* y, const int64_t* y_shape, int y_rank,
+                                        void* stream) {
+    if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
+    if (!x_shape || !y_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
+    DeviceGuard g(rt->device);
+    if (rt->model.op != "TokenMixer2D") return rt_fail(rt, NFX_INTERNAL, "TokenMixer2D not initialized");
+    int s = check_tm2d_shapes(rt, x_shape, x_rank, y_shape, y_rank);
+    if (s != NFX_OK) return s;
+    if (numel(x_shape, x_rank) > 0 && (!x || !y)) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
+    return tm2d_launch(rt, x, x_shape, y, static_cast<cudaStream_t>(stream));
+}
+
+int nfx_runtime_run_tokenmixer2d(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
+                                 float* y, const int64_t* y_shape, int y_rank) {
+    if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
+    if (!x_shape || !y_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
+    DeviceGuard g(rt->device);
+    if (rt->model.op != "TokenMixer2D") return rt_fail(rt, NFX_INTERNAL, "TokenMixer2D not initialized");
+    int s = check_tm2d_shapes(rt, x_shape, x_rank, y_shape, y_rank);
+    if (s != NFX_OK) return s;
+    const size_t nx = static_cast<size_t>(numel(x_shape, x_rank));
+    const size_t ny = static_cast<size_t>(numel(y_shape, y_rank));
+    if (nx == 0) return NFX_OK;
+    if (!x || !y) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
+    if (nx > rt->dx_cap) {
+        if (rt->dx) cudaFree(rt->dx);
+        rt->dx = nullptr;
+        if (!cuda_ok(rt, cudaMalloc(&rt->dx, nx * 4), "cudaMalloc input")) return NFX_INTERNAL;
+        rt->dx_cap = nx;
+    }
+    if (ny > rt->dy_cap) {
+        if (rt->dy) cudaFree(rt->dy);
+        rt->dy = nullptr;
+        if (!cuda_ok(rt, cudaMalloc(&rt->dy, ny * 4), "cudaMalloc output")) return NFX_INTERNAL;
+        rt->dy_cap = ny;
+    }
+    if (!cuda_ok(rt, cudaMemcpyAsync(rt->dx, x, nx * 4, cudaMemcpyHostToDevice, rt->stream), "H2D"))
+        return NFX_INTERNAL;
+    s = tm2d_launch(rt, rt->dx, x_shape, rt->dy, rt->stream);
     if (s != NFX_OK) return s;
     if (!cuda_ok(rt, cudaMemcpyAsync(y, rt->dy, ny * 4, cudaMemcpyDeviceToHost, rt->stream), "D2H"))
         return NFX_INTERNAL;

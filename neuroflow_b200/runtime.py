@@ -61,20 +61,44 @@ class InferenceRuntime:
         if rc != 0:
             raise RuntimeError("Run failed: " + self._err())
 
+    def run_tokenmixer2d(self, x: np.ndarray, y: np.ndarray) -> None:
+        """The reference's `run_tokenmixer2d` (x (B, h, w, in_dim) -> y in place)."""
+        if not (isinstance(y, np.ndarray) and y.dtype == np.float32 and y.flags.c_contiguous):
+            raise RuntimeError("RunTokenMixer2D failed: y must be a C-contiguous float32 array")
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rc = _lib.nfx_runtime_run_tokenmixer2d(self._h, x.ctypes.data_as(C.c_void_p), _shape(x),
+                                               x.ndim, y.ctypes.data_as(C.c_void_p), _shape(y),
+                                               y.ndim)
+        if rc != 0:
+            raise RuntimeError("RunTokenMixer2D failed: " + self._err())
+
+    @staticmethod
+    def _stream(x, stream):
+        import torch
+        if stream is None:
+            return torch.cuda.current_stream(x.device).cuda_stream
+        return stream.cuda_stream if hasattr(stream, "cuda_stream") else stream
+
     def run_device(self, x, y, stream=None) -> None:
         """x, y: CUDA float32 tensors on this runtime's device; asynchronous on `stream`
         (a torch.cuda.Stream or raw handle; default: the current torch stream)."""
-        import torch
-        if stream is None:
-            stream = torch.cuda.current_stream(x.device).cuda_stream
-        elif hasattr(stream, "cuda_stream"):
-            stream = stream.cuda_stream
+        stream = self._stream(x, stream)
         xs = (C.c_int64 * x.dim())(*x.shape)
         ys = (C.c_int64 * y.dim())(*y.shape)
         rc = _lib.nfx_runtime_run_device(self._h, C.c_void_p(x.data_ptr()), xs, x.dim(),
                                          C.c_void_p(y.data_ptr()), ys, y.dim(), C.c_void_p(stream))
         if rc != 0:
             raise RuntimeError("Run failed: " + self._err())
+
+    def run_tokenmixer2d_device(self, x, y, stream=None) -> None:
+        stream = self._stream(x, stream)
+        xs = (C.c_int64 * x.dim())(*x.shape)
+        ys = (C.c_int64 * y.dim())(*y.shape)
+        rc = _lib.nfx_runtime_run_tokenmixer2d_device(self._h, C.c_void_p(x.data_ptr()), xs,
+                                                      x.dim(), C.c_void_p(y.data_ptr()), ys,
+                                                      y.dim(), C.c_void_p(stream))
+        if rc != 0:
+            raise RuntimeError("RunTokenMixer2D failed: " + self._err())
 
     def profile(self, enable: bool = True) -> None:
         """Enable (and reset) or disable per-kernel CUDA-event timing."""
