@@ -315,6 +315,93 @@ def run_nfx(args, ws, rank, local):
     return result, rt, x_host, path
 
 
+# Other BASELINE configurations, timed the same way (device-resident inputs, CUDA
+# events on the launch stream) for the per-config numbers; not the driver's line.
+AUX = {
+    "fno1d": dict(metric="FNO1d samples/s", op="FNO1d", batch=64,
+                  workload="configs[0] FNO1d, n=1024, width 64, 16 modes, 4 layers, per-channel "
+                           "weights, per-token activations (the reference runs its FP32 Linear "
+                           "with per-token fake-quant for this IR; EnableInt8Gemm declines)"),
+    "fno1d_int8": dict(metric="FNO1d INT8 samples/s", op="FNO1d", batch=64,
+                       workload="configs[0] geometry with per-tensor activations: the reference's "
+                                "INT8 LinearForwardBatched dispatch (EnableInt8Gemm)"),
+    "fno2d_fp32": dict(metric="FNO2d FP32 fake-quant samples/s", op="FNO2d", batch=256,
+                       workload="configs[2] geometry without EnableInt8Gemm: the reference FNO2d "
+                                "Run (fp32 with fake-quant at the four .output boundaries)"),
+    "tm2d": dict(metric="TokenMixer2D FP32 samples/s", op="TokenMixer2D", batch=32,
+                 workload="configs[4] TokenMixer2D, 64x64 grid = 4096 tokens, latent 128, "
+                          "4 heads, 4 blocks (the reference RunTokenMixer2D arithmetic)"),
+    "tm2d_int8": dict(metric="TokenMixer2D INT8 samples/s", op="TokenMixer2D", batch=32,
+                      workload="configs[4] with the INT8 per-token q/k/v/o/ffn layers"),
+}
+
+
+def aux_model(name: str) -> str:
+    from neuroflow_b200 import ir, synth
+    key = hashlib.sha1(json.dumps([name, "v1"]).encode()).hexdigest()[:12]
+    path = os.path.join(tempfile.gettempdir(), f"nfx_bench_{name}_{key}.nneuroir")
+    if os.path.exists(path):
+        return path
+    if name in ("fno1d", "fno1d_int8"):
+        m = synth.fno1d_model(0, per_token=(name == "fno1d"))
+    elif name == "fno2d_fp32":
+        return model_path(0)
+    else:
+        m = synth.tm2d_model(0)
+    tmp = path + f".{os.getpid()}"
+    ir.write(tmp, m)
+    os.replace(tmp, path)
+    return path
+
+
+def run_aux(args):
+    import torch
+    from neuroflow_b200 import synth
+    from neuroflow_b200.runtime import InferenceRuntime
+    spec = AUX[args.workload]
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    B = spec["batch"]
+    rng = np.random.default_rng(100)
+    if spec["op"] == "FNO1d":
+        x = synth.fno1d_inputs(rng, B, 1024)
+    elif spec["op"] == "FNO2d":
+        x = inputs(100, B)
+    else:
+        x = synth.tm2d_inputs(rng, B, 64, 64)
+    rt = InferenceRuntime(aux_model(args.workload), 0)
+    if args.workload in ("fno1d", "fno1d_int8", "tm2d_int8"):
+        rt.enable_int8_gemm()
+    dx = torch.from_numpy(x).to(device)
+    dy = torch.empty(tuple(x.shape[:-1]) + (1,), dtype=torch.float32, device=device)
+    stream = torch.cuda.Stream(device)
+    run = rt.run_tokenmixer2d_device if spec["op"] == "TokenMixer2D" else rt.run_device
+    for _ in range(args.warmup):
+        run(dx, dy, stream)
+    torch.cuda.synchronize()
+    rt.check()
+    rt.profile(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            run(dx, dy, stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    prof = rt.profile_read()
+    rt.profile(False)
+    rt.check()
+    tot = sum(v[1] for v in prof.values())
+    line = {"metric": spec["metric"], "value": round(B * args.steps / (ms * 1e-3), 1),
+            "unit": "samples/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+            "data": "synthetic", "config": {"workload": spec["workload"], "batch": B},
+            "kernel_share": {k: round(v[1] / tot, 3) for k, v in prof.items()},
+            "gpu_launches": sum(v[0] for v in prof.values()), "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -327,7 +414,13 @@ def main():
     ap.add_argument("--batch", type=int, default=CFG["batch"],
                     help="samples per GPU (default: the configs[2] batch of 256; smaller "
                          "values only for profiling captures)")
+    ap.add_argument("--workload", default="fno2d_int8", choices=["fno2d_int8"] + sorted(AUX),
+                    help="fno2d_int8 (default): the headline configs[2] line; the others time "
+                         "the remaining BASELINE configurations on one GPU")
     args = ap.parse_args()
+    if args.workload != "fno2d_int8" and args.impl == "nfx":
+        run_aux(args)
+        return
 
     if args.impl == "reference":
         # host-only arm: no process group; under torchrun rank 0 alone runs and prints

@@ -194,8 +194,8 @@ __global__ void __launch_bounds__(kQ) attention_kernel(const float* __restrict__
                                                        const float* __restrict__ V, int NP, int L,
                                                        float scale, float* __restrict__ out) {
     constexpr int kKeys = HD <= 32 ? 128 : 64;  // 32 KB of K and V per chunk
-    __shared__ float sK[kKeys][HD];
-    __shared__ float sV[kKeys][HD];
+    __shared__ float4 sK[kKeys][HD / 4];  // 16-byte broadcast loads in the inner loops
+    __shared__ float4 sV[kKeys][HD / 4];
     const int b = blockIdx.z, head = blockIdx.y;
     const int i = blockIdx.x * kQ + threadIdx.x;
     const bool live = i < NP;
@@ -207,13 +207,20 @@ __global__ void __launch_bounds__(kQ) attention_kernel(const float* __restrict__
     auto score = [&](int jj) {
         float s = 0.0f;
 #pragma unroll
-        for (int d = 0; d < HD; ++d) s = linear_step(s, q[d], sK[jj][d], d >= nu);
+        for (int d4 = 0; d4 < HD / 4; ++d4) {
+            const float4 k4 = sK[jj][d4];
+            s = linear_step(s, q[4 * d4 + 0], k4.x, 4 * d4 + 0 >= nu);
+            s = linear_step(s, q[4 * d4 + 1], k4.y, 4 * d4 + 1 >= nu);
+            s = linear_step(s, q[4 * d4 + 2], k4.z, 4 * d4 + 2 >= nu);
+            s = linear_step(s, q[4 * d4 + 3], k4.w, 4 * d4 + 3 >= nu);
+        }
         return __fmul_rn(s, scale);
     };
-    auto load = [&](float (*dst)[HD], const float* src, int j0) {
+    auto load = [&](float4 (*dst)[HD / 4], const float* src, int j0) {
+        float* flat = reinterpret_cast<float*>(dst);
         for (int t = threadIdx.x; t < kKeys * HD; t += kQ) {
             const int jj = t / HD, d = t % HD;
-            dst[jj][d] = j0 + jj < NP ? src[base + static_cast<int64_t>(j0 + jj) * L + d] : 0.0f;
+            flat[t] = j0 + jj < NP ? src[base + static_cast<int64_t>(j0 + jj) * L + d] : 0.0f;
         }
     };
     // pass 1: row max (fno.cpp:1444-1447)
@@ -222,6 +229,7 @@ __global__ void __launch_bounds__(kQ) attention_kernel(const float* __restrict__
         load(sK, K, j0);
         __syncthreads();
         const int n = min(kKeys, NP - j0);
+#pragma unroll 2
         for (int jj = 0; jj < n; ++jj) {
             const float s = score(jj);
             if (j0 + jj == 0) mx = s;
@@ -235,6 +243,7 @@ __global__ void __launch_bounds__(kQ) attention_kernel(const float* __restrict__
         load(sK, K, j0);
         __syncthreads();
         const int n = min(kKeys, NP - j0);
+#pragma unroll 2
         for (int jj = 0; jj < n; ++jj) sum = __fadd_rn(sum, expf(__fsub_rn(score(jj), mx)));
         __syncthreads();
     }
@@ -253,7 +262,13 @@ __global__ void __launch_bounds__(kQ) attention_kernel(const float* __restrict__
             const float p = __fmul_rn(expf(__fsub_rn(score(jj), mx)), inv);
             const bool fused = j0 + jj >= av_vec;
 #pragma unroll
-            for (int d = 0; d < HD; ++d) acc[d] = linear_step(acc[d], p, sV[jj][d], fused);
+            for (int d4 = 0; d4 < HD / 4; ++d4) {
+                const float4 v4 = sV[jj][d4];
+                acc[4 * d4 + 0] = linear_step(acc[4 * d4 + 0], p, v4.x, fused);
+                acc[4 * d4 + 1] = linear_step(acc[4 * d4 + 1], p, v4.y, fused);
+                acc[4 * d4 + 2] = linear_step(acc[4 * d4 + 2], p, v4.z, fused);
+                acc[4 * d4 + 3] = linear_step(acc[4 * d4 + 3], p, v4.w, fused);
+            }
         }
         __syncthreads();
     }

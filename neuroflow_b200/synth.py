@@ -284,3 +284,92 @@ def tm2d_model(seed: int, in_dim=3, out_dim=1, latent=128, h=64, w=64, n_patches
 def tm2d_inputs(rng: np.random.Generator, n: int, h: int, w: int, in_dim: int = 3) -> np.ndarray:
     """(n, h, w, in_dim): a GRF field (spectrum as configs[2]) + grid coordinates."""
     return fno2d_inputs(rng, n, h, w, in_dim)
+
+
+# ------------------------------------------------------------------------- FNO3d
+def fno3d_inputs(rng: np.random.Generator, n: int, S: int, in_ch: int = 4) -> np.ndarray:
+    """(n, S, S, S, in_ch): a 3-D GRF (spectrum (|k|^2 + 4)^-2) + grid coordinates."""
+    x = np.empty((n, S, S, S, in_ch), np.float32)
+    x[..., 0] = grf3d(rng, n, S)
+    g = np.arange(S, dtype=np.float32) / S
+    if in_ch >= 2:
+        x[..., 1] = g[None, :, None, None]
+    if in_ch >= 3:
+        x[..., 2] = g[None, None, :, None]
+    if in_ch >= 4:
+        x[..., 3] = g[None, None, None, :]
+    for c in range(4, in_ch):
+        x[..., c] = grf3d(rng, n, S)
+    return x
+
+
+def fno3d_weights(rng, in_ch, out_ch, width, modes, L):
+    wts = {}
+    wts["lift.weight"], wts["lift.bias"] = _kaiming_linear(rng, width, in_ch)
+    s = 1.0 / (width * width)
+    for i in range(L):
+        for part in ("weights_real", "weights_imag"):
+            wts[f"specs.{i}.{part}"] = (s * rng.uniform(-1, 1, (width, width) + tuple(modes))).astype(np.float32)
+        wts[f"locs.{i}.weight"], wts[f"locs.{i}.bias"] = _kaiming_linear(rng, width, width)
+    wts["proj_q.weight"], wts["proj_q.bias"] = _kaiming_linear(rng, width, width)
+    wts["proj_out.weight"], wts["proj_out.bias"] = _kaiming_linear(rng, out_ch, width)
+    return wts
+
+
+def fno3d_linear_outputs(wts: dict, x: np.ndarray, L: int, modes) -> dict:
+    """Float32 FNO3d forward (neuroflow/nn/fno3d.py structure: torch.fft, exact GELU)
+    returning every Linear's output."""
+    import torch
+    import torch.nn.functional as F
+
+    def lin(t, name):
+        return t @ torch.from_numpy(wts[name + ".weight"]).T + torch.from_numpy(wts[name + ".bias"])
+
+    mh, mw, md = modes
+    obs = {}
+    with torch.no_grad():
+        h = lin(torch.from_numpy(x), "lift")
+        obs["lift.output"] = h.numpy().copy()
+        h = h.permute(0, 4, 1, 2, 3)
+        S = h.shape[-3:]
+        for i in range(L):
+            xf = torch.fft.rfftn(h, dim=(-3, -2, -1))[..., :mh, :mw, :md]
+            wgt = torch.complex(torch.from_numpy(wts[f"specs.{i}.weights_real"]),
+                                torch.from_numpy(wts[f"specs.{i}.weights_imag"]))
+            of = torch.einsum("bixyz,ioxyz->boxyz", xf, wgt)
+            of = F.pad(of, (0, S[2] // 2 + 1 - md, 0, S[1] - mw, 0, S[0] - mh))
+            x1 = torch.fft.irfftn(of, s=S, dim=(-3, -2, -1))
+            x2 = lin(h.permute(0, 2, 3, 4, 1), f"locs.{i}")
+            obs[f"locs.{i}.output"] = x2.numpy().copy()
+            h = F.gelu(x1 + x2.permute(0, 4, 1, 2, 3))
+        q = lin(h.permute(0, 2, 3, 4, 1), "proj_q")
+        obs["proj_q.output"] = q.numpy().copy()
+        y = lin(F.gelu(q), "proj_out")
+        obs["proj_out.output"] = y.numpy().copy()
+    return obs
+
+
+def fno3d_model(seed: int, in_ch=4, out_ch=1, width=32, modes=(8, 8, 8), L=4, S=64,
+                n_calib=4, calib_chunk=2) -> ir.Model:
+    """A random-init FNO3d (configs[3] shape by default) with FP8 E4M3 per-tensor scales
+    (amax / 448, compute_fp8_e4m3_qparams, static_quant.py:338-352) for every Linear
+    output over a separate calibration batch and for every Linear weight, as NIRQ
+    kind-3 entries.  The reference runtime ignores NIRQ for FNO3d."""
+    rng = np.random.default_rng(seed)
+    wts = fno3d_weights(rng, in_ch, out_ch, width, modes, L)
+    crng = np.random.default_rng(seed + 1)
+    amax = {}
+    done = 0
+    while done < n_calib:
+        nb = min(calib_chunk, n_calib - done)
+        xc = fno3d_inputs(crng, nb, S, in_ch)
+        for k, v in fno3d_linear_outputs(wts, xc, L, modes).items():
+            amax[k] = max(amax.get(k, 0.0), float(np.abs(v).max()))
+        done += nb
+    qp = {k: quant.fp8_qparams(np.array([v], np.float32)) for k, v in amax.items()}
+    for name, t in wts.items():
+        if name.endswith(".weight"):
+            qp[name] = quant.fp8_qparams(t)
+    cfg = dict(in_channels=in_ch, out_channels=out_ch, width=width, modes_h=modes[0],
+               modes_w=modes[1], modes_d=modes[2], n_layers=L, pad_factor=1)
+    return ir.Model(op="FNO3d", config=cfg, weights=wts, qparams=qp, quant_enabled=True)

@@ -84,6 +84,18 @@ class _TM2D(C.Structure):
                    ("pc_s", (_f32p * 8) * MAX_LAYERS), ("pc_zp", (_i32p * 8) * MAX_LAYERS)])
 
 
+class _FNO3d(C.Structure):
+    _fields_ = ([(n, C.c_int32) for n in ("in_ch", "out_ch", "width", "modes_h", "modes_w",
+                                          "modes_d", "n_layers", "pad_factor", "relu")]
+                + [(n, _f32p) for n in ("lift_w", "lift_b", "proj_q_w", "proj_q_b",
+                                        "proj_out_w", "proj_out_b")]
+                + [(n, _f32p * MAX_LAYERS) for n in ("spec_wr", "spec_wi", "loc_w", "loc_b")]
+                + [(n, C.c_float) for n in ("s_lift_w", "s_proj_q_w", "s_proj_out_w")]
+                + [("s_loc_w", C.c_float * MAX_LAYERS)]
+                + [(n, C.c_float) for n in ("s_lift", "s_proj_q", "s_proj_out")]
+                + [("s_locs", C.c_float * MAX_LAYERS)])
+
+
 class _Taps(C.Structure):
     _fields_ = [("codes_in", _i8p * (MAX_LAYERS + 1)), ("x1_out", _f32p * MAX_LAYERS),
                 ("h_out", _f32p * MAX_LAYERS)]
@@ -100,6 +112,13 @@ class Oracle:
         L.nfo_fno2d_forward.restype = C.c_int
         L.nfo_fno2d_forward.argtypes = [C.POINTER(_FNO2d), C.c_int, _f32p, C.c_int, C.c_int,
                                         C.c_int, _f32p, C.POINTER(_Taps)]
+        L.nfo_fno3d_forward.restype = C.c_int
+        L.nfo_fno3d_forward.argtypes = [C.POINTER(_FNO3d), C.c_int, _f32p, C.c_int, C.c_int,
+                                        C.c_int, C.c_int, _f32p]
+        L.nfo_fp32_to_e4m3.restype = C.c_uint8
+        L.nfo_fp32_to_e4m3.argtypes = [C.c_float]
+        L.nfo_e4m3_to_fp32.restype = C.c_float
+        L.nfo_e4m3_to_fp32.argtypes = [C.c_uint8]
         L.nfo_tm2d_forward.restype = C.c_int
         L.nfo_tm2d_forward.argtypes = [C.POINTER(_TM2D), C.c_int, _f32p, C.c_int, _f32p]
         L.nfo_fno1d_forward.restype = C.c_int
@@ -262,6 +281,61 @@ class Oracle:
             raise RuntimeError(f"nfo_tm2d_forward failed: {rc}")
         del keep
         return y
+
+
+    # -- FP8 E4M3 / FNO3d ------------------------------------------------------------
+    def fp32_to_e4m3(self, x):
+        x = _c(x, np.float32).ravel()
+        out = np.empty(x.size, np.uint8)
+        self.lib.nfo_fp32_to_e4m3_array(_p(x), out.ctypes.data_as(C.c_void_p), C.c_int64(x.size))
+        return out
+
+    def fno3d_forward(self, model, x, fp8: bool = False):
+        """mode 0 (fp8=False): the reference FNO3d::Forward; fp8=True: the E4M3 variant."""
+        x = _c(x, np.float32)
+        st, keep = build_fno3d_struct(model)
+        y = np.empty(x.shape[:-1] + (model.config["out_channels"],), np.float32)
+        B, H, W, D, _ = x.shape
+        rc = self.lib.nfo_fno3d_forward(C.byref(st), 1 if fp8 else 0, _p(x), B, H, W, D, _p(y))
+        if rc != 0:
+            raise RuntimeError(f"nfo_fno3d_forward failed: {rc}")
+        del keep
+        return y
+
+
+def build_fno3d_struct(model):
+    from neuroflow_b200 import ir
+    cfg, w = model.config, model.weights
+    keep = []
+    st = _FNO3d()
+    for f, k in (("in_ch", "in_channels"), ("out_ch", "out_channels"), ("width", "width"),
+                 ("modes_h", "modes_h"), ("modes_w", "modes_w"), ("modes_d", "modes_d"),
+                 ("n_layers", "n_layers"), ("pad_factor", "pad_factor")):
+        setattr(st, f, cfg[k])
+    st.relu = 1 if model.activation == "relu" else 0
+
+    def arr(name):
+        a = _c(w[name], np.float32)
+        keep.append(a)
+        return _p(a)
+
+    def fs(name):
+        qp = model.qparams.get(name)
+        return float(qp.scale) if isinstance(qp, ir.FP8) else 1.0
+
+    for fld, nm in (("lift_w", "lift.weight"), ("lift_b", "lift.bias"),
+                    ("proj_q_w", "proj_q.weight"), ("proj_q_b", "proj_q.bias"),
+                    ("proj_out_w", "proj_out.weight"), ("proj_out_b", "proj_out.bias")):
+        setattr(st, fld, arr(nm))
+    st.s_lift_w, st.s_proj_q_w, st.s_proj_out_w = fs("lift.weight"), fs("proj_q.weight"), fs("proj_out.weight")
+    st.s_lift, st.s_proj_q, st.s_proj_out = fs("lift.output"), fs("proj_q.output"), fs("proj_out.output")
+    for i in range(cfg["n_layers"]):
+        for fld, nm in (("spec_wr", f"specs.{i}.weights_real"), ("spec_wi", f"specs.{i}.weights_imag"),
+                        ("loc_w", f"locs.{i}.weight"), ("loc_b", f"locs.{i}.bias")):
+            getattr(st, fld)[i] = arr(nm)
+        st.s_loc_w[i] = fs(f"locs.{i}.weight")
+        st.s_locs[i] = fs(f"locs.{i}.output")
+    return st, keep
 
 
 def build_tm2d_struct(model):

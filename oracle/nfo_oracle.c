@@ -1306,3 +1306,313 @@ int nfo_tm2d_forward(const nfo_tm2d* m, int mode, const float* x, int bsz, float
     free(xp);
     return 0;
 }
+
+/* ------------------------------------------------------------------------- */
+/* FP8 E4M3 (cpp/include/neuroflow/fp8_e4m3.h)                                */
+/* ------------------------------------------------------------------------- */
+
+/* fp8_e4m3.h:106-221 fp32_to_e4m3_bits.  NaN -> 0x7F; +-inf -> +-448; +-0 keeps its
+ * sign.  Normal inputs: the 23-bit mantissa is rounded to 3 bits, half to even on the
+ * 20 dropped bits, a carry bumps the exponent, and biased exponents above 15 saturate
+ * to +-448.  Inputs whose biased exponent is below 1 take the subnormal branch:
+ * round(|v| * 2^9) to nearest-even in double, clamped to [0, 7] -- the clamp keeps
+ * values in [7.5, 8) * 2^-9 at 7 * 2^-9 where an IEEE-style encoder gives 2^-6. */
+uint8_t nfo_fp32_to_e4m3(float v) {
+    if (isnan(v)) return 0x7F;
+    if (isinf(v)) return v < 0.0f ? 0xFE : 0x7E;
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    const uint32_t sign = u >> 31;
+    const uint32_t a = u & 0x7FFFFFFFu;
+    if (a == 0) return (uint8_t)(sign << 7);
+    const int e = (int)((a >> 23) & 0xFFu) - 127 + 7;
+    if (e < 1) {
+        float af;
+        memcpy(&af, &a, 4);
+        double r = nearbyint((double)af * 512.0);
+        if (r < 0.0) r = 0.0;
+        if (r > 7.0) r = 7.0;
+        return (uint8_t)((sign << 7) | (uint32_t)r);
+    }
+    uint32_t m = (a >> 20) & 7u;
+    const uint32_t rest = a & 0xFFFFFu;
+    if (rest > 0x80000u || (rest == 0x80000u && (m & 1u))) m += 1;
+    int ee = e;
+    if (m & 8u) {
+        m &= 7u;
+        ee += 1;
+    }
+    if (ee > 15) return (uint8_t)((sign << 7) | 0x7Eu);
+    return (uint8_t)((sign << 7) | ((uint32_t)ee << 3) | m);
+}
+
+/* fp8_e4m3.h:223-284 e4m3_bits_to_fp32. */
+float nfo_e4m3_to_fp32(uint8_t b) {
+    const uint32_t sign = (b >> 7) & 1u, ex = (b >> 3) & 0xFu, mt = b & 7u;
+    float v;
+    if (ex == 0xFu && mt == 7u) {
+        const uint32_t q = 0x7FC00000u | (sign << 31);
+        memcpy(&v, &q, 4);
+        return v;
+    }
+    if (ex == 0) {
+        if (mt == 0) return sign ? -0.0f : 0.0f;
+        v = ldexpf((float)mt, -9);
+        return sign ? -v : v;
+    }
+    const uint32_t u = (sign << 31) | ((ex + 120u) << 23) | (mt << 20);
+    memcpy(&v, &u, 4);
+    return v;
+}
+
+/* fp8_e4m3.h:312-334 per-tensor fake-quant: scale down by 1/scale, saturate to +-448,
+ * encode, decode, scale up. */
+void nfo_fp8_fake_quant(const float* in, float scale, float* out, int64_t n) {
+    const float inv = scale == 0.0f ? 1.0f : 1.0f / scale;
+    for (int64_t i = 0; i < n; ++i) {
+        float xs = in[i] * inv;
+        xs = xs > 448.0f ? 448.0f : (xs < -448.0f ? -448.0f : xs);
+        out[i] = nfo_e4m3_to_fp32(nfo_fp32_to_e4m3(xs)) * scale;
+    }
+}
+
+void nfo_fp32_to_e4m3_array(const float* in, uint8_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = nfo_fp32_to_e4m3(in[i]);
+}
+
+/* ------------------------------------------------------------------------- */
+/* FNO3d (fno.cpp:1031-1281)                                                  */
+/* ------------------------------------------------------------------------- */
+
+/* fno.cpp:1031-1090 SpectralConv3d on h (b, w, H, W, D). */
+void nfo_spectral_conv3d(const float* h, int bsz, int w, int H, int W, int D, int mh, int mw,
+                         int md, const float* w_real, const float* w_imag, float* out) {
+    const int half_d = D / 2 + 1;
+    const size_t vol = (size_t)H * W * half_d * 2;
+    float* Hs = (float*)malloc(sizeof(float) * vol * w);
+    float* Of = (float*)malloc(sizeof(float) * vol * w);
+    for (int bi = 0; bi < bsz; ++bi) {
+        memset(Of, 0, sizeof(float) * vol * w);
+        for (int wi = 0; wi < w; ++wi)
+            nfo_rfft3(h + ((int64_t)bi * w + wi) * H * W * D, H, W, D, Hs + (size_t)wi * vol);
+        for (int mi = 0; mi < mh; ++mi)
+            for (int mj = 0; mj < mw; ++mj)
+                for (int mk = 0; mk < md; ++mk)
+                    for (int wo = 0; wo < w; ++wo) {
+                        float sr = 0.0f, si = 0.0f;
+                        for (int wi = 0; wi < w; ++wi) {
+                            const float* hp = Hs + (size_t)wi * vol +
+                                              ((((int64_t)mi * W + mj) * half_d + mk) * 2);
+                            const int64_t k = ((((int64_t)wi * w + wo) * mh + mi) * mw + mj) * md + mk;
+                            const float hr = hp[0], hi = hp[1], wr = w_real[k], wim = w_imag[k];
+                            sr = sr + fmaf(hr, wr, -(hi * wim));
+                            si = si + fmaf(hr, wim, hi * wr);
+                        }
+                        float* op = Of + (size_t)wo * vol + ((((int64_t)mi * W + mj) * half_d + mk) * 2);
+                        op[0] = sr;
+                        op[1] = si;
+                    }
+        for (int wo = 0; wo < w; ++wo)
+            nfo_irfft3(Of + (size_t)wo * vol, H, W, D, out + ((int64_t)bi * w + wo) * H * W * D);
+    }
+    free(Of);
+    free(Hs);
+}
+
+/* FNO3d model: weights as loaded; fp8 scales for the FP8 variant. */
+typedef struct {
+    int32_t in_ch, out_ch, width, modes_h, modes_w, modes_d, n_layers, pad_factor, relu;
+    const float* lift_w;
+    const float* lift_b;
+    const float* proj_q_w;
+    const float* proj_q_b;
+    const float* proj_out_w;
+    const float* proj_out_b;
+    const float* spec_wr[NFO_MAX_LAYERS];
+    const float* spec_wi[NFO_MAX_LAYERS];
+    const float* loc_w[NFO_MAX_LAYERS];
+    const float* loc_b[NFO_MAX_LAYERS];
+    /* FP8 variant: per-tensor scales of the Linear weights and of the ".output" keys */
+    float s_lift_w, s_proj_q_w, s_proj_out_w;
+    float s_loc_w[NFO_MAX_LAYERS];
+    float s_lift, s_proj_q, s_proj_out;
+    float s_locs[NFO_MAX_LAYERS];
+} nfo_fno3d;
+
+/* E4M3 codes of in / scale as fp8_e4m3_per_tensor_fake_quant forms them: xq = the
+ * decoded E4M3 value, snapped = xq * scale (the fake-quantised value). */
+static void fp8_codes(const float* in, float scale, float* xq, float* snapped, int64_t n) {
+    const float inv = scale == 0.0f ? 1.0f : 1.0f / scale;
+    for (int64_t i = 0; i < n; ++i) {
+        float xs = in[i] * inv;
+        xs = xs > 448.0f ? 448.0f : (xs < -448.0f ? -448.0f : xs);
+        const float q = nfo_e4m3_to_fp32(nfo_fp32_to_e4m3(xs));
+        if (xq) xq[i] = q;
+        if (snapped) snapped[i] = q * scale;
+    }
+}
+
+/* the FP8 variant's local layer: exact products of E4M3 values summed in fp32 in k
+ * order, y = acc * (s_in * s_w) + bias */
+static void fp8_linear(const float* aq, const float* wq, const float* b, int64_t M, int K, int N,
+                       float sc, float* y) {
+    for (int64_t r = 0; r < M; ++r)
+        for (int o = 0; o < N; ++o) {
+            float acc = 0.0f;
+            for (int k = 0; k < K; ++k) acc += aq[r * K + k] * wq[(int64_t)o * K + k];
+            y[r * N + o] = acc * sc + b[o];
+        }
+}
+
+/* mode 0: FNO3d::Forward (fno.cpp:1096-1281), FP32, no quantisation (the reference
+ *         runtime builds FNO3d without its NIRQ block, runtime.cpp:51-54).
+ * mode 1: the FP8 E4M3 variant (no reference counterpart): Linear weights
+ *         fake-quantised to E4M3 per tensor at load (fp8_e4m3.h:312-334); the lift
+ *         output and every layer output (after the activation) become E4M3 codes with
+ *         the ".output" scale of the Linear that produced them (the FNO1d input-snap
+ *         convention, fno.cpp:488-508); the local layers and proj_q multiply the
+ *         E4M3 codes exactly and sum in fp32 in k order (fp8_linear);
+ *         locs.i.output, proj_q.output and proj_out.output are E4M3 fake-quantised
+ *         like FNO2d's boundaries (fno.cpp:810-844).
+ * x (b, H, W, D, in_ch) -> y (b, H, W, D, out_ch). */
+int nfo_fno3d_forward(const nfo_fno3d* m, int mode, const float* x, int bsz, int H0, int W0, int D0,
+                      float* y) {
+    const int w = m->width, mh = m->modes_h, mw = m->modes_w, md = m->modes_d, L = m->n_layers;
+    const int in_ch = m->in_ch, out_ch = m->out_ch;
+    if (L > NFO_MAX_LAYERS) return 1;
+    const int pw[3] = {H0, W0, D0};
+    for (int i = 0; i < 3; ++i)
+        if (pw[i] <= 0 || (pw[i] & (pw[i] - 1))) return 1;
+    float* lift_w = dup_floats(m->lift_w, (int64_t)w * in_ch);
+    float* pq_w = dup_floats(m->proj_q_w, (int64_t)w * w);
+    float* po_w = dup_floats(m->proj_out_w, (int64_t)out_ch * w);
+    float* pq_q = (float*)malloc(sizeof(float) * (size_t)w * w);
+    float* lw[NFO_MAX_LAYERS];
+    float* lq[NFO_MAX_LAYERS];
+    for (int i = 0; i < L; ++i) {
+        lw[i] = dup_floats(m->loc_w[i], (int64_t)w * w);
+        lq[i] = (float*)malloc(sizeof(float) * (size_t)w * w);
+    }
+    if (mode == 1) {
+        fp8_codes(lift_w, m->s_lift_w, NULL, lift_w, (int64_t)w * in_ch);
+        fp8_codes(pq_w, m->s_proj_q_w, pq_q, pq_w, (int64_t)w * w);
+        fp8_codes(po_w, m->s_proj_out_w, NULL, po_w, (int64_t)out_ch * w);
+        for (int i = 0; i < L; ++i) fp8_codes(lw[i], m->s_loc_w[i], lq[i], lw[i], (int64_t)w * w);
+    }
+    int64_t H = H0, W = W0, D = D0;
+    const int64_t P = H * W * D, M = (int64_t)bsz * P;
+    float* h = (float*)malloc(sizeof(float) * (size_t)(M * w));
+    nfo_linear(x, lift_w, m->lift_b, (int)M, in_ch, w, h);
+    float* hp = (float*)calloc((size_t)(M * w), sizeof(float));   /* channel-first values */
+    float* xq = (float*)calloc((size_t)(M * w), sizeof(float));   /* channel-first E4M3 codes */
+    if (mode == 1) fp8_codes(h, m->s_lift, NULL, h, M * w);
+    for (int64_t bi = 0; bi < bsz; ++bi)
+        for (int wi = 0; wi < w; ++wi)
+            for (int64_t p = 0; p < P; ++p) hp[(bi * w + wi) * P + p] = h[(bi * P + p) * w + wi];
+    if (mode == 1) fp8_codes(hp, m->s_lift, xq, NULL, M * w);  /* the codes of the snapped lift */
+    int64_t pad[3] = {0, 0, 0};
+    if (m->pad_factor > 1) {
+        const int pf = m->pad_factor;
+        const int64_t dims[3] = {H, W, D};
+        for (int i = 0; i < 3; ++i) pad[i] = (pf - (dims[i] % pf)) % pf;
+        if (pad[0] || pad[1] || pad[2]) {
+            const int64_t Hp = H + pad[0], Wp = W + pad[1], Dp = D + pad[2];
+            float* a = (float*)calloc((size_t)(bsz * w * Hp * Wp * Dp), sizeof(float));
+            float* b = (float*)calloc((size_t)(bsz * w * Hp * Wp * Dp), sizeof(float));
+            for (int64_t bw = 0; bw < (int64_t)bsz * w; ++bw)
+                for (int64_t hi = 0; hi < H; ++hi)
+                    for (int64_t wj = 0; wj < W; ++wj) {
+                        memcpy(a + ((bw * Hp + hi) * Wp + wj) * Dp, hp + ((bw * H + hi) * W + wj) * D,
+                               sizeof(float) * D);
+                        memcpy(b + ((bw * Hp + hi) * Wp + wj) * Dp, xq + ((bw * H + hi) * W + wj) * D,
+                               sizeof(float) * D);
+                    }
+            free(hp);
+            free(xq);
+            hp = a;
+            xq = b;
+            H = Hp;
+            W = Wp;
+            D = Dp;
+        }
+    }
+    const int64_t Pp = H * W * D, Mp = (int64_t)bsz * Pp;
+    float* x1 = (float*)malloc(sizeof(float) * (size_t)(Mp * w));
+    float* pin = (float*)malloc(sizeof(float) * (size_t)(Mp * w));
+    float* pout = (float*)malloc(sizeof(float) * (size_t)(Mp * w));
+    for (int i = 0; i < L; ++i) {
+        nfo_spectral_conv3d(hp, bsz, w, (int)H, (int)W, (int)D, mh, mw, md, m->spec_wr[i], m->spec_wi[i], x1);
+        const float* src = mode == 1 ? xq : hp;
+        for (int64_t bi = 0; bi < bsz; ++bi)
+            for (int64_t p = 0; p < Pp; ++p)
+                for (int wi = 0; wi < w; ++wi) pin[(bi * Pp + p) * w + wi] = src[(bi * w + wi) * Pp + p];
+        if (mode == 1) {
+            const float s_in = i == 0 ? m->s_lift : m->s_locs[i - 1];
+            fp8_linear(pin, lq[i], m->loc_b[i], Mp, w, w, s_in * m->s_loc_w[i], pout);
+            fp8_codes(pout, m->s_locs[i], NULL, pout, Mp * w);
+        } else {
+            nfo_linear(pin, lw[i], m->loc_b[i], (int)Mp, w, w, pout);
+        }
+        for (int64_t bi = 0; bi < bsz; ++bi)
+            for (int wi = 0; wi < w; ++wi)
+                for (int64_t p = 0; p < Pp; ++p) {
+                    const int64_t k = (bi * w + wi) * Pp + p;
+                    hp[k] = x1[k] + pout[(bi * Pp + p) * w + wi];
+                }
+        nfo_apply_activation(hp, Mp * w, m->relu);
+        if (mode == 1) fp8_codes(hp, m->s_locs[i], xq, hp, Mp * w);
+    }
+    if (pad[0] || pad[1] || pad[2]) {
+        const int64_t oh = H - pad[0], ow = W - pad[1], od = D - pad[2];
+        float* a = (float*)malloc(sizeof(float) * (size_t)(bsz * w * oh * ow * od));
+        float* b = (float*)malloc(sizeof(float) * (size_t)(bsz * w * oh * ow * od));
+        for (int64_t bw = 0; bw < (int64_t)bsz * w; ++bw)
+            for (int64_t hi = 0; hi < oh; ++hi)
+                for (int64_t wj = 0; wj < ow; ++wj) {
+                    memcpy(a + ((bw * oh + hi) * ow + wj) * od, hp + ((bw * H + hi) * W + wj) * D,
+                           sizeof(float) * od);
+                    memcpy(b + ((bw * oh + hi) * ow + wj) * od, xq + ((bw * H + hi) * W + wj) * D,
+                           sizeof(float) * od);
+                }
+        free(hp);
+        free(xq);
+        hp = a;
+        xq = b;
+        H = oh;
+        W = ow;
+        D = od;
+    }
+    float* hb = (float*)malloc(sizeof(float) * (size_t)(M * w));
+    const float* src = mode == 1 ? xq : hp;
+    for (int64_t bi = 0; bi < bsz; ++bi)
+        for (int64_t p = 0; p < P; ++p)
+            for (int wi = 0; wi < w; ++wi) hb[(bi * P + p) * w + wi] = src[(bi * w + wi) * P + p];
+    float* q = (float*)malloc(sizeof(float) * (size_t)(M * w));
+    if (mode == 1) {
+        const float s_in = L == 0 ? m->s_lift : m->s_locs[L - 1];
+        fp8_linear(hb, pq_q, m->proj_q_b, M, w, w, s_in * m->s_proj_q_w, q);
+        fp8_codes(q, m->s_proj_q, NULL, q, M * w);
+    } else {
+        nfo_linear(hb, pq_w, m->proj_q_b, (int)M, w, w, q);
+    }
+    nfo_apply_activation(q, M * w, m->relu);
+    nfo_linear(q, po_w, m->proj_out_b, (int)M, w, out_ch, y);
+    if (mode == 1) fp8_codes(y, m->s_proj_out, NULL, y, M * out_ch);
+    free(q);
+    free(hb);
+    free(pout);
+    free(pin);
+    free(x1);
+    free(xq);
+    free(hp);
+    free(h);
+    for (int i = 0; i < L; ++i) {
+        free(lw[i]);
+        free(lq[i]);
+    }
+    free(pq_q);
+    free(po_w);
+    free(pq_w);
+    free(lift_w);
+    return 0;
+}

@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "neuroflow/fft.h"
+#include "neuroflow/fp8_e4m3.h"
 #include "neuroflow/int8_gemm.h"
 #include "neuroflow/runtime.h"
 
@@ -109,6 +110,18 @@ void ref_rfft3(const float* x, int H, int W, int D, float* out) {
 }
 void ref_irfft3(const float* x, int H, int W, int D, float* out) {
     nflow::fft::Irfft3(x, H, W, D, out);
+}
+
+// fp8_e4m3.h:106-298 / :312-334 (header-only; the reference's own encoder and
+// per-tensor fake-quant)
+void ref_fp32_to_e4m3(const float* in, uint8_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = nflow::fp32_to_e4m3_bits(in[i]);
+}
+void ref_e4m3_to_fp32(const uint8_t* in, float* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = nflow::e4m3_bits_to_fp32(in[i]);
+}
+void ref_fp8_fake_quant(const float* in, float scale, float* out, int64_t n) {
+    nflow::fp8_e4m3_per_tensor_fake_quant(in, scale, out, static_cast<size_t>(n));
 }
 
 // int8_gemm.cpp:507-520

@@ -68,6 +68,22 @@ def test_golden_tm2d_network():
     assert np.array_equal(_bits(Oracle().tm2d_forward(m, d["x"])), _bits(d["y"]))
 
 
+def test_e4m3_known_answers():
+    """The reference's own FP8 known-answer cases (cpp/tests/test_fp8_e4m3.cpp:50-140)
+    and the F6 band: [7.5, 8) * 2^-9 stays at code 7 (an IEEE-style encoder gives 2^-6)."""
+    o = Oracle()
+    kat = [(0.0, 0x00), (-0.0, 0x80), (1.0, 0x38), (-1.0, 0xB8), (448.0, 0x7E),
+           (-448.0, 0xFE), (1.0625, 0x38), (1.1875, 0x3A), (1.10, 0x39), (1000.0, 0x7E),
+           (-1000.0, 0xFE), (float("inf"), 0x7E), (float("-inf"), 0xFE),
+           (float("nan"), 0x7F), (7.6 / 512, 0x07), (7.99 / 512, 0x07), (1.0 / 64, 0x08),
+           (3.0 / 512, 0x03)]
+    for v, b in kat:
+        assert o.lib.nfo_fp32_to_e4m3(v) == b, (v, hex(o.lib.nfo_fp32_to_e4m3(v)))
+    assert o.lib.nfo_e4m3_to_fp32(0x38) == 1.0 and o.lib.nfo_e4m3_to_fp32(0x7E) == 448.0
+    assert o.lib.nfo_e4m3_to_fp32(0x08) == 1.0 / 64
+    assert np.isnan(o.lib.nfo_e4m3_to_fp32(0x7F)) and np.isnan(o.lib.nfo_e4m3_to_fp32(0xFF))
+
+
 def test_golden_linear_forward_batched_and_quantiser():
     d = _g("int8_gemm.npz")
     o = Oracle()
@@ -218,6 +234,42 @@ def test_ref_tm2d_network_bitexact(tmp_path, kw):
         (2, kw["h"], kw["w"], kw.get("in_dim", 3))).astype(np.float32)
     want = Reference().run(p, x, kw.get("out_dim", 1), tokenmixer2d=True)
     assert np.array_equal(_bits(Oracle().tm2d_forward(m, x)), _bits(want))
+
+
+@needs_ref
+def test_ref_e4m3_encoder_sweep_bitexact():
+    """Every 97th float32 bit pattern (44 M values over all signs, exponents, NaN and
+    infinity) and every decode, against the reference header's encoder/decoder."""
+    import ctypes as C
+    o, r = Oracle(), Reference()
+    u = np.arange(0, 1 << 32, 97, dtype=np.uint64).astype(np.uint32)
+    f = u.view(np.float32)
+    want = np.empty(f.size, np.uint8)
+    r.lib.ref_fp32_to_e4m3(f.ctypes.data_as(C.c_void_p), want.ctypes.data_as(C.c_void_p),
+                           C.c_int64(f.size))
+    assert np.array_equal(o.fp32_to_e4m3(f), want)
+    codes = np.arange(256, dtype=np.uint8)
+    dec = np.empty(256, np.float32)
+    r.lib.ref_e4m3_to_fp32(codes.ctypes.data_as(C.c_void_p), dec.ctypes.data_as(C.c_void_p),
+                           C.c_int64(256))
+    mine = np.array([o.lib.nfo_e4m3_to_fp32(int(c)) for c in codes], np.float32)
+    assert np.array_equal(_bits(mine), _bits(dec))
+
+
+@needs_ref
+@pytest.mark.parametrize("kw", [dict(width=8, modes=(3, 3, 2), L=2, S=8),
+                                dict(width=12, modes=(2, 4, 3), L=1, S=16, in_ch=5)])
+def test_ref_fno3d_network_bitexact(tmp_path, kw):
+    m = synth.fno3d_model(4, n_calib=2, **kw)
+    p = str(tmp_path / "m.nneuroir")
+    ir.write(p, m)
+    x = synth.fno3d_inputs(np.random.default_rng(1), 2, kw["S"], kw.get("in_ch", 4))
+    want = Reference().run(p, x, 1)
+    o = Oracle()
+    assert np.array_equal(_bits(o.fno3d_forward(m, x)), _bits(want))
+    # the FP8 variant stays within the E4M3 rounding of the FP32 network
+    rel = np.linalg.norm(o.fno3d_forward(m, x, fp8=True) - want) / np.linalg.norm(want)
+    assert rel < 0.1
 
 
 @needs_ref
