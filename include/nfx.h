@@ -67,6 +67,14 @@ void nfx_runtime_enable_int8_gemm(nfx_runtime* rt);
 /* InferenceRuntime::IsInt8GemmEnabled (runtime.h:126-128). */
 int nfx_runtime_is_int8_gemm_enabled(const nfx_runtime* rt);
 
+/* Enable the FP8 E4M3 executor of FNO3d (per-tensor E4M3 weights, E4M3 activation codes
+ * between layers, E4M3 fake-quant at the ".output" boundaries; the scales are the
+ * NIRQ kind-3 entries of every Linear weight and ".output" key).  No counterpart in
+ * the reference (its FNO3d has no quantised path; the switch mirrors EnableInt8Gemm and
+ * is likewise a no-op when the IR lacks the scales). */
+void nfx_runtime_enable_fp8(nfx_runtime* rt);
+int nfx_runtime_is_fp8_enabled(const nfx_runtime* rt);
+
 /* InferenceRuntime::Run (runtime.h:76-79, runtime.cpp:85-101).  x and y are HOST
  * float32 row-major buffers owned by the caller; shapes as the reference's
  * FNO*::Forward checks them (batch first, channels last).  Synchronous. */

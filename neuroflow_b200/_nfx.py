@@ -46,6 +46,10 @@ if hasattr(lib, "nfx_runtime_create"):
     lib.nfx_runtime_run.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int]
     lib.nfx_runtime_run_device.restype = C.c_int
     lib.nfx_runtime_run_device.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int, _vp]
+    lib.nfx_runtime_enable_fp8.restype = None
+    lib.nfx_runtime_enable_fp8.argtypes = [_vp]
+    lib.nfx_runtime_is_fp8_enabled.restype = C.c_int
+    lib.nfx_runtime_is_fp8_enabled.argtypes = [_vp]
     lib.nfx_runtime_run_tokenmixer2d.restype = C.c_int
     lib.nfx_runtime_run_tokenmixer2d.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int]
     lib.nfx_runtime_run_tokenmixer2d_device.restype = C.c_int

@@ -182,6 +182,61 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
     return false;
 }
 
+uint8_t e4m3_encode(float v) {
+    if (std::isnan(v)) return 0x7F;
+    if (std::isinf(v)) return v < 0.0f ? 0xFE : 0x7E;
+    uint32_t u;
+    std::memcpy(&u, &v, 4);
+    const uint32_t sign = u >> 31, a = u & 0x7FFFFFFFu;
+    if (a == 0) return static_cast<uint8_t>(sign << 7);
+    const int e = static_cast<int>((a >> 23) & 0xFFu) - 120;
+    if (e < 1) {
+        float af;
+        std::memcpy(&af, &a, 4);
+        double r = std::nearbyint(static_cast<double>(af) * 512.0);
+        r = r < 0.0 ? 0.0 : (r > 7.0 ? 7.0 : r);
+        return static_cast<uint8_t>((sign << 7) | static_cast<uint32_t>(r));
+    }
+    uint32_t m = (a >> 20) & 7u;
+    const uint32_t rest = a & 0xFFFFFu;
+    if (rest > 0x80000u || (rest == 0x80000u && (m & 1u))) ++m;
+    int ee = e;
+    if (m & 8u) {
+        m &= 7u;
+        ++ee;
+    }
+    if (ee > 15) return static_cast<uint8_t>((sign << 7) | 0x7Eu);
+    return static_cast<uint8_t>((sign << 7) | (static_cast<uint32_t>(ee) << 3) | m);
+}
+
+float e4m3_decode(uint8_t b) {
+    const uint32_t sign = (b >> 7) & 1u, ex = (b >> 3) & 15u, mt = b & 7u;
+    float v;
+    if (ex == 15u && mt == 7u) {
+        const uint32_t q = 0x7FC00000u | (sign << 31);
+        std::memcpy(&v, &q, 4);
+        return v;
+    }
+    if (ex == 0u) {
+        v = std::ldexp(static_cast<float>(mt), -9);
+        return sign ? -v : v;
+    }
+    const uint32_t u = (sign << 31) | ((ex + 120u) << 23) | (mt << 20);
+    std::memcpy(&v, &u, 4);
+    return v;
+}
+
+void e4m3_fake_quant(const float* in, float scale, float* xq, float* out, size_t n) {
+    const float inv = scale == 0.0f ? 1.0f : 1.0f / scale;
+    for (size_t i = 0; i < n; ++i) {
+        float xs = in[i] * inv;
+        xs = xs > 448.0f ? 448.0f : (xs < -448.0f ? -448.0f : xs);
+        const float q = e4m3_decode(e4m3_encode(xs));
+        if (xq) xq[i] = q;
+        if (out) out[i] = q * scale;
+    }
+}
+
 std::vector<float> build_fft_twiddles(int n, bool inverse) {
     std::vector<float> t(2 * static_cast<size_t>(n > 1 ? n - 1 : 0));
     const float pi = static_cast<float>(3.14159265358979323846);

@@ -56,4 +56,11 @@ std::vector<float> build_act_table(float s, int zp, int act);
 //    interleaved re, im).
 std::vector<float> build_fft_twiddles(int n, bool inverse);
 
+// 4. E4M3 (fp8_e4m3.h:106-334), host side: the reference encoder (with its subnormal
+//    clamp), decoder, and the per-tensor fake-quant of a weight tensor.  `xq` receives
+//    the decoded E4M3 values, `out` the fake-quantised ones (either may be null).
+uint8_t e4m3_encode(float v);
+float e4m3_decode(uint8_t b);
+void e4m3_fake_quant(const float* in, float scale, float* xq, float* out, size_t n);
+
 }  // namespace nfx

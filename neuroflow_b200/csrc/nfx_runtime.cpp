@@ -18,6 +18,7 @@
 #include "../../include/nfx.h"
 #include "fno1d.h"
 #include "fno2d.h"
+#include "fno3d.h"
 #include "nfx_internal.h"
 #include "nfx_ir.h"
 #include "nfx_lut.h"
@@ -118,6 +119,13 @@ struct nfx_runtime {
     int64_t f2_cap[4] = {0, 0, 0, 0};
     float2* f2_tw[4] = {nullptr, nullptr, nullptr, nullptr};   // fwd W, inv W, fwd H, inv H
     int f2_tw_H = 0, f2_tw_W = 0;
+    // FNO3d state
+    nfx::Fno3dPlan plan3{};
+    bool fp8_enabled = false;
+    void* f3_bufs[6] = {};           // h0, h1, A, Xs, colinv, x1
+    int64_t f3_cap[6] = {};
+    float2* f3_tw[6] = {};
+    int f3_tw_dims[3] = {0, 0, 0};
     // TokenMixer2D state
     nfx::Tm2dPlan plan_tm{};
     void* tm_bufs[12] = {};
@@ -787,6 +795,171 @@ int fno1d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
 }
 
 // ---------------------------------------------------------------------------
+// FNO3d (fno.cpp:1096-1281)
+// ---------------------------------------------------------------------------
+int fno3d_create(nfx_runtime* rt) {
+    // the reference builds FNO3d from the raw weights without its NIRQ block
+    // (runtime.cpp:51-54)
+    auto& m = rt->model;
+    auto& pl = rt->plan3;
+    const int* c = m.cfg;
+    pl.in_ch = c[0];
+    pl.out_ch = c[1];
+    pl.C = c[2];
+    pl.MH = c[3];
+    pl.MW = c[4];
+    pl.MD = c[5];
+    pl.L = c[6];
+    pl.act = m.activation == "relu" ? 1 : 0;
+    if (pl.L > nfx::kFno3dMaxLayers || pl.in_ch < 1) return NFX_OK;  // Run reports it
+    pl.lift_w = wptr(rt, "lift.weight");
+    pl.lift_b = wptr(rt, "lift.bias");
+    pl.pq_w = wptr(rt, "proj_q.weight");
+    pl.pq_b = wptr(rt, "proj_q.bias");
+    pl.po_w = wptr(rt, "proj_out.weight");
+    pl.po_b = wptr(rt, "proj_out.bias");
+    if (!pl.lift_w || !pl.lift_b || !pl.pq_w || !pl.pq_b || !pl.po_w || !pl.po_b)
+        return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+    for (int i = 0; i < pl.L; ++i) {
+        const std::string s = std::to_string(i);
+        auto& L = pl.layer[i];
+        L.wr = wptr(rt, "specs." + s + ".weights_real");
+        L.wi = wptr(rt, "specs." + s + ".weights_imag");
+        L.loc_w = wptr(rt, "locs." + s + ".weight");
+        L.loc_b = wptr(rt, "locs." + s + ".bias");
+        if (!L.wr || !L.wi || !L.loc_w || !L.loc_b) return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+    }
+    return NFX_OK;
+}
+
+// FP8 E4M3 executor (no reference counterpart): needs an FP8 scale (NIRQ kind 3) for
+// every Linear weight and every ".output" key.
+void fno3d_enable_fp8(nfx_runtime* rt) {
+    auto& m = rt->model;
+    auto& pl = rt->plan3;
+    if (!pl.lift_w || !m.quant_enabled) return;
+    auto sc = [&](const std::string& k, float& out) {
+        auto it = m.activation_fp8_qparams.find(k);
+        if (it == m.activation_fp8_qparams.end()) return false;
+        out = it->second;
+        return true;
+    };
+    float s_lift_w, s_pq_w, s_po_w, s_lift, s_pq, s_po;
+    std::vector<float> s_lw(pl.L), s_lo(pl.L);
+    if (!sc("lift.weight", s_lift_w) || !sc("proj_q.weight", s_pq_w) || !sc("proj_out.weight", s_po_w) ||
+        !sc("lift.output", s_lift) || !sc("proj_q.output", s_pq) || !sc("proj_out.output", s_po))
+        return;
+    for (int i = 0; i < pl.L; ++i)
+        if (!sc("locs." + std::to_string(i) + ".weight", s_lw[i]) || !sc("locs." + std::to_string(i) + ".output", s_lo[i]))
+            return;
+    auto fq = [&](const std::string& name, float scale, bool want_xq, const float** fq_out, const float** xq_out) {
+        const auto& t = m.weights.at(name);
+        std::vector<float> xq(t.data.size()), v(t.data.size());
+        nfx::e4m3_fake_quant(t.data.data(), scale, xq.data(), v.data(), t.data.size());
+        if (fq_out) *fq_out = upload(rt, v.data(), v.size());
+        if (want_xq) *xq_out = upload(rt, xq.data(), xq.size());
+    };
+    nfx::Fno3dPlan q = pl;
+    fq("lift.weight", s_lift_w, false, &q.lift_w, nullptr);
+    fq("proj_out.weight", s_po_w, false, &q.po_w, nullptr);
+    fq("proj_q.weight", s_pq_w, true, nullptr, &q.pq_q);
+    for (int i = 0; i < pl.L; ++i)
+        fq("locs." + std::to_string(i) + ".weight", s_lw[i], true, nullptr, &q.layer[i].loc_q);
+    if (!q.lift_w || !q.po_w || !q.pq_q) return;
+    for (int i = 0; i < pl.L; ++i) {
+        if (!q.layer[i].loc_q) return;
+        q.layer[i].s_in = i == 0 ? s_lift : s_lo[i - 1];
+        q.layer[i].s_w = s_lw[i];
+        q.layer[i].s_out = s_lo[i];
+    }
+    q.s_lift = s_lift;
+    q.s_pq_w = s_pq_w;
+    q.s_pq = s_pq;
+    q.s_po = s_po;
+    q.fp8 = 1;
+    pl = q;
+    rt->fp8_enabled = true;
+}
+
+int check_fno3d_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t* ys, int yr) {
+    const auto& pl = rt->plan3;
+    if (xr != 5) return rt_fail(rt, NFX_SHAPE_MISMATCH, "expected 5D input (batch, h, w, d, in_ch)");
+    if (xs[4] != pl.in_ch) return rt_fail(rt, NFX_SHAPE_MISMATCH, "input channels mismatch");
+    if (yr != 5 || ys[0] != xs[0] || ys[1] != xs[1] || ys[2] != xs[2] || ys[3] != xs[3] || ys[4] != pl.out_ch)
+        return rt_fail(rt, NFX_SHAPE_MISMATCH, "output buffer shape mismatch");
+    auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
+    if (!pow2(xs[1]) || !pow2(xs[2]) || !pow2(xs[3]))
+        return rt_fail(rt, NFX_INVALID_ARG, "FNO3d: H, W, and D must each be a power of two");
+    return NFX_OK;
+}
+
+int fno3d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
+    auto& pl0 = rt->plan3;
+    if (!pl0.lift_w) return rt_fail(rt, NFX_UNSUPPORTED_OP, "FNO3d GPU executor: needs <= 8 layers");
+    const int B = static_cast<int>(xs[0]);
+    int dims[3] = {static_cast<int>(xs[1]), static_cast<int>(xs[2]), static_cast<int>(xs[3])};
+    int pd[3] = {dims[0], dims[1], dims[2]};
+    const int pf = rt->model.cfg[7];
+    if (pf > 1)
+        for (int i = 0; i < 3; ++i) pd[i] = dims[i] + (pf - dims[i] % pf) % pf;
+    for (int i = 0; i < 3; ++i)
+        if (pd[i] & (pd[i] - 1)) return rt_fail(rt, NFX_INVALID_ARG, "FNO3d: padded sides must be powers of two");
+    if (pl0.MH > pd[0] || pl0.MW > pd[1] || pl0.MD > pd[2] / 2 + 1)
+        return rt_fail(rt, NFX_INVALID_ARG, "FNO3d: modes exceed the (padded) grid");
+    if (const char* why = nfx::fno3d_unsupported(pl0.C, pd[0], pd[1], pd[2], pl0.MH, pl0.MW, pl0.MD, pl0.out_ch))
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, why);
+    if (B == 0) return NFX_OK;
+    if (rt->f3_tw_dims[0] != pd[0] || rt->f3_tw_dims[1] != pd[1] || rt->f3_tw_dims[2] != pd[2]) {
+        for (int i = 0; i < 6; ++i) {
+            const std::vector<float> t = nfx::build_fft_twiddles(pd[i / 2], (i & 1) == 1);
+            if (rt->f3_tw[i]) cudaFree(rt->f3_tw[i]);
+            rt->f3_tw[i] = nullptr;
+            void* p = nullptr;
+            if (!cuda_ok(rt, cudaMalloc(&p, t.size() * 4 + 16), "cudaMalloc twiddles")) return NFX_INTERNAL;
+            rt->f3_tw[i] = static_cast<float2*>(p);
+            if (!t.empty() && !cuda_ok(rt, cudaMemcpy(p, t.data(), t.size() * 4, cudaMemcpyHostToDevice),
+                                       "cudaMemcpy twiddles"))
+                return NFX_INTERNAL;
+        }
+        for (int i = 0; i < 3; ++i) rt->f3_tw_dims[i] = pd[i];
+    }
+    const int64_t vol = static_cast<int64_t>(B) * pl0.C * pd[0] * pd[1] * pd[2];
+    const int64_t kk = static_cast<int64_t>(B) * pl0.C * pl0.MW * pl0.MD;
+    const int64_t sizes[6] = {vol * 4, vol * 4, kk * pd[0] * 8, kk * pl0.MH * 8, kk * pd[0] * 8, vol * 4};
+    for (int i = 0; i < 6; ++i) {
+        if (sizes[i] <= rt->f3_cap[i]) continue;
+        if (rt->f3_bufs[i]) cudaFree(rt->f3_bufs[i]);
+        rt->f3_bufs[i] = nullptr;
+        rt->f3_cap[i] = 0;
+        if (!cuda_ok(rt, cudaMalloc(&rt->f3_bufs[i], static_cast<size_t>(sizes[i]) + 256), "cudaMalloc activations"))
+            return NFX_INTERNAL;
+        rt->f3_cap[i] = sizes[i];
+    }
+    nfx::Fno3dPlan pl = pl0;
+    pl.B = B;
+    pl.H = dims[0];
+    pl.W = dims[1];
+    pl.D = dims[2];
+    pl.Hp = pd[0];
+    pl.Wp = pd[1];
+    pl.Dp = pd[2];
+    pl.x = dx;
+    pl.y = dy;
+    for (int i = 0; i < 6; ++i) pl.tw[i] = rt->f3_tw[i];
+    pl.h[0] = rt->f3_bufs[0];
+    pl.h[1] = rt->f3_bufs[1];
+    pl.A = static_cast<float2*>(rt->f3_bufs[2]);
+    pl.Xs = static_cast<float2*>(rt->f3_bufs[3]);
+    pl.colinv = static_cast<float2*>(rt->f3_bufs[4]);
+    pl.x1 = static_cast<float*>(rt->f3_bufs[5]);
+    pl.timer = rt->timer.get();
+    const cudaError_t e = nfx::fno3d_run(pl, st);
+    if (e != cudaSuccess)
+        return rt_fail(rt, NFX_INTERNAL, std::string("FNO3d launch failed: ") + cudaGetErrorString(e));
+    return NFX_OK;
+}
+
+// ---------------------------------------------------------------------------
 // TokenMixer2D (fno.cpp:1756-1956)
 // ---------------------------------------------------------------------------
 const char* kTmParts[8] = {"ln1", "q_proj", "k_proj", "v_proj", "o_proj", "ln2", "ffn0", "ffn1"};
@@ -922,14 +1095,14 @@ int tm2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, 
 int check_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t* ys, int yr) {
     if (rt->model.op == "FNO2d") return check_fno2d_shapes(rt, xs, xr, ys, yr);
     if (rt->model.op == "FNO1d") return check_fno1d_shapes(rt, xs, xr, ys, yr);
-    if (rt->model.op == "FNO3d")
-        return rt_fail(rt, NFX_UNSUPPORTED_OP, "the GPU runtime does not execute FNO3d yet");
+    if (rt->model.op == "FNO3d") return check_fno3d_shapes(rt, xs, xr, ys, yr);
     // runtime.cpp:97-100: Run serves the FNO family only
     return rt_fail(rt, NFX_INTERNAL, "runtime does not support op: " + rt->model.op);
 }
 
 int launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
     if (rt->model.op == "FNO1d") return fno1d_launch(rt, dx, xs, dy, st);
+    if (rt->model.op == "FNO3d") return fno3d_launch(rt, dx, xs, dy, st);
     return fno2d_launch(rt, dx, xs, dy, st);
 }
 
@@ -1027,6 +1200,9 @@ int nfx_runtime_create(const char* ir_path, int device, nfx_runtime** out) {
     } else if (op == "FNO1d") {
         s = fno1d_create(rt.get());
         if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
+    } else if (op == "FNO3d") {
+        s = fno3d_create(rt.get());
+        if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
     } else if (op == "TokenMixer2D") {
         s = tm2d_create(rt.get());
         if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
@@ -1070,6 +1246,10 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
     for (void* p : rt->f2_bufs)
         if (p) cudaFree(p);
     for (void* p : rt->tm_bufs)
+        if (p) cudaFree(p);
+    for (void* p : rt->f3_bufs)
+        if (p) cudaFree(p);
+    for (auto* p : rt->f3_tw)
         if (p) cudaFree(p);
     for (auto* p : rt->f2_tw)
         if (p) cudaFree(p);
@@ -1189,6 +1369,14 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
     if (!cuda_ok(rt, cudaStreamSynchronize(rt->stream), "execution")) return NFX_INTERNAL;
     return nfx_runtime_check(rt);
 }
+
+void nfx_runtime_enable_fp8(nfx_runtime* rt) {
+    if (!rt) return;
+    DeviceGuard g(rt->device);
+    if (rt->model.op == "FNO3d") fno3d_enable_fp8(rt);
+}
+
+int nfx_runtime_is_fp8_enabled(const nfx_runtime* rt) { return rt && rt->fp8_enabled ? 1 : 0; }
 
 int nfx_runtime_run_tokenmixer2d_device(nfx_runtime* rt, const float* x, const int64_t* x_shape,
                                         int x_rank, float* y, const int64_t* y_shape, int y_rank,

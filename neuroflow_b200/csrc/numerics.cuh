@@ -91,6 +91,55 @@ __device__ __forceinline__ float fp8_log2_snap(float v, float scale) {
     return __fmul_rn(__fmul_rn(sign, fminf(qv, 448.0f)), scale);
 }
 
+// fp8_e4m3.h:106-221 fp32_to_e4m3_bits, the reference's encoder: NaN -> 0x7F, +-inf ->
+// +-448, round-half-even of the mantissa to 3 bits with exponent carry and saturation
+// to +-448; below the normal range round(|v| * 2^9) clamped to [0, 7] (so values in
+// [7.5, 8) * 2^-9 stay at code 7 where the hardware cvt gives the smallest normal).
+__device__ __forceinline__ uint32_t e4m3_encode_ref(float v) {
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t sign = u >> 31, a = u & 0x7FFFFFFFu;
+    if (a > 0x7F800000u) return 0x7Fu;
+    if (a == 0x7F800000u) return sign ? 0xFEu : 0x7Eu;
+    if (a == 0) return sign << 7;
+    const int e = static_cast<int>(a >> 23) - 120;
+    if (e < 1) {
+        const float r = fminf(fmaxf(rintf(__fmul_rn(__uint_as_float(a), 512.0f)), 0.0f), 7.0f);
+        return (sign << 7) | static_cast<uint32_t>(r);
+    }
+    uint32_t m = (a >> 20) & 7u;
+    const uint32_t rest = a & 0xFFFFFu;
+    if (rest > 0x80000u || (rest == 0x80000u && (m & 1u))) ++m;
+    int ee = e;
+    if (m & 8u) {
+        m &= 7u;
+        ++ee;
+    }
+    if (ee > 15) return (sign << 7) | 0x7Eu;
+    return (sign << 7) | (static_cast<uint32_t>(ee) << 3) | m;
+}
+
+// fp8_e4m3.h:223-284 e4m3_bits_to_fp32.
+__device__ __forceinline__ float e4m3_decode_ref(uint32_t b) {
+    const uint32_t sign = (b >> 7) & 1u, ex = (b >> 3) & 15u, mt = b & 7u;
+    if (ex == 15u && mt == 7u) return __uint_as_float(0x7FC00000u | (sign << 31));
+    if (ex == 0u) {
+        const float v = __fmul_rn(static_cast<float>(mt), 0.001953125f);
+        return sign ? -v : v;
+    }
+    return __uint_as_float((sign << 31) | ((ex + 120u) << 23) | (mt << 20));
+}
+
+// fp8_e4m3.h:312-334: the E4M3 code of v under `inv` = 1/scale (scale 0 -> 1).
+__device__ __forceinline__ uint32_t e4m3_code(float v, float inv) {
+    float xs = __fmul_rn(v, inv);
+    xs = xs > 448.0f ? 448.0f : (xs < -448.0f ? -448.0f : xs);
+    return e4m3_encode_ref(xs);
+}
+// ... and the fake-quantised value
+__device__ __forceinline__ float fp8_fake_quant(float v, float scale, float inv) {
+    return __fmul_rn(e4m3_decode_ref(e4m3_code(v, inv)), scale);
+}
+
 // fno.cpp:810-844 apply_fake_quant for one element: FP8 first, else INT8 per-tensor.
 __device__ __forceinline__ float apply_fq(float v, const FqParam& q) {
     if (q.kind == 1) return fake_quant(v, q.scale, static_cast<float>(q.zp));

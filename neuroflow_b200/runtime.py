@@ -48,6 +48,13 @@ class InferenceRuntime:
     def is_int8_gemm_enabled(self) -> bool:
         return bool(_lib.nfx_runtime_is_int8_gemm_enabled(self._h))
 
+    def enable_fp8(self) -> None:
+        """FNO3d: switch to the FP8 E4M3 executor (needs NIRQ FP8 scales)."""
+        _lib.nfx_runtime_enable_fp8(self._h)
+
+    def is_fp8_enabled(self) -> bool:
+        return bool(_lib.nfx_runtime_is_fp8_enabled(self._h))
+
     def _err(self) -> str:
         return _lib.nfx_runtime_last_error(self._h).decode()
 

@@ -1,0 +1,101 @@
+"""FNO3d executor on the GPU vs the CPU restatement (oracle, pinned bit-exact against
+the reference runtime's FNO3d::Forward).
+
+FP32 path: the reference's transforms, contraction, Linear rounding; ReLU models are
+bit-identical, GELU models differ only through CUDA's tanhf.  FP8 E4M3 variant (no
+reference counterpart): the reference's own E4M3 encoder on the GPU, exact products
+of E4M3 codes summed in k order -- ReLU models bit-identical, GELU within the
+north-star FP8 tolerance of 1e-3 relative L2.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from neuroflow_b200 import ir, synth
+from oracle.cpu import Oracle
+
+
+def _bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def _rel(a, b):
+    return float(np.linalg.norm(a - b) / (np.linalg.norm(b) + 1e-30))
+
+
+def _model(tmp_path, act="gelu", pad=1, **kw):
+    m = synth.fno3d_model(4, n_calib=2, **kw)
+    m.activation = act
+    m.config["pad_factor"] = pad
+    p = os.path.join(str(tmp_path), f"f3_{act}_{pad}.nneuroir")
+    ir.write(p, m)
+    return m, p
+
+
+def _run(path, x, out_ch, fp8=False):
+    from neuroflow_b200.runtime import InferenceRuntime
+    rt = InferenceRuntime(path)
+    if fp8:
+        rt.enable_fp8()
+        assert rt.is_fp8_enabled()
+    y = np.zeros(x.shape[:-1] + (out_ch,), np.float32)
+    rt.run(x, y)
+    return y
+
+
+GEOMS = [dict(width=8, modes=(3, 3, 2), L=2, S=8),
+         dict(width=16, modes=(2, 4, 3), L=1, S=16, in_ch=5),
+         dict(width=32, modes=(4, 4, 4), L=2, S=16)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kw", GEOMS)
+@pytest.mark.parametrize("fp8", [False, True])
+def test_fno3d_relu_bit_exact(tmp_path, kw, fp8):
+    m, p = _model(tmp_path, "relu", **kw)
+    x = synth.fno3d_inputs(np.random.default_rng(1), 2, kw["S"], kw.get("in_ch", 4))
+    want = Oracle().fno3d_forward(m, x, fp8=fp8)
+    got = _run(p, x, 1, fp8)
+    assert np.array_equal(_bits(got), _bits(want)), float(np.abs(got - want).max())
+
+
+@pytest.mark.gpu
+def test_fno3d_relu_bit_exact_padded(tmp_path):
+    m, p = _model(tmp_path, "relu", pad=16, width=8, modes=(3, 3, 3), L=1, S=8)
+    x = synth.fno3d_inputs(np.random.default_rng(2), 1, 8)
+    for fp8 in (False, True):
+        want = Oracle().fno3d_forward(m, x, fp8=fp8)
+        got = _run(p, x, 1, fp8)
+        assert np.array_equal(_bits(got), _bits(want)), (fp8, float(np.abs(got - want).max()))
+
+
+@pytest.mark.gpu
+def test_fno3d_configs3_blocks_gelu(tmp_path):
+    """configs[3] block geometry (width 32, 8x8x8 modes, 4 layers) on a 32^3 grid."""
+    m, p = _model(tmp_path, width=32, modes=(8, 8, 8), L=4, S=32)
+    x = synth.fno3d_inputs(np.random.default_rng(3), 2, 32)
+    o = Oracle()
+    want = o.fno3d_forward(m, x)
+    got = _run(p, x, 1)
+    assert _rel(got, want) < 1e-5, _rel(got, want)
+    want8 = o.fno3d_forward(m, x, fp8=True)
+    got8 = _run(p, x, 1, fp8=True)
+    print("fp8 rel", _rel(got8, want8), "fp8 vs fp32", _rel(want8, want))
+    assert _rel(got8, want8) < 1e-3
+
+
+@pytest.mark.gpu
+def test_fno3d_errors(tmp_path):
+    from neuroflow_b200.runtime import InferenceRuntime
+    _, p = _model(tmp_path, width=8, modes=(2, 2, 2), L=1, S=8)
+    rt = InferenceRuntime(p)
+    assert rt.op() == "FNO3d" and not rt.is_fp8_enabled()
+    with pytest.raises(RuntimeError, match="expected 5D input"):
+        rt.run(np.zeros((1, 8, 8, 4), np.float32), np.zeros((1, 8, 8, 1), np.float32))
+    with pytest.raises(RuntimeError, match="input channels mismatch"):
+        rt.run(np.zeros((1, 8, 8, 8, 3), np.float32), np.zeros((1, 8, 8, 8, 1), np.float32))
+    with pytest.raises(RuntimeError, match="output buffer shape mismatch"):
+        rt.run(np.zeros((1, 8, 8, 8, 4), np.float32), np.zeros((1, 8, 8, 4, 1), np.float32))
+    with pytest.raises(RuntimeError, match="power of two"):
+        rt.run(np.zeros((1, 8, 6, 8, 4), np.float32), np.zeros((1, 8, 6, 8, 1), np.float32))
