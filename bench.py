@@ -328,6 +328,12 @@ AUX = {
     "fno2d_fp32": dict(metric="FNO2d FP32 fake-quant samples/s", op="FNO2d", batch=256,
                        workload="configs[2] geometry without EnableInt8Gemm: the reference FNO2d "
                                 "Run (fp32 with fake-quant at the four .output boundaries)"),
+    "fno3d": dict(metric="FNO3d FP32 samples/s", op="FNO3d", batch=16,
+                  workload="configs[3] geometry, FP32 (the reference FNO3d Run: 64^3 grid, "
+                           "width 32, 8x8x8 modes, 4 layers)"),
+    "fno3d_fp8": dict(metric="FNO3d FP8-E4M3 samples/s", op="FNO3d", batch=16,
+                      workload="configs[3] FNO3d FP8-E4M3 per-tensor (E4M3 codes between "
+                               "layers, amax/448 scales from a 4-sample calibration batch)"),
     "tm2d": dict(metric="TokenMixer2D FP32 samples/s", op="TokenMixer2D", batch=32,
                  workload="configs[4] TokenMixer2D, 64x64 grid = 4096 tokens, latent 128, "
                           "4 heads, 4 blocks (the reference RunTokenMixer2D arithmetic)"),
@@ -346,6 +352,8 @@ def aux_model(name: str) -> str:
         m = synth.fno1d_model(0, per_token=(name == "fno1d"))
     elif name == "fno2d_fp32":
         return model_path(0)
+    elif name in ("fno3d", "fno3d_fp8"):
+        m = synth.fno3d_model(0)
     else:
         m = synth.tm2d_model(0)
     tmp = path + f".{os.getpid()}"
@@ -367,11 +375,17 @@ def run_aux(args):
         x = synth.fno1d_inputs(rng, B, 1024)
     elif spec["op"] == "FNO2d":
         x = inputs(100, B)
+    elif spec["op"] == "FNO3d":
+        x = synth.fno3d_inputs(rng, B, 64)
     else:
         x = synth.tm2d_inputs(rng, B, 64, 64)
     rt = InferenceRuntime(aux_model(args.workload), 0)
     if args.workload in ("fno1d", "fno1d_int8", "tm2d_int8"):
         rt.enable_int8_gemm()
+    if args.workload == "fno3d_fp8":
+        rt.enable_fp8()
+        if not rt.is_fp8_enabled():
+            raise RuntimeError("FP8 path not enabled for the bench model")
     dx = torch.from_numpy(x).to(device)
     dy = torch.empty(tuple(x.shape[:-1]) + (1,), dtype=torch.float32, device=device)
     stream = torch.cuda.Stream(device)

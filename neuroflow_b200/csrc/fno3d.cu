@@ -206,10 +206,11 @@ __global__ void __launch_bounds__(256) inv3d_kernel(Fno3dPlan p) {
 // local layer + epilogue, one point per thread; smem weights [C][C]
 template <int C>
 __global__ void __launch_bounds__(128) local3d_kernel(Fno3dPlan p, Fno3dLayer L, const void* hin, void* hout) {
-    __shared__ float sW[C * C];
+    __shared__ float4 sW4[C * C / 4];  // transposed [k][o]: 16-byte broadcast loads over o
     __shared__ float sB[C];
+    float* sW = reinterpret_cast<float*>(sW4);
     const float* wsrc = p.fp8 ? L.loc_q : L.loc_w;
-    for (int i = threadIdx.x; i < C * C; i += blockDim.x) sW[i] = wsrc[i];
+    for (int i = threadIdx.x; i < C * C; i += blockDim.x) sW[(i % C) * C + i / C] = wsrc[i];
     for (int i = threadIdx.x; i < C; i += blockDim.x) sB[i] = L.loc_b[i];
     __syncthreads();
     const int64_t P = static_cast<int64_t>(p.Hp) * p.Wp * p.Dp;
@@ -228,15 +229,28 @@ __global__ void __launch_bounds__(128) local3d_kernel(Fno3dPlan p, Fno3dLayer L,
             for (int k = 0; k < C; ++k) {
                 const float a = e4m3_decode_ref(static_cast<const uint8_t*>(hin)[base + k * P]);
 #pragma unroll
-                for (int o = 0; o < C; ++o) acc[o] = __fadd_rn(acc[o], __fmul_rn(a, sW[o * C + k]));
+                for (int o4 = 0; o4 < C / 4; ++o4) {
+                    const float4 w = sW4[k * (C / 4) + o4];
+                    acc[4 * o4 + 0] = __fadd_rn(acc[4 * o4 + 0], __fmul_rn(a, w.x));
+                    acc[4 * o4 + 1] = __fadd_rn(acc[4 * o4 + 1], __fmul_rn(a, w.y));
+                    acc[4 * o4 + 2] = __fadd_rn(acc[4 * o4 + 2], __fmul_rn(a, w.z));
+                    acc[4 * o4 + 3] = __fadd_rn(acc[4 * o4 + 3], __fmul_rn(a, w.w));
+                }
             }
         } else {
 #pragma unroll
             for (int o = 0; o < C; ++o) acc[o] = sB[o];
             for (int k = 0; k < C; ++k) {
                 const float a = static_cast<const float*>(hin)[base + k * P];
+                const bool fused = k >= nu;
 #pragma unroll
-                for (int o = 0; o < C; ++o) acc[o] = linear_step(acc[o], a, sW[o * C + k], k >= nu);
+                for (int o4 = 0; o4 < C / 4; ++o4) {
+                    const float4 w = sW4[k * (C / 4) + o4];
+                    acc[4 * o4 + 0] = linear_step(acc[4 * o4 + 0], a, w.x, fused);
+                    acc[4 * o4 + 1] = linear_step(acc[4 * o4 + 1], a, w.y, fused);
+                    acc[4 * o4 + 2] = linear_step(acc[4 * o4 + 2], a, w.z, fused);
+                    acc[4 * o4 + 3] = linear_step(acc[4 * o4 + 3], a, w.w, fused);
+                }
             }
         }
 #pragma unroll

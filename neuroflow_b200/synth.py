@@ -42,7 +42,7 @@ def grf3d(rng: np.random.Generator, n: int, S: int, tau: float = 2.0) -> np.ndar
     out = np.empty((n, S, S, S), np.float32)
     for i in range(n):
         z = rng.standard_normal(amp.shape) + 1j * rng.standard_normal(amp.shape)
-        f = np.fft.irfftn(z * amp, s=(S, S, S))
+        f = np.fft.irfftn(z * amp, s=(S, S, S), axes=(0, 1, 2))
         f = (f - f.mean()) / (f.std() + 1e-12)
         out[i] = f.astype(np.float32)
     return out
