@@ -369,7 +369,7 @@ def run_aux(args):
     spec = AUX[args.workload]
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    B = spec["batch"]
+    B = args.batch if args.batch else spec["batch"]
     rng = np.random.default_rng(100)
     if spec["op"] == "FNO1d":
         x = synth.fno1d_inputs(rng, B, 1024)
@@ -425,9 +425,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--batch", type=int, default=CFG["batch"],
-                    help="samples per GPU (default: the configs[2] batch of 256; smaller "
-                         "values only for profiling captures)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="samples per GPU (default: the configuration's batch, 256 for the "
+                         "headline; smaller values only for profiling captures)")
     ap.add_argument("--workload", default="fno2d_int8", choices=["fno2d_int8"] + sorted(AUX),
                     help="fno2d_int8 (default): the headline configs[2] line; the others time "
                          "the remaining BASELINE configurations on one GPU")
@@ -467,6 +467,8 @@ def main():
         print(json.dumps(line), flush=True)
         return
 
+    if not args.batch:
+        args.batch = CFG["batch"]
     ws, rank, local = dist_setup(args.gpus)
     result, rt, x_host, path = run_nfx(args, ws, rank, local)
     if rank == 0:
