@@ -4,7 +4,7 @@
 
 Compiles neuroflow_b200/csrc/*.cu and *.cpp with nvcc for sm_100a only
 (-gencode arch=compute_100a,code=sm_100a), objects under _build/, and links
-neuroflow_b200/libnfx.so.  The CUDA runtime is linked statically so the library does
+neuroflow_b200/libnfx.so and the nflow_infer command-line front-end next to it.  The CUDA runtime is linked statically so the library does
 not depend on which libcudart the host process (e.g. torch) loaded.
 """
 from __future__ import annotations
@@ -64,7 +64,24 @@ def build(verbose: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    _build_cli()
     return LIB
+
+
+CLI_SRC = os.path.join(PKG, "cli", "nflow_infer.cpp")
+CLI = os.path.join(PKG, "nflow_infer")
+
+
+def _build_cli() -> None:
+    """The nflow_infer executable, linked against libnfx.so (found next to it)."""
+    if os.path.exists(CLI) and os.path.getmtime(CLI) >= max(os.path.getmtime(CLI_SRC),
+                                                              os.path.getmtime(LIB)):
+        return
+    cmd = ["g++", "-std=c++17", "-O2", "-I" + os.path.join(ROOT, "include"), CLI_SRC, "-o", CLI,
+           "-L" + PKG, "-lnfx", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nflow_infer build failed:\n{r.stdout}\n{r.stderr}")
 
 
 if __name__ == "__main__":

@@ -22,6 +22,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "fno2d.h"
 #include "nfx_internal.h"
@@ -477,6 +478,8 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
         const int R = 128 / p.W > 0 ? 128 / p.W : 1;
         const float s_out = p.fq_out.scale, inv_out = p.fq_out.inv_scale;
         const float zpo = static_cast<float>(p.fq_out.zp);
+        const float klo = -128.0f - zpo, khi = 127.0f - zpo;         // code offsets' range
+        const float lut_c = __fmul_rn(-p.lut_zlo, p.lut_inv_delta);  // table index offset
         int cached_b = -1;
         int it = 0, nstore = 0;
         uint32_t nsync = 0;
@@ -676,23 +679,36 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                         if (use_lut) return code_from_lut(z, sLut, p.lut_cells, p.lut_zlo, p.lut_inv_delta);
                         return static_cast<int>(fq_code(activation(z, p.act), s_out, zpo));
                     };
+                    // Per element: dequantise + bias, the fast fake-quant offset k (x2 =
+                    // k * s exactly), z = x1 + x2, and the next code, inserted into the
+                    // packed word with one byte permute: the table cell's bytes hold the
+                    // codes below / from its breakpoint, the selector picks one.
                     uint32_t packed[8];
+                    auto chunk = [&](auto lut_tag) {
 #pragma unroll
-                    for (int j = 0; j < L::kCh; ++j) {
-                        const float x1 = x1_of(j, x1r[j]);
-                        const float4 cp = sCol[c0 + j];
-                        const int vint = static_cast<int>(raw[j]) + __float_as_int(cp.y) * rconst -
-                                         __float_as_int(cp.z);
-                        const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
-                        bool b;
-                        const float q2 = fq_code_try(v, inv_out, zpo, b);
-                        bad |= static_cast<uint32_t>(b) << j;
-                        const float x2 = __fmul_rn(__fsub_rn(q2, zpo), s_out);
-                        const int code = code_of(__fadd_rn(x1, x2));
-                        const uint32_t byte = static_cast<uint32_t>(code) & 0xFFu;
-                        if ((j & 3) == 0) packed[j >> 2] = byte;
-                        else packed[j >> 2] |= byte << (8 * (j & 3));
-                    }
+                        for (int j = 0; j < L::kCh; ++j) {
+                            const float x1 = x1_of(j, x1r[j]);
+                            const float4 cp = sCol[c0 + j];
+                            const int vint = static_cast<int>(raw[j]) + __float_as_int(cp.y) * rconst -
+                                             __float_as_int(cp.z);
+                            const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
+                            bool b;
+                            const float kq = fq_offset_try(v, inv_out, klo, khi, b);
+                            bad |= static_cast<uint32_t>(b) << j;
+                            const float z = __fadd_rn(x1, __fmul_rn(kq, s_out));
+                            const uint32_t prev = (j & 3) == 0 ? 0u : packed[j >> 2];
+                            const uint32_t sel_lo = (0x3210u & ~(0xFu << (4 * (j & 3)))) | (4u << (4 * (j & 3)));
+                            if constexpr (decltype(lut_tag)::value) {
+                                const int2 cell = lut_cell(z, sLut, p.lut_cells, p.lut_inv_delta, lut_c);
+                                const uint32_t sel = z >= __int_as_float(cell.x) ? sel_lo + (1u << (4 * (j & 3))) : sel_lo;
+                                packed[j >> 2] = __byte_perm(prev, static_cast<uint32_t>(cell.y), sel);
+                            } else {
+                                packed[j >> 2] = __byte_perm(prev, static_cast<uint32_t>(code_of(z)), sel_lo);
+                            }
+                        }
+                    };
+                    if (use_lut) chunk(std::true_type{});
+                    else chunk(std::false_type{});
                     uint8_t* buf = sStage + (ew * 2 + (nstore & 1)) * 512;
                     if (nstore >= 2) {
                         if (lane == 0) tma_store_wait_read<1>();

@@ -110,7 +110,8 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
     if (tr.empty()) {
         out.zlo = 0.0f;
         out.inv_delta = 1.0f;
-        out.cells.assign(1, CodeCell{std::numeric_limits<float>::infinity(), code(0.0f) & 0xFF});
+        out.cells.assign(1, CodeCell{std::numeric_limits<float>::infinity(),
+                                     (code(0.0f) & 0xFF) | ((code(0.0f) & 0xFF) << 8)});
         return true;
     }
     double delta = std::fmin(0.25, 0.5 * s);
@@ -143,7 +144,7 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
                 d = tr[k].after - tr[k].before;
                 ++n;
             }
-            c.packed = (base & 0xFF) | ((d & 0xFF) << 8);
+            c.packed = (base & 0xFF) | (((base + d) & 0xFF) << 8);
             cells[j] = c;
         }
         if (!ok) continue;
@@ -155,14 +156,14 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
         for (int k = 0; k < 20000; ++k) {
             st = st * 1664525u + 1013904223u;
             const float z = static_cast<float>(lo_z - 1.0 + (hi_z - lo_z + 2.0) * (st >> 8) / 16777216.0);
-            float fi = (z - out.zlo) * out.inv_delta;
+            // the device's index: fma(z, inv_delta, -zlo * inv_delta), truncated
+            const float cofs = -out.zlo * out.inv_delta;
+            const float fi = std::fma(z, out.inv_delta, cofs);
             int idx = static_cast<int>(fi);
             if (fi < 0.0f) idx = 0;
             if (idx > ncells - 1) idx = ncells - 1;
             const CodeCell& cc = out.cells[idx];
-            const int base = static_cast<int8_t>(cc.packed & 0xFF);
-            const int dd = static_cast<int8_t>((cc.packed >> 8) & 0xFF);
-            const int got = base + (z >= cc.t ? dd : 0);
+            const int got = static_cast<int8_t>(((z >= cc.t) ? (cc.packed >> 8) : cc.packed) & 0xFF);
             const int want = code(z);
             if (got != want) {
                 // accept only the flip windows of a few ulps around a breakpoint

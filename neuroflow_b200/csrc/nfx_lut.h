@@ -6,12 +6,13 @@
 //    with act the reference GELU (fno.cpp:36-48, glibc tanhf) or ReLU and fq_code the
 //    reference float quantiser (fno.cpp:497-505).  code(z) is a step function of the
 //    float z = x1 + x2.  The table splits z into uniform cells; each cell stores the
-//    code at its (slightly extended) left edge and at most one breakpoint inside,
-//    found exactly by bisection over consecutive float values using the host's
-//    reference-equivalent arithmetic.  The GPU evaluates
-//        code = base + d*(z >= t)
-//    for the cell of z.  Where float rounding makes code(z) flip back and forth within
-//    a few ulps of a breakpoint, the table keeps one breakpoint of that window.
+//    code at its (slightly extended) left edge, the code after its breakpoint and at
+//    most one breakpoint inside, found exactly by bisection over consecutive float
+//    values using the host's reference-equivalent arithmetic.  The GPU evaluates
+//        code = z >= t ? hi : lo
+//    for the cell of z (index fma(z, inv_delta, -zlo * inv_delta)).  Where float
+//    rounding makes code(z) flip back and forth within a few ulps of a breakpoint, the
+//    table keeps one breakpoint of that window.
 // 2. Activation table.  The projection applies the activation to a fake-quantised
 //    value, which takes one of 256 values (k - zp)*s; the table holds the reference
 //    activation of each.
@@ -25,7 +26,7 @@ namespace nfx {
 
 struct CodeCell {
     float t;        // breakpoint (+inf when unused)
-    int32_t packed; // base code (int8) | d (int8) << 8
+    int32_t packed; // code below t (byte 0) | code from t on (byte 1)
 };
 
 struct CodeLut {

@@ -49,12 +49,24 @@ __device__ __forceinline__ float fq_code_fast(float v, float s, float inv_s, flo
 
 // Branch-free form of the fast path for unrolled epilogues: returns the fast code and
 // reports in `bad` whether the element needs the exact path (the caller fixes those
-// elements afterwards, outside the unrolled loop).
+// elements afterwards, outside the unrolled loop).  No magnitude check is needed here:
+// where |v/s| >= 2^10 both the fast and the exact quotient saturate the code, and NaN
+// fails the half-integer test.
 __device__ __forceinline__ float fq_code_try(float v, float inv_s, float zp, bool& bad) {
     const float r = __fmul_rn(v, inv_s);
     const float k = rintf(r);
-    bad = !(fabsf(__fsub_rn(r, k)) < 0.49951171875f) || !(fabsf(r) < 1024.0f);
+    bad = !(fabsf(__fsub_rn(r, k)) < 0.49951171875f);
     return fminf(fmaxf(__fadd_rn(k, zp), -128.0f), 127.0f);
+}
+
+// The same test returning the snapped value's integer offset directly:
+// (fq_code - zp) = clamp(k, -128 - zp, 127 - zp), exact because k is an integer-valued
+// float below 2^24 on the fast path.  klo = -128 - zp, khi = 127 - zp.
+__device__ __forceinline__ float fq_offset_try(float v, float inv_s, float klo, float khi, bool& bad) {
+    const float r = __fmul_rn(v, inv_s);
+    const float k = rintf(r);
+    bad = !(fabsf(__fsub_rn(r, k)) < 0.49951171875f);
+    return fminf(fmaxf(k, klo), khi);
 }
 
 // fake-quant round trip: (q - zp) * s.
@@ -159,17 +171,21 @@ __device__ __forceinline__ float linear_step(float acc, float x, float w, bool f
     return fused ? __fmaf_rn(x, w, acc) : __fadd_rn(acc, __fmul_rn(x, w));
 }
 
-// The next layer's code from z = x1 + x2 via the host-built exact table (nfx_lut.h):
-// cell of z, then base + d * (z >= breakpoint).
+// The next layer's code from z = x1 + x2 via the host-built exact table (nfx_lut.h).
+// Cell index fma(z, inv_delta, c) with c = -zlo * inv_delta (the cells overlap their
+// neighbours by far more than this index's rounding); the cell holds the breakpoint t
+// and the codes below / from t as bytes lo | hi << 8.
+__device__ __forceinline__ int2 lut_cell(float z, const int2* lut, int ncells, float inv_delta,
+                                         float c) {
+    int idx = __float2int_rz(__fmaf_rn(z, inv_delta, c));
+    idx = idx < 0 ? 0 : (idx > ncells - 1 ? ncells - 1 : idx);
+    return lut[idx];
+}
 __device__ __forceinline__ int code_from_lut(float z, const int2* lut, int ncells, float zlo,
                                              float inv_delta) {
-    const float fi = __fmul_rn(__fsub_rn(z, zlo), inv_delta);
-    int idx = __float2int_rz(fi);
-    idx = idx < 0 ? 0 : (idx > ncells - 1 ? ncells - 1 : idx);
-    const int2 c = lut[idx];
-    const int base = (c.y << 24) >> 24;
-    const int d = (c.y << 16) >> 24;
-    return base + (z >= __int_as_float(c.x) ? d : 0);
+    const int2 cell = lut_cell(z, lut, ncells, inv_delta, __fmul_rn(-zlo, inv_delta));
+    const int w = z >= __int_as_float(cell.x) ? (cell.y >> 8) : cell.y;
+    return static_cast<int>(static_cast<int8_t>(w & 0xFF));
 }
 
 // int8_gemm.cpp:574-577 epilogue of LinearForwardBatched for one output:

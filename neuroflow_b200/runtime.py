@@ -1,6 +1,7 @@
 """Python front-end of the GPU runtime, mirroring the reference `neuroflow_cpp` module
 (cpp/bindings/pybind_module.cpp:61-197): `InferenceRuntime(path)` with `op()`,
-`enable_int8_gemm()`, `is_int8_gemm_enabled()` and `run(x, y)`, plus `infer_arrays`.
+`enable_int8_gemm()`, `is_int8_gemm_enabled()`, `run(x, y)` and `run_tokenmixer2d(x, y)`,
+plus the module functions `infer` and `infer_arrays`.
 Errors raise RuntimeError like the reference binding.  Every call goes through the
 C-ABI of libnfx.so; there is no CPU fallback.
 """
@@ -132,13 +133,42 @@ class InferenceRuntime:
             raise RuntimeError("device error: " + self._err())
 
 
-def infer_arrays(model_path: str, x: np.ndarray, out_channels: int, enable_int8: bool = True,
-                 device: int = 0) -> np.ndarray:
-    """Load, run once, return y (the reference's `infer_arrays`, with the output channel
-    count given explicitly)."""
+_RANK = {"FNO1d": 3, "FNO2d": 4, "FNO3d": 5, "TokenMixer2D": 4}
+
+
+def _run_once(model_path: str, x: np.ndarray, enable_int8: bool, enable_fp8: bool,
+              device: int) -> np.ndarray:
+    op, cfg, _, _ = _nfx.load_neuroir(model_path)
+    if op not in _RANK or x.ndim != _RANK[op]:
+        raise RuntimeError("input rank mismatch for op " + op)
     rt = InferenceRuntime(model_path, device)
     if enable_int8:
         rt.enable_int8_gemm()
-    y = np.zeros(tuple(x.shape[:-1]) + (out_channels,), np.float32)
-    rt.run(x, y)
+    if enable_fp8:
+        rt.enable_fp8()
+    y = np.zeros(tuple(x.shape[:-1]) + (cfg[1],), np.float32)
+    if op == "TokenMixer2D":
+        rt.run_tokenmixer2d(x, y)
+    else:
+        rt.run(x, y)
     return y
+
+
+def infer_arrays(model_path: str, x: np.ndarray, enable_int8: bool = False,
+                 enable_fp8: bool = False, device: int = 0) -> np.ndarray:
+    """The reference's `infer_arrays` (pybind_module.cpp:113-158): load, run once,
+    return y; the output channel count comes from the IR.  `enable_int8` / `enable_fp8`
+    switch to the quantised executors (the reference function has no such switch)."""
+    return _run_once(model_path, np.ascontiguousarray(x, dtype=np.float32), enable_int8,
+                     enable_fp8, device)
+
+
+def infer(model_path: str, input_path: str, output_path: str, enable_int8: bool = False,
+          enable_fp8: bool = False, device: int = 0) -> str:
+    """The reference's `infer` (pybind_module.cpp:61-111): .npy in, .npy out."""
+    x = np.load(input_path)
+    if x.dtype != np.float32:
+        x = x.astype(np.float32)
+    y = _run_once(model_path, np.ascontiguousarray(x), enable_int8, enable_fp8, device)
+    np.save(output_path, y)
+    return "ok"

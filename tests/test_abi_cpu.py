@@ -25,3 +25,15 @@ def test_library_is_sm100a_only():
     # the build targets sm_100a exclusively
     from neuroflow_b200 import build
     assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def test_nflow_infer_cli_usage():
+    """The command-line front-end is built next to the library and keeps the
+    reference's flags and exit codes (cpp/src/main.cpp:27-50)."""
+    import subprocess
+    cli = os.path.join(ROOT, "neuroflow_b200", "nflow_infer")
+    assert os.path.exists(cli)
+    r = subprocess.run([cli, "--help"], capture_output=True, text=True)
+    assert r.returncode == 0 and "--model" in r.stdout and "--input" in r.stdout
+    r = subprocess.run([cli, "--model", "m.nneuroir"], capture_output=True, text=True)
+    assert r.returncode == 1
