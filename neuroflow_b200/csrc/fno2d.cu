@@ -53,9 +53,10 @@ __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, 
                                                    float inv_s, int8_t* __restrict__ codes) {
     // one thread per (point, group of 16 channels)
     constexpr int kG = C / 16;
-    __shared__ float sw[C * 8];
+    __shared__ float4 sw4[C * 8 / 4];  // transposed [k][c]: 16 channels of one k in 4 loads
     __shared__ float sb[C];
-    for (int i = threadIdx.x; i < C * in_ch; i += blockDim.x) sw[i] = w[i];
+    float* sw = reinterpret_cast<float*>(sw4);
+    for (int i = threadIdx.x; i < C * in_ch; i += blockDim.x) sw[(i % in_ch) * C + i / in_ch] = w[i];
     for (int i = threadIdx.x; i < C; i += blockDim.x) sb[i] = b[i];
     __syncthreads();
     const float zpf = static_cast<float>(zp);
@@ -70,8 +71,15 @@ __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, 
         const int nu = linear_unfused_len(in_ch);
         for (int k = 0; k < in_ch; ++k) {
             const float xv = __ldg(x + m * in_ch + k);
+            const float4* wk = sw4 + (k * C + o0) / 4;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) acc[j] = linear_step(acc[j], xv, sw[(o0 + j) * in_ch + k], k >= nu);
+            for (int j4 = 0; j4 < 4; ++j4) {
+                const float4 wv = wk[j4];
+                acc[4 * j4 + 0] = linear_step(acc[4 * j4 + 0], xv, wv.x, k >= nu);
+                acc[4 * j4 + 1] = linear_step(acc[4 * j4 + 1], xv, wv.y, k >= nu);
+                acc[4 * j4 + 2] = linear_step(acc[4 * j4 + 2], xv, wv.z, k >= nu);
+                acc[4 * j4 + 3] = linear_step(acc[4 * j4 + 3], xv, wv.w, k >= nu);
+            }
         }
         uint32_t words[4];
         uint32_t badmask = 0;
@@ -89,7 +97,7 @@ __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, 
             badmask &= badmask - 1;
             float a = sb[o0 + j];
             for (int k = 0; k < in_ch; ++k)
-                a = linear_step(a, __ldg(x + m * in_ch + k), sw[(o0 + j) * in_ch + k], k >= nu);
+                a = linear_step(a, __ldg(x + m * in_ch + k), sw[k * C + o0 + j], k >= nu);
             const uint32_t byte = static_cast<uint32_t>(static_cast<int>(fq_code(a, s, zpf))) & 0xFFu;
             words[j >> 2] = (words[j >> 2] & ~(0xFFu << (8 * (j & 3)))) | (byte << (8 * (j & 3)));
         }

@@ -32,16 +32,18 @@ __device__ __forceinline__ float fq_code(float v, float s, float zp) {
     return q;
 }
 
-// The same code without a division on the common path.  r = v * (1/s) differs from
-// the correctly rounded quotient v / s by less than 2^-12 while |v/s| < 2^10, so
-// rounding r to the nearest integer gives the quotient's rounding whenever r is not
-// within 2^-11 of a half-integer (there round-half-away and round-half-even agree
-// too).  Inputs near a half-integer, |r| >= 2^10, and NaN take the exact path.
+// The same code without a division on the common path.  r = v * fl(1/s) differs from
+// v / s by at most |v/s| * 2^-23, and the reference's quotient fl(v / s) from v / s by
+// at most |v/s| * 2^-24; for |v/s| < 2^9 the two are within 1.5 * 2^-14 of each other,
+// so rounding r to the nearest integer gives the rounding of the reference's quotient
+// whenever r is not within 2^-13 of a half-integer (there round-half-away and
+// round-half-even agree too).  For |v/s| >= 2^9 both roundings saturate the code
+// (|k| > 255 for any zero point).  Inputs next to a half-integer, and NaN, take the
+// exact path.
 __device__ __forceinline__ float fq_code_fast(float v, float s, float inv_s, float zp) {
     const float r = __fmul_rn(v, inv_s);
     const float k = rintf(r);
-    if (!(fabsf(__fsub_rn(r, k)) < 0.49951171875f) || !(fabsf(r) < 1024.0f))
-        return fq_code(v, s, zp);
+    if (!(fabsf(__fsub_rn(r, k)) < 0.4998779296875f)) return fq_code(v, s, zp);
     float q = __fadd_rn(k, zp);
     q = fminf(fmaxf(q, -128.0f), 127.0f);
     return q;
@@ -49,13 +51,11 @@ __device__ __forceinline__ float fq_code_fast(float v, float s, float inv_s, flo
 
 // Branch-free form of the fast path for unrolled epilogues: returns the fast code and
 // reports in `bad` whether the element needs the exact path (the caller fixes those
-// elements afterwards, outside the unrolled loop).  No magnitude check is needed here:
-// where |v/s| >= 2^10 both the fast and the exact quotient saturate the code, and NaN
-// fails the half-integer test.
+// elements afterwards, outside the unrolled loop).
 __device__ __forceinline__ float fq_code_try(float v, float inv_s, float zp, bool& bad) {
     const float r = __fmul_rn(v, inv_s);
     const float k = rintf(r);
-    bad = !(fabsf(__fsub_rn(r, k)) < 0.49951171875f);
+    bad = !(fabsf(__fsub_rn(r, k)) < 0.4998779296875f);
     return fminf(fmaxf(__fadd_rn(k, zp), -128.0f), 127.0f);
 }
 
@@ -65,7 +65,7 @@ __device__ __forceinline__ float fq_code_try(float v, float inv_s, float zp, boo
 __device__ __forceinline__ float fq_offset_try(float v, float inv_s, float klo, float khi, bool& bad) {
     const float r = __fmul_rn(v, inv_s);
     const float k = rintf(r);
-    bad = !(fabsf(__fsub_rn(r, k)) < 0.49951171875f);
+    bad = !(fabsf(__fsub_rn(r, k)) < 0.4998779296875f);
     return fminf(fmaxf(k, klo), khi);
 }
 

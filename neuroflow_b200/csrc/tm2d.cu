@@ -16,6 +16,8 @@
 //               tail); three passes over the keys instead of a materialised n x n matrix
 //   row_quant   INT8 path: per-row qparams (the compute_tensor_qparams rule in double)
 //               and the activation codes (QuantiseActivation, int8_gemm.cpp:507-520)
+//   attention_online  INT8 path: one pass over the keys with an online softmax and
+//               fused multiply-adds (fp32-accurate, not the reference's order)
 //
 // Approximate operations: CUDA's expf in the softmax and tanhf in GELU (a few ulps
 // from glibc's); everything else is bit-identical to the reference arithmetic.
@@ -279,6 +281,81 @@ __global__ void __launch_bounds__(kQ) attention_kernel(const float* __restrict__
 }
 
 // ---------------------------------------------------------------------------
+// attention of the INT8 variant (no reference counterpart): one pass over the keys
+// with an online softmax (running max, rescaled sum and accumulator), fused
+// multiply-adds.  Same grid and shared-memory staging as attention_kernel; the result
+// equals the reference-order attention to fp32 rounding, not bit for bit.
+// ---------------------------------------------------------------------------
+template <int HD>
+__global__ void __launch_bounds__(kQ) attention_online_kernel(const float* __restrict__ Q,
+                                                              const float* __restrict__ K,
+                                                              const float* __restrict__ V, int NP,
+                                                              int L, float scale,
+                                                              float* __restrict__ out) {
+    constexpr int kKeys = HD <= 32 ? 128 : 64;
+    __shared__ float4 sK[kKeys][HD / 4];
+    __shared__ float4 sV[kKeys][HD / 4];
+    const int b = blockIdx.z, head = blockIdx.y;
+    const int i = blockIdx.x * kQ + threadIdx.x;
+    const bool live = i < NP;
+    const int64_t base = static_cast<int64_t>(b) * NP * L + head * HD;
+    float q[HD], acc[HD];
+#pragma unroll
+    for (int d = 0; d < HD; ++d) {
+        q[d] = live ? Q[base + static_cast<int64_t>(i) * L + d] : 0.0f;
+        acc[d] = 0.0f;
+    }
+    float mx = -INFINITY, l = 0.0f;
+    for (int j0 = 0; j0 < NP; j0 += kKeys) {
+        float* fk = reinterpret_cast<float*>(sK);
+        float* fv = reinterpret_cast<float*>(sV);
+        for (int t = threadIdx.x; t < kKeys * HD; t += kQ) {
+            const int jj = t / HD, d = t % HD;
+            const bool in = j0 + jj < NP;
+            fk[t] = in ? K[base + static_cast<int64_t>(j0 + jj) * L + d] : 0.0f;
+            fv[t] = in ? V[base + static_cast<int64_t>(j0 + jj) * L + d] : 0.0f;
+        }
+        __syncthreads();
+        const int n = min(kKeys, NP - j0);
+        for (int jj = 0; jj < n; ++jj) {
+            float sc = 0.0f;
+#pragma unroll
+            for (int d4 = 0; d4 < HD / 4; ++d4) {
+                const float4 k4 = sK[jj][d4];
+                sc = fmaf(q[4 * d4], k4.x, sc);
+                sc = fmaf(q[4 * d4 + 1], k4.y, sc);
+                sc = fmaf(q[4 * d4 + 2], k4.z, sc);
+                sc = fmaf(q[4 * d4 + 3], k4.w, sc);
+            }
+            sc *= scale;
+            if (sc > mx) {
+                const float c = expf(mx - sc);
+                l *= c;
+#pragma unroll
+                for (int d = 0; d < HD; ++d) acc[d] *= c;
+                mx = sc;
+            }
+            const float pj = expf(sc - mx);
+            l += pj;
+#pragma unroll
+            for (int d4 = 0; d4 < HD / 4; ++d4) {
+                const float4 v4 = sV[jj][d4];
+                acc[4 * d4] = fmaf(pj, v4.x, acc[4 * d4]);
+                acc[4 * d4 + 1] = fmaf(pj, v4.y, acc[4 * d4 + 1]);
+                acc[4 * d4 + 2] = fmaf(pj, v4.z, acc[4 * d4 + 2]);
+                acc[4 * d4 + 3] = fmaf(pj, v4.w, acc[4 * d4 + 3]);
+            }
+        }
+        __syncthreads();
+    }
+    if (live) {
+        const float inv = 1.0f / l;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) out[base + static_cast<int64_t>(i) * L + d] = acc[d] * inv;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // INT8 path: per-row qparams + codes.  32 rows per warp staged [32][K + 1].
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) row_quant_kernel(const float* __restrict__ A, int64_t rows,
@@ -362,7 +439,8 @@ cudaError_t attention(const Tm2dPlan& p, cudaStream_t st) {
     const dim3 grid((p.NP + kQ - 1) / kQ, p.heads, p.B);
     // fno.cpp:1799: 1.0f / std::sqrt((float)head_dim), IEEE on the host
     const float scale = 1.0f / std::sqrt(static_cast<float>(HD));
-    attention_kernel<HD><<<grid, kQ, 0, st>>>(p.q, p.k, p.v, p.NP, p.L, scale, p.ho);
+    if (p.int8) attention_online_kernel<HD><<<grid, kQ, 0, st>>>(p.q, p.k, p.v, p.NP, p.L, scale, p.ho);
+    else attention_kernel<HD><<<grid, kQ, 0, st>>>(p.q, p.k, p.v, p.NP, p.L, scale, p.ho);
     return cudaGetLastError();
 }
 
