@@ -89,7 +89,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.f,
                 stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -220,13 +220,20 @@ def run_nfx(args, ws, rank, local):
     torch.cuda.synchronize()
     rt.check()
 
-    rt.profile(True)
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        # keep the GPU busy while the clock sampler starts (untimed, like the warm-up;
+        # the same count on every rank, since each step ends in a collective)
+        for _ in range(args.preheat):
+            step()
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        rt.profile(True)
         e0.record(stream)
         for _ in range(args.steps):
             step()
@@ -419,9 +426,11 @@ def run_aux(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="nfx", choices=["nfx", "reference"])
+    ap.add_argument("--preheat", type=int, default=40,
+                    help="untimed steps run after the clock sampler starts")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

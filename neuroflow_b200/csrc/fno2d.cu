@@ -290,8 +290,9 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
              const LayerArgs p) {
     using L = LCfg<C, MH, MW, PROJ, TCX>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~static_cast<uintptr_t>(1023));
+    // 1024-byte aligned base, derived by indexing the shared array so that the
+    // compiler keeps shared-memory (not generic) loads and stores through it
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sW = smem + L::kOffW;
     uint8_t* sOnes = smem + L::kOffOnes;
     uint8_t* sA = smem + L::kOffA;
@@ -684,7 +685,13 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                         }
                     };
                     auto code_of = [&](float z) -> int {
-                        if (use_lut) return code_from_lut(z, sLut, p.lut_cells, p.lut_zlo, p.lut_inv_delta);
+                        if (use_lut) {
+                            const bool s0 = z < p.lut_split && p.lut_two;
+                            const int2 cell = lut_cell(z, sLut, p.lut_cells, s0 ? p.lut_inv0 : (p.lut_two ? p.lut_inv1 : p.lut_inv_delta),
+                                                       s0 ? p.lut_c0 : (p.lut_two ? p.lut_c1 : lut_c));
+                            const int w = z >= __int_as_float(cell.x) ? (cell.y >> 8) : cell.y;
+                            return static_cast<int>(static_cast<int8_t>(w & 0xFF));
+                        }
                         return static_cast<int>(fq_code(activation(z, p.act), s_out, zpo));
                     };
                     // Per element: dequantise + bias, the fast fake-quant offset k (x2 =
@@ -706,8 +713,15 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                             const float z = __fadd_rn(x1, __fmul_rn(kq, s_out));
                             const uint32_t prev = (j & 3) == 0 ? 0u : packed[j >> 2];
                             const uint32_t sel_lo = (0x3210u & ~(0xFu << (4 * (j & 3)))) | (4u << (4 * (j & 3)));
-                            if constexpr (decltype(lut_tag)::value) {
-                                const int2 cell = lut_cell(z, sLut, p.lut_cells, p.lut_inv_delta, lut_c);
+                            if constexpr (decltype(lut_tag)::value != 0) {
+                                int2 cell;
+                                if constexpr (decltype(lut_tag)::value == 2) {
+                                    const bool s0 = z < p.lut_split;
+                                    cell = lut_cell(z, sLut, p.lut_cells, s0 ? p.lut_inv0 : p.lut_inv1,
+                                                    s0 ? p.lut_c0 : p.lut_c1);
+                                } else {
+                                    cell = lut_cell(z, sLut, p.lut_cells, p.lut_inv_delta, lut_c);
+                                }
                                 const uint32_t sel = z >= __int_as_float(cell.x) ? sel_lo + (1u << (4 * (j & 3))) : sel_lo;
                                 packed[j >> 2] = __byte_perm(prev, static_cast<uint32_t>(cell.y), sel);
                             } else {
@@ -715,8 +729,9 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                             }
                         }
                     };
-                    if (use_lut) chunk(std::true_type{});
-                    else chunk(std::false_type{});
+                    if (use_lut && p.lut_two) chunk(std::integral_constant<int, 2>{});
+                    else if (use_lut) chunk(std::integral_constant<int, 1>{});
+                    else chunk(std::integral_constant<int, 0>{});
                     uint8_t* buf = sStage + (ew * 2 + (nstore & 1)) * 512;
                     if (nstore >= 2) {
                         if (lane == 0) tma_store_wait_read<1>();
@@ -873,8 +888,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArgs p) {
     using F = FCfg<C, MH, MW>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~static_cast<uintptr_t>(1023));
+    // 1024-byte aligned base, derived by indexing the shared array so that the
+    // compiler keeps shared-memory (not generic) loads and stores through it
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sA = smem + F::kOffA;
     uint8_t* sB = smem + F::kOffB;
     float2* sF = reinterpret_cast<float2*>(smem + F::kOffF);

@@ -30,6 +30,10 @@ struct LayerArgs {
     const int2* code_lut;  // CodeCell[lut_cells] {breakpoint, base | d << 8}
     int lut_cells;
     float lut_zlo, lut_inv_delta;
+    // two-segment tables (lut_two != 0): cell index z < lut_split ? fma(z, inv0, c0)
+    // : fma(z, inv1, c1) (CodeLut in nfx_lut.h)
+    int lut_two;
+    float lut_split, lut_inv0, lut_c0, lut_inv1, lut_c1;
     // activation of the 256 fake-quantised proj_q values (projection; nullptr: direct)
     const float* act_table;
     // projection only

@@ -91,8 +91,9 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                const GemmArgs p) {
     using C = Cfg<K, N>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~static_cast<uintptr_t>(1023));
+    // 1024-byte aligned base, derived by indexing the shared array so that the
+    // compiler keeps shared-memory (not generic) loads and stores through it
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sW = smem + C::kOffW;
     uint8_t* sOnes = smem + C::kOffOnes;
     uint8_t* sA = smem + C::kOffA;

@@ -59,7 +59,8 @@ std::vector<float> build_act_table(float s, int zp, int act) {
     return t;
 }
 
-bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::string& why) {
+bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::string& why,
+                    bool allow_split) {
     if (!(s > 0.0f) || !std::isfinite(s)) {
         why = "scale must be positive and finite";
         return false;
@@ -110,59 +111,62 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
     if (tr.empty()) {
         out.zlo = 0.0f;
         out.inv_delta = 1.0f;
+        out.zsplit = -std::numeric_limits<float>::infinity();
+        out.inv0 = out.inv1 = 1.0f;
+        out.c0 = out.c1 = 0.0f;
         out.cells.assign(1, CodeCell{std::numeric_limits<float>::infinity(),
                                      (code(0.0f) & 0xFF) | ((code(0.0f) & 0xFF) << 8)});
         return true;
     }
-    double delta = std::fmin(0.25, 0.5 * s);
-    const double lo_z = tr.front().t, hi_z = tr.back().t;
-    for (int attempt = 0; attempt < 10; ++attempt, delta *= 0.5) {
-        const double zlo = lo_z - 2.0 * delta;
-        const int ncells = static_cast<int>(std::ceil((hi_z - zlo) / delta)) + 2;
-        if (ncells > max_cells) {
-            why = "code table would need more than the allowed number of cells";
-            return false;
-        }
+    // Cells of one segment: [zlo + delta j, zlo + delta (j + 1)) widened by a margin of
+    // delta / 64 on both sides, at most one breakpoint each.  The last cell of the last
+    // segment is open to +inf.
+    auto fill = [&](double zlo, double delta, int ncells, bool open_end,
+                    std::vector<CodeCell>& cells) -> bool {
         const double margin = delta / 64.0;
-        std::vector<CodeCell> cells(static_cast<size_t>(ncells));
-        bool ok = true;
         size_t first = 0;  // first transition not left of the current cell's range
-        for (int j = 0; j < ncells && ok; ++j) {
+        for (int j = 0; j < ncells; ++j) {
             const double a = zlo + delta * j - margin;
-            const double b = (j == ncells - 1) ? 1e30 : zlo + delta * (j + 1) + margin;
+            const double b = (open_end && j == ncells - 1) ? 1e30 : zlo + delta * (j + 1) + margin;
             while (first < tr.size() && tr[first].t < a) ++first;
             const int base = first == 0 ? tr.front().before : tr[first - 1].after;
             CodeCell c{std::numeric_limits<float>::infinity(), 0};
             int d = 0;
             int n = 0;
             for (size_t k = first; k < tr.size() && tr[k].t < b; ++k) {
-                if (n == 1) {
-                    ok = false;
-                    break;
-                }
+                if (n == 1) return false;
                 c.t = tr[k].t;
                 d = tr[k].after - tr[k].before;
                 ++n;
             }
             c.packed = (base & 0xFF) | (((base + d) & 0xFF) << 8);
-            cells[j] = c;
+            cells.push_back(c);
         }
-        if (!ok) continue;
-        out.zlo = static_cast<float>(zlo);
-        out.inv_delta = static_cast<float>(1.0 / delta);
-        out.cells = std::move(cells);
-        // self-check on random points against the direct evaluation
+        return true;
+    };
+    // Every z is checked against the device's lookup (lut_index in numerics.cuh).
+    auto self_check = [&](const CodeLut& L) -> bool {
+        const int n = static_cast<int>(L.cells.size());
+        const double lo_z = tr.front().t, hi_z = tr.back().t;
         uint32_t st = 12345u;
-        for (int k = 0; k < 20000; ++k) {
+        for (int k = 0; k < 40000; ++k) {
             st = st * 1664525u + 1013904223u;
-            const float z = static_cast<float>(lo_z - 1.0 + (hi_z - lo_z + 2.0) * (st >> 8) / 16777216.0);
-            // the device's index: fma(z, inv_delta, -zlo * inv_delta), truncated
-            const float cofs = -out.zlo * out.inv_delta;
-            const float fi = std::fma(z, out.inv_delta, cofs);
+            float z = static_cast<float>(lo_z - 1.0 + (hi_z - lo_z + 2.0) * (st >> 8) / 16777216.0);
+            if (k & 1) {  // half of the points next to a breakpoint or the split
+                const float t = (k & 2) ? L.zsplit : tr[(st >> 3) % tr.size()].t;
+                if (std::isfinite(t)) {
+                    int32_t b;
+                    std::memcpy(&b, &t, 4);
+                    b += static_cast<int32_t>((st >> 11) % 9) - 4;
+                    std::memcpy(&z, &b, 4);
+                }
+            }
+            const bool s0 = z < L.zsplit;
+            const float fi = std::fma(z, s0 ? L.inv0 : L.inv1, s0 ? L.c0 : L.c1);
             int idx = static_cast<int>(fi);
             if (fi < 0.0f) idx = 0;
-            if (idx > ncells - 1) idx = ncells - 1;
-            const CodeCell& cc = out.cells[idx];
+            if (idx > n - 1) idx = n - 1;
+            const CodeCell& cc = L.cells[idx];
             const int got = static_cast<int8_t>(((z >= cc.t) ? (cc.packed >> 8) : cc.packed) & 0xFF);
             const int want = code(z);
             if (got != want) {
@@ -171,16 +175,106 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
                 for (const auto& t : tr)
                     if (std::fabs(static_cast<double>(z) - t.t) <= 64.0 * std::fabs(next_up(t.t) - t.t))
                         near = true;
-                if (!near) {
-                    why = "code table self-check failed";
-                    return false;
-                }
+                if (!near) return false;
             }
         }
         return true;
+    };
+    // Largest cell size 2^-k (2 <= k < 26) for which the transitions in [zlo, zhi) fall
+    // at most one per cell; 0 if none.
+    const double delta0 = std::fmin(0.25, 0.5 * s);
+    auto cell_size = [&](double zlo_t, double zhi_t) -> double {
+        double gap = 1e30;
+        float prev = 0.0f;
+        bool have = false;
+        for (const auto& t : tr) {
+            if (t.t < zlo_t || t.t >= zhi_t) continue;
+            if (have) gap = std::fmin(gap, static_cast<double>(t.t) - prev);
+            prev = t.t;
+            have = true;
+        }
+        double d = 0.25;
+        for (int k = 0; k < 24; ++k, d *= 0.5)
+            if (d * (1.0 + 1.0 / 16.0) < gap) return d;
+        return 0.0;
+    };
+
+    const double lo_z = tr.front().t, hi_z = tr.back().t;
+    // one segment: index fma(z, inv_delta, -zlo * inv_delta)
+    for (double delta = delta0; delta > delta0 / 1024.0; delta *= 0.5) {
+        const double zlo = lo_z - 2.0 * delta;
+        const int ncells = static_cast<int>(std::ceil((hi_z - zlo) / delta)) + 2;
+        if (ncells > max_cells) break;
+        std::vector<CodeCell> cells;
+        if (!fill(zlo, delta, ncells, true, cells)) continue;
+        CodeLut L;
+        L.zlo = static_cast<float>(zlo);
+        L.inv_delta = static_cast<float>(1.0 / delta);
+        L.zsplit = -std::numeric_limits<float>::infinity();
+        L.inv0 = L.inv1 = L.inv_delta;
+        L.c0 = L.c1 = -L.zlo * L.inv_delta;
+        L.cells = std::move(cells);
+        if (!self_check(L)) {
+            why = "code table self-check failed";
+            return false;
+        }
+        out = std::move(L);
+        return true;
     }
-    why = "no cell size gives at most one breakpoint per cell";
-    return false;
+    if (!allow_split) {
+        why = "code table would need more than the allowed number of cells";
+        return false;
+    }
+    // two segments, split in the middle of a gap between consecutive breakpoints: the
+    // dense and the sparse side of the activation get their own cell size.
+    int best_cells = max_cells + 1;
+    double best_split = 0.0, best_d0 = 0.0, best_d1 = 0.0;
+    for (size_t i = 0; i + 1 < tr.size(); ++i) {
+        const double zs = 0.5 * (static_cast<double>(tr[i].t) + tr[i + 1].t);
+        const double d0 = cell_size(-1e30, zs), d1 = cell_size(zs, 1e30);
+        if (d0 <= 0.0 || d1 <= 0.0) continue;
+        const double g = std::fmin(zs - tr[i].t, tr[i + 1].t - zs);
+        if (g < 4.0 * std::fmax(d0, d1)) continue;  // keep the split well away from breakpoints
+        const int n0 = static_cast<int>(std::ceil((zs - (lo_z - 2.0 * d0)) / d0)) + 2;
+        const int n1 = static_cast<int>(std::ceil((hi_z - (zs - 2.0 * d1)) / d1)) + 2;
+        if (n0 + n1 < best_cells) {
+            best_cells = n0 + n1;
+            best_split = zs;
+            best_d0 = d0;
+            best_d1 = d1;
+        }
+    }
+    if (best_cells > max_cells) {
+        why = "code table would need more than the allowed number of cells";
+        return false;
+    }
+    {
+        const float zs = static_cast<float>(best_split);
+        const double zlo0 = lo_z - 2.0 * best_d0;
+        const int n0 = static_cast<int>(std::ceil((static_cast<double>(zs) - zlo0) / best_d0)) + 2;
+        const double zlo1 = static_cast<double>(zs) - 2.0 * best_d1;
+        const int n1 = static_cast<int>(std::ceil((hi_z - zlo1) / best_d1)) + 2;
+        std::vector<CodeCell> cells;
+        if (!fill(zlo0, best_d0, n0, false, cells) || !fill(zlo1, best_d1, n1, true, cells)) {
+            why = "no cell size gives at most one breakpoint per cell";
+            return false;
+        }
+        CodeLut L;
+        L.zlo = static_cast<float>(zlo0);
+        L.inv_delta = 0.0f;  // not a one-segment table
+        L.zsplit = zs;
+        L.inv0 = static_cast<float>(1.0 / best_d0);
+        L.c0 = -static_cast<float>(zlo0) * L.inv0;
+        L.inv1 = static_cast<float>(1.0 / best_d1);
+        L.c1 = static_cast<float>(n0) - static_cast<float>(zlo1) * L.inv1;
+        L.cells = std::move(cells);
+        if (!self_check(L)) {
+            why = "code table self-check failed";
+            return false;
+        }
+        out = std::move(L);
+        return true;
+    }
 }
 
 uint8_t e4m3_encode(float v) {

@@ -30,8 +30,14 @@ struct CodeCell {
 };
 
 struct CodeLut {
-    float zlo = 0.f;
-    float inv_delta = 0.f;
+    float zlo = 0.f;        // one-segment tables: index fma(z, inv_delta, -zlo * inv_delta)
+    float inv_delta = 0.f;  // (0 for a two-segment table)
+    // General index: z < zsplit ? fma(z, inv0, c0) : fma(z, inv1, c1), truncated and
+    // clamped to the cells.  One-segment tables have zsplit = -inf and (inv1, c1) equal
+    // to the form above; two-segment tables give the sides of the split their own cell
+    // size (the negative branch of GELU needs far coarser cells than the positive one).
+    float zsplit = 0.f;
+    float inv0 = 0.f, c0 = 0.f, inv1 = 0.f, c1 = 0.f;
     std::vector<CodeCell> cells;
 };
 
@@ -41,8 +47,10 @@ float act_ref(float z, int act);
 float fq_code_ref(float v, float s, float zp);
 
 // Build the z -> code table for (s, zp, act).  Returns false (with a reason) if no
-// table with at most `max_cells` cells and one breakpoint per cell exists.
-bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::string& why);
+// table with at most `max_cells` cells and one breakpoint per cell exists (with
+// `allow_split`, two segments of different cell sizes are tried after one).
+bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::string& why,
+                    bool allow_split = false);
 
 // act_ref((k - zp) * s) for k = -128..127 (index k + 128).
 std::vector<float> build_act_table(float s, int zp, int act);

@@ -322,12 +322,19 @@ void fno2d_enable_int8(nfx_runtime* rt) {
             std::string why;
             a.code_lut = nullptr;
             a.lut_cells = 0;
-            if (nfx::build_code_lut(a.fq_out.scale, a.fq_out.zp, a.act, 3072, lut, why)) {
+            a.lut_two = 0;
+            if (nfx::build_code_lut(a.fq_out.scale, a.fq_out.zp, a.act, 3072, lut, why, true)) {
                 a.code_lut = reinterpret_cast<const int2*>(upload(rt, lut.cells.data(), lut.cells.size()));
                 if (a.code_lut) {
                     a.lut_cells = static_cast<int>(lut.cells.size());
                     a.lut_zlo = lut.zlo;
                     a.lut_inv_delta = lut.inv_delta;
+                    a.lut_two = std::isfinite(lut.zsplit) ? 1 : 0;
+                    a.lut_split = lut.zsplit;
+                    a.lut_inv0 = lut.inv0;
+                    a.lut_c0 = lut.c0;
+                    a.lut_inv1 = lut.inv1;
+                    a.lut_c1 = lut.c1;
                 }
             }
         } else {

@@ -95,3 +95,26 @@ def test_fno2d_growing_batch_reuses_handle(tmp_path):
         rt.run(x, got)
         st = _stats(got, o.fno2d_forward(m, x, mode=1), step)
         assert st["rel_l2"] < 2e-2 and st["frac_diff"] < 0.05, (B, st)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("scale,zp", [(0.0014373305020853877, 1), (0.0005, 0)])
+def test_fno2d_int8_two_segment_code_table(tmp_path, scale, zp):
+    """A layer output scale this small needs more uniform table cells than fit in
+    shared memory; the executor then splits the z -> code table at a gap between
+    breakpoints into a coarse (GELU's negative branch) and a fine segment."""
+    from neuroflow_b200.ir import PerTensor
+    from neuroflow_b200.runtime import InferenceRuntime
+    m, _ = _model(tmp_path, L=3)
+    m.qparams["locs.1.output"] = PerTensor(scale, zp)
+    path = os.path.join(str(tmp_path), "small_scale.nneuroir")
+    ir.write(path, m)
+    x = synth.fno2d_inputs(np.random.default_rng(5), 2, 32, 32)
+    want = Oracle().fno2d_forward(m, x, mode=1)
+    rt = InferenceRuntime(path)
+    rt.enable_int8_gemm()
+    got = np.zeros_like(want)
+    rt.run(x, got)
+    st = _stats(got, want, m.qparams["proj_out.output"].scale)
+    print(scale, zp, st)
+    assert st["rel_l2"] < 2e-2 and st["frac_diff"] < 0.05, st
