@@ -43,61 +43,74 @@ __device__ __forceinline__ float activation(float z, int act) {
 }
 
 // ---------------------------------------------------------------------------
+// Division-free code of v under (s, zp) with the fast-path test of fq_code_fast
+// (numerics.cuh), in the form the epilogues pack directly:
+//   r = v * (1/s);  t = r + (1.5 * 2^23 + zp)
+// rounds r to an integer in t's last place (t has unit spacing for |r| < 2^22), so
+// k = t - (1.5 * 2^23 + zp) = rint(r) exactly, and t clamped to 1.5 * 2^23 +
+// [-128, 127] carries the clamped code clamp(rint(r) + zp) as its low byte (and as
+// bits(t) - 0x4B400000).  `bad` is set where the element needs the exact division:
+// r within 2^-13 of a half-integer (where rint and std::round may differ too), or NaN.
+// ---------------------------------------------------------------------------
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+__device__ __forceinline__ float fast_code_t(float v, float inv_s, float magic_zp, bool& bad) {
+    const float r = __fmul_rn(v, inv_s);
+    const float t = __fadd_rn(r, magic_zp);
+    const float k = __fsub_rn(t, magic_zp);
+    bad = !(fabsf(__fsub_rn(r, k)) < 0.4998779296875f);
+    return fminf(fmaxf(t, kMagic - 128.0f), kMagic + 127.0f);
+}
+
+// ---------------------------------------------------------------------------
 // lift: x (M, in_ch) fp32 -> codes (M, C) with the lift.output qparams.
 // fno.cpp:848-853 (Linear + fake-quant), fno.cpp:51-80 (the dot product from the bias).
+// One thread per (point, 16 channels); the channel group of a thread is fixed, so its
+// weights and biases stay in registers for the whole grid-stride loop.
 // ---------------------------------------------------------------------------
-template <int C>
+template <int C, int IN>
 __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, int64_t M,
-                                                   int in_ch, const float* __restrict__ w,
+                                                   const float* __restrict__ w,
                                                    const float* __restrict__ b, float s, int zp,
                                                    float inv_s, int8_t* __restrict__ codes) {
-    // one thread per (point, group of 16 channels)
     constexpr int kG = C / 16;
-    __shared__ float4 sw4[C * 8 / 4];  // transposed [k][c]: 16 channels of one k in 4 loads
-    __shared__ float sb[C];
-    float* sw = reinterpret_cast<float*>(sw4);
-    for (int i = threadIdx.x; i < C * in_ch; i += blockDim.x) sw[(i % in_ch) * C + i / in_ch] = w[i];
-    for (int i = threadIdx.x; i < C; i += blockDim.x) sb[i] = b[i];
-    __syncthreads();
+    static_assert(256 % kG == 0, "channel groups per block");
+    constexpr int nu = linear_unfused_len(IN);
+    const int64_t t0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    const int o0 = static_cast<int>(t0 % kG) * 16;
+    float wr[IN][16], br[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        br[j] = __ldg(b + o0 + j);
+#pragma unroll
+        for (int k = 0; k < IN; ++k) wr[k][j] = __ldg(w + (o0 + j) * IN + k);
+    }
+    const float magic_zp = kMagic + static_cast<float>(zp);
     const float zpf = static_cast<float>(zp);
     const int64_t n = M * kG;
-    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < n;
-         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t t = t0; t < n; t += stride) {
         const int64_t m = t / kG;
-        const int o0 = static_cast<int>(t % kG) * 16;
-        float acc[16];
+        float xv[IN];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = sb[o0 + j];
-        const int nu = linear_unfused_len(in_ch);
-        for (int k = 0; k < in_ch; ++k) {
-            const float xv = __ldg(x + m * in_ch + k);
-            const float4* wk = sw4 + (k * C + o0) / 4;
-#pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-                const float4 wv = wk[j4];
-                acc[4 * j4 + 0] = linear_step(acc[4 * j4 + 0], xv, wv.x, k >= nu);
-                acc[4 * j4 + 1] = linear_step(acc[4 * j4 + 1], xv, wv.y, k >= nu);
-                acc[4 * j4 + 2] = linear_step(acc[4 * j4 + 2], xv, wv.z, k >= nu);
-                acc[4 * j4 + 3] = linear_step(acc[4 * j4 + 3], xv, wv.w, k >= nu);
-            }
-        }
-        uint32_t words[4];
+        for (int k = 0; k < IN; ++k) xv[k] = __ldg(x + m * IN + k);
+        uint32_t words[4] = {0u, 0u, 0u, 0u};
         uint32_t badmask = 0;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
+            float acc = br[j];
+#pragma unroll
+            for (int k = 0; k < IN; ++k) acc = linear_step(acc, xv[k], wr[k][j], k >= nu);
             bool bad;
-            const float q = fq_code_try(acc[j], inv_s, zpf, bad);
+            const float tc = fast_code_t(acc, inv_s, magic_zp, bad);
             badmask |= static_cast<uint32_t>(bad) << j;
-            const uint32_t byte = static_cast<uint32_t>(static_cast<int>(q)) & 0xFFu;
-            if ((j & 3) == 0) words[j >> 2] = byte;
-            else words[j >> 2] |= byte << (8 * (j & 3));
+            const uint32_t sel = (0x3210u & ~(0xFu << (4 * (j & 3)))) | (4u << (4 * (j & 3)));
+            words[j >> 2] = __byte_perm(words[j >> 2], __float_as_uint(tc), sel);
         }
-        while (badmask) {  // rare: quotient near a half-integer, huge or NaN
+        while (badmask) {  // rare: quotient next to a half-integer, huge or NaN
             const int j = __ffs(badmask) - 1;
             badmask &= badmask - 1;
-            float a = sb[o0 + j];
-            for (int k = 0; k < in_ch; ++k)
-                a = linear_step(a, __ldg(x + m * in_ch + k), sw[k * C + o0 + j], k >= nu);
+            float a = __ldg(b + o0 + j);
+            for (int k = 0; k < IN; ++k) a = linear_step(a, xv[k], __ldg(w + (o0 + j) * IN + k), k >= nu);
             const uint32_t byte = static_cast<uint32_t>(static_cast<int>(fq_code(a, s, zpf))) & 0xFFu;
             words[j >> 2] = (words[j >> 2] & ~(0xFFu << (8 * (j & 3)))) | (byte << (8 * (j & 3)));
         }
@@ -165,45 +178,76 @@ __global__ void __launch_bounds__(C * MW) spec_fwd_kernel(const int8_t* __restri
 }
 
 // ---------------------------------------------------------------------------
-// spec_mix: grid (MH*MW, ceil(B / SB)), 256 threads.  Y[b][m][o] = sum_i X[b][m][i] W[m][i][o]
-// with X = sum over the row-block partials (fixed order) and W re-laid as [m][i][o].
+// spec_mix: grid (MH*MW, ceil(B / 32)), 256 threads, dynamic shared memory
+// kMixSmem.  Y[b][m][o] = sum_i X[b][m][i] W[m][i][o] (fno.cpp:740-764), with X the
+// sum of the row-block partials (fixed order) and W re-laid as [m][i][o].  A block
+// holds one mode's weights and 32 samples' spectra; each thread accumulates 2 samples
+// x 4 outputs, so one pair of shared loads feeds 8 complex products.
 // ---------------------------------------------------------------------------
+constexpr int kMixSamples = 32;
+template <int C>
+constexpr int mix_smem_bytes() { return (C * C + C * (kMixSamples + 1)) * 8; }
+
 template <int C, int MH, int MW>
 __global__ void __launch_bounds__(256) spec_mix_kernel(const float2* __restrict__ xpart, int nHB,
-                                                       int B, int SB,
-                                                       const float2* __restrict__ wspec,
+                                                       int B, const float2* __restrict__ wspec,
                                                        float2* __restrict__ Y) {
     constexpr int M = MH * MW;
-    __shared__ float2 sw[C * C];
-    __shared__ float2 sx[256 / C][C];
+    constexpr int SB = kMixSamples;
+    static_assert(C == 64, "thread layout is for width 64");
+    extern __shared__ float2 smix[];
+    float2* sw = smix;               // [i][o]
+    float2* sx = smix + C * C;       // [i][SB + 1]
     const int m = blockIdx.x;
-    for (int i = threadIdx.x; i < C * C; i += 256) sw[i] = wspec[static_cast<int64_t>(m) * C * C + i];
-    constexpr int kLanes = 256 / C;  // samples processed at once
-    const int o = threadIdx.x % C, sl = threadIdx.x / C;
     const int b0 = blockIdx.y * SB;
-    const int b1 = min(B, b0 + SB);
-    for (int bb = b0; bb < b1; bb += kLanes) {
-        __syncthreads();
-        const int b = bb + sl;
-        if (b < b1) {
-            float2 s = make_float2(0.f, 0.f);
+    const int nb = min(SB, B - b0);
+    {
+        const float4* src = reinterpret_cast<const float4*>(wspec + static_cast<int64_t>(m) * C * C);
+        float4* dst = reinterpret_cast<float4*>(sw);
+        for (int i = threadIdx.x; i < C * C / 2; i += 256) dst[i] = src[i];
+    }
+    for (int idx = threadIdx.x; idx < SB * C; idx += 256) {
+        const int sl = idx / C, i = idx % C;
+        float2 v = make_float2(0.f, 0.f);
+        if (sl < nb) {
+            const float2* p = xpart + (static_cast<int64_t>(b0 + sl) * nHB * M + m) * C + i;
             for (int hb = 0; hb < nHB; ++hb) {
-                const float2 v = xpart[((static_cast<int64_t>(b) * nHB + hb) * M + m) * C + o];
-                s.x += v.x;
-                s.y += v.y;
+                const float2 u = p[static_cast<int64_t>(hb) * M * C];
+                v.x += u.x;
+                v.y += u.y;
             }
-            sx[sl][o] = s;
         }
-        __syncthreads();
-        if (b < b1) {
-            float yr = 0.f, yi = 0.f;
-            for (int i = 0; i < C; ++i) {
-                const float2 xv = sx[sl][i];
-                const float2 wv = sw[i * C + o];
-                yr = fmaf(xv.x, wv.x, fmaf(-xv.y, wv.y, yr));
-                yi = fmaf(xv.x, wv.y, fmaf(xv.y, wv.x, yi));
+        sx[i * (SB + 1) + sl] = v;
+    }
+    __syncthreads();
+    const int og = threadIdx.x & 15, sg = threadIdx.x >> 4;  // outputs og + 16k, samples sg + 16j
+    float yr[2][4], yi[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) yr[j][k] = yi[j][k] = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < C; ++i) {
+        float2 xv[2], wv[4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) xv[j] = sx[i * (SB + 1) + sg + 16 * j];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) wv[k] = sw[i * C + og + 16 * k];
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                yr[j][k] = fmaf(xv[j].x, wv[k].x, fmaf(-xv[j].y, wv[k].y, yr[j][k]));
+                yi[j][k] = fmaf(xv[j].x, wv[k].y, fmaf(xv[j].y, wv[k].x, yi[j][k]));
             }
-            Y[(static_cast<int64_t>(b) * M + m) * C + o] = make_float2(yr, yi);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int sl = sg + 16 * j;
+        if (sl < nb) {
+            float2* dst = Y + (static_cast<int64_t>(b0 + sl) * M + m) * C;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) dst[og + 16 * k] = make_float2(yr[j][k], yi[j][k]);
         }
     }
 }
@@ -839,6 +883,290 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
 }
 
 // ---------------------------------------------------------------------------
+// proj: the projection (fno.cpp:972-993) over 128-point tiles.
+//   q = LinearForwardBatched(codes, proj_q) + bias   (tcgen05 kind::i8, as the layers)
+//   g = act(fake_quant(q, proj_q.output))            (the 256-entry activation table)
+//   y = fake_quant(proj_out(g), proj_out.output)     (the reference's sequential
+//                                                      out_ch-wide dot product)
+// The proj_out dot product runs over a point's 64 activations in order, so one thread
+// owns a point and all its columns.  Four epilogue warp groups (one warp per TMEM lane
+// quadrant each) take turns over the CTA's tiles; group g drains accumulator stage g,
+// so four tiles are in flight and no activation leaves the registers.
+// ---------------------------------------------------------------------------
+template <int C>
+struct PCfg {
+    static constexpr int kGroups = 4;
+    static constexpr int kEpiWarps = 4 * kGroups;
+    static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
+    static constexpr int kABytes = 128 * C;
+    static constexpr int kStages = 4;
+    static constexpr int kOnesCol = C;
+    static constexpr int kAccCols = ((C + 16 + 31) / 32) * 32;
+    static constexpr int kAccStages = kGroups;
+    static constexpr int kTmemCols = pow2ceil(kAccStages * kAccCols);
+    static_assert(kTmemCols <= 512, "TMEM");
+    static constexpr int up1k(int v) { return (v + 1023) / 1024 * 1024; }
+    static constexpr int kOffW = 0;
+    static constexpr int kOffOnes = up1k(C * C);
+    static constexpr int kOffA = kOffOnes + 1024;
+    static constexpr int kOffCol = kOffA + kStages * kABytes;          // float4 [C]
+    static constexpr int kOffAct = kOffCol + C * 16;                    // float [256]
+    static constexpr int kOffWout = kOffAct + 256 * 4;                  // float [4][C], [4]
+    static constexpr int kOffBars = kOffWout + 4 * C * 4 + 16;
+    static constexpr int kNumBars = 2 * kStages + 2 * kAccStages;
+    static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
+    static_assert(kSmemBytes <= 227 * 1024, "smem");
+};
+
+// Wait for this thread's outstanding tcgen05.ld; naming the destination registers
+// keeps their uses after the wait.
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+template <int C>
+__global__ void __launch_bounds__(PCfg<C>::kThreads, 1)
+proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p) {
+    using L = PCfg<C>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* sW = smem + L::kOffW;
+    uint8_t* sOnes = smem + L::kOffOnes;
+    uint8_t* sA = smem + L::kOffA;
+    float4* sCol = reinterpret_cast<float4*>(smem + L::kOffCol);  // {sW*s_in, zp_w, zp_in*sum_w, bias}
+    float* sAct = reinterpret_cast<float*>(smem + L::kOffAct);
+    float* sWout = reinterpret_cast<float*>(smem + L::kOffWout);  // [out_ch][C]
+    float* sBout = sWout + 4 * C;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBars);
+    uint64_t* empty = full + L::kStages;
+    uint64_t* accFull = empty + L::kStages;
+    uint64_t* accEmpty = accFull + L::kAccStages;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(accEmpty + L::kAccStages);
+    volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int num_tiles = static_cast<int>((p.M + 127) / 128);
+    const int t_begin = static_cast<int>(static_cast<int64_t>(num_tiles) * blockIdx.x / gridDim.x);
+    const int t_end = static_cast<int>(static_cast<int64_t>(num_tiles) * (blockIdx.x + 1) / gridDim.x);
+    const bool use_act = p.act_table != nullptr && p.fq_out.kind == 1;
+
+    {
+        constexpr int kChunks = C / 16;
+        for (int idx = threadIdx.x; idx < C * kChunks; idx += L::kThreads) {
+            const int o = idx / kChunks, c = idx % kChunks;
+            const uint4 v = *reinterpret_cast<const uint4*>(p.Wq + o * C + c * 16);
+            *reinterpret_cast<uint4*>(sW + swz_offset(o * C + c * 16, C)) = v;
+        }
+        for (int idx = threadIdx.x; idx < 1024 / 16; idx += L::kThreads) {
+            const uint32_t one = (idx * 16 < C) ? 0x01010101u : 0u;  // row 0 = ones
+            *reinterpret_cast<uint4*>(sOnes + idx * 16) = make_uint4(one, one, one, one);
+        }
+        for (int o = threadIdx.x; o < C; o += L::kThreads)
+            sCol[o] = make_float4(__fmul_rn(p.scale_w[o], p.s_in), __int_as_float(p.zp_w[o]),
+                                  __int_as_float(p.zp_in * p.sum_w[o]), p.bias[o]);
+        for (int i = threadIdx.x; i < p.out_ch * C; i += L::kThreads) sWout[i] = p.w_out[i];
+        for (int i = threadIdx.x; i < p.out_ch; i += L::kThreads) sBout[i] = p.b_out[i];
+        if (use_act)
+            for (int i = threadIdx.x; i < 256; i += L::kThreads) sAct[i] = p.act_table[i];
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < L::kStages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            for (int s = 0; s < L::kAccStages; ++s) {
+                mbar_init(&accFull[s], 1);
+                mbar_init(&accEmpty[s], 4);  // the group's four warps
+            }
+            *sAbort = 0;
+            fence_mbar_init();
+        }
+        if (warp == 1) tmem_alloc(sTmem, L::kTmemCols);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    const uint32_t tmem_base = *sTmem;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            prefetch_tmap(&tmIn);
+            int it = 0;
+            for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+                const int s = it % L::kStages;
+                const uint32_t ph = (it / L::kStages) & 1;
+                if (!mbar_wait(&empty[s], ph ^ 1, sAbort)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitSlotFree);
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], L::kABytes);
+                tma_load_2d(sA + s * L::kABytes, &tmIn, &full[s], 0, tile * 128);
+            }
+            for (int j = (it > L::kStages ? it - L::kStages : 0); j < it; ++j)
+                if (!mbar_wait(&full[j % L::kStages], (j / L::kStages) & 1, sAbort)) break;
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (elect_one()) {
+            int it = 0;
+            for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+                const int s = it % L::kStages;
+                const uint32_t ph = (it / L::kStages) & 1;
+                const int a = it % L::kAccStages;
+                const uint32_t aph = (it / L::kAccStages) & 1;
+                if (!mbar_wait(&accEmpty[a], aph ^ 1, sAbort)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitAccFree);
+                    break;
+                }
+                if (!mbar_wait(&full[s], ph, sAbort)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitTmaFull);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + a * L::kAccCols;
+                const uint32_t aBase = smem_u32(sA + s * L::kABytes);
+#pragma unroll
+                for (int kk = 0; kk < C / 32; ++kk) {
+                    const uint64_t ad = umma_desc(aBase + kk * 32, C);
+                    const uint64_t wd = umma_desc(smem_u32(sW) + kk * 32, C);
+                    const uint64_t od = umma_desc(smem_u32(sOnes) + kk * 32, C);
+                    mma_i8(d, ad, wd, idesc_i8(C), kk > 0 ? 1u : 0u);
+                    mma_i8(d + L::kOnesCol, ad, od, idesc_i8(16), kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&empty[s]);
+                mma_commit(&accFull[a]);
+            }
+            if (it > 0) {
+                const int j = it - 1;
+                mbar_wait(&accFull[j % L::kAccStages], (j / L::kAccStages) & 1, sAbort);
+            }
+        }
+        __syncwarp();
+    } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + L::kEpiWarps) {
+        const int ew = warp - kEpiWarp0;
+        const int quad = warp & 3;
+        const int grp = ew >> 2;
+        const int row = quad * 32 + lane;
+        const float s_out = p.fq_out.scale, inv_out = p.fq_out.inv_scale;
+        const float zpo = static_cast<float>(p.fq_out.zp);
+        const float magic_zp = kMagic + zpo;
+        constexpr int nu = linear_unfused_len(C);
+        const int out_ch = p.out_ch;
+        for (int it = grp; t_begin + it < t_end; it += L::kGroups) {
+            const int tile = t_begin + it;
+            const uint32_t aph = (it / L::kGroups) & 1;
+            if (!mbar_wait(&accFull[grp], aph, sAbort)) {
+                *sAbort = 1;
+                atomicOr(p.err, kErrWaitAccFull);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + grp * L::kAccCols;
+            uint32_t raw[2][16];
+            uint32_t sum_u;
+            tmem_ld1(tbase + L::kOnesCol, sum_u);
+            tmem_ld16_async(tbase, raw[0]);
+            tmem_wait_ld16(raw[0]);
+            asm volatile("" : "+r"(sum_u));  // sum_u is used after the wait above
+            const int rconst = C * p.zp_in - 2 * static_cast<int>(sum_u);
+            float acc_out[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc_out[j] = j < out_ch ? sBout[j] : 0.0f;
+#pragma unroll
+            for (int c = 0; c < C / 16; ++c) {
+                uint32_t (&cur)[16] = raw[c & 1];
+                if (c + 1 < C / 16) tmem_ld16_async(tbase + (c + 1) * 16, raw[(c + 1) & 1]);
+                float g[16];
+                uint32_t bad = 0;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float4 cp = sCol[c * 16 + j];
+                    const int vint = static_cast<int>(cur[j]) + __float_as_int(cp.y) * rconst -
+                                     __float_as_int(cp.z);
+                    const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
+                    if (use_act) {
+                        bool b;
+                        const float tc = fast_code_t(v, inv_out, magic_zp, b);
+                        bad |= static_cast<uint32_t>(b) << j;
+                        g[j] = sAct[__float_as_int(tc) - (0x4B400000 - 128)];
+                    } else {
+                        g[j] = activation(apply_fq(v, p.fq_out), p.act);
+                    }
+                }
+                while (bad) {  // rare: exact division for quotients next to a half-integer
+                    const int j = __ffs(bad) - 1;
+                    bad &= bad - 1;
+                    const float4 cp = sCol[c * 16 + j];
+                    uint32_t rj = 0;
+#pragma unroll
+                    for (int k = 0; k < 16; ++k)
+                        if (k == j) rj = cur[k];
+                    const int vint = static_cast<int>(rj) + __float_as_int(cp.y) * rconst -
+                                     __float_as_int(cp.z);
+                    const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
+                    const float gj = sAct[static_cast<int>(fq_code(v, s_out, zpo)) + 128];
+#pragma unroll
+                    for (int k = 0; k < 16; ++k)
+                        if (k == j) g[k] = gj;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int o = c * 16 + j;
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj)
+                        if (jj < out_ch) acc_out[jj] = linear_step(acc_out[jj], g[j], sWout[jj * C + o], o >= nu);
+                }
+                if (c + 1 < C / 16) tmem_wait_ld16(raw[(c + 1) & 1]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&accEmpty[grp]);
+            const int64_t m = static_cast<int64_t>(tile) * 128 + row;
+            if (m < p.M) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (j >= out_ch) break;
+                    float yv = acc_out[j];
+                    if (p.fq_final.kind == 1) {
+                        const float zf = static_cast<float>(p.fq_final.zp);
+                        const float q = fq_code_fast(yv, p.fq_final.scale, p.fq_final.inv_scale, zf);
+                        yv = __fmul_rn(__fsub_rn(q, zf), p.fq_final.scale);
+                    } else {
+                        yv = apply_fq(yv, p.fq_final);
+                    }
+                    p.y[m * out_ch + j] = yv;
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, L::kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // spec_fwd_tc: the forward transform of a layer on tensor cores (W == 128).
 //
 // Row DFT (along W) as an exact integer GEMM: for a pair of grid rows,
@@ -1125,10 +1453,19 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
     // lift
     {
         const int64_t blocks64 = (M * (C / 16) + 255) / 256;
-        const int grid = static_cast<int>(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
+        const int grid = static_cast<int>(blocks64 < 148 * 8 ? blocks64 : 148 * 8);
         if (pl.timer) pl.timer->begin("fno2d_lift", st);
-        lift_kernel<C><<<grid, 256, 0, st>>>(pl.x, M, pl.in_ch, pl.lift_w, pl.lift_b,
-                                             pl.lift_s, pl.lift_zp, pl.lift_inv_s, pl.codes[0]);
+        switch (pl.in_ch) {
+#define NFX_LIFT(n)                                                                            \
+    case n:                                                                                    \
+        lift_kernel<C, n><<<grid, 256, 0, st>>>(pl.x, M, pl.lift_w, pl.lift_b, pl.lift_s,       \
+                                                pl.lift_zp, pl.lift_inv_s, pl.codes[0]);        \
+        break;
+            NFX_LIFT(1) NFX_LIFT(2) NFX_LIFT(3) NFX_LIFT(4) NFX_LIFT(5) NFX_LIFT(6) NFX_LIFT(7)
+            NFX_LIFT(8)
+#undef NFX_LIFT
+            default: return cudaErrorInvalidValue;
+        }
         if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
@@ -1164,10 +1501,11 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
         {
-            const int SB = 32;
+            auto k = spec_mix_kernel<C, MH, MW>;
+            if ((e = set_smem(k, mix_smem_bytes<C>())) != cudaSuccess) return e;
             if (pl.timer) pl.timer->begin("fno2d_spec_mix", st);
-            spec_mix_kernel<C, MH, MW><<<dim3(MH * MW, (pl.B + SB - 1) / SB), 256, 0, st>>>(
-                pl.xpart, nHB, pl.B, SB, pl.layer[i].wspec, pl.Y);
+            k<<<dim3(MH * MW, (pl.B + kMixSamples - 1) / kMixSamples), 256, mix_smem_bytes<C>(), st>>>(
+                pl.xpart, nHB, pl.B, pl.layer[i].wspec, pl.Y);
             if (pl.timer) pl.timer->end(st);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
@@ -1203,9 +1541,9 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
         cur ^= 1;
     }
     {
-        using LC = LCfg<C, MH, MW, true, false>;
-        auto k = layer_kernel<C, MH, MW, true, false>;
-        if ((e = set_smem(k, LC::kSmemBytes)) != cudaSuccess) return e;
+        using PC = PCfg<C>;
+        auto k = proj_kernel<C>;
+        if ((e = set_smem(k, PC::kSmemBytes)) != cudaSuccess) return e;
         CUtensorMap tin;
         if (!encode_2d(&tin, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur], C, M, C, C, 128, C))
             return cudaErrorInvalidValue;
@@ -1216,7 +1554,7 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
         a.err = pl.err;
         a.y = pl.y;
         if (pl.timer) pl.timer->begin("fno2d_proj", st);
-        k<<<grid_l, LC::kThreads, LC::kSmemBytes, st>>>(tin, tin, a);
+        k<<<grid_l, PC::kThreads, PC::kSmemBytes, st>>>(tin, a);
         if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }

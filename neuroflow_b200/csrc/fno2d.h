@@ -93,6 +93,10 @@ struct Fno2dPlan {
     KernelTimer* timer;    // nullptr unless profiling is enabled
 };
 
+// Row blocks per sample of the forward transform's partial spectra (B x this many
+// partials of MH*MW*C complex values are written by spec_fwd and summed by spec_mix).
+inline int fno2d_row_blocks(int H) { return H < 4 ? H : 4; }
+
 bool fno2d_supported(int C, int MH, int MW);
 cudaError_t fno2d_run(const Fno2dPlan& plan, cudaStream_t stream);
 

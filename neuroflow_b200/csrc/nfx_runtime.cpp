@@ -441,7 +441,7 @@ int ensure_buffers(nfx_runtime* rt, int B, int H, int W) {
     }
     const auto& pl = rt->plan;
     const size_t M = static_cast<size_t>(B) * H * W;
-    const int nHB = H < 8 ? H : 8;
+    const int nHB = nfx::fno2d_row_blocks(H);
     const size_t sizes[4] = {M * pl.C, M * pl.C,
                              static_cast<size_t>(B) * nHB * pl.MH * pl.MW * pl.C * sizeof(float2),
                              static_cast<size_t>(B) * pl.MH * pl.MW * pl.C * sizeof(float2)};
@@ -562,7 +562,7 @@ int fno2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
     pl.B = B;
     pl.H = H;
     pl.W = W;
-    pl.HB = H / (H < 8 ? H : 8);
+    pl.HB = H / nfx::fno2d_row_blocks(H);
     pl.x = dx;
     pl.y = dy;
     pl.codes[0] = static_cast<int8_t*>(rt->act_bufs[0]);
@@ -1169,7 +1169,7 @@ int fno2d_noalloc_plan(nfx_runtime* rt, const float* x, const int64_t* x_shape, 
     plan->B = B;
     plan->H = H;
     plan->W = W;
-    plan->HB = H / (H < 8 ? H : 8);
+    plan->HB = H / nfx::fno2d_row_blocks(H);
     plan->x = x;
     plan->y = y;
     plan->fwd_limbs = nullptr;
