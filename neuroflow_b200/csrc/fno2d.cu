@@ -444,7 +444,7 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
             for (int tile = t_begin; tile < t_end; ++tile, ++it) {
                 const int s = it % L::kStages;
                 const uint32_t ph = (it / L::kStages) & 1;
-                if (!mbar_wait(&empty[s], ph ^ 1, sAbort)) {
+                if (!mbar_wait_backoff(&empty[s], ph ^ 1, sAbort, 1024)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitSlotFree);
                     break;
@@ -453,7 +453,7 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                 tma_load_2d(sA + s * L::kABytes, &tmIn, &full[s], 0, tile * 128);
             }
             for (int j = (it > L::kStages ? it - L::kStages : 0); j < it; ++j)
-                if (!mbar_wait(&full[j % L::kStages], (j / L::kStages) & 1, sAbort)) break;
+                if (!mbar_wait_backoff(&full[j % L::kStages], (j / L::kStages) & 1, sAbort, 1024)) break;
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -464,18 +464,18 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
                 const uint32_t ph = (it / L::kStages) & 1;
                 const int a = it % L::kAccStages;
                 const uint32_t aph = (it / L::kAccStages) & 1;
-                if (!mbar_wait(&accEmpty[a], aph ^ 1, sAbort)) {
+                if (!mbar_wait_backoff(&accEmpty[a], aph ^ 1, sAbort, 128)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitAccFree);
                     break;
                 }
-                if (!mbar_wait(&full[s], ph, sAbort)) {
+                if (!mbar_wait_backoff(&full[s], ph, sAbort, 128)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitTmaFull);
                     break;
                 }
                 if constexpr (TCX && !PROJ) {
-                    if (!mbar_wait(&tReady[it & 1], (it >> 1) & 1, sAbort)) {
+                    if (!mbar_wait_backoff(&tReady[it & 1], (it >> 1) & 1, sAbort, 128)) {
                         *sAbort = 1;
                         atomicOr(p.err, kErrWaitDrain);
                         break;
@@ -516,7 +516,7 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
             }
             if (it > 0) {
                 const int j = it - 1;
-                mbar_wait(&accFull[j % L::kAccStages], (j / L::kAccStages) & 1, sAbort);
+                mbar_wait_backoff(&accFull[j % L::kAccStages], (j / L::kAccStages) & 1, sAbort, 1024);
             }
         }
         __syncwarp();
@@ -882,6 +882,440 @@ layer_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ C
     }
 }
 
+// Wait for this thread's outstanding tcgen05.ld; naming the destination registers
+// keeps their uses after the wait.
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+// ---------------------------------------------------------------------------
+// layer_tc: the local layer + spectral branch of one FNO2d layer on W == 128 grids
+// (one 128-point tile = one grid row), with the work split over warp roles:
+//   warp 0       TMA producer of the layer-input codes (ring of kStages tiles)
+//   warp 1       MMA issuer and TMEM owner: per tile the int8 local GEMM, the ones
+//                block (sum_a) and the 3xTF32 inverse W-transform x1 = Binv T
+//   warps 2-5    T builders (one per SM sub-partition): the H-direction inverse
+//                transform T[o][kw] of the tile's row from the cached spectrum Y,
+//                split into tf32 hi/lo halves, double-buffered
+//   warps 6-21   epilogue: 4 warps per TMEM lane quadrant, 16 columns each.  Per
+//                element: dequantise + bias (constant-bank operands), the fast
+//                fake-quant offset k, z = x1 + k s, the next code from the table.
+// The epilogue reads both accumulators into registers and frees the TMEM stage
+// before any arithmetic, so the MMA of the tile after next overlaps it.
+// ---------------------------------------------------------------------------
+template <int C, int MH, int MW>
+struct TCfg {
+    static constexpr int kTBuild0 = 2;                  // first T-builder warp
+    static constexpr int kTBuildWarps = 4;
+    static constexpr int kEpi0 = kTBuild0 + kTBuildWarps;  // 6: quadrant = warp & 3
+    static constexpr int kEpiWarps = 16;
+    static constexpr int kThreads = 32 * (kEpi0 + kEpiWarps);
+    static constexpr int kABytes = 128 * C;
+    static constexpr int kStages = 3;
+    static constexpr int kOnesCol = C;
+    static constexpr int kX1Col = ((C + 16 + 31) / 32) * 32;
+    static constexpr int kAccCols = kX1Col + C;
+    static constexpr int kAccStages = 2;
+    static constexpr int kTmemCols = pow2ceil(kAccStages * kAccCols);
+    static constexpr int kKx = 32;                      // padded K of the x1 MMA (fp32)
+    static_assert(2 * MW <= kKx, "x1 MMA K");
+    static_assert(C == 64, "the epilogue is laid out for width 64");
+    static constexpr int up1k(int v) { return (v + 1023) / 1024 * 1024; }
+    static constexpr int kOffW = 0;
+    static constexpr int kOffOnes = up1k(C * C);
+    static constexpr int kOffA = kOffOnes + 1024;
+    static constexpr int kOffStage = kOffA + kStages * kABytes;        // 16 warps x 2 x 512
+    static constexpr int kOffY = kOffStage + kEpiWarps * 2 * 512;
+    static constexpr int kYBytes = MH * MW * C * 8;
+    static constexpr int kOffBinv = up1k(kOffY + kYBytes);
+    static constexpr int kBinvBytes = 2 * 128 * kKx * 4;                // hi, lo
+    static constexpr int kOffTop = kOffBinv + kBinvBytes;
+    static constexpr int kTopBytes = 2 * 2 * C * kKx * 4;               // 2 buffers x (hi, lo)
+    static constexpr int kOffLut = kOffTop + kTopBytes;
+    static constexpr int kLutBytes = kLutMaxCells * 8;
+    static constexpr int kOffCol = kOffLut + kLutBytes;                // float4 [C]
+    static constexpr int kOffBars = kOffCol + C * 16;
+    static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2 + 2;
+    static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
+    static_assert(kSmemBytes <= 227 * 1024, "smem");
+};
+
+__device__ __forceinline__ void tmem_wait_ld_33(uint32_t (&a)[16], uint32_t (&b)[16], uint32_t& c) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]),
+                   "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]),
+                   "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]), "+r"(b[0]), "+r"(b[1]),
+                   "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]),
+                   "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]),
+                   "+r"(b[14]), "+r"(b[15]), "+r"(c)
+                 :
+                 : "memory");
+}
+
+// Table cell of z in the saturating form: u = sat(fma(z, alpha, beta)) (NaN -> 0),
+// idx = rint(u * nm1) read from the bits of fma(u, nm1, 1.5 * 2^23).
+__device__ __forceinline__ int2 lut_cell_sat(float z, const int2* lut, float alpha, float beta,
+                                             float nm1) {
+    const float u = __saturatef(__fmaf_rn(z, alpha, beta));
+    const float x = __fmaf_rn(u, nm1, kMagic);
+    return lut[__float_as_int(x) - 0x4B400000];
+}
+
+template <int C, int MH, int MW, bool TWO>
+__global__ void __launch_bounds__(TCfg<C, MH, MW>::kThreads, 1)
+layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmOut,
+                const LayerArgs p, const __grid_constant__ LayerCols cols) {
+    using L = TCfg<C, MH, MW>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* sW = smem + L::kOffW;
+    uint8_t* sOnes = smem + L::kOffOnes;
+    uint8_t* sA = smem + L::kOffA;
+    uint8_t* sStage = smem + L::kOffStage;
+    float2* sY = reinterpret_cast<float2*>(smem + L::kOffY);
+    uint8_t* sBinv = smem + L::kOffBinv;
+    uint8_t* sTop = smem + L::kOffTop;
+    int2* sLut = reinterpret_cast<int2*>(smem + L::kOffLut);
+    float4* sCol = reinterpret_cast<float4*>(smem + L::kOffCol);  // {a, zp, nk, b} per column
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBars);
+    uint64_t* empty = full + L::kStages;
+    uint64_t* accFull = empty + L::kStages;
+    uint64_t* accEmpty = accFull + L::kAccStages;
+    uint64_t* tReady = accEmpty + L::kAccStages;
+    uint64_t* tFree = tReady + 2;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(tFree + 2);
+    volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int num_tiles = static_cast<int>((p.M + 127) / 128);
+    const int t_begin = static_cast<int>(static_cast<int64_t>(num_tiles) * blockIdx.x / gridDim.x);
+    const int t_end = static_cast<int>(static_cast<int64_t>(num_tiles) * (blockIdx.x + 1) / gridDim.x);
+    const int P = p.H * p.W;
+
+    // ---- set-up
+    {
+        constexpr int kChunks = C / 16;
+        for (int idx = threadIdx.x; idx < C * kChunks; idx += L::kThreads) {
+            const int o = idx / kChunks, c = idx % kChunks;
+            const uint4 v = *reinterpret_cast<const uint4*>(p.Wq + o * C + c * 16);
+            *reinterpret_cast<uint4*>(sW + swz_offset(o * C + c * 16, C)) = v;
+        }
+        for (int idx = threadIdx.x; idx < 1024 / 16; idx += L::kThreads) {
+            const uint32_t one = (idx * 16 < C) ? 0x01010101u : 0u;  // row 0 = ones
+            *reinterpret_cast<uint4*>(sOnes + idx * 16) = make_uint4(one, one, one, one);
+        }
+        for (int i = threadIdx.x; i < p.lut_cells; i += L::kThreads) sLut[i] = p.code_lut[i];
+        for (int o = threadIdx.x; o < C; o += L::kThreads)
+            sCol[o] = make_float4(cols.a[o], __int_as_float(cols.zp[o]), __int_as_float(cols.nk[o]),
+                                  cols.b[o]);
+        // Binv (A operand of the x1 MMA, 128 points x kKx, SW128 K-major), hi and lo
+        for (int idx = threadIdx.x; idx < 128 * L::kKx; idx += L::kThreads) {
+            const int w = idx / L::kKx, j = idx % L::kKx;
+            float v = 0.0f;
+            if (j < 2 * MW) {
+                const float2 t = p.twi_w[(j >> 1) * p.W + w];
+                v = (j & 1) ? -t.y : t.x;
+            }
+            float hi, lo;
+            split_tf32(v, hi, lo);
+            const uint32_t off = swz_offset(w * 128 + j * 4, 128);
+            *reinterpret_cast<float*>(sBinv + off) = hi;
+            *reinterpret_cast<float*>(sBinv + 128 * 128 + off) = lo;
+        }
+        // T operand buffers: zero (the K padding columns stay zero)
+        for (int idx = threadIdx.x; idx < L::kTopBytes / 16; idx += L::kThreads)
+            reinterpret_cast<uint4*>(sTop)[idx] = make_uint4(0, 0, 0, 0);
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < L::kStages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            for (int s = 0; s < L::kAccStages; ++s) {
+                mbar_init(&accFull[s], 1);
+                mbar_init(&accEmpty[s], L::kEpiWarps);
+            }
+            for (int b = 0; b < 2; ++b) {
+                mbar_init(&tReady[b], L::kTBuildWarps * 32);
+                mbar_init(&tFree[b], 1);
+            }
+            *sAbort = 0;
+            fence_mbar_init();
+        }
+        if (warp == 1) tmem_alloc(sTmem, L::kTmemCols);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    const uint32_t tmem_base = *sTmem;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            prefetch_tmap(&tmIn);
+            int it = 0;
+            for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+                const int s = it % L::kStages;
+                const uint32_t ph = (it / L::kStages) & 1;
+                if (!mbar_wait_backoff(&empty[s], ph ^ 1, sAbort, 1024)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitSlotFree);
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], L::kABytes);
+                tma_load_2d(sA + s * L::kABytes, &tmIn, &full[s], 0, tile * 128);
+            }
+            for (int j = (it > L::kStages ? it - L::kStages : 0); j < it; ++j)
+                if (!mbar_wait_backoff(&full[j % L::kStages], (j / L::kStages) & 1, sAbort, 1024)) break;
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (elect_one()) {
+            int it = 0;
+            for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+                const int s = it % L::kStages;
+                const uint32_t ph = (it / L::kStages) & 1;
+                const int a = it % L::kAccStages;
+                const uint32_t aph = (it / L::kAccStages) & 1;
+                const int b = it & 1;
+                if (!mbar_wait_backoff(&accEmpty[a], aph ^ 1, sAbort, 128)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitAccFree);
+                    break;
+                }
+                if (!mbar_wait_backoff(&full[s], ph, sAbort, 128)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitTmaFull);
+                    break;
+                }
+                if (!mbar_wait_backoff(&tReady[b], (it >> 1) & 1, sAbort, 128)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitDrain);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + a * L::kAccCols;
+                const uint32_t aBase = smem_u32(sA + s * L::kABytes);
+#pragma unroll
+                for (int kk = 0; kk < C / 32; ++kk) {
+                    const uint64_t ad = umma_desc(aBase + kk * 32, C);
+                    const uint64_t wd = umma_desc(smem_u32(sW) + kk * 32, C);
+                    const uint64_t od = umma_desc(smem_u32(sOnes) + kk * 32, C);
+                    mma_i8(d, ad, wd, idesc_i8(C), kk > 0 ? 1u : 0u);
+                    mma_i8(d + L::kOnesCol, ad, od, idesc_i8(16), kk > 0 ? 1u : 0u);
+                }
+                {
+                    const uint32_t dx = d + L::kX1Col;
+                    const uint32_t bhi = smem_u32(sBinv), blo = bhi + 128 * 128;
+                    const uint32_t thi = smem_u32(sTop) + b * (2 * C * 128);
+                    const uint32_t tlo = thi + C * 128;
+                    constexpr uint32_t idx1 = idesc_tf32(C);
+#pragma unroll
+                    for (int kk = 0; kk < L::kKx / 8; ++kk)
+                        mma_tf32(dx, umma_desc(bhi + kk * 32, 128), umma_desc(thi + kk * 32, 128),
+                                 idx1, kk > 0 ? 1u : 0u);
+#pragma unroll
+                    for (int kk = 0; kk < L::kKx / 8; ++kk)
+                        mma_tf32(dx, umma_desc(blo + kk * 32, 128), umma_desc(thi + kk * 32, 128),
+                                 idx1, 1u);
+#pragma unroll
+                    for (int kk = 0; kk < L::kKx / 8; ++kk)
+                        mma_tf32(dx, umma_desc(bhi + kk * 32, 128), umma_desc(tlo + kk * 32, 128),
+                                 idx1, 1u);
+                }
+                mma_commit(&empty[s]);
+                mma_commit(&accFull[a]);
+                mma_commit(&tFree[b]);
+            }
+            if (it > 0) {
+                const int j = it - 1;
+                mbar_wait_backoff(&accFull[j % L::kAccStages], (j / L::kAccStages) & 1, sAbort, 1024);
+            }
+        }
+        __syncwarp();
+    } else if (warp >= L::kTBuild0 && warp < L::kEpi0) {
+        // ---------------- T builders
+        const int ctid = (warp - L::kTBuild0) * 32 + lane;  // 0..127
+        constexpr int kBT = L::kTBuildWarps * 32;
+        constexpr int kPer = MW * C / kBT;                   // (kw, o) pairs per thread
+        static_assert(MW * C % kBT == 0, "T builder layout");
+        const int o = ctid % C;
+        int cached_b = -1;
+        int it = 0;
+        for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+            const int b = it & 1;
+            if (!mbar_wait_backoff(&tFree[b], ((it >> 1) & 1) ^ 1, sAbort, 256)) {
+                *sAbort = 1;
+                atomicOr(p.err, kErrWaitDrain);
+                break;
+            }
+            const int64_t g0 = static_cast<int64_t>(tile) * 128;
+            const int smp = static_cast<int>(g0 / P);
+            const int h = static_cast<int>((g0 % P) / p.W);
+            if (smp != cached_b) {
+                // each builder caches exactly the spectrum entries it reads below, so the
+                // reload needs no barrier among the builders
+                const float2* src = p.Y + static_cast<int64_t>(smp) * MH * MW * C;
+#pragma unroll 1
+                for (int r = 0; r < kPer; ++r) {
+                    const int kw = (ctid + kBT * r) / C;
+#pragma unroll
+                    for (int kh = 0; kh < MH; ++kh)
+                        sY[(kh * MW + kw) * C + o] = __ldg(src + (kh * MW + kw) * C + o);
+                }
+                cached_b = smp;
+            }
+            float2 eh[MH];
+#pragma unroll
+            for (int kh = 0; kh < MH; ++kh) eh[kh] = __ldg(p.twi_h + h * MH + kh);
+            uint8_t* thi = sTop + b * (2 * C * 128);
+            uint8_t* tlo = thi + C * 128;
+#pragma unroll
+            for (int r = 0; r < kPer; ++r) {
+                const int kw = (ctid + kBT * r) / C;
+                float tr = 0.f, ti = 0.f;
+#pragma unroll
+                for (int kh = 0; kh < MH; ++kh) {
+                    const float2 y = sY[(kh * MW + kw) * C + o];
+                    tr = fmaf(y.x, eh[kh].x, fmaf(-y.y, eh[kh].y, tr));
+                    ti = fmaf(y.x, eh[kh].y, fmaf(y.y, eh[kh].x, ti));
+                }
+                float h0, l0, h1, l1;
+                split_tf32(tr, h0, l0);
+                split_tf32(ti, h1, l1);
+                const uint32_t off = swz_offset(o * 128 + (2 * kw) * 4, 128);
+                *reinterpret_cast<float2*>(thi + off) = make_float2(h0, h1);
+                *reinterpret_cast<float2*>(tlo + off) = make_float2(l0, l1);
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&tReady[b]);
+        }
+    } else if (warp >= L::kEpi0 && warp < L::kEpi0 + L::kEpiWarps) {
+        // ---------------- epilogue
+        const int ew = warp - L::kEpi0;
+        const int quad = warp & 3;
+        const int c0 = (ew >> 2) * 16;      // this warp's columns c0 .. c0 + 15
+        const int kzp = C * p.zp_in;
+        const float s_out = p.fq_out.scale, inv_out = p.fq_out.inv_scale;
+        const float zpo = static_cast<float>(p.fq_out.zp);
+        const float klo = -128.0f - zpo, khi = 127.0f - zpo;
+        int it = 0, nstore = 0;
+        for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+            const int a = it % L::kAccStages;
+            const uint32_t aph = (it / L::kAccStages) & 1;
+            if (!mbar_wait(&accFull[a], aph, sAbort)) {
+                *sAbort = 1;
+                atomicOr(p.err, kErrWaitAccFull);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * L::kAccCols;
+            uint32_t raw[16], x1r[16], sum_u;
+            tmem_ld16_async(tbase + c0, raw);
+            tmem_ld16_async(tbase + L::kX1Col + c0, x1r);
+            tmem_ld1(tbase + L::kOnesCol, sum_u);
+            tmem_wait_ld_33(raw, x1r, sum_u);
+            const int m2s = kzp - 2 * static_cast<int>(sum_u);
+            // Per element: dequantise + bias, the fast fake-quant offset k (x2 = k s), z =
+            // x1 + x2 and the next code from the table cell (breakpoint t, codes below /
+            // from t), inserted into the packed word with one byte permute.
+            uint32_t packed[4];
+            uint32_t bad = 0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const float4 cp = sCol[c0 + j];
+                const int vint = static_cast<int>(raw[j]) + __float_as_int(cp.y) * m2s + __float_as_int(cp.z);
+                const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
+                const float r = __fmul_rn(v, inv_out);
+                const float k = rintf(r);
+                bad |= static_cast<uint32_t>(!(fabsf(__fsub_rn(r, k)) < 0.4998779296875f)) << j;
+                const float kq = fminf(fmaxf(k, klo), khi);
+                const float z = __fadd_rn(__uint_as_float(x1r[j]), __fmul_rn(kq, s_out));
+                int2 cell;
+                if constexpr (TWO) {
+                    const bool s0 = z < p.lut_split;
+                    cell = lut_cell_sat(z, sLut, s0 ? p.lut_alpha0 : p.lut_alpha1,
+                                        s0 ? p.lut_beta0 : p.lut_beta1, p.lut_nm1);
+                } else {
+                    cell = lut_cell_sat(z, sLut, p.lut_alpha1, p.lut_beta1, p.lut_nm1);
+                }
+                const uint32_t sel_lo = (0x3210u & ~(0xFu << (4 * (j & 3)))) | (4u << (4 * (j & 3)));
+                const uint32_t sel = z >= __int_as_float(cell.x) ? sel_lo + (1u << (4 * (j & 3))) : sel_lo;
+                const uint32_t prev = (j & 3) == 0 ? 0u : packed[j >> 2];
+                packed[j >> 2] = __byte_perm(prev, static_cast<uint32_t>(cell.y), sel);
+            }
+            // rare: elements whose quotient lies next to a half-integer (or is NaN) take
+            // the exact division; their accumulators are read again from TMEM
+            uint32_t any = __reduce_or_sync(0xffffffffu, bad);
+            while (any) {
+                const int j = __ffs(any) - 1;
+                any &= any - 1;
+                uint32_t rj, xj;
+                tmem_ld1(tbase + c0 + j, rj);
+                tmem_ld1(tbase + L::kX1Col + c0 + j, xj);
+                tmem_wait_ld();
+                if (bad & (1u << j)) {
+                    const float4 cp = sCol[c0 + j];
+                    const int vint = static_cast<int>(rj) + __float_as_int(cp.y) * m2s + __float_as_int(cp.z);
+                    const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
+                    const float x2 = __fmul_rn(__fsub_rn(fq_code(v, s_out, zpo), zpo), s_out);
+                    const float z = __fadd_rn(__uint_as_float(xj), x2);
+                    const bool s0 = TWO && z < p.lut_split;
+                    const int2 cell = lut_cell_sat(z, sLut, s0 ? p.lut_alpha0 : p.lut_alpha1,
+                                                   s0 ? p.lut_beta0 : p.lut_beta1, p.lut_nm1);
+                    const uint32_t code = (z >= __int_as_float(cell.x) ? (cell.y >> 8) : cell.y) & 0xFFu;
+                    const int sh = 8 * (j & 3);
+                    uint32_t w = j < 4 ? packed[0] : (j < 8 ? packed[1] : (j < 12 ? packed[2] : packed[3]));
+                    w = (w & ~(0xFFu << sh)) | (code << sh);
+                    if (j < 4) packed[0] = w;
+                    else if (j < 8) packed[1] = w;
+                    else if (j < 12) packed[2] = w;
+                    else packed[3] = w;
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&accEmpty[a]);
+            uint8_t* buf = sStage + (ew * 2 + (nstore & 1)) * 512;
+            if (nstore >= 2) {
+                if (lane == 0) tma_store_wait_read<1>();
+                __syncwarp();
+            }
+            *reinterpret_cast<uint4*>(buf + lane * 16) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&tmOut, buf, c0, tile * 128 + quad * 32);
+                tma_store_commit();
+            }
+            ++nstore;
+        }
+        if (lane == 0) tma_store_wait_all<0>();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, L::kTmemCols);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // proj: the projection (fno.cpp:972-993) over 128-point tiles.
 //   q = LinearForwardBatched(codes, proj_q) + bias   (tcgen05 kind::i8, as the layers)
@@ -917,26 +1351,6 @@ struct PCfg {
     static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
     static_assert(kSmemBytes <= 227 * 1024, "smem");
 };
-
-// Wait for this thread's outstanding tcgen05.ld; naming the destination registers
-// keeps their uses after the wait.
-__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
-                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
-                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
-                 :
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-}
 
 template <int C>
 __global__ void __launch_bounds__(PCfg<C>::kThreads, 1)
@@ -1010,7 +1424,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p) {
             for (int tile = t_begin; tile < t_end; ++tile, ++it) {
                 const int s = it % L::kStages;
                 const uint32_t ph = (it / L::kStages) & 1;
-                if (!mbar_wait(&empty[s], ph ^ 1, sAbort)) {
+                if (!mbar_wait_backoff(&empty[s], ph ^ 1, sAbort, 1024)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitSlotFree);
                     break;
@@ -1019,7 +1433,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p) {
                 tma_load_2d(sA + s * L::kABytes, &tmIn, &full[s], 0, tile * 128);
             }
             for (int j = (it > L::kStages ? it - L::kStages : 0); j < it; ++j)
-                if (!mbar_wait(&full[j % L::kStages], (j / L::kStages) & 1, sAbort)) break;
+                if (!mbar_wait_backoff(&full[j % L::kStages], (j / L::kStages) & 1, sAbort, 1024)) break;
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -1030,12 +1444,12 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p) {
                 const uint32_t ph = (it / L::kStages) & 1;
                 const int a = it % L::kAccStages;
                 const uint32_t aph = (it / L::kAccStages) & 1;
-                if (!mbar_wait(&accEmpty[a], aph ^ 1, sAbort)) {
+                if (!mbar_wait_backoff(&accEmpty[a], aph ^ 1, sAbort, 128)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitAccFree);
                     break;
                 }
-                if (!mbar_wait(&full[s], ph, sAbort)) {
+                if (!mbar_wait_backoff(&full[s], ph, sAbort, 128)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitTmaFull);
                     break;
@@ -1056,7 +1470,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p) {
             }
             if (it > 0) {
                 const int j = it - 1;
-                mbar_wait(&accFull[j % L::kAccStages], (j / L::kAccStages) & 1, sAbort);
+                mbar_wait_backoff(&accFull[j % L::kAccStages], (j / L::kAccStages) & 1, sAbort, 1024);
             }
         }
         __syncwarp();
@@ -1276,7 +1690,7 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
                 for (int k = 0; k < pairs_per_unit; ++k, ++it) {
                     const int s = it % F::kStages;
                     const uint32_t ph = (it / F::kStages) & 1;
-                    if (!mbar_wait(&empty[s], ph ^ 1, sAbort)) {
+                    if (!mbar_wait_backoff(&empty[s], ph ^ 1, sAbort, 1024)) {
                         *sAbort = 1;
                         atomicOr(p.err, kErrWaitSlotFree);
                         goto producer_done;
@@ -1289,7 +1703,7 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
             }
         producer_done:
             for (int j = (it > F::kStages ? it - F::kStages : 0); j < it; ++j)
-                if (!mbar_wait(&full[j % F::kStages], (j / F::kStages) & 1, sAbort)) break;
+                if (!mbar_wait_backoff(&full[j % F::kStages], (j / F::kStages) & 1, sAbort, 1024)) break;
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -1304,12 +1718,12 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
                 const uint32_t ph = (it / F::kStages) & 1;
                 const int a = it & 1;
                 const uint32_t aph = (it >> 1) & 1;
-                if (!mbar_wait(&accEmpty[a], aph ^ 1, sAbort)) {
+                if (!mbar_wait_backoff(&accEmpty[a], aph ^ 1, sAbort, 128)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitAccFree);
                     break;
                 }
-                if (!mbar_wait(&full[s], ph, sAbort)) {
+                if (!mbar_wait_backoff(&full[s], ph, sAbort, 128)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitTmaFull);
                     break;
@@ -1328,7 +1742,7 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
                 mma_commit(&empty[s]);
                 mma_commit(&accFull[a]);
             }
-            if (it > 0) mbar_wait(&accFull[(it - 1) & 1], ((it - 1) >> 1) & 1, sAbort);
+            if (it > 0) mbar_wait_backoff(&accFull[(it - 1) & 1], ((it - 1) >> 1) & 1, sAbort, 1024);
         }
         __syncwarp();
     } else if (warp >= 4) {
@@ -1524,7 +1938,12 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
                            32, 0))
                 return cudaErrorInvalidValue;
             if (pl.timer) pl.timer->begin("fno2d_layer", st);
-            if (pl.W == 128) {
+            if (pl.W == 128 && a.lut_cells > 0 && a.lut_cells <= kLutMaxCells) {
+                using TC = TCfg<C, MH, MW>;
+                auto k = a.lut_two ? layer_tc_kernel<C, MH, MW, true> : layer_tc_kernel<C, MH, MW, false>;
+                if ((e = set_smem(k, TC::kSmemBytes)) != cudaSuccess) return e;
+                k<<<grid_l, TC::kThreads, TC::kSmemBytes, st>>>(tin, tout, a, pl.layer[i].cols);
+            } else if (pl.W == 128) {
                 using LC = LCfg<C, MH, MW, false, true>;
                 auto k = layer_kernel<C, MH, MW, false, true>;
                 if ((e = set_smem(k, LC::kSmemBytes)) != cudaSuccess) return e;

@@ -34,6 +34,8 @@ struct LayerArgs {
     // : fma(z, inv1, c1) (CodeLut in nfx_lut.h)
     int lut_two;
     float lut_split, lut_inv0, lut_c0, lut_inv1, lut_c1;
+    // the same index in saturating form (CodeLut::alpha0 .. nm1 in nfx_lut.h)
+    float lut_alpha0, lut_beta0, lut_alpha1, lut_beta1, lut_nm1;
     // activation of the 256 fake-quantised proj_q values (projection; nullptr: direct)
     const float* act_table;
     // projection only
@@ -59,11 +61,24 @@ struct SpecFwdArgs {
     unsigned* err;
 };
 
+// Per-output-channel constants of a local layer's epilogue, passed by value so that
+// the kernel reads them as constant-bank operands:
+//   v = a[o] * float(raw + zp[o] * (K zp_in - 2 sum_a) + nk[o]) + b[o]
+// with a = scale_w * s_in, nk = -zp_in * sum_w (int8_gemm.cpp:574-577, fno.cpp:541-548).
+constexpr int kFno2dColMax = 64;
+struct LayerCols {
+    float a[kFno2dColMax];
+    int zp[kFno2dColMax];
+    int nk[kFno2dColMax];
+    float b[kFno2dColMax];
+};
+
 struct Fno2dLayerPlan {
     float s_in;
     int zp_in;
     const float2* wspec;  // (MH*MW, C, C) complex, [mode][in][out]
     LayerArgs args;
+    LayerCols cols;
 };
 
 constexpr int kFno2dMaxLayers = 8;

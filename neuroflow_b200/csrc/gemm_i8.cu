@@ -165,7 +165,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
                 const int s = it % C::kStages;
                 const uint32_t ph = (it / C::kStages) & 1;
-                if (!mbar_wait(&empty[s], ph ^ 1, sAbort)) {
+                if (!mbar_wait_backoff(&empty[s], ph ^ 1, sAbort, 1024)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitSlotFree);
                     break;
@@ -178,7 +178,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // Drain: every load this thread issued must land before the CTA exits.
             const int issued = it;
             for (int j = (issued > C::kStages ? issued - C::kStages : 0); j < issued; ++j) {
-                if (!mbar_wait(&full[j % C::kStages], (j / C::kStages) & 1, sAbort) && *sAbort) {
+                if (!mbar_wait_backoff(&full[j % C::kStages], (j / C::kStages) & 1, sAbort, 1024) && *sAbort) {
                     // a load that never completes leaves nothing else to wait for
                     break;
                 }
@@ -194,12 +194,12 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const uint32_t ph = (it / C::kStages) & 1;
                 const int a = it % C::kAccStages;
                 const uint32_t aph = (it / C::kAccStages) & 1;
-                if (!mbar_wait(&accEmpty[a], aph ^ 1, sAbort)) {
+                if (!mbar_wait_backoff(&accEmpty[a], aph ^ 1, sAbort, 128)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitAccFree);
                     break;
                 }
-                if (!mbar_wait(&full[s], ph, sAbort)) {
+                if (!mbar_wait_backoff(&full[s], ph, sAbort, 128)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitTmaFull);
                     break;
@@ -224,7 +224,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // Drain: the last commit must complete before TMEM is released.
             if (it > 0) {
                 const int j = it - 1;
-                mbar_wait(&accFull[j % C::kAccStages], (j / C::kAccStages) & 1, sAbort);
+                mbar_wait_backoff(&accFull[j % C::kAccStages], (j / C::kAccStages) & 1, sAbort, 1024);
             }
         }
         __syncwarp();

@@ -34,7 +34,34 @@ struct Transition {
     int before, after;
 };
 
+// Saturating index form: cell j of a segment covers [zlo + j delta, zlo + (j + 1) delta)
+// (plus margins), i.e. idx = round((z - zlo) / delta - 0.5) + offset, evaluated as
+// u = sat((z * inv + c) / (n - 1)) and idx = rint(u * (n - 1)) via the 1.5 * 2^23
+// addend; the extra roundings move the index by far less than the cell margin.
+void set_sat_params(CodeLut& L, double zlo0, double d0, double zlo1, double d1, int off1) {
+    const double nm1 = static_cast<double>(L.cells.size()) - 1.0;
+    L.nm1 = static_cast<float>(nm1);
+    if (nm1 <= 0.0) {
+        L.alpha0 = L.alpha1 = L.beta0 = L.beta1 = 0.0f;
+        return;
+    }
+    L.alpha0 = static_cast<float>(1.0 / d0 / nm1);
+    L.beta0 = static_cast<float>((-zlo0 / d0 - 0.5) / nm1);
+    L.alpha1 = static_cast<float>(1.0 / d1 / nm1);
+    L.beta1 = static_cast<float>((off1 - zlo1 / d1 - 0.5) / nm1);
+}
+
 }  // namespace
+
+int lut_index_sat(float z, const CodeLut& L) {
+    const bool s0 = z < L.zsplit;
+    float u = std::fma(z, s0 ? L.alpha0 : L.alpha1, s0 ? L.beta0 : L.beta1);
+    u = (u > 0.0f) ? (u < 1.0f ? u : 1.0f) : 0.0f;  // saturate; NaN -> 0
+    const float x = std::fma(u, L.nm1, 12582912.0f);
+    int32_t b;
+    std::memcpy(&b, &x, 4);
+    return b - 0x4B400000;
+}
 
 float act_ref(float z, int act) {
     if (act == 1) return z < 0.0f ? 0.0f : z;
@@ -114,6 +141,8 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
         out.zsplit = -std::numeric_limits<float>::infinity();
         out.inv0 = out.inv1 = 1.0f;
         out.c0 = out.c1 = 0.0f;
+        out.alpha0 = out.alpha1 = out.beta0 = out.beta1 = 0.0f;
+        out.nm1 = 0.0f;
         out.cells.assign(1, CodeCell{std::numeric_limits<float>::infinity(),
                                      (code(0.0f) & 0xFF) | ((code(0.0f) & 0xFF) << 8)});
         return true;
@@ -166,10 +195,13 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
             int idx = static_cast<int>(fi);
             if (fi < 0.0f) idx = 0;
             if (idx > n - 1) idx = n - 1;
+            const int idx_sat = lut_index_sat(z, L);
             const CodeCell& cc = L.cells[idx];
+            const CodeCell& cs = L.cells[idx_sat];
             const int got = static_cast<int8_t>(((z >= cc.t) ? (cc.packed >> 8) : cc.packed) & 0xFF);
+            const int got_sat = static_cast<int8_t>(((z >= cs.t) ? (cs.packed >> 8) : cs.packed) & 0xFF);
             const int want = code(z);
-            if (got != want) {
+            if (got != want || got_sat != want) {
                 // accept only the flip windows of a few ulps around a breakpoint
                 bool near = false;
                 for (const auto& t : tr)
@@ -214,6 +246,7 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
         L.inv0 = L.inv1 = L.inv_delta;
         L.c0 = L.c1 = -L.zlo * L.inv_delta;
         L.cells = std::move(cells);
+        set_sat_params(L, zlo, delta, zlo, delta, 0);
         if (!self_check(L)) {
             why = "code table self-check failed";
             return false;
@@ -268,6 +301,7 @@ bool build_code_lut(float s, int zp, int act, int max_cells, CodeLut& out, std::
         L.inv1 = static_cast<float>(1.0 / best_d1);
         L.c1 = static_cast<float>(n0) - static_cast<float>(zlo1) * L.inv1;
         L.cells = std::move(cells);
+        set_sat_params(L, zlo0, best_d0, zlo1, best_d1, n0);
         if (!self_check(L)) {
             why = "code table self-check failed";
             return false;

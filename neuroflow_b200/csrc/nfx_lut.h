@@ -38,8 +38,14 @@ struct CodeLut {
     // size (the negative branch of GELU needs far coarser cells than the positive one).
     float zsplit = 0.f;
     float inv0 = 0.f, c0 = 0.f, inv1 = 0.f, c1 = 0.f;
+    // Saturating form of the same index (lut_index_sat): u = sat(fma(z, alpha, beta)),
+    // idx = rint(u * nm1), with (alpha, beta) of the segment; nm1 = cells - 1.
+    float alpha0 = 0.f, beta0 = 0.f, alpha1 = 0.f, beta1 = 0.f, nm1 = 0.f;
     std::vector<CodeCell> cells;
 };
+
+// The saturating index of z (the device's lut_index_sat, evaluated on the host).
+int lut_index_sat(float z, const CodeLut& L);
 
 // Reference activation (act 0: GELU tanh form, act 1: ReLU) in float.
 float act_ref(float z, int act);

@@ -335,7 +335,21 @@ void fno2d_enable_int8(nfx_runtime* rt) {
                     a.lut_c0 = lut.c0;
                     a.lut_inv1 = lut.inv1;
                     a.lut_c1 = lut.c1;
+                    a.lut_alpha0 = lut.alpha0;
+                    a.lut_beta0 = lut.beta0;
+                    a.lut_alpha1 = lut.alpha1;
+                    a.lut_beta1 = lut.beta1;
+                    a.lut_nm1 = lut.nm1;
                 }
+            }
+            // epilogue constants (the device's former per-element shared loads)
+            nfx::LayerCols& cols = pl.layer[i].cols;
+            const std::vector<float>& bias = m.weights.at("locs." + std::to_string(i) + ".bias").data;
+            for (int o = 0; o < c.width && o < nfx::kFno2dColMax; ++o) {
+                cols.a[o] = pc->second.scales[o] * in.scale;
+                cols.zp[o] = pc->second.zero_points[o];
+                cols.nk[o] = -(in.zero_point * sum_w[o]);
+                cols.b[o] = bias[o];
             }
         } else {
             a.fq_out = fq_for(m, "proj_q.output");

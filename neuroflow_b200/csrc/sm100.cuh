@@ -78,31 +78,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
     return ok != 0;
 }
 
-// The same test, letting the thread sleep until the phase completes or `hint_ns`
-// nanoseconds pass (the suspend-time hint of mbarrier.try_wait).  A waiting warp then
-// costs no issue slots, instead of re-polling the barrier in a tight loop.
-constexpr uint32_t kSuspendHintNs = 0x989680u;  // 10 ms
-__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t addr, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred P;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, P;\n\t}"
-        : "=r"(ok)
-        : "r"(addr), "r"(parity), "r"(kSuspendHintNs)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait for the phase with the given parity to complete.  Gives up early when
-// another warp of the CTA has raised `abort`.  Each try sleeps for at most the
-// suspend hint, so the abort flag and the 2 s budget are checked at least every 10 ms.
+// Bounded wait for the phase with the given parity to complete, polling.  Gives up
+// early when another warp of the CTA has raised `abort`.  For waits on a kernel's
+// critical path (an epilogue waiting for its accumulator): the warp resumes as soon
+// as the phase completes.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
     const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(addr, parity)) return true;
+        if ((i & 63u) == 0u) {
+            if (*abort) return false;
+            if (global_ns() - t0 > kWaitNs) return false;
+        }
+    }
+}
+
+// The same wait with exponential back-off (__nanosleep from 32 ns up to `max_ns`)
+// between tries: a waiting warp takes almost no issue slots from the warps doing the
+// arithmetic, at the price of resuming up to `max_ns` late.  For producers that run
+// stages ahead and for the single-thread MMA issuer.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                  uint32_t max_ns) {
+    const uint32_t addr = smem_u32(bar);
+    if (mbar_try_wait(addr, parity)) return true;
+    const uint64_t t0 = global_ns();
+    uint32_t ns = 32;
     for (;;) {
-        if (mbar_try_wait_sleep(addr, parity)) return true;
+        __nanosleep(ns);
+        if (mbar_try_wait(addr, parity)) return true;
+        ns = ns * 2 < max_ns ? ns * 2 : max_ns;
         if (*abort) return false;
         if (global_ns() - t0 > kWaitNs) return false;
     }
