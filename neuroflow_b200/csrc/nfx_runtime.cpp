@@ -100,6 +100,10 @@ struct nfx_runtime {
     std::string err;
     bool int8_enabled = false;
     cudaStream_t stream = nullptr;  // used by the synchronous host-buffer Run
+    // host-buffer Run of a large batch: copies on their own streams, overlapped with
+    // the compute of neighbouring batch chunks
+    cudaStream_t s_h2d = nullptr, s_d2h = nullptr;
+    cudaEvent_t ev_in[4] = {}, ev_out[4] = {};
     std::vector<void*> allocs;      // weights and tables (freed at destroy)
     // FNO2d state
     nfx::Fno2dPlan plan{};
@@ -1281,6 +1285,12 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
     if (rt->dx) cudaFree(rt->dx);
     if (rt->dy) cudaFree(rt->dy);
     if (rt->stream) cudaStreamDestroy(rt->stream);
+    if (rt->s_h2d) cudaStreamDestroy(rt->s_h2d);
+    if (rt->s_d2h) cudaStreamDestroy(rt->s_d2h);
+    for (int i = 0; i < 4; ++i) {
+        if (rt->ev_in[i]) cudaEventDestroy(rt->ev_in[i]);
+        if (rt->ev_out[i]) cudaEventDestroy(rt->ev_out[i]);
+    }
     rt->timer.reset();
     delete rt;
 }
@@ -1381,13 +1391,66 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
         if (!cuda_ok(rt, cudaMalloc(&rt->dy, ny * 4), "cudaMalloc output")) return NFX_INTERNAL;
         rt->dy_cap = ny;
     }
-    if (!cuda_ok(rt, cudaMemcpyAsync(rt->dx, x, nx * 4, cudaMemcpyHostToDevice, rt->stream), "H2D"))
-        return NFX_INTERNAL;
-    s = launch(rt, rt->dx, x_shape, rt->dy, rt->stream);
-    if (s != NFX_OK) return s;
-    if (!cuda_ok(rt, cudaMemcpyAsync(y, rt->dy, ny * 4, cudaMemcpyDeviceToHost, rt->stream), "D2H"))
-        return NFX_INTERNAL;
-    if (!cuda_ok(rt, cudaStreamSynchronize(rt->stream), "execution")) return NFX_INTERNAL;
+    // Samples are independent, so a large batch runs as up to four chunks: the input
+    // copy of chunk c+1 and the output copy of chunk c-1 overlap the compute of chunk
+    // c (the copy engines of both directions and the SMs work at once; with pinned
+    // host buffers the copies are truly asynchronous).
+    const int64_t B = x_shape[0];
+    const int nchunk = B >= 128 ? 4 : (B >= 32 ? 2 : 1);
+    if (nchunk > 1 && !rt->s_h2d) {
+        bool ok = cudaStreamCreateWithFlags(&rt->s_h2d, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaStreamCreateWithFlags(&rt->s_d2h, cudaStreamNonBlocking) == cudaSuccess;
+        for (int i = 0; i < 4 && ok; ++i)
+            ok = cudaEventCreateWithFlags(&rt->ev_in[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&rt->ev_out[i], cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) return rt_fail(rt, NFX_INTERNAL, "creating the copy streams failed");
+    }
+    if (nchunk == 1) {
+        if (!cuda_ok(rt, cudaMemcpyAsync(rt->dx, x, nx * 4, cudaMemcpyHostToDevice, rt->stream), "H2D"))
+            return NFX_INTERNAL;
+        s = launch(rt, rt->dx, x_shape, rt->dy, rt->stream);
+        if (s != NFX_OK) return s;
+        if (!cuda_ok(rt, cudaMemcpyAsync(y, rt->dy, ny * 4, cudaMemcpyDeviceToHost, rt->stream), "D2H"))
+            return NFX_INTERNAL;
+        if (!cuda_ok(rt, cudaStreamSynchronize(rt->stream), "execution")) return NFX_INTERNAL;
+        return nfx_runtime_check(rt);
+    }
+    const size_t xs = nx / static_cast<size_t>(B), ys = ny / static_cast<size_t>(B);
+    int64_t b0s[4], nbs[4];
+    for (int c = 0; c < nchunk; ++c) {
+        b0s[c] = B * c / nchunk;
+        nbs[c] = B * (c + 1) / nchunk - b0s[c];
+    }
+    for (int c = 0; c < nchunk; ++c) {
+        const size_t off = static_cast<size_t>(b0s[c]) * xs;
+        if (!cuda_ok(rt, cudaMemcpyAsync(rt->dx + off, x + off, static_cast<size_t>(nbs[c]) * xs * 4,
+                                         cudaMemcpyHostToDevice, rt->s_h2d), "H2D") ||
+            !cuda_ok(rt, cudaEventRecord(rt->ev_in[c], rt->s_h2d), "event"))
+            return NFX_INTERNAL;
+    }
+    int rc = NFX_OK;
+    for (int c = 0; c < nchunk && rc == NFX_OK; ++c) {
+        std::vector<int64_t> shp(x_shape, x_shape + x_rank);
+        shp[0] = nbs[c];
+        const size_t xo = static_cast<size_t>(b0s[c]) * xs, yo = static_cast<size_t>(b0s[c]) * ys;
+        if (!cuda_ok(rt, cudaStreamWaitEvent(rt->stream, rt->ev_in[c], 0), "event wait")) {
+            rc = NFX_INTERNAL;
+            break;
+        }
+        rc = launch(rt, rt->dx + xo, shp.data(), rt->dy + yo, rt->stream);
+        if (rc != NFX_OK) break;
+        if (!cuda_ok(rt, cudaEventRecord(rt->ev_out[c], rt->stream), "event") ||
+            !cuda_ok(rt, cudaStreamWaitEvent(rt->s_d2h, rt->ev_out[c], 0), "event wait") ||
+            !cuda_ok(rt, cudaMemcpyAsync(y + yo, rt->dy + yo, static_cast<size_t>(nbs[c]) * ys * 4,
+                                         cudaMemcpyDeviceToHost, rt->s_d2h), "D2H"))
+            rc = NFX_INTERNAL;
+    }
+    // every queued copy and kernel ends before Run returns, also on the error path
+    const bool synced = cuda_ok(rt, cudaStreamSynchronize(rt->s_h2d), "input copy") &&
+                        cuda_ok(rt, cudaStreamSynchronize(rt->stream), "execution") &&
+                        cuda_ok(rt, cudaStreamSynchronize(rt->s_d2h), "output copy");
+    if (rc != NFX_OK) return rc;
+    if (!synced) return NFX_INTERNAL;
     return nfx_runtime_check(rt);
 }
 

@@ -118,3 +118,23 @@ def test_fno2d_int8_two_segment_code_table(tmp_path, scale, zp):
     st = _stats(got, want, m.qparams["proj_out.output"].scale)
     print(scale, zp, st)
     assert st["rel_l2"] < 2e-2 and st["frac_diff"] < 0.05, st
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B", [40, 130])
+def test_fno2d_host_run_chunked_matches_device_run(tmp_path, B):
+    """The host-buffer Run of a large batch overlaps copies and compute over batch
+    chunks; the result is bit-identical to one device-buffer run of the whole batch."""
+    import torch
+    from neuroflow_b200.runtime import InferenceRuntime
+    m, path = _model(tmp_path, L=2)
+    x = synth.fno2d_inputs(np.random.default_rng(31), B, 32, 32)
+    rt = InferenceRuntime(path)
+    rt.enable_int8_gemm()
+    got = np.zeros((B, 32, 32, 1), np.float32)
+    rt.run(x, got)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty((B, 32, 32, 1), dtype=torch.float32, device="cuda")
+    rt.run_device(dx, dy, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    assert np.array_equal(got, dy.cpu().numpy())
