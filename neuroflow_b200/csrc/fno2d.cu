@@ -206,18 +206,50 @@ __global__ void __launch_bounds__(256) spec_mix_kernel(const float2* __restrict_
         float4* dst = reinterpret_cast<float4*>(sw);
         for (int i = threadIdx.x; i < C * C / 2; i += 256) dst[i] = src[i];
     }
-    for (int idx = threadIdx.x; idx < SB * C; idx += 256) {
-        const int sl = idx / C, i = idx % C;
-        float2 v = make_float2(0.f, 0.f);
-        if (sl < nb) {
-            const float2* p = xpart + (static_cast<int64_t>(b0 + sl) * nHB * M + m) * C + i;
-            for (int hb = 0; hb < nHB; ++hb) {
-                const float2 u = p[static_cast<int64_t>(hb) * M * C];
-                v.x += u.x;
-                v.y += u.y;
+    // all partial loads of a thread are issued before the first sum
+    constexpr int kPerThr = SB * C / 256;
+    float2 v[kPerThr];
+#pragma unroll
+    for (int t = 0; t < kPerThr; ++t) v[t] = make_float2(0.f, 0.f);
+    if (nHB == 4) {
+        float2 u[kPerThr][4];
+#pragma unroll
+        for (int t = 0; t < kPerThr; ++t) {
+            const int idx = threadIdx.x + 256 * t;
+            const int sl = idx / C, i = idx % C;
+            const float2* q = xpart + (static_cast<int64_t>(b0 + (sl < nb ? sl : 0)) * nHB * M + m) * C + i;
+#pragma unroll
+            for (int hb = 0; hb < 4; ++hb) u[t][hb] = __ldg(q + static_cast<int64_t>(hb) * M * C);
+        }
+#pragma unroll
+        for (int t = 0; t < kPerThr; ++t) {
+            const int sl = (threadIdx.x + 256 * t) / C;
+            if (sl < nb) {
+#pragma unroll
+                for (int hb = 0; hb < 4; ++hb) {
+                    v[t].x += u[t][hb].x;
+                    v[t].y += u[t][hb].y;
+                }
             }
         }
-        sx[i * (SB + 1) + sl] = v;
+    } else {
+        for (int t = 0; t < kPerThr; ++t) {
+            const int idx = threadIdx.x + 256 * t;
+            const int sl = idx / C, i = idx % C;
+            if (sl < nb) {
+                const float2* q = xpart + (static_cast<int64_t>(b0 + sl) * nHB * M + m) * C + i;
+                for (int hb = 0; hb < nHB; ++hb) {
+                    const float2 w = q[static_cast<int64_t>(hb) * M * C];
+                    v[t].x += w.x;
+                    v[t].y += w.y;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < kPerThr; ++t) {
+        const int idx = threadIdx.x + 256 * t;
+        sx[(idx % C) * (SB + 1) + idx / C] = v[t];
     }
     __syncthreads();
     const int og = threadIdx.x & 15, sg = threadIdx.x >> 4;  // outputs og + 16k, samples sg + 16j
@@ -1596,6 +1628,9 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p) {
 //   X[kh][kw][c] += F[h][kw][c] * e^{-2 pi i kh h / H}.
 // A work unit is (sample, block of HB rows); CTAs loop over units.
 // ---------------------------------------------------------------------------
+constexpr int kFwdEpiWarps = 12;  // 3 per TMEM lane quadrant
+constexpr int kFwdThreads = 32 * (4 + kFwdEpiWarps);
+
 template <int C, int MH, int MW>
 struct FCfg {
     static constexpr int kTile = 128 * C;                   // one grid row of codes
@@ -1626,7 +1661,7 @@ __device__ __forceinline__ uint64_t umma_desc_mn64(uint32_t smem_addr, uint32_t 
 }
 
 template <int C, int MH, int MW>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
 spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArgs p) {
     using F = FCfg<C, MH, MW>;
     extern __shared__ uint8_t smem_raw[];
@@ -1653,13 +1688,13 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
 
     {
         // digit matrices -> shared memory (K-major, 128-byte swizzle)
-        for (int idx = threadIdx.x; idx < 4 * F::kN * 8; idx += kThreads) {
+        for (int idx = threadIdx.x; idx < 4 * F::kN * 8; idx += kFwdThreads) {
             const int l = idx / (F::kN * 8), rem = idx % (F::kN * 8);
             const int n = rem / 8, ch = rem % 8;
             const uint4 v = *reinterpret_cast<const uint4*>(p.limbs + (l * F::kN + n) * 128 + ch * 16);
             *reinterpret_cast<uint4*>(sB + l * F::kLimbBytes + swz_offset(n * 128 + ch * 16, 128)) = v;
         }
-        for (int i = threadIdx.x; i < p.H * MH; i += kThreads) sE[i] = p.twf_h[i];
+        for (int i = threadIdx.x; i < p.H * MH; i += kFwdThreads) sE[i] = p.twf_h[i];
         if (threadIdx.x == 0) {
             for (int s = 0; s < F::kStages; ++s) {
                 mbar_init(&full[s], 1);
@@ -1667,9 +1702,9 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
             }
             for (int s = 0; s < 2; ++s) {
                 mbar_init(&accFull[s], 1);
-                mbar_init(&accEmpty[s], 8);
+                mbar_init(&accEmpty[s], kFwdEpiWarps);
             }
-            mbar_init(epiBar, 256);
+            mbar_init(epiBar, kFwdEpiWarps * 32);
             *sAbort = 0;
             fence_mbar_init();
         }
@@ -1746,14 +1781,16 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
         }
         __syncwarp();
     } else if (warp >= 4) {
-        const int ew = warp - 4;            // 0..7
-        const int etid = ew * 32 + lane;    // 0..255
+        const int ew = warp - 4;            // 0..11
+        const int etid = ew * 32 + lane;    // 0..383
         const int quad = warp & 3;
-        const int half = ew >> 2;           // basis columns [16 half, 16 half + 12)
+        const int third = ew >> 2;          // basis columns [8 third, 8 third + 8)
         const int m = quad * 32 + lane;     // TMEM lane = (r, c)
         const int r = m / C, c = m % C;
         constexpr int kPairs = C * MW;
-        constexpr int kPer = (kPairs + 255) / 256;
+        constexpr int kEpiThr = kFwdEpiWarps * 32;
+        constexpr int kPer = (kPairs + kEpiThr - 1) / kEpiThr;
+        static_assert(kPairs % kEpiThr == 0, "pairs per thread");
         const double scale = static_cast<double>(p.s) * 7.450580596923828125e-9;  // s / 2^27
         uint32_t nsync = 0;
         bool ok = true;
@@ -1772,17 +1809,15 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
                     break;
                 }
                 tc_fence_after();
-                const uint32_t tb = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * 128 + 16 * half;
-                uint32_t d[4][16];
+                const uint32_t tb = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * 128 + 8 * third;
+                uint32_t d[4][8];
 #pragma unroll
                 for (int l = 0; l < 4; ++l) {
                     asm volatile(
-                        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-                        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                        "tcgen05.ld.sync.aligned.32x32b.x8.b32 "
+                        "{%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                         : "=r"(d[l][0]), "=r"(d[l][1]), "=r"(d[l][2]), "=r"(d[l][3]), "=r"(d[l][4]),
-                          "=r"(d[l][5]), "=r"(d[l][6]), "=r"(d[l][7]), "=r"(d[l][8]), "=r"(d[l][9]),
-                          "=r"(d[l][10]), "=r"(d[l][11]), "=r"(d[l][12]), "=r"(d[l][13]),
-                          "=r"(d[l][14]), "=r"(d[l][15])
+                          "=r"(d[l][5]), "=r"(d[l][6]), "=r"(d[l][7])
                         : "r"(tb + l * 32));
                 }
                 tmem_wait_ld();
@@ -1791,8 +1826,8 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
                 if (lane == 0) mbar_arrive(&accEmpty[a]);
                 float2* f = sF + (it & 1) * (2 * MW * C);
 #pragma unroll
-                for (int t = 0; t < 12; ++t) {
-                    const int j = 12 * half + t;
+                for (int t = 0; t < 8; ++t) {
+                    const int j = 8 * third + t;
                     const long long v = ((static_cast<long long>(static_cast<int>(d[0][t])) * 256 +
                                           static_cast<int>(d[1][t])) * 256 +
                                          static_cast<int>(d[2][t])) * 256 +
@@ -1812,7 +1847,7 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
                 const int h0 = hb * p.HB + 2 * k;
 #pragma unroll
                 for (int i = 0; i < kPer; ++i) {
-                    const int q = etid + 256 * i;
+                    const int q = etid + kEpiThr * i;
                     if (q < kPairs) {
                         const int kw = q / C, cc = q % C;
 #pragma unroll
@@ -1833,7 +1868,7 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
             float2* dst = p.xpart + (static_cast<int64_t>(b) * nHB + hb) * (MH * MW * C);
 #pragma unroll
             for (int i = 0; i < kPer; ++i) {
-                const int q = etid + 256 * i;
+                const int q = etid + kEpiThr * i;
                 if (q < kPairs) {
                     const int kw = q / C, cc = q % C;
 #pragma unroll
@@ -1901,7 +1936,7 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
                            pl.layer[i].zp_in, pl.B, pl.H, pl.HB, pl.err};
             const int units = pl.B * nHB;
             if (pl.timer) pl.timer->begin("fno2d_spec_fwd", st);
-            k<<<units < sms ? units : sms, kThreads, FC::kSmemBytes, st>>>(tc, fa);
+            k<<<units < sms ? units : sms, kFwdThreads, FC::kSmemBytes, st>>>(tc, fa);
             if (pl.timer) pl.timer->end(st);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         } else {
