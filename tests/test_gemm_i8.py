@@ -2,9 +2,10 @@
 
 Bit-exact: the int32 accumulators (checked through unit scales) and the fp32 outputs
 without activation.  With GELU the outputs agree within rtol 1e-5 plus an absolute
-term of 2^-22 * max|y| (the reference's glibc tanhf and CUDA's tanhf differ by a few
-ulps, which the cancellation in 1 + tanh(u) for u << 0 turns into a larger relative
-error on tiny outputs)."""
+term of 2^-22 * max|y|: the kernel evaluates GELU as z * sigmoid(2u) with the hardware
+exp2 approximation (a few ulp from the exact GELU), while the reference's
+0.5 z (1 + tanh u) with glibc tanhf loses relative accuracy to cancellation on tiny
+outputs (u << 0)."""
 import numpy as np
 import pytest
 
@@ -71,9 +72,10 @@ def test_gemm_gelu_tolerance(K, N):
     got = _run_gpu(case, act=1)
     tol = 1e-5 * np.abs(want) + 2.0 ** -22 * np.abs(want).max()
     assert np.all(np.abs(got - want) <= tol)
-    # glibc's tanhf is itself correctly rounded for only ~86% of inputs, so bit
-    # identity is frequent but not universal
-    assert np.mean(got == want) > 0.5
+    # away from the cancellation region the two agree to a few ulp
+    big = np.abs(want) > 1e-3 * np.abs(want).max()
+    ulp = np.abs(got.view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64))
+    assert np.percentile(ulp[big], 99) <= 8 and np.median(ulp[big]) <= 2
 
 
 @pytest.mark.gpu
