@@ -187,6 +187,66 @@ def gemm_sweep(device):
     return out
 
 
+def run_gemm(args):
+    """the standalone INT8 GEMM of the local 1x1 layer over the whole sweep
+    (M in {4096, 65536, 1048576}, K = N in {32, 64, 128, 256}, bias and bias + GELU
+    epilogues).  Each case rotates over enough distinct A / C buffers that every
+    launch reads and writes memory outside L2 (> 256 MB per rotation)."""
+    import torch
+    from neuroflow_b200 import _nfx, quant
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    hbm, src = peaks()
+    rows = []
+    for M in ([args.gemm_m] if args.gemm_m else (4096, 65536, 1 << 20)):
+        for K in ([args.gemm_k] if args.gemm_k else (32, 64, 128, 256)):
+            N = K
+            c = quant.gemm_case(K, 4096, K, N)  # weights + qparams
+            t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(device)
+                 for k, v in c.items() if k in ("Wq", "sW", "zW", "sum_w", "bias")}
+            per_call = M * K + 4 * M * N + 8 * M
+            nbuf = max(1, min(512, -(-(256 << 20) // per_call)))
+            rng = np.random.default_rng(K + M)
+            bufs = []
+            for _ in range(nbuf):
+                A = torch.from_numpy(rng.integers(-128, 128, (M, K), dtype=np.int8)).to(device)
+                sA = torch.from_numpy(rng.uniform(0.005, 0.02, M).astype(np.float32)).to(device)
+                zA = torch.from_numpy(rng.integers(-20, 20, M).astype(np.int32)).to(device)
+                bufs.append((A, sA, zA, torch.empty((M, N), dtype=torch.float32, device=device)))
+            reps = max(20, min(2000, int(2.5e9 // per_call)))
+            for act in (0, 1):
+                def call(i):
+                    A, sA, zA, C_ = bufs[i % nbuf]
+                    _nfx.int8_gemm(A, t["Wq"], t["sW"], t["zW"], t["sum_w"], bias=t["bias"],
+                                   scale_a=sA, zp_a=zA, act=act, out=C_)
+                for i in range(max(3, nbuf)):
+                    call(i)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for i in range(reps):
+                    call(i)
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) / reps * 1e3
+                byts = M * K + N * K + 4 * M * N + 16 * N + 8 * M
+                gbs = byts / (us * 1e-6) / 1e9
+                rows.append({"M": M, "K": K, "N": N, "epilogue": "bias+GELU" if act else "bias",
+                             "us": round(us, 2), "GBps": round(gbs, 1),
+                             "frac": round(gbs / hbm, 3), "buffers": nbuf})
+            del bufs
+            torch.cuda.empty_cache()
+    big = [r for r in rows if r["M"] == max(x["M"] for x in rows) and r["epilogue"] == "bias"]
+    line = {"metric": "INT8 GEMM HBM GB/s (configs[1], largest M, bias epilogue, mean over K = N)",
+            "value": round(float(np.mean([r["GBps"] for r in big])), 1), "unit": "GB/s",
+            "n_gpus": 1, "higher_is_better": True, "dtype": "int8", "data": "synthetic",
+            "peak": hbm, "peak_source": src,
+            "config": {"workload": "configs[1] INT8 GEMM sweep (algorithmic bytes: A + W + "
+                                   "fp32 C + per-channel and per-row qparams)"},
+            "sweep": rows}
+    print(json.dumps(line), flush=True)
+
+
 def run_nfx(args, ws, rank, local):
     import torch
     from neuroflow_b200.runtime import InferenceRuntime
@@ -429,6 +489,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="nfx", choices=["nfx", "reference"])
+    ap.add_argument("--gemm-m", type=int, default=0, help="--workload gemm: one M only")
+    ap.add_argument("--gemm-k", type=int, default=0, help="--workload gemm: one K = N only")
     ap.add_argument("--preheat", type=int, default=40,
                     help="untimed steps run after the clock sampler starts")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -437,10 +499,13 @@ def main():
     ap.add_argument("--batch", type=int, default=0,
                     help="samples per GPU (default: the configuration's batch, 256 for the "
                          "headline; smaller values only for profiling captures)")
-    ap.add_argument("--workload", default="fno2d_int8", choices=["fno2d_int8"] + sorted(AUX),
+    ap.add_argument("--workload", default="fno2d_int8", choices=["fno2d_int8", "gemm"] + sorted(AUX),
                     help="fno2d_int8 (default): the headline configs[2] line; the others time "
                          "the remaining BASELINE configurations on one GPU")
     args = ap.parse_args()
+    if args.workload == "gemm" and args.impl == "nfx":
+        run_gemm(args)
+        return
     if args.workload != "fno2d_int8" and args.impl == "nfx":
         run_aux(args)
         return

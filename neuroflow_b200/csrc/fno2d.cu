@@ -1053,8 +1053,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
         }
         for (int i = threadIdx.x; i < p.lut_cells; i += L::kThreads) sLut[i] = p.code_lut[i];
         for (int o = threadIdx.x; o < C; o += L::kThreads)
-            sCol[o] = make_float4(cols.a[o], __int_as_float(cols.zp[o]), __int_as_float(cols.nk[o]),
-                                  cols.b[o]);
+            sCol[o] = cols.v[o];
         // Binv (A operand of the x1 MMA, 128 points x kKx, SW128 K-major), hi and lo
         for (int idx = threadIdx.x; idx < 128 * L::kKx; idx += L::kThreads) {
             const int w = idx / L::kKx, j = idx % L::kKx;
@@ -1269,7 +1268,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
             uint32_t bad = 0;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-                const float4 cp = sCol[c0 + j];
+                const float4 cp = cols.v[c0 + j];  // constant cache, uniform
                 const int vint = static_cast<int>(raw[j]) + __float_as_int(cp.y) * m2s + __float_as_int(cp.z);
                 const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
                 const float r = __fmul_rn(v, inv_out);

@@ -62,15 +62,14 @@ struct SpecFwdArgs {
 };
 
 // Per-output-channel constants of a local layer's epilogue, passed by value so that
-// the kernel reads them as constant-bank operands:
+// the kernel reads them through the constant cache (one uniform 16-byte load per
+// element, off the shared-memory pipe):
 //   v = a[o] * float(raw + zp[o] * (K zp_in - 2 sum_a) + nk[o]) + b[o]
-// with a = scale_w * s_in, nk = -zp_in * sum_w (int8_gemm.cpp:574-577, fno.cpp:541-548).
+// with a = scale_w * s_in, nk = -zp_in * sum_w (int8_gemm.cpp:574-577, fno.cpp:541-548),
+// stored as float4 {a, bits(zp), bits(nk), b}.
 constexpr int kFno2dColMax = 64;
 struct LayerCols {
-    float a[kFno2dColMax];
-    int zp[kFno2dColMax];
-    int nk[kFno2dColMax];
-    float b[kFno2dColMax];
+    float4 v[kFno2dColMax];
 };
 
 struct Fno2dLayerPlan {

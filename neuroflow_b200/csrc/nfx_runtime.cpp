@@ -350,10 +350,12 @@ void fno2d_enable_int8(nfx_runtime* rt) {
             nfx::LayerCols& cols = pl.layer[i].cols;
             const std::vector<float>& bias = m.weights.at("locs." + std::to_string(i) + ".bias").data;
             for (int o = 0; o < c.width && o < nfx::kFno2dColMax; ++o) {
-                cols.a[o] = pc->second.scales[o] * in.scale;
-                cols.zp[o] = pc->second.zero_points[o];
-                cols.nk[o] = -(in.zero_point * sum_w[o]);
-                cols.b[o] = bias[o];
+                const int32_t zp = pc->second.zero_points[o];
+                const int32_t nk = -(in.zero_point * sum_w[o]);
+                float zpf, nkf;
+                std::memcpy(&zpf, &zp, 4);
+                std::memcpy(&nkf, &nk, 4);
+                cols.v[o] = make_float4(pc->second.scales[o] * in.scale, zpf, nkf, bias[o]);
             }
         } else {
             a.fq_out = fq_for(m, "proj_q.output");
