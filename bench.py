@@ -147,59 +147,17 @@ def cpu_reference(path: str, x: np.ndarray, nthreads: int, target_s: float = 8.0
     return n * reps / wall, n, reps, t1
 
 
-def gemm_sweep(device):
-    """configs[1] GEMM at M = 1,048,576 rows: achieved HBM GB/s of nfx_int8_gemm."""
+def gemm_rows(device, Ms, Ks):
+    """configs[1] GEMM cases: achieved GB/s of nfx_int8_gemm (bias and bias + GELU).
+    Each case rotates over enough distinct A / C buffers that every launch reads and
+    writes memory outside L2 (> 256 MB per rotation), and replays its launches from a
+    CUDA graph (device time per launch, CUDA events)."""
     import torch
     from neuroflow_b200 import _nfx, quant
-    hbm, src = peaks()
-    out = []
-    M = 1 << 20
-    for K in (32, 64, 128, 256):
-        N = K
-        c = quant.gemm_case(K, 4096, K, N)     # weights + qparams; rows tiled below
-        rng = np.random.default_rng(K)
-        A = torch.from_numpy(rng.integers(-128, 128, (M, K), dtype=np.int8)).to(device)
-        sA = torch.from_numpy(rng.uniform(0.005, 0.02, M).astype(np.float32)).to(device)
-        zA = torch.from_numpy(rng.integers(-20, 20, M).astype(np.int32)).to(device)
-        t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(device)
-             for k, v in c.items() if k in ("Wq", "sW", "zW", "sum_w", "bias")}
-        C_ = torch.empty((M, N), dtype=torch.float32, device=device)
-        for act in (0, 1):
-            for _ in range(3):
-                _nfx.int8_gemm(A, t["Wq"], t["sW"], t["zW"], t["sum_w"], bias=t["bias"],
-                               scale_a=sA, zp_a=zA, act=act, out=C_)
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            reps = 20
-            e0.record()
-            for _ in range(reps):
-                _nfx.int8_gemm(A, t["Wq"], t["sW"], t["zW"], t["sum_w"], bias=t["bias"],
-                               scale_a=sA, zp_a=zA, act=act, out=C_)
-            e1.record()
-            torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / reps
-            byts = M * K + N * K + 4 * M * N + 16 * N + 8 * M
-            gbs = byts / (ms * 1e-3) / 1e9
-            out.append({"M": M, "K": K, "N": N, "epilogue": "bias+GELU" if act else "bias",
-                        "us": round(ms * 1e3, 2), "GBps": round(gbs, 1),
-                        "frac": round(gbs / hbm, 3)})
-        del A, sA, zA, C_
-    return out
-
-
-def run_gemm(args):
-    """configs[1]: the standalone INT8 GEMM of the local 1x1 layer over the whole sweep
-    (M in {4096, 65536, 1048576}, K = N in {32, 64, 128, 256}, bias and bias + GELU
-    epilogues).  Each case rotates over enough distinct A / C buffers that every
-    launch reads and writes memory outside L2 (> 256 MB per rotation)."""
-    import torch
-    from neuroflow_b200 import _nfx, quant
-    device = torch.device("cuda", 0)
-    torch.cuda.set_device(device)
     hbm, src = peaks()
     rows = []
-    for M in ([args.gemm_m] if args.gemm_m else (4096, 65536, 1 << 20)):
-        for K in ([args.gemm_k] if args.gemm_k else (32, 64, 128, 256)):
+    for M in Ms:
+        for K in Ks:
             N = K
             c = quant.gemm_case(K, 4096, K, N)  # weights + qparams
             t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(device)
@@ -222,13 +180,21 @@ def run_gemm(args):
                 for i in range(max(3, nbuf)):
                     call(i)
                 torch.cuda.synchronize()
+                # the launches are replayed from a CUDA graph, so that small M measures
+                # the GPU and not the host's launch rate
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for i in range(reps):
+                        call(i)
+                g.replay()
+                torch.cuda.synchronize()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
-                for i in range(reps):
-                    call(i)
+                g.replay()
                 e1.record()
                 torch.cuda.synchronize()
                 us = e0.elapsed_time(e1) / reps * 1e3
+                del g
                 byts = M * K + N * K + 4 * M * N + 16 * N + 8 * M
                 gbs = byts / (us * 1e-6) / 1e9
                 rows.append({"M": M, "K": K, "N": N, "epilogue": "bias+GELU" if act else "bias",
@@ -236,6 +202,19 @@ def run_gemm(args):
                              "frac": round(gbs / hbm, 3), "buffers": nbuf})
             del bufs
             torch.cuda.empty_cache()
+    return rows
+
+
+def run_gemm(args):
+    """configs[1]: the standalone INT8 GEMM of the local 1x1 layer over the whole sweep
+    (M in {4096, 65536, 1048576}, K = N in {32, 64, 128, 256}, bias and bias + GELU
+    epilogues), one JSON line."""
+    import torch
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    hbm, src = peaks()
+    rows = gemm_rows(device, [args.gemm_m] if args.gemm_m else (4096, 65536, 1 << 20),
+                     [args.gemm_k] if args.gemm_k else (32, 64, 128, 256))
     big = [r for r in rows if r["M"] == max(x["M"] for x in rows) and r["epilogue"] == "bias"]
     line = {"metric": "INT8 GEMM HBM GB/s (configs[1], largest M, bias epilogue, mean over K = N)",
             "value": round(float(np.mean([r["GBps"] for r in big])), 1), "unit": "GB/s",
@@ -352,7 +331,10 @@ def run_nfx(args, ws, rank, local):
         traffic = None
         tp = os.path.join(ROOT, "profiles", "traffic.json")
         if os.path.exists(tp):
-            traffic = json.load(open(tp)).get(name)
+            tj = json.load(open(tp))
+            t = tj.get("bytes_per_launch", {}).get(name)
+            if t is not None:
+                traffic = int(t * B / tj.get("batch", B))
         share = {k: round(v[1] / sum(vv[1] for vv in prof.values()), 3) for k, v in prof.items()}
         total_launches = sum(v[0] for v in prof.values())
         result = {
@@ -548,7 +530,8 @@ def main():
     if rank == 0:
         if ws == 1 and not args.no_gemm:
             import torch
-            result["gemm_sweep"] = gemm_sweep(torch.device("cuda", local))
+            result["gemm_sweep"] = gemm_rows(torch.device("cuda", local), (1 << 20,),
+                                             (32, 64, 128, 256))
         if ws == 1 and not args.no_cpu_baseline:
             n = os.cpu_count() or 1
             v, nthr, reps, t1 = cpu_reference(path, x_host, n)
