@@ -109,7 +109,7 @@ extern "C" int nfx_runtime_run_device_noalloc(nfx_runtime* rt, const float* x,
     if (off > kNoAllocScratchBytes)
         return nfx::runtime_fail(rt, NFX_INVALID_ARG,
                                  "nfx_runtime_run_device_noalloc: this batch needs more than the "
-                                 "32 MiB of fixed scratch (about 2.8 MB per 128x128 sample at "
+                                 "32 MiB of fixed scratch (about 2.5 MB per 128x128 sample at "
                                  "width 64); split the batch");
 
     void* base = nullptr;
