@@ -1620,7 +1620,8 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p) {
 // scaled by 2^27, rounded to an integer and split into four balanced base-256
 // digits Blimb_0..3.  The codes are the MMA's A operand in MN-major layout (two
 // TMA-loaded [w][c] tiles, one per row, as the two 64-wide M atoms); the digit
-// matrices are the K-major B operand.  Recombined exactly in int64,
+// matrices are the K-major B operand.  Recombined in fp32 (exact digit partials and
+// power-of-two weights; four rounded multiply-adds),
 //   F[h][j][c] = s * (sum_l D_l 256^(3-l) - zp * sum_w Bint[j][w]) / 2^27
 // is the row DFT of the snapped activation (code - zp) * s.  The H-axis DFT is then
 // accumulated on CUDA cores over the unit's rows:
@@ -1790,7 +1791,12 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
         constexpr int kEpiThr = kFwdEpiWarps * 32;
         constexpr int kPer = (kPairs + kEpiThr - 1) / kEpiThr;
         static_assert(kPairs % kEpiThr == 0, "pairs per thread");
-        const double scale = static_cast<double>(p.s) * 7.450580596923828125e-9;  // s / 2^27
+        // the zero-point term -zp * sum_w Bint[j][w] / 2^27 of this thread's basis columns
+        float czp[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+            czp[t] = static_cast<float>(-static_cast<double>(static_cast<long long>(p.zp) * p.sum_b[8 * third + t]) *
+                                        7.450580596923828125e-9);
         uint32_t nsync = 0;
         bool ok = true;
         int it = 0;
@@ -1827,14 +1833,15 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
 #pragma unroll
                 for (int t = 0; t < 8; ++t) {
                     const int j = 8 * third + t;
-                    const long long v = ((static_cast<long long>(static_cast<int>(d[0][t])) * 256 +
-                                          static_cast<int>(d[1][t])) * 256 +
-                                         static_cast<int>(d[2][t])) * 256 +
-                                        static_cast<int>(d[3][t]) -
-                                        static_cast<long long>(p.zp) * p.sum_b[j];
-                    const float fv = static_cast<float>(static_cast<double>(v) * scale);
+                    // sum_l D_l 256^(3-l) / 2^27 from the smallest term up: every digit
+                    // partial is an integer below 2^22 (exact in fp32) and the power-of-two
+                    // weights are exact, so only the four multiply-adds round
+                    float u = __fmaf_rn(__int2float_rn(static_cast<int>(d[3][t])), 0x1p-27f, czp[t]);
+                    u = __fmaf_rn(__int2float_rn(static_cast<int>(d[2][t])), 0x1p-19f, u);
+                    u = __fmaf_rn(__int2float_rn(static_cast<int>(d[1][t])), 0x1p-11f, u);
+                    u = __fmaf_rn(__int2float_rn(static_cast<int>(d[0][t])), 0x1p-3f, u);
                     float* dst = reinterpret_cast<float*>(f + (r * MW + (j >> 1)) * C + c);
-                    dst[j & 1] = fv;
+                    dst[j & 1] = __fmul_rn(u, p.s);
                 }
                 // everyone's row DFT of this row pair is in sF before the H accumulation
                 mbar_arrive(epiBar);
