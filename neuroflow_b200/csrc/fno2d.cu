@@ -1612,7 +1612,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p) {
 }
 
 // ---------------------------------------------------------------------------
-// spec_fwd_tc: the forward transform of a layer on tensor cores (W == 128).
+// spec_fwd_tc2: the forward transform of a layer on tensor cores (W == 128).
 //
 // Row DFT (along W) as an exact integer GEMM: for a pair of grid rows,
 //   D_l[(r, c)][n] = sum_w code[h+r][w][c] * Blimb_l[n][w]      (tcgen05 kind::i8)
@@ -1623,33 +1623,13 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p) {
 // matrices are the K-major B operand.  Recombined in fp32 (exact digit partials and
 // power-of-two weights; four rounded multiply-adds),
 //   F[h][j][c] = s * (sum_l D_l 256^(3-l) - zp * sum_w Bint[j][w]) / 2^27
-// is the row DFT of the snapped activation (code - zp) * s.  The H-axis DFT is then
-// accumulated on CUDA cores over the unit's rows:
-//   X[kh][kw][c] += F[h][kw][c] * e^{-2 pi i kh h / H}.
+// is the row DFT of the snapped activation (code - zp) * s.  The H-axis DFT
+//   X[kh][kw][c] += F[h][kw][c] * e^{-2 pi i kh h / H}
+// is a second (3xTF32) MMA over groups of four rows, described below.
 // A work unit is (sample, block of HB rows); CTAs loop over units.
 // ---------------------------------------------------------------------------
 constexpr int kFwdEpiWarps = 12;  // 3 per TMEM lane quadrant
 constexpr int kFwdThreads = 32 * (4 + kFwdEpiWarps);
-
-template <int C, int MH, int MW>
-struct FCfg {
-    static constexpr int kTile = 128 * C;                   // one grid row of codes
-    static constexpr int kStages = 4;                       // row-pair ring
-    static constexpr int kStageBytes = 2 * kTile;
-    static constexpr int kN = 32;                           // basis rows per digit (padded)
-    static constexpr int kLimbBytes = kN * 128;             // [32][128] int8, SW128
-    static constexpr int kOffA = 0;
-    static constexpr int kOffB = kOffA + kStages * kStageBytes;
-    static constexpr int kOffF = kOffB + 4 * kLimbBytes;    // 2 x [2][MW][C] float2
-    static constexpr int kFBytes = 2 * 2 * MW * C * 8;
-    static constexpr int kOffE = kOffF + kFBytes;           // twf_h [H][MH] float2 (H <= 512)
-    static constexpr int kEBytes = 512 * MH * 8;
-    static constexpr int kOffBars = kOffE + kEBytes;
-    static constexpr int kSmemBytes = kOffBars + 8 * (2 * kStages + 4 + 1) + 16 + 1024;
-    static constexpr int kTmemCols = 256;                   // 2 stages x 4 digits x 32
-    static_assert(kSmemBytes <= 227 * 1024, "smem");
-    static_assert(2 * MW <= 24, "basis rows");
-};
 
 // MN-major descriptor: SW64 atoms of 64 bytes along M, `lbo` between M atoms,
 // `sbo` between groups of 8 K rows.
@@ -1660,51 +1640,98 @@ __device__ __forceinline__ uint64_t umma_desc_mn64(uint32_t smem_addr, uint32_t 
            (static_cast<uint64_t>(4u) << 61);
 }
 
+// ---------------------------------------------------------------------------
+// The drain warps recombine each row pair's digit accumulators to fp32 F and write
+// it, split into tf32 hi and lo halves, as the A operand of the H-axis MMA, which
+// accumulates in TMEM:
+//   X[(kw, c)][(kh, ri)] += sum_{(h, f)} F[h][kw][c][f] * E[(kh, ri)][(h, f)]
+// over groups of four rows (K = 4 rows x {re, im} = 8), with E the complex twiddle
+// e^{-2 pi i kh h / H} written as a real 2x2 block per (kh, h) (3xTF32 products).
+// M = (kw, c) is 768 = six 128-lane blocks, N = (kh, ri) = 24 padded to 32.  At the
+// end of a unit the drain warps read X from TMEM and write the unit's partial
+// spectrum.
+// ---------------------------------------------------------------------------
+template <int C, int MH, int MW>
+struct F2Cfg {
+    static constexpr int kTile = 128 * C;                   // one grid row of codes
+    static constexpr int kStages = 4;                       // row-pair ring
+    static constexpr int kStageBytes = 2 * kTile;
+    static constexpr int kN = 32;                           // basis rows per digit (padded)
+    static constexpr int kLimbBytes = kN * 128;             // [32][128] int8, SW128
+    static constexpr int kMBlocks = (MW * C) / 128;         // M blocks of the H-DFT MMA
+    static constexpr int kA2Block = 128 * 32;               // [128 m][8 k] fp32, SW32
+    static constexpr int kA2Bytes = kMBlocks * kA2Block;    // one of hi / lo
+    static constexpr int kB2Bytes = 32 * 32;                // [32 n][8 k] fp32, SW32
+    static constexpr int kOffA = 0;
+    static constexpr int kOffB = kOffA + kStages * kStageBytes;
+    static constexpr int kOffA2 = kOffB + 4 * kLimbBytes;    // 2 buffers x (hi, lo)
+    static constexpr int kOffB2 = kOffA2 + 2 * 2 * kA2Bytes; // 2 buffers x (hi, lo)
+    static constexpr int kOffBars = kOffB2 + 2 * 2 * kB2Bytes;
+    static constexpr int kNumBars = 2 * kStages + 2 + 2 + 2 + 2 + 2;
+    static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
+    static constexpr int kXCol = 256;                       // X accumulator columns
+    static constexpr int kTmemCols = 512;                   // D1: 2 x 128, X: 6 x 32
+    static_assert(kSmemBytes <= 227 * 1024, "smem");
+    static_assert(2 * MW <= 24 && MH * 2 <= 32, "basis rows");
+    static_assert((MW * C) % 128 == 0 && kMBlocks * 32 <= 256, "H-DFT MMA blocks");
+    static_assert(2 * MW == 24, "drain layout: 8 basis columns per warp third");
+};
+
 template <int C, int MH, int MW>
 __global__ void __launch_bounds__(kFwdThreads, 1)
-spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArgs p) {
-    using F = FCfg<C, MH, MW>;
+spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArgs p) {
+    using F = F2Cfg<C, MH, MW>;
     extern __shared__ uint8_t smem_raw[];
-    // 1024-byte aligned base, derived by indexing the shared array so that the
-    // compiler keeps shared-memory (not generic) loads and stores through it
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sA = smem + F::kOffA;
     uint8_t* sB = smem + F::kOffB;
-    float2* sF = reinterpret_cast<float2*>(smem + F::kOffF);
-    float2* sE = reinterpret_cast<float2*>(smem + F::kOffE);
+    uint8_t* sA2 = smem + F::kOffA2;
+    uint8_t* sB2 = smem + F::kOffB2;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + F::kOffBars);
     uint64_t* empty = full + F::kStages;
-    uint64_t* accFull = empty + F::kStages;
-    uint64_t* accEmpty = accFull + 2;
-    uint64_t* epiBar = accEmpty + 2;
-    uint32_t* sTmem = reinterpret_cast<uint32_t*>(epiBar + 1);
+    uint64_t* d1Full = empty + F::kStages;
+    uint64_t* d1Empty = d1Full + 2;
+    uint64_t* a2Ready = d1Empty + 2;
+    uint64_t* a2Free = a2Ready + 2;
+    uint64_t* xFull = a2Free + 2;
+    uint64_t* xEmpty = xFull + 1;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(xFull + 2);
     volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int pairs_per_unit = p.HB / 2;
+    const int pairs_per_unit = p.HB / 2;      // even (HB is a multiple of 4)
+    const int groups_per_unit = pairs_per_unit / 2;
     const int nHB = p.H / p.HB;
     const int num_units = p.B * nHB;
+    const int my_units = (num_units - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                         static_cast<int>(gridDim.x);
+    const int total = my_units * pairs_per_unit;   // row pairs of this CTA
+    constexpr int kDrainThr = kFwdEpiWarps * 32;
 
     {
-        // digit matrices -> shared memory (K-major, 128-byte swizzle)
         for (int idx = threadIdx.x; idx < 4 * F::kN * 8; idx += kFwdThreads) {
             const int l = idx / (F::kN * 8), rem = idx % (F::kN * 8);
             const int n = rem / 8, ch = rem % 8;
             const uint4 v = *reinterpret_cast<const uint4*>(p.limbs + (l * F::kN + n) * 128 + ch * 16);
             *reinterpret_cast<uint4*>(sB + l * F::kLimbBytes + swz_offset(n * 128 + ch * 16, 128)) = v;
         }
-        for (int i = threadIdx.x; i < p.H * MH; i += kFwdThreads) sE[i] = p.twf_h[i];
+        // B2 rows n >= 2*MH stay zero
+        for (int idx = threadIdx.x; idx < 2 * 2 * F::kB2Bytes / 16; idx += kFwdThreads)
+            reinterpret_cast<uint4*>(sB2)[idx] = make_uint4(0, 0, 0, 0);
         if (threadIdx.x == 0) {
             for (int s = 0; s < F::kStages; ++s) {
                 mbar_init(&full[s], 1);
                 mbar_init(&empty[s], 1);
             }
             for (int s = 0; s < 2; ++s) {
-                mbar_init(&accFull[s], 1);
-                mbar_init(&accEmpty[s], kFwdEpiWarps);
+                mbar_init(&d1Full[s], 1);
+                mbar_init(&d1Empty[s], kFwdEpiWarps);
+                mbar_init(&a2Ready[s], 2 * kDrainThr);
+                mbar_init(&a2Free[s], 1);
             }
-            mbar_init(epiBar, kFwdEpiWarps * 32);
+            mbar_init(xFull, 1);
+            mbar_init(xEmpty, kFwdEpiWarps);
             *sAbort = 0;
             fence_mbar_init();
         }
@@ -1728,39 +1755,66 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
                     if (!mbar_wait_backoff(&empty[s], ph ^ 1, sAbort, 1024)) {
                         *sAbort = 1;
                         atomicOr(p.err, kErrWaitSlotFree);
-                        goto producer_done;
+                        goto producer_done2;
                     }
                     mbar_arrive_expect_tx(&full[s], F::kStageBytes);
-                    const int row = b * p.H + hb * p.HB + 2 * k;   // tile index of grid row h
+                    const int row = b * p.H + hb * p.HB + 2 * k;
                     tma_load_2d(sA + s * F::kStageBytes, &tmCodes, &full[s], 0, row * 128);
                     tma_load_2d(sA + s * F::kStageBytes + F::kTile, &tmCodes, &full[s], 0, (row + 1) * 128);
                 }
             }
-        producer_done:
+        producer_done2:
             for (int j = (it > F::kStages ? it - F::kStages : 0); j < it; ++j)
                 if (!mbar_wait_backoff(&full[j % F::kStages], (j / F::kStages) & 1, sAbort, 1024)) break;
         }
         __syncwarp();
     } else if (warp == 1) {
         if (elect_one()) {
-            // kind::i8, signed, int32 D, A MN-major, B K-major, M = 128, N = 32
-            constexpr uint32_t idesc = idesc_i8(F::kN) | (1u << 15);
+            constexpr uint32_t idesc1 = idesc_i8(F::kN) | (1u << 15);  // A MN-major
+            constexpr uint32_t idesc2 = idesc_tf32(32);
+            bool ok = true;
+            // the H-DFT MMA of group g (row pairs 2g, 2g+1)
+            auto mma2 = [&](int g) -> bool {
+                if (!mbar_wait_backoff(&a2Ready[g & 1], (g >> 1) & 1, sAbort, 128)) {
+                    atomicOr(p.err, kErrWaitDrain);
+                    return false;
+                }
+                const bool first = (g % groups_per_unit) == 0;
+                if (first && !mbar_wait_backoff(xEmpty, ((g / groups_per_unit) & 1) ^ 1, sAbort, 128)) {
+                    atomicOr(p.err, kErrWaitAccFree);
+                    return false;
+                }
+                tc_fence_after();
+                const uint32_t ahi = smem_u32(sA2) + (g & 1) * 2 * F::kA2Bytes;
+                const uint32_t alo = ahi + F::kA2Bytes;
+                const uint32_t bhi = smem_u32(sB2) + (g & 1) * 2 * F::kB2Bytes;
+                const uint32_t blo = bhi + F::kB2Bytes;
+#pragma unroll
+                for (int mb = 0; mb < F::kMBlocks; ++mb) {
+                    const uint32_t d = tmem_base + F::kXCol + mb * 32;
+                    const uint32_t ao = mb * F::kA2Block;
+                    mma_tf32(d, umma_desc(ahi + ao, 32), umma_desc(bhi, 32), idesc2, first ? 0u : 1u);
+                    mma_tf32(d, umma_desc(alo + ao, 32), umma_desc(bhi, 32), idesc2, 1u);
+                    mma_tf32(d, umma_desc(ahi + ao, 32), umma_desc(blo, 32), idesc2, 1u);
+                }
+                mma_commit(&a2Free[g & 1]);
+                if ((g % groups_per_unit) == groups_per_unit - 1) mma_commit(xFull);
+                return true;
+            };
             int it = 0;
-            const int total = ((num_units - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                               static_cast<int>(gridDim.x)) * pairs_per_unit;
-            for (; it < total; ++it) {
+            for (; it < total && ok; ++it) {
                 const int s = it % F::kStages;
                 const uint32_t ph = (it / F::kStages) & 1;
                 const int a = it & 1;
                 const uint32_t aph = (it >> 1) & 1;
-                if (!mbar_wait_backoff(&accEmpty[a], aph ^ 1, sAbort, 128)) {
-                    *sAbort = 1;
+                if (!mbar_wait_backoff(&d1Empty[a], aph ^ 1, sAbort, 128)) {
                     atomicOr(p.err, kErrWaitAccFree);
+                    ok = false;
                     break;
                 }
                 if (!mbar_wait_backoff(&full[s], ph, sAbort, 128)) {
-                    *sAbort = 1;
                     atomicOr(p.err, kErrWaitTmaFull);
+                    ok = false;
                     break;
                 }
                 tc_fence_after();
@@ -1772,12 +1826,16 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         mma_i8(d, umma_desc_mn64(aBase + kk * 2048, F::kTile, 512),
-                               umma_desc(bBase + kk * 32, 128), idesc, kk > 0 ? 1u : 0u);
+                               umma_desc(bBase + kk * 32, 128), idesc1, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&empty[s]);
-                mma_commit(&accFull[a]);
+                mma_commit(&d1Full[a]);
+                // the H-DFT of the previous group, after this pair's row DFT is queued
+                if (it >= 2 && (it & 1) == 0) ok = mma2(it / 2 - 1);
             }
-            if (it > 0) mbar_wait_backoff(&accFull[(it - 1) & 1], ((it - 1) >> 1) & 1, sAbort, 1024);
+            if (ok && total > 0) ok = mma2(total / 2 - 1);
+            if (!ok) *sAbort = 1;
+            if (ok && total > 0) mbar_wait_backoff(xFull, (my_units - 1) & 1, sAbort, 1024);
         }
         __syncwarp();
     } else if (warp >= 4) {
@@ -1787,99 +1845,126 @@ spec_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdArg
         const int third = ew >> 2;          // basis columns [8 third, 8 third + 8)
         const int m = quad * 32 + lane;     // TMEM lane = (r, c)
         const int r = m / C, c = m % C;
-        constexpr int kPairs = C * MW;
-        constexpr int kEpiThr = kFwdEpiWarps * 32;
-        constexpr int kPer = (kPairs + kEpiThr - 1) / kEpiThr;
-        static_assert(kPairs % kEpiThr == 0, "pairs per thread");
-        // the zero-point term -zp * sum_w Bint[j][w] / 2^27 of this thread's basis columns
-        float czp[8];
+        float czp[8];                       // -zp * sum_w Bint[j][w] / 2^27
 #pragma unroll
         for (int t = 0; t < 8; ++t)
             czp[t] = static_cast<float>(-static_cast<double>(static_cast<long long>(p.zp) * p.sum_b[8 * third + t]) *
                                         7.450580596923828125e-9);
-        uint32_t nsync = 0;
         bool ok = true;
-        int it = 0;
-        for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-            const int b = u / nHB, hb = u % nHB;
-            float2 acc[kPer][MH];
+        int u_local = 0;
+        for (int it = 0; it < total && ok; ++it) {
+            const int g = it >> 1;
+            const int pig = it & 1;                        // pair in group
+            const int a = it & 1;
+            if (pig == 0 && !mbar_wait(&a2Free[g & 1], ((g >> 1) & 1) ^ 1, sAbort)) {
+                ok = false;
+                break;
+            }
+            if (!mbar_wait(&d1Full[a], (it >> 1) & 1, sAbort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tb = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * 128 + 8 * third;
+            uint32_t d[4][8];
 #pragma unroll
-            for (int i = 0; i < kPer; ++i)
+            for (int l = 0; l < 4; ++l) {
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x8.b32 "
+                    "{%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                    : "=r"(d[l][0]), "=r"(d[l][1]), "=r"(d[l][2]), "=r"(d[l][3]), "=r"(d[l][4]),
+                      "=r"(d[l][5]), "=r"(d[l][6]), "=r"(d[l][7])
+                    : "r"(tb + l * 32));
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&d1Empty[a]);
+            // F of this thread's basis columns -> A2 (rows m2 = (kw, c), k = (h, f))
+            uint8_t* ahi = sA2 + (g & 1) * 2 * F::kA2Bytes;
+            uint8_t* alo = ahi + F::kA2Bytes;
+            const int hl = 2 * pig + r;                    // row within the group
 #pragma unroll
-                for (int kh = 0; kh < MH; ++kh) acc[i][kh] = make_float2(0.f, 0.f);
-            for (int k = 0; k < pairs_per_unit; ++k, ++it) {
-                const int a = it & 1;
-                if (!mbar_wait(&accFull[a], (it >> 1) & 1, sAbort)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t tb = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * 128 + 8 * third;
-                uint32_t d[4][8];
+            for (int t2 = 0; t2 < 4; ++t2) {
+                float fv[2];
 #pragma unroll
-                for (int l = 0; l < 4; ++l) {
-                    asm volatile(
-                        "tcgen05.ld.sync.aligned.32x32b.x8.b32 "
-                        "{%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                        : "=r"(d[l][0]), "=r"(d[l][1]), "=r"(d[l][2]), "=r"(d[l][3]), "=r"(d[l][4]),
-                          "=r"(d[l][5]), "=r"(d[l][6]), "=r"(d[l][7])
-                        : "r"(tb + l * 32));
-                }
-                tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&accEmpty[a]);
-                float2* f = sF + (it & 1) * (2 * MW * C);
-#pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                    const int j = 8 * third + t;
-                    // sum_l D_l 256^(3-l) / 2^27 from the smallest term up: every digit
-                    // partial is an integer below 2^22 (exact in fp32) and the power-of-two
-                    // weights are exact, so only the four multiply-adds round
+                for (int f = 0; f < 2; ++f) {
+                    const int t = 2 * t2 + f;
                     float u = __fmaf_rn(__int2float_rn(static_cast<int>(d[3][t])), 0x1p-27f, czp[t]);
                     u = __fmaf_rn(__int2float_rn(static_cast<int>(d[2][t])), 0x1p-19f, u);
                     u = __fmaf_rn(__int2float_rn(static_cast<int>(d[1][t])), 0x1p-11f, u);
                     u = __fmaf_rn(__int2float_rn(static_cast<int>(d[0][t])), 0x1p-3f, u);
-                    float* dst = reinterpret_cast<float*>(f + (r * MW + (j >> 1)) * C + c);
-                    dst[j & 1] = __fmul_rn(u, p.s);
+                    fv[f] = __fmul_rn(u, p.s);
                 }
-                // everyone's row DFT of this row pair is in sF before the H accumulation
-                mbar_arrive(epiBar);
-                if (!mbar_wait(epiBar, nsync & 1u, sAbort)) {
+                const int kw = 4 * third + t2;
+                const int mb = kw >> 1;
+                const int ml = (kw & 1) * C + c;
+                float h0, l0, h1, l1;
+                split_tf32(fv[0], h0, l0);
+                split_tf32(fv[1], h1, l1);
+                const uint32_t off = mb * F::kA2Block + swz_offset(ml * 32 + hl * 8, 32);
+                *reinterpret_cast<float2*>(ahi + off) = make_float2(h0, h1);
+                *reinterpret_cast<float2*>(alo + off) = make_float2(l0, l1);
+            }
+            if (pig == 0 && etid < 32 * 8) {
+                // E of the group's four rows -> B2 (rows n = (kh, ri), k = (h, f))
+                const int n = etid >> 3, k = etid & 7;
+                const int kh = n >> 1, ri = n & 1, hh = k >> 1, f = k & 1;
+                float v = 0.0f;
+                if (kh < MH) {
+                    const int unit = blockIdx.x + (it / pairs_per_unit) * gridDim.x;
+                    const int h = (unit % nHB) * p.HB + 2 * (it % pairs_per_unit) + hh;
+                    const float2 e = __ldg(p.twf_h + h * MH + kh);
+                    v = ri == 0 ? (f == 0 ? e.x : -e.y) : (f == 0 ? e.y : e.x);
+                }
+                float hi, lo;
+                split_tf32(v, hi, lo);
+                uint8_t* bhi = sB2 + (g & 1) * 2 * F::kB2Bytes;
+                const uint32_t off = swz_offset(n * 32 + k * 4, 32);
+                *reinterpret_cast<float*>(bhi + off) = hi;
+                *reinterpret_cast<float*>(bhi + F::kB2Bytes + off) = lo;
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&a2Ready[g & 1]);
+            if (pig == 1 && (g % groups_per_unit) == groups_per_unit - 1) {
+                // unit complete: X -> partial spectrum of (sample, row block)
+                if (!mbar_wait(xFull, u_local & 1, sAbort)) {
                     ok = false;
                     break;
                 }
-                ++nsync;
-                const int h0 = hb * p.HB + 2 * k;
+                tc_fence_after();
+                const int unit = blockIdx.x + u_local * gridDim.x;
+                const int b = unit / nHB, hb = unit % nHB;
+                float2* dst = p.xpart + (static_cast<int64_t>(b) * nHB + hb) * (MH * MW * C);
 #pragma unroll
-                for (int i = 0; i < kPer; ++i) {
-                    const int q = etid + kEpiThr * i;
-                    if (q < kPairs) {
-                        const int kw = q / C, cc = q % C;
+                for (int q = 0; q < 2; ++q) {
+                    const int mb = 2 * third + q;
+                    uint32_t x[24];
+                    const uint32_t xa = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + F::kXCol + mb * 32;
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                        : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]),
+                          "=r"(x[6]), "=r"(x[7]), "=r"(x[8]), "=r"(x[9]), "=r"(x[10]), "=r"(x[11]),
+                          "=r"(x[12]), "=r"(x[13]), "=r"(x[14]), "=r"(x[15])
+                        : "r"(xa));
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x8.b32 "
+                        "{%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                        : "=r"(x[16]), "=r"(x[17]), "=r"(x[18]), "=r"(x[19]), "=r"(x[20]),
+                          "=r"(x[21]), "=r"(x[22]), "=r"(x[23])
+                        : "r"(xa + 16));
+                    tmem_wait_ld();
+                    const int kw = 2 * mb + (m >> 6), cc = m & 63;
 #pragma unroll
-                        for (int rr = 0; rr < 2; ++rr) {
-                            const float2 fv = f[(rr * MW + kw) * C + cc];
-                            const float2* e = sE + (h0 + rr) * MH;
-#pragma unroll
-                            for (int kh = 0; kh < MH; ++kh) {
-                                const float2 ev = e[kh];
-                                acc[i][kh].x = fmaf(fv.x, ev.x, fmaf(-fv.y, ev.y, acc[i][kh].x));
-                                acc[i][kh].y = fmaf(fv.x, ev.y, fmaf(fv.y, ev.x, acc[i][kh].y));
-                            }
-                        }
-                    }
+                    for (int kh = 0; kh < MH; ++kh)
+                        dst[(kh * MW + kw) * C + cc] =
+                            make_float2(__uint_as_float(x[2 * kh]), __uint_as_float(x[2 * kh + 1]));
                 }
-            }
-            if (!ok) break;
-            float2* dst = p.xpart + (static_cast<int64_t>(b) * nHB + hb) * (MH * MW * C);
-#pragma unroll
-            for (int i = 0; i < kPer; ++i) {
-                const int q = etid + kEpiThr * i;
-                if (q < kPairs) {
-                    const int kw = q / C, cc = q % C;
-#pragma unroll
-                    for (int kh = 0; kh < MH; ++kh) dst[(kh * MW + kw) * C + cc] = acc[i][kh];
-                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(xEmpty);
+                ++u_local;
             }
         }
         if (!ok) {
@@ -1931,9 +2016,9 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
     for (int i = 0; i < pl.L; ++i) {
         const int nHB = pl.H / pl.HB;
         const int sm_fwd = (pl.W * C + MW * pl.W * 2) * 4;
-        if (pl.W == 128 && pl.fwd_limbs && pl.H <= 512 && (pl.HB % 2) == 0) {
-            using FC = FCfg<C, MH, MW>;
-            auto k = spec_fwd_tc_kernel<C, MH, MW>;
+        if (pl.W == 128 && pl.fwd_limbs && (pl.HB % 4) == 0) {
+            using FC = F2Cfg<C, MH, MW>;
+            auto k = spec_fwd_tc2_kernel<C, MH, MW>;
             if ((e = set_smem(k, FC::kSmemBytes)) != cudaSuccess) return e;
             CUtensorMap tc;
             if (!encode_2d(&tc, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur], C, M, C, C, 128, C))
