@@ -1393,12 +1393,14 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
         if (!cuda_ok(rt, cudaMalloc(&rt->dy, ny * 4), "cudaMalloc output")) return NFX_INTERNAL;
         rt->dy_cap = ny;
     }
-    // Samples are independent, so a large batch runs as up to four chunks: the input
+    // Samples are independent, so a large batch runs as two or three chunks: the input
     // copy of chunk c+1 and the output copy of chunk c-1 overlap the compute of chunk
     // c (the copy engines of both directions and the SMs work at once; with pinned
-    // host buffers the copies are truly asynchronous).
+    // host buffers the copies are truly asynchronous).  Three chunks split the batch
+    // 1/4, 1/2, 1/4: the first and last copies, which nothing hides, stay small, and
+    // the middle chunk runs at nearly the full batch's efficiency.
     const int64_t B = x_shape[0];
-    const int nchunk = B >= 128 ? 4 : (B >= 32 ? 2 : 1);
+    const int nchunk = B >= 128 ? 3 : (B >= 32 ? 2 : 1);
     if (nchunk > 1 && !rt->s_h2d) {
         bool ok = cudaStreamCreateWithFlags(&rt->s_h2d, cudaStreamNonBlocking) == cudaSuccess &&
                   cudaStreamCreateWithFlags(&rt->s_d2h, cudaStreamNonBlocking) == cudaSuccess;
@@ -1419,9 +1421,18 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
     }
     const size_t xs = nx / static_cast<size_t>(B), ys = ny / static_cast<size_t>(B);
     int64_t b0s[4], nbs[4];
-    for (int c = 0; c < nchunk; ++c) {
-        b0s[c] = B * c / nchunk;
-        nbs[c] = B * (c + 1) / nchunk - b0s[c];
+    if (nchunk == 3) {
+        b0s[0] = 0;
+        b0s[1] = B / 4;
+        b0s[2] = B - B / 4;
+        nbs[0] = b0s[1];
+        nbs[1] = b0s[2] - b0s[1];
+        nbs[2] = B - b0s[2];
+    } else {
+        for (int c = 0; c < nchunk; ++c) {
+            b0s[c] = B * c / nchunk;
+            nbs[c] = B * (c + 1) / nchunk - b0s[c];
+        }
     }
     for (int c = 0; c < nchunk; ++c) {
         const size_t off = static_cast<size_t>(b0s[c]) * xs;
