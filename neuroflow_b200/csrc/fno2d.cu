@@ -297,8 +297,7 @@ __global__ void __launch_bounds__(256) spec_mix_kernel(const float2* __restrict_
 // product accumulated as hi*hi + lo*hi + hi*lo (error ~2^-21 relative).  TCX needs the
 // tile to be one grid row (W == 128); narrower grids evaluate x1 on CUDA cores.
 // ---------------------------------------------------------------------------
-constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA/TMEM, warps 4..11 epilogue
-constexpr int kEpiWarp0 = 4;
+constexpr int kEpiWarp0 = 4;  // warp 0 TMA, warp 1 MMA/TMEM, epilogue warps from 4
 constexpr int kLutMaxCells = 3072;
 
 template <int C, int MH, int MW, bool PROJ, bool TCX>
@@ -1037,7 +1036,13 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
     const int num_tiles = static_cast<int>((p.M + 127) / 128);
     const int t_begin = static_cast<int>(static_cast<int64_t>(num_tiles) * blockIdx.x / gridDim.x);
     const int t_end = static_cast<int>(static_cast<int64_t>(num_tiles) * (blockIdx.x + 1) / gridDim.x);
-    const int P = p.H * p.W;
+    // Logical tile L (the CTA loop order) -> grid row: within a sample, L = 2q and
+    // 2q + 1 are the rows q and q + H/2 (one 128-point tile is one row, W == 128).
+    auto tile_row = [&](int Lt) -> int {
+        const int b = Lt / p.H;
+        const int r = Lt - b * p.H;
+        return b * p.H + (r >> 1) + (r & 1) * (p.H >> 1);
+    };
 
     // ---- set-up
     {
@@ -1108,7 +1113,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                     break;
                 }
                 mbar_arrive_expect_tx(&full[s], L::kABytes);
-                tma_load_2d(sA + s * L::kABytes, &tmIn, &full[s], 0, tile * 128);
+                tma_load_2d(sA + s * L::kABytes, &tmIn, &full[s], 0, tile_row(tile) * 128);
             }
             for (int j = (it > L::kStages ? it - L::kStages : 0); j < it; ++j)
                 if (!mbar_wait_backoff(&full[j % L::kStages], (j / L::kStages) & 1, sAbort, 1024)) break;
@@ -1180,23 +1185,34 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
         __syncwarp();
     } else if (warp >= L::kTBuild0 && warp < L::kEpi0) {
         // ---------------- T builders
-        const int ctid = (warp - L::kTBuild0) * 32 + lane;  // 0..127
+        // Consecutive logical tiles 2q, 2q+1 of a sample are the rows h and h + H/2
+        // (tile_row), whose twiddles differ only by (-1)^kh: with E and O the sums over
+        // even and odd kh, T(h) = E + O and T(h + H/2) = E - O, so one pass over the
+        // cached spectrum builds both T operands.
+        const int ctid = (warp - L::kTBuild0) * 32 + lane;
         constexpr int kBT = L::kTBuildWarps * 32;
         constexpr int kPer = MW * C / kBT;                   // (kw, o) pairs per thread
         static_assert(MW * C % kBT == 0, "T builder layout");
         const int o = ctid % C;
         int cached_b = -1;
         int it = 0;
-        for (int tile = t_begin; tile < t_end; ++tile, ++it) {
-            const int b = it & 1;
-            if (!mbar_wait_backoff(&tFree[b], ((it >> 1) & 1) ^ 1, sAbort, 256)) {
-                *sAbort = 1;
-                atomicOr(p.err, kErrWaitDrain);
-                break;
+        for (int tile = t_begin; tile < t_end && it >= 0;) {
+            // a pair when this logical tile is the even one and its partner is ours too
+            const int two = ((tile & 1) == 0 && tile + 1 < t_end) ? 2 : 1;
+            bool ok = true;
+            for (int q = 0; q < two; ++q) {
+                const int bq = (it + q) & 1;
+                if (!mbar_wait_backoff(&tFree[bq], (((it + q) >> 1) & 1) ^ 1, sAbort, 256)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitDrain);
+                    ok = false;
+                    break;
+                }
             }
-            const int64_t g0 = static_cast<int64_t>(tile) * 128;
-            const int smp = static_cast<int>(g0 / P);
-            const int h = static_cast<int>((g0 % P) / p.W);
+            if (!ok) break;
+            const int pt = tile_row(tile);                   // physical row of this tile
+            const int smp = pt / p.H;
+            const int h = pt - smp * p.H;
             if (smp != cached_b) {
                 // each builder caches exactly the spectrum entries it reads below, so the
                 // reload needs no barrier among the builders
@@ -1213,27 +1229,41 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
             float2 eh[MH];
 #pragma unroll
             for (int kh = 0; kh < MH; ++kh) eh[kh] = __ldg(p.twi_h + h * MH + kh);
-            uint8_t* thi = sTop + b * (2 * C * 128);
-            uint8_t* tlo = thi + C * 128;
+            uint8_t* thi0 = sTop + (it & 1) * (2 * C * 128);
+            uint8_t* thi1 = sTop + ((it + 1) & 1) * (2 * C * 128);
 #pragma unroll
             for (int r = 0; r < kPer; ++r) {
                 const int kw = (ctid + kBT * r) / C;
-                float tr = 0.f, ti = 0.f;
+                float er = 0.f, ei = 0.f, orr = 0.f, oi = 0.f;
 #pragma unroll
-                for (int kh = 0; kh < MH; ++kh) {
+                for (int kh = 0; kh < MH; kh += 2) {
                     const float2 y = sY[(kh * MW + kw) * C + o];
-                    tr = fmaf(y.x, eh[kh].x, fmaf(-y.y, eh[kh].y, tr));
-                    ti = fmaf(y.x, eh[kh].y, fmaf(y.y, eh[kh].x, ti));
+                    er = fmaf(y.x, eh[kh].x, fmaf(-y.y, eh[kh].y, er));
+                    ei = fmaf(y.x, eh[kh].y, fmaf(y.y, eh[kh].x, ei));
                 }
-                float h0, l0, h1, l1;
-                split_tf32(tr, h0, l0);
-                split_tf32(ti, h1, l1);
+#pragma unroll
+                for (int kh = 1; kh < MH; kh += 2) {
+                    const float2 y = sY[(kh * MW + kw) * C + o];
+                    orr = fmaf(y.x, eh[kh].x, fmaf(-y.y, eh[kh].y, orr));
+                    oi = fmaf(y.x, eh[kh].y, fmaf(y.y, eh[kh].x, oi));
+                }
                 const uint32_t off = swz_offset(o * 128 + (2 * kw) * 4, 128);
-                *reinterpret_cast<float2*>(thi + off) = make_float2(h0, h1);
-                *reinterpret_cast<float2*>(tlo + off) = make_float2(l0, l1);
+                float h0, l0, h1, l1;
+                split_tf32(__fadd_rn(er, orr), h0, l0);
+                split_tf32(__fadd_rn(ei, oi), h1, l1);
+                *reinterpret_cast<float2*>(thi0 + off) = make_float2(h0, h1);
+                *reinterpret_cast<float2*>(thi0 + C * 128 + off) = make_float2(l0, l1);
+                if (two == 2) {
+                    split_tf32(__fsub_rn(er, orr), h0, l0);
+                    split_tf32(__fsub_rn(ei, oi), h1, l1);
+                    *reinterpret_cast<float2*>(thi1 + off) = make_float2(h0, h1);
+                    *reinterpret_cast<float2*>(thi1 + C * 128 + off) = make_float2(l0, l1);
+                }
             }
             fence_proxy_async_smem();
-            mbar_arrive(&tReady[b]);
+            for (int q = 0; q < two; ++q) mbar_arrive(&tReady[(it + q) & 1]);
+            tile += two;
+            it += two;
         }
     } else if (warp >= L::kEpi0 && warp < L::kEpi0 + L::kEpiWarps) {
         // ---------------- epilogue
@@ -1330,7 +1360,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                tma_store_2d(&tmOut, buf, c0, tile * 128 + quad * 32);
+                tma_store_2d(&tmOut, buf, c0, tile_row(tile) * 128 + quad * 32);
                 tma_store_commit();
             }
             ++nstore;
