@@ -88,11 +88,22 @@ __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, 
     const float zpf = static_cast<float>(zp);
     const int64_t n = M * kG;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    // the next point's inputs are loaded one iteration ahead
+    float xn[IN];
+    if (t0 < n) {
+#pragma unroll
+        for (int k = 0; k < IN; ++k) xn[k] = __ldg(x + (t0 / kG) * IN + k);
+    }
     for (int64_t t = t0; t < n; t += stride) {
         const int64_t m = t / kG;
         float xv[IN];
 #pragma unroll
-        for (int k = 0; k < IN; ++k) xv[k] = __ldg(x + m * IN + k);
+        for (int k = 0; k < IN; ++k) xv[k] = xn[k];
+        if (t + stride < n) {
+            const int64_t mn = (t + stride) / kG;
+#pragma unroll
+            for (int k = 0; k < IN; ++k) xn[k] = __ldg(x + mn * IN + k);
+        }
         uint32_t words[4] = {0u, 0u, 0u, 0u};
         uint32_t badmask = 0;
 #pragma unroll
@@ -1415,7 +1426,8 @@ struct PCfg {
 
 template <int C>
 __global__ void __launch_bounds__(PCfg<C>::kThreads, 1)
-proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p) {
+proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
+            const __grid_constant__ LayerCols cols) {
     using L = PCfg<C>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1573,8 +1585,8 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p) {
                 uint32_t bad = 0;
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const float4 cp = sCol[c * 16 + j];
-                    const int vint = static_cast<int>(cur[j]) + __float_as_int(cp.y) * rconst -
+                    const float4 cp = cols.v[c * 16 + j];  // constant-bank operands
+                    const int vint = static_cast<int>(cur[j]) + __float_as_int(cp.y) * rconst +
                                      __float_as_int(cp.z);
                     const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
                     if (use_act) {
@@ -2129,7 +2141,7 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
         a.err = pl.err;
         a.y = pl.y;
         if (pl.timer) pl.timer->begin("fno2d_proj", st);
-        k<<<grid_l, PC::kThreads, PC::kSmemBytes, st>>>(tin, a);
+        k<<<grid_l, PC::kThreads, PC::kSmemBytes, st>>>(tin, a, pl.proj_cols);
         if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }

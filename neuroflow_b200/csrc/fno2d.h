@@ -103,6 +103,7 @@ struct Fno2dPlan {
     const float2* twi_h;
     Fno2dLayerPlan layer[kFno2dMaxLayers];
     LayerArgs proj;
+    LayerCols proj_cols;   // proj_q epilogue constants
     unsigned* err;
     KernelTimer* timer;    // nullptr unless profiling is enabled
 };

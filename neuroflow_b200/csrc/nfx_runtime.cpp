@@ -358,6 +358,16 @@ void fno2d_enable_int8(nfx_runtime* rt) {
                 cols.v[o] = make_float4(pc->second.scales[o] * in.scale, zpf, nkf, bias[o]);
             }
         } else {
+            nfx::LayerCols& cols = pl.proj_cols;
+            const std::vector<float>& bias = m.weights.at("proj_q.bias").data;
+            for (int o = 0; o < c.width && o < nfx::kFno2dColMax; ++o) {
+                const int32_t zp = pc->second.zero_points[o];
+                const int32_t nk = -(in.zero_point * sum_w[o]);
+                float zpf, nkf;
+                std::memcpy(&zpf, &zp, 4);
+                std::memcpy(&nkf, &nk, 4);
+                cols.v[o] = make_float4(pc->second.scales[o] * in.scale, zpf, nkf, bias[o]);
+            }
             a.fq_out = fq_for(m, "proj_q.output");
             a.fq_final = fq_for(m, "proj_out.output");
             a.act_table = nullptr;
