@@ -1698,24 +1698,31 @@ struct F2Cfg {
     static constexpr int kTile = 128 * C;                   // one grid row of codes
     static constexpr int kStages = 4;                       // row-pair ring
     static constexpr int kStageBytes = 2 * kTile;
-    static constexpr int kN = 32;                           // basis rows per digit (padded)
-    static constexpr int kLimbBytes = kN * 128;             // [32][128] int8, SW128
+    static constexpr int kN = 32;                           // basis rows per digit in p.limbs
+    static constexpr int kN1 = 4 * 2 * MW;                  // row-DFT MMA N: 4 digits x 24
+    static constexpr int kLimbBytes = kN1 * 128;            // [96][128] int8, SW128
+    static constexpr int kD1Stages = 3;                     // row-DFT accumulator stages
     static constexpr int kMBlocks = (MW * C) / 128;         // M blocks of the H-DFT MMA
     static constexpr int kA2Block = 128 * 32;               // [128 m][8 k] fp32, SW32
     static constexpr int kA2Bytes = kMBlocks * kA2Block;    // one of hi / lo
     static constexpr int kB2Bytes = 32 * 32;                // [32 n][8 k] fp32, SW32
     static constexpr int kOffA = 0;
     static constexpr int kOffB = kOffA + kStages * kStageBytes;
-    static constexpr int kOffA2 = kOffB + 4 * kLimbBytes;    // 2 buffers x (hi, lo)
+    static constexpr int kOffA2 = kOffB + ((kLimbBytes + 1023) / 1024) * 1024;  // 2 x (hi, lo)
     static constexpr int kOffB2 = kOffA2 + 2 * 2 * kA2Bytes; // 2 buffers x (hi, lo)
     static constexpr int kOffBars = kOffB2 + 2 * 2 * kB2Bytes;
-    static constexpr int kNumBars = 2 * kStages + 2 + 2 + 2 + 2 + 2;
+    static constexpr int kNumBars = 2 * kStages + 2 * kD1Stages + 2 + 2 + 2;
     static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
-    static constexpr int kXCol = 256;                       // X accumulator columns
-    static constexpr int kTmemCols = 512;                   // D1: 2 x 128, X: 6 x 32
+    // TMEM: row-DFT stage a at columns [128 a, 128 a + 96); the six 32-column X blocks
+    // fill the gaps [128 a + 96, 128 a + 128) and [384, 480)
+    static constexpr int kTmemCols = 512;
+    __device__ static constexpr uint32_t x_col(int mb) {
+        return mb < 3 ? static_cast<uint32_t>(mb * 128 + 96) : static_cast<uint32_t>(384 + (mb - 3) * 32);
+    }
     static_assert(kSmemBytes <= 227 * 1024, "smem");
     static_assert(2 * MW <= 24 && MH * 2 <= 32, "basis rows");
-    static_assert((MW * C) % 128 == 0 && kMBlocks * 32 <= 256, "H-DFT MMA blocks");
+    static_assert((MW * C) % 128 == 0 && kMBlocks == 6, "H-DFT MMA blocks");
+    static_assert(kN1 % 16 == 0 && kN1 <= 96, "row-DFT MMA N");
     static_assert(2 * MW == 24, "drain layout: 8 basis columns per warp third");
 };
 
@@ -1732,8 +1739,8 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + F::kOffBars);
     uint64_t* empty = full + F::kStages;
     uint64_t* d1Full = empty + F::kStages;
-    uint64_t* d1Empty = d1Full + 2;
-    uint64_t* a2Ready = d1Empty + 2;
+    uint64_t* d1Empty = d1Full + F::kD1Stages;
+    uint64_t* a2Ready = d1Empty + F::kD1Stages;
     uint64_t* a2Free = a2Ready + 2;
     uint64_t* xFull = a2Free + 2;
     uint64_t* xEmpty = xFull + 1;
@@ -1749,14 +1756,15 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
     const int my_units = (num_units - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                          static_cast<int>(gridDim.x);
     const int total = my_units * pairs_per_unit;   // row pairs of this CTA
-    constexpr int kDrainThr = kFwdEpiWarps * 32;
 
     {
-        for (int idx = threadIdx.x; idx < 4 * F::kN * 8; idx += kFwdThreads) {
-            const int l = idx / (F::kN * 8), rem = idx % (F::kN * 8);
-            const int n = rem / 8, ch = rem % 8;
+        // the four digit matrices stacked into one B operand: row l*24 + j = digit l of
+        // basis row j (K-major, 128-byte swizzle)
+        for (int idx = threadIdx.x; idx < F::kN1 * 8; idx += kFwdThreads) {
+            const int row = idx / 8, ch = idx % 8;
+            const int l = row / (2 * MW), n = row % (2 * MW);
             const uint4 v = *reinterpret_cast<const uint4*>(p.limbs + (l * F::kN + n) * 128 + ch * 16);
-            *reinterpret_cast<uint4*>(sB + l * F::kLimbBytes + swz_offset(n * 128 + ch * 16, 128)) = v;
+            *reinterpret_cast<uint4*>(sB + swz_offset(row * 128 + ch * 16, 128)) = v;
         }
         // B2 rows n >= 2*MH stay zero
         for (int idx = threadIdx.x; idx < 2 * 2 * F::kB2Bytes / 16; idx += kFwdThreads)
@@ -1766,14 +1774,16 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
                 mbar_init(&full[s], 1);
                 mbar_init(&empty[s], 1);
             }
-            for (int s = 0; s < 2; ++s) {
+            for (int s = 0; s < F::kD1Stages; ++s) {
                 mbar_init(&d1Full[s], 1);
-                mbar_init(&d1Empty[s], kFwdEpiWarps);
-                mbar_init(&a2Ready[s], 2 * kDrainThr);
+                mbar_init(&d1Empty[s], 4);                // the drain group of this stage
+            }
+            for (int s = 0; s < 2; ++s) {
+                mbar_init(&a2Ready[s], 2 * 128);          // two pairs, one drain group each
                 mbar_init(&a2Free[s], 1);
             }
             mbar_init(xFull, 1);
-            mbar_init(xEmpty, kFwdEpiWarps);
+            mbar_init(xEmpty, 4);                         // the group that drains X
             *sAbort = 0;
             fence_mbar_init();
         }
@@ -1812,7 +1822,7 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
         __syncwarp();
     } else if (warp == 1) {
         if (elect_one()) {
-            constexpr uint32_t idesc1 = idesc_i8(F::kN) | (1u << 15);  // A MN-major
+            constexpr uint32_t idesc1 = idesc_i8(F::kN1) | (1u << 15);  // A MN-major
             constexpr uint32_t idesc2 = idesc_tf32(32);
             bool ok = true;
             // the H-DFT MMA of group g (row pairs 2g, 2g+1)
@@ -1833,7 +1843,7 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
                 const uint32_t blo = bhi + F::kB2Bytes;
 #pragma unroll
                 for (int mb = 0; mb < F::kMBlocks; ++mb) {
-                    const uint32_t d = tmem_base + F::kXCol + mb * 32;
+                    const uint32_t d = tmem_base + F::x_col(mb);
                     const uint32_t ao = mb * F::kA2Block;
                     mma_tf32(d, umma_desc(ahi + ao, 32), umma_desc(bhi, 32), idesc2, first ? 0u : 1u);
                     mma_tf32(d, umma_desc(alo + ao, 32), umma_desc(bhi, 32), idesc2, 1u);
@@ -1847,8 +1857,8 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
             for (; it < total && ok; ++it) {
                 const int s = it % F::kStages;
                 const uint32_t ph = (it / F::kStages) & 1;
-                const int a = it & 1;
-                const uint32_t aph = (it >> 1) & 1;
+                const int a = it % F::kD1Stages;
+                const uint32_t aph = (it / F::kD1Stages) & 1;
                 if (!mbar_wait_backoff(&d1Empty[a], aph ^ 1, sAbort, 128)) {
                     atomicOr(p.err, kErrWaitAccFree);
                     ok = false;
@@ -1861,10 +1871,9 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
                 }
                 tc_fence_after();
                 const uint32_t aBase = smem_u32(sA + s * F::kStageBytes);
-#pragma unroll
-                for (int l = 0; l < 4; ++l) {
-                    const uint32_t d = tmem_base + a * 128 + l * 32;
-                    const uint32_t bBase = smem_u32(sB + l * F::kLimbBytes);
+                {
+                    const uint32_t d = tmem_base + a * 128;
+                    const uint32_t bBase = smem_u32(sB);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         mma_i8(d, umma_desc_mn64(aBase + kk * 2048, F::kTile, 512),
@@ -1881,95 +1890,109 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
         }
         __syncwarp();
     } else if (warp >= 4) {
+        // Three drain groups of four warps (one per TMEM lane quadrant) take turns over
+        // the row pairs (group g drains row-DFT stage g), so three pairs' TMEM reads,
+        // recombination and operand stores overlap.  Each thread recombines all 24
+        // basis columns of its lane (r, c).
         const int ew = warp - 4;            // 0..11
-        const int etid = ew * 32 + lane;    // 0..383
+        const int grp = ew >> 2;            // 0..2
+        const int gtid = (ew & 3) * 32 + lane;  // 0..127 within the group
         const int quad = warp & 3;
-        const int third = ew >> 2;          // basis columns [8 third, 8 third + 8)
         const int m = quad * 32 + lane;     // TMEM lane = (r, c)
         const int r = m / C, c = m % C;
-        float czp[8];                       // -zp * sum_w Bint[j][w] / 2^27
+        constexpr int kJ = 2 * MW;          // 24 basis columns
+        float czp[kJ];                      // -zp * sum_w Bint[j][w] / 2^27
 #pragma unroll
-        for (int t = 0; t < 8; ++t)
-            czp[t] = static_cast<float>(-static_cast<double>(static_cast<long long>(p.zp) * p.sum_b[8 * third + t]) *
+        for (int t = 0; t < kJ; ++t)
+            czp[t] = static_cast<float>(-static_cast<double>(static_cast<long long>(p.zp) * p.sum_b[t]) *
                                         7.450580596923828125e-9);
         bool ok = true;
-        int u_local = 0;
-        for (int it = 0; it < total && ok; ++it) {
+        for (int it = grp; it < total && ok; it += F::kD1Stages) {
             const int g = it >> 1;
-            const int pig = it & 1;                        // pair in group
-            const int a = it & 1;
-            if (pig == 0 && !mbar_wait(&a2Free[g & 1], ((g >> 1) & 1) ^ 1, sAbort)) {
+            const int pig = it & 1;                        // pair in group of four rows
+            const int a = grp;                             // = it % kD1Stages
+            if (!mbar_wait(&a2Free[g & 1], ((g >> 1) & 1) ^ 1, sAbort)) {
                 ok = false;
                 break;
             }
-            if (!mbar_wait(&d1Full[a], (it >> 1) & 1, sAbort)) {
+            if (!mbar_wait(&d1Full[a], (it / F::kD1Stages) & 1, sAbort)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t tb = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * 128 + 8 * third;
-            uint32_t d[4][8];
-#pragma unroll
-            for (int l = 0; l < 4; ++l) {
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x8.b32 "
-                    "{%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                    : "=r"(d[l][0]), "=r"(d[l][1]), "=r"(d[l][2]), "=r"(d[l][3]), "=r"(d[l][4]),
-                      "=r"(d[l][5]), "=r"(d[l][6]), "=r"(d[l][7])
-                    : "r"(tb + l * 32));
-            }
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&d1Empty[a]);
-            // F of this thread's basis columns -> A2 (rows m2 = (kw, c), k = (h, f))
             uint8_t* ahi = sA2 + (g & 1) * 2 * F::kA2Bytes;
             uint8_t* alo = ahi + F::kA2Bytes;
             const int hl = 2 * pig + r;                    // row within the group
+            const uint32_t tb = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * 128;
 #pragma unroll
-            for (int t2 = 0; t2 < 4; ++t2) {
-                float fv[2];
+            for (int part = 0; part < 3; ++part) {         // basis columns 8 part .. 8 part + 7
+                uint32_t d[4][8];
 #pragma unroll
-                for (int f = 0; f < 2; ++f) {
-                    const int t = 2 * t2 + f;
-                    float u = __fmaf_rn(__int2float_rn(static_cast<int>(d[3][t])), 0x1p-27f, czp[t]);
-                    u = __fmaf_rn(__int2float_rn(static_cast<int>(d[2][t])), 0x1p-19f, u);
-                    u = __fmaf_rn(__int2float_rn(static_cast<int>(d[1][t])), 0x1p-11f, u);
-                    u = __fmaf_rn(__int2float_rn(static_cast<int>(d[0][t])), 0x1p-3f, u);
-                    fv[f] = __fmul_rn(u, p.s);
+                for (int l = 0; l < 4; ++l) {
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x8.b32 "
+                        "{%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                        : "=r"(d[l][0]), "=r"(d[l][1]), "=r"(d[l][2]), "=r"(d[l][3]), "=r"(d[l][4]),
+                          "=r"(d[l][5]), "=r"(d[l][6]), "=r"(d[l][7])
+                        : "r"(tb + l * kJ + 8 * part));
                 }
-                const int kw = 4 * third + t2;
-                const int mb = kw >> 1;
-                const int ml = (kw & 1) * C + c;
-                float h0, l0, h1, l1;
-                split_tf32(fv[0], h0, l0);
-                split_tf32(fv[1], h1, l1);
-                const uint32_t off = mb * F::kA2Block + swz_offset(ml * 32 + hl * 8, 32);
-                *reinterpret_cast<float2*>(ahi + off) = make_float2(h0, h1);
-                *reinterpret_cast<float2*>(alo + off) = make_float2(l0, l1);
+                tmem_wait_ld();
+                if (part == 2) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&d1Empty[a]);
+                }
+#pragma unroll
+                for (int t2 = 0; t2 < 4; ++t2) {
+                    float fv[2];
+#pragma unroll
+                    for (int f = 0; f < 2; ++f) {
+                        const int t = 2 * t2 + f;
+                        float u = __fmaf_rn(__int2float_rn(static_cast<int>(d[3][t])), 0x1p-27f, czp[8 * part + t]);
+                        u = __fmaf_rn(__int2float_rn(static_cast<int>(d[2][t])), 0x1p-19f, u);
+                        u = __fmaf_rn(__int2float_rn(static_cast<int>(d[1][t])), 0x1p-11f, u);
+                        u = __fmaf_rn(__int2float_rn(static_cast<int>(d[0][t])), 0x1p-3f, u);
+                        fv[f] = __fmul_rn(u, p.s);
+                    }
+                    const int kw = 4 * part + t2;
+                    const int mb = kw >> 1;
+                    const int ml = (kw & 1) * C + c;
+                    float h0, l0, h1, l1;
+                    split_tf32(fv[0], h0, l0);
+                    split_tf32(fv[1], h1, l1);
+                    const uint32_t off = mb * F::kA2Block + swz_offset(ml * 32 + hl * 8, 32);
+                    *reinterpret_cast<float2*>(ahi + off) = make_float2(h0, h1);
+                    *reinterpret_cast<float2*>(alo + off) = make_float2(l0, l1);
+                }
             }
-            if (pig == 0 && etid < 32 * 8) {
-                // E of the group's four rows -> B2 (rows n = (kh, ri), k = (h, f))
-                const int n = etid >> 3, k = etid & 7;
-                const int kh = n >> 1, ri = n & 1, hh = k >> 1, f = k & 1;
-                float v = 0.0f;
-                if (kh < MH) {
-                    const int unit = blockIdx.x + (it / pairs_per_unit) * gridDim.x;
-                    const int h = (unit % nHB) * p.HB + 2 * (it % pairs_per_unit) + hh;
-                    const float2 e = __ldg(p.twf_h + h * MH + kh);
-                    v = ri == 0 ? (f == 0 ? e.x : -e.y) : (f == 0 ? e.y : e.x);
+            if (pig == 0) {
+                // E of the group's four rows -> B2 (rows n = (kh, ri), k = (h, f)),
+                // two entries per thread of the group draining the first pair
+#pragma unroll
+                for (int e2 = 0; e2 < 2; ++e2) {
+                    const int idx = gtid + 128 * e2;
+                    const int n = idx >> 3, k = idx & 7;
+                    const int kh = n >> 1, ri = n & 1, hh = k >> 1, f = k & 1;
+                    float v = 0.0f;
+                    if (kh < MH) {
+                        const int unit = blockIdx.x + (it / pairs_per_unit) * gridDim.x;
+                        const int h = (unit % nHB) * p.HB + 2 * (it % pairs_per_unit) + hh;
+                        const float2 e = __ldg(p.twf_h + h * MH + kh);
+                        v = ri == 0 ? (f == 0 ? e.x : -e.y) : (f == 0 ? e.y : e.x);
+                    }
+                    float hi, lo;
+                    split_tf32(v, hi, lo);
+                    uint8_t* bhi = sB2 + (g & 1) * 2 * F::kB2Bytes;
+                    const uint32_t off = swz_offset(n * 32 + k * 4, 32);
+                    *reinterpret_cast<float*>(bhi + off) = hi;
+                    *reinterpret_cast<float*>(bhi + F::kB2Bytes + off) = lo;
                 }
-                float hi, lo;
-                split_tf32(v, hi, lo);
-                uint8_t* bhi = sB2 + (g & 1) * 2 * F::kB2Bytes;
-                const uint32_t off = swz_offset(n * 32 + k * 4, 32);
-                *reinterpret_cast<float*>(bhi + off) = hi;
-                *reinterpret_cast<float*>(bhi + F::kB2Bytes + off) = lo;
             }
             fence_proxy_async_smem();
             mbar_arrive(&a2Ready[g & 1]);
             if (pig == 1 && (g % groups_per_unit) == groups_per_unit - 1) {
                 // unit complete: X -> partial spectrum of (sample, row block)
+                const int u_local = it / pairs_per_unit;
                 if (!mbar_wait(xFull, u_local & 1, sAbort)) {
                     ok = false;
                     break;
@@ -1978,11 +2001,10 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
                 const int unit = blockIdx.x + u_local * gridDim.x;
                 const int b = unit / nHB, hb = unit % nHB;
                 float2* dst = p.xpart + (static_cast<int64_t>(b) * nHB + hb) * (MH * MW * C);
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const int mb = 2 * third + q;
+#pragma unroll 1
+                for (int mb = 0; mb < F::kMBlocks; ++mb) {
                     uint32_t x[24];
-                    const uint32_t xa = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + F::kXCol + mb * 32;
+                    const uint32_t xa = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + F::x_col(mb);
                     asm volatile(
                         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
                         "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
@@ -2006,7 +2028,6 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(xEmpty);
-                ++u_local;
             }
         }
         if (!ok) {
