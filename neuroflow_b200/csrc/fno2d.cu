@@ -1424,10 +1424,10 @@ struct PCfg {
     static_assert(kSmemBytes <= 227 * 1024, "smem");
 };
 
-template <int C>
+template <int C, int OUT>
 __global__ void __launch_bounds__(PCfg<C>::kThreads, 1)
 proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
-            const __grid_constant__ LayerCols cols) {
+            const __grid_constant__ ProjCols cols) {
     using L = PCfg<C>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1436,8 +1436,6 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
     uint8_t* sA = smem + L::kOffA;
     float4* sCol = reinterpret_cast<float4*>(smem + L::kOffCol);  // {sW*s_in, zp_w, zp_in*sum_w, bias}
     float* sAct = reinterpret_cast<float*>(smem + L::kOffAct);
-    float* sWout = reinterpret_cast<float*>(smem + L::kOffWout);  // [out_ch][C]
-    float* sBout = sWout + 4 * C;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBars);
     uint64_t* empty = full + L::kStages;
     uint64_t* accFull = empty + L::kStages;
@@ -1466,8 +1464,6 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
         for (int o = threadIdx.x; o < C; o += L::kThreads)
             sCol[o] = make_float4(__fmul_rn(p.scale_w[o], p.s_in), __int_as_float(p.zp_w[o]),
                                   __int_as_float(p.zp_in * p.sum_w[o]), p.bias[o]);
-        for (int i = threadIdx.x; i < p.out_ch * C; i += L::kThreads) sWout[i] = p.w_out[i];
-        for (int i = threadIdx.x; i < p.out_ch; i += L::kThreads) sBout[i] = p.b_out[i];
         if (use_act)
             for (int i = threadIdx.x; i < 256; i += L::kThreads) sAct[i] = p.act_table[i];
         if (threadIdx.x == 0) {
@@ -1556,7 +1552,6 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
         const float zpo = static_cast<float>(p.fq_out.zp);
         const float magic_zp = kMagic + zpo;
         constexpr int nu = linear_unfused_len(C);
-        const int out_ch = p.out_ch;
         for (int it = grp; t_begin + it < t_end; it += L::kGroups) {
             const int tile = t_begin + it;
             const uint32_t aph = (it / L::kGroups) & 1;
@@ -1574,9 +1569,9 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
             tmem_wait_ld16(raw[0]);
             asm volatile("" : "+r"(sum_u));  // sum_u is used after the wait above
             const int rconst = C * p.zp_in - 2 * static_cast<int>(sum_u);
-            float acc_out[4];
+            float acc_out[OUT];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc_out[j] = j < out_ch ? sBout[j] : 0.0f;
+            for (int j = 0; j < OUT; ++j) acc_out[j] = cols.bout[j];
 #pragma unroll
             for (int c = 0; c < C / 16; ++c) {
                 uint32_t (&cur)[16] = raw[c & 1];
@@ -1618,8 +1613,8 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
                 for (int j = 0; j < 16; ++j) {
                     const int o = c * 16 + j;
 #pragma unroll
-                    for (int jj = 0; jj < 4; ++jj)
-                        if (jj < out_ch) acc_out[jj] = linear_step(acc_out[jj], g[j], sWout[jj * C + o], o >= nu);
+                    for (int jj = 0; jj < OUT; ++jj)
+                        acc_out[jj] = linear_step(acc_out[jj], g[j], cols.wout[jj][o], o >= nu);
                 }
                 if (c + 1 < C / 16) tmem_wait_ld16(raw[(c + 1) & 1]);
             }
@@ -1629,8 +1624,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
             const int64_t m = static_cast<int64_t>(tile) * 128 + row;
             if (m < p.M) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    if (j >= out_ch) break;
+                for (int j = 0; j < OUT; ++j) {
                     float yv = acc_out[j];
                     if (p.fq_final.kind == 1) {
                         const float zf = static_cast<float>(p.fq_final.zp);
@@ -1639,7 +1633,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
                     } else {
                         yv = apply_fq(yv, p.fq_final);
                     }
-                    p.y[m * out_ch + j] = yv;
+                    p.y[m * OUT + j] = yv;
                 }
             }
         }
@@ -2150,7 +2144,9 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
     }
     {
         using PC = PCfg<C>;
-        auto k = proj_kernel<C>;
+        auto k = pl.proj.out_ch == 1 ? proj_kernel<C, 1>
+                 : pl.proj.out_ch == 2 ? proj_kernel<C, 2>
+                 : pl.proj.out_ch == 3 ? proj_kernel<C, 3> : proj_kernel<C, 4>;
         if ((e = set_smem(k, PC::kSmemBytes)) != cudaSuccess) return e;
         CUtensorMap tin;
         if (!encode_2d(&tin, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur], C, M, C, C, 128, C))

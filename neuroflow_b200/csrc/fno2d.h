@@ -71,6 +71,13 @@ constexpr int kFno2dColMax = 64;
 struct LayerCols {
     float4 v[kFno2dColMax];
 };
+// The projection's constants: proj_q's epilogue columns as above, and proj_out's
+// weights and biases (out_ch <= 4), read as constant-bank operands.
+struct ProjCols {
+    float4 v[kFno2dColMax];
+    float wout[4][kFno2dColMax];
+    float bout[4];
+};
 
 struct Fno2dLayerPlan {
     float s_in;
@@ -103,7 +110,7 @@ struct Fno2dPlan {
     const float2* twi_h;
     Fno2dLayerPlan layer[kFno2dMaxLayers];
     LayerArgs proj;
-    LayerCols proj_cols;   // proj_q epilogue constants
+    ProjCols proj_cols;    // proj_q epilogue and proj_out constants
     unsigned* err;
     KernelTimer* timer;    // nullptr unless profiling is enabled
 };

@@ -358,7 +358,14 @@ void fno2d_enable_int8(nfx_runtime* rt) {
                 cols.v[o] = make_float4(pc->second.scales[o] * in.scale, zpf, nkf, bias[o]);
             }
         } else {
-            nfx::LayerCols& cols = pl.proj_cols;
+            nfx::ProjCols& cols = pl.proj_cols;
+            const std::vector<float>& wo = m.weights.at("proj_out.weight").data;  // (out_ch, C)
+            const std::vector<float>& bo = m.weights.at("proj_out.bias").data;
+            for (int j = 0; j < 4; ++j) {
+                cols.bout[j] = j < c.out_ch ? bo[j] : 0.0f;
+                for (int o = 0; o < nfx::kFno2dColMax; ++o)
+                    cols.wout[j][o] = (j < c.out_ch && o < c.width) ? wo[static_cast<size_t>(j) * c.width + o] : 0.0f;
+            }
             const std::vector<float>& bias = m.weights.at("proj_q.bias").data;
             for (int o = 0; o < c.width && o < nfx::kFno2dColMax; ++o) {
                 const int32_t zp = pc->second.zero_points[o];
@@ -430,7 +437,7 @@ int ensure_twiddles(nfx_runtime* rt, int H, int W) {
         std::vector<int8_t> limbs(4 * 32 * 128, 0);
         std::vector<long long> sum_b(2 * MW, 0);
         for (int j = 0; j < 2 * MW; ++j) {
-            const int kw = j / 2, n = j < 12 ? j : j + 4;
+            const int kw = j / 2, n = j;  // basis row j of every digit matrix
             for (int w = 0; w < W; ++w) {
                 const double a = two_pi * static_cast<double>((static_cast<int64_t>(kw) * w) % W) / W;
                 const double v = (j & 1) ? -std::sin(a) : std::cos(a);

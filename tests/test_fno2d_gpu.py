@@ -1,4 +1,10 @@
-"""FNO2d INT8 executor on the GPU vs the CPU restatement (oracle mode 1)."""
+"""FNO2d INT8 executor on the GPU vs the CPU restatement (oracle mode 1).
+
+The GPU evaluates the truncated transforms exactly (forward: integer DFT digits on
+tensor cores; inverse: 3xTF32) while the restatement follows the reference's radix-2
+FFT rounding, so an int8 code can in principle flip where z lies within rounding
+distance of a table breakpoint.  On every model and input tested no output moved;
+the tests allow 0.1 % of outputs to move by at most two output steps."""
 import os
 
 import numpy as np
@@ -39,8 +45,7 @@ def test_fno2d_int8_end_to_end(tmp_path, H, W):
     st = _stats(got, want, step)
     print(H, W, st)
     assert np.all(np.isfinite(got))
-    assert st["rel_l2"] < 2e-2, st
-    assert st["frac_diff"] < 0.05, st
+    assert st["frac_diff"] < 1e-3 and st["max_steps"] <= 2, st
 
 
 @pytest.mark.gpu
@@ -94,7 +99,7 @@ def test_fno2d_growing_batch_reuses_handle(tmp_path):
         got = np.zeros((B, 32, 128, 1), np.float32)
         rt.run(x, got)
         st = _stats(got, o.fno2d_forward(m, x, mode=1), step)
-        assert st["rel_l2"] < 2e-2 and st["frac_diff"] < 0.05, (B, st)
+        assert st["frac_diff"] < 1e-3 and st["max_steps"] <= 2, (B, st)
 
 
 @pytest.mark.gpu
@@ -117,7 +122,7 @@ def test_fno2d_int8_two_segment_code_table(tmp_path, scale, zp):
     rt.run(x, got)
     st = _stats(got, want, m.qparams["proj_out.output"].scale)
     print(scale, zp, st)
-    assert st["rel_l2"] < 2e-2 and st["frac_diff"] < 0.05, st
+    assert st["frac_diff"] < 1e-3 and st["max_steps"] <= 2, st
 
 
 @pytest.mark.gpu
@@ -138,3 +143,20 @@ def test_fno2d_host_run_chunked_matches_device_run(tmp_path, B):
     rt.run_device(dx, dy, torch.cuda.current_stream())
     torch.cuda.synchronize()
     assert np.array_equal(got, dy.cpu().numpy())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("in_ch,out_ch", [(2, 2), (4, 4)])
+def test_fno2d_int8_channel_counts(tmp_path, in_ch, out_ch):
+    """Other lift widths and proj_out widths (out_ch up to 4) through the same kernels."""
+    from neuroflow_b200.runtime import InferenceRuntime
+    m, path = _model(tmp_path, L=2, H=32, W=128, in_ch=in_ch, out_ch=out_ch)
+    x = synth.fno2d_inputs(np.random.default_rng(13), 2, 32, 128, in_ch)
+    want = Oracle().fno2d_forward(m, x, mode=1)
+    rt = InferenceRuntime(path)
+    rt.enable_int8_gemm()
+    assert rt.is_int8_gemm_enabled()
+    got = np.zeros_like(want)
+    rt.run(x, got)
+    st = _stats(got, want, m.qparams["proj_out.output"].scale)
+    assert st["frac_diff"] < 1e-3 and st["max_steps"] <= 2, st

@@ -67,7 +67,7 @@ def test_noalloc_matches_allocating_entry_point(tmp_path):
         d = np.abs(got - want)
         assert np.all(np.isfinite(got))
         # the tolerance of the FNO2d end-to-end tests (units of the output step)
-        assert np.mean(d > 0) < 0.05 and d.max() <= 4 * step, (call, d.max(), np.mean(d > 0))
+        assert np.mean(d > 0) < 1e-3 and d.max() <= 2 * step, (call, d.max(), np.mean(d > 0))
 
 
 @pytest.mark.gpu
