@@ -95,22 +95,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
-// The same wait with exponential back-off (__nanosleep from 32 ns up to `max_ns`)
-// between tries: a waiting warp takes almost no issue slots from the warps doing the
+// The same wait with exponential back-off (__nanosleep from `min_ns` up to `max_ns`)
+// between tries (the abort flag and the time budget are checked every 8 tries): a waiting warp takes almost no issue slots from the warps doing the
 // arithmetic, at the price of resuming up to `max_ns` late.  For producers that run
 // stages ahead and for the single-thread MMA issuer.
 __device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                                  uint32_t max_ns) {
+                                                  uint32_t max_ns, uint32_t min_ns = 32) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
     const uint64_t t0 = global_ns();
-    uint32_t ns = 32;
-    for (;;) {
+    uint32_t ns = min_ns;
+    for (uint32_t i = 1;; ++i) {
         __nanosleep(ns);
         if (mbar_try_wait(addr, parity)) return true;
         ns = ns * 2 < max_ns ? ns * 2 : max_ns;
-        if (*abort) return false;
-        if (global_ns() - t0 > kWaitNs) return false;
+        if ((i & 7u) == 0u) {
+            if (*abort) return false;
+            if (global_ns() - t0 > kWaitNs) return false;
+        }
     }
 }
 
