@@ -973,8 +973,13 @@ struct TCfg {
     static constexpr int kAccCols = kX1Col + C;
     static constexpr int kAccStages = 2;
     static constexpr int kTmemCols = pow2ceil(kAccStages * kAccCols);
-    static constexpr int kKx = 32;                      // padded K of the x1 MMA (fp32)
-    static_assert(2 * MW <= kKx, "x1 MMA K");
+    // x1 MMA operands: K = 2 MW = 24 (kw, re/im) in three K-blocks of 8 fp32, each a
+    // 32-byte-row SW32 tile (Binv: 128 points x 8, T: C outputs x 8)
+    static constexpr int kKb = 3;
+    static_assert(2 * MW == 8 * kKb, "x1 MMA K");
+    static constexpr int kBinvBlk = 128 * 32;
+    static constexpr int kTBlk = C * 32;
+    static constexpr int kTBufs = 4;                    // T operand buffers (two tile pairs)
     static_assert(C == 64, "the epilogue is laid out for width 64");
     static constexpr int up1k(int v) { return (v + 1023) / 1024 * 1024; }
     static constexpr int kOffW = 0;
@@ -984,14 +989,15 @@ struct TCfg {
     static constexpr int kOffY = kOffStage + kEpiWarps * 2 * 512;
     static constexpr int kYBytes = MH * MW * C * 8;
     static constexpr int kOffBinv = up1k(kOffY + kYBytes);
-    static constexpr int kBinvBytes = 2 * 128 * kKx * 4;                // hi, lo
+    static constexpr int kBinvBytes = 2 * kKb * kBinvBlk;               // hi, lo
     static constexpr int kOffTop = kOffBinv + kBinvBytes;
-    static constexpr int kTopBytes = 2 * 2 * C * kKx * 4;               // 2 buffers x (hi, lo)
+    static constexpr int kTBuf = 2 * kKb * kTBlk;                       // hi, lo of one T
+    static constexpr int kTopBytes = kTBufs * kTBuf;
     static constexpr int kOffLut = kOffTop + kTopBytes;
     static constexpr int kLutBytes = kLutMaxCells * 8;
     static constexpr int kOffCol = kOffLut + kLutBytes;                // float4 [C]
     static constexpr int kOffBars = kOffCol + C * 16;
-    static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2 + 2;
+    static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2 * kTBufs;
     static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
     static_assert(kSmemBytes <= 227 * 1024, "smem");
 };
@@ -1038,8 +1044,8 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
     uint64_t* accFull = empty + L::kStages;
     uint64_t* accEmpty = accFull + L::kAccStages;
     uint64_t* tReady = accEmpty + L::kAccStages;
-    uint64_t* tFree = tReady + 2;
-    uint32_t* sTmem = reinterpret_cast<uint32_t*>(tFree + 2);
+    uint64_t* tFree = tReady + L::kTBufs;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(tFree + L::kTBufs);
     volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -1070,23 +1076,17 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
         for (int i = threadIdx.x; i < p.lut_cells; i += L::kThreads) sLut[i] = p.code_lut[i];
         for (int o = threadIdx.x; o < C; o += L::kThreads)
             sCol[o] = cols.v[o];
-        // Binv (A operand of the x1 MMA, 128 points x kKx, SW128 K-major), hi and lo
-        for (int idx = threadIdx.x; idx < 128 * L::kKx; idx += L::kThreads) {
-            const int w = idx / L::kKx, j = idx % L::kKx;
-            float v = 0.0f;
-            if (j < 2 * MW) {
-                const float2 t = p.twi_w[(j >> 1) * p.W + w];
-                v = (j & 1) ? -t.y : t.x;
-            }
+        // Binv (A operand of the x1 MMA, 128 points x 24 in three SW32 K-blocks), hi, lo
+        for (int idx = threadIdx.x; idx < 128 * 2 * MW; idx += L::kThreads) {
+            const int w = idx / (2 * MW), j = idx % (2 * MW);
+            const float2 t = p.twi_w[(j >> 1) * p.W + w];
+            const float v = (j & 1) ? -t.y : t.x;
             float hi, lo;
             split_tf32(v, hi, lo);
-            const uint32_t off = swz_offset(w * 128 + j * 4, 128);
+            const uint32_t off = (j >> 3) * L::kBinvBlk + swz_offset(w * 32 + (j & 7) * 4, 32);
             *reinterpret_cast<float*>(sBinv + off) = hi;
-            *reinterpret_cast<float*>(sBinv + 128 * 128 + off) = lo;
+            *reinterpret_cast<float*>(sBinv + L::kKb * L::kBinvBlk + off) = lo;
         }
-        // T operand buffers: zero (the K padding columns stay zero)
-        for (int idx = threadIdx.x; idx < L::kTopBytes / 16; idx += L::kThreads)
-            reinterpret_cast<uint4*>(sTop)[idx] = make_uint4(0, 0, 0, 0);
         if (threadIdx.x == 0) {
             for (int s = 0; s < L::kStages; ++s) {
                 mbar_init(&full[s], 1);
@@ -1096,7 +1096,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                 mbar_init(&accFull[s], 1);
                 mbar_init(&accEmpty[s], L::kEpiWarps);
             }
-            for (int b = 0; b < 2; ++b) {
+            for (int b = 0; b < L::kTBufs; ++b) {
                 mbar_init(&tReady[b], L::kTBuildWarps * 32);
                 mbar_init(&tFree[b], 1);
             }
@@ -1138,7 +1138,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                 const uint32_t ph = (it / L::kStages) & 1;
                 const int a = it % L::kAccStages;
                 const uint32_t aph = (it / L::kAccStages) & 1;
-                const int b = it & 1;
+                const int b = it % L::kTBufs;
                 if (!mbar_wait_backoff(&accEmpty[a], aph ^ 1, sAbort, 128)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitAccFree);
@@ -1149,7 +1149,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                     atomicOr(p.err, kErrWaitTmaFull);
                     break;
                 }
-                if (!mbar_wait_backoff(&tReady[b], (it >> 1) & 1, sAbort, 128)) {
+                if (!mbar_wait_backoff(&tReady[b], (it / L::kTBufs) & 1, sAbort, 128)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitDrain);
                     break;
@@ -1167,21 +1167,21 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                 }
                 {
                     const uint32_t dx = d + L::kX1Col;
-                    const uint32_t bhi = smem_u32(sBinv), blo = bhi + 128 * 128;
-                    const uint32_t thi = smem_u32(sTop) + b * (2 * C * 128);
-                    const uint32_t tlo = thi + C * 128;
+                    const uint32_t bhi = smem_u32(sBinv), blo = bhi + L::kKb * L::kBinvBlk;
+                    const uint32_t thi = smem_u32(sTop) + b * L::kTBuf;
+                    const uint32_t tlo = thi + L::kKb * L::kTBlk;
                     constexpr uint32_t idx1 = idesc_tf32(C);
 #pragma unroll
-                    for (int kk = 0; kk < L::kKx / 8; ++kk)
-                        mma_tf32(dx, umma_desc(bhi + kk * 32, 128), umma_desc(thi + kk * 32, 128),
+                    for (int kk = 0; kk < L::kKb; ++kk)
+                        mma_tf32(dx, umma_desc(bhi + kk * L::kBinvBlk, 32), umma_desc(thi + kk * L::kTBlk, 32),
                                  idx1, kk > 0 ? 1u : 0u);
 #pragma unroll
-                    for (int kk = 0; kk < L::kKx / 8; ++kk)
-                        mma_tf32(dx, umma_desc(blo + kk * 32, 128), umma_desc(thi + kk * 32, 128),
+                    for (int kk = 0; kk < L::kKb; ++kk)
+                        mma_tf32(dx, umma_desc(blo + kk * L::kBinvBlk, 32), umma_desc(thi + kk * L::kTBlk, 32),
                                  idx1, 1u);
 #pragma unroll
-                    for (int kk = 0; kk < L::kKx / 8; ++kk)
-                        mma_tf32(dx, umma_desc(bhi + kk * 32, 128), umma_desc(tlo + kk * 32, 128),
+                    for (int kk = 0; kk < L::kKb; ++kk)
+                        mma_tf32(dx, umma_desc(bhi + kk * L::kBinvBlk, 32), umma_desc(tlo + kk * L::kTBlk, 32),
                                  idx1, 1u);
                 }
                 mma_commit(&empty[s]);
@@ -1212,8 +1212,8 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
             const int two = ((tile & 1) == 0 && tile + 1 < t_end) ? 2 : 1;
             bool ok = true;
             for (int q = 0; q < two; ++q) {
-                const int bq = (it + q) & 1;
-                if (!mbar_wait_backoff(&tFree[bq], (((it + q) >> 1) & 1) ^ 1, sAbort, 256)) {
+                const int bq = (it + q) % L::kTBufs;
+                if (!mbar_wait_backoff(&tFree[bq], (((it + q) / L::kTBufs) & 1) ^ 1, sAbort, 256)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitDrain);
                     ok = false;
@@ -1240,8 +1240,8 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
             float2 eh[MH];
 #pragma unroll
             for (int kh = 0; kh < MH; ++kh) eh[kh] = __ldg(p.twi_h + h * MH + kh);
-            uint8_t* thi0 = sTop + (it & 1) * (2 * C * 128);
-            uint8_t* thi1 = sTop + ((it + 1) & 1) * (2 * C * 128);
+            uint8_t* thi0 = sTop + (it % L::kTBufs) * L::kTBuf;
+            uint8_t* thi1 = sTop + ((it + 1) % L::kTBufs) * L::kTBuf;
 #pragma unroll
             for (int r = 0; r < kPer; ++r) {
                 const int kw = (ctid + kBT * r) / C;
@@ -1258,21 +1258,23 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                     orr = fmaf(y.x, eh[kh].x, fmaf(-y.y, eh[kh].y, orr));
                     oi = fmaf(y.x, eh[kh].y, fmaf(y.y, eh[kh].x, oi));
                 }
-                const uint32_t off = swz_offset(o * 128 + (2 * kw) * 4, 128);
+                // element (o, j = 2 kw + re/im): K-block j / 8, column j % 8
+                const uint32_t off = (kw >> 2) * L::kTBlk + swz_offset(o * 32 + (2 * kw & 7) * 4, 32);
+                constexpr int kLo = L::kKb * L::kTBlk;
                 float h0, l0, h1, l1;
                 split_tf32(__fadd_rn(er, orr), h0, l0);
                 split_tf32(__fadd_rn(ei, oi), h1, l1);
                 *reinterpret_cast<float2*>(thi0 + off) = make_float2(h0, h1);
-                *reinterpret_cast<float2*>(thi0 + C * 128 + off) = make_float2(l0, l1);
+                *reinterpret_cast<float2*>(thi0 + kLo + off) = make_float2(l0, l1);
                 if (two == 2) {
                     split_tf32(__fsub_rn(er, orr), h0, l0);
                     split_tf32(__fsub_rn(ei, oi), h1, l1);
                     *reinterpret_cast<float2*>(thi1 + off) = make_float2(h0, h1);
-                    *reinterpret_cast<float2*>(thi1 + C * 128 + off) = make_float2(l0, l1);
+                    *reinterpret_cast<float2*>(thi1 + kLo + off) = make_float2(l0, l1);
                 }
             }
             fence_proxy_async_smem();
-            for (int q = 0; q < two; ++q) mbar_arrive(&tReady[(it + q) & 1]);
+            for (int q = 0; q < two; ++q) mbar_arrive(&tReady[(it + q) % L::kTBufs]);
             tile += two;
             it += two;
         }
