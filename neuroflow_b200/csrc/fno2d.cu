@@ -50,14 +50,14 @@ __device__ __forceinline__ float activation(float z, int act) {
 // k = t - (1.5 * 2^23 + zp) = rint(r) exactly, and t clamped to 1.5 * 2^23 +
 // [-128, 127] carries the clamped code clamp(rint(r) + zp) as its low byte (and as
 // bits(t) - 0x4B400000).  `bad` is set where the element needs the exact division:
-// r within 2^-13 of a half-integer (where rint and std::round may differ too), or NaN.
+// r within 2^-14 of a half-integer (where rint and std::round may differ too), or NaN.
 // ---------------------------------------------------------------------------
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
 __device__ __forceinline__ float fast_code_t(float v, float inv_s, float magic_zp, bool& bad) {
     const float r = __fmul_rn(v, inv_s);
     const float t = __fadd_rn(r, magic_zp);
     const float k = __fsub_rn(t, magic_zp);
-    bad = !(fabsf(__fsub_rn(r, k)) < 0.4998779296875f);
+    bad = !(fabsf(__fsub_rn(r, k)) < kFastRoundLimit);
     return fminf(fmaxf(t, kMagic - 128.0f), kMagic + 127.0f);
 }
 
@@ -950,10 +950,10 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16
 //   warp 0       TMA producer of the layer-input codes (ring of kStages tiles)
 //   warp 1       MMA issuer and TMEM owner: per tile the int8 local GEMM, the ones
 //                block (sum_a) and the 3xTF32 inverse W-transform x1 = Binv T
-//   warps 2-9    T builders (two per SM sub-partition): the H-direction inverse
-//                transform T[o][kw] of the tile's row from the cached spectrum Y,
-//                split into tf32 hi/lo halves, double-buffered
-//   warps 10-25  epilogue: 4 warps per TMEM lane quadrant, 16 columns each.  Per
+//   warps 2-5    T builders (one per SM sub-partition): the H-direction inverse
+//                transform T[o][kw] of the tile's rows from the cached spectrum Y,
+//                split into tf32 hi/lo halves, four T buffers
+//   warps 6-21   epilogue: 4 warps per TMEM lane quadrant, 16 columns each.  Per
 //                element: dequantise + bias (constant-bank operands), the fast
 //                fake-quant offset k, z = x1 + k s, the next code from the table.
 // The epilogue reads both accumulators into registers and frees the TMEM stage
@@ -962,7 +962,7 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16
 template <int C, int MH, int MW>
 struct TCfg {
     static constexpr int kTBuild0 = 2;                  // first T-builder warp
-    static constexpr int kTBuildWarps = 8;                 // two per SM sub-partition
+    static constexpr int kTBuildWarps = 4;                 // one per SM sub-partition
     static constexpr int kEpi0 = kTBuild0 + kTBuildWarps;  // quadrant = warp & 3
     static constexpr int kEpiWarps = 16;
     static constexpr int kThreads = 32 * (kEpi0 + kEpiWarps);
@@ -971,7 +971,7 @@ struct TCfg {
     static constexpr int kOnesCol = C;
     static constexpr int kX1Col = ((C + 16 + 31) / 32) * 32;
     static constexpr int kAccCols = kX1Col + C;
-    static constexpr int kAccStages = 2;
+    static constexpr int kAccStages = 3;
     static constexpr int kTmemCols = pow2ceil(kAccStages * kAccCols);
     // x1 MMA operands: K = 2 MW = 24 (kw, re/im) in three K-blocks of 8 fp32, each a
     // 32-byte-row SW32 tile (Binv: 128 points x 8, T: C outputs x 8)
@@ -1316,7 +1316,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                 const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
                 const float r = __fmul_rn(v, inv_out);
                 const float k = rintf(r);
-                bad |= static_cast<uint32_t>(!(fabsf(__fsub_rn(r, k)) < 0.4998779296875f)) << j;
+                bad |= static_cast<uint32_t>(!(fabsf(__fsub_rn(r, k)) < kFastRoundLimit)) << j;
                 const float kq = fminf(fmaxf(k, klo), khi);
                 const float z = __fadd_rn(__uint_as_float(x1r[j]), __fmul_rn(kq, s_out));
                 int2 cell;
@@ -1692,7 +1692,7 @@ __device__ __forceinline__ uint64_t umma_desc_mn64(uint32_t smem_addr, uint32_t 
 template <int C, int MH, int MW>
 struct F2Cfg {
     static constexpr int kTile = 128 * C;                   // one grid row of codes
-    static constexpr int kStages = 4;                       // row-pair ring
+    static constexpr int kStages = 6;                       // row-pair ring
     static constexpr int kStageBytes = 2 * kTile;
     static constexpr int kN = 32;                           // basis rows per digit in p.limbs
     static constexpr int kN1 = 4 * 2 * MW;                  // row-DFT MMA N: 4 digits x 24
@@ -1708,7 +1708,8 @@ struct F2Cfg {
     static constexpr int kOffB2 = kOffA2 + 2 * 2 * kA2Bytes; // 2 buffers x (hi, lo)
     static constexpr int kOffBars = kOffB2 + 2 * 2 * kB2Bytes;
     static constexpr int kNumBars = 2 * kStages + 2 * kD1Stages + 2 + 2 + 2;
-    static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
+    static constexpr int kOffCzp = kOffBars + 8 * kNumBars + 16;  // 2*MW floats
+    static constexpr int kSmemBytes = kOffCzp + 4 * 2 * MW + 1024;
     // TMEM: row-DFT stage a at columns [128 a, 128 a + 96); the six 32-column X blocks
     // fill the gaps [128 a + 96, 128 a + 128) and [384, 480)
     static constexpr int kTmemCols = 512;
@@ -1742,6 +1743,7 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
     uint64_t* xEmpty = xFull + 1;
     uint32_t* sTmem = reinterpret_cast<uint32_t*>(xFull + 2);
     volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+    float* sCzp = reinterpret_cast<float*>(smem + F::kOffCzp);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -1765,6 +1767,11 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
         // B2 rows n >= 2*MH stay zero
         for (int idx = threadIdx.x; idx < 2 * 2 * F::kB2Bytes / 16; idx += kFwdThreads)
             reinterpret_cast<uint4*>(sB2)[idx] = make_uint4(0, 0, 0, 0);
+        // the zero-point term of basis column t: -zp * sum_w Bint[t][w] / 2^27
+        if (threadIdx.x < 2 * MW)
+            sCzp[threadIdx.x] = static_cast<float>(
+                -static_cast<double>(static_cast<long long>(p.zp) * p.sum_b[threadIdx.x]) *
+                7.450580596923828125e-9);
         if (threadIdx.x == 0) {
             for (int s = 0; s < F::kStages; ++s) {
                 mbar_init(&full[s], 1);
@@ -1904,20 +1911,69 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
         const int quad = warp & 3;
         const int m = quad * 32 + lane;     // TMEM lane = (r, c)
         const int r = m / C, c = m % C;
-        constexpr int kJ = 2 * MW;          // 24 basis columns
-        float czp[kJ];                      // -zp * sum_w Bint[j][w] / 2^27
+        // digit l of basis columns 8 part .. 8 part + 7 of this thread's lane
+        auto ld_part = [&](uint32_t tb, int part, uint32_t (&d)[4][8]) {
 #pragma unroll
-        for (int t = 0; t < kJ; ++t)
-            czp[t] = static_cast<float>(-static_cast<double>(static_cast<long long>(p.zp) * p.sum_b[t]) *
-                                        7.450580596923828125e-9);
+            for (int l = 0; l < 4; ++l)
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x8.b32 "
+                    "{%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                    : "=r"(d[l][0]), "=r"(d[l][1]), "=r"(d[l][2]), "=r"(d[l][3]), "=r"(d[l][4]),
+                      "=r"(d[l][5]), "=r"(d[l][6]), "=r"(d[l][7])
+                    : "r"(tb + l * 2 * MW + 8 * part)
+                    : "memory");
+        };
+        // keeps every use of d after the tcgen05.wait::ld that precedes it
+        auto pin = [](uint32_t (&d)[4][8]) {
+#pragma unroll
+            for (int l = 0; l < 4; ++l)
+                asm volatile("" : "+r"(d[l][0]), "+r"(d[l][1]), "+r"(d[l][2]), "+r"(d[l][3]),
+                                  "+r"(d[l][4]), "+r"(d[l][5]), "+r"(d[l][6]), "+r"(d[l][7]));
+        };
+        // digits -> fp32 F of 8 basis columns (4 kw x re/im), stored as tf32 hi / lo
+        auto recombine = [&](int part, const uint32_t (&d)[4][8], uint8_t* ahi, uint8_t* alo, int hl) {
+#pragma unroll
+            for (int t2 = 0; t2 < 4; ++t2) {
+                float fv[2];
+#pragma unroll
+                for (int f = 0; f < 2; ++f) {
+                    const int t = 2 * t2 + f;
+                    float u = __fmaf_rn(__int2float_rn(static_cast<int>(d[3][t])), 0x1p-27f, sCzp[8 * part + t]);
+                    u = __fmaf_rn(__int2float_rn(static_cast<int>(d[2][t])), 0x1p-19f, u);
+                    u = __fmaf_rn(__int2float_rn(static_cast<int>(d[1][t])), 0x1p-11f, u);
+                    u = __fmaf_rn(__int2float_rn(static_cast<int>(d[0][t])), 0x1p-3f, u);
+                    fv[f] = __fmul_rn(u, p.s);
+                }
+                const int kw = 4 * part + t2;
+                const int mb = kw >> 1;
+                const int ml = (kw & 1) * C + c;
+                float h0, l0, h1, l1;
+                split_tf32(fv[0], h0, l0);
+                split_tf32(fv[1], h1, l1);
+                const uint32_t off = mb * F::kA2Block + swz_offset(ml * 32 + hl * 8, 32);
+                *reinterpret_cast<float2*>(ahi + off) = make_float2(h0, h1);
+                *reinterpret_cast<float2*>(alo + off) = make_float2(l0, l1);
+            }
+        };
         bool ok = true;
         for (int it = grp; it < total && ok; it += F::kD1Stages) {
             const int g = it >> 1;
             const int pig = it & 1;                        // pair in group of four rows
             const int a = grp;                             // = it % kD1Stages
-            if (!mbar_wait(&a2Free[g & 1], ((g >> 1) & 1) ^ 1, sAbort)) {
-                ok = false;
-                break;
+            // twiddles of the group's E entries (two per thread of the group draining
+            // the first pair), loaded before the waits
+            float2 ev[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            if (pig == 0) {
+#pragma unroll
+                for (int e2 = 0; e2 < 2; ++e2) {
+                    const int idx = gtid + 128 * e2;
+                    const int kh = idx >> 4, hh = (idx & 7) >> 1;
+                    if (kh < MH) {
+                        const int unit = blockIdx.x + (it / pairs_per_unit) * gridDim.x;
+                        const int h = (unit % nHB) * p.HB + 2 * (it % pairs_per_unit) + hh;
+                        ev[e2] = __ldg(p.twf_h + h * MH + kh);
+                    }
+                }
             }
             if (!mbar_wait(&d1Full[a], (it / F::kD1Stages) & 1, sAbort)) {
                 ok = false;
@@ -1928,62 +1984,37 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
             uint8_t* alo = ahi + F::kA2Bytes;
             const int hl = 2 * pig + r;                    // row within the group
             const uint32_t tb = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * 128;
-#pragma unroll
-            for (int part = 0; part < 3; ++part) {         // basis columns 8 part .. 8 part + 7
-                uint32_t d[4][8];
-#pragma unroll
-                for (int l = 0; l < 4; ++l) {
-                    asm volatile(
-                        "tcgen05.ld.sync.aligned.32x32b.x8.b32 "
-                        "{%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                        : "=r"(d[l][0]), "=r"(d[l][1]), "=r"(d[l][2]), "=r"(d[l][3]), "=r"(d[l][4]),
-                          "=r"(d[l][5]), "=r"(d[l][6]), "=r"(d[l][7])
-                        : "r"(tb + l * kJ + 8 * part));
-                }
-                tmem_wait_ld();
-                if (part == 2) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&d1Empty[a]);
-                }
-#pragma unroll
-                for (int t2 = 0; t2 < 4; ++t2) {
-                    float fv[2];
-#pragma unroll
-                    for (int f = 0; f < 2; ++f) {
-                        const int t = 2 * t2 + f;
-                        float u = __fmaf_rn(__int2float_rn(static_cast<int>(d[3][t])), 0x1p-27f, czp[8 * part + t]);
-                        u = __fmaf_rn(__int2float_rn(static_cast<int>(d[2][t])), 0x1p-19f, u);
-                        u = __fmaf_rn(__int2float_rn(static_cast<int>(d[1][t])), 0x1p-11f, u);
-                        u = __fmaf_rn(__int2float_rn(static_cast<int>(d[0][t])), 0x1p-3f, u);
-                        fv[f] = __fmul_rn(u, p.s);
-                    }
-                    const int kw = 4 * part + t2;
-                    const int mb = kw >> 1;
-                    const int ml = (kw & 1) * C + c;
-                    float h0, l0, h1, l1;
-                    split_tf32(fv[0], h0, l0);
-                    split_tf32(fv[1], h1, l1);
-                    const uint32_t off = mb * F::kA2Block + swz_offset(ml * 32 + hl * 8, 32);
-                    *reinterpret_cast<float2*>(ahi + off) = make_float2(h0, h1);
-                    *reinterpret_cast<float2*>(alo + off) = make_float2(l0, l1);
-                }
+            uint32_t dA[4][8], dB[4][8];
+            ld_part(tb, 0, dA);
+            ld_part(tb, 1, dB);
+            // the A2 buffer is free once the H-DFT of two groups back has completed
+            const bool free_ok = mbar_wait(&a2Free[g & 1], ((g >> 1) & 1) ^ 1, sAbort);
+            tmem_wait_ld();
+            pin(dA);
+            pin(dB);
+            if (!free_ok) {
+                ok = false;
+                break;
             }
+            recombine(0, dA, ahi, alo, hl);
+            ld_part(tb, 2, dA);
+            recombine(1, dB, ahi, alo, hl);
+            tmem_wait_ld();
+            pin(dA);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&d1Empty[a]);
+            recombine(2, dA, ahi, alo, hl);
             if (pig == 0) {
-                // E of the group's four rows -> B2 (rows n = (kh, ri), k = (h, f)),
-                // two entries per thread of the group draining the first pair
+                // E of the group's four rows -> B2 (rows n = (kh, ri), k = (h, f))
 #pragma unroll
                 for (int e2 = 0; e2 < 2; ++e2) {
                     const int idx = gtid + 128 * e2;
                     const int n = idx >> 3, k = idx & 7;
-                    const int kh = n >> 1, ri = n & 1, hh = k >> 1, f = k & 1;
+                    const int kh = n >> 1, ri = n & 1, f = k & 1;
+                    const float2 e = ev[e2];
                     float v = 0.0f;
-                    if (kh < MH) {
-                        const int unit = blockIdx.x + (it / pairs_per_unit) * gridDim.x;
-                        const int h = (unit % nHB) * p.HB + 2 * (it % pairs_per_unit) + hh;
-                        const float2 e = __ldg(p.twf_h + h * MH + kh);
-                        v = ri == 0 ? (f == 0 ? e.x : -e.y) : (f == 0 ? e.y : e.x);
-                    }
+                    if (kh < MH) v = ri == 0 ? (f == 0 ? e.x : -e.y) : (f == 0 ? e.y : e.x);
                     float hi, lo;
                     split_tf32(v, hi, lo);
                     uint8_t* bhi = sB2 + (g & 1) * 2 * F::kB2Bytes;

@@ -34,16 +34,17 @@ __device__ __forceinline__ float fq_code(float v, float s, float zp) {
 
 // The same code without a division on the common path.  r = v * fl(1/s) differs from
 // v / s by at most |v/s| * 2^-23, and the reference's quotient fl(v / s) from v / s by
-// at most |v/s| * 2^-24; for |v/s| < 2^9 the two are within 1.5 * 2^-14 of each other,
+// at most |v/s| * 2^-24; for |v/s| < 2^8 the two are within 1.5 * 2^-15 of each other,
 // so rounding r to the nearest integer gives the rounding of the reference's quotient
-// whenever r is not within 2^-13 of a half-integer (there round-half-away and
-// round-half-even agree too).  For |v/s| >= 2^9 both roundings saturate the code
-// (|k| > 255 for any zero point).  Inputs next to a half-integer, and NaN, take the
-// exact path.
+// whenever r is not within 2^-14 of a half-integer (there round-half-away and
+// round-half-even agree too; r - rint(r) is exact).  For |v/s| >= 2^8 both roundings
+// are at least 256 in magnitude and saturate the code (|k| > 255 for any zero point).
+// Inputs next to a half-integer, and NaN, take the exact path.
+constexpr float kFastRoundLimit = 0.49993896484375f;  // 0.5 - 2^-14
 __device__ __forceinline__ float fq_code_fast(float v, float s, float inv_s, float zp) {
     const float r = __fmul_rn(v, inv_s);
     const float k = rintf(r);
-    if (!(fabsf(__fsub_rn(r, k)) < 0.4998779296875f)) return fq_code(v, s, zp);
+    if (!(fabsf(__fsub_rn(r, k)) < kFastRoundLimit)) return fq_code(v, s, zp);
     float q = __fadd_rn(k, zp);
     q = fminf(fmaxf(q, -128.0f), 127.0f);
     return q;
@@ -55,7 +56,7 @@ __device__ __forceinline__ float fq_code_fast(float v, float s, float inv_s, flo
 __device__ __forceinline__ float fq_code_try(float v, float inv_s, float zp, bool& bad) {
     const float r = __fmul_rn(v, inv_s);
     const float k = rintf(r);
-    bad = !(fabsf(__fsub_rn(r, k)) < 0.4998779296875f);
+    bad = !(fabsf(__fsub_rn(r, k)) < kFastRoundLimit);
     return fminf(fmaxf(__fadd_rn(k, zp), -128.0f), 127.0f);
 }
 
@@ -65,7 +66,7 @@ __device__ __forceinline__ float fq_code_try(float v, float inv_s, float zp, boo
 __device__ __forceinline__ float fq_offset_try(float v, float inv_s, float klo, float khi, bool& bad) {
     const float r = __fmul_rn(v, inv_s);
     const float k = rintf(r);
-    bad = !(fabsf(__fsub_rn(r, k)) < 0.4998779296875f);
+    bad = !(fabsf(__fsub_rn(r, k)) < kFastRoundLimit);
     return fminf(fmaxf(k, klo), khi);
 }
 
