@@ -1308,7 +1308,9 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
             // x1 + x2 and the next code from the table cell (breakpoint t, codes below /
             // from t), inserted into the packed word with one byte permute.
             uint32_t packed[4];
-            uint32_t bad = 0;
+            // per packed word, the largest |r - rint(r)| of its four elements (r is finite:
+            // v comes from an integer accumulator)
+            float dmax[4];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const float4 cp = cols.v[c0 + j];  // constant cache, uniform
@@ -1316,7 +1318,8 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                 const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
                 const float r = __fmul_rn(v, inv_out);
                 const float k = rintf(r);
-                bad |= static_cast<uint32_t>(!(fabsf(__fsub_rn(r, k)) < kFastRoundLimit)) << j;
+                const float d = fabsf(__fsub_rn(r, k));
+                dmax[j >> 2] = (j & 3) == 0 ? d : fmaxf(dmax[j >> 2], d);
                 const float kq = fminf(fmaxf(k, klo), khi);
                 const float z = __fadd_rn(__uint_as_float(x1r[j]), __fmul_rn(kq, s_out));
                 int2 cell;
@@ -1332,32 +1335,41 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                 const uint32_t prev = (j & 3) == 0 ? 0u : packed[j >> 2];
                 packed[j >> 2] = __byte_perm(prev, static_cast<uint32_t>(cell.y), sel);
             }
-            // rare: elements whose quotient lies next to a half-integer (or is NaN) take
-            // the exact division; their accumulators are read again from TMEM
-            uint32_t any = __reduce_or_sync(0xffffffffu, bad);
+            // rare: a word holding an element whose quotient lies next to a half-integer;
+            // its four accumulators are read again from TMEM and those elements take the
+            // exact division
+            const uint32_t badw = (dmax[0] < kFastRoundLimit ? 0u : 1u) | (dmax[1] < kFastRoundLimit ? 0u : 2u) |
+                                  (dmax[2] < kFastRoundLimit ? 0u : 4u) | (dmax[3] < kFastRoundLimit ? 0u : 8u);
+            uint32_t any = __reduce_or_sync(0xffffffffu, badw);
             while (any) {
-                const int j = __ffs(any) - 1;
+                const int w4 = __ffs(any) - 1;
                 any &= any - 1;
-                uint32_t rj, xj;
-                tmem_ld1(tbase + c0 + j, rj);
-                tmem_ld1(tbase + L::kX1Col + c0 + j, xj);
+                uint32_t rj[4], xj[4];
+                tmem_ld4(tbase + c0 + 4 * w4, rj);
+                tmem_ld4(tbase + L::kX1Col + c0 + 4 * w4, xj);
                 tmem_wait_ld();
-                if (bad & (1u << j)) {
-                    const float4 cp = sCol[c0 + j];
-                    const int vint = static_cast<int>(rj) + __float_as_int(cp.y) * m2s + __float_as_int(cp.z);
-                    const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
-                    const float x2 = __fmul_rn(__fsub_rn(fq_code(v, s_out, zpo), zpo), s_out);
-                    const float z = __fadd_rn(__uint_as_float(xj), x2);
-                    const bool s0 = TWO && z < p.lut_split;
-                    const int2 cell = lut_cell_sat(z, sLut, s0 ? p.lut_alpha0 : p.lut_alpha1,
-                                                   s0 ? p.lut_beta0 : p.lut_beta1, p.lut_nm1);
-                    const uint32_t code = (z >= __int_as_float(cell.x) ? (cell.y >> 8) : cell.y) & 0xFFu;
-                    const int sh = 8 * (j & 3);
-                    uint32_t w = j < 4 ? packed[0] : (j < 8 ? packed[1] : (j < 12 ? packed[2] : packed[3]));
-                    w = (w & ~(0xFFu << sh)) | (code << sh);
-                    if (j < 4) packed[0] = w;
-                    else if (j < 8) packed[1] = w;
-                    else if (j < 12) packed[2] = w;
+                asm volatile("" : "+r"(rj[0]), "+r"(rj[1]), "+r"(rj[2]), "+r"(rj[3]), "+r"(xj[0]),
+                                  "+r"(xj[1]), "+r"(xj[2]), "+r"(xj[3]));  // uses stay after the wait
+                if (badw & (1u << w4)) {
+                    uint32_t w = w4 == 0 ? packed[0] : (w4 == 1 ? packed[1] : (w4 == 2 ? packed[2] : packed[3]));
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        const float4 cp = sCol[c0 + 4 * w4 + jj];
+                        const int vint = static_cast<int>(rj[jj]) + __float_as_int(cp.y) * m2s + __float_as_int(cp.z);
+                        const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
+                        const float r = __fmul_rn(v, inv_out);
+                        if (fabsf(__fsub_rn(r, rintf(r))) < kFastRoundLimit) continue;
+                        const float x2 = __fmul_rn(__fsub_rn(fq_code(v, s_out, zpo), zpo), s_out);
+                        const float z = __fadd_rn(__uint_as_float(xj[jj]), x2);
+                        const bool s0 = TWO && z < p.lut_split;
+                        const int2 cell = lut_cell_sat(z, sLut, s0 ? p.lut_alpha0 : p.lut_alpha1,
+                                                       s0 ? p.lut_beta0 : p.lut_beta1, p.lut_nm1);
+                        const uint32_t code = (z >= __int_as_float(cell.x) ? (cell.y >> 8) : cell.y) & 0xFFu;
+                        w = (w & ~(0xFFu << (8 * jj))) | (code << (8 * jj));
+                    }
+                    if (w4 == 0) packed[0] = w;
+                    else if (w4 == 1) packed[1] = w;
+                    else if (w4 == 2) packed[2] = w;
                     else packed[3] = w;
                 }
             }
