@@ -64,68 +64,65 @@ __device__ __forceinline__ float fast_code_t(float v, float inv_s, float magic_z
 // ---------------------------------------------------------------------------
 // lift: x (M, in_ch) fp32 -> codes (M, C) with the lift.output qparams.
 // fno.cpp:848-853 (Linear + fake-quant), fno.cpp:51-80 (the dot product from the bias).
-// One thread per (point, 16 channels); the channel group of a thread is fixed, so its
-// weights and biases stay in registers for the whole grid-stride loop.
+// One thread per point and all C channels: the weights and biases are constant-bank
+// operands (compile-time offsets), so a thread holds only its inputs and packed codes
+// and the kernel runs at full occupancy.  The fast-path test keeps the largest
+// |r - rint(r)| of the point (NaN-propagating max); a point with a near-half-integer
+// quotient, or a NaN, recomputes its channels with the exact division.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
 template <int C, int IN>
 __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, int64_t M,
-                                                   const float* __restrict__ w,
-                                                   const float* __restrict__ b, float s, int zp,
+                                                   const __grid_constant__ LiftCols lc, float s, int zp,
                                                    float inv_s, int8_t* __restrict__ codes) {
-    constexpr int kG = C / 16;
-    static_assert(256 % kG == 0, "channel groups per block");
+    static_assert(C % 16 == 0 && C <= kFno2dColMax && IN <= kFno2dLiftInMax, "lift layout");
     constexpr int nu = linear_unfused_len(IN);
-    const int64_t t0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-    const int o0 = static_cast<int>(t0 % kG) * 16;
-    float wr[IN][16], br[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        br[j] = __ldg(b + o0 + j);
-#pragma unroll
-        for (int k = 0; k < IN; ++k) wr[k][j] = __ldg(w + (o0 + j) * IN + k);
-    }
     const float magic_zp = kMagic + static_cast<float>(zp);
     const float zpf = static_cast<float>(zp);
-    const int64_t n = M * kG;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    // the next point's inputs are loaded one iteration ahead
-    float xn[IN];
-    if (t0 < n) {
-#pragma unroll
-        for (int k = 0; k < IN; ++k) xn[k] = __ldg(x + (t0 / kG) * IN + k);
-    }
-    for (int64_t t = t0; t < n; t += stride) {
-        const int64_t m = t / kG;
+    for (int64_t m = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; m < M; m += stride) {
         float xv[IN];
 #pragma unroll
-        for (int k = 0; k < IN; ++k) xv[k] = xn[k];
-        if (t + stride < n) {
-            const int64_t mn = (t + stride) / kG;
+        for (int k = 0; k < IN; ++k) xv[k] = __ldg(x + m * IN + k);
+        uint32_t words[C / 4];
+        float dmax[C / 16];   // per group of 16 channels
 #pragma unroll
-            for (int k = 0; k < IN; ++k) xn[k] = __ldg(x + mn * IN + k);
-        }
-        uint32_t words[4] = {0u, 0u, 0u, 0u};
-        uint32_t badmask = 0;
+        for (int o = 0; o < C; ++o) {
+            float acc = lc.b[o];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            float acc = br[j];
+            for (int k = 0; k < IN; ++k) acc = linear_step(acc, xv[k], lc.w[o][k], k >= nu);
+            const float r = __fmul_rn(acc, inv_s);
+            const float t = __fadd_rn(r, magic_zp);
+            const float d = fabsf(__fsub_rn(r, __fsub_rn(t, magic_zp)));
+            dmax[o >> 4] = (o & 15) == 0 ? d : fmax_nan(dmax[o >> 4], d);
+            const float tc = fminf(fmaxf(t, kMagic - 128.0f), kMagic + 127.0f);
+            const uint32_t sel = (0x3210u & ~(0xFu << (4 * (o & 3)))) | (4u << (4 * (o & 3)));
+            words[o >> 2] = __byte_perm((o & 3) == 0 ? 0u : words[o >> 2], __float_as_uint(tc), sel);
+        }
 #pragma unroll
-            for (int k = 0; k < IN; ++k) acc = linear_step(acc, xv[k], wr[k][j], k >= nu);
-            bool bad;
-            const float tc = fast_code_t(acc, inv_s, magic_zp, bad);
-            badmask |= static_cast<uint32_t>(bad) << j;
-            const uint32_t sel = (0x3210u & ~(0xFu << (4 * (j & 3)))) | (4u << (4 * (j & 3)));
-            words[j >> 2] = __byte_perm(words[j >> 2], __float_as_uint(tc), sel);
+        for (int g = 0; g < C / 16; ++g) {
+            if (dmax[g] < kFastRoundLimit) continue;
+            // rare: a quotient next to a half-integer, huge or NaN in this group
+#pragma unroll 1
+            for (int o = 16 * g; o < 16 * g + 16; ++o) {
+                float a = lc.b[o];
+                for (int k = 0; k < IN; ++k) a = linear_step(a, xv[k], lc.w[o][k], k >= nu);
+                const float r = __fmul_rn(a, inv_s);
+                if (fabsf(__fsub_rn(r, rintf(r))) < kFastRoundLimit) continue;
+                const uint32_t byte = static_cast<uint32_t>(static_cast<int>(fq_code(a, s, zpf))) & 0xFFu;
+                uint32_t& w = words[o >> 2];
+                w = (w & ~(0xFFu << (8 * (o & 3)))) | (byte << (8 * (o & 3)));
+            }
         }
-        while (badmask) {  // rare: quotient next to a half-integer, huge or NaN
-            const int j = __ffs(badmask) - 1;
-            badmask &= badmask - 1;
-            float a = __ldg(b + o0 + j);
-            for (int k = 0; k < IN; ++k) a = linear_step(a, xv[k], __ldg(w + (o0 + j) * IN + k), k >= nu);
-            const uint32_t byte = static_cast<uint32_t>(static_cast<int>(fq_code(a, s, zpf))) & 0xFFu;
-            words[j >> 2] = (words[j >> 2] & ~(0xFFu << (8 * (j & 3)))) | (byte << (8 * (j & 3)));
-        }
-        *reinterpret_cast<uint4*>(codes + m * C + o0) = make_uint4(words[0], words[1], words[2], words[3]);
+        uint4* dst = reinterpret_cast<uint4*>(codes + m * C);
+#pragma unroll
+        for (int q = 0; q < C / 16; ++q)
+            dst[q] = make_uint4(words[4 * q], words[4 * q + 1], words[4 * q + 2], words[4 * q + 3]);
     }
 }
 
@@ -2102,13 +2099,13 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
     const int64_t M = static_cast<int64_t>(pl.B) * pl.H * pl.W;
     // lift
     {
-        const int64_t blocks64 = (M * (C / 16) + 255) / 256;
+        const int64_t blocks64 = (M + 255) / 256;
         const int grid = static_cast<int>(blocks64 < 148 * 8 ? blocks64 : 148 * 8);
         if (pl.timer) pl.timer->begin("fno2d_lift", st);
         switch (pl.in_ch) {
 #define NFX_LIFT(n)                                                                            \
     case n:                                                                                    \
-        lift_kernel<C, n><<<grid, 256, 0, st>>>(pl.x, M, pl.lift_w, pl.lift_b, pl.lift_s,       \
+        lift_kernel<C, n><<<grid, 256, 0, st>>>(pl.x, M, pl.lift_cols, pl.lift_s,               \
                                                 pl.lift_zp, pl.lift_inv_s, pl.codes[0]);        \
         break;
             NFX_LIFT(1) NFX_LIFT(2) NFX_LIFT(3) NFX_LIFT(4) NFX_LIFT(5) NFX_LIFT(6) NFX_LIFT(7)

@@ -79,6 +79,13 @@ struct ProjCols {
     float bout[4];
 };
 
+// The lift's weights (C, in_ch <= 8) and biases, read as constant-bank operands.
+constexpr int kFno2dLiftInMax = 8;
+struct LiftCols {
+    float w[kFno2dColMax][kFno2dLiftInMax];
+    float b[kFno2dColMax];
+};
+
 struct Fno2dLayerPlan {
     float s_in;
     int zp_in;
@@ -99,6 +106,7 @@ struct Fno2dPlan {
     float lift_s;
     int lift_zp;
     float lift_inv_s;
+    LiftCols lift_cols;    // the same weights and biases as constant-bank operands
     int8_t* codes[2];      // ping-pong (B*H*W, C)
     float2* xpart;         // (B, H/HB, MH*MW, C)
     float2* Y;             // (B, MH*MW, C)

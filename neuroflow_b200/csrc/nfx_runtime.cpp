@@ -388,6 +388,16 @@ void fno2d_enable_int8(nfx_runtime* rt) {
     pl.lift_s = lq.scale;
     pl.lift_zp = lq.zero_point;
     pl.lift_inv_s = 1.0f / lq.scale;
+    {
+        const std::vector<float>& lw = m.weights.at("lift.weight").data;  // (C, in_ch)
+        const std::vector<float>& lb = m.weights.at("lift.bias").data;
+        pl.lift_cols = nfx::LiftCols{};
+        for (int o = 0; o < c.width && o < nfx::kFno2dColMax; ++o) {
+            pl.lift_cols.b[o] = lb[o];
+            for (int k = 0; k < c.in_ch && k < nfx::kFno2dLiftInMax; ++k)
+                pl.lift_cols.w[o][k] = lw[static_cast<size_t>(o) * c.in_ch + k];
+        }
+    }
     rt->int8_enabled = true;
 }
 
