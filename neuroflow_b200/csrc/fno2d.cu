@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, 
 #pragma unroll
         for (int k = 0; k < IN; ++k) xv[k] = __ldg(x + m * IN + k);
         uint32_t words[C / 4];
-        float dmax[C / 16];   // per group of 16 channels
+        float dmax[C / 4];    // per packed word of 4 channels
 #pragma unroll
         for (int o = 0; o < C; ++o) {
             float acc = lc.b[o];
@@ -99,17 +99,17 @@ __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, 
             const float r = __fmul_rn(acc, inv_s);
             const float t = __fadd_rn(r, magic_zp);
             const float d = fabsf(__fsub_rn(r, __fsub_rn(t, magic_zp)));
-            dmax[o >> 4] = (o & 15) == 0 ? d : fmax_nan(dmax[o >> 4], d);
+            dmax[o >> 2] = (o & 3) == 0 ? d : fmax_nan(dmax[o >> 2], d);
             const float tc = fminf(fmaxf(t, kMagic - 128.0f), kMagic + 127.0f);
             const uint32_t sel = (0x3210u & ~(0xFu << (4 * (o & 3)))) | (4u << (4 * (o & 3)));
             words[o >> 2] = __byte_perm((o & 3) == 0 ? 0u : words[o >> 2], __float_as_uint(tc), sel);
         }
 #pragma unroll
-        for (int g = 0; g < C / 16; ++g) {
+        for (int g = 0; g < C / 4; ++g) {
             if (dmax[g] < kFastRoundLimit) continue;
             // rare: a quotient next to a half-integer, huge or NaN in this group
 #pragma unroll 1
-            for (int o = 16 * g; o < 16 * g + 16; ++o) {
+            for (int o = 4 * g; o < 4 * g + 4; ++o) {
                 float a = lc.b[o];
                 for (int k = 0; k < IN; ++k) a = linear_step(a, xv[k], lc.w[o][k], k >= nu);
                 const float r = __fmul_rn(a, inv_s);
