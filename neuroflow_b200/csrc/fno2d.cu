@@ -1308,6 +1308,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
             // per packed word, the largest |r - rint(r)| of its four elements (r is finite:
             // v comes from an integer accumulator)
             float dmax[4];
+            float zz[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const float4 cp = cols.v[c0 + j];  // constant cache, uniform
@@ -1318,19 +1319,31 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                 const float d = fabsf(__fsub_rn(r, k));
                 dmax[j >> 2] = (j & 3) == 0 ? d : fmaxf(dmax[j >> 2], d);
                 const float kq = fminf(fmaxf(k, klo), khi);
-                const float z = __fadd_rn(__uint_as_float(x1r[j]), __fmul_rn(kq, s_out));
-                int2 cell;
-                if constexpr (TWO) {
-                    const bool s0 = z < p.lut_split;
-                    cell = lut_cell_sat(z, sLut, s0 ? p.lut_alpha0 : p.lut_alpha1,
-                                        s0 ? p.lut_beta0 : p.lut_beta1, p.lut_nm1);
-                } else {
-                    cell = lut_cell_sat(z, sLut, p.lut_alpha1, p.lut_beta1, p.lut_nm1);
+                zz[j] = __fadd_rn(__uint_as_float(x1r[j]), __fmul_rn(kq, s_out));
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                int2 cell[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float z = zz[8 * h + q];
+                    if constexpr (TWO) {
+                        const bool s0 = z < p.lut_split;
+                        cell[q] = lut_cell_sat(z, sLut, s0 ? p.lut_alpha0 : p.lut_alpha1,
+                                               s0 ? p.lut_beta0 : p.lut_beta1, p.lut_nm1);
+                    } else {
+                        cell[q] = lut_cell_sat(z, sLut, p.lut_alpha1, p.lut_beta1, p.lut_nm1);
+                    }
                 }
-                const uint32_t sel_lo = (0x3210u & ~(0xFu << (4 * (j & 3)))) | (4u << (4 * (j & 3)));
-                const uint32_t sel = z >= __int_as_float(cell.x) ? sel_lo + (1u << (4 * (j & 3))) : sel_lo;
-                const uint32_t prev = (j & 3) == 0 ? 0u : packed[j >> 2];
-                packed[j >> 2] = __byte_perm(prev, static_cast<uint32_t>(cell.y), sel);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int j = 8 * h + q;
+                    const float z = zz[j];
+                    const uint32_t sel_lo = (0x3210u & ~(0xFu << (4 * (j & 3)))) | (4u << (4 * (j & 3)));
+                    const uint32_t sel = z >= __int_as_float(cell[q].x) ? sel_lo + (1u << (4 * (j & 3))) : sel_lo;
+                    const uint32_t prev = (j & 3) == 0 ? 0u : packed[j >> 2];
+                    packed[j >> 2] = __byte_perm(prev, static_cast<uint32_t>(cell[q].y), sel);
+                }
             }
             // rare: a word holding an element whose quotient lies next to a half-integer;
             // its four accumulators are read again from TMEM and those elements take the
