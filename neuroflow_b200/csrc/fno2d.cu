@@ -950,11 +950,13 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16
 //   warps 2-5    T builders (one per SM sub-partition): the H-direction inverse
 //                transform T[o][kw] of the tile's rows from the cached spectrum Y,
 //                split into tf32 hi/lo halves, four T buffers
-//   warps 6-21   epilogue: 4 warps per TMEM lane quadrant, 16 columns each.  Per
+//   warps 6-21   epilogue: two groups of 8 warps take turns over the tiles; in a
+//                group, 2 warps per TMEM lane quadrant, 32 columns each.  Per
 //                element: dequantise + bias (constant-bank operands), the fast
 //                fake-quant offset k, z = x1 + k s, the next code from the table.
-// The epilogue reads both accumulators into registers and frees the TMEM stage
-// before any arithmetic, so the MMA of the tile after next overlaps it.
+// Three accumulator stages: the MMA runs up to two tiles ahead of the epilogue
+// groups, and a group finishing tile t - 2 implies (in-order MMA completion) that the
+// stage of tile t has completed the phase of tile t - 3, so parity waits stay exact.
 // ---------------------------------------------------------------------------
 template <int C, int MH, int MW>
 struct TCfg {
@@ -982,7 +984,7 @@ struct TCfg {
     static constexpr int kOffW = 0;
     static constexpr int kOffOnes = up1k(C * C);
     static constexpr int kOffA = kOffOnes + 1024;
-    static constexpr int kOffStage = kOffA + kStages * kABytes;        // 16 warps x 2 x 512
+    static constexpr int kOffStage = kOffA + kStages * kABytes;        // 16 warps x 1 KB
     static constexpr int kOffY = kOffStage + kEpiWarps * 2 * 512;
     static constexpr int kYBytes = MH * MW * C * 8;
     static constexpr int kOffBinv = up1k(kOffY + kYBytes);
@@ -1091,7 +1093,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
             }
             for (int s = 0; s < L::kAccStages; ++s) {
                 mbar_init(&accFull[s], 1);
-                mbar_init(&accEmpty[s], L::kEpiWarps);
+                mbar_init(&accEmpty[s], L::kEpiWarps / 2);
             }
             for (int b = 0; b < L::kTBufs; ++b) {
                 mbar_init(&tReady[b], L::kTBuildWarps * 32);
@@ -1279,13 +1281,16 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
         // ---------------- epilogue
         const int ew = warp - L::kEpi0;
         const int quad = warp & 3;
-        const int c0 = (ew >> 2) * 16;      // this warp's columns c0 .. c0 + 15
+        const int grp = ew >> 3;                 // two groups take turns over the tiles
+        const int cw = ((ew >> 2) & 1) * 32;     // this warp's columns cw .. cw + 31
         const int kzp = C * p.zp_in;
         const float s_out = p.fq_out.scale, inv_out = p.fq_out.inv_scale;
         const float zpo = static_cast<float>(p.fq_out.zp);
         const float klo = -128.0f - zpo, khi = 127.0f - zpo;
-        int it = 0, nstore = 0;
-        for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+        int nstore = 0;
+        uint8_t* buf = sStage + ew * 1024;
+        for (int it = grp; t_begin + it < t_end; it += 2) {
+            const int tile = t_begin + it;
             const int a = it % L::kAccStages;
             const uint32_t aph = (it / L::kAccStages) & 1;
             if (!mbar_wait(&accFull[a], aph, sAbort)) {
@@ -1295,6 +1300,13 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
             }
             tc_fence_after();
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * L::kAccCols;
+            if (nstore > 0) {
+                if (lane == 0) tma_store_wait_read<0>();
+                __syncwarp();
+            }
+#pragma unroll 1
+            for (int ch = 0; ch < 2; ++ch) {
+            const int c0 = cw + 16 * ch;
             uint32_t raw[16], x1r[16], sum_u;
             tmem_ld16_async(tbase + c0, raw);
             tmem_ld16_async(tbase + L::kX1Col + c0, x1r);
@@ -1383,19 +1395,15 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                     else packed[3] = w;
                 }
             }
+            *reinterpret_cast<uint4*>(buf + lane * 32 + ch * 16) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&accEmpty[a]);
-            uint8_t* buf = sStage + (ew * 2 + (nstore & 1)) * 512;
-            if (nstore >= 2) {
-                if (lane == 0) tma_store_wait_read<1>();
-                __syncwarp();
-            }
-            *reinterpret_cast<uint4*>(buf + lane * 16) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                tma_store_2d(&tmOut, buf, c0, tile_row(tile) * 128 + quad * 32);
+                tma_store_2d(&tmOut, buf, cw, tile_row(tile) * 128 + quad * 32);
                 tma_store_commit();
             }
             ++nstore;
@@ -2186,6 +2194,8 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
             if (pl.timer) pl.timer->begin("fno2d_layer", st);
             if (pl.W == 128 && a.lut_cells > 0 && a.lut_cells <= kLutMaxCells) {
                 using TC = TCfg<C, MH, MW>;
+                if (!encode_2d(&tout, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur ^ 1], C, M, C, C / 2, 32, 0))
+                    return cudaErrorInvalidValue;
                 auto k = a.lut_two ? layer_tc_kernel<C, MH, MW, true> : layer_tc_kernel<C, MH, MW, false>;
                 if ((e = set_smem(k, TC::kSmemBytes)) != cudaSuccess) return e;
                 k<<<grid_l, TC::kThreads, TC::kSmemBytes, st>>>(tin, tout, a, pl.layer[i].cols);
