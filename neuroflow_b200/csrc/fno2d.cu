@@ -293,6 +293,189 @@ __global__ void __launch_bounds__(256) spec_mix_kernel(const float2* __restrict_
 }
 
 // ---------------------------------------------------------------------------
+// spec_mix_tc: the per-mode contraction on tensor cores (C == 64).  For mode m and a
+// tile of 128 samples, with x the sum of the row-block partials (fixed order) as the
+// real row [re, im] per input channel, y = x Wr where Wr is the real (2C x 2C) form of
+// the complex weights (fno.cpp:740-764):
+//   D[b][n] = sum_k X[b][k] Wr[k][n]     (tcgen05 kind::tf32, 3xTF32: hi.hi + lo.hi + hi.lo)
+// in four K chunks of 32 floats (one 128-byte swizzle atom); the weights' tf32 halves
+// are prepared on the host and loaded by TMA, the activations are summed and split by
+// all threads.  Accumulator: 128 lanes (samples) x 128 columns (2 out + re/im).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void split_tf32_m(float x, float& hi, float& lo) {
+    hi = __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+    lo = __fsub_rn(x, hi);
+}
+
+constexpr int kMixTcThreads = 256;
+template <int C>
+struct MixCfg {
+    static constexpr int kK = 2 * C;                 // 128 floats per row
+    static constexpr int kChunk = 32;                // floats per K chunk
+    static constexpr int kChunks = kK / kChunk;
+    static constexpr int kTile = 128 * 128;          // [128 rows][32 floats], SW128
+    static constexpr int kOffAhi = 0;
+    static constexpr int kOffAlo = kTile;
+    static constexpr int kOffBhi = 2 * kTile;
+    static constexpr int kOffBlo = 3 * kTile;
+    static constexpr int kOffBars = 4 * kTile;
+    static constexpr int kSmemBytes = kOffBars + 64 + 1024;
+    static_assert(C == 64, "one 128-column accumulator");
+};
+
+template <int C, int MH, int MW>
+__global__ void __launch_bounds__(kMixTcThreads) spec_mix_tc_kernel(const __grid_constant__ CUtensorMap tmWhi,
+                                                                    const __grid_constant__ CUtensorMap tmWlo,
+                                                                    const float2* __restrict__ xpart, int nHB,
+                                                                    int B, float2* __restrict__ Y,
+                                                                    unsigned* err) {
+    using F = MixCfg<C>;
+    constexpr int M = MH * MW;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* sAhi = smem + F::kOffAhi;
+    uint8_t* sAlo = smem + F::kOffAlo;
+    uint8_t* sBhi = smem + F::kOffBhi;
+    uint8_t* sBlo = smem + F::kOffBlo;
+    uint64_t* bFull = reinterpret_cast<uint64_t*>(smem + F::kOffBars);
+    uint64_t* mmaDone = bFull + 1;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(bFull + 2);
+    volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m = blockIdx.x;
+    const int b0 = blockIdx.y * 128;
+
+    if (threadIdx.x == 0) {
+        mbar_init(bFull, 1);
+        mbar_init(mmaDone, 1);
+        *sAbort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(sTmem, 128);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *sTmem;
+    constexpr uint32_t idesc = idesc_tf32(128);
+    bool ok = true;
+    int issued = 0;   // TMA chunk loads issued
+
+    for (int c = 0; c < F::kChunks && ok; ++c) {
+        if (c > 0 && !mbar_wait(mmaDone, (c - 1) & 1, sAbort)) {
+            ok = false;
+            break;
+        }
+        if (threadIdx.x == 0) {
+            if (c == 0) {
+                prefetch_tmap(&tmWhi);
+                prefetch_tmap(&tmWlo);
+            }
+            mbar_arrive_expect_tx(bFull, 2 * F::kTile);
+            tma_load_2d(sBhi, &tmWhi, bFull, c * F::kChunk, m * F::kK);
+            tma_load_2d(sBlo, &tmWlo, bFull, c * F::kChunk, m * F::kK);
+        }
+        ++issued;
+        // A chunk: rows = samples, columns k = 2 i + re/im for i in [16 c, 16 c + 16)
+        constexpr int kPer = 128 * 16 / kMixTcThreads;   // (row, channel) pairs per thread
+        float2 u[kPer][4];
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) {
+            const int idx = threadIdx.x + kMixTcThreads * q;
+            const int r = idx >> 4, i = 16 * c + (idx & 15);
+            const int b = b0 + r < B ? b0 + r : B - 1;
+            const float2* src = xpart + (static_cast<int64_t>(b) * nHB * M + m) * C + i;
+            if (nHB == 4) {
+#pragma unroll
+                for (int hb = 0; hb < 4; ++hb) u[q][hb] = __ldg(src + static_cast<int64_t>(hb) * M * C);
+            } else {
+                u[q][0] = __ldg(src);
+                for (int hb = 1; hb < nHB; ++hb) {
+                    const float2 w = __ldg(src + static_cast<int64_t>(hb) * M * C);
+                    u[q][0].x += w.x;
+                    u[q][0].y += w.y;
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) {
+            const int idx = threadIdx.x + kMixTcThreads * q;
+            const int r = idx >> 4, il = idx & 15;
+            float2 v = u[q][0];
+            if (nHB == 4) {
+#pragma unroll
+                for (int hb = 1; hb < 4; ++hb) {
+                    v.x += u[q][hb].x;
+                    v.y += u[q][hb].y;
+                }
+            }
+            if (b0 + r >= B) v = make_float2(0.f, 0.f);
+            float hr, lr, hi, li;
+            split_tf32_m(v.x, hr, lr);
+            split_tf32_m(v.y, hi, li);
+            const uint32_t off = swz_offset(r * 128 + il * 8, 128);
+            *reinterpret_cast<float2*>(sAhi + off) = make_float2(hr, hi);
+            *reinterpret_cast<float2*>(sAlo + off) = make_float2(lr, li);
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            if (!mbar_wait(bFull, c & 1, sAbort)) {
+                *sAbort = 1;
+                atomicOr(err, kErrWaitTmaFull);
+            } else {
+                tc_fence_after();
+                const uint32_t ahi = smem_u32(sAhi), alo = smem_u32(sAlo);
+                const uint32_t bhi = smem_u32(sBhi), blo = smem_u32(sBlo);
+#pragma unroll
+                for (int kk = 0; kk < F::kChunk / 8; ++kk) {
+                    mma_tf32(tmem_base, umma_desc(ahi + kk * 32, 128), umma_desc(bhi + kk * 32, 128), idesc,
+                             (c > 0 || kk > 0) ? 1u : 0u);
+                    mma_tf32(tmem_base, umma_desc(alo + kk * 32, 128), umma_desc(bhi + kk * 32, 128), idesc, 1u);
+                    mma_tf32(tmem_base, umma_desc(ahi + kk * 32, 128), umma_desc(blo + kk * 32, 128), idesc, 1u);
+                }
+                mma_commit(mmaDone);
+            }
+        }
+        if (*sAbort) ok = false;
+    }
+    // the last chunk's MMAs
+    if (ok && !mbar_wait(mmaDone, (F::kChunks - 1) & 1, sAbort)) ok = false;
+    if (!ok) {
+        if (threadIdx.x == 0) {
+            atomicOr(err, kErrWaitAccFull);
+            // the TMA loads already issued land before the CTA leaves
+            mbar_wait(bFull, (issued - 1) & 1, sAbort);
+        }
+    } else if (warp < 4) {
+        tc_fence_after();
+        const int r = warp * 32 + lane;
+        const int b = b0 + r;
+        const uint32_t tb = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint32_t v[64];
+            tmem_ld32(tb + h * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
+            tmem_ld32(tb + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+            tmem_wait_ld();
+            asm volatile("" ::: "memory");
+            if (b < B) {
+                float4* dst = reinterpret_cast<float4*>(Y + (static_cast<int64_t>(b) * M + m) * C) + h * 16;
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                    dst[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                         __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 128);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // layer / projection: tcgen05 GEMM over 128-point tiles with fused epilogues.
 //
 // TMEM per accumulator stage: [0, C) int32 local-layer accumulator, [C, C+16)
@@ -2168,7 +2351,26 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
             if (pl.timer) pl.timer->end(st);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
-        {
+        if constexpr (C == 64) {
+            if (pl.layer[i].wmix_hi != nullptr) {
+                using FM = MixCfg<C>;
+                auto k = spec_mix_tc_kernel<C, MH, MW>;
+                if ((e = set_smem(k, FM::kSmemBytes)) != cudaSuccess) return e;
+                CUtensorMap thi, tlo;
+                const uint64_t rows = static_cast<uint64_t>(MH) * MW * FM::kK;
+                if (!encode_2d(&thi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pl.layer[i].wmix_hi, FM::kK, rows,
+                               FM::kK * 4, FM::kChunk, FM::kK, 128) ||
+                    !encode_2d(&tlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pl.layer[i].wmix_lo, FM::kK, rows,
+                               FM::kK * 4, FM::kChunk, FM::kK, 128))
+                    return cudaErrorInvalidValue;
+                if (pl.timer) pl.timer->begin("fno2d_spec_mix", st);
+                k<<<dim3(MH * MW, (pl.B + 127) / 128), kMixTcThreads, FM::kSmemBytes, st>>>(
+                    thi, tlo, pl.xpart, nHB, pl.B, pl.Y, pl.err);
+                if (pl.timer) pl.timer->end(st);
+                if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            }
+        }
+        if (C != 64 || pl.layer[i].wmix_hi == nullptr) {
             auto k = spec_mix_kernel<C, MH, MW>;
             if ((e = set_smem(k, mix_smem_bytes<C>())) != cudaSuccess) return e;
             if (pl.timer) pl.timer->begin("fno2d_spec_mix", st);

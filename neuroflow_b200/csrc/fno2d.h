@@ -90,6 +90,11 @@ struct Fno2dLayerPlan {
     float s_in;
     int zp_in;
     const float2* wspec;  // (MH*MW, C, C) complex, [mode][in][out]
+    // The same weights as one real (2C x 2C) matrix per mode for the tensor-core
+    // contraction, transposed (row n = 2 out + re/im, column k = 2 in + re/im) and split
+    // into tf32 high and low parts: (MH*MW*2C, 2C) each; null when C != 64.
+    const float* wmix_hi;
+    const float* wmix_lo;
     LayerArgs args;
     LayerCols cols;
 };

@@ -271,6 +271,36 @@ int fno2d_create(nfx_runtime* rt) {
                     packed[dst + 1] = wi.data[src];
                 }
         pl.layer[i].wspec = reinterpret_cast<const float2*>(upload(rt, packed.data(), packed.size()));
+        pl.layer[i].wmix_hi = nullptr;
+        pl.layer[i].wmix_lo = nullptr;
+        if (C == 64) {
+            // per mode the real form of y = x W (x, y complex rows): row n = 2 o + ri_out,
+            // column k = 2 in + ri_in; tf32 split as the device's split_tf32
+            const int K = 2 * C;
+            std::vector<float> hi(static_cast<size_t>(M) * K * K), lo(hi.size());
+            auto split = [](float x, float& h, float& l) {
+                uint32_t u;
+                std::memcpy(&u, &x, 4);
+                u = (u + 0x1000u) & 0xFFFFE000u;
+                std::memcpy(&h, &u, 4);
+                l = x - h;
+            };
+            for (int md = 0; md < M; ++md)
+                for (int in = 0; in < C; ++in)
+                    for (int o = 0; o < C; ++o) {
+                        const size_t src = (static_cast<size_t>(in) * C + o) * M + md;
+                        const float r = wr.data[src], im = wi.data[src];
+                        const float v[2][2] = {{r, im}, {-im, r}};  // [ri_in][ri_out]
+                        for (int a2 = 0; a2 < 2; ++a2)
+                            for (int b2 = 0; b2 < 2; ++b2) {
+                                const size_t d = (static_cast<size_t>(md) * K + 2 * o + b2) * K + 2 * in + a2;
+                                split(v[a2][b2], hi[d], lo[d]);
+                            }
+                    }
+            pl.layer[i].wmix_hi = upload(rt, hi.data(), hi.size());
+            pl.layer[i].wmix_lo = upload(rt, lo.data(), lo.size());
+            if (!pl.layer[i].wmix_hi || !pl.layer[i].wmix_lo) return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+        }
         auto& a = pl.layer[i].args;
         a.bias = wptr(rt, "locs." + std::to_string(i) + ".bias");
         if (!pl.layer[i].wspec || !a.bias) return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
