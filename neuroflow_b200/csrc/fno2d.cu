@@ -360,24 +360,11 @@ __global__ void __launch_bounds__(kMixTcThreads) spec_mix_tc_kernel(const __grid
     bool ok = true;
     int issued = 0;   // TMA chunk loads issued
 
-    for (int c = 0; c < F::kChunks && ok; ++c) {
-        if (c > 0 && !mbar_wait(mmaDone, (c - 1) & 1, sAbort)) {
-            ok = false;
-            break;
-        }
-        if (threadIdx.x == 0) {
-            if (c == 0) {
-                prefetch_tmap(&tmWhi);
-                prefetch_tmap(&tmWlo);
-            }
-            mbar_arrive_expect_tx(bFull, 2 * F::kTile);
-            tma_load_2d(sBhi, &tmWhi, bFull, c * F::kChunk, m * F::kK);
-            tma_load_2d(sBlo, &tmWlo, bFull, c * F::kChunk, m * F::kK);
-        }
-        ++issued;
-        // A chunk: rows = samples, columns k = 2 i + re/im for i in [16 c, 16 c + 16)
-        constexpr int kPer = 128 * 16 / kMixTcThreads;   // (row, channel) pairs per thread
-        float2 u[kPer][4];
+    // A chunk c: rows = samples, columns k = 2 i + re/im for i in [16 c, 16 c + 16); the
+    // partials of chunk c + 1 are loaded while the MMAs of chunk c run
+    constexpr int kPer = 128 * 16 / kMixTcThreads;   // (row, channel) pairs per thread
+    float2 u[kPer][4];
+    auto load_chunk = [&](int c) {
 #pragma unroll
         for (int q = 0; q < kPer; ++q) {
             const int idx = threadIdx.x + kMixTcThreads * q;
@@ -396,6 +383,23 @@ __global__ void __launch_bounds__(kMixTcThreads) spec_mix_tc_kernel(const __grid
                 }
             }
         }
+    };
+    load_chunk(0);
+    for (int c = 0; c < F::kChunks && ok; ++c) {
+        if (c > 0 && !mbar_wait(mmaDone, (c - 1) & 1, sAbort)) {
+            ok = false;
+            break;
+        }
+        if (threadIdx.x == 0) {
+            if (c == 0) {
+                prefetch_tmap(&tmWhi);
+                prefetch_tmap(&tmWlo);
+            }
+            mbar_arrive_expect_tx(bFull, 2 * F::kTile);
+            tma_load_2d(sBhi, &tmWhi, bFull, c * F::kChunk, m * F::kK);
+            tma_load_2d(sBlo, &tmWlo, bFull, c * F::kChunk, m * F::kK);
+        }
+        ++issued;
 #pragma unroll
         for (int q = 0; q < kPer; ++q) {
             const int idx = threadIdx.x + kMixTcThreads * q;
@@ -436,6 +440,7 @@ __global__ void __launch_bounds__(kMixTcThreads) spec_mix_tc_kernel(const __grid
                 mma_commit(mmaDone);
             }
         }
+        if (c + 1 < F::kChunks) load_chunk(c + 1);
         if (*sAbort) ok = false;
     }
     // the last chunk's MMAs
