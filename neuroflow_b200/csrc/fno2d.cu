@@ -2042,79 +2042,65 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
         }
         __syncwarp();
     } else if (warp == 1) {
+        // row DFTs: one N = 96 int8 MMA chain per row pair into its D1 stage
         if (elect_one()) {
             constexpr uint32_t idesc1 = idesc_i8(F::kN1) | (1u << 15);  // A MN-major
+            for (int it = 0; it < total; ++it) {
+                const int s = it % F::kStages;
+                const uint32_t ph = (it / F::kStages) & 1;
+                const int a = it % F::kD1Stages;
+                const uint32_t aph = (it / F::kD1Stages) & 1;
+                if (!mbar_wait_backoff(&d1Empty[a], aph ^ 1, sAbort, 128) ||
+                    !mbar_wait_backoff(&full[s], ph, sAbort, 128)) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitAccFree);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t aBase = smem_u32(sA + s * F::kStageBytes);
+                const uint32_t d = tmem_base + a * 128;
+                const uint32_t bBase = smem_u32(sB);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_i8(d, umma_desc_mn64(aBase + kk * 2048, F::kTile, 512),
+                           umma_desc(bBase + kk * 32, 128), idesc1, kk > 0 ? 1u : 0u);
+                mma_commit(&empty[s]);
+                mma_commit(&d1Full[a]);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 2) {
+        // H-DFTs: per group of four rows (row pairs 2g, 2g+1), 3xTF32 into the X blocks;
+        // a second issuing thread, so the row DFTs never queue behind these waits
+        if (elect_one()) {
             constexpr uint32_t idesc2 = idesc_tf32(32);
-            bool ok = true;
-            // Event loop: issue the next row pair's row DFT and the next group's H-DFT
-            // (row pairs 2g, 2g+1) each as soon as its barriers allow, never blocking
-            // on one while the other is ready, so every drain group stays busy.
             const int ngroups = total / 2;
-            int it = 0;   // next row pair
-            int gh = 0;   // next H-DFT group
-            uint32_t ns = 32;
-            uint32_t idle = 0;
-            uint64_t t0 = 0;
-            while (gh < ngroups) {
-                bool progress = false;
-                if (it < total) {
-                    const int s = it % F::kStages;
-                    const uint32_t ph = (it / F::kStages) & 1;
-                    const int a = it % F::kD1Stages;
-                    const uint32_t aph = (it / F::kD1Stages) & 1;
-                    if (mbar_test(&d1Empty[a], aph ^ 1) && mbar_test(&full[s], ph)) {
-                        tc_fence_after();
-                        const uint32_t aBase = smem_u32(sA + s * F::kStageBytes);
-                        const uint32_t d = tmem_base + a * 128;
-                        const uint32_t bBase = smem_u32(sB);
-#pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            mma_i8(d, umma_desc_mn64(aBase + kk * 2048, F::kTile, 512),
-                                   umma_desc(bBase + kk * 32, 128), idesc1, kk > 0 ? 1u : 0u);
-                        mma_commit(&empty[s]);
-                        mma_commit(&d1Full[a]);
-                        ++it;
-                        progress = true;
-                    }
-                }
-                if (2 * gh + 1 < it) {
-                    const bool first = (gh % groups_per_unit) == 0;
-                    if (mbar_test(&a2Ready[gh & 1], (gh >> 1) & 1) &&
-                        (!first || mbar_test(xEmpty, ((gh / groups_per_unit) & 1) ^ 1))) {
-                        tc_fence_after();
-                        const uint32_t ahi = smem_u32(sA2) + (gh & 1) * 2 * F::kA2Bytes;
-                        const uint32_t alo = ahi + F::kA2Bytes;
-                        const uint32_t bhi = smem_u32(sB2) + (gh & 1) * 2 * F::kB2Bytes;
-                        const uint32_t blo = bhi + F::kB2Bytes;
-#pragma unroll
-                        for (int mb = 0; mb < F::kMBlocks; ++mb) {
-                            const uint32_t d = tmem_base + F::x_col(mb);
-                            const uint32_t ao = mb * F::kA2Block;
-                            mma_tf32(d, umma_desc(ahi + ao, 32), umma_desc(bhi, 32), idesc2, first ? 0u : 1u);
-                            mma_tf32(d, umma_desc(alo + ao, 32), umma_desc(bhi, 32), idesc2, 1u);
-                            mma_tf32(d, umma_desc(ahi + ao, 32), umma_desc(blo, 32), idesc2, 1u);
-                        }
-                        mma_commit(&a2Free[gh & 1]);
-                        if ((gh % groups_per_unit) == groups_per_unit - 1) mma_commit(xFull);
-                        ++gh;
-                        progress = true;
-                    }
-                }
-                if (progress) {
-                    ns = 32;
-                    idle = 0;
-                    continue;
-                }
-                if (idle == 0) t0 = global_ns();
-                __nanosleep(ns);
-                ns = ns * 2 < 128 ? ns * 2 : 128;
-                if ((++idle & 7u) == 0u && (*sAbort || global_ns() - t0 > kWaitNs)) {
-                    atomicOr(p.err, it < total ? kErrWaitAccFree : kErrWaitDrain);
+            bool ok = true;
+            for (int gh = 0; gh < ngroups; ++gh) {
+                const bool first = (gh % groups_per_unit) == 0;
+                if (!mbar_wait_backoff(&a2Ready[gh & 1], (gh >> 1) & 1, sAbort, 128) ||
+                    (first && !mbar_wait_backoff(xEmpty, ((gh / groups_per_unit) & 1) ^ 1, sAbort, 128))) {
+                    *sAbort = 1;
+                    atomicOr(p.err, kErrWaitDrain);
                     ok = false;
                     break;
                 }
+                tc_fence_after();
+                const uint32_t ahi = smem_u32(sA2) + (gh & 1) * 2 * F::kA2Bytes;
+                const uint32_t alo = ahi + F::kA2Bytes;
+                const uint32_t bhi = smem_u32(sB2) + (gh & 1) * 2 * F::kB2Bytes;
+                const uint32_t blo = bhi + F::kB2Bytes;
+#pragma unroll
+                for (int mb = 0; mb < F::kMBlocks; ++mb) {
+                    const uint32_t d = tmem_base + F::x_col(mb);
+                    const uint32_t ao = mb * F::kA2Block;
+                    mma_tf32(d, umma_desc(ahi + ao, 32), umma_desc(bhi, 32), idesc2, first ? 0u : 1u);
+                    mma_tf32(d, umma_desc(alo + ao, 32), umma_desc(bhi, 32), idesc2, 1u);
+                    mma_tf32(d, umma_desc(ahi + ao, 32), umma_desc(blo, 32), idesc2, 1u);
+                }
+                mma_commit(&a2Free[gh & 1]);
+                if ((gh % groups_per_unit) == groups_per_unit - 1) mma_commit(xFull);
             }
-            if (!ok) *sAbort = 1;
             if (ok && total > 0) mbar_wait_backoff(xFull, (my_units - 1) & 1, sAbort, 1024);
         }
         __syncwarp();
