@@ -23,6 +23,7 @@
 
 #include <cstdint>
 #include <type_traits>
+#include <utility>
 
 #include "fno2d.h"
 #include "nfx_internal.h"
@@ -84,6 +85,8 @@ __global__ void __launch_bounds__(256) lift_kernel(const float* __restrict__ x, 
     constexpr int nu = linear_unfused_len(IN);
     const float magic_zp = kMagic + static_cast<float>(zp);
     const float zpf = static_cast<float>(zp);
+    grid_dep_wait();   // x and the codes buffer may still be in use by the previous kernel
+    grid_dep_launch();
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t m = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; m < M; m += stride) {
         float xv[IN];
@@ -356,6 +359,9 @@ __global__ void __launch_bounds__(kMixTcThreads) spec_mix_tc_kernel(const __grid
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *sTmem;
+    // the prologue above touched only this CTA's state and read-only tables
+    grid_dep_wait();
+    grid_dep_launch();
     constexpr uint32_t idesc = idesc_tf32(128);
     bool ok = true;
     int issued = 0;   // TMA chunk loads issued
@@ -1297,6 +1303,9 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
         tc_fence_after();
     }
     const uint32_t tmem_base = *sTmem;
+    // the prologue above touched only this CTA's state and read-only tables
+    grid_dep_wait();
+    grid_dep_launch();
 
     if (warp == 0) {
         if (elect_one()) {
@@ -1705,6 +1714,9 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
         tc_fence_after();
     }
     const uint32_t tmem_base = *sTmem;
+    // the prologue above touched only this CTA's state and read-only tables
+    grid_dep_wait();
+    grid_dep_launch();
 
     if (warp == 0) {
         if (elect_one()) {
@@ -2015,6 +2027,9 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
         tc_fence_after();
     }
     const uint32_t tmem_base = *sTmem;
+    // the prologue above touched only this CTA's state and read-only tables
+    grid_dep_wait();
+    grid_dep_launch();
 
     if (warp == 0) {
         if (elect_one()) {
@@ -2283,6 +2298,23 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
     }
 }
 
+// Launch with programmatic stream serialization (see grid_dep_wait in sm100.cuh).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <typename Kern>
 cudaError_t set_smem(Kern k, int bytes) {
     return set_max_dynamic_smem(reinterpret_cast<const void*>(k), bytes);
@@ -2300,14 +2332,15 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
         switch (pl.in_ch) {
 #define NFX_LIFT(n)                                                                            \
     case n:                                                                                    \
-        lift_kernel<C, n><<<grid, 256, 0, st>>>(pl.x, M, pl.lift_cols, pl.lift_s,               \
-                                                pl.lift_zp, pl.lift_inv_s, pl.codes[0]);        \
+        e = launch_pdl(lift_kernel<C, n>, dim3(grid), dim3(256), 0, st, pl.x, M, pl.lift_cols,   \
+                       pl.lift_s, pl.lift_zp, pl.lift_inv_s, pl.codes[0]);                       \
         break;
             NFX_LIFT(1) NFX_LIFT(2) NFX_LIFT(3) NFX_LIFT(4) NFX_LIFT(5) NFX_LIFT(6) NFX_LIFT(7)
             NFX_LIFT(8)
 #undef NFX_LIFT
             default: return cudaErrorInvalidValue;
         }
+        if (e != cudaSuccess) return e;
         if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
@@ -2329,7 +2362,8 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
                            pl.layer[i].zp_in, pl.B, pl.H, pl.HB, pl.err};
             const int units = pl.B * nHB;
             if (pl.timer) pl.timer->begin("fno2d_spec_fwd", st);
-            k<<<units < sms ? units : sms, kFwdThreads, FC::kSmemBytes, st>>>(tc, fa);
+            e = launch_pdl(k, dim3(units < sms ? units : sms), dim3(kFwdThreads), FC::kSmemBytes, st, tc, fa);
+            if (e != cudaSuccess) return e;
             if (pl.timer) pl.timer->end(st);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         } else {
@@ -2355,8 +2389,9 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
                                FM::kK * 4, FM::kChunk, FM::kK, 128))
                     return cudaErrorInvalidValue;
                 if (pl.timer) pl.timer->begin("fno2d_spec_mix", st);
-                k<<<dim3(MH * MW, (pl.B + 127) / 128), kMixTcThreads, FM::kSmemBytes, st>>>(
-                    thi, tlo, pl.xpart, nHB, pl.B, pl.Y, pl.err);
+                e = launch_pdl(k, dim3(MH * MW, (pl.B + 127) / 128), dim3(kMixTcThreads), FM::kSmemBytes, st,
+                               thi, tlo, static_cast<const float2*>(pl.xpart), nHB, pl.B, pl.Y, pl.err);
+                if (e != cudaSuccess) return e;
                 if (pl.timer) pl.timer->end(st);
                 if ((e = cudaGetLastError()) != cudaSuccess) return e;
             }
@@ -2391,7 +2426,9 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
                     return cudaErrorInvalidValue;
                 auto k = a.lut_two ? layer_tc_kernel<C, MH, MW, true> : layer_tc_kernel<C, MH, MW, false>;
                 if ((e = set_smem(k, TC::kSmemBytes)) != cudaSuccess) return e;
-                k<<<grid_l, TC::kThreads, TC::kSmemBytes, st>>>(tin, tout, a, pl.layer[i].cols);
+                e = launch_pdl(k, dim3(grid_l), dim3(TC::kThreads), TC::kSmemBytes, st, tin, tout, a,
+                               pl.layer[i].cols);
+                if (e != cudaSuccess) return e;
             } else if (pl.W == 128) {
                 using LC = LCfg<C, MH, MW, false, true>;
                 auto k = layer_kernel<C, MH, MW, false, true>;
@@ -2424,7 +2461,8 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
         a.err = pl.err;
         a.y = pl.y;
         if (pl.timer) pl.timer->begin("fno2d_proj", st);
-        k<<<grid_l, PC::kThreads, PC::kSmemBytes, st>>>(tin, a, pl.proj_cols);
+        e = launch_pdl(k, dim3(grid_l), dim3(PC::kThreads), PC::kSmemBytes, st, tin, a, pl.proj_cols);
+        if (e != cudaSuccess) return e;
         if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }

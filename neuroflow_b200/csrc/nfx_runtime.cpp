@@ -103,7 +103,7 @@ struct nfx_runtime {
     // host-buffer Run of a large batch: copies on their own streams, overlapped with
     // the compute of neighbouring batch chunks
     cudaStream_t s_h2d = nullptr, s_d2h = nullptr;
-    cudaEvent_t ev_in[4] = {}, ev_out[4] = {};
+    cudaEvent_t ev_in[8] = {}, ev_out[8] = {};
     std::vector<void*> allocs;      // weights and tables (freed at destroy)
     // FNO2d state
     nfx::Fno2dPlan plan{};
@@ -1346,7 +1346,7 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
     if (rt->stream) cudaStreamDestroy(rt->stream);
     if (rt->s_h2d) cudaStreamDestroy(rt->s_h2d);
     if (rt->s_d2h) cudaStreamDestroy(rt->s_d2h);
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 8; ++i) {
         if (rt->ev_in[i]) cudaEventDestroy(rt->ev_in[i]);
         if (rt->ev_out[i]) cudaEventDestroy(rt->ev_out[i]);
     }
@@ -1450,18 +1450,48 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
         if (!cuda_ok(rt, cudaMalloc(&rt->dy, ny * 4), "cudaMalloc output")) return NFX_INTERNAL;
         rt->dy_cap = ny;
     }
-    // Samples are independent, so a large batch runs as two or three chunks: the input
-    // copy of chunk c+1 and the output copy of chunk c-1 overlap the compute of chunk
-    // c (the copy engines of both directions and the SMs work at once; with pinned
-    // host buffers the copies are truly asynchronous).  Three chunks split the batch
-    // 1/4, 1/2, 1/4: the first and last copies, which nothing hides, stay small, and
-    // the middle chunk runs at nearly the full batch's efficiency.
+    // Samples are independent, so a large batch runs as several chunks: the input copy
+    // of chunk c+1 and the output copy of chunk c-1 overlap the compute of chunk c (the
+    // copy engines of both directions and the SMs work at once; with pinned host
+    // buffers the copies are truly asynchronous).  Nothing hides the first chunk's
+    // input copy and the last chunk's output copy, so both chunks are small; the ones
+    // between double in size (an input copy must finish within the previous chunk's
+    // compute, which takes about 2.5x as long per sample).  Chunk sizes are multiples
+    // of q = SMs / gcd(SMs, 4) samples, so that the persistent kernels' units (4 row
+    // blocks or 128 points per sample) fill whole rounds of the SMs.
     const int64_t B = x_shape[0];
-    const int nchunk = B >= 128 ? 3 : (B >= 32 ? 2 : 1);
+    int64_t nbs[8], b0s[8];
+    int nchunk = 1;
+    nbs[0] = B;
+    {
+        const int sms = nfx::device_sm_count();
+        int g = 4, a = sms > 0 ? sms : 4;
+        while (a % g) --g;  // gcd(sms, 4)
+        const int64_t q = std::max<int64_t>(8, (sms > 0 ? sms : 32) / g);
+        if (B >= 4 * q) {
+            nchunk = 0;
+            nbs[nchunk++] = q;
+            int64_t rem = B - 2 * q, step = 2 * q;
+            while (rem > 0) {
+                int64_t take = std::min(step, rem);
+                if (rem - take < q / 2 || nchunk == 6) take = rem;
+                nbs[nchunk++] = take;
+                rem -= take;
+                step *= 2;
+            }
+            nbs[nchunk++] = q;
+        } else if (B >= 32) {
+            nchunk = 2;
+            nbs[0] = B / 2;
+            nbs[1] = B - B / 2;
+        }
+        b0s[0] = 0;
+        for (int c = 1; c < nchunk; ++c) b0s[c] = b0s[c - 1] + nbs[c - 1];
+    }
     if (nchunk > 1 && !rt->s_h2d) {
         bool ok = cudaStreamCreateWithFlags(&rt->s_h2d, cudaStreamNonBlocking) == cudaSuccess &&
                   cudaStreamCreateWithFlags(&rt->s_d2h, cudaStreamNonBlocking) == cudaSuccess;
-        for (int i = 0; i < 4 && ok; ++i)
+        for (int i = 0; i < 8 && ok; ++i)
             ok = cudaEventCreateWithFlags(&rt->ev_in[i], cudaEventDisableTiming) == cudaSuccess &&
                  cudaEventCreateWithFlags(&rt->ev_out[i], cudaEventDisableTiming) == cudaSuccess;
         if (!ok) return rt_fail(rt, NFX_INTERNAL, "creating the copy streams failed");
@@ -1477,20 +1507,6 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
         return nfx_runtime_check(rt);
     }
     const size_t xs = nx / static_cast<size_t>(B), ys = ny / static_cast<size_t>(B);
-    int64_t b0s[4], nbs[4];
-    if (nchunk == 3) {
-        b0s[0] = 0;
-        b0s[1] = B / 4;
-        b0s[2] = B - B / 4;
-        nbs[0] = b0s[1];
-        nbs[1] = b0s[2] - b0s[1];
-        nbs[2] = B - b0s[2];
-    } else {
-        for (int c = 0; c < nchunk; ++c) {
-            b0s[c] = B * c / nchunk;
-            nbs[c] = B * (c + 1) / nchunk - b0s[c];
-        }
-    }
     for (int c = 0; c < nchunk; ++c) {
         const size_t off = static_cast<size_t>(b0s[c]) * xs;
         if (!cuda_ok(rt, cudaMemcpyAsync(rt->dx + off, x + off, static_cast<size_t>(nbs[c]) * xs * 4,

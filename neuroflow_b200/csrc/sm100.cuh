@@ -130,6 +130,21 @@ __device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the previous kernel in the stream still runs; it
+// touches only its own shared memory, TMEM and read-only tables until grid_dep_wait(),
+// which returns once the previous grid has completed and its memory is visible (at
+// once when there is no such dependency).  grid_dep_launch() lets the next kernel
+// launch early; its CTAs are placed as this kernel's CTAs leave the SMs.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor) -- loads without multicast only.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
