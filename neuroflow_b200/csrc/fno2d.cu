@@ -1161,8 +1161,7 @@ struct TCfg {
     static constexpr int kThreads = 32 * (kEpi0 + kEpiWarps);
     static constexpr int kABytes = 128 * C;
     static constexpr int kStages = 3;
-    static constexpr int kOnesCol = C;
-    static constexpr int kX1Col = ((C + 16 + 31) / 32) * 32;
+    static constexpr int kX1Col = C;
     static constexpr int kAccCols = kX1Col + C;
     static constexpr int kAccStages = 3;
     static constexpr int kTmemCols = pow2ceil(kAccStages * kAccCols);
@@ -1176,8 +1175,8 @@ struct TCfg {
     static_assert(C == 64, "the epilogue is laid out for width 64");
     static constexpr int up1k(int v) { return (v + 1023) / 1024 * 1024; }
     static constexpr int kOffW = 0;
-    static constexpr int kOffOnes = up1k(C * C);
-    static constexpr int kOffA = kOffOnes + 1024;
+    static constexpr int kOffZ = up1k(C * C);                           // [3][C][32] int8
+    static constexpr int kOffA = kOffZ + up1k(3 * C * 32);
     static constexpr int kOffStage = kOffA + kStages * kABytes;        // 16 warps x 1 KB
     static constexpr int kOffY = kOffStage + kEpiWarps * 2 * 512;
     static constexpr int kYBytes = MH * MW * C * 8;
@@ -1224,7 +1223,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sW = smem + L::kOffW;
-    uint8_t* sOnes = smem + L::kOffOnes;
+    uint8_t* sZ = smem + L::kOffZ;
     uint8_t* sA = smem + L::kOffA;
     uint8_t* sStage = smem + L::kOffStage;
     float2* sY = reinterpret_cast<float2*>(smem + L::kOffY);
@@ -1262,10 +1261,9 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
             const uint4 v = *reinterpret_cast<const uint4*>(p.Wq + o * C + c * 16);
             *reinterpret_cast<uint4*>(sW + swz_offset(o * C + c * 16, C)) = v;
         }
-        for (int idx = threadIdx.x; idx < 1024 / 16; idx += L::kThreads) {
-            const uint32_t one = (idx * 16 < C) ? 0x01010101u : 0u;  // row 0 = ones
-            *reinterpret_cast<uint4*>(sOnes + idx * 16) = make_uint4(one, one, one, one);
-        }
+        // Z blocks: one value per row, so the 32-byte swizzle leaves them unchanged
+        for (int idx = threadIdx.x; idx < 3 * C * 32 / 16; idx += L::kThreads)
+            reinterpret_cast<uint4*>(sZ)[idx] = reinterpret_cast<const uint4*>(p.zrows)[idx];
         for (int i = threadIdx.x; i < p.lut_cells; i += L::kThreads) sLut[i] = p.code_lut[i];
         for (int o = threadIdx.x; o < C; o += L::kThreads)
             sCol[o] = cols.v[o];
@@ -1357,9 +1355,10 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                 for (int kk = 0; kk < C / 32; ++kk) {
                     const uint64_t ad = umma_desc(aBase + kk * 32, C);
                     const uint64_t wd = umma_desc(smem_u32(sW) + kk * 32, C);
-                    const uint64_t od = umma_desc(smem_u32(sOnes) + kk * 32, C);
                     mma_i8(d, ad, wd, idesc_i8(C), kk > 0 ? 1u : 0u);
-                    mma_i8(d + L::kOnesCol, ad, od, idesc_i8(16), kk > 0 ? 1u : 0u);
+                    // + sum_k a_k z_q: the same 32-column Z block serves both K halves
+                    for (int q = 0; q < p.nz; ++q)
+                        mma_i8(d, ad, umma_desc(smem_u32(sZ) + q * C * 32, 32), idesc_i8(C), 1u);
                 }
                 {
                     const uint32_t dx = d + L::kX1Col;
@@ -1480,7 +1479,6 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
         const int quad = warp & 3;
         const int grp = ew >> 3;                 // two groups take turns over the tiles
         const int cw = ((ew >> 2) & 1) * 32;     // this warp's columns cw .. cw + 31
-        const int kzp = C * p.zp_in;
         const float s_out = p.fq_out.scale, inv_out = p.fq_out.inv_scale;
         const float zpo = static_cast<float>(p.fq_out.zp);
         const float klo = -128.0f - zpo, khi = 127.0f - zpo;
@@ -1504,12 +1502,10 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
 #pragma unroll 1
             for (int ch = 0; ch < 2; ++ch) {
             const int c0 = cw + 16 * ch;
-            uint32_t raw[16], x1r[16], sum_u;
+            uint32_t raw[16], x1r[16], none = 0;
             tmem_ld16_async(tbase + c0, raw);
             tmem_ld16_async(tbase + L::kX1Col + c0, x1r);
-            tmem_ld1(tbase + L::kOnesCol, sum_u);
-            tmem_wait_ld_33(raw, x1r, sum_u);
-            const int m2s = kzp - 2 * static_cast<int>(sum_u);
+            tmem_wait_ld_33(raw, x1r, none);
             // Per element: dequantise + bias, the fast fake-quant offset k (x2 = k s), z =
             // x1 + x2 and the next code from the table cell (breakpoint t, codes below /
             // from t), inserted into the packed word with one byte permute.
@@ -1521,7 +1517,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const float4 cp = cols.v[c0 + j];  // constant cache, uniform
-                const int vint = static_cast<int>(raw[j]) + __float_as_int(cp.y) * m2s + __float_as_int(cp.z);
+                const int vint = static_cast<int>(raw[j]) + __float_as_int(cp.z);
                 const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
                 const float r = __fmul_rn(v, inv_out);
                 const float k = rintf(r);
@@ -1574,7 +1570,7 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
 #pragma unroll
                     for (int jj = 0; jj < 4; ++jj) {
                         const float4 cp = sCol[c0 + 4 * w4 + jj];
-                        const int vint = static_cast<int>(rj[jj]) + __float_as_int(cp.y) * m2s + __float_as_int(cp.z);
+                        const int vint = static_cast<int>(rj[jj]) + __float_as_int(cp.z);
                         const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
                         const float r = __fmul_rn(v, inv_out);
                         if (fabsf(__fsub_rn(r, rintf(r))) < kFastRoundLimit) continue;

@@ -17,6 +17,11 @@ struct LayerArgs {
     const int32_t* zp_w;
     const int32_t* sum_w;
     const float* bias;
+    // -2 zp_w split into nz int8 parts, each as a (C rows, 32 columns) K-major block of
+    // one repeated value per row: the layer's MMA adds A x Z_p, so the accumulator holds
+    // sum_k a_k (w_k - 2 zp_w) and the epilogue needs only a per-column constant
+    const int8_t* zrows;  // [3][C][32]
+    int nz;
     float s_in;       // input activation qparams (the layer-input key)
     int zp_in;
     FqParam fq_out;   // locs.i.output (layer) / proj_q.output (projection)
@@ -62,11 +67,13 @@ struct SpecFwdArgs {
 };
 
 // Per-output-channel constants of a local layer's epilogue, passed by value so that
-// the kernel reads them through the constant cache (one uniform 16-byte load per
-// element, off the shared-memory pipe):
-//   v = a[o] * float(raw + zp[o] * (K zp_in - 2 sum_a) + nk[o]) + b[o]
-// with a = scale_w * s_in, nk = -zp_in * sum_w (int8_gemm.cpp:574-577, fno.cpp:541-548),
-// stored as float4 {a, bits(zp), bits(nk), b}.
+// the kernel reads them through the constant cache (off the shared-memory pipe).  The
+// reference's integer (int8_gemm.cpp:574-577, fno.cpp:541-548) is
+//   acc - zp_w sum_a - zp_in sum_w + K zp_w zp_in,  acc = sum_k a_k (w_k - zp_w),
+// i.e. sum_k a_k (w_k - 2 zp_w) + nk' with nk' = zp_in (K zp_w - sum_w); the MMA
+// produces the first term (the Z blocks of LayerArgs), so
+//   v = a[o] * float(raw' + nk'[o]) + b[o],  a = scale_w * s_in,
+// stored as float4 {a, bits(zp_w), bits(nk'), b}.
 constexpr int kFno2dColMax = 64;
 struct LayerCols {
     float4 v[kFno2dColMax];

@@ -343,6 +343,24 @@ void fno2d_enable_int8(nfx_runtime* rt) {
         a.zp_w = upload(rt, pc->second.zero_points.data(), static_cast<size_t>(c.width));
         a.sum_w = upload(rt, sum_w.data(), sum_w.size());
         if (!a.Wq || !a.scale_w || !a.zp_w || !a.sum_w) return;
+        {
+            // -2 zp_w (in [-254, 256]) as up to three int8 parts per output channel
+            std::vector<int8_t> zr(static_cast<size_t>(3) * c.width * 32, 0);
+            a.nz = 2;
+            for (int o = 0; o < c.width; ++o) {
+                const int v = -2 * pc->second.zero_points[o];
+                const int z0 = std::min(127, std::max(-128, v));
+                const int z1 = std::min(127, std::max(-128, v - z0));
+                const int z2 = v - z0 - z1;
+                if (z2 != 0) a.nz = 3;
+                const int zp3[3] = {z0, z1, z2};
+                for (int q = 0; q < 3; ++q)
+                    for (int k = 0; k < 32; ++k)
+                        zr[(static_cast<size_t>(q) * c.width + o) * 32 + k] = static_cast<int8_t>(zp3[q]);
+            }
+            a.zrows = upload(rt, zr.data(), zr.size());
+            if (!a.zrows) return;
+        }
         const nfx::QP in = m.activation_qparams.at(act_key(i));
         a.s_in = in.scale;
         a.zp_in = in.zero_point;
@@ -381,7 +399,7 @@ void fno2d_enable_int8(nfx_runtime* rt) {
             const std::vector<float>& bias = m.weights.at("locs." + std::to_string(i) + ".bias").data;
             for (int o = 0; o < c.width && o < nfx::kFno2dColMax; ++o) {
                 const int32_t zp = pc->second.zero_points[o];
-                const int32_t nk = -(in.zero_point * sum_w[o]);
+                const int32_t nk = in.zero_point * (c.width * zp - sum_w[o]);
                 float zpf, nkf;
                 std::memcpy(&zpf, &zp, 4);
                 std::memcpy(&nkf, &nk, 4);
