@@ -1141,10 +1141,10 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16
 //   warp 0       TMA producer of the layer-input codes (ring of kStages tiles)
 //   warp 1       MMA issuer and TMEM owner: per tile the int8 local GEMM, the ones
 //                block (sum_a) and the 3xTF32 inverse W-transform x1 = Binv T
-//   warps 2-5    T builders (one per SM sub-partition): the H-direction inverse
+//   warps 2-7    T builders: the H-direction inverse
 //                transform T[o][kw] of the tile's rows from the cached spectrum Y,
 //                split into tf32 hi/lo halves, four T buffers
-//   warps 6-21   epilogue: two groups of 8 warps take turns over the tiles; in a
+//   warps 8-23   epilogue: two groups of 8 warps take turns over the tiles; in a
 //                group, 2 warps per TMEM lane quadrant, 32 columns each.  Per
 //                element: dequantise + bias (constant-bank operands), the fast
 //                fake-quant offset k, z = x1 + k s, the next code from the table.
@@ -1155,7 +1155,7 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16
 template <int C, int MH, int MW>
 struct TCfg {
     static constexpr int kTBuild0 = 2;                  // first T-builder warp
-    static constexpr int kTBuildWarps = 4;                 // one per SM sub-partition
+    static constexpr int kTBuildWarps = 6;
     static constexpr int kEpi0 = kTBuild0 + kTBuildWarps;  // quadrant = warp & 3
     static constexpr int kEpiWarps = 16;
     static constexpr int kThreads = 32 * (kEpi0 + kEpiWarps);
