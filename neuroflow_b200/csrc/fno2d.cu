@@ -2061,8 +2061,8 @@ spec_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmCodes, const SpecFwdAr
                 const uint32_t ph = (it / F::kStages) & 1;
                 const int a = it % F::kD1Stages;
                 const uint32_t aph = (it / F::kD1Stages) & 1;
-                if (!mbar_wait_backoff(&d1Empty[a], aph ^ 1, sAbort, 128) ||
-                    !mbar_wait_backoff(&full[s], ph, sAbort, 128)) {
+                if (!mbar_wait(&d1Empty[a], aph ^ 1, sAbort) ||
+                    !mbar_wait(&full[s], ph, sAbort)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitAccFree);
                     break;
