@@ -1649,6 +1649,12 @@ struct PCfg {
     static_assert(kSmemBytes <= 227 * 1024, "smem");
 };
 
+// The activation-table value of v through the exact fake-quant division (the rare
+// path of proj_kernel's fast code test), out of line.
+__device__ __noinline__ float proj_exact_g(float v, float s_out, float zpo, const float* sAct) {
+    return sAct[static_cast<int>(fq_code(v, s_out, zpo)) + 128];
+}
+
 template <int C, int OUT>
 __global__ void __launch_bounds__(PCfg<C>::kThreads, 1)
 proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
@@ -1805,37 +1811,34 @@ proj_kernel(const __grid_constant__ CUtensorMap tmIn, const LayerArgs p,
                 uint32_t (&cur)[16] = raw[c & 1];
                 if (c + 1 < C / 16) tmem_ld16_async(tbase + (c + 1) * 16, raw[(c + 1) & 1]);
                 float g[16];
-                uint32_t bad = 0;
+                float vv[16];
+                float dmax = 0.0f;   // largest |r - rint(r)| of the chunk (v is finite)
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const float4 cp = cols.v[c * 16 + j];  // constant-bank operands
                     const int vint = static_cast<int>(cur[j]) + __float_as_int(cp.y) * rconst +
                                      __float_as_int(cp.z);
                     const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
+                    vv[j] = v;
                     if (use_act) {
-                        bool b;
-                        const float tc = fast_code_t(v, inv_out, magic_zp, b);
-                        bad |= static_cast<uint32_t>(b) << j;
+                        const float r = __fmul_rn(v, inv_out);
+                        const float t = __fadd_rn(r, magic_zp);
+                        dmax = fmaxf(dmax, fabsf(__fsub_rn(r, __fsub_rn(t, magic_zp))));
+                        const float tc = fminf(fmaxf(t, kMagic - 128.0f), kMagic + 127.0f);
                         g[j] = sAct[__float_as_int(tc) - (0x4B400000 - 128)];
                     } else {
                         g[j] = activation(apply_fq(v, p.fq_out), p.act);
                     }
                 }
-                while (bad) {  // rare: exact division for quotients next to a half-integer
-                    const int j = __ffs(bad) - 1;
-                    bad &= bad - 1;
-                    const float4 cp = sCol[c * 16 + j];
-                    uint32_t rj = 0;
+                if (use_act && !(dmax < kFastRoundLimit)) {
+                    // rare: the chunk holds a quotient next to a half-integer; those
+                    // elements take the exact division (out of line)
 #pragma unroll
-                    for (int k = 0; k < 16; ++k)
-                        if (k == j) rj = cur[k];
-                    const int vint = static_cast<int>(rj) + __float_as_int(cp.y) * rconst -
-                                     __float_as_int(cp.z);
-                    const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
-                    const float gj = sAct[static_cast<int>(fq_code(v, s_out, zpo)) + 128];
-#pragma unroll
-                    for (int k = 0; k < 16; ++k)
-                        if (k == j) g[k] = gj;
+                    for (int j = 0; j < 16; ++j) {
+                        const float r = __fmul_rn(vv[j], inv_out);
+                        if (!(fabsf(__fsub_rn(r, rintf(r))) < kFastRoundLimit))
+                            g[j] = proj_exact_g(vv[j], s_out, zpo, sAct);
+                    }
                 }
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
