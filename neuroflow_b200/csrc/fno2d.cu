@@ -189,113 +189,6 @@ __global__ void __launch_bounds__(C * MW) spec_fwd_kernel(const int8_t* __restri
 }
 
 // ---------------------------------------------------------------------------
-// spec_mix: grid (MH*MW, ceil(B / 32)), 256 threads, dynamic shared memory
-// kMixSmem.  Y[b][m][o] = sum_i X[b][m][i] W[m][i][o] (fno.cpp:740-764), with X the
-// sum of the row-block partials (fixed order) and W re-laid as [m][i][o].  A block
-// holds one mode's weights and 32 samples' spectra; each thread accumulates 2 samples
-// x 4 outputs, so one pair of shared loads feeds 8 complex products.
-// ---------------------------------------------------------------------------
-constexpr int kMixSamples = 32;
-template <int C>
-constexpr int mix_smem_bytes() { return (C * C + C * (kMixSamples + 1)) * 8; }
-
-template <int C, int MH, int MW>
-__global__ void __launch_bounds__(256) spec_mix_kernel(const float2* __restrict__ xpart, int nHB,
-                                                       int B, const float2* __restrict__ wspec,
-                                                       float2* __restrict__ Y) {
-    constexpr int M = MH * MW;
-    constexpr int SB = kMixSamples;
-    static_assert(C == 64, "thread layout is for width 64");
-    extern __shared__ float2 smix[];
-    float2* sw = smix;               // [i][o]
-    float2* sx = smix + C * C;       // [i][SB + 1]
-    const int m = blockIdx.x;
-    const int b0 = blockIdx.y * SB;
-    const int nb = min(SB, B - b0);
-    {
-        const float4* src = reinterpret_cast<const float4*>(wspec + static_cast<int64_t>(m) * C * C);
-        float4* dst = reinterpret_cast<float4*>(sw);
-        for (int i = threadIdx.x; i < C * C / 2; i += 256) dst[i] = src[i];
-    }
-    // all partial loads of a thread are issued before the first sum
-    constexpr int kPerThr = SB * C / 256;
-    float2 v[kPerThr];
-#pragma unroll
-    for (int t = 0; t < kPerThr; ++t) v[t] = make_float2(0.f, 0.f);
-    if (nHB == 4) {
-        float2 u[kPerThr][4];
-#pragma unroll
-        for (int t = 0; t < kPerThr; ++t) {
-            const int idx = threadIdx.x + 256 * t;
-            const int sl = idx / C, i = idx % C;
-            const float2* q = xpart + (static_cast<int64_t>(b0 + (sl < nb ? sl : 0)) * nHB * M + m) * C + i;
-#pragma unroll
-            for (int hb = 0; hb < 4; ++hb) u[t][hb] = __ldg(q + static_cast<int64_t>(hb) * M * C);
-        }
-#pragma unroll
-        for (int t = 0; t < kPerThr; ++t) {
-            const int sl = (threadIdx.x + 256 * t) / C;
-            if (sl < nb) {
-#pragma unroll
-                for (int hb = 0; hb < 4; ++hb) {
-                    v[t].x += u[t][hb].x;
-                    v[t].y += u[t][hb].y;
-                }
-            }
-        }
-    } else {
-        for (int t = 0; t < kPerThr; ++t) {
-            const int idx = threadIdx.x + 256 * t;
-            const int sl = idx / C, i = idx % C;
-            if (sl < nb) {
-                const float2* q = xpart + (static_cast<int64_t>(b0 + sl) * nHB * M + m) * C + i;
-                for (int hb = 0; hb < nHB; ++hb) {
-                    const float2 w = q[static_cast<int64_t>(hb) * M * C];
-                    v[t].x += w.x;
-                    v[t].y += w.y;
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int t = 0; t < kPerThr; ++t) {
-        const int idx = threadIdx.x + 256 * t;
-        sx[(idx % C) * (SB + 1) + idx / C] = v[t];
-    }
-    __syncthreads();
-    const int og = threadIdx.x & 15, sg = threadIdx.x >> 4;  // outputs og + 16k, samples sg + 16j
-    float yr[2][4], yi[2][4];
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) yr[j][k] = yi[j][k] = 0.f;
-#pragma unroll 4
-    for (int i = 0; i < C; ++i) {
-        float2 xv[2], wv[4];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) xv[j] = sx[i * (SB + 1) + sg + 16 * j];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) wv[k] = sw[i * C + og + 16 * k];
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                yr[j][k] = fmaf(xv[j].x, wv[k].x, fmaf(-xv[j].y, wv[k].y, yr[j][k]));
-                yi[j][k] = fmaf(xv[j].x, wv[k].y, fmaf(xv[j].y, wv[k].x, yi[j][k]));
-            }
-    }
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const int sl = sg + 16 * j;
-        if (sl < nb) {
-            float2* dst = Y + (static_cast<int64_t>(b0 + sl) * M + m) * C;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) dst[og + 16 * k] = make_float2(yr[j][k], yi[j][k]);
-        }
-    }
-}
-
-// ---------------------------------------------------------------------------
 // spec_mix_tc: the per-mode contraction on tensor cores (C == 64).  For mode m and a
 // tile of 128 samples, with x the sum of the row-block partials (fixed order) as the
 // real row [re, im] per input channel, y = x Wr where Wr is the real (2C x 2C) form of
@@ -2375,32 +2268,22 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
             if (pl.timer) pl.timer->end(st);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
-        if constexpr (C == 64) {
-            if (pl.layer[i].wmix_hi != nullptr) {
-                using FM = MixCfg<C>;
-                auto k = spec_mix_tc_kernel<C, MH, MW>;
-                if ((e = set_smem(k, FM::kSmemBytes)) != cudaSuccess) return e;
-                CUtensorMap thi, tlo;
-                const uint64_t rows = static_cast<uint64_t>(MH) * MW * FM::kK;
-                if (!encode_2d(&thi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pl.layer[i].wmix_hi, FM::kK, rows,
-                               FM::kK * 4, FM::kChunk, FM::kK, 128) ||
-                    !encode_2d(&tlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pl.layer[i].wmix_lo, FM::kK, rows,
-                               FM::kK * 4, FM::kChunk, FM::kK, 128))
-                    return cudaErrorInvalidValue;
-                if (pl.timer) pl.timer->begin("fno2d_spec_mix", st);
-                e = launch_pdl(k, dim3(MH * MW, (pl.B + 127) / 128), dim3(kMixTcThreads), FM::kSmemBytes, st,
-                               thi, tlo, static_cast<const float2*>(pl.xpart), nHB, pl.B, pl.Y, pl.err);
-                if (e != cudaSuccess) return e;
-                if (pl.timer) pl.timer->end(st);
-                if ((e = cudaGetLastError()) != cudaSuccess) return e;
-            }
-        }
-        if (C != 64 || pl.layer[i].wmix_hi == nullptr) {
-            auto k = spec_mix_kernel<C, MH, MW>;
-            if ((e = set_smem(k, mix_smem_bytes<C>())) != cudaSuccess) return e;
+        {
+            if (pl.layer[i].wmix_hi == nullptr || pl.layer[i].wmix_lo == nullptr) return cudaErrorInvalidValue;
+            using FM = MixCfg<C>;
+            auto k = spec_mix_tc_kernel<C, MH, MW>;
+            if ((e = set_smem(k, FM::kSmemBytes)) != cudaSuccess) return e;
+            CUtensorMap thi, tlo;
+            const uint64_t rows = static_cast<uint64_t>(MH) * MW * FM::kK;
+            if (!encode_2d(&thi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pl.layer[i].wmix_hi, FM::kK, rows,
+                           FM::kK * 4, FM::kChunk, FM::kK, 128) ||
+                !encode_2d(&tlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pl.layer[i].wmix_lo, FM::kK, rows,
+                           FM::kK * 4, FM::kChunk, FM::kK, 128))
+                return cudaErrorInvalidValue;
             if (pl.timer) pl.timer->begin("fno2d_spec_mix", st);
-            k<<<dim3(MH * MW, (pl.B + kMixSamples - 1) / kMixSamples), 256, mix_smem_bytes<C>(), st>>>(
-                pl.xpart, nHB, pl.B, pl.layer[i].wspec, pl.Y);
+            e = launch_pdl(k, dim3(MH * MW, (pl.B + 127) / 128), dim3(kMixTcThreads), FM::kSmemBytes, st,
+                           thi, tlo, static_cast<const float2*>(pl.xpart), nHB, pl.B, pl.Y, pl.err);
+            if (e != cudaSuccess) return e;
             if (pl.timer) pl.timer->end(st);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
