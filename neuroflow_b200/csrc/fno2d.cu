@@ -9,7 +9,7 @@
 //              (rows: W-axis DFT restricted to kw < MW; then the H-axis DFT
 //              restricted to kh < MH, accumulated over the block's rows).
 //   spec_mix   sum of the partials, then the per-mode complex (in x out) contraction
-//              (fno.cpp:740-764) -> Y (b, kh, kw, o).
+//              (fno.cpp:740-764) on tensor cores (3xTF32) -> Y (b, kh, kw, o).
 //   layer      tcgen05 kind::i8 GEMM of the local 1x1 layer (codes x locs.i codes),
 //              fused with: inverse truncated 2D transform of Y evaluated at the
 //              tile's points (x1), the LinearForwardBatched dequant epilogue + bias,
