@@ -14,7 +14,7 @@
 //              fused with: inverse truncated 2D transform of Y evaluated at the
 //              tile's points (x1), the LinearForwardBatched dequant epilogue + bias,
 //              locs.i.output fake-quant (x2), x1 + x2, activation, and quantisation
-//              to the next layer's codes (TMA store).
+//              to the next layer's codes (16-byte stores; TMA stores in the W != 128 kernel).
 //
 // lift (K = in_ch, CUDA cores) and the projection (tcgen05 GEMM for proj_q, the
 // out_ch-wide proj_out dot product in the epilogue) close the network.
@@ -1040,7 +1040,8 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16
 //   warps 8-23   epilogue: two groups of 8 warps take turns over the tiles; in a
 //                group, 2 warps per TMEM lane quadrant, 32 columns each.  Per
 //                element: dequantise + bias (constant-bank operands), the fast
-//                fake-quant offset k, z = x1 + k s, the next code from the table.
+//                fake-quant offset k, z = x1 + k s, the next code from the table;
+//                16 packed codes per thread and chunk go out as one 16-byte store.
 // Three accumulator stages: the MMA runs up to two tiles ahead of the epilogue
 // groups, and a group finishing tile t - 2 implies (in-order MMA completion) that the
 // stage of tile t has completed the phase of tile t - 3, so parity waits stay exact.
@@ -1070,8 +1071,7 @@ struct TCfg {
     static constexpr int kOffW = 0;
     static constexpr int kOffZ = up1k(C * C);                           // [3][C][32] int8
     static constexpr int kOffA = kOffZ + up1k(3 * C * 32);
-    static constexpr int kOffStage = kOffA + kStages * kABytes;        // 16 warps x 1 KB
-    static constexpr int kOffY = kOffStage + kEpiWarps * 2 * 512;
+    static constexpr int kOffY = kOffA + kStages * kABytes;
     static constexpr int kYBytes = MH * MW * C * 8;
     static constexpr int kOffBinv = up1k(kOffY + kYBytes);
     static constexpr int kBinvBytes = 2 * kKb * kBinvBlk;               // hi, lo
@@ -1110,7 +1110,7 @@ __device__ __forceinline__ int2 lut_cell_sat(float z, const int2* lut, float alp
 
 template <int C, int MH, int MW, bool TWO>
 __global__ void __launch_bounds__(TCfg<C, MH, MW>::kThreads, 1)
-layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant__ CUtensorMap tmOut,
+layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn,
                 const LayerArgs p, const __grid_constant__ LayerCols cols) {
     using L = TCfg<C, MH, MW>;
     extern __shared__ uint8_t smem_raw[];
@@ -1118,7 +1118,6 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
     uint8_t* sW = smem + L::kOffW;
     uint8_t* sZ = smem + L::kOffZ;
     uint8_t* sA = smem + L::kOffA;
-    uint8_t* sStage = smem + L::kOffStage;
     float2* sY = reinterpret_cast<float2*>(smem + L::kOffY);
     uint8_t* sBinv = smem + L::kOffBinv;
     uint8_t* sTop = smem + L::kOffTop;
@@ -1375,8 +1374,6 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
         const float s_out = p.fq_out.scale, inv_out = p.fq_out.inv_scale;
         const float zpo = static_cast<float>(p.fq_out.zp);
         const float klo = -128.0f - zpo, khi = 127.0f - zpo;
-        int nstore = 0;
-        uint8_t* buf = sStage + ew * 1024;
         for (int it = grp; t_begin + it < t_end; it += 2) {
             const int tile = t_begin + it;
             const int a = it % L::kAccStages;
@@ -1388,10 +1385,8 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
             }
             tc_fence_after();
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * L::kAccCols;
-            if (nstore > 0) {
-                if (lane == 0) tma_store_wait_read<0>();
-                __syncwarp();
-            }
+            uint4* dst = reinterpret_cast<uint4*>(p.codes_out +
+                                                  (static_cast<int64_t>(tile_row(tile)) * 128 + quad * 32 + lane) * C + cw);
 #pragma unroll 1
             for (int ch = 0; ch < 2; ++ch) {
             const int c0 = cw + 16 * ch;
@@ -1481,21 +1476,12 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const __grid_constant_
                     else packed[3] = w;
                 }
             }
-            *reinterpret_cast<uint4*>(buf + lane * 32 + ch * 16) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            dst[ch] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&accEmpty[a]);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                tma_store_2d(&tmOut, buf, cw, tile_row(tile) * 128 + quad * 32);
-                tma_store_commit();
-            }
-            ++nstore;
         }
-        if (lane == 0) tma_store_wait_all<0>();
-        __syncwarp();
     }
 
     tc_fence_before();
@@ -2306,9 +2292,10 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
                 using TC = TCfg<C, MH, MW>;
                 if (!encode_2d(&tout, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur ^ 1], C, M, C, C / 2, 32, 0))
                     return cudaErrorInvalidValue;
+                a.codes_out = pl.codes[cur ^ 1];
                 auto k = a.lut_two ? layer_tc_kernel<C, MH, MW, true> : layer_tc_kernel<C, MH, MW, false>;
                 if ((e = set_smem(k, TC::kSmemBytes)) != cudaSuccess) return e;
-                e = launch_pdl(k, dim3(grid_l), dim3(TC::kThreads), TC::kSmemBytes, st, tin, tout, a,
+                e = launch_pdl(k, dim3(grid_l), dim3(TC::kThreads), TC::kSmemBytes, st, tin, a,
                                pl.layer[i].cols);
                 if (e != cudaSuccess) return e;
             } else if (pl.W == 128) {

@@ -21,6 +21,7 @@ struct LayerArgs {
     // one repeated value per row: the layer's MMA adds A x Z_p, so the accumulator holds
     // sum_k a_k (w_k - 2 zp_w) and the epilogue needs only a per-column constant
     const int8_t* zrows;  // [3][C][32]
+    int8_t* codes_out;    // layer_tc: the (M, C) output codes
     int nz;
     float s_in;       // input activation qparams (the layer-input key)
     int zp_in;
