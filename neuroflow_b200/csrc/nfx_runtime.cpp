@@ -1472,11 +1472,11 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
     // of chunk c+1 and the output copy of chunk c-1 overlap the compute of chunk c (the
     // copy engines of both directions and the SMs work at once; with pinned host
     // buffers the copies are truly asynchronous).  Nothing hides the first chunk's
-    // input copy and the last chunk's output copy, so both chunks are small; the ones
-    // between double in size (an input copy must finish within the previous chunk's
-    // compute, which takes about 2.5x as long per sample).  Chunk sizes are multiples
-    // of q = SMs / gcd(SMs, 4) samples, so that the persistent kernels' units (4 row
-    // blocks or 128 points per sample) fill whole rounds of the SMs.
+    // input copy and the last chunk's output copy, so both chunks are small (q / 2 and
+    // q); the ones between are 2q, 4q, ... (an input copy must finish within the
+    // previous chunk's compute, which takes about 2.5x as long per sample).  With q =
+    // SMs / gcd(SMs, 4) samples the middle chunks fill whole rounds of the persistent
+    // kernels' units (4 row blocks or 128 points per sample).
     const int64_t B = x_shape[0];
     int64_t nbs[8], b0s[8];
     int nchunk = 1;
@@ -1488,8 +1488,9 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
         const int64_t q = std::max<int64_t>(8, (sms > 0 ? sms : 32) / g);
         if (B >= 4 * q) {
             nchunk = 0;
-            nbs[nchunk++] = q;
-            int64_t rem = B - 2 * q, step = 2 * q;
+            const int64_t first = (q + 1) / 2;
+            nbs[nchunk++] = first;
+            int64_t rem = B - first - q, step = 2 * q;
             while (rem > 0) {
                 int64_t take = std::min(step, rem);
                 if (rem - take < q / 2 || nchunk == 6) take = rem;

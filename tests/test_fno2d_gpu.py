@@ -129,8 +129,8 @@ def test_fno2d_int8_two_segment_code_table(tmp_path, scale, zp):
 @pytest.mark.parametrize("B", [40, 130, 160, 300])
 def test_fno2d_host_run_chunked_matches_device_run(tmp_path, B):
     """The host-buffer Run of a large batch overlaps copies and compute over batch
-    chunks (2 halves below 4 q samples, q = SMs / gcd(SMs, 4); above, q, 2q, ..., q:
-    3 chunks at 160 and 4 at 300 on 148 SMs); the result is bit-identical to one
+    chunks (2 halves below 4 q samples, q = SMs / gcd(SMs, 4); above, q / 2, 2q, ..., q:
+    4 chunks at 160 and 5 at 300 on 148 SMs); the result is bit-identical to one
     device-buffer run of the whole batch."""
     import torch
     from neuroflow_b200.runtime import InferenceRuntime
