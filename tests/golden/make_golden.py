@@ -3,7 +3,7 @@
 Run in a container that has the reference tree (read-only) and its compiled sources
 (oracle/_ref, `make -C oracle ref`):
 
-    python tests/golden/make_golden.py [/root/reference]
+    python tests/golden/make_golden.py [path of the reference checkout]
 
 What it writes (small files, committed):
   fno2d_q.nneuroir      a tiny FNO2d (width 16, 4x4 modes, 2 layers, 16x16) built by
