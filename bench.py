@@ -5,8 +5,9 @@
 
 One step = one forward pass of the FNO2d INT8 executor over a batch of 256 samples
 (128x128 grid, 3 input channels, width 64, 12x12 modes, 4 layers, out_ch 1) per GPU
-(weak scaling: every rank runs its own 256-sample batch; rank 0 gathers all outputs
-over NCCL, the only collective).  Inputs are seeded synthetic Gaussian random fields;
+(weak scaling: every rank runs its own 256-sample batch and keeps its own outputs;
+samples are independent, so the data path has no collective -- the process group
+only lines the ranks up for timing and takes the maximum of their times).  Inputs are seeded synthetic Gaussian random fields;
 weights are random-init and calibrated on a separate 32-sample batch (no dataset or
 checkpoint is available offline).  The per-step working set (268 MB of int8 codes
 per layer boundary + 50 MB of input) is larger than the 126 MB L2, so no L2 flush is
@@ -136,6 +137,25 @@ def dist_setup(n_gpus: int):
     return ws, rank, local
 
 
+def max_over_ranks(x: float, ws: int, device) -> float:
+    """The largest of the ranks' values (a time), on every rank; x itself for one rank.
+    `device` holds the one-element tensor of the reduction (a GPU for NCCL, the CPU
+    for gloo)."""
+    if ws <= 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_rate(ws: int, batch_per_rank: int, steps: int, seconds: float) -> float:
+    """Whole-job samples/s: every rank ran `steps` steps of its own batch in at most
+    `seconds` (weak scaling)."""
+    return ws * batch_per_rank * steps / seconds
+
+
 def cpu_reference(path: str, x: np.ndarray, nthreads: int, target_s: float = 8.0):
     """Reference runtime on the host cores: returns (samples/s, sample description)."""
     from oracle.cpu import Reference
@@ -243,16 +263,11 @@ def run_nfx(args, ws, rank, local):
     dy = torch.empty((B, CFG["H"], CFG["W"], CFG["out_channels"]), dtype=torch.float32,
                      device=device)
     stream = torch.cuda.Stream(device)
-    gathered = None
     if ws > 1:
         import torch.distributed as dist
-        gathered = torch.empty((ws,) + tuple(dy.shape), dtype=torch.float32, device=device)
 
     def step():
         rt.run_device(dx, dy, stream)
-        if ws > 1:
-            with torch.cuda.stream(stream):
-                dist.all_gather_into_tensor(gathered, dy)
 
     for _ in range(args.warmup):
         step()
@@ -266,7 +281,7 @@ def run_nfx(args, ws, rank, local):
     e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         # keep the GPU busy while the clock sampler starts (untimed, like the warm-up;
-        # the same count on every rank, since each step ends in a collective)
+        # the same count on every rank)
         for _ in range(args.preheat):
             step()
         if ws > 1:
@@ -284,11 +299,8 @@ def run_nfx(args, ws, rank, local):
     prof = rt.profile_read()
     rt.profile(False)
     rt.check()
-    if ws > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = ws * B * args.steps / (ms * 1e-3)
+    ms = max_over_ranks(ms, ws, device)
+    value = job_rate(ws, B, args.steps, ms * 1e-3)
 
     # end-to-end through the host-buffer API (pinned host memory)
     if args.no_e2e:
@@ -305,11 +317,8 @@ def run_nfx(args, ws, rank, local):
     for _ in range(e2e_steps):
         rt.run(xn, yn)
     e2e_s = max(time.perf_counter() - t0, 1e-9)
-    if ws > 1:
-        t = torch.tensor([e2e_s], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = ws * B * e2e_steps / e2e_s if e2e_steps else None
+    e2e_s = max_over_ranks(e2e_s, ws, device)
+    e2e = job_rate(ws, B, e2e_steps, e2e_s) if e2e_steps else None
 
     result = None
     if rank == 0:
