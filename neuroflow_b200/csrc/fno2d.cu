@@ -2201,6 +2201,8 @@ cudaError_t set_smem(Kern k, int bytes) {
 template <int C, int MH, int MW>
 cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
     cudaError_t e;
+    // the forward's launches follow each other on `st` with nothing between them
+    TimerChain chained(pl.timer);
     const int64_t M = static_cast<int64_t>(pl.B) * pl.H * pl.W;
     // lift
     {

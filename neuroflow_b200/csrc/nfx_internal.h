@@ -43,7 +43,21 @@ cudaError_t gemm_i8_launch(const GemmArgs& p, int K, int N, cudaStream_t stream)
 struct KernelTimer {
     virtual void begin(const char* name, cudaStream_t s) = 0;
     virtual void end(cudaStream_t s) = 0;
+    // chain(true): a begin() that directly follows an end() on the same stream (with
+    // no other stream operation between them) reuses that end event, one event per
+    // kernel boundary instead of two; chain(false) ends such a run of launches.
+    virtual void chain(bool on) { (void)on; }
     virtual ~KernelTimer() = default;
+};
+// Keeps a timer chained for one scope (a run of back-to-back launches).
+struct TimerChain {
+    KernelTimer* t;
+    explicit TimerChain(KernelTimer* timer) : t(timer) {
+        if (t) t->chain(true);
+    }
+    ~TimerChain() {
+        if (t) t->chain(false);
+    }
 };
 
 // Host helpers (nfx_host.cpp)

@@ -35,7 +35,11 @@ struct EventTimer : KernelTimer {
     struct Pending {
         std::string name;
         cudaEvent_t a, b;
+        bool shared_a;   // a is the previous entry's b (chained launches)
     };
+    bool chain_on = false;
+    cudaEvent_t last_end = nullptr;
+    cudaStream_t last_stream = nullptr;
     std::vector<Pending> pending;
     std::vector<cudaEvent_t> pool;
     std::vector<std::string> names;
@@ -52,12 +56,21 @@ struct EventTimer : KernelTimer {
         return e;
     }
     void begin(const char* name, cudaStream_t s) override {
-        Pending p{name, take(), take()};
-        cudaEventRecord(p.a, s);
+        const bool share = chain_on && last_end != nullptr && last_stream == s;
+        Pending p{name, share ? last_end : take(), take(), share};
+        if (!share) cudaEventRecord(p.a, s);
+        last_end = nullptr;
         pending.push_back(p);
     }
     void end(cudaStream_t s) override {
-        if (!pending.empty()) cudaEventRecord(pending.back().b, s);
+        if (pending.empty()) return;
+        cudaEventRecord(pending.back().b, s);
+        last_end = pending.back().b;
+        last_stream = s;
+    }
+    void chain(bool on) override {
+        chain_on = on;
+        last_end = nullptr;
     }
     void collect() {
         for (auto& p : pending) {
@@ -73,10 +86,11 @@ struct EventTimer : KernelTimer {
             }
             launches[i] += 1;
             total_ms[i] += ms;
-            pool.push_back(p.a);
+            if (!p.shared_a) pool.push_back(p.a);
             pool.push_back(p.b);
         }
         pending.clear();
+        last_end = nullptr;
     }
     void reset() {
         collect();
@@ -86,7 +100,7 @@ struct EventTimer : KernelTimer {
     }
     ~EventTimer() override {
         for (auto& p : pending) {
-            cudaEventDestroy(p.a);
+            if (!p.shared_a) cudaEventDestroy(p.a);
             cudaEventDestroy(p.b);
         }
         for (auto e : pool) cudaEventDestroy(e);
