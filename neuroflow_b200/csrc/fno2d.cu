@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(kMixTcThreads) spec_mix_tc_kernel(const __grid
 // tile to be one grid row (W == 128); narrower grids evaluate x1 on CUDA cores.
 // ---------------------------------------------------------------------------
 constexpr int kEpiWarp0 = 4;  // warp 0 TMA, warp 1 MMA/TMEM, epilogue warps from 4
-constexpr int kLutMaxCells = 3072;
+constexpr int kLutMaxCells = kFno2dLutCells;
 
 template <int C, int MH, int MW, bool PROJ, bool TCX>
 struct LCfg {
@@ -1079,7 +1079,7 @@ struct TCfg {
     static constexpr int kTBuf = 2 * kKb * kTBlk;                       // hi, lo of one T
     static constexpr int kTopBytes = kTBufs * kTBuf;
     static constexpr int kOffLut = kOffTop + kTopBytes;
-    static constexpr int kLutBytes = kLutMaxCells * 8;
+    static constexpr int kLutBytes = kFno2dLutCellsTc * 8;
     static constexpr int kOffCol = kOffLut + kLutBytes;                // float4 [C]
     static constexpr int kOffBars = kOffCol + C * 16;
     static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2 * kTBufs;
@@ -2276,7 +2276,7 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
         {
-            LayerArgs a = pl.layer[i].args;
+            LayerArgs a = pl.W == 128 ? pl.layer[i].args_tc : pl.layer[i].args;
             a.M = M;
             a.H = pl.H;
             a.W = pl.W;
@@ -2290,7 +2290,7 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
                            32, 0))
                 return cudaErrorInvalidValue;
             if (pl.timer) pl.timer->begin("fno2d_layer", st);
-            if (pl.W == 128 && a.lut_cells > 0 && a.lut_cells <= kLutMaxCells) {
+            if (pl.W == 128 && a.lut_cells > 0 && a.lut_cells <= kFno2dLutCellsTc) {
                 using TC = TCfg<C, MH, MW>;
                 if (!encode_2d(&tout, CU_TENSOR_MAP_DATA_TYPE_UINT8, pl.codes[cur ^ 1], C, M, C, C / 2, 32, 0))
                     return cudaErrorInvalidValue;

@@ -94,6 +94,12 @@ struct LiftCols {
     float b[kFno2dColMax];
 };
 
+// Code-table capacities (cells of 8 bytes in shared memory): the W == 128 layer
+// kernel has room for a one-segment table of up to kFno2dLutCellsTc cells; the general
+// layer kernel for up to kFno2dLutCells (two segments when one does not fit).
+constexpr int kFno2dLutCells = 3072;
+constexpr int kFno2dLutCellsTc = 5632;
+
 struct Fno2dLayerPlan {
     float s_in;
     int zp_in;
@@ -104,6 +110,7 @@ struct Fno2dLayerPlan {
     const float* wmix_hi;
     const float* wmix_lo;
     LayerArgs args;
+    LayerArgs args_tc;    // the same with the W == 128 kernel's code table
     LayerCols cols;
 };
 

@@ -389,7 +389,7 @@ void fno2d_enable_int8(nfx_runtime* rt) {
             a.code_lut = nullptr;
             a.lut_cells = 0;
             a.lut_two = 0;
-            if (nfx::build_code_lut(a.fq_out.scale, a.fq_out.zp, a.act, 3072, lut, why, true)) {
+            if (nfx::build_code_lut(a.fq_out.scale, a.fq_out.zp, a.act, nfx::kFno2dLutCells, lut, why, true)) {
                 a.code_lut = reinterpret_cast<const int2*>(upload(rt, lut.cells.data(), lut.cells.size()));
                 if (a.code_lut) {
                     a.lut_cells = static_cast<int>(lut.cells.size());
@@ -406,6 +406,35 @@ void fno2d_enable_int8(nfx_runtime* rt) {
                     a.lut_alpha1 = lut.alpha1;
                     a.lut_beta1 = lut.beta1;
                     a.lut_nm1 = lut.nm1;
+                }
+            }
+            // the W == 128 kernel's table: one segment when up to kFno2dLutCellsTc cells do
+            pl.layer[i].args_tc = a;
+            if (a.lut_two) {
+                nfx::CodeLut lut1;
+                std::string why1;
+                if (nfx::build_code_lut(a.fq_out.scale, a.fq_out.zp, a.act, nfx::kFno2dLutCellsTc, lut1,
+                                        why1, false)) {
+                    nfx::LayerArgs& t = pl.layer[i].args_tc;
+                    t.code_lut = reinterpret_cast<const int2*>(upload(rt, lut1.cells.data(), lut1.cells.size()));
+                    if (t.code_lut) {
+                        t.lut_cells = static_cast<int>(lut1.cells.size());
+                        t.lut_zlo = lut1.zlo;
+                        t.lut_inv_delta = lut1.inv_delta;
+                        t.lut_two = 0;
+                        t.lut_split = lut1.zsplit;
+                        t.lut_inv0 = lut1.inv0;
+                        t.lut_c0 = lut1.c0;
+                        t.lut_inv1 = lut1.inv1;
+                        t.lut_c1 = lut1.c1;
+                        t.lut_alpha0 = lut1.alpha0;
+                        t.lut_beta0 = lut1.beta0;
+                        t.lut_alpha1 = lut1.alpha1;
+                        t.lut_beta1 = lut1.beta1;
+                        t.lut_nm1 = lut1.nm1;
+                    } else {
+                        t = a;
+                    }
                 }
             }
             // epilogue constants (the device's former per-element shared loads)

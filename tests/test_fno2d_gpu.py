@@ -103,18 +103,21 @@ def test_fno2d_growing_batch_reuses_handle(tmp_path):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("W", [32, 128])
 @pytest.mark.parametrize("scale,zp", [(0.0014373305020853877, 1), (0.0005, 0)])
-def test_fno2d_int8_two_segment_code_table(tmp_path, scale, zp):
+def test_fno2d_int8_two_segment_code_table(tmp_path, scale, zp, W):
     """A layer output scale this small needs more uniform table cells than fit in
     shared memory; the executor then splits the z -> code table at a gap between
-    breakpoints into a coarse (GELU's negative branch) and a fine segment."""
+    breakpoints into a coarse (GELU's negative branch) and a fine segment.  The W = 128
+    kernel has room for more cells: at the first scale it takes a one-segment table of
+    about 5.2k cells, at the second the split table."""
     from neuroflow_b200.ir import PerTensor
     from neuroflow_b200.runtime import InferenceRuntime
-    m, _ = _model(tmp_path, L=3)
+    m, _ = _model(tmp_path, L=3, W=W)
     m.qparams["locs.1.output"] = PerTensor(scale, zp)
     path = os.path.join(str(tmp_path), "small_scale.nneuroir")
     ir.write(path, m)
-    x = synth.fno2d_inputs(np.random.default_rng(5), 2, 32, 32)
+    x = synth.fno2d_inputs(np.random.default_rng(5), 2, 32, W)
     want = Oracle().fno2d_forward(m, x, mode=1)
     rt = InferenceRuntime(path)
     rt.enable_int8_gemm()
