@@ -329,7 +329,7 @@ def run_nfx(args, ws, rank, local):
         per_launch_s = tot_ms / launches * 1e-3
         M = B * P
         C = CFG["width"]
-        alg = {  # algorithmic bytes per launch of each kernel (see DESIGN.md)
+        alg = {  # algorithmic bytes per launch of each kernel
             "fno2d_layer": 2 * M * C,                      # codes in + codes out
             "fno2d_spec_fwd": M * C,                       # codes in
             "fno2d_proj": M * C + 4 * M * CFG["out_channels"],

@@ -3,7 +3,7 @@
 Run in a container that has the reference tree (read-only) and its compiled sources
 (oracle/_ref, `make -C oracle ref`):
 
-    python tests/golden/make_golden.py [path of the reference checkout]
+    python tests/golden/make_golden.py <path of the reference checkout>
 
 What it writes (small files, committed):
   fno2d_q.nneuroir      a tiny FNO2d (width 16, 4x4 modes, 2 layers, 16x16) built by
@@ -42,7 +42,9 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) < 2:
+    sys.exit("usage: python tests/golden/make_golden.py <reference project root>")
+REF = sys.argv[1]
 sys.dont_write_bytecode = True  # never write into the reference tree
 sys.path.insert(0, REF)
 sys.path.insert(0, ROOT)
