@@ -107,19 +107,34 @@ int nfx_runtime_run_tokenmixer2d_device(nfx_runtime* rt, const float* x,
 /* Allocation-free variant of nfx_runtime_run_device, for callers that cannot call
  * cudaMalloc while they run inference (their device memory belongs to another
  * allocator, or allocation is forbidden or too slow on their inference path).  It
- * runs the same FNO2d INT8 kernels but keeps all scratch (activation codes, spectra,
- * transform tables, error word) in one fixed 32 MiB device array inside libnfx.so,
- * held on every GPU that loads the library until exit; a batch that needs more
- * returns NFX_INVALID_ARG (about 11 samples of 128x128 at width 64).  The first call
- * on a device looks up the array's device address (and registers the kernels'
- * shared-memory limits), so make it before any stream capture; later calls allocate
- * nothing on the device or the host.  Calls share the array: calls that overlap on
- * the GPU race and must be serialised by the caller.  x and y are device pointers;
- * the call returns after the work on `stream` has finished.  No counterpart in the
- * reference. */
+ * runs the same FNO2d INT8 kernels, with bit-identical results, but keeps all scratch
+ * (activation codes, spectra, transform tables, error word) in one fixed 32 MiB device
+ * array inside libnfx.so; a batch that needs more returns NFX_INVALID_ARG (2,465,792 B
+ * per 128x128 sample at width 64, so at most 13 such samples per call).  With CUDA's
+ * lazy module loading (the default) the 32 MiB is reserved on a device by the first
+ * call there, which looks up the array's device address and uploads the transform
+ * tables; it is then held until the process exits.  Make that first call at start-up
+ * and before any stream capture; a call whose grid differs from the previous call's on
+ * that device uploads the tables again (synchronously).  Other calls allocate nothing on
+ * the device or the host.  Calls share the array: calls that overlap on the GPU race
+ * and must be serialised by the caller.  x and y are device pointers; the call returns
+ * after the work on `stream` has finished.  No counterpart in the reference. */
 int nfx_runtime_run_device_noalloc(nfx_runtime* rt, const float* x, const int64_t* x_shape,
                                    int x_rank, float* y, const int64_t* y_shape, int y_rank,
                                    void* stream);
+
+/* Parity taps of the FNO2d INT8 executor: while `device_buffer` is set (NULL turns the
+ * taps off), every FNO2d INT8 forward on this handle also copies the int8 activation
+ * codes of each layer input -- the lift's output, then every Fourier layer's output,
+ * the last being the projection's input -- into it as n_layers + 1 consecutive
+ * (batch*h*w, width) channel-last blocks, on the launch stream after the kernel that
+ * wrote them.  A forward whose taps do not fit in `capacity_bytes` fails with
+ * NFX_INVALID_ARG.  The host-buffer Run of a large batch runs in chunks, so its taps
+ * hold the last chunk only; use nfx_runtime_run_device for whole-batch taps.  No
+ * counterpart in the reference runtime: it exposes, for layer-wise parity checks, the
+ * activations between the iterations of FNO2d::Forward's layer loop
+ * (cpp/src/fno.cpp:900-945) in their int8 form. */
+int nfx_runtime_set_code_taps(nfx_runtime* rt, int8_t* device_buffer, int64_t capacity_bytes);
 
 /* Synchronise the runtime's work and report device-side errors (bounded waits that
  * timed out inside a kernel) as NFX_INTERNAL. */

@@ -55,6 +55,8 @@ if hasattr(lib, "nfx_runtime_create"):
     lib.nfx_runtime_run_tokenmixer2d_device.restype = C.c_int
     lib.nfx_runtime_run_tokenmixer2d_device.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p,
                                                         C.c_int, _vp]
+    lib.nfx_runtime_set_code_taps.restype = C.c_int
+    lib.nfx_runtime_set_code_taps.argtypes = [_vp, _vp, C.c_int64]
     lib.nfx_runtime_check.restype = C.c_int
     lib.nfx_runtime_check.argtypes = [_vp]
     lib.nfx_runtime_last_error.restype = C.c_char_p

@@ -2223,6 +2223,10 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if (pl.tap_codes &&
+            (e = cudaMemcpyAsync(pl.tap_codes, pl.codes[0], static_cast<size_t>(M) * C,
+                                 cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
+            return e;
     }
     const int sms = device_sm_count();
     const int num_tiles = static_cast<int>((M + 127) / 128);
@@ -2315,6 +2319,10 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
         cur ^= 1;
+        if (pl.tap_codes &&
+            (e = cudaMemcpyAsync(pl.tap_codes + static_cast<size_t>(i + 1) * M * C, pl.codes[cur],
+                                 static_cast<size_t>(M) * C, cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
+            return e;
     }
     {
         using PC = PCfg<C>;

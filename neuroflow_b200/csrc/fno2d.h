@@ -141,6 +141,10 @@ struct Fno2dPlan {
     ProjCols proj_cols;    // proj_q epilogue and proj_out constants
     unsigned* err;
     KernelTimer* timer;    // nullptr unless profiling is enabled
+    // parity taps (nullptr: off): the int8 codes of every layer input -- the lift's
+    // output, then each layer's output, the last one being the projection's input --
+    // copied as L + 1 consecutive (B*H*W, C) blocks after the kernel that wrote them
+    int8_t* tap_codes;
 };
 
 // Row blocks per sample of the forward transform's partial spectra (B x this many
@@ -148,6 +152,18 @@ struct Fno2dPlan {
 inline int fno2d_row_blocks(int H) { return H < 4 ? H : 4; }
 
 bool fno2d_supported(int C, int MH, int MW);
+
+// The forward transform runs on tensor cores (spec_fwd_tc2_kernel) for W = 128 rows
+// with at most 12 kept W-modes, from the basis digits below; elsewhere on CUDA cores.
+inline bool fno2d_tc_forward(int W, int MW) { return W == 128 && 2 * MW <= 24; }
+constexpr int kFno2dLimbBytes = 4 * 32 * 128;   // [4][32][128] int8 basis digits
+
+// Host-side transform tables of the INT8 executor for an H x W grid (nfx_runtime.cpp):
+// fw, iw (MW, W) and fh, ih (H, MH) complex as float pairs (layouts of Fno2dPlan's
+// twf_w, twi_w, twf_h, twi_h), and, when fno2d_tc_forward(W, MW) and limbs / sum_b are
+// not null, the tensor-core forward basis (SpecFwdArgs::limbs, sum_b [2 MW]).
+void fno2d_tables(int H, int W, int MH, int MW, float* fw, float* fh, float* iw, float* ih,
+                  int8_t* limbs, long long* sum_b);
 cudaError_t fno2d_run(const Fno2dPlan& plan, cudaStream_t stream);
 
 // ---------------------------------------------------------------------------

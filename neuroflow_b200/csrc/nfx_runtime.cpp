@@ -29,6 +29,52 @@ int set_thread_error(int code, const std::string& msg);
 }
 
 namespace nfx {
+void fno2d_tables(int H, int W, int MH, int MW, float* fw, float* fh, float* iw, float* ih,
+                  int8_t* limbs, long long* sum_b) {
+    const double two_pi = 6.283185307179586476925286766559;
+    for (int k = 0; k < MW; ++k)
+        for (int w = 0; w < W; ++w) {
+            const double a = two_pi * static_cast<double>((static_cast<int64_t>(k) * w) % W) / W;
+            const double f = (k == 0 || 2 * k == W) ? 1.0 : 2.0;
+            fw[2 * (k * W + w)] = static_cast<float>(std::cos(a));
+            fw[2 * (k * W + w) + 1] = static_cast<float>(-std::sin(a));
+            iw[2 * (k * W + w)] = static_cast<float>(f * std::cos(a) / W);
+            iw[2 * (k * W + w) + 1] = static_cast<float>(f * std::sin(a) / W);
+        }
+    for (int h = 0; h < H; ++h)
+        for (int k = 0; k < MH; ++k) {
+            const double a = two_pi * static_cast<double>((static_cast<int64_t>(k) * h) % H) / H;
+            fh[2 * (h * MH + k)] = static_cast<float>(std::cos(a));
+            fh[2 * (h * MH + k) + 1] = static_cast<float>(-std::sin(a));
+            ih[2 * (h * MH + k)] = static_cast<float>(std::cos(a) / H);
+            ih[2 * (h * MH + k) + 1] = static_cast<float>(std::sin(a) / H);
+        }
+    if (!limbs || !sum_b || !fno2d_tc_forward(W, MW)) return;
+    // integer DFT basis of the tensor-core forward transform: the basis scaled by 2^27
+    // and rounded, split into four balanced base-256 digits
+    std::memset(limbs, 0, kFno2dLimbBytes);
+    for (int j = 0; j < 2 * MW; ++j) {
+        const int kw = j / 2, n = j;  // basis row j of every digit matrix
+        sum_b[j] = 0;
+        for (int w = 0; w < W; ++w) {
+            const double a = two_pi * static_cast<double>((static_cast<int64_t>(kw) * w) % W) / W;
+            const double v = (j & 1) ? -std::sin(a) : std::cos(a);
+            long long r = std::llround(v * 134217728.0);
+            sum_b[j] += r;
+            int dig[4];
+            for (int l = 3; l >= 1; --l) {
+                const long long d = ((r + 128) & 255) - 128;
+                dig[l] = static_cast<int>(d);
+                r = (r - d) / 256;
+            }
+            dig[0] = static_cast<int>(r);
+            for (int l = 0; l < 4; ++l) limbs[(l * 32 + n) * 128 + w] = static_cast<int8_t>(dig[l]);
+        }
+    }
+}
+}  // namespace nfx
+
+namespace nfx {
 // Event-pair timer: begin/end record events on the launch stream; read() waits for
 // them and folds the elapsed times into per-kernel totals.
 struct EventTimer : KernelTimer {
@@ -131,6 +177,8 @@ struct nfx_runtime {
     int tw_H = 0, tw_W = 0;
     int8_t* fwd_limbs = nullptr;      // tensor-core forward basis digits (W == 128)
     long long* fwd_sum_b = nullptr;
+    int8_t* tap_codes = nullptr;      // caller's parity-tap buffer (nfx_runtime_set_code_taps)
+    int64_t tap_cap = 0;
     // FNO2d FP32 (reference fake-quant) state
     nfx::Fno2dF32Plan plan2f{};
     void* f2_bufs[4] = {nullptr, nullptr, nullptr, nullptr};  // h0, h1, Xs, colinv
@@ -492,29 +540,16 @@ void fno2d_enable_int8(nfx_runtime* rt) {
     rt->int8_enabled = true;
 }
 
-// Twiddle tables in double precision, rounded once to float.
+// Twiddle tables in double precision, rounded once to float (fno2d_tables).
 int ensure_twiddles(nfx_runtime* rt, int H, int W) {
     if (rt->tw_H == H && rt->tw_W == W) return NFX_OK;
     const int MH = rt->plan.MH, MW = rt->plan.MW;
     std::vector<float> fw(2 * MW * W), fh(2 * H * MH), iw(2 * MW * W), ih(2 * H * MH);
-    const double two_pi = 6.283185307179586476925286766559;
-    for (int k = 0; k < MW; ++k)
-        for (int w = 0; w < W; ++w) {
-            const double a = two_pi * static_cast<double>((static_cast<int64_t>(k) * w) % W) / W;
-            const double f = (k == 0 || 2 * k == W) ? 1.0 : 2.0;
-            fw[2 * (k * W + w)] = static_cast<float>(std::cos(a));
-            fw[2 * (k * W + w) + 1] = static_cast<float>(-std::sin(a));
-            iw[2 * (k * W + w)] = static_cast<float>(f * std::cos(a) / W);
-            iw[2 * (k * W + w) + 1] = static_cast<float>(f * std::sin(a) / W);
-        }
-    for (int h = 0; h < H; ++h)
-        for (int k = 0; k < MH; ++k) {
-            const double a = two_pi * static_cast<double>((static_cast<int64_t>(k) * h) % H) / H;
-            fh[2 * (h * MH + k)] = static_cast<float>(std::cos(a));
-            fh[2 * (h * MH + k) + 1] = static_cast<float>(-std::sin(a));
-            ih[2 * (h * MH + k)] = static_cast<float>(std::cos(a) / H);
-            ih[2 * (h * MH + k) + 1] = static_cast<float>(std::sin(a) / H);
-        }
+    const bool tc = nfx::fno2d_tc_forward(W, MW);
+    std::vector<int8_t> limbs(tc ? nfx::kFno2dLimbBytes : 0);
+    std::vector<long long> sum_b(tc ? 2 * MW : 0);
+    nfx::fno2d_tables(H, W, MH, MW, fw.data(), fh.data(), iw.data(), ih.data(),
+                      tc ? limbs.data() : nullptr, tc ? sum_b.data() : nullptr);
     for (auto*& p : rt->tw) {
         if (p) cudaFree(p);
         p = nullptr;
@@ -528,32 +563,11 @@ int ensure_twiddles(nfx_runtime* rt, int H, int W) {
                      "cudaMemcpy"))
             return NFX_INTERNAL;
     }
-    // integer DFT basis for the tensor-core forward transform (W == 128): the basis
-    // scaled by 2^27 and rounded, split into four balanced base-256 digits
     if (rt->fwd_limbs) cudaFree(rt->fwd_limbs);
     if (rt->fwd_sum_b) cudaFree(rt->fwd_sum_b);
     rt->fwd_limbs = nullptr;
     rt->fwd_sum_b = nullptr;
-    if (W == 128 && 2 * MW <= 24) {
-        std::vector<int8_t> limbs(4 * 32 * 128, 0);
-        std::vector<long long> sum_b(2 * MW, 0);
-        for (int j = 0; j < 2 * MW; ++j) {
-            const int kw = j / 2, n = j;  // basis row j of every digit matrix
-            for (int w = 0; w < W; ++w) {
-                const double a = two_pi * static_cast<double>((static_cast<int64_t>(kw) * w) % W) / W;
-                const double v = (j & 1) ? -std::sin(a) : std::cos(a);
-                long long r = std::llround(v * 134217728.0);
-                sum_b[j] += r;
-                int dig[4];
-                for (int l = 3; l >= 1; --l) {
-                    const long long d = ((r + 128) & 255) - 128;
-                    dig[l] = static_cast<int>(d);
-                    r = (r - d) / 256;
-                }
-                dig[0] = static_cast<int>(r);
-                for (int l = 0; l < 4; ++l) limbs[(l * 32 + n) * 128 + w] = static_cast<int8_t>(dig[l]);
-            }
-        }
+    if (tc) {
         void* p1 = nullptr;
         void* p2 = nullptr;
         if (!cuda_ok(rt, cudaMalloc(&p1, limbs.size()), "cudaMalloc") ||
@@ -716,6 +730,14 @@ int fno2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
     pl.err = nfx::device_error_word();
     if (!pl.err) return rt_fail(rt, NFX_INTERNAL, "no device error word");
     pl.timer = rt->timer.get();
+    pl.tap_codes = nullptr;
+    if (rt->tap_codes) {
+        const int64_t need = static_cast<int64_t>(c.L + 1) * B * H * W * c.width;
+        if (need > rt->tap_cap)
+            return rt_fail(rt, NFX_INVALID_ARG, "code-tap buffer too small: needs " +
+                                                    std::to_string(need) + " bytes");
+        pl.tap_codes = rt->tap_codes;
+    }
     const cudaError_t e = nfx::fno2d_run(pl, st);
     if (e != cudaSuccess)
         return rt_fail(rt, NFX_INTERNAL, std::string("FNO2d launch failed: ") + cudaGetErrorString(e));
@@ -1310,9 +1332,10 @@ int fno2d_noalloc_plan(nfx_runtime* rt, const float* x, const int64_t* x_shape, 
     plan->HB = H / nfx::fno2d_row_blocks(H);
     plan->x = x;
     plan->y = y;
-    plan->fwd_limbs = nullptr;
+    plan->fwd_limbs = nullptr;  // the caller places the transform tables
     plan->fwd_sum_b = nullptr;
     plan->timer = nullptr;
+    plan->tap_codes = nullptr;
     return NFX_OK;
 }
 
@@ -1470,6 +1493,14 @@ int nfx_runtime_run_device(nfx_runtime* rt, const float* x, const int64_t* x_sha
     if (s != NFX_OK) return s;
     if (numel(x_shape, x_rank) > 0 && (!x || !y)) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
     return launch(rt, x, x_shape, y, static_cast<cudaStream_t>(stream));
+}
+
+int nfx_runtime_set_code_taps(nfx_runtime* rt, int8_t* device_buffer, int64_t capacity_bytes) {
+    if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
+    if (device_buffer && capacity_bytes <= 0) return rt_fail(rt, NFX_INVALID_ARG, "tap capacity must be > 0");
+    rt->tap_codes = device_buffer;
+    rt->tap_cap = device_buffer ? capacity_bytes : 0;
+    return NFX_OK;
 }
 
 int nfx_runtime_check(nfx_runtime* rt) {

@@ -108,6 +108,18 @@ class InferenceRuntime:
         if rc != 0:
             raise RuntimeError("RunTokenMixer2D failed: " + self._err())
 
+    def set_code_taps(self, buf=None) -> None:
+        """FNO2d INT8 parity taps: `buf` an int8 CUDA tensor of at least
+        (n_layers + 1) * batch * h * w * width bytes receives the codes of every layer
+        input on each later device run; None turns the taps off."""
+        if buf is None:
+            rc = _lib.nfx_runtime_set_code_taps(self._h, None, 0)
+        else:
+            rc = _lib.nfx_runtime_set_code_taps(self._h, C.c_void_p(buf.data_ptr()),
+                                                int(buf.numel() * buf.element_size()))
+        if rc != 0:
+            raise RuntimeError(self._err())
+
     def profile(self, enable: bool = True) -> None:
         """Enable (and reset) or disable per-kernel CUDA-event timing."""
         rc = _lib.nfx_runtime_profile_enable(self._h, int(bool(enable)))
