@@ -3,19 +3,23 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nfx|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...     (one process per GPU)
 
-One step = one forward pass of the FNO2d INT8 executor over a batch of 256 samples
-(128x128 grid, 3 input channels, width 64, 12x12 modes, 4 layers, out_ch 1) per GPU
-(weak scaling: every rank runs its own 256-sample batch and keeps its own outputs;
-samples are independent, so the data path has no collective -- the process group
-only lines the ranks up for timing and takes the maximum of their times).  Inputs are seeded synthetic Gaussian random fields;
-weights are random-init and calibrated on a separate 32-sample batch (no dataset or
-checkpoint is available offline).  The per-step working set (268 MB of int8 codes
-per layer boundary + 50 MB of input) is larger than the 126 MB L2, so no L2 flush is
-needed between steps.
+One step = one forward pass of the FNO2d INT8 executor over the global batch of 256
+samples (128x128 grid, 3 input channels, width 64, 12x12 modes, 4 layers, out_ch 1).
+At N > 1 the batch is partitioned across the ranks (strong scaling): every rank holds
+the whole batch, computes its contiguous slice of ceil(256 / N) samples with replicated
+weights, and NCCL all-gathers the fp32 outputs into every rank's buffer inside the
+timed region (InferenceRuntime.run_sharded).  The weak-scaling rate (every rank its own
+256 samples, no collective) is reported as "weak_scaling".  Inputs are seeded synthetic
+Gaussian random fields; weights are random-init and calibrated on a separate 32-sample
+batch (no dataset or checkpoint is available offline).  The per-step working set at
+256 samples per GPU (268 MB of int8 codes per layer boundary + 50 MB of input) is
+larger than the 126 MB L2, so no L2 flush is needed between steps; at N = 8 (32
+samples per GPU, 34 MB of codes) the slice fits in L2, which the line states.
 
 `value`: samples/s of the whole job with inputs resident in HBM, device-timed with
 CUDA events, max over ranks.  `e2e`: the same metric through the public host-buffer
-API (InferenceRuntime.run: pinned host x -> device -> host y every step).
+API (pinned host x -> device -> host y every step; at N > 1 run_sharded_host, each
+rank copying its input slice in and rank 0 copying the gathered outputs out).
 `--impl reference`: the reference's own CPU runtime (compiled from its sources into
 oracle/_ref) on all host cores, one InferenceRuntime per thread.
 """
@@ -246,19 +250,39 @@ def run_gemm(args):
     print(json.dumps(line), flush=True)
 
 
+def make_comm(ws: int, rank: int, local: int):
+    """The library's NCCL communicator for the sharded Run (None for one rank): rank 0
+    makes the unique id, the process group's broadcast hands it to the others."""
+    if ws <= 1:
+        return None
+    import torch.distributed as dist
+    from neuroflow_b200.runtime import Comm, comm_unique_id
+    box = [comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    return Comm(box[0], ws, rank, local)
+
+
 def run_nfx(args, ws, rank, local):
+    """One step = the forward of the global batch (configs[2]: 256 samples).  At N > 1
+    the batch is partitioned: every rank holds the whole input batch, computes its
+    contiguous slice of ceil(256 / N) samples and the outputs are all-gathered with NCCL
+    into every rank's y inside the timed region (strong scaling); the weak-scaling rate
+    (every rank its own 256 samples, no collective) is reported beside it."""
     import torch
+    from neuroflow_b200 import _nfx
     from neuroflow_b200.runtime import InferenceRuntime
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    B = args.batch
+    B = args.batch                       # global batch
     path = model_path(0)
-    x_host = inputs(100 + rank, B)
+    x_host = inputs(100, B)              # the same batch on every rank
     rt = InferenceRuntime(path, local)
     rt.enable_int8_gemm()
     if not rt.is_int8_gemm_enabled():
         raise RuntimeError("INT8 path not enabled for the bench model")
+    comm = make_comm(ws, rank, local)
+    b0, nb = _nfx.batch_slice(B, ws, rank)
     dx = torch.from_numpy(x_host).to(device)
     dy = torch.empty((B, CFG["H"], CFG["W"], CFG["out_channels"]), dtype=torch.float32,
                      device=device)
@@ -267,7 +291,42 @@ def run_nfx(args, ws, rank, local):
         import torch.distributed as dist
 
     def step():
-        rt.run_device(dx, dy, stream)
+        if comm is None:
+            rt.run_device(dx, dy, stream)
+        else:
+            rt.run_sharded(comm, dx, dy, -1, stream)
+
+    # a slice whose per-step working set fits in the 126 MB L2 (32 samples per GPU at
+    # N = 8: 34 MB of codes per layer boundary) gets an L2 flush between timed steps
+    # (a 256 MB write, outside the timed intervals: each step is timed by its own pair
+    # of events and the intervals are summed)
+    flush = None
+    if nb * P * CFG["width"] * 2 < 256 << 20:
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def timed(fn, steps):
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        if flush is None:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        for a, b in ev:
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in ev)
 
     for _ in range(args.warmup):
         step()
@@ -277,57 +336,66 @@ def run_nfx(args, ws, rank, local):
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         # keep the GPU busy while the clock sampler starts (untimed, like the warm-up;
         # the same count on every rank)
         for _ in range(args.preheat):
             step()
-        if ws > 1:
-            dist.barrier()
         torch.cuda.synchronize()
         rt.profile(True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            step()
-        e1.record(stream)
-        torch.cuda.synchronize()
+        ms = timed(step, args.steps)
     if ws > 1:
         dist.barrier()
-    ms = e0.elapsed_time(e1)
     prof = rt.profile_read()
     rt.profile(False)
     rt.check()
     ms = max_over_ranks(ms, ws, device)
-    value = job_rate(ws, B, args.steps, ms * 1e-3)
+    value = B * args.steps / (ms * 1e-3)
 
-    # end-to-end through the host-buffer API (pinned host memory)
-    if args.no_e2e:
-        e2e_steps = 0
+    weak = None
+    if ws > 1:
+        # every rank its own full batch, no collective (the previous bench line)
+        def own():
+            rt.run_device(dx, dy, stream)
+        for _ in range(args.warmup):
+            own()
+        wms = max_over_ranks(timed(own, args.steps), ws, device)
+        weak = {"value": round(job_rate(ws, B, args.steps, wms * 1e-3), 1), "unit": UNIT,
+                "batch_per_gpu": B, "ms_per_step": round(wms / args.steps, 3)}
+        rt.check()
+
+    # end to end through the host-buffer API (pinned host memory): the whole batch in,
+    # the whole output back (at N > 1 each rank copies its input slice in, the outputs
+    # are gathered to rank 0, which copies them out)
     xp = torch.from_numpy(x_host).pin_memory()
     yp = torch.empty(tuple(dy.shape), dtype=torch.float32).pin_memory()
     xn, yn = xp.numpy(), yp.numpy()
     e2e_steps = 0 if args.no_e2e else max(3, args.steps // 2)
+
+    def e2e_step():
+        if comm is None:
+            rt.run(xn, yn)
+        else:
+            rt.run_sharded_host(comm, xn, yn, 0)
     for _ in range(max(1, args.warmup) if e2e_steps else 0):
-        rt.run(xn, yn)
+        e2e_step()
     if ws > 1:
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        rt.run(xn, yn)
+        e2e_step()
     e2e_s = max(time.perf_counter() - t0, 1e-9)
     e2e_s = max_over_ranks(e2e_s, ws, device)
-    e2e = job_rate(ws, B, e2e_steps, e2e_s) if e2e_steps else None
+    e2e = B * e2e_steps / e2e_s if e2e_steps else None
 
     result = None
     if rank == 0:
         hbm, src = peaks()
-        # dominant kernel of the step
+        # dominant kernel of the step (rank 0's launches over its slice)
         top = max(prof.items(), key=lambda kv: kv[1][1])
         name, (launches, tot_ms) = top
         per_launch_s = tot_ms / launches * 1e-3
-        M = B * P
+        M = nb * P
         C = CFG["width"]
         alg = {  # algorithmic bytes per launch of each kernel
             "fno2d_layer": 2 * M * C,                      # codes in + codes out
@@ -343,19 +411,24 @@ def run_nfx(args, ws, rank, local):
             tj = json.load(open(tp))
             t = tj.get("bytes_per_launch", {}).get(name)
             if t is not None:
-                traffic = int(t * B / tj.get("batch", B))
+                traffic = int(t * nb / tj.get("batch", nb))
         share = {k: round(v[1] / sum(vv[1] for vv in prof.values()), 3) for k, v in prof.items()}
         total_launches = sum(v[0] for v in prof.values())
         result = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "batch_per_gpu": B, "global_batch": B * ws,
+            "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": B, "batch_per_gpu": nb,
                        "grid": [CFG["H"], CFG["W"]], "in_channels": CFG["in_channels"],
                        "out_channels": CFG["out_channels"], "width": C, "modes": [12, 12],
-                       "n_layers": CFG["n_layers"], "parallelism": f"batch x{ws}",
-                       "l2": "working set > L2 (268 MB codes per layer boundary)"},
+                       "n_layers": CFG["n_layers"],
+                       "parallelism": f"batch x{ws}" + (", NCCL all-gather of the outputs"
+                                                        if ws > 1 else ""),
+                       "l2": ("working set > L2 (268 MB codes per layer boundary at 256 "
+                              "samples)") if flush is None else
+                             "L2 flushed between timed steps (256 MB write, untimed)"},
             "e2e": {"value": round(e2e, 1) if e2e else None, "unit": UNIT,
                     "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(4 * B * P)},
             "roofline": {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1),
@@ -370,6 +443,12 @@ def run_nfx(args, ws, rank, local):
             "gpu_launches": total_launches,
             "clocks": clk.summary(),
         }
+        if weak is not None:
+            result["weak_scaling"] = weak
+    if comm is not None:
+        if ws > 1:
+            dist.barrier()
+        comm.close()
     return result, rt, x_host, path
 
 

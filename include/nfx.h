@@ -157,6 +157,69 @@ const char* nfx_runtime_last_error(const nfx_runtime* rt);
 /* Message of the last failing handle-less call of this thread. */
 const char* nfx_last_error(void);
 
+/* ---- Batch partitioned across the GPUs of one node ------------------------------
+ * Samples are independent, so a batch of B runs as contiguous slices of ceil(B / G)
+ * samples on G GPUs with replicated weights; the only communication is moving inputs
+ * to and outputs from the GPU that holds the caller's buffers (NCCL, loaded at run time
+ * from libnccl.so.2 or $NFX_NCCL_LIB).  The reference runs one batch per Run on one
+ * host (cpp/src/runtime.cpp:85-101); these entry points keep that call shape. */
+
+/* The slice [first, first + count) of a batch of `batch` samples that rank `rank` of
+ * `world` computes (count may be 0 for the last ranks). */
+void nfx_batch_slice(int64_t batch, int world, int rank, int64_t* first, int64_t* count);
+
+/* One process driving several GPUs: InferenceRuntime::Create (runtime.h:72-74) with a
+ * device list.  Every device gets its own runtime (weights uploaded to each). */
+typedef struct nfx_group nfx_group;
+int nfx_group_create(const char* ir_path, const int* devices, int n_devices, nfx_group** out);
+void nfx_group_destroy(nfx_group* g);
+int nfx_group_size(const nfx_group* g);
+/* The member runtime on the i-th listed device (owned by the group). */
+nfx_runtime* nfx_group_member(nfx_group* g, int i);
+const char* nfx_group_last_error(const nfx_group* g);
+/* EnableInt8Gemm / IsInt8GemmEnabled / enable_fp8 on every member (runtime.h:116-128). */
+void nfx_group_enable_int8_gemm(nfx_group* g);
+int nfx_group_is_int8_gemm_enabled(const nfx_group* g);
+void nfx_group_enable_fp8(nfx_group* g);
+/* InferenceRuntime::Run (runtime.h:76-79) over the group: HOST x and y; every device
+ * copies its own slice in and its outputs out (one host thread per device, each
+ * overlapping its copies with its compute).  Synchronous. */
+int nfx_group_run(nfx_group* g, const float* x, const int64_t* x_shape, int x_rank, float* y,
+                  const int64_t* y_shape, int y_rank);
+/* Device-buffer Run over the group: x and y are DEVICE buffers on the first listed
+ * device.  NCCL point-to-point transfers (over NVLink) scatter the input slices to the
+ * other devices and gather their outputs into y; ordered after the work queued on
+ * `stream` (a stream of the first device) before the call, and work queued on it after
+ * the call waits for the gathered outputs.  Asynchronous; nfx_group_check reports
+ * device-side errors.  No counterpart in the reference. */
+int nfx_group_run_device(nfx_group* g, const float* x, const int64_t* x_shape, int x_rank,
+                         float* y, const int64_t* y_shape, int y_rank, void* stream);
+int nfx_group_check(nfx_group* g);
+
+/* One process per GPU (torchrun style): an NCCL communicator of `world` ranks.  Rank 0
+ * creates the 128-byte unique id, the caller distributes it (e.g. over its own process
+ * group's store), and every rank creates its communicator on its runtime's device. */
+typedef struct nfx_comm nfx_comm;
+int nfx_comm_unique_id(unsigned char* id_out, int id_bytes);
+int nfx_comm_create(const unsigned char* id, int id_bytes, int world, int rank, int device,
+                    nfx_comm** out);
+void nfx_comm_destroy(nfx_comm* comm);
+/* Run over a batch partitioned across the communicator's ranks: every rank passes the
+ * WHOLE batch (x, y device buffers of the full shape on its own device), computes its
+ * slice and writes it into y, then the slices are gathered with NCCL -- into every
+ * rank's y (root < 0: an all-gather) or into `root`'s y only (the other ranks' y then
+ * hold just their own slice).  Every rank must make the same call.  Asynchronous on
+ * `stream`, like nfx_runtime_run_device.  No counterpart in the reference. */
+int nfx_runtime_run_sharded(nfx_runtime* rt, nfx_comm* comm, const float* x,
+                            const int64_t* x_shape, int x_rank, float* y,
+                            const int64_t* y_shape, int y_rank, int root, void* stream);
+/* The same with HOST buffers (InferenceRuntime::Run's contract, runtime.h:76-79): each
+ * rank copies only its own input slice to its GPU; after the gather, y is written on
+ * every rank (root < 0) or on `root` only.  Synchronous. */
+int nfx_runtime_run_sharded_host(nfx_runtime* rt, nfx_comm* comm, const float* x,
+                                 const int64_t* x_shape, int x_rank, float* y,
+                                 const int64_t* y_shape, int y_rank, int root);
+
 /* ---- nflow-quant GEMM (cpp/include/neuroflow/int8_gemm.h) ----------------------- */
 
 /* W8A8 GEMM over activation CODES with one (scale, zero point) per row, per-channel

@@ -69,6 +69,50 @@ if hasattr(lib, "nfx_runtime_create"):
     lib.nfx_runtime_profile_entry.argtypes = [_vp, C.c_int, C.POINTER(C.c_char_p),
                                               C.POINTER(C.c_int), C.POINTER(C.c_double)]
 
+    lib.nfx_batch_slice.restype = None
+    lib.nfx_batch_slice.argtypes = [C.c_int64, C.c_int, C.c_int, _i64p, _i64p]
+    lib.nfx_group_create.restype = C.c_int
+    lib.nfx_group_create.argtypes = [C.c_char_p, C.POINTER(C.c_int), C.c_int, C.POINTER(_vp)]
+    lib.nfx_group_destroy.restype = None
+    lib.nfx_group_destroy.argtypes = [_vp]
+    lib.nfx_group_size.restype = C.c_int
+    lib.nfx_group_size.argtypes = [_vp]
+    lib.nfx_group_member.restype = _vp
+    lib.nfx_group_member.argtypes = [_vp, C.c_int]
+    lib.nfx_group_last_error.restype = C.c_char_p
+    lib.nfx_group_last_error.argtypes = [_vp]
+    lib.nfx_group_enable_int8_gemm.restype = None
+    lib.nfx_group_enable_int8_gemm.argtypes = [_vp]
+    lib.nfx_group_is_int8_gemm_enabled.restype = C.c_int
+    lib.nfx_group_is_int8_gemm_enabled.argtypes = [_vp]
+    lib.nfx_group_enable_fp8.restype = None
+    lib.nfx_group_enable_fp8.argtypes = [_vp]
+    lib.nfx_group_run.restype = C.c_int
+    lib.nfx_group_run.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int]
+    lib.nfx_group_run_device.restype = C.c_int
+    lib.nfx_group_run_device.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int, _vp]
+    lib.nfx_group_check.restype = C.c_int
+    lib.nfx_group_check.argtypes = [_vp]
+    lib.nfx_comm_unique_id.restype = C.c_int
+    lib.nfx_comm_unique_id.argtypes = [C.c_char_p, C.c_int]
+    lib.nfx_comm_create.restype = C.c_int
+    lib.nfx_comm_create.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
+    lib.nfx_comm_destroy.restype = None
+    lib.nfx_comm_destroy.argtypes = [_vp]
+    lib.nfx_runtime_run_sharded.restype = C.c_int
+    lib.nfx_runtime_run_sharded.argtypes = [_vp, _vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int,
+                                            C.c_int, _vp]
+    lib.nfx_runtime_run_sharded_host.restype = C.c_int
+    lib.nfx_runtime_run_sharded_host.argtypes = [_vp, _vp, _vp, _i64p, C.c_int, _vp, _i64p,
+                                                 C.c_int, C.c_int]
+
+
+def batch_slice(batch: int, world: int, rank: int):
+    """(first, count): the samples rank `rank` of `world` computes (nfx_batch_slice)."""
+    a, b = C.c_int64(), C.c_int64()
+    lib.nfx_batch_slice(int(batch), int(world), int(rank), C.byref(a), C.byref(b))
+    return a.value, b.value
+
 
 class NfxError(RuntimeError):
     def __init__(self, code: int, msg: str):

@@ -60,7 +60,7 @@ def build(verbose: bool = False) -> str:
         objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
     if (not os.path.exists(LIB)
             or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs)):
-        cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs, "-lpthread"]
+        cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs, "-lpthread", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

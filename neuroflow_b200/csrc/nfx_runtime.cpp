@@ -1303,6 +1303,41 @@ int runtime_device(const nfx_runtime* rt) { return rt->device; }
 
 int runtime_fail(nfx_runtime* rt, int code, const char* msg) { return rt_fail(rt, code, msg); }
 
+// Helpers of the multi-GPU entry points (nfx_multi.cpp).
+int runtime_check_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t* ys, int yr) {
+    if (!xs || !ys) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
+    return check_shapes(rt, xs, xr, ys, yr);
+}
+
+int runtime_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
+    return launch(rt, dx, xs, dy, st);
+}
+
+cudaStream_t runtime_stream(nfx_runtime* rt) { return rt->stream; }
+
+// The handle's device staging buffers, grown to hold nx input and ny output floats.
+int runtime_staging(nfx_runtime* rt, size_t nx, size_t ny, float** dx, float** dy) {
+    if (nx > rt->dx_cap) {
+        if (rt->dx) cudaFree(rt->dx);
+        rt->dx = nullptr;
+        rt->dx_cap = 0;
+        if (!cuda_ok(rt, cudaMalloc(&rt->dx, nx * 4), "cudaMalloc input")) return NFX_INTERNAL;
+        rt->dx_cap = nx;
+    }
+    if (ny > rt->dy_cap) {
+        if (rt->dy) cudaFree(rt->dy);
+        rt->dy = nullptr;
+        rt->dy_cap = 0;
+        if (!cuda_ok(rt, cudaMalloc(&rt->dy, ny * 4), "cudaMalloc output")) return NFX_INTERNAL;
+        rt->dy_cap = ny;
+    }
+    *dx = rt->dx;
+    *dy = rt->dy;
+    return NFX_OK;
+}
+
+int runtime_fail_str(nfx_runtime* rt, int code, const std::string& msg) { return rt_fail(rt, code, msg); }
+
 int fno2d_noalloc_plan(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
                        float* y, const int64_t* y_shape, int y_rank, Fno2dPlan* plan) {
     if (!x_shape || !y_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");

@@ -145,6 +145,126 @@ class InferenceRuntime:
             raise RuntimeError("device error: " + self._err())
 
 
+    def run_sharded(self, comm: "Comm", x, y, root: int = -1, stream=None) -> None:
+        """Batch partitioned over the ranks of `comm` (one process per GPU): x, y are the
+        WHOLE batch as CUDA tensors on this runtime's device; this rank computes its
+        slice and NCCL gathers the outputs into every rank's y (root < 0) or into the
+        root's y.  Every rank makes the same call.  Asynchronous on `stream`."""
+        stream = self._stream(x, stream)
+        xs = (C.c_int64 * x.dim())(*x.shape)
+        ys = (C.c_int64 * y.dim())(*y.shape)
+        rc = _lib.nfx_runtime_run_sharded(self._h, comm._h, C.c_void_p(x.data_ptr()), xs, x.dim(),
+                                          C.c_void_p(y.data_ptr()), ys, y.dim(), int(root),
+                                          C.c_void_p(stream))
+        if rc != 0:
+            raise RuntimeError("Run failed: " + self._err())
+
+    def run_sharded_host(self, comm: "Comm", x: np.ndarray, y: np.ndarray, root: int = -1) -> None:
+        """The same with host arrays (synchronous): each rank copies only its own input
+        slice; y is written on every rank (root < 0) or on the root only."""
+        if not (isinstance(y, np.ndarray) and y.dtype == np.float32 and y.flags.c_contiguous):
+            raise RuntimeError("Run failed: y must be a C-contiguous float32 array")
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rc = _lib.nfx_runtime_run_sharded_host(self._h, comm._h, x.ctypes.data_as(C.c_void_p),
+                                               _shape(x), x.ndim, y.ctypes.data_as(C.c_void_p),
+                                               _shape(y), y.ndim, int(root))
+        if rc != 0:
+            raise RuntimeError("Run failed: " + self._err())
+
+
+def comm_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for Comm(); made on one rank, shared by all."""
+    buf = C.create_string_buffer(128)
+    rc = _lib.nfx_comm_unique_id(buf, 128)
+    if rc != 0:
+        raise RuntimeError("nfx_comm_unique_id failed: " + _lib.nfx_last_error().decode())
+    return buf.raw
+
+
+class Comm:
+    """NCCL communicator of one rank (one process per GPU) for InferenceRuntime.run_sharded."""
+
+    def __init__(self, unique_id: bytes, world: int, rank: int, device: int):
+        h = C.c_void_p()
+        rc = _lib.nfx_comm_create(bytes(unique_id), len(unique_id), int(world), int(rank),
+                                  int(device), C.byref(h))
+        if rc != 0:
+            raise RuntimeError("nfx_comm_create failed: " + _lib.nfx_last_error().decode())
+        self._h = h
+        self.world, self.rank, self.device = int(world), int(rank), int(device)
+
+    def close(self):
+        h = getattr(self, "_h", None)
+        if h:
+            _lib.nfx_comm_destroy(h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+
+class RuntimeGroup:
+    """One process driving several GPUs: InferenceRuntime's calls over a device list; a
+    batch runs as contiguous slices, one per device, with the weights on every device."""
+
+    def __init__(self, ir_path: str, devices):
+        devices = [int(d) for d in devices]
+        arr = (C.c_int * len(devices))(*devices)
+        h = C.c_void_p()
+        rc = _lib.nfx_group_create(str(ir_path).encode(), arr, len(devices), C.byref(h))
+        if rc != 0:
+            raise RuntimeError("create runtime group failed: " + _lib.nfx_last_error().decode())
+        self._h = h
+        self.devices = devices
+
+    def close(self):
+        h = getattr(self, "_h", None)
+        if h:
+            _lib.nfx_group_destroy(h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def _err(self) -> str:
+        return _lib.nfx_group_last_error(self._h).decode()
+
+    def enable_int8_gemm(self) -> None:
+        _lib.nfx_group_enable_int8_gemm(self._h)
+
+    def is_int8_gemm_enabled(self) -> bool:
+        return bool(_lib.nfx_group_is_int8_gemm_enabled(self._h))
+
+    def enable_fp8(self) -> None:
+        _lib.nfx_group_enable_fp8(self._h)
+
+    def run(self, x: np.ndarray, y: np.ndarray) -> None:
+        """Host arrays: every device copies its own slice in and out."""
+        if not (isinstance(y, np.ndarray) and y.dtype == np.float32 and y.flags.c_contiguous):
+            raise RuntimeError("Run failed: y must be a C-contiguous float32 array")
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rc = _lib.nfx_group_run(self._h, x.ctypes.data_as(C.c_void_p), _shape(x), x.ndim,
+                                y.ctypes.data_as(C.c_void_p), _shape(y), y.ndim)
+        if rc != 0:
+            raise RuntimeError("Run failed: " + self._err())
+
+    def run_device(self, x, y, stream=None) -> None:
+        """CUDA tensors on the first device; NCCL scatters the inputs and gathers the
+        outputs.  Asynchronous on `stream` (a stream of the first device)."""
+        stream = InferenceRuntime._stream(x, stream)
+        xs = (C.c_int64 * x.dim())(*x.shape)
+        ys = (C.c_int64 * y.dim())(*y.shape)
+        rc = _lib.nfx_group_run_device(self._h, C.c_void_p(x.data_ptr()), xs, x.dim(),
+                                       C.c_void_p(y.data_ptr()), ys, y.dim(), C.c_void_p(stream))
+        if rc != 0:
+            raise RuntimeError("Run failed: " + self._err())
+
+    def check(self) -> None:
+        rc = _lib.nfx_group_check(self._h)
+        if rc != 0:
+            raise RuntimeError("device error: " + self._err())
+
+
 _RANK = {"FNO1d": 3, "FNO2d": 4, "FNO3d": 5, "TokenMixer2D": 4}
 
 
