@@ -238,6 +238,17 @@ int nfx_int8_gemm(const int8_t* A, const float* scale_a, const int32_t* zp_a, fl
                   const int32_t* zp_w, const int32_t* sum_w, const float* bias, int N, int act,
                   float* C, void* stream);
 
+/* Failure-path test hook: the budget, in nanoseconds, of the pipeline waits inside the
+ * INT8 GEMM kernel (nfx_int8_gemm and the GEMM layers of the FNO1d / TokenMixer2D
+ * executors) for launches made after the call; 0 restores the default of 2 s.  With a
+ * budget far below the kernel's latency the waits run out: the kernel raises its abort
+ * flag, records the timeout in the device error word, waits (with the default budget)
+ * for its own loads and MMAs in flight, releases its tensor memory and returns, and the
+ * next nfx_device_errors / nfx_runtime_check reports it (NFX_INTERNAL); the context
+ * stays usable.  Process-wide; not for production use.  No counterpart in the reference
+ * (its errors are host-side Status codes, cpp/include/neuroflow/tensor.h:29-60). */
+void nfx_debug_set_wait_budget_ns(unsigned long long ns);
+
 /* Read and clear the device error word of the current device (bit flags of waits
  * that timed out inside kernels).  Synchronises the device. */
 int nfx_device_errors(unsigned* flags_out);

@@ -154,6 +154,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int num_tiles = (p.M + 127) / 128;
+    const uint64_t budget = p.wait_ns ? p.wait_ns : kWaitNs;
 
     // ---- one-time set-up: weights (swizzled), ones block, column params, barriers
     {
@@ -209,7 +210,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
                 const int s = it % C::kStages;
                 const uint32_t ph = (it / C::kStages) & 1;
-                if (!mbar_wait_backoff(&empty[s], ph ^ 1, sAbort, 1024)) {
+                if (!mbar_wait_backoff(&empty[s], ph ^ 1, sAbort, 1024, 32, budget)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitSlotFree);
                     break;
@@ -219,11 +220,12 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     tma_load_2d(sA + s * C::kABytes + kb * 128 * C::kRowBytes, &tmA, &full[s],
                                 kb * C::kRowBytes, tile * 128);
             }
-            // Drain: every load this thread issued must land before the CTA exits.
+            // Drain: every load this thread issued must land before the CTA exits, also
+            // after an abort (the loads complete by themselves).
             const int issued = it;
             for (int j = (issued > C::kStages ? issued - C::kStages : 0); j < issued; ++j) {
-                if (!mbar_wait_backoff(&full[j % C::kStages], (j / C::kStages) & 1, sAbort, 1024) && *sAbort) {
-                    // a load that never completes leaves nothing else to wait for
+                if (!mbar_wait_drain(&full[j % C::kStages], (j / C::kStages) & 1)) {
+                    atomicOr(p.err, kErrWaitDrain);
                     break;
                 }
             }
@@ -238,12 +240,12 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const uint32_t ph = (it / C::kStages) & 1;
                 const int a = it % C::kAccStages;
                 const uint32_t aph = (it / C::kAccStages) & 1;
-                if (!mbar_wait_backoff(&accEmpty[a], aph ^ 1, sAbort, 128)) {
+                if (!mbar_wait_backoff(&accEmpty[a], aph ^ 1, sAbort, 128, 32, budget)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitAccFree);
                     break;
                 }
-                if (!mbar_wait_backoff(&full[s], ph, sAbort, 128)) {
+                if (!mbar_wait_backoff(&full[s], ph, sAbort, 128, 32, budget)) {
                     *sAbort = 1;
                     atomicOr(p.err, kErrWaitTmaFull);
                     break;
@@ -265,10 +267,12 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 mma_commit(&empty[s]);
                 mma_commit(&accFull[a]);
             }
-            // Drain: the last commit must complete before TMEM is released.
+            // Drain: the last commit must complete before TMEM is released, also after
+            // an abort (the MMAs issued so far complete by themselves, in order).
             if (it > 0) {
                 const int j = it - 1;
-                mbar_wait_backoff(&accFull[j % C::kAccStages], (j / C::kAccStages) & 1, sAbort, 1024);
+                if (!mbar_wait_drain(&accFull[j % C::kAccStages], (j / C::kAccStages) & 1))
+                    atomicOr(p.err, kErrWaitDrain);
             }
         }
         __syncwarp();
@@ -302,7 +306,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             row_params(tile + tstride, sA_next, zA_next);
             const int a = it % C::kAccStages;
             const uint32_t aph = (it / C::kAccStages) & 1;
-            if (!mbar_wait(&accFull[a], aph, sAbort)) {
+            if (!mbar_wait(&accFull[a], aph, sAbort, budget)) {
                 *sAbort = 1;
                 atomicOr(p.err, kErrWaitAccFull);
                 break;
@@ -409,7 +413,9 @@ bool gemm_i8_supported(int K, int N) {
     return ok(K) && ok(N);
 }
 
-cudaError_t gemm_i8_launch(const GemmArgs& p, int K, int N, cudaStream_t stream) {
+cudaError_t gemm_i8_launch(const GemmArgs& p_in, int K, int N, cudaStream_t stream) {
+    GemmArgs p = p_in;
+    p.wait_ns = debug_wait_budget_ns();
     const int row_bytes = K >= 128 ? 128 : K;
     CUtensorMap tmA;
     if (!encode_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.A, K, p.M, K, row_bytes, 128, row_bytes))

@@ -2,6 +2,7 @@
 // include/nfx.h.  (The runtime handle entry points live in nfx_runtime.cpp.)
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdio>
 #include <string>
 
@@ -19,11 +20,20 @@ int fail(int code, const std::string& msg) {
 
 namespace nfx {
 int set_thread_error(int code, const std::string& msg) { return fail(code, msg); }
+
+namespace {
+std::atomic<unsigned long long> g_wait_budget_ns{0};
+}
+unsigned long long debug_wait_budget_ns() { return g_wait_budget_ns.load(std::memory_order_relaxed); }
 }  // namespace nfx
 
 extern "C" {
 
 const char* nfx_last_error(void) { return g_err.c_str(); }
+
+void nfx_debug_set_wait_budget_ns(unsigned long long ns) {
+    nfx::g_wait_budget_ns.store(ns, std::memory_order_relaxed);
+}
 
 int nfx_int8_gemm(const int8_t* A, const float* scale_a, const int32_t* zp_a, float scale_a_t,
                   int32_t zp_a_t, int M, int K, const int8_t* W, const float* scale_w,

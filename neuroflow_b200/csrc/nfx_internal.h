@@ -34,7 +34,14 @@ struct GemmArgs {
     float* C;                 // (M, N) fp32 output
     int M;
     unsigned* err;            // device error word
+    // budget of the kernel's pipeline waits in ns (0: the default of 2 s); the drains
+    // before teardown always use the default
+    unsigned long long wait_ns;
 };
+
+// Test hook of the failure path (nfx_debug_set_wait_budget_ns): the pipeline-wait
+// budget that gemm_i8_launch gives every GEMM launch (0: the default).
+unsigned long long debug_wait_budget_ns();
 
 bool gemm_i8_supported(int K, int N);
 cudaError_t gemm_i8_launch(const GemmArgs& p, int K, int N, cudaStream_t stream);

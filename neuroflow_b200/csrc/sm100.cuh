@@ -78,6 +78,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test of a phase (mbarrier.test_wait: never suspends the thread).
+__device__ __forceinline__ bool mbar_test_addr(uint32_t addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// One try of a bounded wait.  try_wait may suspend the thread until the phase completes,
+// so a wait with a budget below the default tests without suspending instead: then the
+// budget, not the phase, decides when the wait ends.
+__device__ __forceinline__ bool mbar_try_budget(uint32_t addr, uint32_t parity, uint64_t budget_ns) {
+    if (budget_ns >= kWaitNs) return mbar_try_wait(addr, parity);
+    return mbar_test_addr(addr, parity);
+}
+
+// The budget has run out.  Budgets below kTimerGrainNs are finer than the global
+// timer's update interval, so they count as spent at the first retry.
+constexpr uint64_t kTimerGrainNs = 1000;
+__device__ __forceinline__ bool budget_spent(uint64_t t0, uint64_t budget_ns) {
+    return budget_ns < kTimerGrainNs || global_ns() - t0 > budget_ns;
+}
+
 // Non-blocking test: true when the phase with the given parity has completed.
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
@@ -95,15 +123,16 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 // early when another warp of the CTA has raised `abort`.  For waits on a kernel's
 // critical path (an epilogue waiting for its accumulator): the warp resumes as soon
 // as the phase completes.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint64_t budget_ns = kWaitNs) {
     const uint32_t addr = smem_u32(bar);
-    if (mbar_try_wait(addr, parity)) return true;
+    if (mbar_try_budget(addr, parity, budget_ns)) return true;
     const uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(addr, parity)) return true;
-        if ((i & 63u) == 0u) {
+        if (mbar_try_budget(addr, parity, budget_ns)) return true;
+        if ((i & 63u) == 1u) {
             if (*abort) return false;
-            if (global_ns() - t0 > kWaitNs) return false;
+            if (budget_spent(t0, budget_ns)) return false;
         }
     }
 }
@@ -113,19 +142,36 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // arithmetic, at the price of resuming up to `max_ns` late.  For producers that run
 // stages ahead and for the single-thread MMA issuer.
 __device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                                  uint32_t max_ns, uint32_t min_ns = 32) {
+                                                  uint32_t max_ns, uint32_t min_ns = 32,
+                                                  uint64_t budget_ns = kWaitNs) {
     const uint32_t addr = smem_u32(bar);
-    if (mbar_try_wait(addr, parity)) return true;
+    if (mbar_try_budget(addr, parity, budget_ns)) return true;
     const uint64_t t0 = global_ns();
     uint32_t ns = min_ns;
     for (uint32_t i = 1;; ++i) {
         __nanosleep(ns);
-        if (mbar_try_wait(addr, parity)) return true;
+        if (mbar_try_budget(addr, parity, budget_ns)) return true;
         ns = ns * 2 < max_ns ? ns * 2 : max_ns;
-        if ((i & 7u) == 0u) {
+        if ((i & 7u) == 1u) {
             if (*abort) return false;
-            if (global_ns() - t0 > kWaitNs) return false;
+            if (budget_spent(t0, budget_ns)) return false;
         }
+    }
+}
+
+// Wait for this CTA's own asynchronous work (a TMA load it issued, the completion of
+// an MMA commit) before teardown.  Such work completes by itself, so the wait ignores
+// the abort flag; it is still bounded by the default budget.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+    const uint32_t addr = smem_u32(bar);
+    if (mbar_try_wait(addr, parity)) return true;
+    const uint64_t t0 = global_ns();
+    uint32_t ns = 32;
+    for (;;) {
+        __nanosleep(ns);
+        if (mbar_try_wait(addr, parity)) return true;
+        ns = ns * 2 < 1024u ? ns * 2 : 1024u;
+        if (global_ns() - t0 > kWaitNs) return false;
     }
 }
 
