@@ -249,6 +249,21 @@ int nfx_int8_gemm(const int8_t* A, const float* scale_a, const int32_t* zp_a, fl
  * (its errors are host-side Status codes, cpp/include/neuroflow/tensor.h:29-60). */
 void nfx_debug_set_wait_budget_ns(unsigned long long ns);
 
+/* ---- FP8 E4M3 (cpp/include/neuroflow/fp8_e4m3.h) -------------------------------
+ * The reference's bit-level encoder and decoder on the GPU: fp32_array_to_e4m3_bits
+ * (fp8_e4m3.h:286, RNE with saturation to +-448, NaN -> 0x7F, its subnormal rule),
+ * e4m3_bits_to_fp32_array (:295) and fp8_e4m3_per_tensor_fake_quant (:312-334;
+ * scale 0 acts as 1 for the division).  The plain names take DEVICE pointers of the
+ * current device and run asynchronously on `stream`; the _host names take host
+ * pointers (the neuroflow_cpp module's fp8_e4m3_* helpers, fp8_e4m3_pybind.h:24-66)
+ * and return when the result is in `out`. */
+int nfx_fp8_e4m3_to_bits(const float* x, uint8_t* bits, int64_t n, void* stream);
+int nfx_fp8_e4m3_from_bits(const uint8_t* bits, float* y, int64_t n, void* stream);
+int nfx_fp8_e4m3_fake_quant(const float* x, float scale, float* y, int64_t n, void* stream);
+int nfx_fp8_e4m3_to_bits_host(const float* x, uint8_t* bits, int64_t n);
+int nfx_fp8_e4m3_from_bits_host(const uint8_t* bits, float* y, int64_t n);
+int nfx_fp8_e4m3_fake_quant_host(const float* x, float scale, float* y, int64_t n);
+
 /* Read and clear the device error word of the current device (bit flags of waits
  * that timed out inside kernels).  Synchronises the device. */
 int nfx_device_errors(unsigned* flags_out);

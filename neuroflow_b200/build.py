@@ -74,8 +74,10 @@ CLI = os.path.join(PKG, "nflow_infer")
 
 def _build_cli() -> None:
     """The nflow_infer executable, linked against libnfx.so (found next to it)."""
+    hpp = os.path.join(ROOT, "include", "nflow_runtime.hpp")
     if os.path.exists(CLI) and os.path.getmtime(CLI) >= max(os.path.getmtime(CLI_SRC),
-                                                              os.path.getmtime(LIB)):
+                                                              os.path.getmtime(LIB),
+                                                              os.path.getmtime(hpp)):
         return
     cmd = ["g++", "-std=c++17", "-O2", "-I" + os.path.join(ROOT, "include"), CLI_SRC, "-o", CLI,
            "-L" + PKG, "-lnfx", "-Wl,-rpath,$ORIGIN"]

@@ -1,5 +1,7 @@
 // nflow_infer -- command-line front-end of libnfx.so with the reference CLI's flags
 // (cpp/src/main.cpp:27-115): --model <file.nneuroir> --input <x.npy> --output <y.npy>.
+// Written against nflow::InferenceRuntime (include/nflow_runtime.hpp), the reference's
+// C++ interface over the C-ABI, as the reference CLI is written against its own.
 // Extra flags: --int8 (EnableInt8Gemm), --fp8 (the FNO3d E4M3 executor), --device N.
 // TokenMixer2D models run through RunTokenMixer2D like the reference's `infer`
 // (pybind_module.cpp:61-111).  Exit code 0 on success, 1 on any error, as the reference.
@@ -12,7 +14,7 @@
 #include <string>
 #include <vector>
 
-#include "nfx.h"
+#include "nflow_runtime.hpp"
 
 namespace {
 
@@ -139,20 +141,19 @@ int main(int argc, char** argv) {
         usage();
         return 1;
     }
-    char op[32] = {0};
-    int32_t cfg[8];
-    int nw = 0, q = 0;
-    if (nfx_load_neuroir(model.c_str(), op, sizeof(op), cfg, &nw, &q) != NFX_OK) {
-        std::cerr << "model load failed: " << nfx_last_error() << std::endl;
+    nflow::LoadedModelInfo info;
+    nflow::Status st = nflow::LoadNeuroIr(model, info);
+    if (!st.ok()) {
+        std::cerr << "model load failed: " << st.message() << std::endl;
         return 1;
     }
-    const std::string ops(op);
+    const std::string& ops = info.op;
     int rank = 0;
     int64_t out_ch = 0;
-    if (ops == "FNO1d") rank = 3, out_ch = cfg[1];
-    else if (ops == "FNO2d") rank = 4, out_ch = cfg[1];
-    else if (ops == "FNO3d") rank = 5, out_ch = cfg[1];
-    else if (ops == "TokenMixer2D") rank = 4, out_ch = cfg[1];
+    if (ops == "FNO1d") rank = 3, out_ch = info.cfg[1];
+    else if (ops == "FNO2d") rank = 4, out_ch = info.cfg[1];
+    else if (ops == "FNO3d") rank = 5, out_ch = info.cfg[1];
+    else if (ops == "TokenMixer2D") rank = 4, out_ch = info.cfg[1];
     else {
         std::cerr << "unsupported op in IR: " << ops << std::endl;
         return 1;
@@ -168,27 +169,26 @@ int main(int argc, char** argv) {
         std::cerr << "expected " << rank << "D input for " << ops << ", got rank " << xs.size() << std::endl;
         return 1;
     }
-    nfx_runtime* rt = nullptr;
-    if (nfx_runtime_create(model.c_str(), device, &rt) != NFX_OK) {
-        std::cerr << "runtime create failed: " << nfx_last_error() << std::endl;
+    std::unique_ptr<nflow::InferenceRuntime> rt;
+    st = nflow::InferenceRuntime::CreateOnDevice(model, device, rt);
+    if (!st.ok()) {
+        std::cerr << "runtime create failed: " << st.message() << std::endl;
         return 1;
     }
-    if (int8) nfx_runtime_enable_int8_gemm(rt);
-    if (fp8) nfx_runtime_enable_fp8(rt);
+    if (int8) rt->EnableInt8Gemm();
+    if (fp8) rt->EnableFp8();
     std::vector<int64_t> ys = xs;
     ys.back() = out_ch;
     int64_t ny = 1;
     for (auto d : ys) ny *= d;
     std::vector<float> y(static_cast<size_t>(ny));
-    const int s = ops == "TokenMixer2D"
-                      ? nfx_runtime_run_tokenmixer2d(rt, x.data(), xs.data(), rank, y.data(), ys.data(), rank)
-                      : nfx_runtime_run(rt, x.data(), xs.data(), rank, y.data(), ys.data(), rank);
-    if (s != NFX_OK) {
-        std::cerr << "inference failed: " << nfx_runtime_last_error(rt) << std::endl;
-        nfx_runtime_destroy(rt);
+    st = ops == "TokenMixer2D" ? rt->RunTokenMixer2D(x.data(), xs, y.data(), ys)
+                               : rt->Run(x.data(), xs, y.data(), ys);
+    if (!st.ok()) {
+        std::cerr << "inference failed: " << st.message() << std::endl;
         return 1;
     }
-    nfx_runtime_destroy(rt);
+    rt.reset();
     if (!write_npy(output, ys, y, err)) {
         std::cerr << "output write failed: " << err << std::endl;
         return 1;
