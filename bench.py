@@ -388,6 +388,19 @@ def run_nfx(args, ws, rank, local):
     e2e_s = max_over_ranks(e2e_s, ws, device)
     e2e = B * e2e_steps / e2e_s if e2e_steps else None
 
+    # the same with ordinary (pageable) numpy buffers, which the runtime stages through
+    # its own pinned memory (one GPU)
+    e2e_pageable = None
+    if e2e_steps and ws == 1:
+        xq = np.ascontiguousarray(x_host)
+        yq = np.zeros(tuple(dy.shape), np.float32)
+        for _ in range(max(1, args.warmup)):
+            rt.run(xq, yq)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            rt.run(xq, yq)
+        e2e_pageable = B * e2e_steps / max(time.perf_counter() - t0, 1e-9)
+
     result = None
     if rank == 0:
         hbm, src = peaks()
@@ -430,7 +443,9 @@ def run_nfx(args, ws, rank, local):
                               "samples)") if flush is None else
                              "L2 flushed between timed steps (256 MB write, untimed)"},
             "e2e": {"value": round(e2e, 1) if e2e else None, "unit": UNIT,
-                    "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(4 * B * P)},
+                    "h2d_bytes_per_step": int(x_host.nbytes), "d2h_bytes_per_step": int(4 * B * P),
+                    "host_buffers": "pinned",
+                    "pageable_value": round(e2e_pageable, 1) if e2e_pageable else None},
             "roofline": {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 3),
                          "peak_source": src, "traffic": traffic,

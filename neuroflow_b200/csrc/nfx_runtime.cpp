@@ -13,6 +13,7 @@
 #include <cstring>
 #include <memory>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/nfx.h"
@@ -21,6 +22,7 @@
 #include "fno3d.h"
 #include "nfx_internal.h"
 #include "nfx_ir.h"
+#include "nfx_copy_pool.h"
 #include "nfx_lut.h"
 #include "tm2d.h"
 
@@ -163,7 +165,13 @@ struct nfx_runtime {
     // host-buffer Run of a large batch: copies on their own streams, overlapped with
     // the compute of neighbouring batch chunks
     cudaStream_t s_h2d = nullptr, s_d2h = nullptr;
-    cudaEvent_t ev_in[8] = {}, ev_out[8] = {};
+    cudaEvent_t ev_in[8] = {}, ev_out[8] = {}, ev_done[8] = {};
+    // pageable caller buffers: pinned staging copies of x and y, filled and drained by
+    // a pool of host copy threads while the GPU works on neighbouring chunks
+    float* hx = nullptr;
+    float* hy = nullptr;
+    size_t hx_cap = 0, hy_cap = 0;
+    std::unique_ptr<nfx::CopyPool> pool;
     std::vector<void*> allocs;      // weights and tables (freed at destroy)
     // FNO2d state
     nfx::Fno2dPlan plan{};
@@ -1292,6 +1300,95 @@ int64_t numel(const int64_t* s, int r) {
     return n;
 }
 
+// Page-locked (pinned or registered) host memory, which the copy engines read and
+// write asynchronously; ordinary pageable memory is not.
+bool host_pinned(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost || a.type == cudaMemoryTypeManaged;
+}
+
+// Host-buffer Run for pageable x / y: per chunk, the copy pool moves the chunk's input
+// into pinned staging, the copy engine takes it to the device, the chunk computes, the
+// output comes back to pinned staging and the pool moves it to y.  The host copies of
+// chunk c + 1 overlap the device copies and compute of chunk c, and the output copies
+// of chunk c overlap the compute of the chunks after it.
+int staged_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank, float* y,
+               size_t nx, size_t ny, const int64_t* nbs, const int64_t* b0s, int nchunk) {
+    if (nx > rt->hx_cap) {
+        if (rt->hx) cudaFreeHost(rt->hx);
+        rt->hx = nullptr;
+        rt->hx_cap = 0;
+        if (!cuda_ok(rt, cudaHostAlloc(&rt->hx, nx * 4, cudaHostAllocDefault), "pinned staging"))
+            return NFX_INTERNAL;
+        rt->hx_cap = nx;
+    }
+    if (ny > rt->hy_cap) {
+        if (rt->hy) cudaFreeHost(rt->hy);
+        rt->hy = nullptr;
+        rt->hy_cap = 0;
+        if (!cuda_ok(rt, cudaHostAlloc(&rt->hy, ny * 4, cudaHostAllocDefault), "pinned staging"))
+            return NFX_INTERNAL;
+        rt->hy_cap = ny;
+    }
+    if (!rt->pool) {
+        const int hw = static_cast<int>(std::thread::hardware_concurrency());
+        rt->pool.reset(new nfx::CopyPool(std::max(0, std::min(7, hw / 2 - 1))));
+    }
+    const int64_t B = x_shape[0];
+    const size_t xs = nx / static_cast<size_t>(B), ys = ny / static_cast<size_t>(B);
+    int rc = NFX_OK;
+    int issued = 0, drained = 0;
+    auto drain = [&](int c) {
+        const size_t yo = static_cast<size_t>(b0s[c]) * ys, yn = static_cast<size_t>(nbs[c]) * ys;
+        rt->pool->copy(y + yo, rt->hy + yo, yn * 4);
+    };
+    for (int c = 0; c < nchunk && rc == NFX_OK; ++c) {
+        // outputs that have already arrived leave staging between the input copies
+        while (drained < issued && cudaEventQuery(rt->ev_done[drained]) == cudaSuccess) drain(drained++);
+        const size_t xo = static_cast<size_t>(b0s[c]) * xs, yo = static_cast<size_t>(b0s[c]) * ys;
+        const size_t xn = static_cast<size_t>(nbs[c]) * xs, yn = static_cast<size_t>(nbs[c]) * ys;
+        rt->pool->copy(rt->hx + xo, x + xo, xn * 4);
+        std::vector<int64_t> shp(x_shape, x_shape + x_rank);
+        shp[0] = nbs[c];
+        if (!cuda_ok(rt, cudaMemcpyAsync(rt->dx + xo, rt->hx + xo, xn * 4, cudaMemcpyHostToDevice, rt->s_h2d),
+                     "H2D") ||
+            !cuda_ok(rt, cudaEventRecord(rt->ev_in[c], rt->s_h2d), "event") ||
+            !cuda_ok(rt, cudaStreamWaitEvent(rt->stream, rt->ev_in[c], 0), "event wait")) {
+            rc = NFX_INTERNAL;
+            break;
+        }
+        rc = launch(rt, rt->dx + xo, shp.data(), rt->dy + yo, rt->stream);
+        if (rc != NFX_OK) break;
+        if (!cuda_ok(rt, cudaEventRecord(rt->ev_out[c], rt->stream), "event") ||
+            !cuda_ok(rt, cudaStreamWaitEvent(rt->s_d2h, rt->ev_out[c], 0), "event wait") ||
+            !cuda_ok(rt, cudaMemcpyAsync(rt->hy + yo, rt->dy + yo, yn * 4, cudaMemcpyDeviceToHost, rt->s_d2h),
+                     "D2H") ||
+            !cuda_ok(rt, cudaEventRecord(rt->ev_done[c], rt->s_d2h), "event")) {
+            rc = NFX_INTERNAL;
+            break;
+        }
+        issued = c + 1;
+    }
+    for (int c = drained; c < issued && rc == NFX_OK; ++c) {
+        if (!cuda_ok(rt, cudaEventSynchronize(rt->ev_done[c]), "output copy")) {
+            rc = NFX_INTERNAL;
+            break;
+        }
+        drain(c);
+    }
+    // every queued copy and kernel ends before Run returns, also on the error path
+    const bool synced = cuda_ok(rt, cudaStreamSynchronize(rt->s_h2d), "input copy") &&
+                        cuda_ok(rt, cudaStreamSynchronize(rt->stream), "execution") &&
+                        cuda_ok(rt, cudaStreamSynchronize(rt->s_d2h), "output copy");
+    if (rc != NFX_OK) return rc;
+    if (!synced) return NFX_INTERNAL;
+    return nfx_runtime_check(rt);
+}
+
 }  // namespace
 
 namespace nfx {
@@ -1468,7 +1565,11 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
     for (int i = 0; i < 8; ++i) {
         if (rt->ev_in[i]) cudaEventDestroy(rt->ev_in[i]);
         if (rt->ev_out[i]) cudaEventDestroy(rt->ev_out[i]);
+        if (rt->ev_done[i]) cudaEventDestroy(rt->ev_done[i]);
     }
+    if (rt->hx) cudaFreeHost(rt->hx);
+    if (rt->hy) cudaFreeHost(rt->hy);
+    rt->pool.reset();
     rt->timer.reset();
     delete rt;
 }
@@ -1616,14 +1717,19 @@ int nfx_runtime_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int
         b0s[0] = 0;
         for (int c = 1; c < nchunk; ++c) b0s[c] = b0s[c - 1] + nbs[c - 1];
     }
-    if (nchunk > 1 && !rt->s_h2d) {
+    // Pageable (ordinary) caller memory cannot feed the copy engines asynchronously:
+    // such buffers are staged through pinned copies (staged_run below).
+    const bool staged = !host_pinned(x) || !host_pinned(y);
+    if ((nchunk > 1 || staged) && !rt->s_h2d) {
         bool ok = cudaStreamCreateWithFlags(&rt->s_h2d, cudaStreamNonBlocking) == cudaSuccess &&
                   cudaStreamCreateWithFlags(&rt->s_d2h, cudaStreamNonBlocking) == cudaSuccess;
         for (int i = 0; i < 8 && ok; ++i)
             ok = cudaEventCreateWithFlags(&rt->ev_in[i], cudaEventDisableTiming) == cudaSuccess &&
-                 cudaEventCreateWithFlags(&rt->ev_out[i], cudaEventDisableTiming) == cudaSuccess;
+                 cudaEventCreateWithFlags(&rt->ev_out[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&rt->ev_done[i], cudaEventDisableTiming) == cudaSuccess;
         if (!ok) return rt_fail(rt, NFX_INTERNAL, "creating the copy streams failed");
     }
+    if (staged) return staged_run(rt, x, x_shape, x_rank, y, nx, ny, nbs, b0s, nchunk);
     if (nchunk == 1) {
         if (!cuda_ok(rt, cudaMemcpyAsync(rt->dx, x, nx * 4, cudaMemcpyHostToDevice, rt->stream), "H2D"))
             return NFX_INTERNAL;

@@ -130,19 +130,25 @@ def test_fno2d_int8_two_segment_code_table(tmp_path, scale, zp, W):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("B", [40, 130, 160, 300])
-def test_fno2d_host_run_chunked_matches_device_run(tmp_path, B):
+@pytest.mark.parametrize("pinned", [False, True])
+@pytest.mark.parametrize("B", [5, 40, 130, 160, 300])
+def test_fno2d_host_run_chunked_matches_device_run(tmp_path, B, pinned):
     """The host-buffer Run of a large batch overlaps copies and compute over batch
     chunks (2 halves below 4 q samples, q = SMs / gcd(SMs, 4); above, q / 2, 2q, ..., q:
-    4 chunks at 160 and 5 at 300 on 148 SMs); the result is bit-identical to one
-    device-buffer run of the whole batch."""
+    4 chunks at 160 and 5 at 300 on 148 SMs), reading pinned caller buffers directly and
+    staging pageable ones through the runtime's pinned buffers; the result is
+    bit-identical to one device-buffer run of the whole batch."""
     import torch
     from neuroflow_b200.runtime import InferenceRuntime
     m, path = _model(tmp_path, L=2)
     x = synth.fno2d_inputs(np.random.default_rng(31), B, 32, 32)
     rt = InferenceRuntime(path)
     rt.enable_int8_gemm()
-    got = np.zeros((B, 32, 32, 1), np.float32)
+    if pinned:
+        x = torch.from_numpy(x).pin_memory().numpy()
+        got = torch.zeros((B, 32, 32, 1), dtype=torch.float32).pin_memory().numpy()
+    else:
+        got = np.zeros((B, 32, 32, 1), np.float32)
     rt.run(x, got)
     dx = torch.from_numpy(x).cuda()
     dy = torch.empty((B, 32, 32, 1), dtype=torch.float32, device="cuda")
