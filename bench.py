@@ -476,7 +476,9 @@ AUX = {
                            "with per-token fake-quant for this IR; EnableInt8Gemm declines)"),
     "fno1d_int8": dict(metric="FNO1d INT8 samples/s", op="FNO1d", batch=64,
                        workload="configs[0] geometry with per-tensor activations: the reference's "
-                                "INT8 LinearForwardBatched dispatch (EnableInt8Gemm)"),
+                                "INT8 LinearForwardBatched dispatch (EnableInt8Gemm)",
+                       # 12 P + 14 P C with P = 1024, C = 64
+                       bytes_per_sample=12 * 1024 + 14 * 1024 * 64),
     "fno2d_fp32": dict(metric="FNO2d FP32 fake-quant samples/s", op="FNO2d", batch=256,
                        workload="configs[2] geometry without EnableInt8Gemm: the reference FNO2d "
                                 "Run (fp32 with fake-quant at the four .output boundaries)"),
@@ -485,7 +487,9 @@ AUX = {
                            "width 32, 8x8x8 modes, 4 layers)"),
     "fno3d_fp8": dict(metric="FNO3d FP8-E4M3 samples/s", op="FNO3d", batch=16,
                       workload="configs[3] FNO3d FP8-E4M3 per-tensor (E4M3 codes between "
-                               "layers, amax/448 scales from a 4-sample calibration batch)"),
+                               "layers, amax/448 scales from a 4-sample calibration batch)",
+                      # 20 P + 14 P C with P = 64^3, C = 32 (one-byte codes between layers)
+                      bytes_per_sample=20 * 64 ** 3 + 14 * 64 ** 3 * 32),
     "tm2d": dict(metric="TokenMixer2D FP32 samples/s", op="TokenMixer2D", batch=32,
                  workload="configs[4] TokenMixer2D, 64x64 grid = 4096 tokens, latent 128, "
                           "4 heads, 4 blocks (the reference RunTokenMixer2D arithmetic)"),
@@ -565,6 +569,12 @@ def run_aux(args):
             "data": "synthetic", "config": {"workload": spec["workload"], "batch": B},
             "kernel_share": {k: round(v[1] / tot, 3) for k, v in prof.items()},
             "gpu_launches": sum(v[0] for v in prof.values()), "clocks": clk.summary()}
+    if "bytes_per_sample" in spec:
+        hbm, src = peaks()
+        gbs = line["value"] * spec["bytes_per_sample"] / 1e9
+        line["network_roofline"] = {"bytes_per_sample": spec["bytes_per_sample"],
+                                    "achieved_GBps": round(gbs, 1), "peak": hbm,
+                                    "peak_source": src, "frac": round(gbs / hbm, 4)}
     print(json.dumps(line), flush=True)
 
 

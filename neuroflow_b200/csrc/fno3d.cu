@@ -28,6 +28,7 @@
 #include "fno3d.h"
 #include "nfx_internal.h"
 #include "numerics.cuh"
+#include "sm100.cuh"
 
 namespace nfx {
 namespace {
@@ -264,6 +265,200 @@ __global__ void __launch_bounds__(128) local3d_kernel(Fno3dPlan p, Fno3dLayer L,
     }
 }
 
+// ---------------------------------------------------------------------------
+// local3d_tc: the FP8 local layer on tensor cores (C = 32 or 64, tiles of 128 points
+// of one sample).  The layer input codes are channel-first (b, c, point), so a tile is
+// the MMA's A operand in MN-major layout: two TMA boxes of [C channels][64 points], one
+// per 64-point M atom (64-byte swizzle).  The weights are the E4M3 codes of the decoded
+// weights, a K-major [C out][C in] tile.  D = A W^T by tcgen05.mma.kind::f8f6f4 (E4M3 x
+// E4M3, fp32 accumulation) into one of four TMEM stages; the products are exact, the
+// tensor core's summation order is its own, so D may differ from the CUDA-core
+// kernel's k-order sum in the last bits (within the FP8 path's 1e-3 tolerance).
+//   warp 0      TMA producer (ring of A tiles)
+//   warp 1      MMA issuer
+//   warps 2-17  epilogue: four groups of four warps (one per TMEM lane quadrant) take
+//               turns over the tiles; per element dequantise + bias, E4M3 fake-quant,
+//               x1 + x2, the activation, the output code (as local3d_kernel).
+// ---------------------------------------------------------------------------
+template <int C>
+struct L3Cfg {
+    static constexpr int kGroups = 4;
+    static constexpr int kEpiWarps = 4 * kGroups;
+    static constexpr int kThreads = 32 * (2 + kEpiWarps);
+    static constexpr int kStages = 6;
+    static constexpr int kABytes = 128 * C;             // two [C][64] boxes
+    static constexpr int kAccStages = kGroups;
+    static constexpr int kTmemCols = kAccStages * C <= 128 ? 128 : 256;
+    static constexpr int kOffA = 0;
+    static constexpr int kOffW = kOffA + kStages * kABytes;
+    static constexpr int kOffBias = kOffW + ((C * C + 1023) / 1024) * 1024;
+    static constexpr int kOffBars = kOffBias + C * 4;
+    static constexpr int kNumBars = 2 * kStages + 2 * kAccStages;
+    static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
+};
+
+template <int C>
+__global__ void __launch_bounds__(L3Cfg<C>::kThreads, 1)
+local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, const Fno3dLayer L,
+                  uint8_t* __restrict__ hout, unsigned* err) {
+    using F = L3Cfg<C>;
+    static_assert(C == 32 || C == 64, "K = C must be a multiple of 32");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* sA = smem + F::kOffA;
+    uint8_t* sW = smem + F::kOffW;
+    float* sBias = reinterpret_cast<float*>(smem + F::kOffBias);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + F::kOffBars);
+    uint64_t* empty = full + F::kStages;
+    uint64_t* accFull = empty + F::kStages;
+    uint64_t* accEmpty = accFull + F::kAccStages;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(accEmpty + F::kAccStages);
+    volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t Pp = static_cast<int64_t>(p.Hp) * p.Wp * p.Dp;
+    const int tiles_per_sample = static_cast<int>(Pp / 128);
+    const int num_tiles = p.B * tiles_per_sample;
+    const int t_begin = static_cast<int>(static_cast<int64_t>(num_tiles) * blockIdx.x / gridDim.x);
+    const int t_end = static_cast<int>(static_cast<int64_t>(num_tiles) * (blockIdx.x + 1) / gridDim.x);
+
+    {
+        // weights: E4M3 codes of the decoded weights, K-major rows of C bytes, swizzled
+        for (int i = threadIdx.x; i < C * C; i += F::kThreads) {
+            const int o = i / C, k = i % C;
+            sW[swz_offset(o * C + k, C)] = static_cast<uint8_t>(e4m3_encode_ref(L.loc_q[i]));
+        }
+        for (int o = threadIdx.x; o < C; o += F::kThreads) sBias[o] = L.loc_b[o];
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < F::kStages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            for (int s = 0; s < F::kAccStages; ++s) {
+                mbar_init(&accFull[s], 1);
+                mbar_init(&accEmpty[s], 4);
+            }
+            *sAbort = 0;
+            fence_mbar_init();
+        }
+        if (warp == 1) tmem_alloc(sTmem, F::kTmemCols);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    const uint32_t tmem_base = *sTmem;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            prefetch_tmap(&tmIn);
+            int it = 0;
+            for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+                const int s = it % F::kStages;
+                const uint32_t ph = (it / F::kStages) & 1;
+                if (!mbar_wait_backoff(&empty[s], ph ^ 1, sAbort, 1024)) {
+                    *sAbort = 1;
+                    atomicOr(err, kErrWaitSlotFree);
+                    break;
+                }
+                const int b = tile / tiles_per_sample;
+                const int p0 = (tile - b * tiles_per_sample) * 128;
+                mbar_arrive_expect_tx(&full[s], F::kABytes);
+                tma_load_2d(sA + s * F::kABytes, &tmIn, &full[s], p0, b * C);
+                tma_load_2d(sA + s * F::kABytes + F::kABytes / 2, &tmIn, &full[s], p0 + 64, b * C);
+            }
+            for (int j = (it > F::kStages ? it - F::kStages : 0); j < it; ++j)
+                if (!mbar_wait_drain(&full[j % F::kStages], (j / F::kStages) & 1)) {
+                    atomicOr(err, kErrWaitDrain);
+                    break;
+                }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (elect_one()) {
+            constexpr uint32_t idesc = idesc_e4m3(C) | (1u << 15);  // A MN-major
+            int it = 0;
+            for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+                const int s = it % F::kStages;
+                const uint32_t ph = (it / F::kStages) & 1;
+                const int a = it % F::kAccStages;
+                const uint32_t aph = (it / F::kAccStages) & 1;
+                if (!mbar_wait_backoff(&accEmpty[a], aph ^ 1, sAbort, 128) ||
+                    !mbar_wait_backoff(&full[s], ph, sAbort, 128)) {
+                    *sAbort = 1;
+                    atomicOr(err, kErrWaitTmaFull);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t aBase = smem_u32(sA + s * F::kABytes);
+#pragma unroll
+                for (int kk = 0; kk < C / 32; ++kk)
+                    mma_f8(tmem_base + a * C, umma_desc_mn_sw64(aBase + kk * 2048, F::kABytes / 2, 512),
+                           umma_desc(smem_u32(sW) + kk * 32, C), idesc, kk > 0 ? 1u : 0u);
+                mma_commit(&empty[s]);
+                mma_commit(&accFull[a]);
+            }
+            if (it > 0) {
+                const int j = it - 1;
+                if (!mbar_wait_drain(&accFull[j % F::kAccStages], (j / F::kAccStages) & 1))
+                    atomicOr(err, kErrWaitDrain);
+            }
+        }
+        __syncwarp();
+    } else {
+        const int ew = warp - 2;
+        const int quad = warp & 3;
+        const int grp = ew >> 2;
+        const float sc = __fmul_rn(L.s_in, L.s_w);
+        const float inv_out = inv_of(L.s_out);
+        for (int it = grp; t_begin + it < t_end; it += F::kGroups) {
+            const int tile = t_begin + it;
+            const uint32_t aph = (it / F::kAccStages) & 1;
+            if (!mbar_wait(&accFull[grp], aph, sAbort)) {
+                *sAbort = 1;
+                atomicOr(err, kErrWaitAccFull);
+                break;
+            }
+            tc_fence_after();
+            const int b = tile / tiles_per_sample;
+            const int64_t pt = static_cast<int64_t>(tile - b * tiles_per_sample) * 128 + quad * 32 + lane;
+            const int64_t base = static_cast<int64_t>(b) * C * Pp + pt;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + grp * C;
+#pragma unroll 1
+            for (int h = 0; h < C / 32; ++h) {
+                uint32_t acc[32];
+                float x1v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) x1v[j] = __ldg(p.x1 + base + static_cast<int64_t>(32 * h + j) * Pp);
+                tmem_ld32(tbase + 32 * h, acc);
+                tmem_wait_ld();
+                if (h == C / 32 - 1) {
+                    // the accumulator stage is free once every TMEM read of it is done
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&accEmpty[grp]);
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int o = 32 * h + j;
+                    const float x2 = fp8_fake_quant(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[o]),
+                                                    L.s_out, inv_out);
+                    const float z = act_f(__fadd_rn(x1v[j], x2), p.act);
+                    hout[base + static_cast<int64_t>(o) * Pp] = static_cast<uint8_t>(e4m3_code(z, inv_out));
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, F::kTmemCols);
+    }
+}
+
 // projection, one unpadded point per thread
 template <int C>
 __global__ void __launch_bounds__(128) proj3d_kernel(Fno3dPlan p, const void* hin, float s_in) {
@@ -368,8 +563,32 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
             return e;
         if ((e = timed("fno3d_inv", [&] { inv3d_kernel<<<dim3(p.Hp, p.C, p.B), 256, si, st>>>(p); })) != cudaSuccess)
             return e;
-        if ((e = timed("fno3d_local", [&] { local3d_kernel<C><<<lgrid, 128, 0, st>>>(p, L, hin, hout); })) !=
-            cudaSuccess)
+        bool tc = false;
+        if constexpr (C == 32 || C == 64) {
+            // FP8: the local layer on tensor cores when a sample is whole 128-point tiles
+            if (p.fp8 && Pp % 128 == 0) {
+                using F = L3Cfg<C>;
+                CUtensorMap tm;
+                unsigned* err = device_error_word();
+                if (!err) return cudaErrorMemoryAllocation;
+                if (!encode_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, hin, static_cast<uint64_t>(Pp),
+                               static_cast<uint64_t>(p.B) * C, static_cast<uint64_t>(Pp), 64, C, 64))
+                    return cudaErrorInvalidValue;
+                auto k = local3d_tc_kernel<C>;
+                if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(k), F::kSmemBytes)) != cudaSuccess)
+                    return e;
+                const int64_t tiles = static_cast<int64_t>(p.B) * (Pp / 128);
+                const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
+                if ((e = timed("fno3d_local", [&] {
+                         k<<<grid, F::kThreads, F::kSmemBytes, st>>>(tm, p, L, static_cast<uint8_t*>(hout), err);
+                     })) != cudaSuccess)
+                    return e;
+                tc = true;
+            }
+        }
+        if (!tc &&
+            (e = timed("fno3d_local", [&] { local3d_kernel<C><<<lgrid, 128, 0, st>>>(p, L, hin, hout); })) !=
+                cudaSuccess)
             return e;
     }
     const int64_t tq = static_cast<int64_t>(p.B) * p.H * p.W * p.D;

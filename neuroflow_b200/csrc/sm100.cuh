@@ -283,6 +283,19 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64
         : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, FP8 x FP8 -> fp32 (formats in the instruction
+// descriptor; both E4M3 here).  One thread issues.
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+            d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+        : "memory");
+}
+
 // Arrive on `bar` once all previously issued tcgen05 ops of this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile(
@@ -352,6 +365,21 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t smem_addr, int row_bytes)
 __host__ __device__ constexpr uint32_t idesc_i8(int n) {
     return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
            (static_cast<uint32_t>(128 >> 4) << 24);
+}
+
+// kind::f8f6f4 with E4M3 A and B (format code 0), fp32 D, both K-major, M = 128
+// (set bit 15 for an MN-major A).
+__host__ __device__ constexpr uint32_t idesc_e4m3(int n) {
+    return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
+}
+
+// MN-major operand, 64-byte swizzle: atoms of 8 K rows x 64 bytes of M, `lbo` bytes
+// between M atoms, `sbo` bytes between groups of 8 K rows.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw64(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) |
+           (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) |
+           (static_cast<uint64_t>(4u) << 61);
 }
 
 // kind::tf32, fp32 D, both K-major, M = 128.

@@ -4,8 +4,11 @@ the reference runtime's FNO3d::Forward).
 FP32 path: the reference's transforms, contraction, Linear rounding; ReLU models are
 bit-identical, GELU models differ only through CUDA's tanhf.  FP8 E4M3 variant (no
 reference counterpart): the reference's own E4M3 encoder on the GPU, exact products
-of E4M3 codes summed in k order -- ReLU models bit-identical, GELU within the
-north-star FP8 tolerance of 1e-3 relative L2.
+of E4M3 codes.  At widths 8 and 16 the local layer sums them in k order on CUDA cores
+(ReLU models bit-identical); at widths 32 and 64 it runs on tensor cores
+(tcgen05.mma.kind::f8f6f4), whose summation order differs from the oracle's k order in
+the last bits, so those models are held to the north-star FP8 tolerance of 1e-3
+relative L2 (as are all GELU models).
 """
 import os
 
@@ -57,7 +60,11 @@ def test_fno3d_relu_bit_exact(tmp_path, kw, fp8):
     x = synth.fno3d_inputs(np.random.default_rng(1), 2, kw["S"], kw.get("in_ch", 4))
     want = Oracle().fno3d_forward(m, x, fp8=fp8)
     got = _run(p, x, 1, fp8)
-    assert np.array_equal(_bits(got), _bits(want)), float(np.abs(got - want).max())
+    if fp8 and kw["width"] >= 32:   # tensor-core local layer
+        print("fp8 tc rel", _rel(got, want), "moved", int(np.sum(got != want)), "of", got.size)
+        assert _rel(got, want) < 1e-3
+    else:
+        assert np.array_equal(_bits(got), _bits(want)), float(np.abs(got - want).max())
 
 
 @pytest.mark.gpu
@@ -83,6 +90,24 @@ def test_fno3d_configs3_blocks_gelu(tmp_path):
     got8 = _run(p, x, 1, fp8=True)
     print("fp8 rel", _rel(got8, want8), "fp8 vs fp32", _rel(want8, want))
     assert _rel(got8, want8) < 1e-3
+
+
+@pytest.mark.gpu
+def test_fno3d_fp8_configs3_grid():
+    """configs[3] itself: the benchmarked FP8 model (64^3 grid, width 32, 8x8x8 modes, 4
+    layers, scales from a 4-sample calibration batch), one of the benchmark's samples,
+    within 1e-3 relative L2 of the oracle."""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    path = bench.aux_model("fno3d_fp8")
+    m = ir.read(path)
+    x = synth.fno3d_inputs(np.random.default_rng(100), 1, 64)
+    want = Oracle().fno3d_forward(m, x, fp8=True)
+    got = _run(path, x, 1, fp8=True)
+    print("configs[3] fp8 rel", _rel(got, want), "moved", int(np.sum(got != want)), "of", got.size)
+    assert np.all(np.isfinite(got))
+    assert _rel(got, want) < 1e-3
 
 
 @pytest.mark.gpu
