@@ -220,6 +220,29 @@ int nfx_runtime_run_sharded_host(nfx_runtime* rt, nfx_comm* comm, const float* x
                                  const int64_t* x_shape, int x_rank, float* y,
                                  const int64_t* y_shape, int y_rank, int root);
 
+/* ---- Calibration on the GPU (neuroflow/quant/static_quant.py:609-741) ------------
+ * The reference calibrates by running its FP32 PyTorch model over a calibration set with
+ * hooks on every Linear and reducing the outputs on the host.  Here an FNO2d handle
+ * created from the FP32 IR (no EnableInt8Gemm) runs its FP32 executor over the batches
+ * with observers in the kernels, without fake-quant, and reduces on the GPU:
+ *   begin(keep_values)    reset; keep_values != 0 also keeps every value (percentiles)
+ *   observe(x)            one HOST batch (batch, h, w, in_ch), synchronous
+ *   count()               observed tensors: lift, locs.0 .. locs.L-1, proj_q, proj_out
+ *   result(i, pct, ...)   the tensor's ".output" key, its INT8 (scale, zero point) --
+ *                         compute_tensor_qparams (:480-533) for pct = 100, else the
+ *                         percentile rule of calibrate (:699-716) with numpy's linear
+ *                         percentiles of all kept values -- its FP8 E4M3 scale
+ *                         (compute_fp8_e4m3_qparams, :338-352), and the [lo, hi] used;
+ *                         a NaN value gives scale 1 and zero point 0
+ *   end()                 release the statistics and kept values. */
+int nfx_calibrate_begin(nfx_runtime* rt, int keep_values);
+int nfx_calibrate_observe(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank);
+int nfx_calibrate_count(const nfx_runtime* rt);
+int nfx_calibrate_result(nfx_runtime* rt, int index, double percentile, char* name_out, int name_cap,
+                         float* scale_out, int32_t* zero_point_out, float* fp8_scale_out,
+                         double* lo_out, double* hi_out);
+int nfx_calibrate_end(nfx_runtime* rt);
+
 /* ---- nflow-quant GEMM (cpp/include/neuroflow/int8_gemm.h) ----------------------- */
 
 /* W8A8 GEMM over activation CODES with one (scale, zero point) per row, per-channel

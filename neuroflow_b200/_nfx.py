@@ -105,6 +105,19 @@ if hasattr(lib, "nfx_runtime_create"):
     lib.nfx_runtime_run_sharded_host.restype = C.c_int
     lib.nfx_runtime_run_sharded_host.argtypes = [_vp, _vp, _vp, _i64p, C.c_int, _vp, _i64p,
                                                  C.c_int, C.c_int]
+    lib.nfx_calibrate_begin.restype = C.c_int
+    lib.nfx_calibrate_begin.argtypes = [_vp, C.c_int]
+    lib.nfx_calibrate_observe.restype = C.c_int
+    lib.nfx_calibrate_observe.argtypes = [_vp, _vp, _i64p, C.c_int]
+    lib.nfx_calibrate_count.restype = C.c_int
+    lib.nfx_calibrate_count.argtypes = [_vp]
+    lib.nfx_calibrate_result.restype = C.c_int
+    lib.nfx_calibrate_result.argtypes = [_vp, C.c_int, C.c_double, C.c_char_p, C.c_int,
+                                         C.POINTER(C.c_float), C.POINTER(C.c_int32),
+                                         C.POINTER(C.c_float), C.POINTER(C.c_double),
+                                         C.POINTER(C.c_double)]
+    lib.nfx_calibrate_end.restype = C.c_int
+    lib.nfx_calibrate_end.argtypes = [_vp]
 
 
 def batch_slice(batch: int, world: int, rank: int):

@@ -201,7 +201,15 @@ struct Fno2dF32Plan {
     float2* Xs;           // (B, C, MH, MW) truncated spectra
     float2* colinv;       // (B, C, Hp, MW) column-inverse transforms
     KernelTimer* timer;
+    // Calibration observers (nullptr: off).  Observed tensor i -- 0 lift, 1 + l locs.l,
+    // L + 1 proj_q, L + 2 proj_out, the Linear outputs before their fake-quant -- updates
+    // obs[i] (ordered-float key of the minimum), obs[kFno2dObsMax + i] (key of the
+    // maximum), obs[2 kFno2dObsMax + i] (nonzero after a NaN), and, when obs_vals[i] is
+    // set, stores every value at its channel-last element index in obs_vals[i].
+    unsigned* obs;
+    float* obs_vals[16];
 };
+constexpr int kFno2dObsMax = 16;
 
 // Geometry limits of the FP32 executor; returns nullptr or the reason it is unsupported.
 const char* fno2d_f32_unsupported(int C, int MH, int MW, int Hp, int Wp, int out_ch);

@@ -39,6 +39,33 @@ __device__ __forceinline__ float act_f(float z, int act) {
     return act == 1 ? relu_ref(z) : gelu_tanh(z);
 }
 
+// Calibration observer of one thread: the range of the values it saw, merged across
+// the warp and into the tensor's global keys at the end of the kernel.
+struct Obs {
+    float lo = INFINITY, hi = -INFINITY;
+    bool nan = false;
+    __device__ __forceinline__ void see(float v) {
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+        nan = nan || (v != v);
+    }
+    // whole warp
+    __device__ __forceinline__ void flush(unsigned* obs, int i) {
+        for (int o = 16; o > 0; o >>= 1) {
+            lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+            hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+        }
+        const bool any_nan = __any_sync(0xffffffffu, nan);
+        if ((threadIdx.x & 31) == 0) {
+            if (lo <= hi) {
+                atomicMin(obs + i, float_order_key(lo));
+                atomicMax(obs + kFno2dObsMax + i, float_order_key(hi));
+            }
+            if (any_nan) atomicOr(obs + 2 * kFno2dObsMax + i, 1u);
+        }
+    }
+};
+
 int ilog2(int v) {
     int l = 0;
     while ((1 << l) < v) ++l;
@@ -50,6 +77,7 @@ int ilog2(int v) {
 __global__ void __launch_bounds__(256) lift2d_f32_kernel(Fno2dF32Plan p) {
     const int64_t total = static_cast<int64_t>(p.B) * p.C * p.Hp * p.Wp;
     const int nu = linear_unfused_len(p.in_ch);
+    Obs ob;
     for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
          t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int ww = static_cast<int>(t % p.Wp);
@@ -64,10 +92,15 @@ __global__ void __launch_bounds__(256) lift2d_f32_kernel(Fno2dF32Plan p) {
             v = __ldg(p.lift_b + c);
             for (int k = 0; k < p.in_ch; ++k)
                 v = linear_step(v, __ldg(xr + k), __ldg(p.lift_w + c * p.in_ch + k), k >= nu);
+            if (p.obs) {
+                ob.see(v);
+                if (p.obs_vals[0]) p.obs_vals[0][((b * p.H + hh) * p.W + ww) * p.C + c] = v;
+            }
             v = apply_fq(v, p.fq_lift);
         }
         p.h[0][t] = v;
     }
+    if (p.obs) ob.flush(p.obs, 0);
 }
 
 // forward truncated Rfft2 of one (b, c) plane; 256 threads; shared memory
@@ -158,6 +191,9 @@ struct Layer2dArgs {
     const float* loc_b;
     FqParam fq;
     int Hp, Wp, C, MW, act;
+    unsigned* obs;        // calibration observers (Fno2dF32Plan::obs), tensor obs_i
+    float* obs_vals;
+    int obs_i;
 };
 
 __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
@@ -176,6 +212,7 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
     const float invW = __fdiv_rn(1.0f, static_cast<float>(Wp));
     const int nu = linear_unfused_len(C);
     const int nj = Wp / 32 > 0 ? Wp / 32 : 1;
+    Obs ob;
     for (int o0 = 0; o0 < C; o0 += kChunk) {
         // row pass of Irfft2 (fft.cpp:86-99) for kChunk output channels
         for (int r = warp; r < kChunk && o0 + r < C; r += 8) {
@@ -219,6 +256,10 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
             for (int j = 0; j < kMaxWp / 32; ++j) {
                 const int w = lane + 32 * j;
                 if (j < nj && w < Wp) {
+                    if (a.obs) {
+                        ob.see(acc[j]);
+                        if (a.obs_vals) a.obs_vals[((static_cast<int64_t>(b) * Hp + hh) * Wp + w) * C + o] = acc[j];
+                    }
                     const float x2 = apply_fq(acc[j], a.fq);
                     const float x1 = __fmul_rn(sX1[static_cast<size_t>(r) * Wp + w].x, invW);
                     dst[w] = act_f(__fadd_rn(x1, x2), a.act);
@@ -227,6 +268,7 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
         }
         __syncthreads();
     }
+    if (a.obs) ob.flush(a.obs, a.obs_i);
 }
 
 // projection (fno.cpp:966-993): one unpadded point per thread, its channel column
@@ -237,6 +279,8 @@ __global__ void __launch_bounds__(128) proj2d_f32_kernel(Fno2dF32Plan p, const f
     const int64_t total = static_cast<int64_t>(p.B) * p.H * p.W;
     const int C = p.C;
     const int nu = linear_unfused_len(C);
+    Obs obq, obo;
+    const int iq = p.L + 1, io = p.L + 2;
     for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
          t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int ww = static_cast<int>(t % p.W);
@@ -251,6 +295,10 @@ __global__ void __launch_bounds__(128) proj2d_f32_kernel(Fno2dF32Plan p, const f
             float q = __ldg(p.pq_b + c);
             const float* wr = p.pq_w + static_cast<int64_t>(c) * C;
             for (int k = 0; k < C; ++k) q = linear_step(q, mine[k], __ldg(wr + k), k >= nu);
+            if (p.obs) {
+                obq.see(q);
+                if (p.obs_vals[iq]) p.obs_vals[iq][t * C + c] = q;
+            }
             q = act_f(apply_fq(q, p.fq_pq), p.act);
 #pragma unroll
             for (int j = 0; j < 16; ++j)
@@ -260,7 +308,17 @@ __global__ void __launch_bounds__(128) proj2d_f32_kernel(Fno2dF32Plan p, const f
         float* yr = p.y + t * p.out_ch;
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-            if (j < p.out_ch) yr[j] = apply_fq(acc[j], p.fq_po);
+            if (j < p.out_ch) {
+                if (p.obs) {
+                    obo.see(acc[j]);
+                    if (p.obs_vals[io]) p.obs_vals[io][t * p.out_ch + j] = acc[j];
+                }
+                yr[j] = apply_fq(acc[j], p.fq_po);
+            }
+    }
+    if (p.obs) {
+        obq.flush(p.obs, iq);
+        obo.flush(p.obs, io);
     }
 }
 
@@ -331,6 +389,9 @@ cudaError_t fno2d_f32_run(const Fno2dF32Plan& p, cudaStream_t st) {
         a.loc_w = L.loc_w;
         a.loc_b = L.loc_b;
         a.fq = L.fq;
+        a.obs = p.obs;
+        a.obs_vals = p.obs ? p.obs_vals[1 + i] : nullptr;
+        a.obs_i = 1 + i;
         a.Hp = p.Hp;
         a.Wp = p.Wp;
         a.C = p.C;

@@ -187,6 +187,11 @@ struct nfx_runtime {
     long long* fwd_sum_b = nullptr;
     int8_t* tap_codes = nullptr;      // caller's parity-tap buffer (nfx_runtime_set_code_taps)
     int64_t tap_cap = 0;
+    // GPU calibration (nfx_calibrate_*): range keys of every observed Linear output,
+    // and, when values are kept, one device chunk per tensor and observed batch
+    unsigned* calib_stats = nullptr;
+    int calib_keep = 0;
+    std::vector<std::vector<std::pair<float*, int64_t>>> calib_vals;
     // FNO2d FP32 (reference fake-quant) state
     nfx::Fno2dF32Plan plan2f{};
     void* f2_bufs[4] = {nullptr, nullptr, nullptr, nullptr};  // h0, h1, Xs, colinv
@@ -637,8 +642,10 @@ int ensure_f2_buf(nfx_runtime* rt, int i, int64_t bytes) {
     return NFX_OK;
 }
 
-// FNO2d without EnableInt8Gemm: the reference's FP32 fake-quant network
-int fno2d_f32_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
+// FNO2d without EnableInt8Gemm: the reference's FP32 fake-quant network.  With `obs`
+// (calibration), the Linear outputs are observed and no fake-quant is applied.
+int fno2d_f32_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st,
+                     unsigned* obs = nullptr, float* const* obs_vals = nullptr) {
     const F2 c = fno2d_cfg(rt->model);
     auto& pl0 = rt->plan2f;
     if (!pl0.lift_w)
@@ -695,6 +702,14 @@ int fno2d_f32_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float*
     pl.Xs = static_cast<float2*>(rt->f2_bufs[2]);
     pl.colinv = static_cast<float2*>(rt->f2_bufs[3]);
     pl.timer = rt->timer.get();
+    pl.obs = obs;
+    for (int i = 0; i < nfx::kFno2dObsMax; ++i) pl.obs_vals[i] = obs && obs_vals ? obs_vals[i] : nullptr;
+    if (obs) {
+        pl.fq_lift.kind = 0;
+        pl.fq_pq.kind = 0;
+        pl.fq_po.kind = 0;
+        for (int i = 0; i < pl.L && i < nfx::kFno2dMaxLayers; ++i) pl.layer[i].fq.kind = 0;
+    }
     const cudaError_t e = nfx::fno2d_f32_run(pl, st);
     if (e != cudaSuccess)
         return rt_fail(rt, NFX_INTERNAL, std::string("FNO2d launch failed: ") + cudaGetErrorString(e));
@@ -1319,7 +1334,10 @@ bool host_pinned(const void* p) {
 int staged_run(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank, float* y,
                size_t nx, size_t ny, const int64_t* nbs, const int64_t* b0s, int nchunk) {
     if (nx > rt->hx_cap) {
-        if (rt->hx) cudaFreeHost(rt->hx);
+        if (rt->calib_stats) cudaFree(rt->calib_stats);
+    for (auto& t : rt->calib_vals)
+        for (auto& c : t) cudaFree(c.first);
+    if (rt->hx) cudaFreeHost(rt->hx);
         rt->hx = nullptr;
         rt->hx_cap = 0;
         if (!cuda_ok(rt, cudaHostAlloc(&rt->hx, nx * 4, cudaHostAllocDefault), "pinned staging"))
@@ -1434,6 +1452,71 @@ int runtime_staging(nfx_runtime* rt, size_t nx, size_t ny, float** dx, float** d
 }
 
 int runtime_fail_str(nfx_runtime* rt, int code, const std::string& msg) { return rt_fail(rt, code, msg); }
+
+// ---- calibration (nfx_calib.cu) --------------------------------------------------
+// Observed tensors of an FNO2d handle: lift, locs.0 .. locs.L-1, proj_q, proj_out.
+int calib_tensors(const nfx_runtime* rt) {
+    if (rt->model.op != "FNO2d") return 0;
+    return fno2d_cfg(rt->model).L + 3;
+}
+
+std::string calib_name(const nfx_runtime* rt, int i) {
+    const int L = fno2d_cfg(rt->model).L;
+    if (i == 0) return "lift.output";
+    if (i <= L) return "locs." + std::to_string(i - 1) + ".output";
+    return i == L + 1 ? "proj_q.output" : "proj_out.output";
+}
+
+unsigned*& calib_stats(nfx_runtime* rt) { return rt->calib_stats; }
+int& calib_keep(nfx_runtime* rt) { return rt->calib_keep; }
+std::vector<std::vector<std::pair<float*, int64_t>>>& calib_vals(nfx_runtime* rt) { return rt->calib_vals; }
+
+// One calibration batch (host x): the FP32 network without fake-quant, observing every
+// Linear output; with kept values, each tensor's values go to a new device chunk.
+int calib_observe(nfx_runtime* rt, const float* x, const int64_t* xs, int xr) {
+    if (rt->model.op != "FNO2d" || rt->int8_enabled)
+        return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                       "calibration observes the FP32 FNO2d network: create the runtime without "
+                       "EnableInt8Gemm");
+    if (!rt->calib_stats) return rt_fail(rt, NFX_INVALID_ARG, "call nfx_calibrate_begin first");
+    const F2 c = fno2d_cfg(rt->model);
+    if (!xs || xr != 4) return rt_fail(rt, NFX_SHAPE_MISMATCH, "expected 4D input (batch, h, w, in_ch)");
+    const int64_t ys[4] = {xs[0], xs[1], xs[2], c.out_ch};
+    int s = check_fno2d_shapes(rt, xs, xr, ys, 4);
+    if (s != NFX_OK) return s;
+    const int64_t B = xs[0], H = xs[1], W = xs[2];
+    if (B == 0) return NFX_OK;
+    if (!x) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
+    int64_t Hp = H, Wp = W;
+    if (c.pad > 1) {
+        Hp = H + (c.pad - H % c.pad) % c.pad;
+        Wp = W + (c.pad - W % c.pad) % c.pad;
+    }
+    const size_t nx = static_cast<size_t>(B * H * W * c.in_ch), ny = static_cast<size_t>(B * H * W * c.out_ch);
+    float* dx = nullptr;
+    float* dy = nullptr;
+    s = nfx::runtime_staging(rt, nx, ny, &dx, &dy);
+    if (s != NFX_OK) return s;
+    float* vals[kFno2dObsMax] = {};
+    const int n = c.L + 3;
+    if (rt->calib_keep) {
+        for (int i = 0; i < n; ++i) {
+            const int64_t cnt = i == 0 ? B * H * W * c.width
+                                : i <= c.L ? B * Hp * Wp * c.width
+                                : i == c.L + 1 ? B * H * W * c.width : B * H * W * c.out_ch;
+            void* p = nullptr;
+            if (!cuda_ok(rt, cudaMalloc(&p, static_cast<size_t>(cnt) * 4), "cudaMalloc calibration values"))
+                return NFX_INTERNAL;
+            vals[i] = static_cast<float*>(p);
+            rt->calib_vals[i].push_back({vals[i], cnt});
+        }
+    }
+    if (!cuda_ok(rt, cudaMemcpyAsync(dx, x, nx * 4, cudaMemcpyHostToDevice, rt->stream), "H2D")) return NFX_INTERNAL;
+    s = fno2d_f32_launch(rt, dx, xs, dy, rt->stream, rt->calib_stats, vals);
+    if (s != NFX_OK) return s;
+    if (!cuda_ok(rt, cudaStreamSynchronize(rt->stream), "calibration batch")) return NFX_INTERNAL;
+    return nfx_runtime_check(rt);
+}
 
 int fno2d_noalloc_plan(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
                        float* y, const int64_t* y_shape, int y_rank, Fno2dPlan* plan) {
@@ -1567,6 +1650,9 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
         if (rt->ev_out[i]) cudaEventDestroy(rt->ev_out[i]);
         if (rt->ev_done[i]) cudaEventDestroy(rt->ev_done[i]);
     }
+    if (rt->calib_stats) cudaFree(rt->calib_stats);
+    for (auto& t : rt->calib_vals)
+        for (auto& c : t) cudaFree(c.first);
     if (rt->hx) cudaFreeHost(rt->hx);
     if (rt->hy) cudaFreeHost(rt->hy);
     rt->pool.reset();

@@ -104,6 +104,28 @@ __device__ __forceinline__ float fp8_log2_snap(float v, float scale) {
     return __fmul_rn(__fmul_rn(sign, fminf(qv, 448.0f)), scale);
 }
 
+// A float's bits mapped to an unsigned key with the same order (negative values
+// reversed), so that atomicMin / atomicMax on keys are min / max on the floats.
+__host__ __device__ __forceinline__ unsigned float_order_key(float v) {
+#ifdef __CUDA_ARCH__
+    const unsigned u = __float_as_uint(v);
+#else
+    unsigned u;
+    memcpy(&u, &v, 4);
+#endif
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__host__ __device__ __forceinline__ float float_from_order_key(unsigned k) {
+    const unsigned u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(u);
+#else
+    float v;
+    memcpy(&v, &u, 4);
+    return v;
+#endif
+}
+
 // fp8_e4m3.h:106-221 fp32_to_e4m3_bits, the reference's encoder: NaN -> 0x7F, +-inf ->
 // +-448, round-half-even of the mantissa to 3 bits with exponent carry and saturation
 // to +-448; below the normal range round(|v| * 2^9) clamped to [0, 7] (so values in

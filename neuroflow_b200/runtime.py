@@ -145,6 +145,36 @@ class InferenceRuntime:
             raise RuntimeError("device error: " + self._err())
 
 
+    # -- calibration on the GPU (nfx_calibrate_*) --------------------------------------
+    def calibrate_begin(self, keep_values: bool = False) -> None:
+        rc = _lib.nfx_calibrate_begin(self._h, int(bool(keep_values)))
+        if rc != 0:
+            raise RuntimeError("calibration failed: " + self._err())
+
+    def calibrate_observe(self, x: np.ndarray) -> None:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rc = _lib.nfx_calibrate_observe(self._h, x.ctypes.data_as(C.c_void_p), _shape(x), x.ndim)
+        if rc != 0:
+            raise RuntimeError("calibration failed: " + self._err())
+
+    def calibrate_results(self, percentile: float = 100.0) -> dict:
+        """{".output" key: (scale, zero_point, fp8_scale, lo, hi)} of every observed
+        Linear output."""
+        out = {}
+        for i in range(_lib.nfx_calibrate_count(self._h)):
+            name = C.create_string_buffer(64)
+            sc, zp, f8 = C.c_float(), C.c_int32(), C.c_float()
+            lo, hi = C.c_double(), C.c_double()
+            rc = _lib.nfx_calibrate_result(self._h, i, float(percentile), name, 64, C.byref(sc),
+                                           C.byref(zp), C.byref(f8), C.byref(lo), C.byref(hi))
+            if rc != 0:
+                raise RuntimeError("calibration failed: " + self._err())
+            out[name.value.decode()] = (sc.value, zp.value, f8.value, lo.value, hi.value)
+        return out
+
+    def calibrate_end(self) -> None:
+        _lib.nfx_calibrate_end(self._h)
+
     def run_sharded(self, comm: "Comm", x, y, root: int = -1, stream=None) -> None:
         """Batch partitioned over the ranks of `comm` (one process per GPU): x, y are the
         WHOLE batch as CUDA tensors on this runtime's device; this rank computes its

@@ -98,7 +98,8 @@ class _FNO3d(C.Structure):
 
 class _Taps(C.Structure):
     _fields_ = [("codes_in", _i8p * (MAX_LAYERS + 1)), ("x1_out", _f32p * MAX_LAYERS),
-                ("h_out", _f32p * MAX_LAYERS)]
+                ("h_out", _f32p * MAX_LAYERS), ("lift_out", _f32p), ("x2_out", _f32p * MAX_LAYERS),
+                ("q_out", _f32p)]
 
 
 class Oracle:
@@ -239,13 +240,23 @@ class Oracle:
                 a = np.zeros((B, H, W, w), np.int8)
                 tap_arrays[f"codes_in.{i}"] = a
                 tp.codes_in[i] = _p(a, _i8p)
+            pf = cfg.get("pad_factor", 0)
+            Hp = H + ((pf - H % pf) % pf if pf > 1 else 0)
+            Wp = W + ((pf - W % pf) % pf if pf > 1 else 0)
             for i in range(L):
-                a = np.zeros((B, w, H, W), np.float32)
+                a = np.zeros((B, w, Hp, Wp), np.float32)
                 tap_arrays[f"x1.{i}"] = a
                 tp.x1_out[i] = _p(a)
-                a = np.zeros((B, H, W, w), np.float32)
+                a = np.zeros((B, Hp, Wp, w), np.float32)
                 tap_arrays[f"h.{i}"] = a
                 tp.h_out[i] = _p(a)
+                a = np.zeros((B, Hp, Wp, w), np.float32)
+                tap_arrays[f"x2.{i}"] = a
+                tp.x2_out[i] = _p(a)
+            for key in ("lift_out", "q_out"):
+                a = np.zeros((B, H, W, w), np.float32)
+                tap_arrays[key] = a
+                setattr(tp, key, _p(a))
         rc = self.lib.nfo_fno2d_forward(C.byref(st), int(mode), _p(x), B, H, W, _p(y),
                                         C.byref(tp) if tp is not None else None)
         if rc != 0:

@@ -627,11 +627,17 @@ static void apply_input_fq(float* data, int64_t numel, const nfo_aq* a, int quan
 /* Optional per-layer taps for layer-wise parity checks (may be NULL):
  * codes_in[i]  : int8 codes of the layer-i input (channel-last), int8 mode only
  * x1_out[i]    : spectral branch output, channel-first (b, w, H, W)
- * h_out[i]     : layer-i output after the activation, channel-last (b, H, W, w) */
+ * h_out[i]     : layer-i output after the activation, channel-last (b, H, W, w)
+ * Linear outputs before their fake-quant -- what calibrate()'s hooks observe
+ * (neuroflow/quant/static_quant.py:656-668): lift_out (b, H, W, w), x2_out[i] the
+ * local Linear of layer i (b, Hp, Wp, w), q_out proj_q (b, H, W, w); proj_out's is y. */
 typedef struct {
     int8_t* codes_in[NFO_MAX_LAYERS + 1];
     float* x1_out[NFO_MAX_LAYERS];
     float* h_out[NFO_MAX_LAYERS];
+    float* lift_out;
+    float* x2_out[NFO_MAX_LAYERS];
+    float* q_out;
 } nfo_taps;
 
 /* mode 0: fno.cpp:777-995 with the Create-time weight fake-quant (fno.cpp:997-1020).
@@ -703,6 +709,7 @@ int nfo_fno2d_forward(const nfo_fno2d* m, int mode, const float* x, int bsz, int
 
     float* h = (float*)calloc((size_t)(M * w), sizeof(float));        /* (b,H,W,w) */
     nfo_linear(x, lift_w, lift_b, (int)M, in_ch, w, h);
+    if (taps && taps->lift_out) memcpy(taps->lift_out, h, sizeof(float) * M * w);
     apply_fq(h, M * w, &m->a_lift, m->quant_enabled);
 
     float* h_perm = (float*)calloc((size_t)(M * w), sizeof(float));   /* (b,w,H,W) */
@@ -758,6 +765,7 @@ int nfo_fno2d_forward(const nfo_fno2d* m, int mode, const float* x, int bsz, int
         } else {
             nfo_linear(pin, lw[i], lb[i], (int)Mp, w, w, pout);
         }
+        if (taps && taps->x2_out[i]) memcpy(taps->x2_out[i], pout, sizeof(float) * Mp * w);
         for (int64_t bi = 0; bi < bsz; ++bi)
             for (int wi = 0; wi < w; ++wi)
                 for (int64_t hi = 0; hi < H; ++hi)
@@ -809,6 +817,7 @@ int nfo_fno2d_forward(const nfo_fno2d* m, int mode, const float* x, int bsz, int
     } else {
         nfo_linear(h_back, pq_w, pq_b, (int)M, w, w, q);
     }
+    if (taps && taps->q_out) memcpy(taps->q_out, q, sizeof(float) * M * w);
     apply_fq(q, M * w, &m->a_proj_q, m->quant_enabled);
     nfo_apply_activation(q, M * w, m->relu);
     nfo_linear(q, po_w, po_b, (int)M, w, out_ch, y);

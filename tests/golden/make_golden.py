@@ -13,6 +13,8 @@ What it writes (small files, committed):
   fno2d_q.npz           input x, the reference C++ runtime's output y (fake-quant FP32
                         FNO2d, oracle/_ref), and the reference Python qparams
   fno2d_plain.nneuroir  the same model without NIRQ, with its runtime output
+  calib.npz             its calibration batch and the reference's calibration of it with
+                        the 99th-percentile rule and FP8 E4M3 scales (quantise_model)
   fno1d_pt.nneuroir     a tiny FNO1d (width 16, 6 modes, 2 layers, n = 64) calibrated with
                         `quantise_model(per_channel_weights=True,
                         per_token_activations=True)` (NIRQ kind 2) and exported by
@@ -88,6 +90,15 @@ def main():
                         act_keys=np.array(sorted(act)),
                         act_scale=np.array([act[k][0] for k in sorted(act)], np.float32),
                         act_zp=np.array([act[k][1] for k in sorted(act)], np.int32))
+    # the same model's calibration by the reference: its calibration batch, min/max
+    # (above), the 99th-percentile rule and the FP8 E4M3 scales
+    qm99 = quantise_model(model, [calib], per_channel_weights=True, per_token_activations=False,
+                          percentile=99.0, fp8_activations=True)
+    keys = sorted(qm99.activation_qparams)
+    np.savez_compressed(os.path.join(HERE, "calib.npz"), calib=calib.numpy(), keys=np.array(keys),
+                        p99_scale=np.array([qm99.activation_qparams[k].scale for k in keys], np.float32),
+                        p99_zp=np.array([qm99.activation_qparams[k].zero_point for k in keys], np.int32),
+                        fp8_scale=np.array([qm99.fp8_qparams[k].scale for k in keys], np.float32))
 
     # --- FNO1d, per-token and per-tensor activations ------------------------------
     torch.manual_seed(1)
