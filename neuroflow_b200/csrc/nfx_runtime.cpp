@@ -207,7 +207,7 @@ struct nfx_runtime {
     int f3_tw_dims[3] = {0, 0, 0};
     // TokenMixer2D state
     nfx::Tm2dPlan plan_tm{};
-    void* tm_bufs[12] = {};
+    void* tm_bufs[13] = {};
     int64_t tm_cap_T = 0, tm_cap_P = 0;
     // FNO1d state
     nfx::Fno1dPlan plan1{};
@@ -1253,9 +1253,10 @@ int tm2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, 
             if (p) cudaFree(p);
             p = nullptr;
         }
-        const int64_t sizes[12] = {T * pl0.in_d * 4, T * L * 4, T * L * 4, T * L * 4, T * L * 4, T * L * 4,
-                                   T * L * 4, T * 2 * L * 4, T * L * 4, P * L * 4, T * 2 * L, T * 8};
-        for (int i = 0; i < 12; ++i)
+        const int64_t sizes[13] = {T * pl0.in_d * 4, T * L * 4, T * L * 4, T * L * 4, T * L * 4, T * L * 4,
+                                   T * L * 4, T * 2 * L * 4, T * L * 4, P * L * 4, T * 2 * L, T * 8,
+                                   6 * T * L * 4};
+        for (int i = 0; i < 13; ++i)
             if (!cuda_ok(rt, cudaMalloc(&rt->tm_bufs[i], static_cast<size_t>(sizes[i]) + 256), "cudaMalloc activations"))
                 return NFX_INTERNAL;
         rt->tm_cap_T = T;
@@ -1270,6 +1271,10 @@ int tm2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, 
     pl.codes = static_cast<int8_t*>(rt->tm_bufs[10]);
     pl.row_s = static_cast<float*>(rt->tm_bufs[11]);
     pl.row_zp = reinterpret_cast<int32_t*>(static_cast<char*>(rt->tm_bufs[11]) + T * 4);
+    pl.qkv_split = static_cast<float*>(rt->tm_bufs[12]);
+    // attention on tensor cores (3xTF32, fp32-accurate; head dim 32); the FP32 path's
+    // outputs stay within rtol 1e-5 of the reference-order attention
+    pl.tc_attention = 1;
     pl.err = nfx::device_error_word();
     if (!pl.err) return rt_fail(rt, NFX_INTERNAL, "no device error word");
     pl.timer = rt->timer.get();

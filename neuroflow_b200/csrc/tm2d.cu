@@ -18,6 +18,10 @@
 //               and the activation codes (QuantiseActivation, int8_gemm.cpp:507-520)
 //   attention_online  INT8 path: one pass over the keys with an online softmax and
 //               fused multiply-adds (fp32-accurate, not the reference's order)
+//   attention_tc  head dim 32, both paths: the same attention on tensor cores (3xTF32
+//               tcgen05 MMAs, TMEM accumulators, online softmax); fp32-accurate, not the
+//               reference's summation order -- the FP32 network stays within rtol 1e-5
+//               of the reference's
 //
 // Approximate operations: CUDA's expf in the softmax and tanhf in GELU (a few ulps
 // from glibc's); everything else is bit-identical to the reference arithmetic.
@@ -29,6 +33,7 @@
 
 #include "nfx_internal.h"
 #include "numerics.cuh"
+#include "sm100.cuh"
 #include "tm2d.h"
 
 namespace nfx {
@@ -434,11 +439,362 @@ LinArgs lin(const float* A, int64_t M, int K, const float* W, const float* b, in
     return a;
 }
 
+// ---------------------------------------------------------------------------
+// attention_tc (head dim 32): softmax(Q K^T * scale) V on tensor cores in 3xTF32, one
+// CTA per (128 queries, head, sample), keys in tiles of 64 (a flash-attention
+// schedule: no n x n matrix).  Every operand x is held as the tf32 pair
+// hi = x with its 13 low mantissa bits cleared and lo = x - hi (split_qkv_kernel for
+// Q, K, V; the softmax warps for P), and each product as hi*hi + lo*hi + hi*lo
+// (about 2^-21 relative error).
+//   warp 0      TMA: the Q pair once, then K and V pairs of each key tile (ring of 2)
+//   warp 1      MMA issuer: S_j = Q K_j^T into one of two TMEM buffers (64 columns),
+//               O_j = P_j V_j into one of two TMEM buffers (32 columns)
+//   warps 2-5   softmax, one query row per thread (TMEM lane): the row max, the
+//               exponentials exp2((s - m) scale log2 e), the running sum, P_j written
+//               to shared memory as the A operand, V_j transposed into the K-major B
+//               operand (an MN-major tf32 operand would need the 32-byte-atom swizzle),
+//               and O accumulated in registers with the online rescaling; O / sum is
+//               written at the end.
+// The result equals softmax attention to fp32 accuracy but not in the reference's
+// summation order (fno.cpp:1441-1456, 1919-1929), which attention_kernel keeps.
+// ---------------------------------------------------------------------------
+struct AttnCfg {
+    static constexpr int kQT = 128;                  // queries per CTA
+    static constexpr int kKT = 64;                   // keys per tile
+    static constexpr int kQBytes = kQT * 128;        // [128 rows][32 f32], SW128
+    static constexpr int kKVBytes = kKT * 128;       // [64 rows][32 f32], SW128
+    static constexpr int kStages = 2;
+    static constexpr int kStageBytes = 4 * kKVBytes; // K hi, K lo, V hi, V lo
+    static constexpr int kPBlk = kQT * 128;          // [128 rows][32 keys] f32, SW128
+    static constexpr int kPBytes = 2 * kPBlk;        // 64 keys = two K blocks
+    static constexpr int kOffQ = 0;                  // Q hi, Q lo
+    static constexpr int kOffKV = 2 * kQBytes;
+    static constexpr int kOffP = kOffKV + kStages * kStageBytes;  // P hi, P lo
+    static constexpr int kVtBlk = 32 * 128;          // V^T [32 dims][32 keys] f32, SW128
+    static constexpr int kVtBytes = 2 * kVtBlk;      // 64 keys
+    static constexpr int kOffVt = kOffP + 2 * kPBytes;             // V^T hi, V^T lo
+    static constexpr int kOffBars = kOffVt + 2 * kVtBytes;
+    static constexpr int kSmemBytes = kOffBars + 256 + 1024;
+    static constexpr int kThreads = 192;
+    static constexpr int kTmemCols = 256;            // S 2 x 64 at 0, O 2 x 32 at 128
+};
+
+// hi / lo tf32 pairs of q, k and v (T rows x L): hi keeps the top 10 mantissa bits
+__global__ void __launch_bounds__(256) split_qkv_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                                        const float* __restrict__ v, int64_t n,
+                                                        float* __restrict__ out) {
+    const float* src[3] = {q, k, v};
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+#pragma unroll
+        for (int t = 0; t < 3; ++t) {
+            const float x = src[t][i];
+            const float hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+            out[(2 * t) * n + i] = hi;
+            out[(2 * t + 1) * n + i] = __fsub_rn(x, hi);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(AttnCfg::kThreads, 1)
+attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
+                    const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
+                    const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl, int NP,
+                    int L, float scale, float* __restrict__ out, unsigned* err) {
+    using F = AttnCfg;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* sQ = smem + F::kOffQ;
+    uint8_t* sKV = smem + F::kOffKV;
+    uint8_t* sP = smem + F::kOffP;
+    uint8_t* sVt = smem + F::kOffVt;
+    uint64_t* qFull = reinterpret_cast<uint64_t*>(smem + F::kOffBars);
+    uint64_t* kvFull = qFull + 1;
+    uint64_t* kvEmpty = kvFull + F::kStages;
+    uint64_t* sFull = kvEmpty + F::kStages;
+    uint64_t* sFree = sFull + 2;
+    uint64_t* pReady = sFree + 2;
+    uint64_t* oFull = pReady + 1;
+    uint64_t* oFree = oFull + 2;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(oFree + 2);
+    volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.z, head = blockIdx.y, q0 = blockIdx.x * F::kQT;
+    const int row0 = b * NP;
+    const int nt = (NP + F::kKT - 1) / F::kKT;
+
+    if (threadIdx.x == 0) {
+        mbar_init(qFull, 1);
+        for (int s = 0; s < F::kStages; ++s) {
+            mbar_init(&kvFull[s], 1);
+            mbar_init(&kvEmpty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&sFull[s], 1);
+            mbar_init(&sFree[s], 4);
+            mbar_init(&oFull[s], 1);
+            mbar_init(&oFree[s], 4);
+        }
+        mbar_init(pReady, 4);
+        *sAbort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(sTmem, F::kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *sTmem;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            prefetch_tmap(&tmQh);
+            prefetch_tmap(&tmKh);
+            mbar_arrive_expect_tx(qFull, 2 * F::kQBytes);
+            tma_load_2d(sQ, &tmQh, qFull, head * 32, row0 + q0);
+            tma_load_2d(sQ + F::kQBytes, &tmQl, qFull, head * 32, row0 + q0);
+            int j = 0;
+            for (; j < nt; ++j) {
+                const int s = j % F::kStages;
+                if (!mbar_wait_backoff(&kvEmpty[s], ((j / F::kStages) & 1) ^ 1, sAbort, 512)) {
+                    *sAbort = 1;
+                    atomicOr(err, kErrWaitSlotFree);
+                    break;
+                }
+                uint8_t* st = sKV + s * F::kStageBytes;
+                const int y = row0 + j * F::kKT;
+                mbar_arrive_expect_tx(&kvFull[s], F::kStageBytes);
+                tma_load_2d(st, &tmKh, &kvFull[s], head * 32, y);
+                tma_load_2d(st + F::kKVBytes, &tmKl, &kvFull[s], head * 32, y);
+                tma_load_2d(st + 2 * F::kKVBytes, &tmVh, &kvFull[s], head * 32, y);
+                tma_load_2d(st + 3 * F::kKVBytes, &tmVl, &kvFull[s], head * 32, y);
+            }
+            // every load issued lands before the CTA leaves
+            if (!mbar_wait_drain(qFull, 0)) atomicOr(err, kErrWaitDrain);
+            for (int i = (j > F::kStages ? j - F::kStages : 0); i < j; ++i)
+                if (!mbar_wait_drain(&kvFull[i % F::kStages], (i / F::kStages) & 1)) {
+                    atomicOr(err, kErrWaitDrain);
+                    break;
+                }
+        }
+        __syncwarp();
+    }
+    else if (warp == 1) {
+        if (elect_one()) {
+            constexpr uint32_t idS = idesc_tf32(F::kKT);          // A, B K-major
+            constexpr uint32_t idO = idesc_tf32(32);                // B = V^T, K-major
+            const uint32_t qh = smem_u32(sQ), ql = qh + F::kQBytes;
+            const uint32_t ph = smem_u32(sP), pl = ph + F::kPBytes;
+            bool ok = mbar_wait(qFull, 0, sAbort);
+            uint64_t* last_bar = nullptr;   // the barrier of the last commit issued
+            uint32_t last_ph = 0;
+            auto s_issue = [&](int j) -> bool {
+                const int s = j % F::kStages, bs = j & 1;
+                if (!mbar_wait(&kvFull[s], (j / F::kStages) & 1, sAbort) ||
+                    !mbar_wait_backoff(&sFree[bs], ((j >> 1) & 1) ^ 1, sAbort, 128))
+                    return false;
+                tc_fence_after();
+                const uint32_t kh = smem_u32(sKV + s * F::kStageBytes), kl = kh + F::kKVBytes;
+                const uint32_t d = tmem_base + bs * F::kKT;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t a = umma_desc(qh + kk * 32, 128), al = umma_desc(ql + kk * 32, 128);
+                    const uint64_t bh = umma_desc(kh + kk * 32, 128), bl = umma_desc(kl + kk * 32, 128);
+                    mma_tf32(d, a, bh, idS, kk > 0 ? 1u : 0u);
+                    mma_tf32(d, al, bh, idS, 1u);
+                    mma_tf32(d, a, bl, idS, 1u);
+                }
+                mma_commit(&sFull[bs]);
+                last_bar = &sFull[bs];
+                last_ph = (j >> 1) & 1;
+                return true;
+            };
+            auto pv_issue = [&](int j) -> bool {
+                const int s = j % F::kStages, bs = j & 1;
+                if (!mbar_wait(pReady, j & 1, sAbort) ||
+                    !mbar_wait_backoff(&oFree[bs], ((j >> 1) & 1) ^ 1, sAbort, 128))
+                    return false;
+                tc_fence_after();
+                const uint32_t vh = smem_u32(sVt), vl = vh + F::kVtBytes;
+                const uint32_t d = tmem_base + 128 + bs * 32;
+#pragma unroll
+                for (int kk = 0; kk < F::kKT / 8; ++kk) {
+                    const uint32_t po = (kk >> 2) * F::kPBlk + (kk & 3) * 32;
+                    const uint32_t vo = (kk >> 2) * F::kVtBlk + (kk & 3) * 32;
+                    const uint64_t a = umma_desc(ph + po, 128), al = umma_desc(pl + po, 128);
+                    const uint64_t bh = umma_desc(vh + vo, 128), bl = umma_desc(vl + vo, 128);
+                    mma_tf32(d, a, bh, idO, kk > 0 ? 1u : 0u);
+                    mma_tf32(d, al, bh, idO, 1u);
+                    mma_tf32(d, a, bl, idO, 1u);
+                }
+                mma_commit(&oFull[bs]);
+                mma_commit(&kvEmpty[s]);
+                last_bar = &oFull[bs];
+                last_ph = (j >> 1) & 1;
+                return true;
+            };
+            if (ok) ok = s_issue(0);
+            if (ok && nt > 1) ok = s_issue(1);
+            for (int j = 0; j < nt && ok; ++j) {
+                ok = pv_issue(j);
+                if (ok && j + 2 < nt) ok = s_issue(j + 2);
+            }
+            if (!ok) {
+                *sAbort = 1;
+                atomicOr(err, kErrWaitAccFree);
+            }
+            // the MMAs issued so far (in order) complete before TMEM is released
+            if (last_bar && !mbar_wait_drain(last_bar, last_ph)) atomicOr(err, kErrWaitDrain);
+        }
+        __syncwarp();
+    } else {
+        // softmax: one query row per thread
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const float c2 = __fmul_rn(scale, 1.4426950408889634f);
+        const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+        float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
+        float o[32];
+#pragma unroll
+        for (int d = 0; d < 32; ++d) o[d] = 0.0f;
+        auto take_o = [&](int j) -> bool {
+            const int bs = j & 1;
+            if (!mbar_wait(&oFull[bs], (j >> 1) & 1, sAbort)) return false;
+            tc_fence_after();
+            uint32_t ot[32];
+            tmem_ld32(tmem_base + lane_base + 128 + bs * 32, ot);
+            tmem_wait_ld();
+#pragma unroll
+            for (int d = 0; d < 32; ++d) o[d] = fmaf(o[d], alpha_prev, __uint_as_float(ot[d]));
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&oFree[bs]);
+            return true;
+        };
+        bool ok = true;
+        for (int j = 0; j < nt && ok; ++j) {
+            const int bs = j & 1;
+            if (!mbar_wait(&sFull[bs], (j >> 1) & 1, sAbort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sv[64];
+            tmem_ld32(tmem_base + lane_base + bs * F::kKT, *reinterpret_cast<uint32_t(*)[32]>(sv));
+            tmem_ld32(tmem_base + lane_base + bs * F::kKT + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+            tmem_wait_ld();
+            asm volatile("" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sFree[bs]);
+            const int nk = min(F::kKT, NP - j * F::kKT);
+            float mx = -INFINITY;
+#pragma unroll
+            for (int cc = 0; cc < 64; ++cc)
+                if (cc < nk) mx = fmaxf(mx, __uint_as_float(sv[cc]));
+            const float m_new = fmaxf(m, mx);
+            const float alpha = m == -INFINITY ? 0.0f : exp2f((m - m_new) * c2);
+            // P_{j-1} has been consumed once O_{j-1} is ready: take it, then write P_j
+            if (j > 0 && !take_o(j - 1)) {
+                ok = false;
+                break;
+            }
+            float sum = 0.0f;
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+#pragma unroll
+                for (int c4 = 0; c4 < 8; ++c4) {
+                    float ph4[4], pl4[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int cc = blk * 32 + c4 * 4 + u;
+                        const float p = cc < nk ? exp2f((__uint_as_float(sv[cc]) - m_new) * c2) : 0.0f;
+                        sum += p;
+                        ph4[u] = __uint_as_float(__float_as_uint(p) & 0xFFFFE000u);
+                        pl4[u] = p - ph4[u];
+                    }
+                    const uint32_t off = blk * F::kPBlk + swz_offset(r * 128 + c4 * 16, 128);
+                    *reinterpret_cast<float4*>(sP + off) = make_float4(ph4[0], ph4[1], ph4[2], ph4[3]);
+                    *reinterpret_cast<float4*>(sP + F::kPBytes + off) = make_float4(pl4[0], pl4[1], pl4[2], pl4[3]);
+                }
+            }
+            // V_j (landed with the stage that S_j was computed from) transposed into the
+            // K-major V^T operand: thread (warp, lane) moves dim `lane` of 16 keys
+            {
+                const int s = j % F::kStages;
+                if (!mbar_wait(&kvFull[s], (j / F::kStages) & 1, sAbort)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* vsrc = sKV + s * F::kStageBytes + 2 * F::kKVBytes;
+                const int k0 = (warp - 2) * 16;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+#pragma unroll 4
+                    for (int kq = 0; kq < 16; ++kq) {
+                        const int key = k0 + kq;
+                        const float x = *reinterpret_cast<const float*>(vsrc + h * F::kKVBytes +
+                                                                        swz_offset(key * 128 + lane * 4, 128));
+                        *reinterpret_cast<float*>(sVt + h * F::kVtBytes + (key >> 5) * F::kVtBlk +
+                                                  swz_offset(lane * 128 + (key & 31) * 4, 128)) = x;
+                    }
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pReady);
+            l = fmaf(l, alpha, sum);
+            m = m_new;
+            alpha_prev = alpha;
+        }
+        if (ok) ok = take_o(nt - 1);
+        if (!ok) {
+            *sAbort = 1;
+            atomicOr(err, kErrWaitAccFull);
+        } else if (q0 + r < NP) {
+            const float inv = __fdiv_rn(1.0f, l);
+            float* dst = out + static_cast<int64_t>(row0 + q0 + r) * L + head * 32;
+#pragma unroll
+            for (int d4 = 0; d4 < 8; ++d4)
+                reinterpret_cast<float4*>(dst)[d4] =
+                    make_float4(o[4 * d4] * inv, o[4 * d4 + 1] * inv, o[4 * d4 + 2] * inv, o[4 * d4 + 3] * inv);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, F::kTmemCols);
+    }
+}
+
 template <int HD>
 cudaError_t attention(const Tm2dPlan& p, cudaStream_t st) {
     const dim3 grid((p.NP + kQ - 1) / kQ, p.heads, p.B);
     // fno.cpp:1799: 1.0f / std::sqrt((float)head_dim), IEEE on the host
     const float scale = 1.0f / std::sqrt(static_cast<float>(HD));
+    if constexpr (HD == 32) {
+        if (p.tc_attention && p.qkv_split) {
+            using F = AttnCfg;
+            const int64_t T = static_cast<int64_t>(p.B) * p.NP;
+            const int64_t n = T * p.L;
+            const int sms = device_sm_count();
+            split_qkv_kernel<<<static_cast<int>(std::min<int64_t>((n + 255) / 256, 8 * sms)), 256, 0, st>>>(
+                p.q, p.k, p.v, n, p.qkv_split);
+            CUtensorMap m[6];
+            for (int t = 0; t < 6; ++t) {
+                const int rows = (t == 0 || t == 1) ? F::kQT : F::kKT;
+                if (!encode_2d(&m[t], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.qkv_split + t * n, p.L, T,
+                               static_cast<uint64_t>(p.L) * 4, 32, rows, 128))
+                    return cudaErrorInvalidValue;
+            }
+            cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(attention_tc_kernel), F::kSmemBytes);
+            if (e != cudaSuccess) return e;
+            attention_tc_kernel<<<dim3((p.NP + F::kQT - 1) / F::kQT, p.heads, p.B), F::kThreads, F::kSmemBytes, st>>>(
+                m[0], m[1], m[2], m[3], m[4], m[5], p.NP, p.L, scale, p.ho, p.err);
+            return cudaGetLastError();
+        }
+    }
     if (p.int8) attention_online_kernel<HD><<<grid, kQ, 0, st>>>(p.q, p.k, p.v, p.NP, p.L, scale, p.ho);
     else attention_kernel<HD><<<grid, kQ, 0, st>>>(p.q, p.k, p.v, p.NP, p.L, scale, p.ho);
     return cudaGetLastError();

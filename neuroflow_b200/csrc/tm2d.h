@@ -52,6 +52,8 @@ struct Tm2dPlan {
     float* f0;              // (B*NP, 2L)
     float* f1;              // (B*NP, L)
     float* feat;            // (B*h*w, L)
+    float* qkv_split;       // (6, B*NP, L): tf32 hi / lo pairs of q, k, v (tensor-core attention)
+    int tc_attention;       // 1: attention on tensor cores (head dim 32), else on CUDA cores
     int8_t* codes;          // INT8 path: (B*NP, 2L) activation codes
     float* row_s;           // (B*NP,) per-row scales
     int32_t* row_zp;
