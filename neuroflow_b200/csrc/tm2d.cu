@@ -451,10 +451,10 @@ LinArgs lin(const float* A, int64_t M, int K, const float* W, const float* b, in
 //               O_j = P_j V_j into one of two TMEM buffers (32 columns)
 //   warps 2-5   softmax, one query row per thread (TMEM lane): the row max, the
 //               exponentials exp2((s - m) scale log2 e), the running sum, P_j written
-//               to shared memory as the A operand, V_j transposed into the K-major B
-//               operand (an MN-major tf32 operand would need the 32-byte-atom swizzle),
-//               and O accumulated in registers with the online rescaling; O / sum is
-//               written at the end.
+//               to shared memory as the A operand, and O accumulated in registers with
+//               the online rescaling; O / sum is written at the end
+//   warps 6-7   V_j transposed into the K-major B operand (two buffers; an MN-major tf32
+//               operand would need the 32-byte-atom swizzle)
 // The result equals softmax attention to fp32 accuracy but not in the reference's
 // summation order (fno.cpp:1441-1456, 1919-1929), which attention_kernel keeps.
 // ---------------------------------------------------------------------------
@@ -472,10 +472,10 @@ struct AttnCfg {
     static constexpr int kOffP = kOffKV + kStages * kStageBytes;  // P hi, P lo
     static constexpr int kVtBlk = 32 * 128;          // V^T [32 dims][32 keys] f32, SW128
     static constexpr int kVtBytes = 2 * kVtBlk;      // 64 keys
-    static constexpr int kOffVt = kOffP + 2 * kPBytes;             // V^T hi, V^T lo
-    static constexpr int kOffBars = kOffVt + 2 * kVtBytes;
+    static constexpr int kOffVt = kOffP + 2 * kPBytes;             // 2 x (V^T hi, V^T lo)
+    static constexpr int kOffBars = kOffVt + 4 * kVtBytes;
     static constexpr int kSmemBytes = kOffBars + 256 + 1024;
-    static constexpr int kThreads = 192;
+    static constexpr int kThreads = 256;
     static constexpr int kTmemCols = 256;            // S 2 x 64 at 0, O 2 x 32 at 128
 };
 
@@ -516,7 +516,8 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_const
     uint64_t* pReady = sFree + 2;
     uint64_t* oFull = pReady + 1;
     uint64_t* oFree = oFull + 2;
-    uint32_t* sTmem = reinterpret_cast<uint32_t*>(oFree + 2);
+    uint64_t* vtReady = oFree + 2;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(vtReady + 2);
     volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -535,6 +536,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_const
             mbar_init(&sFree[s], 4);
             mbar_init(&oFull[s], 1);
             mbar_init(&oFree[s], 4);
+            mbar_init(&vtReady[s], 2);
         }
         mbar_init(pReady, 4);
         *sAbort = 0;
@@ -591,7 +593,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_const
             auto s_issue = [&](int j) -> bool {
                 const int s = j % F::kStages, bs = j & 1;
                 if (!mbar_wait(&kvFull[s], (j / F::kStages) & 1, sAbort) ||
-                    !mbar_wait_backoff(&sFree[bs], ((j >> 1) & 1) ^ 1, sAbort, 128))
+                    !mbar_wait(&sFree[bs], ((j >> 1) & 1) ^ 1, sAbort))
                     return false;
                 tc_fence_after();
                 const uint32_t kh = smem_u32(sKV + s * F::kStageBytes), kl = kh + F::kKVBytes;
@@ -611,11 +613,11 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_const
             };
             auto pv_issue = [&](int j) -> bool {
                 const int s = j % F::kStages, bs = j & 1;
-                if (!mbar_wait(pReady, j & 1, sAbort) ||
-                    !mbar_wait_backoff(&oFree[bs], ((j >> 1) & 1) ^ 1, sAbort, 128))
+                if (!mbar_wait(pReady, j & 1, sAbort) || !mbar_wait(&vtReady[bs], (j >> 1) & 1, sAbort) ||
+                    !mbar_wait(&oFree[bs], ((j >> 1) & 1) ^ 1, sAbort))
                     return false;
                 tc_fence_after();
-                const uint32_t vh = smem_u32(sVt), vl = vh + F::kVtBytes;
+                const uint32_t vh = smem_u32(sVt + bs * 2 * F::kVtBytes), vl = vh + F::kVtBytes;
                 const uint32_t d = tmem_base + 128 + bs * 32;
 #pragma unroll
                 for (int kk = 0; kk < F::kKT / 8; ++kk) {
@@ -647,6 +649,35 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_const
             if (last_bar && !mbar_wait_drain(last_bar, last_ph)) atomicOr(err, kErrWaitDrain);
         }
         __syncwarp();
+    } else if (warp >= 6) {
+        // V_j -> V^T buffer j % 2 once PV_{j-2} (the buffer's previous reader) is done:
+        // thread (warp, lane) moves dim `lane` of 32 keys
+        const int k0 = (warp - 6) * 32;
+        for (int j = 0; j < nt; ++j) {
+            const int s = j % F::kStages, bs = j & 1;
+            if (!mbar_wait(&kvFull[s], (j / F::kStages) & 1, sAbort) ||
+                (j >= 2 && !mbar_wait(&oFull[bs], ((j - 2) >> 1) & 1, sAbort))) {
+                *sAbort = 1;
+                atomicOr(err, kErrWaitDrain);
+                break;
+            }
+            const uint8_t* vsrc = sKV + s * F::kStageBytes + 2 * F::kKVBytes;
+            uint8_t* vdst = sVt + bs * 2 * F::kVtBytes;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+#pragma unroll 8
+                for (int kq = 0; kq < 32; ++kq) {
+                    const int key = k0 + kq;
+                    const float x = *reinterpret_cast<const float*>(vsrc + h * F::kKVBytes +
+                                                                    swz_offset(key * 128 + lane * 4, 128));
+                    *reinterpret_cast<float*>(vdst + h * F::kVtBytes + (key >> 5) * F::kVtBlk +
+                                              swz_offset(lane * 128 + (key & 31) * 4, 128)) = x;
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&vtReady[bs]);
+        }
     } else {
         // softmax: one query row per thread
         const int quad = warp & 3;
@@ -688,18 +719,18 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_const
             __syncwarp();
             if (lane == 0) mbar_arrive(&sFree[bs]);
             const int nk = min(F::kKT, NP - j * F::kKT);
-            float mx = -INFINITY;
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int cc = 0; cc < 64; ++cc)
-                if (cc < nk) mx = fmaxf(mx, __uint_as_float(sv[cc]));
-            const float m_new = fmaxf(m, mx);
+                if (cc < nk) mx4[cc & 3] = fmaxf(mx4[cc & 3], __uint_as_float(sv[cc]));
+            const float m_new = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])));
             const float alpha = m == -INFINITY ? 0.0f : exp2f((m - m_new) * c2);
             // P_{j-1} has been consumed once O_{j-1} is ready: take it, then write P_j
             if (j > 0 && !take_o(j - 1)) {
                 ok = false;
                 break;
             }
-            float sum = 0.0f;
+            float sum4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
             for (int blk = 0; blk < 2; ++blk) {
 #pragma unroll
@@ -709,7 +740,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_const
                     for (int u = 0; u < 4; ++u) {
                         const int cc = blk * 32 + c4 * 4 + u;
                         const float p = cc < nk ? exp2f((__uint_as_float(sv[cc]) - m_new) * c2) : 0.0f;
-                        sum += p;
+                        sum4[u] += p;
                         ph4[u] = __uint_as_float(__float_as_uint(p) & 0xFFFFE000u);
                         pl4[u] = p - ph4[u];
                     }
@@ -718,32 +749,10 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_const
                     *reinterpret_cast<float4*>(sP + F::kPBytes + off) = make_float4(pl4[0], pl4[1], pl4[2], pl4[3]);
                 }
             }
-            // V_j (landed with the stage that S_j was computed from) transposed into the
-            // K-major V^T operand: thread (warp, lane) moves dim `lane` of 16 keys
-            {
-                const int s = j % F::kStages;
-                if (!mbar_wait(&kvFull[s], (j / F::kStages) & 1, sAbort)) {
-                    ok = false;
-                    break;
-                }
-                const uint8_t* vsrc = sKV + s * F::kStageBytes + 2 * F::kKVBytes;
-                const int k0 = (warp - 2) * 16;
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-#pragma unroll 4
-                    for (int kq = 0; kq < 16; ++kq) {
-                        const int key = k0 + kq;
-                        const float x = *reinterpret_cast<const float*>(vsrc + h * F::kKVBytes +
-                                                                        swz_offset(key * 128 + lane * 4, 128));
-                        *reinterpret_cast<float*>(sVt + h * F::kVtBytes + (key >> 5) * F::kVtBlk +
-                                                  swz_offset(lane * 128 + (key & 31) * 4, 128)) = x;
-                    }
-                }
-            }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(pReady);
-            l = fmaf(l, alpha, sum);
+            l = fmaf(l, alpha, (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
             m = m_new;
             alpha_prev = alpha;
         }
