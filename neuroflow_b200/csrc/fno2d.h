@@ -170,13 +170,43 @@ cudaError_t fno2d_run(const Fno2dPlan& plan, cudaStream_t stream);
 // FP32 fake-quant executor (fno2d_fp32.cu): the reference FNO2d::Forward
 // (fno.cpp:777-995) as the runtime runs it without EnableInt8Gemm.  Activations are
 // fp32 channel-first (b, c, h, w) like the reference's h_perm.
+//
+// The same kernels also run the INT8 composition (EnableInt8Gemm) on geometries the
+// width-64 executor above does not take: the layer inputs snapped with the previous
+// ".output" qparams, and the 1x1 layers through LinearForwardBatched on int8 codes
+// (Fno2dI8Linear).  The snapped activations stay fp32 values (q - zp) * s.
 // ---------------------------------------------------------------------------
+
+// One 1x1 layer through LinearForwardBatched (int8_gemm.cpp:530-580) with the
+// QuantiseWeight2D codes (fno.cpp:325-358): the input is quantised with (s_in, zp_in),
+// acc = sum_k a_k (w_ok - zp_w[o]) is exact in fp32 (|acc| < 2^24 for C <= 256), and
+//   y = (scale_w[o] * s_in) * float(acc - zp_w[o] sum_a - zp_in sum_w[o] + C zp_w[o] zp_in)
+// then y + 0.0f and + bias[o] as two roundings.
+struct Fno2dI8Linear {
+    const float* wz;      // (C, C) w_ok - zp_w[o] as floats (nullptr: the FP32 Linear runs)
+    const int4* cols;     // per output channel {float bits of scale_w * s_in, zp_w,
+                          //  C zp_w zp_in - zp_in sum_w, 0}
+    float s_in;
+    int zp_in;
+};
+
+// Snap of a layer's output for its consumer (apply_input_fq of the INT8 composition):
+// kind 1 stores (code - zp) * s, the code from the exact z -> code table when present.
+struct Fno2dSnap {
+    FqParam fq;
+    const int2* code_lut; // one-segment table (nfx_lut.h); nullptr: evaluate directly
+    int lut_cells;
+    float lut_zlo, lut_inv_delta;
+};
+
 struct Fno2dF32Layer {
     const float* wr;      // (C, C, MH, MW) spectral weights (fake-quantised at load)
     const float* wi;
     const float* loc_w;   // (C, C)
     const float* loc_b;
     FqParam fq;           // locs.i.output
+    Fno2dI8Linear i8;     // INT8 composition: the local Linear (wz nullptr: FP32)
+    Fno2dSnap snap;       // INT8 composition: snap of this layer's output (kind 0: none)
 };
 
 struct Fno2dF32Plan {
@@ -193,6 +223,12 @@ struct Fno2dF32Plan {
     const float* po_w;
     const float* po_b;
     FqParam fq_po;
+    // INT8 composition: the lift output's snap (layer 0's input), proj_q through
+    // LinearForwardBatched, and act(proj_q.output fake-quant) from a 256-entry table
+    // (build_act_table; nullptr: evaluated)
+    FqParam snap_lift;
+    Fno2dI8Linear pq_i8;
+    const float* pq_act_table;
     const float2* twf_w;  // recurrence twiddles (nfx_lut.h) for Wp and Hp
     const float2* twi_w;
     const float2* twf_h;

@@ -19,6 +19,12 @@
 // Every product, sum and transform follows the reference's expression shapes
 // (fft_exact.cuh, linear_step); the only approximate operation is CUDA's tanhf inside
 // GELU.  Columns of Irfft2 that the truncation leaves all-zero are taken as +0.
+//
+// With the INT8 composition (Fno2dI8Linear / Fno2dSnap in fno2d.h) the lift and every
+// layer but the last store their output snapped for the next layer, layer2d takes the
+// local Linear over the input's int8 codes, and proj2d does the same for proj_q.  The
+// snaps after an activation come from the host's exact z -> code tables, so GELU stays
+// exact there too.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -98,6 +104,8 @@ __global__ void __launch_bounds__(256) lift2d_f32_kernel(Fno2dF32Plan p) {
             }
             v = apply_fq(v, p.fq_lift);
         }
+        // layer 0's input snap (padding zeros included, as the reference pads first)
+        if (p.snap_lift.kind == 1) v = fake_quant(v, p.snap_lift.scale, static_cast<float>(p.snap_lift.zp));
         p.h[0][t] = v;
     }
     if (p.obs) ob.flush(p.obs, 0);
@@ -181,7 +189,7 @@ __global__ void __launch_bounds__(256) mix2d_kernel(const float2* __restrict__ X
 }
 
 // row inverse + local layer + epilogue for one row of one sample; grid (Hp, B), 256
-// threads; shared memory sH [C][Wp] float, sX1 [kChunk][Wp] float2
+// threads; shared memory sH [C][Wp] float, sX1 [kChunk][Wp] float2, sSum [Wp] float
 struct Layer2dArgs {
     const float* hin;
     float* hout;
@@ -190,6 +198,8 @@ struct Layer2dArgs {
     const float* loc_w;
     const float* loc_b;
     FqParam fq;
+    Fno2dI8Linear i8;     // wz nullptr: FP32 Linear
+    Fno2dSnap snap;       // output snap (kind 0: the activation's value)
     int Hp, Wp, C, MW, act;
     unsigned* obs;        // calibration observers (Fno2dF32Plan::obs), tensor obs_i
     float* obs_vals;
@@ -201,13 +211,27 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
     const int Wp = a.Wp, C = a.C, Hp = a.Hp;
     float* sH = reinterpret_cast<float*>(sm);
     float2* sX1 = sm + (static_cast<size_t>(C) * Wp + 1) / 2;
+    float* sSum = reinterpret_cast<float*>(sX1 + static_cast<size_t>(kChunk) * Wp);
     const int hh = blockIdx.x, b = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int lgW = 31 - __clz(Wp);
     const int half = Wp / 2 + 1;
+    const bool i8 = a.i8.wz != nullptr;
+    const float zp_in = static_cast<float>(a.i8.zp_in);
     for (int t = threadIdx.x; t < C * Wp; t += blockDim.x) {
         const int k = t / Wp, w = t - (t / Wp) * Wp;
-        sH[t] = a.hin[((static_cast<int64_t>(b) * C + k) * Hp + hh) * Wp + w];
+        const float v = a.hin[((static_cast<int64_t>(b) * C + k) * Hp + hh) * Wp + w];
+        // INT8: QuantiseActivation's code (int8_gemm.cpp:507-520) of the snapped input
+        sH[t] = i8 ? fq_code(v, a.i8.s_in, zp_in) : v;
+    }
+    if (i8) {
+        // sum_a of each point (exact: |sum| <= 128 C)
+        __syncthreads();
+        for (int w = threadIdx.x; w < Wp; w += blockDim.x) {
+            float sa = 0.0f;
+            for (int k = 0; k < C; ++k) sa = __fadd_rn(sa, sH[static_cast<size_t>(k) * Wp + w]);
+            sSum[w] = sa;
+        }
     }
     const float invW = __fdiv_rn(1.0f, static_cast<float>(Wp));
     const int nu = linear_unfused_len(C);
@@ -241,15 +265,37 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
             if (o >= C) break;
             float acc[kMaxWp / 32];
             const float bias = __ldg(a.loc_b + o);
+            if (i8) {
+                // exact integer dot product of codes and (w - zp_w), then the epilogue
 #pragma unroll
-            for (int j = 0; j < kMaxWp / 32; ++j) acc[j] = bias;
-            const float* wrow = a.loc_w + static_cast<int64_t>(o) * C;
-            for (int k = 0; k < C; ++k) {
-                const float wv = __ldg(wrow + k);
-                const float* hk = sH + static_cast<size_t>(k) * Wp;
+                for (int j = 0; j < kMaxWp / 32; ++j) acc[j] = 0.0f;
+                const float* wrow = a.i8.wz + static_cast<int64_t>(o) * C;
+                for (int k = 0; k < C; ++k) {
+                    const float wv = __ldg(wrow + k);
+                    const float* hk = sH + static_cast<size_t>(k) * Wp;
+#pragma unroll
+                    for (int j = 0; j < kMaxWp / 32; ++j)
+                        if (j < nj && lane + 32 * j < Wp) acc[j] = __fmaf_rn(hk[lane + 32 * j], wv, acc[j]);
+                }
+                const int4 cc = __ldg(a.i8.cols + o);
 #pragma unroll
                 for (int j = 0; j < kMaxWp / 32; ++j)
-                    if (j < nj && lane + 32 * j < Wp) acc[j] = linear_step(acc[j], hk[lane + 32 * j], wv, k >= nu);
+                    if (j < nj && lane + 32 * j < Wp) {
+                        const int v = __float2int_rn(acc[j]) - cc.y * __float2int_rn(sSum[lane + 32 * j]) + cc.z;
+                        const float y = __fadd_rn(__fmul_rn(__int_as_float(cc.x), __int2float_rn(v)), 0.0f);
+                        acc[j] = __fadd_rn(y, bias);
+                    }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kMaxWp / 32; ++j) acc[j] = bias;
+                const float* wrow = a.loc_w + static_cast<int64_t>(o) * C;
+                for (int k = 0; k < C; ++k) {
+                    const float wv = __ldg(wrow + k);
+                    const float* hk = sH + static_cast<size_t>(k) * Wp;
+#pragma unroll
+                    for (int j = 0; j < kMaxWp / 32; ++j)
+                        if (j < nj && lane + 32 * j < Wp) acc[j] = linear_step(acc[j], hk[lane + 32 * j], wv, k >= nu);
+                }
             }
             float* dst = a.hout + ((static_cast<int64_t>(b) * C + o) * Hp + hh) * Wp;
 #pragma unroll
@@ -262,7 +308,17 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
                     }
                     const float x2 = apply_fq(acc[j], a.fq);
                     const float x1 = __fmul_rn(sX1[static_cast<size_t>(r) * Wp + w].x, invW);
-                    dst[w] = act_f(__fadd_rn(x1, x2), a.act);
+                    const float z = __fadd_rn(x1, x2);
+                    if (a.snap.fq.kind == 1) {
+                        const float zpo = static_cast<float>(a.snap.fq.zp);
+                        const float q = a.snap.code_lut
+                                            ? static_cast<float>(code_from_lut(z, a.snap.code_lut, a.snap.lut_cells,
+                                                                               a.snap.lut_zlo, a.snap.lut_inv_delta))
+                                            : fq_code(act_f(z, a.act), a.snap.fq.scale, zpo);
+                        dst[w] = __fmul_rn(__fsub_rn(q, zpo), a.snap.fq.scale);
+                    } else {
+                        dst[w] = act_f(z, a.act);
+                    }
                 }
             }
         }
@@ -281,6 +337,9 @@ __global__ void __launch_bounds__(128) proj2d_f32_kernel(Fno2dF32Plan p, const f
     const int nu = linear_unfused_len(C);
     Obs obq, obo;
     const int iq = p.L + 1, io = p.L + 2;
+    const bool pq8 = p.pq_i8.wz != nullptr;
+    const float zp_in = static_cast<float>(p.pq_i8.zp_in);
+    const float zp_pq = static_cast<float>(p.fq_pq.zp);
     for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
          t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int ww = static_cast<int>(t % p.W);
@@ -288,18 +347,40 @@ __global__ void __launch_bounds__(128) proj2d_f32_kernel(Fno2dF32Plan p, const f
         const int hh = static_cast<int>(r % p.H);
         const int64_t b = r / p.H;
         for (int k = 0; k < C; ++k) mine[k] = h[((b * C + k) * p.Hp + hh) * p.Wp + ww];
+        // INT8 proj_q: the point's codes and their sum (int8_gemm.cpp:507-520, :567)
+        float sum_a = 0.0f;
+        if (pq8) {
+            for (int k = 0; k < C; ++k) {
+                mine[k] = fq_code(mine[k], p.pq_i8.s_in, zp_in);
+                sum_a = __fadd_rn(sum_a, mine[k]);
+            }
+        }
         float acc[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) acc[j] = j < p.out_ch ? __ldg(p.po_b + j) : 0.0f;
         for (int c = 0; c < C; ++c) {
-            float q = __ldg(p.pq_b + c);
-            const float* wr = p.pq_w + static_cast<int64_t>(c) * C;
-            for (int k = 0; k < C; ++k) q = linear_step(q, mine[k], __ldg(wr + k), k >= nu);
+            float q;
+            if (pq8) {
+                float s = 0.0f;
+                const float* wr = p.pq_i8.wz + static_cast<int64_t>(c) * C;
+                for (int k = 0; k < C; ++k) s = __fmaf_rn(mine[k], __ldg(wr + k), s);
+                const int4 cc = __ldg(p.pq_i8.cols + c);
+                const int v = __float2int_rn(s) - cc.y * __float2int_rn(sum_a) + cc.z;
+                q = __fadd_rn(__fadd_rn(__fmul_rn(__int_as_float(cc.x), __int2float_rn(v)), 0.0f),
+                              __ldg(p.pq_b + c));
+            } else {
+                q = __ldg(p.pq_b + c);
+                const float* wr = p.pq_w + static_cast<int64_t>(c) * C;
+                for (int k = 0; k < C; ++k) q = linear_step(q, mine[k], __ldg(wr + k), k >= nu);
+            }
             if (p.obs) {
                 obq.see(q);
                 if (p.obs_vals[iq]) p.obs_vals[iq][t * C + c] = q;
             }
-            q = act_f(apply_fq(q, p.fq_pq), p.act);
+            if (p.pq_act_table && p.fq_pq.kind == 1)
+                q = __ldg(p.pq_act_table + static_cast<int>(fq_code(q, p.fq_pq.scale, zp_pq)) + 128);
+            else
+                q = act_f(apply_fq(q, p.fq_pq), p.act);
 #pragma unroll
             for (int j = 0; j < 16; ++j)
                 if (j < p.out_ch)
@@ -326,7 +407,8 @@ size_t fwd_smem(int Hp, int Wp, int MW) {
     return (8 * static_cast<size_t>(Wp) + static_cast<size_t>(MW) * Hp) * sizeof(float2);
 }
 size_t layer_smem(int C, int Wp) {
-    return ((static_cast<size_t>(C) * Wp + 1) / 2 + static_cast<size_t>(kChunk) * Wp) * sizeof(float2);
+    return ((static_cast<size_t>(C) * Wp + 1) / 2 + static_cast<size_t>(kChunk) * Wp) * sizeof(float2) +
+           static_cast<size_t>(Wp) * sizeof(float);
 }
 int mix_group(int C) {
     for (int G = 8; G > 1; G >>= 1)
@@ -389,6 +471,8 @@ cudaError_t fno2d_f32_run(const Fno2dF32Plan& p, cudaStream_t st) {
         a.loc_w = L.loc_w;
         a.loc_b = L.loc_b;
         a.fq = L.fq;
+        a.i8 = L.i8;
+        a.snap = L.snap;
         a.obs = p.obs;
         a.obs_vals = p.obs ? p.obs_vals[1 + i] : nullptr;
         a.obs_i = 1 + i;

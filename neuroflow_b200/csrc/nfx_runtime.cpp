@@ -192,8 +192,12 @@ struct nfx_runtime {
     unsigned* calib_stats = nullptr;
     int calib_keep = 0;
     std::vector<std::vector<std::pair<float*, int64_t>>> calib_vals;
-    // FNO2d FP32 (reference fake-quant) state
+    // FNO2d FP32 (reference fake-quant) state; plan2i: the same kernels running the
+    // INT8 composition where the width-64 executor does not apply (f2_fast false, or a
+    // grid outside its range)
     nfx::Fno2dF32Plan plan2f{};
+    nfx::Fno2dF32Plan plan2i{};
+    bool f2_fast = false;
     void* f2_bufs[4] = {nullptr, nullptr, nullptr, nullptr};  // h0, h1, Xs, colinv
     int64_t f2_cap[4] = {0, 0, 0, 0};
     float2* f2_tw[4] = {nullptr, nullptr, nullptr, nullptr};   // fwd W, inv W, fwd H, inv H
@@ -389,35 +393,131 @@ int fno2d_create(nfx_runtime* rt) {
     return NFX_OK;
 }
 
-// EnableInt8Gemm for FNO2d: every locs.i and proj_q needs per-channel (axis 0) weight
-// qparams, and every layer input key needs per-tensor INT8 activation qparams.
+// The INT8 composition on the FP32 executor's kernels (plan2i), for any geometry that
+// executor runs.  Per layer, as the composition defines it: the layer input is
+// snapped with its key's per-tensor INT8 qparams when they exist (lift.output for
+// layer 0, locs.{i-1}.output after), and locs.i / proj_q run LinearForwardBatched
+// when the weight has per-channel axis-0 qparams and the input key per-tensor ones.
+bool fno2d_i8_generic(nfx_runtime* rt) {
+    auto& m = rt->model;
+    const F2 c = fno2d_cfg(m);
+    if (!rt->plan2f.lift_w) return false;
+    nfx::Fno2dF32Plan pl = rt->plan2f;
+    const int act = pl.act;
+    auto in_qp = [&](int i, nfx::QP& q) {
+        auto it = m.activation_qparams.find(i == 0 ? std::string("lift.output")
+                                                   : "locs." + std::to_string(i - 1) + ".output");
+        if (it == m.activation_qparams.end()) return false;
+        q = it->second;
+        return true;
+    };
+    auto fq1 = [](const nfx::QP& q) { return nfx::FqParam{1, q.scale, q.zero_point, 1.0f / q.scale}; };
+    const nfx::FqParam none{0, 1.0f, 0, 1.0f};
+    // i in [0, L]: layer i's local Linear, i == L proj_q
+    auto linear = [&](int i, nfx::Fno2dI8Linear& out) -> bool {
+        out = nfx::Fno2dI8Linear{nullptr, nullptr, 1.0f, 0};
+        const std::string wname = i < c.L ? "locs." + std::to_string(i) + ".weight" : "proj_q.weight";
+        nfx::QP in;
+        auto pc = m.weight_per_channel_qparams.find(wname);
+        if (pc == m.weight_per_channel_qparams.end() || !in_qp(i, in)) return true;  // FP32 Linear
+        std::vector<int8_t> codes;
+        std::vector<int32_t> sum_w;
+        if (!nfx::quantise_weight_2d(m.weights.at(wname), pc->second, codes, sum_w)) return true;
+        const int C = c.width;
+        if (static_cast<int>(codes.size()) != C * C || static_cast<int>(pc->second.zero_points.size()) < C)
+            return true;
+        std::vector<float> wz(codes.size());
+        std::vector<int32_t> cols(static_cast<size_t>(4) * C, 0);
+        for (int o = 0; o < C; ++o) {
+            const int32_t zpw = pc->second.zero_points[o];
+            for (int k = 0; k < C; ++k)
+                wz[static_cast<size_t>(o) * C + k] = static_cast<float>(codes[static_cast<size_t>(o) * C + k] - zpw);
+            const float sws = pc->second.scales[o] * in.scale;
+            std::memcpy(&cols[4 * o], &sws, 4);
+            cols[4 * o + 1] = zpw;
+            cols[4 * o + 2] = C * zpw * in.zero_point - in.zero_point * sum_w[o];
+        }
+        out.wz = upload(rt, wz.data(), wz.size());
+        out.cols = reinterpret_cast<const int4*>(upload(rt, cols.data(), cols.size()));
+        out.s_in = in.scale;
+        out.zp_in = in.zero_point;
+        return out.wz && out.cols;
+    };
+    auto snap = [&](const nfx::QP& q, nfx::Fno2dSnap& out) -> bool {
+        out = nfx::Fno2dSnap{fq1(q), nullptr, 0, 0.0f, 0.0f};
+        nfx::CodeLut lut;
+        std::string why;
+        if (nfx::build_code_lut(q.scale, q.zero_point, act, 1 << 15, lut, why)) {
+            out.code_lut = reinterpret_cast<const int2*>(upload(rt, lut.cells.data(), lut.cells.size()));
+            if (!out.code_lut) return false;
+            out.lut_cells = static_cast<int>(lut.cells.size());
+            out.lut_zlo = lut.zlo;
+            out.lut_inv_delta = lut.inv_delta;
+        }
+        return true;
+    };
+    nfx::QP q;
+    pl.snap_lift = in_qp(0, q) ? fq1(q) : none;
+    for (int i = 0; i <= c.L; ++i) {
+        nfx::Fno2dI8Linear& li = i < c.L ? pl.layer[i].i8 : pl.pq_i8;
+        if (!linear(i, li)) return false;
+    }
+    for (int i = 0; i < c.L; ++i) {
+        pl.layer[i].snap = nfx::Fno2dSnap{none, nullptr, 0, 0.0f, 0.0f};
+        // the next layer's input snap; after the last layer only proj_q's own
+        // quantisation, which the snapped value reproduces (the snap is idempotent)
+        const bool want = i + 1 < c.L ? in_qp(i + 1, q) : (pl.pq_i8.wz != nullptr && in_qp(c.L, q));
+        if (want && !snap(q, pl.layer[i].snap)) return false;
+    }
+    pl.pq_act_table = nullptr;
+    if (pl.fq_pq.kind == 1) {
+        const std::vector<float> t = nfx::build_act_table(pl.fq_pq.scale, pl.fq_pq.zp, act);
+        pl.pq_act_table = upload(rt, t.data(), t.size());
+        if (!pl.pq_act_table) return false;
+    }
+    rt->plan2i = pl;
+    return true;
+}
+
+bool fno2d_i8_fast(nfx_runtime* rt);
+
+// EnableInt8Gemm for FNO2d.  The INT8 composition runs on every geometry through
+// plan2i; the width-64 executor (plan, f2_fast) takes it over when every locs.i and
+// proj_q has per-channel (axis 0) weight qparams and every layer input key per-tensor
+// INT8 activation qparams.
 void fno2d_enable_int8(nfx_runtime* rt) {
+    if (!rt->model.quant_enabled || !fno2d_i8_generic(rt)) return;
+    rt->int8_enabled = true;
+    rt->f2_fast = fno2d_i8_fast(rt);
+}
+
+bool fno2d_i8_fast(nfx_runtime* rt) {
     auto& m = rt->model;
     const F2 c = fno2d_cfg(m);
     if (!m.quant_enabled || !nfx::fno2d_supported(c.width, c.mh, c.mw) || c.L > nfx::kFno2dMaxLayers)
-        return;
-    if (c.out_ch < 1 || c.out_ch > 4 || c.in_ch < 1 || c.in_ch > 8) return;
+        return false;
+    if (c.out_ch < 1 || c.out_ch > 4 || c.in_ch < 1 || c.in_ch > 8) return false;
     auto act_key = [](int i) { return i == 0 ? std::string("lift.output")
                                              : "locs." + std::to_string(i - 1) + ".output"; };
     for (int i = 0; i <= c.L; ++i) {
-        if (!m.activation_qparams.count(act_key(i))) return;
-        if (m.activation_fp8_qparams.count(act_key(i))) return;
+        if (!m.activation_qparams.count(act_key(i))) return false;
+        if (m.activation_fp8_qparams.count(act_key(i))) return false;
     }
     auto& pl = rt->plan;
     for (int i = 0; i <= c.L; ++i) {
         const std::string wname = i < c.L ? "locs." + std::to_string(i) + ".weight" : "proj_q.weight";
         auto pc = m.weight_per_channel_qparams.find(wname);
-        if (pc == m.weight_per_channel_qparams.end()) return;
+        if (pc == m.weight_per_channel_qparams.end()) return false;
         std::vector<int8_t> codes;
         std::vector<int32_t> sum_w;
-        if (!nfx::quantise_weight_2d(m.weights.at(wname), pc->second, codes, sum_w)) return;
-        if (static_cast<int>(codes.size()) != c.width * c.width) return;
+        if (!nfx::quantise_weight_2d(m.weights.at(wname), pc->second, codes, sum_w)) return false;
+        if (static_cast<int>(codes.size()) != c.width * c.width) return false;
         nfx::LayerArgs& a = i < c.L ? pl.layer[i].args : pl.proj;
         a.Wq = upload(rt, codes.data(), codes.size());
         a.scale_w = upload(rt, pc->second.scales.data(), static_cast<size_t>(c.width));
         a.zp_w = upload(rt, pc->second.zero_points.data(), static_cast<size_t>(c.width));
         a.sum_w = upload(rt, sum_w.data(), sum_w.size());
-        if (!a.Wq || !a.scale_w || !a.zp_w || !a.sum_w) return;
+        if (!a.Wq || !a.scale_w || !a.zp_w || !a.sum_w) return false;
         {
             // -2 zp_w (in [-254, 256]) as up to three int8 parts per output channel
             std::vector<int8_t> zr(static_cast<size_t>(3) * c.width * 32, 0);
@@ -434,7 +534,7 @@ void fno2d_enable_int8(nfx_runtime* rt) {
                         zr[(static_cast<size_t>(q) * c.width + o) * 32 + k] = static_cast<int8_t>(zp3[q]);
             }
             a.zrows = upload(rt, zr.data(), zr.size());
-            if (!a.zrows) return;
+            if (!a.zrows) return false;
         }
         const nfx::QP in = m.activation_qparams.at(act_key(i));
         a.s_in = in.scale;
@@ -550,7 +650,7 @@ void fno2d_enable_int8(nfx_runtime* rt) {
                 pl.lift_cols.w[o][k] = lw[static_cast<size_t>(o) * c.in_ch + k];
         }
     }
-    rt->int8_enabled = true;
+    return true;
 }
 
 // Twiddle tables in double precision, rounded once to float (fno2d_tables).
@@ -643,11 +743,12 @@ int ensure_f2_buf(nfx_runtime* rt, int i, int64_t bytes) {
 }
 
 // FNO2d without EnableInt8Gemm: the reference's FP32 fake-quant network.  With `obs`
-// (calibration), the Linear outputs are observed and no fake-quant is applied.
+// (calibration), the Linear outputs are observed and no fake-quant is applied.  After
+// EnableInt8Gemm the same kernels run the INT8 composition (plan2i).
 int fno2d_f32_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st,
                      unsigned* obs = nullptr, float* const* obs_vals = nullptr) {
     const F2 c = fno2d_cfg(rt->model);
-    auto& pl0 = rt->plan2f;
+    auto& pl0 = rt->int8_enabled && !obs ? rt->plan2i : rt->plan2f;
     if (!pl0.lift_w)
         return rt_fail(rt, NFX_UNSUPPORTED_OP, "FNO2d GPU executor: needs <= 8 layers");
     const int B = static_cast<int>(xs[0]), H = static_cast<int>(xs[1]), W = static_cast<int>(xs[2]);
@@ -719,16 +820,17 @@ int fno2d_f32_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float*
 int fno2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
     const F2 c = fno2d_cfg(rt->model);
     if (!rt->int8_enabled) return fno2d_f32_launch(rt, dx, xs, dy, st);
-    if (!nfx::fno2d_supported(c.width, c.mh, c.mw))
-        return rt_fail(rt, NFX_UNSUPPORTED_OP,
-                       "FNO2d INT8 executor supports width 64 with 12x12 modes");
     const int B = static_cast<int>(xs[0]), H = static_cast<int>(xs[1]), W = static_cast<int>(xs[2]);
+    // the width-64 executor's range; elsewhere the composition runs on plan2i
+    const bool fast = rt->f2_fast && W >= 32 && W <= 128 && H >= 8 && H <= 4096 && c.mh <= H &&
+                      c.mw <= W / 2 + 1 && !(c.pad > 1 && ((H % c.pad) || (W % c.pad)));
+    if (!fast) {
+        if (rt->tap_codes)
+            return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                           "code taps are written by the width-64 12x12 INT8 executor only");
+        return fno2d_f32_launch(rt, dx, xs, dy, st);
+    }
     if (B == 0) return NFX_OK;
-    if (W < 32 || W > 128 || H < 8 || H > 4096 || c.mh > H || c.mw > W / 2 + 1)
-        return rt_fail(rt, NFX_UNSUPPORTED_OP,
-                       "FNO2d GPU executor: needs 32 <= W <= 128, H >= 8, modes within the grid");
-    if (c.pad > 1 && ((H % c.pad) || (W % c.pad)))
-        return rt_fail(rt, NFX_UNSUPPORTED_OP, "FNO2d GPU executor: padding is not supported");
     int s = ensure_twiddles(rt, H, W);
     if (s != NFX_OK) return s;
     s = ensure_buffers(rt, B, H, W);
@@ -1531,12 +1633,12 @@ int fno2d_noalloc_plan(nfx_runtime* rt, const float* x, const int64_t* x_shape, 
     int s = check_fno2d_shapes(rt, x_shape, x_rank, y_shape, y_rank);
     if (s != NFX_OK) return s;
     const F2 c = fno2d_cfg(rt->model);
-    if (!fno2d_supported(c.width, c.mh, c.mw))
-        return rt_fail(rt, NFX_UNSUPPORTED_OP,
-                       "FNO2d on the GPU runtime supports width 64 with 12x12 modes");
     if (!rt->int8_enabled)
         return rt_fail(rt, NFX_UNSUPPORTED_OP,
-                       "FNO2d on the GPU runtime runs the INT8 path: call EnableInt8Gemm() first");
+                       "the allocation-free entry point runs the FNO2d INT8 path: call EnableInt8Gemm() first");
+    if (!rt->f2_fast)
+        return rt_fail(rt, NFX_UNSUPPORTED_OP,
+                       "the allocation-free entry point runs the width-64 12x12 FNO2d INT8 executor");
     const int B = static_cast<int>(x_shape[0]), H = static_cast<int>(x_shape[1]),
               W = static_cast<int>(x_shape[2]);
     if (W < 32 || W > 128 || H < 8 || H > 4096 || c.mh > H || c.mw > W / 2 + 1)
