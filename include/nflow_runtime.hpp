@@ -7,10 +7,11 @@
 // values and messages stay the same.
 //
 // Differences a caller can see: Create binds the runtime to CUDA device 0 (or the
-// device given to CreateOnDevice); the op-specific Run* of the ops this runtime does
-// not execute (DeepONet, TokenMixer, GraphOp, GraphOp2D) return UnsupportedOp; and
-// LoadNeuroIr fills a LoadedModelInfo (op, config block, weight count, NIRQ flag)
-// rather than the reference's weight-holding LoadedModel.
+// device given to CreateOnDevice); RunDeepONet refuses u and y of different batch
+// sizes (ShapeMismatch), and GraphOp / GraphOp2D a graph whose indices leave the node
+// range (InvalidArg), where the reference reads outside its buffers; and LoadNeuroIr
+// fills a LoadedModelInfo (op, config block, weight count, NIRQ flag) rather than the
+// reference's weight-holding LoadedModel.
 #pragma once
 
 #include <cstdint>
@@ -121,18 +122,30 @@ public:
                                                    y, y_shape.data(), static_cast<int>(y_shape.size())));
     }
 
-    Status RunDeepONet(const float*, const std::vector<int64_t>&, const float*,
-                       const std::vector<int64_t>&, float*, const std::vector<int64_t>&) {
-        return Status::UnsupportedOp("DeepONet is not executed by the GPU runtime");
+    // runtime.h:82-84
+    Status RunDeepONet(const float* u, const std::vector<int64_t>& u_shape, const float* y,
+                       const std::vector<int64_t>& y_shape, float* out, const std::vector<int64_t>& out_shape) {
+        return status(nfx_runtime_run_deeponet(rt_, u, u_shape.data(), static_cast<int>(u_shape.size()), y,
+                                               y_shape.data(), static_cast<int>(y_shape.size()), out,
+                                               out_shape.data(), static_cast<int>(out_shape.size())));
     }
-    Status RunTokenMixer(const float*, const std::vector<int64_t>&, float*, const std::vector<int64_t>&) {
-        return Status::UnsupportedOp("TokenMixer is not executed by the GPU runtime");
+    // runtime.h:88-89
+    Status RunTokenMixer(const float* x, const std::vector<int64_t>& x_shape, float* y,
+                         const std::vector<int64_t>& y_shape) {
+        return status(nfx_runtime_run_tokenmixer(rt_, x, x_shape.data(), static_cast<int>(x_shape.size()), y,
+                                                 y_shape.data(), static_cast<int>(y_shape.size())));
     }
-    Status RunGraphOp(const float*, const std::vector<int64_t>&, float*, const std::vector<int64_t>&) {
-        return Status::UnsupportedOp("GraphOp is not executed by the GPU runtime");
+    // runtime.h:93-94
+    Status RunGraphOp(const float* x, const std::vector<int64_t>& x_shape, float* y,
+                      const std::vector<int64_t>& y_shape) {
+        return status(nfx_runtime_run_graphop(rt_, x, x_shape.data(), static_cast<int>(x_shape.size()), y,
+                                              y_shape.data(), static_cast<int>(y_shape.size())));
     }
-    Status RunGraphOp2D(const float*, const std::vector<int64_t>&, float*, const std::vector<int64_t>&) {
-        return Status::UnsupportedOp("GraphOp2D is not executed by the GPU runtime");
+    // runtime.h:103-104
+    Status RunGraphOp2D(const float* x, const std::vector<int64_t>& x_shape, float* y,
+                        const std::vector<int64_t>& y_shape) {
+        return status(nfx_runtime_run_graphop2d(rt_, x, x_shape.data(), static_cast<int>(x_shape.size()), y,
+                                                y_shape.data(), static_cast<int>(y_shape.size())));
     }
 
     const std::string& op() const { return op_; }

@@ -59,9 +59,11 @@ const char* nfx_runtime_op(const nfx_runtime* rt);
  * the reference's semantics (the flag is set; layers whose input key has per-tensor
  * qparams and whose weight has per-channel qparams run through the INT8 GEMM).  On
  * this runtime it also enables INT8 executors the reference does not have: FNO2d
- * (per-channel weight and per-tensor activation qparams needed) and TokenMixer2D
- * (per-channel weight qparams of q/k/v/o/ffn0/ffn1, per-token activation qparams
- * computed at run time); without those qparams it is a no-op like the reference. */
+ * (with a NIRQ block: each layer input snapped with its key's per-tensor qparams, and
+ * locs.i / proj_q through the INT8 GEMM where the weight has per-channel qparams and
+ * the input key per-tensor ones) and TokenMixer2D / TokenMixer (per-channel weight
+ * qparams of q/k/v/o/ffn0/ffn1, per-token activation qparams computed at run time);
+ * without those qparams it is a no-op like the reference. */
 void nfx_runtime_enable_int8_gemm(nfx_runtime* rt);
 
 /* InferenceRuntime::IsInt8GemmEnabled (runtime.h:126-128). */
@@ -90,7 +92,7 @@ int nfx_runtime_run_device(nfx_runtime* rt, const float* x, const int64_t* x_sha
                            int x_rank, float* y, const int64_t* y_shape, int y_rank,
                            void* stream);
 
-/* InferenceRuntime::RunTokenMixer2D (runtime.h:98-101, runtime.cpp:142-151): x
+/* InferenceRuntime::RunTokenMixer2D (runtime.h:98-99, runtime.cpp:135-143): x
  * (batch, h, w, in_dim) -> y (batch, h, w, out_dim), HOST buffers, synchronous.  On a
  * runtime whose op is not TokenMixer2D it returns NFX_INTERNAL "TokenMixer2D not
  * initialized" as the reference does; nfx_runtime_run on a TokenMixer2D runtime returns
@@ -103,6 +105,52 @@ int nfx_runtime_run_tokenmixer2d(nfx_runtime* rt, const float* x, const int64_t*
 int nfx_runtime_run_tokenmixer2d_device(nfx_runtime* rt, const float* x,
                                         const int64_t* x_shape, int x_rank, float* y,
                                         const int64_t* y_shape, int y_rank, void* stream);
+
+/* InferenceRuntime::RunTokenMixer (runtime.h:88-89, runtime.cpp:115-123): the 1D
+ * TokenMixer, x (batch, n_points, in_dim) -> y (batch, n_points, out_dim), HOST
+ * buffers, synchronous; the TokenMixer2D executor on a 1 x n_points grid (the same
+ * network, fno.cpp:1460-1644).  Another op: NFX_INTERNAL "TokenMixer not initialized". */
+int nfx_runtime_run_tokenmixer(nfx_runtime* rt, const float* x, const int64_t* x_shape,
+                               int x_rank, float* y, const int64_t* y_shape, int y_rank);
+int nfx_runtime_run_tokenmixer_device(nfx_runtime* rt, const float* x, const int64_t* x_shape,
+                                      int x_rank, float* y, const int64_t* y_shape, int y_rank,
+                                      void* stream);
+
+/* InferenceRuntime::RunGraphOp (runtime.h:93-94, runtime.cpp:125-133): x (batch,
+ * n_nodes, in_dim) -> y (batch, n_nodes, out_dim), HOST buffers, synchronous
+ * (GraphOp::Forward, fno.cpp:1653-1741).  The reference's shape checks and messages; a
+ * graph whose CSR indices or offsets leave the node range (the reference reads outside
+ * its buffers) returns NFX_INVALID_ARG.  Another op: NFX_INTERNAL "GraphOp not
+ * initialized". */
+int nfx_runtime_run_graphop(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
+                            float* y, const int64_t* y_shape, int y_rank);
+int nfx_runtime_run_graphop_device(nfx_runtime* rt, const float* x, const int64_t* x_shape,
+                                   int x_rank, float* y, const int64_t* y_shape, int y_rank,
+                                   void* stream);
+
+/* InferenceRuntime::RunGraphOp2D (runtime.h:103-104, runtime.cpp:145-153): x (batch, h,
+ * w, in_dim) -> y (batch, h, w, out_dim), as nfx_runtime_run_graphop (GraphOp2D::Forward,
+ * fno.cpp:1969-2060).  Another op: NFX_INTERNAL "GraphOp2D not initialized". */
+int nfx_runtime_run_graphop2d(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
+                              float* y, const int64_t* y_shape, int y_rank);
+int nfx_runtime_run_graphop2d_device(nfx_runtime* rt, const float* x, const int64_t* x_shape,
+                                     int x_rank, float* y, const int64_t* y_shape, int y_rank,
+                                     void* stream);
+
+/* InferenceRuntime::RunDeepONet (runtime.h:82-84, runtime.cpp:103-113): u (batch,
+ * n_sensor, in_branch), y (batch, n_query, in_trunk) -> out (batch, n_query,
+ * out_channels), HOST buffers, synchronous (DeepONet::Forward, fno.cpp:1289-1406).  The
+ * reference's shape checks and messages, plus NFX_SHAPE_MISMATCH when u and y hold
+ * different batch sizes (the reference reads y with u's batch).  Layer weights whose
+ * shapes disagree with the widths the loader derives give NFX_UNSUPPORTED_OP (the
+ * reference reads past them).  Another op: NFX_INTERNAL "DeepONet not initialized". */
+int nfx_runtime_run_deeponet(nfx_runtime* rt, const float* u, const int64_t* u_shape, int u_rank,
+                             const float* y, const int64_t* y_shape, int y_rank, float* out,
+                             const int64_t* out_shape, int out_rank);
+int nfx_runtime_run_deeponet_device(nfx_runtime* rt, const float* u, const int64_t* u_shape,
+                                    int u_rank, const float* y, const int64_t* y_shape, int y_rank,
+                                    float* out, const int64_t* out_shape, int out_rank,
+                                    void* stream);
 
 /* Allocation-free variant of nfx_runtime_run_device, for callers that cannot call
  * cudaMalloc while they run inference (their device memory belongs to another

@@ -50,6 +50,19 @@ if hasattr(lib, "nfx_runtime_create"):
     lib.nfx_runtime_enable_fp8.argtypes = [_vp]
     lib.nfx_runtime_is_fp8_enabled.restype = C.c_int
     lib.nfx_runtime_is_fp8_enabled.argtypes = [_vp]
+    for name in ("tokenmixer", "graphop", "graphop2d"):
+        f = getattr(lib, "nfx_runtime_run_" + name)
+        f.restype = C.c_int
+        f.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int]
+        f = getattr(lib, "nfx_runtime_run_" + name + "_device")
+        f.restype = C.c_int
+        f.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int, _vp]
+    lib.nfx_runtime_run_deeponet.restype = C.c_int
+    lib.nfx_runtime_run_deeponet.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int, _vp,
+                                             _i64p, C.c_int]
+    lib.nfx_runtime_run_deeponet_device.restype = C.c_int
+    lib.nfx_runtime_run_deeponet_device.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int,
+                                                    _vp, _i64p, C.c_int, _vp]
     lib.nfx_runtime_run_tokenmixer2d.restype = C.c_int
     lib.nfx_runtime_run_tokenmixer2d.argtypes = [_vp, _vp, _i64p, C.c_int, _vp, _i64p, C.c_int]
     lib.nfx_runtime_run_tokenmixer2d_device.restype = C.c_int

@@ -3,8 +3,10 @@
 // Written against nflow::InferenceRuntime (include/nflow_runtime.hpp), the reference's
 // C++ interface over the C-ABI, as the reference CLI is written against its own.
 // Extra flags: --int8 (EnableInt8Gemm), --fp8 (the FNO3d E4M3 executor), --device N.
-// TokenMixer2D models run through RunTokenMixer2D like the reference's `infer`
-// (pybind_module.cpp:61-111).  Exit code 0 on success, 1 on any error, as the reference.
+// TokenMixer, GraphOp, TokenMixer2D and GraphOp2D models run through their own Run
+// calls like the reference's `infer` (pybind_module.cpp:61-111); DeepONet, with two
+// inputs, is refused as by the reference CLI.  Exit code 0 on success, 1 on any error,
+// as the reference.
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -153,7 +155,8 @@ int main(int argc, char** argv) {
     if (ops == "FNO1d") rank = 3, out_ch = info.cfg[1];
     else if (ops == "FNO2d") rank = 4, out_ch = info.cfg[1];
     else if (ops == "FNO3d") rank = 5, out_ch = info.cfg[1];
-    else if (ops == "TokenMixer2D") rank = 4, out_ch = info.cfg[1];
+    else if (ops == "TokenMixer2D" || ops == "GraphOp2D") rank = 4, out_ch = info.cfg[1];
+    else if (ops == "TokenMixer" || ops == "GraphOp") rank = 3, out_ch = info.cfg[1];
     else {
         std::cerr << "unsupported op in IR: " << ops << std::endl;
         return 1;
@@ -182,8 +185,11 @@ int main(int argc, char** argv) {
     int64_t ny = 1;
     for (auto d : ys) ny *= d;
     std::vector<float> y(static_cast<size_t>(ny));
-    st = ops == "TokenMixer2D" ? rt->RunTokenMixer2D(x.data(), xs, y.data(), ys)
-                               : rt->Run(x.data(), xs, y.data(), ys);
+    if (ops == "TokenMixer2D") st = rt->RunTokenMixer2D(x.data(), xs, y.data(), ys);
+    else if (ops == "TokenMixer") st = rt->RunTokenMixer(x.data(), xs, y.data(), ys);
+    else if (ops == "GraphOp") st = rt->RunGraphOp(x.data(), xs, y.data(), ys);
+    else if (ops == "GraphOp2D") st = rt->RunGraphOp2D(x.data(), xs, y.data(), ys);
+    else st = rt->Run(x.data(), xs, y.data(), ys);
     if (!st.ok()) {
         std::cerr << "inference failed: " << st.message() << std::endl;
         return 1;

@@ -23,6 +23,7 @@
 #include "nfx_internal.h"
 #include "nfx_ir.h"
 #include "nfx_copy_pool.h"
+#include "mlp_ops.h"
 #include "nfx_lut.h"
 #include "tm2d.h"
 
@@ -213,6 +214,15 @@ struct nfx_runtime {
     nfx::Tm2dPlan plan_tm{};
     void* tm_bufs[13] = {};
     int64_t tm_cap_T = 0, tm_cap_P = 0;
+    // DeepONet / GraphOp / GraphOp2D state (mlp_ops.h): the layer chains with their
+    // device weights; `mo_why` is why Run refuses the model (empty: runnable)
+    nfx::MlpArgs mo_branch{}, mo_trunk{}, mo_lift{}, mo_head{};
+    nfx::GraphLayerArgs mo_blocks[nfx::kMlpMaxLayers] = {};
+    const float* mo_bias = nullptr;
+    int mo_nodes = 0, mo_layers = 0, mo_code = 0;
+    std::string mo_why;
+    void* mo_bufs[2] = {nullptr, nullptr};
+    int64_t mo_cap[2] = {0, 0};
     // FNO1d state
     nfx::Fno1dPlan plan1{};
     int pt_n[nfx::kFno1dMaxLayers] = {};   // per-token table sizes (locs.i.output)
@@ -1258,18 +1268,27 @@ const char* kTmParts[8] = {"ln1", "q_proj", "k_proj", "v_proj", "o_proj", "ln2",
 
 int tm2d_create(nfx_runtime* rt) {
     // the reference runtime builds TokenMixer2D from the raw weights and ignores NIRQ
-    // (runtime.cpp:61-64)
+    // (runtime.cpp:61-64).  The 1D TokenMixer (fno.cpp:1460-1644) is the same network
+    // on n_points points: it runs as a 1 x n_points grid.
     auto& m = rt->model;
     auto& pl = rt->plan_tm;
     const int* c = m.cfg;
     pl.in_d = c[0];
     pl.out_d = c[1];
     pl.L = c[2];
-    pl.h = c[3];
-    pl.w = c[4];
-    pl.NP = c[5];
-    pl.heads = c[6];
-    pl.layers = c[7];
+    if (m.op == "TokenMixer") {
+        pl.h = 1;
+        pl.w = c[3];
+        pl.NP = c[4];
+        pl.heads = c[5];
+        pl.layers = c[6];
+    } else {
+        pl.h = c[3];
+        pl.w = c[4];
+        pl.NP = c[5];
+        pl.heads = c[6];
+        pl.layers = c[7];
+    }
     pl.act = m.activation == "relu" ? 1 : 0;
     if (pl.layers < 1 || pl.layers > nfx::kTm2dMaxLayers) return NFX_OK;  // Run reports it
     pl.se_w = wptr(rt, "slice_embed.proj.weight");
@@ -1324,7 +1343,28 @@ void tm2d_enable_int8(nfx_runtime* rt) {
     rt->int8_enabled = true;
 }
 
+int check_tm1d_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t* ys, int yr) {
+    // fno.cpp:1461-1497
+    const auto& pl = rt->plan_tm;
+    if (xr != 3) return rt_fail(rt, NFX_SHAPE_MISMATCH, "TokenMixer: expected 3D x (batch, n_points, in_dim)");
+    if (xs[2] != pl.in_d) return rt_fail(rt, NFX_SHAPE_MISMATCH, "TokenMixer: input feature dim mismatch");
+    if (xs[1] != pl.w) return rt_fail(rt, NFX_SHAPE_MISMATCH, "TokenMixer: n_points mismatch");
+    if (yr != 3 || ys[0] != xs[0] || ys[1] != xs[1] || ys[2] != pl.out_d)
+        return rt_fail(rt, NFX_SHAPE_MISMATCH, "TokenMixer: output buffer shape mismatch");
+    if (pl.NP <= 0 || pl.w % pl.NP != 0)
+        return rt_fail(rt, NFX_INVALID_ARG, "TokenMixer: n_points must be a multiple of n_patches");
+    if (pl.heads <= 0 || pl.L % pl.heads != 0)
+        return rt_fail(rt, NFX_INVALID_ARG, "TokenMixer: latent_dim must be a multiple of n_heads");
+    if (pl.layers < 1) return rt_fail(rt, NFX_INVALID_ARG, "TokenMixer: n_layers must be >= 1");
+    if (pl.layers > nfx::kTm2dMaxLayers || !pl.se_w)
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, "TokenMixer GPU executor: at most 8 blocks");
+    if (const char* why = nfx::tm2d_unsupported(pl.L, pl.heads, pl.in_d, pl.out_d))
+        return rt_fail(rt, NFX_UNSUPPORTED_OP, why);
+    return NFX_OK;
+}
+
 int check_tm2d_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t* ys, int yr) {
+    if (rt->model.op == "TokenMixer") return check_tm1d_shapes(rt, xs, xr, ys, yr);
     const auto& pl = rt->plan_tm;
     if (xr != 4) return rt_fail(rt, NFX_SHAPE_MISMATCH, "TokenMixer2D: expected 4D x (batch, h, w, in_dim)");
     if (xs[3] != pl.in_d) return rt_fail(rt, NFX_SHAPE_MISMATCH, "TokenMixer2D: input feature dim mismatch");
@@ -1383,6 +1423,299 @@ int tm2d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, 
     const cudaError_t e = nfx::tm2d_run(pl, st);
     if (e != cudaSuccess)
         return rt_fail(rt, NFX_INTERNAL, std::string("TokenMixer2D launch failed: ") + cudaGetErrorString(e));
+    return NFX_OK;
+}
+
+// ---------------------------------------------------------------------------
+// DeepONet (fno.cpp:1289-1406), GraphOp / GraphOp2D (fno.cpp:1653-1741, :1969-2060)
+// ---------------------------------------------------------------------------
+
+// A weight the reference indexes as (out, in) with the widths the loader derived;
+// the reference reads past a tensor whose shape disagrees, the GPU runtime refuses it.
+bool mo_layer(nfx_runtime* rt, const std::string& wname, const std::string& bname, int in, int out,
+              nfx::MlpLayer& L) {
+    const auto& w = rt->model.weights.at(wname);
+    const auto& b = rt->model.weights.at(bname);
+    if (w.numel() != static_cast<int64_t>(in) * out || b.numel() < out) {
+        rt->mo_why = wname + " does not hold the (" + std::to_string(out) + ", " + std::to_string(in) +
+                     ") weight the configuration implies";
+        return false;
+    }
+    L.w = upload(rt, w.data.data(), w.data.size());
+    L.b = upload(rt, b.data.data(), b.data.size());
+    L.in = in;
+    L.out = out;
+    if (!L.w || !L.b) {
+        rt->mo_why = "weight upload failed";
+        return false;
+    }
+    return true;
+}
+
+int deeponet_create(nfx_runtime* rt) {
+    auto& m = rt->model;
+    const int* c = m.cfg;
+    const int in_b = c[0], in_t = c[1], lat = c[2], oc = c[3], nb = c[4], nt = c[5];
+    const int act = m.activation == "relu" ? 1 : 0;
+    // hidden widths from the second-to-last layer of each net (ir_loader.h:536-547)
+    auto hidden = [&](const char* net, int n) {
+        if (n < 2) return 0;
+        const auto& w = m.weights.at(std::string(net) + ".layers." + std::to_string(n - 2) + ".weight");
+        return w.shape.empty() ? 0 : static_cast<int>(w.shape[0]);
+    };
+    if (nb < 1 || nt < 1 || nb > nfx::kMlpMaxLayers || nt > nfx::kMlpMaxLayers) {
+        rt->mo_why = "DeepONet GPU executor: 1 to 8 layers per net";
+        rt->mo_code = NFX_UNSUPPORTED_OP;
+        return NFX_OK;
+    }
+    const int hb = hidden("branch", nb), ht = hidden("trunk", nt);
+    struct Net {
+        const char* name;
+        int n, in0, hid, last;
+        nfx::MlpArgs* args;
+    } nets[2] = {{"branch", nb, in_b, hb, oc * lat, &rt->mo_branch}, {"trunk", nt, in_t, ht, lat, &rt->mo_trunk}};
+    for (const Net& net : nets) {
+        nfx::MlpArgs& a = *net.args;
+        a = nfx::MlpArgs{};
+        a.n_layers = net.n;
+        a.act = act;
+        for (int i = 0; i < net.n; ++i) {
+            const std::string pre = std::string(net.name) + ".layers." + std::to_string(i);
+            const int in = i == 0 ? net.in0 : net.hid, out = i == net.n - 1 ? net.last : net.hid;
+            if (!mo_layer(rt, pre + ".weight", pre + ".bias", in, out, a.layer[i])) {
+                rt->mo_code = NFX_UNSUPPORTED_OP;
+                return rt->mo_why == "weight upload failed" ? rt_fail(rt, NFX_INTERNAL, rt->mo_why) : NFX_OK;
+            }
+        }
+        if (nfx::mlp_max_dim(a) > nfx::kMlpMaxDim) {
+            rt->mo_why = "DeepONet GPU executor: layer widths above 512";
+            rt->mo_code = NFX_UNSUPPORTED_OP;
+            return NFX_OK;
+        }
+    }
+    const auto& bias = m.weights.at("bias.weight");
+    if (bias.numel() < oc) {
+        rt->mo_why = "bias.weight holds fewer than out_channels values";
+        rt->mo_code = NFX_UNSUPPORTED_OP;
+        return NFX_OK;
+    }
+    rt->mo_bias = upload(rt, bias.data.data(), bias.data.size());
+    if (!rt->mo_bias) return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+    return NFX_OK;
+}
+
+int graphop_create(nfx_runtime* rt) {
+    auto& m = rt->model;
+    const int* c = m.cfg;
+    const bool two = m.op == "GraphOp2D";
+    const int in_d = c[0], out_d = c[1];
+    const int nodes = two ? c[2] * c[3] : c[2];
+    const int hd = two ? c[4] : c[3], L = two ? c[5] : c[4];
+    const int act = m.activation == "relu" ? 1 : 0;
+    rt->mo_nodes = nodes;
+    rt->mo_layers = L;
+    if (L < 1) return NFX_OK;  // Run reports it (fno.cpp:1675-1677)
+    if (L > nfx::kMlpMaxLayers || hd < 1 || hd > nfx::kGraphMaxHidden || in_d > nfx::kMlpMaxDim ||
+        out_d > nfx::kMlpMaxDim) {
+        rt->mo_why = m.op + " GPU executor: at most 8 blocks and hidden_dim <= 256";
+        rt->mo_code = NFX_UNSUPPORTED_OP;
+        return NFX_OK;
+    }
+    auto fail = [&]() {
+        rt->mo_code = NFX_UNSUPPORTED_OP;
+        return rt->mo_why == "weight upload failed" ? rt_fail(rt, NFX_INTERNAL, rt->mo_why) : NFX_OK;
+    };
+    rt->mo_lift = nfx::MlpArgs{};
+    rt->mo_lift.n_layers = 1;
+    rt->mo_head = rt->mo_lift;
+    if (!mo_layer(rt, "lift.weight", "lift.bias", in_d, hd, rt->mo_lift.layer[0]) ||
+        !mo_layer(rt, "head.weight", "head.bias", hd, out_d, rt->mo_head.layer[0]))
+        return fail();
+    for (int i = 0; i < L; ++i) {
+        const std::string pre = "blocks." + std::to_string(i) + ".";
+        nfx::MlpLayer ls{}, ln{};
+        if (!mo_layer(rt, pre + "lin_self.weight", pre + "lin_self.bias", hd, hd, ls) ||
+            !mo_layer(rt, pre + "lin_neigh.weight", pre + "lin_neigh.bias", hd, hd, ln))
+            return fail();
+        nfx::GraphLayerArgs& g = rt->mo_blocks[i];
+        g = nfx::GraphLayerArgs{};
+        g.n_nodes = nodes;
+        g.hidden = hd;
+        g.act = act;
+        g.ws = ls.w;
+        g.bs = ls.b;
+        g.wn = ln.w;
+        g.bn = ln.b;
+    }
+    // CSR adjacency: float tensors converted as the loader does (ir_loader.h:421-431)
+    const auto& off = m.weights.at("graph.adj_offsets").data;
+    const auto& idx = m.weights.at("graph.adj_indices").data;
+    const auto& dinv = m.weights.at("graph.deg_inv").data;
+    std::vector<int32_t> o32(off.size()), i32(idx.size());
+    for (size_t k = 0; k < off.size(); ++k) o32[k] = static_cast<int32_t>(off[k]);
+    for (size_t k = 0; k < idx.size(); ++k) i32[k] = static_cast<int32_t>(idx[k]);
+    if (static_cast<int>(o32.size()) == nodes + 1 && static_cast<int>(dinv.size()) == nodes) {
+        // the reference reads outside h for an index or offset out of range; the GPU
+        // runtime refuses such a graph
+        bool ok = o32[0] == 0;
+        for (int k = 0; k < nodes && ok; ++k) ok = o32[k] <= o32[k + 1];
+        ok = ok && o32[nodes] <= static_cast<int32_t>(i32.size());
+        for (size_t k = 0; k < i32.size() && ok; ++k) ok = i32[k] >= 0 && i32[k] < nodes;
+        if (!ok) {
+            rt->mo_why = m.op + ": adjacency offsets or indices out of range";
+            rt->mo_code = NFX_INVALID_ARG;
+            return NFX_OK;
+        }
+    }
+    const int* doff = upload(rt, o32.data(), o32.size());
+    const int* didx = upload(rt, i32.data(), std::max<size_t>(i32.size(), 1));
+    const float* ddeg = upload(rt, dinv.data(), std::max<size_t>(dinv.size(), 1));
+    if (!doff || !didx || !ddeg) return rt_fail(rt, NFX_INTERNAL, "weight upload failed");
+    for (int i = 0; i < L; ++i) {
+        rt->mo_blocks[i].adj_off = doff;
+        rt->mo_blocks[i].adj_idx = didx;
+        rt->mo_blocks[i].deg_inv = ddeg;
+    }
+    return NFX_OK;
+}
+
+int ensure_mo_buf(nfx_runtime* rt, int i, int64_t floats) {
+    if (floats <= rt->mo_cap[i]) return NFX_OK;
+    if (rt->mo_bufs[i]) cudaFree(rt->mo_bufs[i]);
+    rt->mo_bufs[i] = nullptr;
+    rt->mo_cap[i] = 0;
+    if (!cuda_ok(rt, cudaMalloc(&rt->mo_bufs[i], static_cast<size_t>(floats) * 4 + 256), "cudaMalloc activations"))
+        return NFX_INTERNAL;
+    rt->mo_cap[i] = floats;
+    return NFX_OK;
+}
+
+// fno.cpp:1289-1311 (the reference's checks and messages), and u, y with one batch
+int check_deeponet_shapes(nfx_runtime* rt, const int64_t* us, int ur, const int64_t* ys, int yr,
+                          const int64_t* os, int orank) {
+    const int* c = rt->model.cfg;
+    if (ur != 3) return rt_fail(rt, NFX_SHAPE_MISMATCH, "DeepONet: expected 3D u (batch, n_sensor, in_branch)");
+    if (yr != 3) return rt_fail(rt, NFX_SHAPE_MISMATCH, "DeepONet: expected 3D y (batch, n_query, in_trunk)");
+    if (us[2] != c[0]) return rt_fail(rt, NFX_SHAPE_MISMATCH, "DeepONet: input branch feature dim mismatch");
+    if (ys[2] != c[1]) return rt_fail(rt, NFX_SHAPE_MISMATCH, "DeepONet: input trunk feature dim mismatch");
+    if (orank != 3 || os[0] != us[0] || os[1] != ys[1] || os[2] != c[3])
+        return rt_fail(rt, NFX_SHAPE_MISMATCH, "DeepONet: output buffer shape mismatch");
+    // the reference reads y with u's batch size
+    if (ys[0] != us[0]) return rt_fail(rt, NFX_SHAPE_MISMATCH, "DeepONet: u and y batch sizes differ");
+    if (!rt->mo_why.empty()) return rt_fail(rt, rt->mo_code ? rt->mo_code : NFX_UNSUPPORTED_OP, rt->mo_why);
+    return NFX_OK;
+}
+
+int deeponet_launch(nfx_runtime* rt, const float* du, const int64_t* us, const float* dy, const int64_t* ys,
+                    float* dout, cudaStream_t st) {
+    const int* c = rt->model.cfg;
+    const int64_t B = us[0], ns = us[1], nq = ys[1];
+    const int F = c[3] * c[2];
+    if (B == 0 || nq == 0) return NFX_OK;
+    int s = ensure_mo_buf(rt, 0, B * ns * F);
+    if (s == NFX_OK) s = ensure_mo_buf(rt, 1, B * F);
+    if (s != NFX_OK) return s;
+    float* bflat = static_cast<float*>(rt->mo_bufs[0]);
+    float* bmean = static_cast<float*>(rt->mo_bufs[1]);
+    nfx::MlpArgs br = rt->mo_branch;
+    br.x = du;
+    br.rows = B * ns;
+    br.y = bflat;
+    nfx::MeanArgs mean{bflat, bmean, B, static_cast<int>(ns), F};
+    nfx::MlpArgs tr = rt->mo_trunk;
+    tr.x = dy;
+    tr.rows = B * nq;
+    tr.y = dout;
+    tr.dot_branch = bmean;
+    tr.dot_bias = rt->mo_bias;
+    tr.dot_ch = c[3];
+    tr.rows_per_group = nq;
+    cudaError_t e = cudaSuccess;
+    auto* tm = rt->timer.get();
+    if (tm) tm->begin("deeponet_branch", st);
+    if (ns > 0) e = nfx::mlp_rows(br, st);
+    if (tm) tm->end(st);
+    if (e == cudaSuccess) {
+        if (tm) tm->begin("deeponet_mean", st);
+        e = nfx::sensor_mean(mean, st);
+        if (tm) tm->end(st);
+    }
+    if (e == cudaSuccess) {
+        if (tm) tm->begin("deeponet_trunk_dot", st);
+        e = nfx::mlp_rows(tr, st);
+        if (tm) tm->end(st);
+    }
+    if (e != cudaSuccess)
+        return rt_fail(rt, NFX_INTERNAL, std::string("DeepONet launch failed: ") + cudaGetErrorString(e));
+    return NFX_OK;
+}
+
+// fno.cpp:1653-1687 (GraphOp) and :1969-2010 (GraphOp2D): checks and messages
+int check_graphop_shapes(nfx_runtime* rt, const int64_t* xs, int xr, const int64_t* ys, int yr) {
+    const auto& m = rt->model;
+    const int* c = m.cfg;
+    const bool two = m.op == "GraphOp2D";
+    const std::string& op = m.op;
+    if (two) {
+        if (xr != 4) return rt_fail(rt, NFX_SHAPE_MISMATCH, "GraphOp2D: expected 4D x (batch, h, w, in_dim)");
+        if (xs[3] != c[0]) return rt_fail(rt, NFX_SHAPE_MISMATCH, "GraphOp2D: input feature dim mismatch");
+        if (xs[1] != c[2] || xs[2] != c[3]) return rt_fail(rt, NFX_SHAPE_MISMATCH, "GraphOp2D: h / w mismatch");
+        if (yr != 4 || ys[0] != xs[0] || ys[1] != xs[1] || ys[2] != xs[2] || ys[3] != c[1])
+            return rt_fail(rt, NFX_SHAPE_MISMATCH, "GraphOp2D: output buffer shape mismatch");
+    } else {
+        if (xr != 3) return rt_fail(rt, NFX_SHAPE_MISMATCH, "GraphOp: expected 3D x (batch, n_nodes, in_dim)");
+        if (xs[2] != c[0]) return rt_fail(rt, NFX_SHAPE_MISMATCH, "GraphOp: input feature dim mismatch");
+        if (xs[1] != c[2]) return rt_fail(rt, NFX_SHAPE_MISMATCH, "GraphOp: n_nodes mismatch");
+        if (yr != 3 || ys[0] != xs[0] || ys[1] != xs[1] || ys[2] != c[1])
+            return rt_fail(rt, NFX_SHAPE_MISMATCH, "GraphOp: output buffer shape mismatch");
+    }
+    if (rt->mo_layers < 1) return rt_fail(rt, NFX_INVALID_ARG, op + ": n_layers must be >= 1");
+    const int nodes = rt->mo_nodes;
+    if (static_cast<int>(m.weights.at("graph.adj_offsets").data.size()) != nodes + 1)
+        return rt_fail(rt, NFX_INTERNAL, op + ": adj_offsets size mismatch");
+    if (static_cast<int>(m.weights.at("graph.deg_inv").data.size()) != nodes)
+        return rt_fail(rt, NFX_INTERNAL, op + ": deg_inv size mismatch");
+    if (!rt->mo_why.empty()) return rt_fail(rt, rt->mo_code ? rt->mo_code : NFX_UNSUPPORTED_OP, rt->mo_why);
+    return NFX_OK;
+}
+
+int graphop_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy, cudaStream_t st) {
+    const int64_t B = xs[0];
+    if (B == 0) return NFX_OK;
+    const int64_t rows = B * rt->mo_nodes;
+    const int hd = rt->mo_blocks[0].hidden;
+    int s = ensure_mo_buf(rt, 0, rows * hd);
+    if (s == NFX_OK) s = ensure_mo_buf(rt, 1, rows * hd);
+    if (s != NFX_OK) return s;
+    float* h[2] = {static_cast<float*>(rt->mo_bufs[0]), static_cast<float*>(rt->mo_bufs[1])};
+    auto* tm = rt->timer.get();
+    nfx::MlpArgs lift = rt->mo_lift;
+    lift.x = dx;
+    lift.rows = rows;
+    lift.y = h[0];
+    if (tm) tm->begin("graphop_lift", st);
+    cudaError_t e = nfx::mlp_rows(lift, st);
+    if (tm) tm->end(st);
+    for (int i = 0; i < rt->mo_layers && e == cudaSuccess; ++i) {
+        nfx::GraphLayerArgs g = rt->mo_blocks[i];
+        g.h = h[i & 1];
+        g.out = h[(i + 1) & 1];
+        g.rows = rows;
+        if (tm) tm->begin("graphop_block", st);
+        e = nfx::graph_layer(g, st);
+        if (tm) tm->end(st);
+    }
+    if (e == cudaSuccess) {
+        nfx::MlpArgs head = rt->mo_head;
+        head.x = h[rt->mo_layers & 1];
+        head.rows = rows;
+        head.y = dy;
+        if (tm) tm->begin("graphop_head", st);
+        e = nfx::mlp_rows(head, st);
+        if (tm) tm->end(st);
+    }
+    if (e != cudaSuccess)
+        return rt_fail(rt, NFX_INTERNAL, rt->model.op + " launch failed: " + cudaGetErrorString(e));
     return NFX_OK;
 }
 
@@ -1693,8 +2026,14 @@ int nfx_runtime_create(const char* ir_path, int device, nfx_runtime** out) {
     } else if (op == "FNO3d") {
         s = fno3d_create(rt.get());
         if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
-    } else if (op == "TokenMixer2D") {
+    } else if (op == "TokenMixer2D" || op == "TokenMixer") {
         s = tm2d_create(rt.get());
+        if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
+    } else if (op == "DeepONet") {
+        s = deeponet_create(rt.get());
+        if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
+    } else if (op == "GraphOp" || op == "GraphOp2D") {
+        s = graphop_create(rt.get());
         if (s != NFX_OK) return nfx::set_thread_error(s, rt->err);
     }
     if (!nfx::device_error_word())
@@ -1736,6 +2075,8 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
     for (void* p : rt->f2_bufs)
         if (p) cudaFree(p);
     for (void* p : rt->tm_bufs)
+        if (p) cudaFree(p);
+    for (void* p : rt->mo_bufs)
         if (p) cudaFree(p);
     for (void* p : rt->f3_bufs)
         if (p) cudaFree(p);
@@ -1806,7 +2147,7 @@ void nfx_runtime_enable_int8_gemm(nfx_runtime* rt) {
     DeviceGuard g(rt->device);
     if (rt->model.op == "FNO2d") fno2d_enable_int8(rt);
     if (rt->model.op == "FNO1d") fno1d_enable_int8(rt);
-    if (rt->model.op == "TokenMixer2D") tm2d_enable_int8(rt);
+    if (rt->model.op == "TokenMixer2D" || rt->model.op == "TokenMixer") tm2d_enable_int8(rt);
 }
 
 int nfx_runtime_is_int8_gemm_enabled(const nfx_runtime* rt) { return rt && rt->int8_enabled ? 1 : 0; }
@@ -1975,31 +2316,34 @@ void nfx_runtime_enable_fp8(nfx_runtime* rt) {
 
 int nfx_runtime_is_fp8_enabled(const nfx_runtime* rt) { return rt && rt->fp8_enabled ? 1 : 0; }
 
-int nfx_runtime_run_tokenmixer2d_device(nfx_runtime* rt, const float* x, const int64_t* x_shape,
-                                        int x_rank, float* y, const int64_t* y_shape, int y_rank,
-                                        void* stream) {
-    if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
-    if (!x_shape || !y_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
-    DeviceGuard g(rt->device);
-    if (rt->model.op != "TokenMixer2D") return rt_fail(rt, NFX_INTERNAL, "TokenMixer2D not initialized");
-    int s = check_tm2d_shapes(rt, x_shape, x_rank, y_shape, y_rank);
-    if (s != NFX_OK) return s;
-    if (numel(x_shape, x_rank) > 0 && (!x || !y)) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
-    return tm2d_launch(rt, x, x_shape, y, static_cast<cudaStream_t>(stream));
+}  // extern "C"
+
+namespace {
+
+// Single-input ops outside Run (RunTokenMixer2D, RunTokenMixer, RunGraphOp,
+// RunGraphOp2D; runtime.cpp:115-153): the op's shape checks, then its launcher on
+// device buffers, or through the runtime's device staging for host buffers.
+using OpCheck = int (*)(nfx_runtime*, const int64_t*, int, const int64_t*, int);
+using OpLaunch = int (*)(nfx_runtime*, const float*, const int64_t*, float*, cudaStream_t);
+
+bool op_is(const nfx_runtime* rt, const char* a, const char* b = nullptr) {
+    return rt->model.op == a || (b && rt->model.op == b);
 }
 
-int nfx_runtime_run_tokenmixer2d(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
-                                 float* y, const int64_t* y_shape, int y_rank) {
+int run_other_device(nfx_runtime* rt, const char* op, bool ok_op, OpCheck check, OpLaunch launch_fn,
+                     const float* x, const int64_t* x_shape, int x_rank, float* y, const int64_t* y_shape,
+                     int y_rank, void* stream) {
     if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
     if (!x_shape || !y_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
     DeviceGuard g(rt->device);
-    if (rt->model.op != "TokenMixer2D") return rt_fail(rt, NFX_INTERNAL, "TokenMixer2D not initialized");
-    int s = check_tm2d_shapes(rt, x_shape, x_rank, y_shape, y_rank);
+    if (!ok_op) return rt_fail(rt, NFX_INTERNAL, std::string(op) + " not initialized");
+    int s = check(rt, x_shape, x_rank, y_shape, y_rank);
     if (s != NFX_OK) return s;
-    const size_t nx = static_cast<size_t>(numel(x_shape, x_rank));
-    const size_t ny = static_cast<size_t>(numel(y_shape, y_rank));
-    if (nx == 0) return NFX_OK;
-    if (!x || !y) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
+    if (numel(x_shape, x_rank) > 0 && (!x || !y)) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
+    return launch_fn(rt, x, x_shape, y, static_cast<cudaStream_t>(stream));
+}
+
+int ensure_staging(nfx_runtime* rt, size_t nx, size_t ny) {
     if (nx > rt->dx_cap) {
         if (rt->dx) cudaFree(rt->dx);
         rt->dx = nullptr;
@@ -2012,11 +2356,132 @@ int nfx_runtime_run_tokenmixer2d(nfx_runtime* rt, const float* x, const int64_t*
         if (!cuda_ok(rt, cudaMalloc(&rt->dy, ny * 4), "cudaMalloc output")) return NFX_INTERNAL;
         rt->dy_cap = ny;
     }
+    return NFX_OK;
+}
+
+int run_other_host(nfx_runtime* rt, const char* op, bool ok_op, OpCheck check, OpLaunch launch_fn,
+                   const float* x, const int64_t* x_shape, int x_rank, float* y, const int64_t* y_shape,
+                   int y_rank) {
+    if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
+    if (!x_shape || !y_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
+    DeviceGuard g(rt->device);
+    if (!ok_op) return rt_fail(rt, NFX_INTERNAL, std::string(op) + " not initialized");
+    int s = check(rt, x_shape, x_rank, y_shape, y_rank);
+    if (s != NFX_OK) return s;
+    const size_t nx = static_cast<size_t>(numel(x_shape, x_rank));
+    const size_t ny = static_cast<size_t>(numel(y_shape, y_rank));
+    if (nx == 0 || ny == 0) return NFX_OK;
+    if (!x || !y) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
+    s = ensure_staging(rt, nx, ny);
+    if (s != NFX_OK) return s;
     if (!cuda_ok(rt, cudaMemcpyAsync(rt->dx, x, nx * 4, cudaMemcpyHostToDevice, rt->stream), "H2D"))
         return NFX_INTERNAL;
-    s = tm2d_launch(rt, rt->dx, x_shape, rt->dy, rt->stream);
-    if (s != NFX_OK) return s;
+    s = launch_fn(rt, rt->dx, x_shape, rt->dy, rt->stream);
+    if (s != NFX_OK) {
+        cudaStreamSynchronize(rt->stream);
+        return s;
+    }
     if (!cuda_ok(rt, cudaMemcpyAsync(y, rt->dy, ny * 4, cudaMemcpyDeviceToHost, rt->stream), "D2H"))
+        return NFX_INTERNAL;
+    if (!cuda_ok(rt, cudaStreamSynchronize(rt->stream), "execution")) return NFX_INTERNAL;
+    return nfx_runtime_check(rt);
+}
+
+}  // namespace
+
+extern "C" {
+
+int nfx_runtime_run_tokenmixer2d_device(nfx_runtime* rt, const float* x, const int64_t* x_shape,
+                                        int x_rank, float* y, const int64_t* y_shape, int y_rank,
+                                        void* stream) {
+    return run_other_device(rt, "TokenMixer2D", rt && op_is(rt, "TokenMixer2D"), check_tm2d_shapes, tm2d_launch,
+                            x, x_shape, x_rank, y, y_shape, y_rank, stream);
+}
+
+int nfx_runtime_run_tokenmixer2d(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
+                                 float* y, const int64_t* y_shape, int y_rank) {
+    return run_other_host(rt, "TokenMixer2D", rt && op_is(rt, "TokenMixer2D"), check_tm2d_shapes, tm2d_launch, x,
+                          x_shape, x_rank, y, y_shape, y_rank);
+}
+
+int nfx_runtime_run_tokenmixer_device(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
+                                      float* y, const int64_t* y_shape, int y_rank, void* stream) {
+    return run_other_device(rt, "TokenMixer", rt && op_is(rt, "TokenMixer"), check_tm2d_shapes, tm2d_launch, x,
+                            x_shape, x_rank, y, y_shape, y_rank, stream);
+}
+
+int nfx_runtime_run_tokenmixer(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank, float* y,
+                               const int64_t* y_shape, int y_rank) {
+    return run_other_host(rt, "TokenMixer", rt && op_is(rt, "TokenMixer"), check_tm2d_shapes, tm2d_launch, x,
+                          x_shape, x_rank, y, y_shape, y_rank);
+}
+
+int nfx_runtime_run_graphop_device(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
+                                   float* y, const int64_t* y_shape, int y_rank, void* stream) {
+    return run_other_device(rt, "GraphOp", rt && op_is(rt, "GraphOp"), check_graphop_shapes, graphop_launch, x,
+                            x_shape, x_rank, y, y_shape, y_rank, stream);
+}
+
+int nfx_runtime_run_graphop(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank, float* y,
+                            const int64_t* y_shape, int y_rank) {
+    return run_other_host(rt, "GraphOp", rt && op_is(rt, "GraphOp"), check_graphop_shapes, graphop_launch, x,
+                          x_shape, x_rank, y, y_shape, y_rank);
+}
+
+int nfx_runtime_run_graphop2d_device(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank,
+                                     float* y, const int64_t* y_shape, int y_rank, void* stream) {
+    return run_other_device(rt, "GraphOp2D", rt && op_is(rt, "GraphOp2D"), check_graphop_shapes, graphop_launch,
+                            x, x_shape, x_rank, y, y_shape, y_rank, stream);
+}
+
+int nfx_runtime_run_graphop2d(nfx_runtime* rt, const float* x, const int64_t* x_shape, int x_rank, float* y,
+                              const int64_t* y_shape, int y_rank) {
+    return run_other_host(rt, "GraphOp2D", rt && op_is(rt, "GraphOp2D"), check_graphop_shapes, graphop_launch, x,
+                          x_shape, x_rank, y, y_shape, y_rank);
+}
+
+int nfx_runtime_run_deeponet_device(nfx_runtime* rt, const float* u, const int64_t* u_shape, int u_rank,
+                                    const float* y, const int64_t* y_shape, int y_rank, float* out,
+                                    const int64_t* out_shape, int out_rank, void* stream) {
+    if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
+    if (!u_shape || !y_shape || !out_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
+    DeviceGuard g(rt->device);
+    if (!op_is(rt, "DeepONet")) return rt_fail(rt, NFX_INTERNAL, "DeepONet not initialized");
+    int s = check_deeponet_shapes(rt, u_shape, u_rank, y_shape, y_rank, out_shape, out_rank);
+    if (s != NFX_OK) return s;
+    if (numel(out_shape, out_rank) > 0 && (!y || !out || (numel(u_shape, u_rank) > 0 && !u)))
+        return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
+    return deeponet_launch(rt, u, u_shape, y, y_shape, out, static_cast<cudaStream_t>(stream));
+}
+
+// runtime.cpp:103-113 RunDeepONet on host buffers: u and y staged one after the other
+int nfx_runtime_run_deeponet(nfx_runtime* rt, const float* u, const int64_t* u_shape, int u_rank,
+                             const float* y, const int64_t* y_shape, int y_rank, float* out,
+                             const int64_t* out_shape, int out_rank) {
+    if (!rt) return nfx::set_thread_error(NFX_INVALID_ARG, "null runtime");
+    if (!u_shape || !y_shape || !out_shape) return rt_fail(rt, NFX_INVALID_ARG, "null shape");
+    DeviceGuard g(rt->device);
+    if (!op_is(rt, "DeepONet")) return rt_fail(rt, NFX_INTERNAL, "DeepONet not initialized");
+    int s = check_deeponet_shapes(rt, u_shape, u_rank, y_shape, y_rank, out_shape, out_rank);
+    if (s != NFX_OK) return s;
+    const size_t nu = static_cast<size_t>(numel(u_shape, u_rank));
+    const size_t ny = static_cast<size_t>(numel(y_shape, y_rank));
+    const size_t no = static_cast<size_t>(numel(out_shape, out_rank));
+    if (no == 0) return NFX_OK;
+    if (!y || !out || (nu > 0 && !u)) return rt_fail(rt, NFX_INVALID_ARG, "null buffer");
+    s = ensure_staging(rt, nu + ny, no);
+    if (s != NFX_OK) return s;
+    float* du = rt->dx;
+    float* dyq = rt->dx + nu;
+    if ((nu > 0 && !cuda_ok(rt, cudaMemcpyAsync(du, u, nu * 4, cudaMemcpyHostToDevice, rt->stream), "H2D")) ||
+        !cuda_ok(rt, cudaMemcpyAsync(dyq, y, ny * 4, cudaMemcpyHostToDevice, rt->stream), "H2D"))
+        return NFX_INTERNAL;
+    s = deeponet_launch(rt, du, u_shape, dyq, y_shape, rt->dy, rt->stream);
+    if (s != NFX_OK) {
+        cudaStreamSynchronize(rt->stream);
+        return s;
+    }
+    if (!cuda_ok(rt, cudaMemcpyAsync(out, rt->dy, no * 4, cudaMemcpyDeviceToHost, rt->stream), "D2H"))
         return NFX_INTERNAL;
     if (!cuda_ok(rt, cudaStreamSynchronize(rt->stream), "execution")) return NFX_INTERNAL;
     return nfx_runtime_check(rt);

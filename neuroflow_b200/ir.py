@@ -43,6 +43,12 @@ CONFIG_KEYS = {
               "n_layers", "pad_factor"],
     "TokenMixer2D": ["in_dim", "out_dim", "latent_dim", "h", "w", "n_patches", "n_heads",
                      "n_layers"],
+    "DeepONet": ["in_branch", "in_trunk", "latent_dim", "out_channels", "n_layers_branch",
+                 "n_layers_trunk", "_"],
+    "TokenMixer": ["in_dim", "out_dim", "latent_dim", "n_points", "n_patches", "n_heads",
+                   "n_layers", "_"],
+    "GraphOp": ["in_dim", "out_dim", "n_nodes", "hidden_dim", "n_layers", "_", "_", "_"],
+    "GraphOp2D": ["in_dim", "out_dim", "h", "w", "hidden_dim", "n_layers", "_", "_"],
 }
 
 
@@ -98,6 +104,20 @@ def expected_weight_names(op: str, cfg: Dict[str, int]) -> List[str]:
                 names += [p + part + ".weight", p + part + ".bias"]
         names += ["unslice.proj.weight", "unslice.proj.bias", "head.weight", "head.bias"]
         return names
+    if op in ("GraphOp", "GraphOp2D"):
+        names = ["lift.weight", "lift.bias"]
+        for i in range(cfg["n_layers"]):
+            p = f"blocks.{i}."
+            names += [p + "lin_self.weight", p + "lin_self.bias", p + "lin_neigh.weight",
+                      p + "lin_neigh.bias"]
+        return names + ["head.weight", "head.bias", "graph.adj_offsets", "graph.adj_indices",
+                        "graph.deg_inv"]
+    if op == "DeepONet":
+        names = []
+        for net, n in (("branch", cfg["n_layers_branch"]), ("trunk", cfg["n_layers_trunk"])):
+            for i in range(n):
+                names += [f"{net}.layers.{i}.weight", f"{net}.layers.{i}.bias"]
+        return names + ["bias.weight"]
     raise ValueError(f"unsupported op for the writer: {op}")
 
 
@@ -176,7 +196,7 @@ def read_bytes(buf: bytes) -> Model:
     op = OP_BY_CODE[code]
     clen = OPS[op][2]
     cfg_vals = r.take(f"<{clen}i")
-    keys = CONFIG_KEYS.get(op, [f"c{i}" for i in range(clen)])
+    keys = CONFIG_KEYS[op]
     cfg = {k: v for k, v in zip(keys, cfg_vals) if k != "_"}
     (act,) = r.take("<B")
     r.raw(3)

@@ -1,7 +1,9 @@
 """Python front-end of the GPU runtime, mirroring the reference `neuroflow_cpp` module
 (cpp/bindings/pybind_module.cpp:61-197): `InferenceRuntime(path)` with `op()`,
-`enable_int8_gemm()`, `is_int8_gemm_enabled()`, `run(x, y)` and `run_tokenmixer2d(x, y)`,
-plus the module functions `infer` and `infer_arrays`.
+`enable_int8_gemm()`, `is_int8_gemm_enabled()`, `run(x, y)`, and the reference runtime's
+other Run calls (`run_tokenmixer2d`, `run_tokenmixer`, `run_graphop`, `run_graphop2d`,
+`run_deeponet`), plus the module functions `infer`, `infer_arrays` and
+`infer_deeponet_arrays`.
 Errors raise RuntimeError like the reference binding.  Every call goes through the
 C-ABI of libnfx.so; there is no CPU fallback.
 """
@@ -79,6 +81,63 @@ class InferenceRuntime:
                                                y.ndim)
         if rc != 0:
             raise RuntimeError("RunTokenMixer2D failed: " + self._err())
+
+    def _run_other(self, name: str, label: str, x: np.ndarray, y: np.ndarray) -> None:
+        if not (isinstance(y, np.ndarray) and y.dtype == np.float32 and y.flags.c_contiguous):
+            raise RuntimeError(label + " failed: y must be a C-contiguous float32 array")
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rc = getattr(_lib, "nfx_runtime_run_" + name)(self._h, x.ctypes.data_as(C.c_void_p), _shape(x),
+                                                     x.ndim, y.ctypes.data_as(C.c_void_p), _shape(y),
+                                                     y.ndim)
+        if rc != 0:
+            raise RuntimeError(label + " failed: " + self._err())
+
+    def run_tokenmixer(self, x: np.ndarray, y: np.ndarray) -> None:
+        """RunTokenMixer (runtime.cpp:115-123): x (B, n_points, in_dim) -> y in place."""
+        self._run_other("tokenmixer", "RunTokenMixer", x, y)
+
+    def run_graphop(self, x: np.ndarray, y: np.ndarray) -> None:
+        """RunGraphOp (runtime.cpp:125-133): x (B, n_nodes, in_dim) -> y in place."""
+        self._run_other("graphop", "RunGraphOp", x, y)
+
+    def run_graphop2d(self, x: np.ndarray, y: np.ndarray) -> None:
+        """RunGraphOp2D (runtime.cpp:145-153): x (B, h, w, in_dim) -> y in place."""
+        self._run_other("graphop2d", "RunGraphOp2D", x, y)
+
+    def run_deeponet(self, u: np.ndarray, y: np.ndarray, out: np.ndarray) -> None:
+        """RunDeepONet (runtime.cpp:103-113): u (B, n_sensor, in_branch), y (B, n_query,
+        in_trunk) -> out (B, n_query, out_channels) in place."""
+        if not (isinstance(out, np.ndarray) and out.dtype == np.float32 and out.flags.c_contiguous):
+            raise RuntimeError("RunDeepONet failed: out must be a C-contiguous float32 array")
+        u = np.ascontiguousarray(u, dtype=np.float32)
+        y = np.ascontiguousarray(y, dtype=np.float32)
+        rc = _lib.nfx_runtime_run_deeponet(self._h, u.ctypes.data_as(C.c_void_p), _shape(u), u.ndim,
+                                           y.ctypes.data_as(C.c_void_p), _shape(y), y.ndim,
+                                           out.ctypes.data_as(C.c_void_p), _shape(out), out.ndim)
+        if rc != 0:
+            raise RuntimeError("RunDeepONet failed: " + self._err())
+
+    def run_deeponet_device(self, u, y, out, stream=None) -> None:
+        stream = self._stream(out, stream)
+        sh = lambda t: (C.c_int64 * t.dim())(*t.shape)
+        rc = _lib.nfx_runtime_run_deeponet_device(self._h, C.c_void_p(u.data_ptr()), sh(u), u.dim(),
+                                                  C.c_void_p(y.data_ptr()), sh(y), y.dim(),
+                                                  C.c_void_p(out.data_ptr()), sh(out), out.dim(),
+                                                  C.c_void_p(stream))
+        if rc != 0:
+            raise RuntimeError("RunDeepONet failed: " + self._err())
+
+    def run_other_device(self, name: str, x, y, stream=None) -> None:
+        """Device-buffer RunTokenMixer / RunGraphOp / RunGraphOp2D (`name` "tokenmixer",
+        "graphop" or "graphop2d") on `stream`."""
+        stream = self._stream(x, stream)
+        xs = (C.c_int64 * x.dim())(*x.shape)
+        ys = (C.c_int64 * y.dim())(*y.shape)
+        rc = getattr(_lib, "nfx_runtime_run_" + name + "_device")(
+            self._h, C.c_void_p(x.data_ptr()), xs, x.dim(), C.c_void_p(y.data_ptr()), ys, y.dim(),
+            C.c_void_p(stream))
+        if rc != 0:
+            raise RuntimeError("Run failed: " + self._err())
 
     @staticmethod
     def _stream(x, stream):
@@ -295,7 +354,11 @@ class RuntimeGroup:
             raise RuntimeError("device error: " + self._err())
 
 
-_RANK = {"FNO1d": 3, "FNO2d": 4, "FNO3d": 5, "TokenMixer2D": 4}
+_RANK = {"FNO1d": 3, "FNO2d": 4, "FNO3d": 5, "TokenMixer": 3, "GraphOp": 3, "TokenMixer2D": 4,
+         "GraphOp2D": 4}
+# the Run* call of each op (pybind_module.cpp:95-105)
+_RUN = {"TokenMixer": "run_tokenmixer", "GraphOp": "run_graphop", "TokenMixer2D": "run_tokenmixer2d",
+        "GraphOp2D": "run_graphop2d"}
 
 
 def _run_once(model_path: str, x: np.ndarray, enable_int8: bool, enable_fp8: bool,
@@ -309,11 +372,26 @@ def _run_once(model_path: str, x: np.ndarray, enable_int8: bool, enable_fp8: boo
     if enable_fp8:
         rt.enable_fp8()
     y = np.zeros(tuple(x.shape[:-1]) + (cfg[1],), np.float32)
-    if op == "TokenMixer2D":
-        rt.run_tokenmixer2d(x, y)
-    else:
-        rt.run(x, y)
+    getattr(rt, _RUN.get(op, "run"))(x, y)
     return y
+
+
+def infer_deeponet_arrays(model_path: str, u: np.ndarray, y: np.ndarray, device: int = 0) -> np.ndarray:
+    """The reference's `infer_deeponet_arrays` (pybind_module.cpp:200-233): out (B,
+    n_query, out_channels) with B and n_query from y."""
+    op, cfg, _, _ = _nfx.load_neuroir(model_path)
+    if op != "DeepONet":
+        raise RuntimeError("infer_deeponet_arrays: model op is " + op + ", not DeepONet")
+    u = np.ascontiguousarray(u, dtype=np.float32)
+    y = np.ascontiguousarray(y, dtype=np.float32)
+    if u.ndim != 3:
+        raise RuntimeError("DeepONet u must be 3D (batch, n_sensor, in_branch)")
+    if y.ndim != 3:
+        raise RuntimeError("DeepONet y must be 3D (batch, n_query, in_trunk)")
+    rt = InferenceRuntime(model_path, device)
+    out = np.zeros((y.shape[0], y.shape[1], cfg[3]), np.float32)
+    rt.run_deeponet(u, y, out)
+    return out
 
 
 def infer_arrays(model_path: str, x: np.ndarray, enable_int8: bool = False,

@@ -373,3 +373,103 @@ def fno3d_model(seed: int, in_ch=4, out_ch=1, width=32, modes=(8, 8, 8), L=4, S=
     cfg = dict(in_channels=in_ch, out_channels=out_ch, width=width, modes_h=modes[0],
                modes_w=modes[1], modes_d=modes[2], n_layers=L, pad_factor=1)
     return ir.Model(op="FNO3d", config=cfg, weights=wts, qparams=qp, quant_enabled=True)
+
+
+# ------------------------------------------------------------------------- DeepONet
+def deeponet_model(seed: int, in_branch=1, in_trunk=1, latent=32, out_ch=1, hidden_branch=64,
+                   hidden_trunk=64, n_branch=3, n_trunk=3, activation="gelu") -> ir.Model:
+    """A random-init DeepONet (the reference's default widths): branch and trunk MLPs
+    with Kaiming-uniform Linears (the branch's last layer out_ch * latent wide), output
+    bias U(-0.1, 0.1).  Hidden widths are what the loader infers from the second-to-last
+    layer of each net."""
+    rng = np.random.default_rng(seed)
+    wts = {}
+    for net, n, k0, hid, last in (("branch", n_branch, in_branch, hidden_branch, out_ch * latent),
+                                  ("trunk", n_trunk, in_trunk, hidden_trunk, latent)):
+        k = k0
+        for i in range(n):
+            o = last if i == n - 1 else hid
+            wts[f"{net}.layers.{i}.weight"], wts[f"{net}.layers.{i}.bias"] = _kaiming_linear(rng, o, k)
+            k = o
+    wts["bias.weight"] = rng.uniform(-0.1, 0.1, out_ch).astype(np.float32)
+    cfg = dict(in_branch=in_branch, in_trunk=in_trunk, latent_dim=latent, out_channels=out_ch,
+               n_layers_branch=n_branch, n_layers_trunk=n_trunk)
+    return ir.Model(op="DeepONet", config=cfg, activation=activation, weights=wts)
+
+
+def deeponet_inputs(rng: np.random.Generator, n: int, n_sensor: int, n_query: int, in_branch=1,
+                    in_trunk=1):
+    """u (n, n_sensor, in_branch): GRF values at the sensors (+ further GRF channels);
+    y (n, n_query, in_trunk): query coordinates in [0, 1) (+ uniform extra features)."""
+    u = np.empty((n, n_sensor, in_branch), np.float32)
+    for c in range(in_branch):
+        u[..., c] = grf1d(rng, n, n_sensor)
+    y = rng.uniform(0.0, 1.0, (n, n_query, in_trunk)).astype(np.float32)
+    return u, y
+
+
+# ------------------------------------------------------------------------- GraphOp
+def line_graph(n: int):
+    """CSR of a line graph with self-loops, each node listing itself, then its left and
+    right neighbours (neuroflow/nn/graph_op.py's convention)."""
+    off, idx = [0], []
+    for i in range(n):
+        nb = [i] + ([i - 1] if i > 0 else []) + ([i + 1] if i < n - 1 else [])
+        idx += nb
+        off.append(len(idx))
+    return np.array(off, np.int64), np.array(idx, np.int64)
+
+
+def grid8_graph(h: int, w: int):
+    """CSR of an h x w grid with self-loops and 8-connectivity: itself first, then the
+    in-grid neighbours in (di, dj) row-major order (neuroflow/nn/graph_op2d.py's
+    convention)."""
+    off, idx = [0], []
+    for i in range(h):
+        for j in range(w):
+            nb = [i * w + j]
+            for di in (-1, 0, 1):
+                for dj in (-1, 0, 1):
+                    if (di or dj) and 0 <= i + di < h and 0 <= j + dj < w:
+                        nb.append((i + di) * w + j + dj)
+            idx += nb
+            off.append(len(idx))
+    return np.array(off, np.int64), np.array(idx, np.int64)
+
+
+def graphop_model(seed: int, in_dim=1, out_dim=1, hidden=32, n_layers=1, n_nodes=64, h=None, w=None,
+                  activation="gelu") -> ir.Model:
+    """A random-init GraphOp (n_nodes on a line graph) or, with h and w, GraphOp2D (an
+    8-connected grid); deg_inv = 1 / max(deg, 1) as float32, the adjacency stored as
+    float tensors as the reference's exporter writes it."""
+    rng = np.random.default_rng(seed)
+    two_d = h is not None
+    off, idx = grid8_graph(h, w) if two_d else line_graph(n_nodes)
+    nn_ = (h * w) if two_d else n_nodes
+    deg = np.maximum(np.diff(off).astype(np.float32), 1.0)
+    wts = {}
+    wts["lift.weight"], wts["lift.bias"] = _kaiming_linear(rng, hidden, in_dim)
+    for i in range(n_layers):
+        p = f"blocks.{i}."
+        wts[p + "lin_self.weight"], wts[p + "lin_self.bias"] = _kaiming_linear(rng, hidden, hidden)
+        wts[p + "lin_neigh.weight"], wts[p + "lin_neigh.bias"] = _kaiming_linear(rng, hidden, hidden)
+    wts["head.weight"], wts["head.bias"] = _kaiming_linear(rng, out_dim, hidden)
+    wts["graph.adj_offsets"] = off.astype(np.float32)
+    wts["graph.adj_indices"] = idx.astype(np.float32)
+    wts["graph.deg_inv"] = (np.float32(1.0) / deg).astype(np.float32)
+    if two_d:
+        cfg = dict(in_dim=in_dim, out_dim=out_dim, h=h, w=w, hidden_dim=hidden, n_layers=n_layers)
+        return ir.Model(op="GraphOp2D", config=cfg, activation=activation, weights=wts)
+    cfg = dict(in_dim=in_dim, out_dim=out_dim, n_nodes=n_nodes, hidden_dim=hidden, n_layers=n_layers)
+    return ir.Model(op="GraphOp", config=cfg, activation=activation, weights=wts)
+
+
+def tokenmixer_model(seed: int, in_dim=2, out_dim=1, latent=64, n_points=1024, n_patches=64,
+                     n_heads=4, n_layers=2, activation="gelu") -> ir.Model:
+    """A random-init 1D TokenMixer: the TokenMixer2D weights on n_points points."""
+    m = tm2d_model(seed, in_dim=in_dim, out_dim=out_dim, latent=latent, h=1, w=n_points,
+                   n_patches=n_patches, n_heads=n_heads, n_layers=n_layers, activation=activation)
+    cfg = dict(in_dim=in_dim, out_dim=out_dim, latent_dim=latent, n_points=n_points,
+               n_patches=n_patches, n_heads=n_heads, n_layers=n_layers)
+    return ir.Model(op="TokenMixer", config=cfg, activation=activation, weights=m.weights,
+                    qparams=m.qparams, quant_enabled=m.quant_enabled)

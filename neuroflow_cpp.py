@@ -10,9 +10,10 @@ served by libnfx.so (every call runs on the GPU; there is no CPU path).
     neuroflow_cpp.fp8_e4m3_fake_quant(a, scale)                   # fp8_e4m3_pybind.h:24-66
     neuroflow_cpp.fp8_e4m3_to_bits(a); neuroflow_cpp.fp8_e4m3_from_bits(b)
 
-Runtimes are created on CUDA device 0, or on $NFX_DEVICE.  DeepONet, TokenMixer,
-GraphOp and GraphOp2D models are not executed by the GPU runtime: their calls raise
-RuntimeError as an unsupported op.
+Runtimes are created on CUDA device 0, or on $NFX_DEVICE.  Every op of the reference
+runtime runs on the GPU: FNO1d/2d/3d through `run`, TokenMixer, GraphOp, TokenMixer2D
+and GraphOp2D through their own Run calls (as `infer` dispatches them), DeepONet through
+`infer_deeponet_arrays`.
 """
 from __future__ import annotations
 
@@ -38,7 +39,8 @@ _lib.nfx_fp8_e4m3_fake_quant_host.argtypes = [_C.c_void_p, _C.c_float, _C.c_void
 # input rank and output-channel slot of the IR config per op (pybind_module.cpp:74-89)
 _RANK = {"FNO1d": 3, "FNO2d": 4, "FNO3d": 5, "TokenMixer": 3, "GraphOp": 3,
          "TokenMixer2D": 4, "GraphOp2D": 4}
-_GPU_OPS = ("FNO1d", "FNO2d", "FNO3d", "TokenMixer2D")
+_RUN = {"TokenMixer": "run_tokenmixer", "GraphOp": "run_graphop", "TokenMixer2D": "run_tokenmixer2d",
+        "GraphOp2D": "run_graphop2d"}
 
 
 def _device() -> int:
@@ -56,18 +58,13 @@ def _load(model_path: str):
 def _run_loaded(model_path: str, op: str, cfg, x: _np.ndarray) -> _np.ndarray:
     if op not in _RANK or x.ndim != _RANK[op]:
         raise RuntimeError("input rank mismatch for op " + op)
-    if op not in _GPU_OPS:
-        raise RuntimeError("infer failed: runtime does not support op: " + op)
     try:
         rt = _Runtime(model_path, _device())
     except RuntimeError as e:
         raise RuntimeError("create runtime failed: " + str(e).split(": ", 1)[-1]) from None
     y = _np.zeros(tuple(x.shape[:-1]) + (cfg[1],), _np.float32)
     try:
-        if op == "TokenMixer2D":
-            rt.run_tokenmixer2d(x, y)
-        else:
-            rt.run(x, y)
+        getattr(rt, _RUN.get(op, "run"))(x, y)
     except RuntimeError as e:
         raise RuntimeError("infer failed: " + str(e).split(": ", 1)[-1]) from None
     finally:
@@ -98,11 +95,29 @@ def infer_arrays(model_path: str, x) -> _np.ndarray:
 
 
 def infer_deeponet_arrays(model_path: str, u, y) -> _np.ndarray:
-    """pybind_module.cpp:200-233.  DeepONet is not executed by the GPU runtime."""
-    op, _ = _load(model_path)
+    """DeepONet in memory (pybind_module.cpp:200-233): out (batch, n_query, out_channels)
+    with batch and n_query taken from y."""
+    op, cfg = _load(model_path)
     if op != "DeepONet":
         raise RuntimeError("infer_deeponet_arrays: model op is " + op + ", not DeepONet")
-    raise RuntimeError("infer failed: runtime does not support op: DeepONet")
+    u = _np.ascontiguousarray(u, dtype=_np.float32)
+    y = _np.ascontiguousarray(y, dtype=_np.float32)
+    if u.ndim != 3:
+        raise RuntimeError("DeepONet u must be 3D (batch, n_sensor, in_branch)")
+    if y.ndim != 3:
+        raise RuntimeError("DeepONet y must be 3D (batch, n_query, in_trunk)")
+    try:
+        rt = _Runtime(model_path, _device())
+    except RuntimeError as e:
+        raise RuntimeError("create runtime failed: " + str(e).split(": ", 1)[-1]) from None
+    out = _np.zeros((y.shape[0], y.shape[1], cfg[3]), _np.float32)
+    try:
+        rt.run_deeponet(u, y, out)
+    except RuntimeError as e:
+        raise RuntimeError("infer failed: " + str(e).split(": ", 1)[-1]) from None
+    finally:
+        rt.close()
+    return out
 
 
 class InferenceRuntime:
@@ -130,6 +145,18 @@ class InferenceRuntime:
     # calls of the reference's C++ runtime that its Python class does not expose
     def run_tokenmixer2d(self, x, y) -> None:
         self._rt.run_tokenmixer2d(x, y)
+
+    def run_tokenmixer(self, x, y) -> None:
+        self._rt.run_tokenmixer(x, y)
+
+    def run_graphop(self, x, y) -> None:
+        self._rt.run_graphop(x, y)
+
+    def run_graphop2d(self, x, y) -> None:
+        self._rt.run_graphop2d(x, y)
+
+    def run_deeponet(self, u, y, out) -> None:
+        self._rt.run_deeponet(u, y, out)
 
     def enable_fp8(self) -> None:
         self._rt.enable_fp8()

@@ -96,6 +96,25 @@ class _FNO3d(C.Structure):
                 + [("s_locs", C.c_float * MAX_LAYERS)])
 
 
+MAX_MLP = 8
+
+
+class _DeepONet(C.Structure):
+    _fields_ = ([(n, C.c_int32) for n in ("in_branch", "in_trunk", "latent", "out_ch", "n_branch",
+                                          "n_trunk", "hidden_branch", "hidden_trunk", "relu")]
+                + [("bw", _f32p * MAX_MLP), ("bb", _f32p * MAX_MLP), ("tw", _f32p * MAX_MLP),
+                   ("tb", _f32p * MAX_MLP), ("bias", _f32p)])
+
+
+class _GraphOp(C.Structure):
+    _fields_ = ([(n, C.c_int32) for n in ("in_dim", "out_dim", "n_nodes", "hidden", "n_layers",
+                                          "relu")]
+                + [("lift_w", _f32p), ("lift_b", _f32p), ("self_w", _f32p * MAX_LAYERS),
+                   ("self_b", _f32p * MAX_LAYERS), ("neigh_w", _f32p * MAX_LAYERS),
+                   ("neigh_b", _f32p * MAX_LAYERS), ("head_w", _f32p), ("head_b", _f32p),
+                   ("adj_off", _i32p), ("adj_idx", _i32p), ("deg_inv", _f32p)])
+
+
 class _Taps(C.Structure):
     _fields_ = [("codes_in", _i8p * (MAX_LAYERS + 1)), ("x1_out", _f32p * MAX_LAYERS),
                 ("h_out", _f32p * MAX_LAYERS), ("lift_out", _f32p), ("x2_out", _f32p * MAX_LAYERS),
@@ -294,6 +313,43 @@ class Oracle:
         return y
 
 
+    def tokenmixer_forward(self, model, x, int8: bool = False):
+        """The reference TokenMixer::Forward (fno.cpp:1460-1644): the TokenMixer2D
+        network on a (1, n_points) grid (the same loops, with x (b, n_points, in_dim))."""
+        cfg = model.config
+        m2 = type(model)(op="TokenMixer2D", config=dict(
+            in_dim=cfg["in_dim"], out_dim=cfg["out_dim"], latent_dim=cfg["latent_dim"], h=1,
+            w=cfg["n_points"], n_patches=cfg["n_patches"], n_heads=cfg["n_heads"],
+            n_layers=cfg["n_layers"]), activation=model.activation, weights=model.weights,
+            qparams=model.qparams, quant_enabled=model.quant_enabled)
+        x = _c(x, np.float32)
+        return self.tm2d_forward(m2, x[:, None], int8=int8)[:, 0]
+
+    def deeponet_forward(self, model, u, y):
+        """DeepONet::Forward (fno.cpp:1289-1406): u (b, n_sensor, in_branch), y (b, n_query,
+        in_trunk) -> (b, n_query, out_channels)."""
+        u, y = _c(u, np.float32), _c(y, np.float32)
+        st, keep = build_deeponet_struct(model)
+        out = np.empty((y.shape[0], y.shape[1], model.config["out_channels"]), np.float32)
+        rc = self.lib.nfo_deeponet_forward(C.byref(st), _p(u), u.shape[0], u.shape[1], _p(y),
+                                           y.shape[1], _p(out))
+        if rc != 0:
+            raise RuntimeError(f"nfo_deeponet_forward failed: {rc}")
+        del keep
+        return out
+
+    def graphop_forward(self, model, x):
+        """GraphOp::Forward / GraphOp2D::Forward (fno.cpp:1653-1741, :1969-2060): x (b,
+        n_nodes, in_dim) or (b, h, w, in_dim) -> the same with out_dim."""
+        x = _c(x, np.float32)
+        st, keep = build_graphop_struct(model)
+        y = np.empty(x.shape[:-1] + (model.config["out_dim"],), np.float32)
+        rc = self.lib.nfo_graphop_forward(C.byref(st), _p(x), x.shape[0], _p(y))
+        if rc != 0:
+            raise RuntimeError(f"nfo_graphop_forward failed: {rc}")
+        del keep
+        return y
+
     # -- FP8 E4M3 / FNO3d ------------------------------------------------------------
     def fp32_to_e4m3(self, x):
         x = _c(x, np.float32).ravel()
@@ -346,6 +402,57 @@ def build_fno3d_struct(model):
             getattr(st, fld)[i] = arr(nm)
         st.s_loc_w[i] = fs(f"locs.{i}.weight")
         st.s_locs[i] = fs(f"locs.{i}.output")
+    return st, keep
+
+
+def build_deeponet_struct(model):
+    cfg, w = model.config, model.weights
+    keep = []
+    st = _DeepONet()
+    nb, nt = cfg["n_layers_branch"], cfg["n_layers_trunk"]
+    st.in_branch, st.in_trunk = cfg["in_branch"], cfg["in_trunk"]
+    st.latent, st.out_ch, st.n_branch, st.n_trunk = cfg["latent_dim"], cfg["out_channels"], nb, nt
+    st.hidden_branch = w[f"branch.layers.{nb - 2}.weight"].shape[0] if nb >= 2 else 0
+    st.hidden_trunk = w[f"trunk.layers.{nt - 2}.weight"].shape[0] if nt >= 2 else 0
+    st.relu = 1 if model.activation == "relu" else 0
+
+    def arr(a):
+        a = _c(a, np.float32)
+        keep.append(a)
+        return _p(a)
+
+    for i in range(nb):
+        st.bw[i], st.bb[i] = arr(w[f"branch.layers.{i}.weight"]), arr(w[f"branch.layers.{i}.bias"])
+    for i in range(nt):
+        st.tw[i], st.tb[i] = arr(w[f"trunk.layers.{i}.weight"]), arr(w[f"trunk.layers.{i}.bias"])
+    st.bias = arr(w["bias.weight"])
+    return st, keep
+
+
+def build_graphop_struct(model):
+    cfg, w = model.config, model.weights
+    keep = []
+    st = _GraphOp()
+    st.in_dim, st.out_dim = cfg["in_dim"], cfg["out_dim"]
+    st.n_nodes = cfg["h"] * cfg["w"] if model.op == "GraphOp2D" else cfg["n_nodes"]
+    st.hidden, st.n_layers = cfg["hidden_dim"], cfg["n_layers"]
+    st.relu = 1 if model.activation == "relu" else 0
+
+    def arr(a, dt=np.float32, t=_f32p):
+        a = _c(a, dt)
+        keep.append(a)
+        return _p(a, t)
+
+    st.lift_w, st.lift_b = arr(w["lift.weight"]), arr(w["lift.bias"])
+    for i in range(cfg["n_layers"]):
+        p = f"blocks.{i}."
+        st.self_w[i], st.self_b[i] = arr(w[p + "lin_self.weight"]), arr(w[p + "lin_self.bias"])
+        st.neigh_w[i], st.neigh_b[i] = arr(w[p + "lin_neigh.weight"]), arr(w[p + "lin_neigh.bias"])
+    st.head_w, st.head_b = arr(w["head.weight"]), arr(w["head.bias"])
+    # the loader's float -> int32 conversion of the CSR arrays (ir_loader.h:421-429)
+    st.adj_off = arr(w["graph.adj_offsets"].astype(np.int32), np.int32, _i32p)
+    st.adj_idx = arr(w["graph.adj_indices"].astype(np.int32), np.int32, _i32p)
+    st.deg_inv = arr(w["graph.deg_inv"])
     return st, keep
 
 
@@ -509,6 +616,41 @@ class Reference:
             yv = (C.c_int64 * y.ndim)(*y.shape)
             fn = self.lib.ref_runtime_run_tokenmixer2d if tokenmixer2d else self.lib.ref_runtime_run
             rc = fn(h, _p(x), xs, x.ndim, _p(y), yv, y.ndim)
+            if rc != 0:
+                raise RuntimeError(self.lib.ref_last_error().decode())
+            return y
+        finally:
+            self.lib.ref_runtime_destroy(h)
+
+    def run_deeponet(self, path, u, y, out_ch):
+        """InferenceRuntime::RunDeepONet (runtime.cpp:103-113)."""
+        u, y = _c(u, np.float32), _c(y, np.float32)
+        h = C.c_void_p()
+        if self.lib.ref_runtime_create(path.encode(), C.byref(h)) != 0:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        try:
+            out = np.zeros((y.shape[0], y.shape[1], out_ch), np.float32)
+            shp = lambda a: (C.c_int64 * a.ndim)(*a.shape)
+            rc = self.lib.ref_runtime_run_deeponet(h, _p(u), shp(u), u.ndim, _p(y), shp(y), y.ndim,
+                                                   _p(out), shp(out), out.ndim)
+            if rc != 0:
+                raise RuntimeError(self.lib.ref_last_error().decode())
+            return out
+        finally:
+            self.lib.ref_runtime_destroy(h)
+
+    def run_other(self, path, op, x, out_ch):
+        """RunTokenMixer / RunGraphOp / RunGraphOp2D (runtime.cpp:115-153) by op name."""
+        kind = {"TokenMixer": 0, "GraphOp": 1, "GraphOp2D": 2}[op]
+        x = _c(x, np.float32)
+        h = C.c_void_p()
+        if self.lib.ref_runtime_create(path.encode(), C.byref(h)) != 0:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        try:
+            y = np.zeros(x.shape[:-1] + (out_ch,), np.float32)
+            xs = (C.c_int64 * x.ndim)(*x.shape)
+            ys = (C.c_int64 * y.ndim)(*y.shape)
+            rc = self.lib.ref_runtime_run_other(h, kind, _p(x), xs, x.ndim, _p(y), ys, y.ndim)
             if rc != 0:
                 raise RuntimeError(self.lib.ref_last_error().decode())
             return y

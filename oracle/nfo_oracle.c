@@ -1625,3 +1625,141 @@ int nfo_fno3d_forward(const nfo_fno3d* m, int mode, const float* x, int bsz, int
     free(lift_w);
     return 0;
 }
+
+/* ------------------------------------------------------------------------- */
+/* DeepONet (fno.cpp:1289-1406)                                               */
+/* ------------------------------------------------------------------------- */
+
+#define NFO_MAX_MLP 8
+
+/* Weights as loaded (ir_loader.h:514-547): branch/trunk layers (out, in) + bias, and
+ * the output bias (out_ch).  Hidden widths come from the second-to-last layer. */
+typedef struct {
+    int32_t in_branch, in_trunk, latent, out_ch, n_branch, n_trunk, hidden_branch, hidden_trunk, relu;
+    const float* bw[NFO_MAX_MLP];
+    const float* bb[NFO_MAX_MLP];
+    const float* tw[NFO_MAX_MLP];
+    const float* tb[NFO_MAX_MLP];
+    const float* bias;
+} nfo_deeponet;
+
+/* One MLP as DeepONet::Forward runs it: Linear per layer, activation after every
+ * layer but the last (fno.cpp:1325-1343, :1368-1385). Returns the final rows. */
+static float* deeponet_mlp(const float* x, int64_t rows, int in0, int n, int hidden, int last,
+                           const float* const* W, const float* const* b, int relu) {
+    float* cur = dup_floats(x, rows * in0);
+    int in = in0;
+    for (int i = 0; i < n; ++i) {
+        const int out = (i == n - 1) ? last : hidden;
+        float* next = (float*)calloc((size_t)(rows * out), sizeof(float));
+        nfo_linear(cur, W[i], b[i], (int)rows, in, out, next);
+        if (i < n - 1) nfo_apply_activation(next, rows * out, relu);
+        free(cur);
+        cur = next;
+        in = out;
+    }
+    return cur;
+}
+
+/* u (b, n_sensor, in_branch), y (b, n_query, in_trunk) -> out (b, n_query, out_ch).
+ * The sensor mean is a sequential sum divided by n_sensor (fno.cpp:1352-1361); the
+ * branch/trunk dot product (fno.cpp:1388-1398) is reduced in order and vectorised by
+ * the reference build like Linear: products of the first nfo_linear_unfused_len(latent)
+ * terms rounded then added, the rest fused; then + bias. */
+int nfo_deeponet_forward(const nfo_deeponet* m, const float* u, int bsz, int n_sensor,
+                         const float* y, int n_query, float* out) {
+    if (m->n_branch < 1 || m->n_trunk < 1 || m->n_branch > NFO_MAX_MLP || m->n_trunk > NFO_MAX_MLP)
+        return 3;
+    const int oc = m->out_ch, lat = m->latent;
+    const int64_t rb = (int64_t)bsz * n_sensor, rt = (int64_t)bsz * n_query;
+    float* bf = deeponet_mlp(u, rb, m->in_branch, m->n_branch, m->hidden_branch, oc * lat,
+                             m->bw, m->bb, m->relu);
+    float* bo = (float*)calloc((size_t)bsz * oc * lat, sizeof(float));
+    for (int64_t bi = 0; bi < bsz; ++bi)
+        for (int ci = 0; ci < oc; ++ci)
+            for (int k = 0; k < lat; ++k) {
+                float acc = 0.0f;
+                for (int64_t si = 0; si < n_sensor; ++si)
+                    acc = acc + bf[((bi * n_sensor + si) * oc + ci) * lat + k];
+                bo[(bi * oc + ci) * lat + k] = acc / (float)n_sensor;
+            }
+    float* tf = deeponet_mlp(y, rt, m->in_trunk, m->n_trunk, m->hidden_trunk, lat, m->tw, m->tb,
+                             m->relu);
+    const int vec = nfo_linear_unfused_len(lat);
+    for (int64_t bi = 0; bi < bsz; ++bi)
+        for (int64_t i = 0; i < n_query; ++i)
+            for (int ci = 0; ci < oc; ++ci) {
+                const float* a = bo + (bi * oc + ci) * lat;
+                const float* t = tf + (bi * n_query + i) * lat;
+                float acc = 0.0f;
+                int k = 0;
+                for (; k < vec; ++k) acc = acc + a[k] * t[k];
+                for (; k < lat; ++k) acc = fmaf(a[k], t[k], acc);
+                out[(bi * n_query + i) * oc + ci] = acc + m->bias[ci];
+            }
+    free(tf);
+    free(bo);
+    free(bf);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* GraphOp / GraphOp2D (fno.cpp:1653-1741, :1969-2060)                         */
+/* ------------------------------------------------------------------------- */
+
+/* Both ops run the same network on n_nodes = n_nodes (1D) or h*w (2D) nodes; the
+ * adjacency is CSR (offsets n_nodes + 1, indices), deg_inv per node. */
+typedef struct {
+    int32_t in_dim, out_dim, n_nodes, hidden, n_layers, relu;
+    const float* lift_w;
+    const float* lift_b;
+    const float* self_w[NFO_MAX_LAYERS];
+    const float* self_b[NFO_MAX_LAYERS];
+    const float* neigh_w[NFO_MAX_LAYERS];
+    const float* neigh_b[NFO_MAX_LAYERS];
+    const float* head_w;
+    const float* head_b;
+    const int32_t* adj_off;
+    const int32_t* adj_idx;
+    const float* deg_inv;
+} nfo_graphop;
+
+/* x (b, n_nodes, in_dim) -> y (b, n_nodes, out_dim).  Aggregation: per node and
+ * batch, a sequential sum of the neighbours' rows in CSR order from 0, times deg_inv;
+ * then Linear(h) + Linear(agg), the activation, and h += (fno.cpp:1698-1733). */
+int nfo_graphop_forward(const nfo_graphop* m, const float* x, int bsz, float* y) {
+    if (m->n_layers < 1 || m->n_layers > NFO_MAX_LAYERS) return 3;
+    const int n = m->n_nodes, hd = m->hidden;
+    const int64_t bnh = (int64_t)bsz * n;
+    float* h = (float*)calloc((size_t)(bnh * hd), sizeof(float));
+    float* agg = (float*)calloc((size_t)(bnh * hd), sizeof(float));
+    float* hs = (float*)calloc((size_t)(bnh * hd), sizeof(float));
+    float* hn = (float*)calloc((size_t)(bnh * hd), sizeof(float));
+    nfo_linear(x, m->lift_w, m->lift_b, (int)bnh, m->in_dim, hd, h);
+    for (int li = 0; li < m->n_layers; ++li) {
+        memset(agg, 0, sizeof(float) * (size_t)(bnh * hd));
+        for (int i = 0; i < n; ++i) {
+            const int lo = m->adj_off[i], hi = m->adj_off[i + 1];
+            const float di = m->deg_inv[i];
+            for (int64_t bi = 0; bi < bsz; ++bi) {
+                float* dst = agg + (bi * n + i) * hd;
+                for (int k = lo; k < hi; ++k) {
+                    const float* src = h + (bi * n + m->adj_idx[k]) * hd;
+                    for (int d = 0; d < hd; ++d) dst[d] = dst[d] + src[d];
+                }
+                for (int d = 0; d < hd; ++d) dst[d] = dst[d] * di;
+            }
+        }
+        nfo_linear(h, m->self_w[li], m->self_b[li], (int)bnh, hd, hd, hs);
+        nfo_linear(agg, m->neigh_w[li], m->neigh_b[li], (int)bnh, hd, hd, hn);
+        for (int64_t k = 0; k < bnh * hd; ++k) hs[k] = hs[k] + hn[k];
+        nfo_apply_activation(hs, bnh * hd, m->relu);
+        for (int64_t k = 0; k < bnh * hd; ++k) h[k] = h[k] + hs[k];
+    }
+    nfo_linear(h, m->head_w, m->head_b, (int)bnh, hd, m->out_dim, y);
+    free(hn);
+    free(hs);
+    free(agg);
+    free(h);
+    return 0;
+}

@@ -77,6 +77,27 @@ int ref_runtime_run_tokenmixer2d(void* h, const float* x, const int64_t* xs, int
     return static_cast<int>(s.code());
 }
 
+// runtime.cpp:103-113 InferenceRuntime::RunDeepONet
+int ref_runtime_run_deeponet(void* h, const float* u, const int64_t* us, int ur, const float* y,
+                             const int64_t* ys, int yr, float* out, const int64_t* os, int orank) {
+    auto* rt = static_cast<nflow::InferenceRuntime*>(h);
+    auto s = rt->RunDeepONet(u, ToShape(us, ur), y, ToShape(ys, yr), out, ToShape(os, orank));
+    if (!s.ok()) g_last_error = s.message();
+    return static_cast<int>(s.code());
+}
+
+// runtime.cpp:115-153 RunTokenMixer / RunGraphOp / RunGraphOp2D (kind 0, 1, 2)
+int ref_runtime_run_other(void* h, int kind, const float* x, const int64_t* xs, int xr, float* y,
+                          const int64_t* ys, int yr) {
+    auto* rt = static_cast<nflow::InferenceRuntime*>(h);
+    nflow::Status s = nflow::Status::Ok();
+    if (kind == 0) s = rt->RunTokenMixer(x, ToShape(xs, xr), y, ToShape(ys, yr));
+    else if (kind == 1) s = rt->RunGraphOp(x, ToShape(xs, xr), y, ToShape(ys, yr));
+    else s = rt->RunGraphOp2D(x, ToShape(xs, xr), y, ToShape(ys, yr));
+    if (!s.ok()) g_last_error = s.message();
+    return static_cast<int>(s.code());
+}
+
 // fno.cpp:51-80
 void ref_linear(const float* x, const float* W, const float* b, int bsz, int k, int n,
                 float* y) {

@@ -26,6 +26,13 @@ What it writes (small files, committed):
                         2 blocks) built by the reference's PyTorch model and exported by
                         `export_all`
   tm2d.npz              input x and the reference runtime's RunTokenMixer2D output
+  deeponet.nneuroir     a tiny DeepONet (latent 16, 2 outputs, 3-layer nets of 32 / 24),
+  graphop.nneuroir      GraphOp (40-node line graph, hidden 16, 2 blocks),
+  graphop2d.nneuroir    GraphOp2D (8x8 grid graph, hidden 16, 2 blocks) and
+  tokenmixer.nneuroir   TokenMixer (64 points, 16 patches, latent 16), each built by the
+                        reference's PyTorch model and exported by `export_all`
+  ops.npz               their inputs and the reference runtime's RunDeepONet /
+                        RunGraphOp / RunGraphOp2D / RunTokenMixer outputs
   int8_gemm.npz         LinearForwardBatched vectors (reference C++): W codes, scales,
                         zero points, sum_w, A, C for K = N = 64, plus QuantiseActivation
   fft.npz               Rfft2/Irfft2 of a 16x32 field (reference C++)
@@ -181,6 +188,47 @@ def main():
     xt = rng.standard_normal((2, 8, 8, 3)).astype(np.float32)
     np.savez_compressed(os.path.join(HERE, "tm2d.npz"), x=xt,
                         y=ref.run(path_t, xt, 1, tokenmixer2d=True))
+
+    # --- DeepONet, GraphOp, GraphOp2D, TokenMixer (appended last) -------------------
+    from neuroflow.nn.deeponet import DeepONet, DeepONetConfig
+    from neuroflow.nn.graph_op import GraphOp, GraphOpConfig
+    from neuroflow.nn.graph_op2d import GraphOp2D, GraphOp2DConfig
+    from neuroflow.nn.tokenmixer import TokenMixer, TokenMixerConfig
+
+    def export(model, name):
+        with tempfile.TemporaryDirectory() as d:
+            _, pth = export_all(model, d, basename=name)
+            blob_o = open(pth, "rb").read()
+        path_o = os.path.join(HERE, name + ".nneuroir")
+        open(path_o, "wb").write(blob_o)
+        return path_o
+
+    outs = {}
+    torch.manual_seed(3)
+    dn = DeepONet(DeepONetConfig(in_branch=1, in_trunk=1, latent_dim=16, out_channels=2,
+                                 hidden_branch=32, hidden_trunk=24, n_layers_branch=3,
+                                 n_layers_trunk=3)).eval()
+    path_d = export(dn, "deeponet")
+    outs["don_u"] = rng.standard_normal((2, 20, 1)).astype(np.float32)
+    outs["don_y"] = rng.uniform(0, 1, (2, 30, 1)).astype(np.float32)
+    outs["don_out"] = ref.run_deeponet(path_d, outs["don_u"], outs["don_y"], 2)
+    torch.manual_seed(4)
+    go = GraphOp(GraphOpConfig(in_dim=2, out_dim=1, n_nodes=40, hidden_dim=16, n_layers=2)).eval()
+    path_g = export(go, "graphop")
+    outs["gop_x"] = rng.standard_normal((2, 40, 2)).astype(np.float32)
+    outs["gop_y"] = ref.run_other(path_g, "GraphOp", outs["gop_x"], 1)
+    torch.manual_seed(5)
+    g2 = GraphOp2D(GraphOp2DConfig(in_dim=1, out_dim=2, h=8, w=8, hidden_dim=16, n_layers=2)).eval()
+    path_g2 = export(g2, "graphop2d")
+    outs["g2_x"] = rng.standard_normal((2, 8, 8, 1)).astype(np.float32)
+    outs["g2_y"] = ref.run_other(path_g2, "GraphOp2D", outs["g2_x"], 2)
+    torch.manual_seed(6)
+    tk = TokenMixer(TokenMixerConfig(in_dim=2, out_dim=1, n_points=64, n_patches=16,
+                                     latent_dim=16, n_heads=2, n_layers=1)).eval()
+    path_tk = export(tk, "tokenmixer")
+    outs["tk_x"] = rng.standard_normal((2, 64, 2)).astype(np.float32)
+    outs["tk_y"] = ref.run_other(path_tk, "TokenMixer", outs["tk_x"], 1)
+    np.savez_compressed(os.path.join(HERE, "ops.npz"), **outs)
     print("golden fixtures written to", HERE)
 
 

@@ -131,6 +131,16 @@ def test_golden_ir_through_the_cpp_loader():
     from neuroflow_b200 import _nfx
     op, cfg, nw, q = _nfx.load_neuroir(os.path.join(GOLD, "fno2d_q.nneuroir"))
     assert op == "FNO2d" and cfg[:7] == [3, 1, 16, 4, 4, 2, 1] and nw == 14 and q
+    # the other op families' reference-exported files: op, config block, weight count
+    for name, want_op, want_cfg, want_nw in (
+            ("deeponet", "DeepONet", [1, 1, 16, 2, 3, 3, 0], 13),
+            ("graphop", "GraphOp", [2, 1, 40, 16, 2, 0, 0, 0], 15),
+            ("graphop2d", "GraphOp2D", [1, 2, 8, 8, 16, 2, 0, 0], 15),
+            ("tokenmixer", "TokenMixer", [2, 1, 16, 64, 16, 2, 1, 0], 22)):
+        path = os.path.join(GOLD, name + ".nneuroir")
+        op, cfg, nw, q = _nfx.load_neuroir(path)
+        assert (op, cfg[:len(want_cfg)], nw, q) == (want_op, want_cfg, want_nw, False), name
+        assert ir.write_bytes(ir.read(path)) == open(path, "rb").read()
 
 
 def test_cpp_loader_error_codes(tmp_path):
@@ -314,3 +324,71 @@ def test_int8_mode_close_to_fake_quant_network():
     # layer-0 codes are the lift output's codes
     assert taps["codes_in.0"].min() >= -128 and taps["codes_in.0"].max() <= 127
     assert len(np.unique(taps["codes_in.1"])) > 20
+
+
+# ------------------------------------------ DeepONet, GraphOp, GraphOp2D, TokenMixer
+def test_golden_other_op_families():
+    """DeepONet, GraphOp, GraphOp2D and TokenMixer models built by the reference's
+    PyTorch modules and exported by its exporter; the reference runtime's RunDeepONet /
+    RunGraphOp / RunGraphOp2D / RunTokenMixer outputs, every bit.  The Python reader
+    sees the weight order the reference loader insists on."""
+    d = _g("ops.npz")
+    o = Oracle()
+    m = ir.read(os.path.join(GOLD, "deeponet.nneuroir"))
+    assert m.op == "DeepONet" and list(m.weights) == ir.expected_weight_names(m.op, m.config)
+    assert np.array_equal(_bits(o.deeponet_forward(m, d["don_u"], d["don_y"])), _bits(d["don_out"]))
+    for name, x, y in (("graphop", "gop_x", "gop_y"), ("graphop2d", "g2_x", "g2_y")):
+        m = ir.read(os.path.join(GOLD, name + ".nneuroir"))
+        assert list(m.weights) == ir.expected_weight_names(m.op, m.config)
+        assert np.array_equal(_bits(o.graphop_forward(m, d[x])), _bits(d[y]))
+    m = ir.read(os.path.join(GOLD, "tokenmixer.nneuroir"))
+    assert m.op == "TokenMixer" and list(m.weights) == ir.expected_weight_names(m.op, m.config)
+    assert np.array_equal(_bits(o.tokenmixer_forward(m, d["tk_x"])), _bits(d["tk_y"]))
+
+
+@needs_ref
+@pytest.mark.parametrize("act", ["relu", "gelu"])
+@pytest.mark.parametrize("kw", [
+    dict(),
+    dict(in_branch=3, in_trunk=2, latent=45, out_ch=3, hidden_branch=48, hidden_trunk=72,
+         n_branch=2, n_trunk=4),
+    dict(latent=7, n_branch=1, n_trunk=1, out_ch=2)])
+def test_ref_deeponet_bitexact(tmp_path, act, kw):
+    """Latent widths with an unfused-only (32), mixed (45) and fused-only (7) dot
+    product; one-layer nets (no hidden width)."""
+    m = synth.deeponet_model(1, activation=act, **kw)
+    p = str(tmp_path / "d.nneuroir")
+    ir.write(p, m)
+    u, y = synth.deeponet_inputs(np.random.default_rng(2), 3, 37, 53, m.config["in_branch"],
+                                 m.config["in_trunk"])
+    want = Reference().run_deeponet(p, u, y, m.config["out_channels"])
+    assert np.array_equal(_bits(Oracle().deeponet_forward(m, u, y)), _bits(want))
+
+
+@needs_ref
+@pytest.mark.parametrize("act", ["relu", "gelu"])
+@pytest.mark.parametrize("kw", [
+    dict(), dict(in_dim=3, out_dim=2, hidden=40, n_layers=3, n_nodes=100),
+    dict(h=16, w=16), dict(in_dim=2, out_dim=3, hidden=64, n_layers=2, h=8, w=32)])
+def test_ref_graphop_bitexact(tmp_path, act, kw):
+    m = synth.graphop_model(3, activation=act, **kw)
+    p = str(tmp_path / "g.nneuroir")
+    ir.write(p, m)
+    shape = (2, kw["h"], kw["w"]) if "h" in kw else (2, m.config["n_nodes"])
+    x = np.random.default_rng(4).standard_normal(shape + (m.config["in_dim"],)).astype(np.float32)
+    want = Reference().run_other(p, m.op, x, m.config["out_dim"])
+    assert np.array_equal(_bits(Oracle().graphop_forward(m, x)), _bits(want))
+
+
+@needs_ref
+@pytest.mark.parametrize("act", ["relu", "gelu"])
+def test_ref_tokenmixer_bitexact(tmp_path, act):
+    """The 1D TokenMixer is the TokenMixer2D network on n_points points."""
+    m = synth.tokenmixer_model(7, activation=act, n_points=256, n_patches=32, latent=32,
+                               n_heads=2, n_layers=2)
+    m.quant_enabled = False
+    p = str(tmp_path / "t.nneuroir")
+    ir.write(p, m)
+    x = np.random.default_rng(8).standard_normal((2, 256, 2)).astype(np.float32)
+    want = Reference().run_other(p, "TokenMixer", x, 1)
+    assert np.array_equal(_bits(Oracle().tokenmixer_forward(m, x)), _bits(want))
