@@ -1036,15 +1036,17 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16
 //                block (sum_a) and the 3xTF32 inverse W-transform x1 = Binv T
 //   warps 2-7    T builders: the H-direction inverse
 //                transform T[o][kw] of the tile's rows from the cached spectrum Y,
-//                split into tf32 hi/lo halves, four T buffers
+//                four rows per pass (tile_row's groups), split into tf32 hi/lo
+//                halves, four T buffers
 //   warps 8-23   epilogue: two groups of 8 warps take turns over the tiles; in a
 //                group, 2 warps per TMEM lane quadrant, 32 columns each.  Per
 //                element: dequantise + bias (constant-bank operands), the fast
 //                fake-quant offset k, z = x1 + k s, the next code from the table;
 //                16 packed codes per thread and chunk go out as one 16-byte store.
-// Three accumulator stages: the MMA runs up to two tiles ahead of the epilogue
-// groups, and a group finishing tile t - 2 implies (in-order MMA completion) that the
-// stage of tile t has completed the phase of tile t - 3, so parity waits stay exact.
+// Four accumulator stages (all 512 TMEM columns): each epilogue group alternates
+// between two stages, so the MMA of tile t + 4 has a whole group tile period to land
+// after its group released tile t; a group waits on a stage only after it drained the
+// stage's previous tile itself, so parity waits stay exact.
 // ---------------------------------------------------------------------------
 template <int C, int MH, int MW>
 struct TCfg {
@@ -1057,7 +1059,7 @@ struct TCfg {
     static constexpr int kStages = 3;
     static constexpr int kX1Col = C;
     static constexpr int kAccCols = kX1Col + C;
-    static constexpr int kAccStages = 3;
+    static constexpr int kAccStages = 4;
     static constexpr int kTmemCols = pow2ceil(kAccStages * kAccCols);
     // x1 MMA operands: K = 2 MW = 24 (kw, re/im) in three K-blocks of 8 fp32, each a
     // 32-byte-row SW32 tile (Binv: 128 points x 8, T: C outputs x 8)
@@ -1137,12 +1139,18 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn,
     const int num_tiles = static_cast<int>((p.M + 127) / 128);
     const int t_begin = static_cast<int>(static_cast<int64_t>(num_tiles) * blockIdx.x / gridDim.x);
     const int t_end = static_cast<int>(static_cast<int64_t>(num_tiles) * (blockIdx.x + 1) / gridDim.x);
-    // Logical tile L (the CTA loop order) -> grid row: within a sample, L = 2q and
-    // 2q + 1 are the rows q and q + H/2 (one 128-point tile is one row, W == 128).
+    // Logical tile L (the CTA loop order) -> grid row (one 128-point tile is one row,
+    // W == 128).  Within a sample the logical tiles come in groups of four, group g >= 1
+    // being the rows g, g + H/2, H - g and H/2 - g (whose H-direction twiddles are those
+    // of row g times (-1)^kh and/or conjugated), group 0 the rows 0, H/2, H/4, 3H/4.
     auto tile_row = [&](int Lt) -> int {
         const int b = Lt / p.H;
         const int r = Lt - b * p.H;
-        return b * p.H + (r >> 1) + (r & 1) * (p.H >> 1);
+        const int g = r >> 2, k = r & 3;
+        const int h2 = p.H >> 1;
+        const int row = g == 0 ? (k & 1) * h2 + (k >> 1) * (p.H >> 2)
+                               : (k < 2 ? g : (k == 2 ? p.H - g : h2 - g)) + (k == 1 ? h2 : 0);
+        return b * p.H + row;
     };
 
     // ---- set-up
@@ -1283,34 +1291,28 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn,
         __syncwarp();
     } else if (warp >= L::kTBuild0 && warp < L::kEpi0) {
         // ---------------- T builders
-        // Consecutive logical tiles 2q, 2q+1 of a sample are the rows h and h + H/2
-        // (tile_row), whose twiddles differ only by (-1)^kh: with E and O the sums over
-        // even and odd kh, T(h) = E + O and T(h + H/2) = E - O, so one pass over the
-        // cached spectrum builds both T operands.
+        // One pass over the cached spectrum per group of four logical tiles (tile_row):
+        // with e = e(g, kh) the twiddle of row g, the rows g + H/2, H - g and H/2 - g have
+        // twiddles (-1)^kh e, conj(e) and (-1)^kh conj(e).  Per parity class of kh (E, O)
+        // the four sums Rc = sum Yr c, Is = sum Yi s, Rs = sum Yr s, Ic = sum Yi c give
+        //   T(g)       = (Rc - Is) + i (Rs + Ic)   summed E + O,
+        //   T(g + H/2) = the same, E - O,
+        //   T(H - g)   = (Rc + Is) + i (Ic - Rs)   summed E + O,
+        //   T(H/2 - g) = the same, E - O.
+        // Group 0 takes two passes: g = 0 for rows 0, H/2 and g = H/4 for H/4, 3H/4.
         const int ctid = (warp - L::kTBuild0) * 32 + lane;
         constexpr int kBT = L::kTBuildWarps * 32;
         constexpr int kPer = MW * C / kBT;                   // (kw, o) pairs per thread
         static_assert(MW * C % kBT == 0, "T builder layout");
+        static_assert(MH % 2 == 0, "parity classes");
         const int o = ctid % C;
         int cached_b = -1;
-        int it = 0;
-        for (int tile = t_begin; tile < t_end && it >= 0;) {
-            // a pair when this logical tile is the even one and its partner is ours too
-            const int two = ((tile & 1) == 0 && tile + 1 < t_end) ? 2 : 1;
-            bool ok = true;
-            for (int q = 0; q < two; ++q) {
-                const int bq = (it + q) % L::kTBufs;
-                if (!mbar_wait_backoff(&tFree[bq], (((it + q) / L::kTBufs) & 1) ^ 1, sAbort, 256)) {
-                    *sAbort = 1;
-                    atomicOr(p.err, kErrWaitDrain);
-                    ok = false;
-                    break;
-                }
-            }
-            if (!ok) break;
-            const int pt = tile_row(tile);                   // physical row of this tile
-            const int smp = pt / p.H;
-            const int h = pt - smp * p.H;
+        bool ok = true;
+        for (int L0 = t_begin & ~3; L0 < t_end && ok; L0 += 4) {
+            const int first = L0 > t_begin ? L0 : t_begin;
+            const int last = L0 + 4 < t_end ? L0 + 4 : t_end;
+            const int smp = L0 / p.H;
+            const int g = (L0 - smp * p.H) >> 2;
             if (smp != cached_b) {
                 // each builder caches exactly the spectrum entries it reads below, so the
                 // reload needs no barrier among the builders
@@ -1324,46 +1326,65 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn,
                 }
                 cached_b = smp;
             }
-            float2 eh[MH];
+            for (int pass = 0; pass < (g == 0 ? 2 : 1) && ok; ++pass) {
+                const int h = g == 0 ? pass * (p.H >> 2) : g;
+                const int m0 = g == 0 ? 2 * pass : 0, m1 = g == 0 ? m0 + 2 : 4;  // members
+                if (L0 + m1 <= first || L0 + m0 >= last) continue;
+                float acc[kPer][8];  // per pair: E {Rc, Is, Rs, Ic}, O {Rc, Is, Rs, Ic}
 #pragma unroll
-            for (int kh = 0; kh < MH; ++kh) eh[kh] = __ldg(p.twi_h + h * MH + kh);
-            uint8_t* thi0 = sTop + (it % L::kTBufs) * L::kTBuf;
-            uint8_t* thi1 = sTop + ((it + 1) % L::kTBufs) * L::kTBuf;
+                for (int r = 0; r < kPer; ++r)
 #pragma unroll
-            for (int r = 0; r < kPer; ++r) {
-                const int kw = (ctid + kBT * r) / C;
-                float er = 0.f, ei = 0.f, orr = 0.f, oi = 0.f;
+                    for (int q = 0; q < 8; ++q) acc[r][q] = 0.0f;
 #pragma unroll
-                for (int kh = 0; kh < MH; kh += 2) {
-                    const float2 y = sY[(kh * MW + kw) * C + o];
-                    er = fmaf(y.x, eh[kh].x, fmaf(-y.y, eh[kh].y, er));
-                    ei = fmaf(y.x, eh[kh].y, fmaf(y.y, eh[kh].x, ei));
+                for (int kh = 0; kh < MH; ++kh) {
+                    const float2 e = __ldg(p.twi_h + h * MH + kh);
+#pragma unroll
+                    for (int r = 0; r < kPer; ++r) {
+                        const int kw = (ctid + kBT * r) / C;
+                        const float2 y = sY[(kh * MW + kw) * C + o];
+                        float* a = acc[r] + (kh & 1) * 4;
+                        a[0] = fmaf(y.x, e.x, a[0]);
+                        a[1] = fmaf(y.y, e.y, a[1]);
+                        a[2] = fmaf(y.x, e.y, a[2]);
+                        a[3] = fmaf(y.y, e.x, a[3]);
+                    }
                 }
+                for (int k = m0; k < m1; ++k) {
+                    const int Lk = L0 + k;
+                    if (Lk < first || Lk >= last) continue;
+                    const int itk = Lk - t_begin;
+                    const int bq = itk % L::kTBufs;
+                    if (!mbar_wait_backoff(&tFree[bq], ((itk / L::kTBufs) & 1) ^ 1, sAbort, 256)) {
+                        *sAbort = 1;
+                        atomicOr(p.err, kErrWaitDrain);
+                        ok = false;
+                        break;
+                    }
+                    const bool conj = g != 0 && k >= 2;     // rows H - g, H/2 - g
+                    const bool minus = (k & 1) != 0;        // E - O
+                    uint8_t* tb = sTop + bq * L::kTBuf;
 #pragma unroll
-                for (int kh = 1; kh < MH; kh += 2) {
-                    const float2 y = sY[(kh * MW + kw) * C + o];
-                    orr = fmaf(y.x, eh[kh].x, fmaf(-y.y, eh[kh].y, orr));
-                    oi = fmaf(y.x, eh[kh].y, fmaf(y.y, eh[kh].x, oi));
-                }
-                // element (o, j = 2 kw + re/im): K-block j / 8, column j % 8
-                const uint32_t off = (kw >> 2) * L::kTBlk + swz_offset(o * 32 + (2 * kw & 7) * 4, 32);
-                constexpr int kLo = L::kKb * L::kTBlk;
-                float h0, l0, h1, l1;
-                split_tf32(__fadd_rn(er, orr), h0, l0);
-                split_tf32(__fadd_rn(ei, oi), h1, l1);
-                *reinterpret_cast<float2*>(thi0 + off) = make_float2(h0, h1);
-                *reinterpret_cast<float2*>(thi0 + kLo + off) = make_float2(l0, l1);
-                if (two == 2) {
-                    split_tf32(__fsub_rn(er, orr), h0, l0);
-                    split_tf32(__fsub_rn(ei, oi), h1, l1);
-                    *reinterpret_cast<float2*>(thi1 + off) = make_float2(h0, h1);
-                    *reinterpret_cast<float2*>(thi1 + kLo + off) = make_float2(l0, l1);
+                    for (int r = 0; r < kPer; ++r) {
+                        const int kw = (ctid + kBT * r) / C;
+                        const float* E = acc[r];
+                        const float* O = acc[r] + 4;
+                        const float er = conj ? E[0] + E[1] : E[0] - E[1];
+                        const float ei = conj ? E[3] - E[2] : E[2] + E[3];
+                        const float orr = conj ? O[0] + O[1] : O[0] - O[1];
+                        const float oi = conj ? O[3] - O[2] : O[2] + O[3];
+                        // element (o, j = 2 kw + re/im): K-block j / 8, column j % 8
+                        const uint32_t off = (kw >> 2) * L::kTBlk + swz_offset(o * 32 + (2 * kw & 7) * 4, 32);
+                        constexpr int kLo = L::kKb * L::kTBlk;
+                        float h0, l0, h1, l1;
+                        split_tf32(minus ? __fsub_rn(er, orr) : __fadd_rn(er, orr), h0, l0);
+                        split_tf32(minus ? __fsub_rn(ei, oi) : __fadd_rn(ei, oi), h1, l1);
+                        *reinterpret_cast<float2*>(tb + off) = make_float2(h0, h1);
+                        *reinterpret_cast<float2*>(tb + kLo + off) = make_float2(l0, l1);
+                    }
+                    fence_proxy_async_smem();
+                    mbar_arrive(&tReady[bq]);
                 }
             }
-            fence_proxy_async_smem();
-            for (int q = 0; q < two; ++q) mbar_arrive(&tReady[(it + q) % L::kTBufs]);
-            tile += two;
-            it += two;
         }
     } else if (warp >= L::kEpi0 && warp < L::kEpi0 + L::kEpiWarps) {
         // ---------------- epilogue

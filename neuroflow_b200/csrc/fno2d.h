@@ -74,10 +74,14 @@ struct SpecFwdArgs {
 // i.e. sum_k a_k (w_k - 2 zp_w) + nk' with nk' = zp_in (K zp_w - sum_w); the MMA
 // produces the first term (the Z blocks of LayerArgs), so
 //   v = a[o] * float(raw' + nk'[o]) + b[o],  a = scale_w * s_in,
-// stored as float4 {a, bits(zp_w), bits(nk'), b}.
+// stored as float4 {a, bits(zp_w), bits(nk'), b}, and again per field (a, nk', b),
+// so that one 16-byte constant load brings one field of four columns.
 constexpr int kFno2dColMax = 64;
 struct LayerCols {
     float4 v[kFno2dColMax];
+    float a[kFno2dColMax];
+    int nk[kFno2dColMax];
+    float b[kFno2dColMax];
 };
 // The projection's constants: proj_q's epilogue columns as above, and proj_out's
 // weights and biases (out_ch <= 4), read as constant-bank operands.

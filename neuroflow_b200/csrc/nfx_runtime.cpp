@@ -618,6 +618,9 @@ bool fno2d_i8_fast(nfx_runtime* rt) {
                 std::memcpy(&zpf, &zp, 4);
                 std::memcpy(&nkf, &nk, 4);
                 cols.v[o] = make_float4(pc->second.scales[o] * in.scale, zpf, nkf, bias[o]);
+                cols.a[o] = cols.v[o].x;
+                cols.nk[o] = nk;
+                cols.b[o] = bias[o];
             }
         } else {
             nfx::ProjCols& cols = pl.proj_cols;
