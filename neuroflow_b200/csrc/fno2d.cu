@@ -1040,9 +1040,11 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16
 //                halves, four T buffers
 //   warps 8-23   epilogue: two groups of 8 warps take turns over the tiles; in a
 //                group, 2 warps per TMEM lane quadrant, 32 columns each.  Per
-//                element: dequantise + bias (constant-bank operands), the fast
-//                fake-quant offset k, z = x1 + k s, the next code from the table;
-//                16 packed codes per thread and chunk go out as one 16-byte store.
+//                element: dequantise + bias (one 16-byte constant load per field
+//                and four columns), the fast fake-quant offset k, z = x1 + k s, the
+//                next code from the table, the products two columns per f32x2
+//                instruction; 16 packed codes per thread and chunk go out as one
+//                16-byte store.
 // Four accumulator stages (all 512 TMEM columns): each epilogue group alternates
 // between two stages, so the MMA of tile t + 4 has a whole group tile period to land
 // after its group released tile t; a group waits on a stage only after it drained the
@@ -1338,15 +1340,18 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn,
 #pragma unroll
                 for (int kh = 0; kh < MH; ++kh) {
                     const float2 e = __ldg(p.twi_h + h * MH + kh);
+                    const float2 es = make_float2(e.y, e.x);
 #pragma unroll
                     for (int r = 0; r < kPer; ++r) {
                         const int kw = (ctid + kBT * r) / C;
                         const float2 y = sY[(kh * MW + kw) * C + o];
                         float* a = acc[r] + (kh & 1) * 4;
-                        a[0] = fmaf(y.x, e.x, a[0]);
-                        a[1] = fmaf(y.y, e.y, a[1]);
-                        a[2] = fmaf(y.x, e.y, a[2]);
-                        a[3] = fmaf(y.y, e.x, a[3]);
+                        const float2 a01 = fma2_rn(y, e, make_float2(a[0], a[1]));
+                        const float2 a23 = fma2_rn(y, es, make_float2(a[2], a[3]));
+                        a[0] = a01.x;
+                        a[1] = a01.y;
+                        a[2] = a23.x;
+                        a[3] = a23.y;
                     }
                 }
                 for (int k = m0; k < m1; ++k) {
@@ -1424,30 +1429,48 @@ layer_tc_kernel(const __grid_constant__ CUtensorMap tmIn,
             float dmax[4];
             float zz[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const float4 cp = cols.v[c0 + j];  // constant cache, uniform
-                const int vint = static_cast<int>(raw[j]) + __float_as_int(cp.z);
-                const float v = __fadd_rn(__fmul_rn(cp.x, __int2float_rn(vint)), cp.w);
-                const float r = __fmul_rn(v, inv_out);
-                const float k = rintf(r);
-                const float d = fabsf(__fsub_rn(r, k));
-                dmax[j >> 2] = (j & 3) == 0 ? d : fmaxf(dmax[j >> 2], d);
-                const float kq = fminf(fmaxf(k, klo), khi);
-                zz[j] = __fadd_rn(__uint_as_float(x1r[j]), __fmul_rn(kq, s_out));
+            for (int j = 0; j < 16; j += 2) {
+                // the products of two columns per f32x2 instruction; every sum stays a
+                // scalar add (a packed add of a packed product would be fused)
+                const float4 A4 = reinterpret_cast<const float4*>(cols.a)[(c0 >> 2) + (j >> 2)];
+                const int4 N4 = reinterpret_cast<const int4*>(cols.nk)[(c0 >> 2) + (j >> 2)];
+                const float4 B4 = reinterpret_cast<const float4*>(cols.b)[(c0 >> 2) + (j >> 2)];
+                const bool lo = (j & 2) == 0;
+                const float2 ca = lo ? make_float2(A4.x, A4.y) : make_float2(A4.z, A4.w);
+                const float2 cb = lo ? make_float2(B4.x, B4.y) : make_float2(B4.z, B4.w);
+                const int n0 = lo ? N4.x : N4.z, n1 = lo ? N4.y : N4.w;
+                const float2 f = make_float2(__int2float_rn(static_cast<int>(raw[j]) + n0),
+                                             __int2float_rn(static_cast<int>(raw[j + 1]) + n1));
+                const float2 m = mul2_rn(ca, f);
+                const float2 v = make_float2(__fadd_rn(m.x, cb.x), __fadd_rn(m.y, cb.y));
+                const float2 r = mul2_rn(v, make_float2(inv_out, inv_out));
+                const float k0 = rintf(r.x), k1 = rintf(r.y);
+                const float dm = fmaxf(fabsf(__fsub_rn(r.x, k0)), fabsf(__fsub_rn(r.y, k1)));
+                dmax[j >> 2] = lo ? dm : fmaxf(dmax[j >> 2], dm);
+                const float2 x2 = mul2_rn(make_float2(fminf(fmaxf(k0, klo), khi), fminf(fmaxf(k1, klo), khi)),
+                                          make_float2(s_out, s_out));
+                zz[j] = __fadd_rn(__uint_as_float(x1r[j]), x2.x);
+                zz[j + 1] = __fadd_rn(__uint_as_float(x1r[j + 1]), x2.y);
             }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 int2 cell[8];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float z = zz[8 * h + q];
+                for (int q = 0; q < 8; q += 2) {
+                    const float z0 = zz[8 * h + q], z1 = zz[8 * h + q + 1];
+                    float u0, u1;
                     if constexpr (TWO) {
-                        const bool s0 = z < p.lut_split;
-                        cell[q] = lut_cell_sat(z, sLut, s0 ? p.lut_alpha0 : p.lut_alpha1,
-                                               s0 ? p.lut_beta0 : p.lut_beta1, p.lut_nm1);
+                        const bool s0 = z0 < p.lut_split, s1 = z1 < p.lut_split;
+                        u0 = __saturatef(__fmaf_rn(z0, s0 ? p.lut_alpha0 : p.lut_alpha1, s0 ? p.lut_beta0 : p.lut_beta1));
+                        u1 = __saturatef(__fmaf_rn(z1, s1 ? p.lut_alpha0 : p.lut_alpha1, s1 ? p.lut_beta0 : p.lut_beta1));
                     } else {
-                        cell[q] = lut_cell_sat(z, sLut, p.lut_alpha1, p.lut_beta1, p.lut_nm1);
+                        u0 = __saturatef(__fmaf_rn(z0, p.lut_alpha1, p.lut_beta1));
+                        u1 = __saturatef(__fmaf_rn(z1, p.lut_alpha1, p.lut_beta1));
                     }
+                    const float2 x = fma2_rn(make_float2(u0, u1), make_float2(p.lut_nm1, p.lut_nm1),
+                                             make_float2(kMagic, kMagic));
+                    cell[q] = sLut[__float_as_int(x.x) - 0x4B400000];
+                    cell[q + 1] = sLut[__float_as_int(x.y) - 0x4B400000];
                 }
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {

@@ -70,6 +70,27 @@ __device__ __forceinline__ float fq_offset_try(float v, float inv_s, float klo, 
     return fminf(fmaxf(k, klo), khi);
 }
 
+// Two independent fp32 operations in one instruction (the sm_100 f32x2 forms): IEEE
+// round-to-nearest per lane, so each lane equals the scalar __fmul_rn / __fmaf_rn
+// result bit for bit.  A product from mul2_rn must not feed a packed add or subtract:
+// ptxas contracts mul.rn.f32x2 followed by add.rn.f32x2 into one fused f32x2 FMA
+// despite the explicit rounding (found by comparing against the scalar forms); sums of
+// packed products are therefore written as scalar __fadd_rn / __fsub_rn.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+    float2 r;
+    asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+        "mul.rn.f32x2 z, x, y;\n\tmov.b64 {%0, %1}, z;\n\t}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+    float2 r;
+    asm("{\n\t.reg .b64 x, y, w, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+        "mov.b64 w, {%6, %7};\n\tfma.rn.f32x2 z, x, y, w;\n\tmov.b64 {%0, %1}, z;\n\t}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return r;
+}
+
 // fake-quant round trip: (q - zp) * s.
 __device__ __forceinline__ float fake_quant(float v, float s, float zp) {
     return __fmul_rn(__fsub_rn(fq_code(v, s, zp), zp), s);
