@@ -51,4 +51,41 @@ __device__ __forceinline__ void warp_fft_row(float2* a, int n, const float2* __r
     }
 }
 
+// The same transform when only the first `need` outputs are read.  A later stage reads,
+// of each group of 2*half entries, only the first min(2*half, need) (by induction from
+// the last stage), so a butterfly output is computed only when its position in its
+// group is below that bound; every output computed is the one warp_fft_row computes.
+template <bool INV>
+__device__ __forceinline__ void warp_fft_row_first(float2* a, int n, const float2* __restrict__ tw,
+                                                   int lane, int need) {
+    for (int half = 1; half < n; half <<= 1) {
+        const float2* t = tw + (half - 1);
+        const int nd = need < 2 * half ? need : 2 * half;
+        const int kk = nd < half ? nd : half;        // butterflies per group
+        // lanes over (group, k) with k padded to a power of two (at most half)
+        const int lg = kk <= 1 ? 0 : 32 - __clz(kk - 1);
+        const int groups = n / (2 * half);
+        for (int idx = lane; idx < (groups << lg); idx += 32) {
+            const int k = idx & ((1 << lg) - 1);
+            if (k >= kk) continue;
+            const int i0 = ((idx >> lg) * 2 * half) + k;
+            const int i1 = i0 + half;
+            const float2 w = __ldg(t + k);
+            const float2 u = a[i0];
+            const float2 x = a[i1];
+            float2 v;
+            if (INV) {
+                v.x = __fmaf_rn(x.x, w.x, -__fmul_rn(x.y, w.y));
+                v.y = __fmaf_rn(x.x, w.y, __fmul_rn(x.y, w.x));
+            } else {
+                v.x = __fsub_rn(__fmul_rn(x.x, w.x), __fmul_rn(x.y, w.y));
+                v.y = __fadd_rn(__fmul_rn(x.y, w.x), __fmul_rn(x.x, w.y));
+            }
+            a[i0] = make_float2(__fadd_rn(u.x, v.x), __fadd_rn(u.y, v.y));
+            if (k + half < nd) a[i1] = make_float2(__fsub_rn(u.x, v.x), __fsub_rn(u.y, v.y));
+        }
+        __syncwarp();
+    }
+}
+
 }  // namespace nfx

@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(256) fft1d_fwd_kernel(const void* __restrict__
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float2* row = sa + warp * N;
-    warp_fft_row<false>(row, N, tw, lane);
+    warp_fft_row_first<false>(row, N, tw, lane, modes);
     for (int m = lane; m < modes; m += 32)
         Xs[(static_cast<int64_t>(b) * C + c0 + warp) * modes + m] = row[m];
 }
@@ -244,6 +244,100 @@ __global__ void __launch_bounds__(256) layer1d_kernel(Layer1dArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// projection for widths up to 128, over tiles of kProjTP points (the same arithmetic as
+// proj1d_kernel below, element for element):
+//   phase 1  the tile's activation rows -> sH [TP][C], proj_q transposed -> sWt [C][C]
+//   phase 2  q[p][c]: thread (c, point group) runs the proj_q dot products of eight
+//            points at a time (independent chains; the point's features are warp-
+//            uniform broadcasts, the weight column one conflict-free load per k for
+//            all eight), then the activation -> sQ [TP][C + 1]
+//   phase 3  one thread per point: the proj_out sums over c in order
+// ---------------------------------------------------------------------------
+constexpr int kProjTP = 64;
+constexpr int kProjThreads = 128;
+constexpr int kProjILP = 8;   // points per thread and pass (independent dot products)
+
+size_t proj1d_tiled_smem(int C) {
+    return (static_cast<size_t>(kProjTP) * C + static_cast<size_t>(C) * C +
+            static_cast<size_t>(kProjTP) * (C + 1)) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(kProjThreads) proj1d_tiled_kernel(
+    const float* __restrict__ h, int n, int N, int C, int out_ch, int64_t total,
+    const float* __restrict__ pq_w, const float* __restrict__ pq_b, const float* __restrict__ po_w,
+    const float* __restrict__ po_b, int act, float* __restrict__ y) {
+    extern __shared__ float sh[];
+    float* sH = sh;                                   // [TP][C]
+    float* sWt = sH + static_cast<size_t>(kProjTP) * C;  // [C][C]: sWt[k * C + c] = pq_w[c][k]
+    float* sQ = sWt + static_cast<size_t>(C) * C;     // [TP][C + 1]
+    const int tid = threadIdx.x;
+    for (int t = tid; t < C * C; t += kProjThreads) {
+        const int c = t / C, k = t - (t / C) * C;
+        sWt[k * C + c] = __ldg(pq_w + t);
+    }
+    const int nu = linear_unfused_len(C);
+    const int G = C <= kProjThreads ? kProjThreads / C : 1;  // point groups
+    for (int64_t t0 = static_cast<int64_t>(blockIdx.x) * kProjTP; t0 < total;
+         t0 += static_cast<int64_t>(gridDim.x) * kProjTP) {
+        const int np = static_cast<int>(total - t0 < kProjTP ? total - t0 : kProjTP);
+        __syncthreads();  // the previous tile's sH / sQ are no longer read
+        for (int e = tid; e < np * C; e += kProjThreads) {
+            const int r = e / C, k = e - (e / C) * C;
+            const int64_t t = t0 + r;
+            const int64_t b = t / n;
+            const int pp = static_cast<int>(t - b * n);
+            sH[r * C + k] = h[(b * N + pp) * C + k];
+        }
+        __syncthreads();
+        for (int item = tid; item < C * G; item += kProjThreads) {
+            const int c = item % C, g = item / C;
+            const float bias = __ldg(pq_b + c);
+            for (int r0 = g * kProjILP; r0 < np; r0 += kProjILP * G) {
+                float q[kProjILP];
+                const float* hr[kProjILP];
+#pragma unroll
+                for (int u = 0; u < kProjILP; ++u) {
+                    q[u] = bias;
+                    hr[u] = sH + (r0 + u < np ? r0 + u : r0) * C;
+                }
+                int k = 0;
+                for (; k < nu; ++k) {
+                    const float wv = sWt[k * C + c];
+#pragma unroll
+                    for (int u = 0; u < kProjILP; ++u) q[u] = __fadd_rn(q[u], __fmul_rn(hr[u][k], wv));
+                }
+                for (; k < C; ++k) {
+                    const float wv = sWt[k * C + c];
+#pragma unroll
+                    for (int u = 0; u < kProjILP; ++u) q[u] = __fmaf_rn(hr[u][k], wv, q[u]);
+                }
+#pragma unroll
+                for (int u = 0; u < kProjILP; ++u)
+                    if (r0 + u < np) sQ[(r0 + u) * (C + 1) + c] = act_f(q[u], act);
+            }
+        }
+        __syncthreads();
+        if (tid < np) {
+            const float* qr = sQ + tid * (C + 1);
+            float acc[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] = j < out_ch ? __ldg(po_b + j) : 0.0f;
+            for (int c = 0; c < C; ++c) {
+                const float qv = qr[c];
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (j < out_ch)
+                        acc[j] = linear_step(acc[j], qv, __ldg(po_w + static_cast<int64_t>(j) * C + c), c >= nu);
+            }
+            float* yr = y + (t0 + tid) * out_ch;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (j < out_ch) yr[j] = acc[j];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // projection (fno.cpp:683-702): q = Linear(h, proj_q) -> act -> y = Linear(q, proj_out),
 // both the reference's sequential dot product from the bias (linear_step), the proj_out
 // sum interleaved with the production of q[c] in increasing c (the same operation
@@ -373,7 +467,21 @@ cudaError_t fno1d_run(const Fno1dPlan& pl, cudaStream_t st) {
         if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
-    {
+    if (C <= 128) {
+        const int64_t total = static_cast<int64_t>(pl.B) * pl.n;
+        const size_t smem = proj1d_tiled_smem(C);
+        if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(proj1d_tiled_kernel),
+                                      static_cast<int>(smem))) != cudaSuccess)
+            return e;
+        const int per_sm = smem <= 56 * 1024 ? 4 : (smem <= 112 * 1024 ? 2 : 1);
+        const int grid = static_cast<int>(std::min<int64_t>((total + kProjTP - 1) / kProjTP, sms * per_sm * 2));
+        if (pl.timer) pl.timer->begin("fno1d_proj", st);
+        proj1d_tiled_kernel<<<grid, kProjThreads, smem, st>>>(static_cast<const float*>(pl.h[pl.L & 1]), pl.n, N,
+                                                              C, pl.out_ch, total, pl.pq_w, pl.pq_b, pl.po_w,
+                                                              pl.po_b, pl.act, pl.y);
+        if (pl.timer) pl.timer->end(st);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    } else {
         const int64_t total = static_cast<int64_t>(pl.B) * pl.n;
         const int threads = C > 128 ? 64 : 128;
         const size_t smem = static_cast<size_t>(threads) * (C + 1) * sizeof(float);

@@ -128,14 +128,14 @@ __global__ void __launch_bounds__(256) fwd2d_kernel(const float* __restrict__ hi
     for (int r = warp; r < Hp; r += 8) {
         for (int j = lane; j < Wp; j += 32) row[bit_reverse(j, lgW)] = make_float2(plane[static_cast<int64_t>(r) * Wp + j], 0.0f);
         __syncwarp();
-        warp_fft_row<false>(row, Wp, twf_w, lane);
+        warp_fft_row_first<false>(row, Wp, twf_w, lane, MW);
         const int rr = bit_reverse(r, lgH);
         for (int kw = lane; kw < MW; kw += 32) col[kw * Hp + rr] = row[kw];
         __syncwarp();
     }
     __syncthreads();
     for (int kw = warp; kw < MW; kw += 8) {
-        warp_fft_row<false>(col + kw * Hp, Hp, twf_h, lane);
+        warp_fft_row_first<false>(col + kw * Hp, Hp, twf_h, lane, MH);
         for (int kh = lane; kh < MH; kh += 32)
             Xs[((static_cast<int64_t>(b) * C + c) * MH + kh) * MW + kw] = col[kw * Hp + kh];
     }
