@@ -206,6 +206,10 @@ struct Layer2dArgs {
     int obs_i;
 };
 
+// OBS: calibration observers compiled in; I8: the INT8 composition (int8 Linear and /
+// or the output snap) compiled in.  The plain FP32 network runs the <false, false>
+// instantiation, with neither in its loops.
+template <bool OBS, bool I8>
 __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
     extern __shared__ float2 sm[];
     const int Wp = a.Wp, C = a.C, Hp = a.Hp;
@@ -216,7 +220,7 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int lgW = 31 - __clz(Wp);
     const int half = Wp / 2 + 1;
-    const bool i8 = a.i8.wz != nullptr;
+    const bool i8 = I8 && a.i8.wz != nullptr;
     const float zp_in = static_cast<float>(a.i8.zp_in);
     for (int t = threadIdx.x; t < C * Wp; t += blockDim.x) {
         const int k = t / Wp, w = t - (t / Wp) * Wp;
@@ -302,14 +306,14 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
             for (int j = 0; j < kMaxWp / 32; ++j) {
                 const int w = lane + 32 * j;
                 if (j < nj && w < Wp) {
-                    if (a.obs) {
+                    if (OBS) {
                         ob.see(acc[j]);
                         if (a.obs_vals) a.obs_vals[((static_cast<int64_t>(b) * Hp + hh) * Wp + w) * C + o] = acc[j];
                     }
                     const float x2 = apply_fq(acc[j], a.fq);
                     const float x1 = __fmul_rn(sX1[static_cast<size_t>(r) * Wp + w].x, invW);
                     const float z = __fadd_rn(x1, x2);
-                    if (a.snap.fq.kind == 1) {
+                    if (I8 && a.snap.fq.kind == 1) {
                         const float zpo = static_cast<float>(a.snap.fq.zp);
                         const float q = a.snap.code_lut
                                             ? static_cast<float>(code_from_lut(z, a.snap.code_lut, a.snap.lut_cells,
@@ -324,11 +328,12 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
         }
         __syncthreads();
     }
-    if (a.obs) ob.flush(a.obs, a.obs_i);
+    if (OBS) ob.flush(a.obs, a.obs_i);
 }
 
 // projection (fno.cpp:966-993): one unpadded point per thread, its channel column
 // staged in shared memory [threads][C + 1]
+template <bool OBS, bool I8>
 __global__ void __launch_bounds__(128) proj2d_f32_kernel(Fno2dF32Plan p, const float* __restrict__ h) {
     extern __shared__ float sh[];
     float* mine = sh + static_cast<size_t>(threadIdx.x) * (p.C + 1);
@@ -337,7 +342,7 @@ __global__ void __launch_bounds__(128) proj2d_f32_kernel(Fno2dF32Plan p, const f
     const int nu = linear_unfused_len(C);
     Obs obq, obo;
     const int iq = p.L + 1, io = p.L + 2;
-    const bool pq8 = p.pq_i8.wz != nullptr;
+    const bool pq8 = I8 && p.pq_i8.wz != nullptr;
     const float zp_in = static_cast<float>(p.pq_i8.zp_in);
     const float zp_pq = static_cast<float>(p.fq_pq.zp);
     for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
@@ -373,11 +378,11 @@ __global__ void __launch_bounds__(128) proj2d_f32_kernel(Fno2dF32Plan p, const f
                 const float* wr = p.pq_w + static_cast<int64_t>(c) * C;
                 for (int k = 0; k < C; ++k) q = linear_step(q, mine[k], __ldg(wr + k), k >= nu);
             }
-            if (p.obs) {
+            if (OBS) {
                 obq.see(q);
                 if (p.obs_vals[iq]) p.obs_vals[iq][t * C + c] = q;
             }
-            if (p.pq_act_table && p.fq_pq.kind == 1)
+            if (I8 && p.pq_act_table && p.fq_pq.kind == 1)
                 q = __ldg(p.pq_act_table + static_cast<int>(fq_code(q, p.fq_pq.scale, zp_pq)) + 128);
             else
                 q = act_f(apply_fq(q, p.fq_pq), p.act);
@@ -390,14 +395,14 @@ __global__ void __launch_bounds__(128) proj2d_f32_kernel(Fno2dF32Plan p, const f
 #pragma unroll
         for (int j = 0; j < 16; ++j)
             if (j < p.out_ch) {
-                if (p.obs) {
+                if (OBS) {
                     obo.see(acc[j]);
                     if (p.obs_vals[io]) p.obs_vals[io][t * p.out_ch + j] = acc[j];
                 }
                 yr[j] = apply_fq(acc[j], p.fq_po);
             }
     }
-    if (p.obs) {
+    if (OBS) {
         obq.flush(p.obs, iq);
         obo.flush(p.obs, io);
     }
@@ -447,8 +452,17 @@ cudaError_t fno2d_f32_run(const Fno2dF32Plan& p, cudaStream_t st) {
     const size_t sx = (static_cast<size_t>(G) * p.MH * p.MW + 8 * static_cast<size_t>(p.Hp)) * sizeof(float2);
     const size_t sl = layer_smem(p.C, p.Wp);
     if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(fwd2d_kernel), static_cast<int>(sf))) != cudaSuccess ||
-        (e = set_max_dynamic_smem(reinterpret_cast<const void*>(mix2d_kernel), static_cast<int>(sx))) != cudaSuccess ||
-        (e = set_max_dynamic_smem(reinterpret_cast<const void*>(layer2d_kernel), static_cast<int>(sl))) != cudaSuccess)
+        (e = set_max_dynamic_smem(reinterpret_cast<const void*>(mix2d_kernel), static_cast<int>(sx))) != cudaSuccess)
+        return e;
+    // the instantiation of the layer and projection kernels: observers, INT8 composition
+    const bool obs = p.obs != nullptr;
+    bool i8 = p.pq_i8.wz != nullptr || p.pq_act_table != nullptr;
+    for (int i = 0; i < p.L; ++i) i8 = i8 || p.layer[i].i8.wz != nullptr || p.layer[i].snap.fq.kind != 0;
+    auto layer_k = obs ? (i8 ? layer2d_kernel<true, true> : layer2d_kernel<true, false>)
+                       : (i8 ? layer2d_kernel<false, true> : layer2d_kernel<false, false>);
+    auto proj_k = obs ? (i8 ? proj2d_f32_kernel<true, true> : proj2d_f32_kernel<true, false>)
+                      : (i8 ? proj2d_f32_kernel<false, true> : proj2d_f32_kernel<false, false>);
+    if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(layer_k), static_cast<int>(sl))) != cudaSuccess)
         return e;
     for (int i = 0; i < p.L; ++i) {
         const float* hin = p.h[i & 1];
@@ -482,7 +496,7 @@ cudaError_t fno2d_f32_run(const Fno2dF32Plan& p, cudaStream_t st) {
         a.MW = p.MW;
         a.act = p.act;
         if (p.timer) p.timer->begin("fno2d_f32_layer", st);
-        layer2d_kernel<<<dim3(p.Hp, p.B), 256, sl, st>>>(a);
+        layer_k<<<dim3(p.Hp, p.B), 256, sl, st>>>(a);
         if (p.timer) p.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
@@ -490,12 +504,12 @@ cudaError_t fno2d_f32_run(const Fno2dF32Plan& p, cudaStream_t st) {
         const int64_t total = static_cast<int64_t>(p.B) * p.H * p.W;
         const int threads = p.C > 128 ? 64 : 128;
         const size_t smem = static_cast<size_t>(threads) * (p.C + 1) * sizeof(float);
-        if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(proj2d_f32_kernel), static_cast<int>(smem))) !=
+        if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(proj_k), static_cast<int>(smem))) !=
             cudaSuccess)
             return e;
         const int grid = static_cast<int>(std::min<int64_t>((total + threads - 1) / threads, sms * 8));
         if (p.timer) p.timer->begin("fno2d_f32_proj", st);
-        proj2d_f32_kernel<<<grid, threads, smem, st>>>(p, p.h[p.L & 1]);
+        proj_k<<<grid, threads, smem, st>>>(p, p.h[p.L & 1]);
         if (p.timer) p.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
