@@ -204,48 +204,63 @@ __device__ __forceinline__ void split_tf32_m(float x, float& hi, float& lo) {
 }
 
 constexpr int kMixTcThreads = 256;
-template <int C>
+// PRE: every K chunk's weight tiles resident at once (one weight buffer pair per
+// chunk, 160 KB; used when one sample tile per mode leaves CTAs one per SM), all
+// requested before the kernel waits for its predecessor; otherwise one buffer pair,
+// chunk c's weights requested once chunk c - 1's MMAs have read theirs (66 KB, several
+// CTAs per SM).
+template <int C, bool PRE>
 struct MixCfg {
     static constexpr int kK = 2 * C;                 // 128 floats per row
     static constexpr int kChunk = 32;                // floats per K chunk
     static constexpr int kChunks = kK / kChunk;
     static constexpr int kTile = 128 * 128;          // [128 rows][32 floats], SW128
+    static constexpr int kBufs = PRE ? kChunks : 1;  // weight buffer pairs (hi, lo)
     static constexpr int kOffAhi = 0;
     static constexpr int kOffAlo = kTile;
-    static constexpr int kOffBhi = 2 * kTile;
-    static constexpr int kOffBlo = 3 * kTile;
-    static constexpr int kOffBars = 4 * kTile;
-    static constexpr int kSmemBytes = kOffBars + 64 + 1024;
+    static constexpr int kOffB = 2 * kTile;
+    static constexpr int kOffBars = kOffB + 2 * kBufs * kTile;
+    static constexpr int kSmemBytes = kOffBars + 8 * (kBufs + 1) + 16 + 1024;
     static_assert(C == 64, "one 128-column accumulator");
 };
 
-template <int C, int MH, int MW>
+template <int C, int MH, int MW, bool PRE>
 __global__ void __launch_bounds__(kMixTcThreads) spec_mix_tc_kernel(const __grid_constant__ CUtensorMap tmWhi,
                                                                     const __grid_constant__ CUtensorMap tmWlo,
                                                                     const float2* __restrict__ xpart, int nHB,
                                                                     int B, float2* __restrict__ Y,
                                                                     unsigned* err) {
-    using F = MixCfg<C>;
+    using F = MixCfg<C, PRE>;
     constexpr int M = MH * MW;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sAhi = smem + F::kOffAhi;
     uint8_t* sAlo = smem + F::kOffAlo;
-    uint8_t* sBhi = smem + F::kOffBhi;
-    uint8_t* sBlo = smem + F::kOffBlo;
-    uint64_t* bFull = reinterpret_cast<uint64_t*>(smem + F::kOffBars);
-    uint64_t* mmaDone = bFull + 1;
-    uint32_t* sTmem = reinterpret_cast<uint32_t*>(bFull + 2);
+    uint8_t* sB = smem + F::kOffB;                   // pair q: hi at tile 2q, lo at 2q + 1
+    uint64_t* bFull = reinterpret_cast<uint64_t*>(smem + F::kOffBars);   // [kBufs]
+    uint64_t* mmaDone = bFull + F::kBufs;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(mmaDone + 1);
     volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m = blockIdx.x;
     const int b0 = blockIdx.y * 128;
 
+    // weight chunk c into buffer pair c % kBufs (the weights are read-only and written by
+    // no kernel of the forward, so they may be requested before the predecessor ends)
+    auto load_w = [&](int c) {
+        const int q = c % F::kBufs;
+        mbar_arrive_expect_tx(&bFull[q], 2 * F::kTile);
+        tma_load_2d(sB + 2 * q * F::kTile, &tmWhi, &bFull[q], c * F::kChunk, m * F::kK);
+        tma_load_2d(sB + (2 * q + 1) * F::kTile, &tmWlo, &bFull[q], c * F::kChunk, m * F::kK);
+    };
     if (threadIdx.x == 0) {
-        mbar_init(bFull, 1);
+        for (int q = 0; q < F::kBufs; ++q) mbar_init(&bFull[q], 1);
         mbar_init(mmaDone, 1);
         *sAbort = 0;
         fence_mbar_init();
+        prefetch_tmap(&tmWhi);
+        prefetch_tmap(&tmWlo);
+        for (int c = 0; c < F::kBufs; ++c) load_w(c);
     }
     if (warp == 0) tmem_alloc(sTmem, 128);
     tc_fence_before();
@@ -257,7 +272,7 @@ __global__ void __launch_bounds__(kMixTcThreads) spec_mix_tc_kernel(const __grid
     grid_dep_launch();
     constexpr uint32_t idesc = idesc_tf32(128);
     bool ok = true;
-    int issued = 0;   // TMA chunk loads issued
+    int issued = F::kBufs;   // weight chunk loads issued
 
     // A chunk c: rows = samples, columns k = 2 i + re/im for i in [16 c, 16 c + 16); the
     // partials of chunk c + 1 are loaded while the MMAs of chunk c run
@@ -289,16 +304,10 @@ __global__ void __launch_bounds__(kMixTcThreads) spec_mix_tc_kernel(const __grid
             ok = false;
             break;
         }
-        if (threadIdx.x == 0) {
-            if (c == 0) {
-                prefetch_tmap(&tmWhi);
-                prefetch_tmap(&tmWlo);
-            }
-            mbar_arrive_expect_tx(bFull, 2 * F::kTile);
-            tma_load_2d(sBhi, &tmWhi, bFull, c * F::kChunk, m * F::kK);
-            tma_load_2d(sBlo, &tmWlo, bFull, c * F::kChunk, m * F::kK);
+        if (!PRE && c > 0) {
+            if (threadIdx.x == 0) load_w(c);
+            ++issued;
         }
-        ++issued;
 #pragma unroll
         for (int q = 0; q < kPer; ++q) {
             const int idx = threadIdx.x + kMixTcThreads * q;
@@ -322,13 +331,14 @@ __global__ void __launch_bounds__(kMixTcThreads) spec_mix_tc_kernel(const __grid
         fence_proxy_async_smem();
         __syncthreads();
         if (threadIdx.x == 0) {
-            if (!mbar_wait(bFull, c & 1, sAbort)) {
+            const int q = c % F::kBufs;
+            if (!mbar_wait(&bFull[q], (c / F::kBufs) & 1, sAbort)) {
                 *sAbort = 1;
                 atomicOr(err, kErrWaitTmaFull);
             } else {
                 tc_fence_after();
                 const uint32_t ahi = smem_u32(sAhi), alo = smem_u32(sAlo);
-                const uint32_t bhi = smem_u32(sBhi), blo = smem_u32(sBlo);
+                const uint32_t bhi = smem_u32(sB + 2 * q * F::kTile), blo = bhi + F::kTile;
 #pragma unroll
                 for (int kk = 0; kk < F::kChunk / 8; ++kk) {
                     mma_tf32(tmem_base, umma_desc(ahi + kk * 32, 128), umma_desc(bhi + kk * 32, 128), idesc,
@@ -348,7 +358,11 @@ __global__ void __launch_bounds__(kMixTcThreads) spec_mix_tc_kernel(const __grid
         if (threadIdx.x == 0) {
             atomicOr(err, kErrWaitAccFull);
             // the TMA loads already issued land before the CTA leaves
-            mbar_wait(bFull, (issued - 1) & 1, sAbort);
+            if (PRE) {
+                for (int q = 0; q < F::kBufs; ++q) mbar_wait_drain(&bFull[q], 0);
+            } else {
+                mbar_wait_drain(bFull, (issued - 1) & 1);
+            }
         }
     } else if (warp < 4) {
         tc_fence_after();
@@ -2306,9 +2320,13 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
         }
         {
             if (pl.layer[i].wmix_hi == nullptr || pl.layer[i].wmix_lo == nullptr) return cudaErrorInvalidValue;
-            using FM = MixCfg<C>;
-            auto k = spec_mix_tc_kernel<C, MH, MW>;
-            if ((e = set_smem(k, FM::kSmemBytes)) != cudaSuccess) return e;
+            using FM = MixCfg<C, false>;
+            // every chunk's weights resident when one sample tile per mode gives one CTA
+            // per SM anyway
+            const bool pre = (pl.B + 127) / 128 == 1;
+            auto k = pre ? spec_mix_tc_kernel<C, MH, MW, true> : spec_mix_tc_kernel<C, MH, MW, false>;
+            const int mix_smem = pre ? MixCfg<C, true>::kSmemBytes : FM::kSmemBytes;
+            if ((e = set_smem(k, mix_smem)) != cudaSuccess) return e;
             CUtensorMap thi, tlo;
             const uint64_t rows = static_cast<uint64_t>(MH) * MW * FM::kK;
             if (!encode_2d(&thi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pl.layer[i].wmix_hi, FM::kK, rows,
@@ -2317,7 +2335,7 @@ cudaError_t run_layers(const Fno2dPlan& pl, cudaStream_t st) {
                            FM::kK * 4, FM::kChunk, FM::kK, 128))
                 return cudaErrorInvalidValue;
             if (pl.timer) pl.timer->begin("fno2d_spec_mix", st);
-            e = launch_pdl(k, dim3(MH * MW, (pl.B + 127) / 128), dim3(kMixTcThreads), FM::kSmemBytes, st,
+            e = launch_pdl(k, dim3(MH * MW, (pl.B + 127) / 128), dim3(kMixTcThreads), mix_smem, st,
                            thi, tlo, static_cast<const float2*>(pl.xpart), nHB, pl.B, pl.Y, pl.err);
             if (e != cudaSuccess) return e;
             if (pl.timer) pl.timer->end(st);
