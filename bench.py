@@ -643,7 +643,7 @@ def main():
     if rank == 0:
         if ws == 1 and not args.no_gemm:
             import torch
-            result["gemm_sweep"] = gemm_rows(torch.device("cuda", local), (1 << 20,),
+            result["gemm_sweep"] = gemm_rows(torch.device("cuda", local), (65536, 1 << 20),
                                              (32, 64, 128, 256))
         if ws == 1 and not args.no_cpu_baseline:
             n = os.cpu_count() or 1
