@@ -22,6 +22,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
 
 #include "fft_exact.cuh"
@@ -41,33 +42,36 @@ __device__ __forceinline__ float inv_of(float s) { return s == 0.0f ? 1.0f : __f
 
 // the value of an activation element: fp32, or an E4M3 code times its scale
 __device__ __forceinline__ float value_at(const void* h, int64_t i, int fp8, float s) {
-    if (fp8) return __fmul_rn(e4m3_decode_ref(static_cast<const uint8_t*>(h)[i]), s);
+    if (fp8) return __fmul_rn(e4m3_decode_fast(static_cast<const uint8_t*>(h)[i]), s);
     return static_cast<const float*>(h)[i];
 }
 
+// one padded point per thread, every channel (the padded sides are powers of two, so
+// the point index splits by shifts; the input row is read once into L1)
 __global__ void __launch_bounds__(256) lift3d_kernel(Fno3dPlan p) {
-    const int64_t P = static_cast<int64_t>(p.Hp) * p.Wp * p.Dp;
-    const int64_t total = static_cast<int64_t>(p.B) * p.C * P;
+    const int lgD = 31 - __clz(p.Dp), lgW = 31 - __clz(p.Wp);
+    const int lgP = lgD + lgW + (31 - __clz(p.Hp));
+    const int64_t total = static_cast<int64_t>(p.B) << lgP;
     const int nu = linear_unfused_len(p.in_ch);
     const float inv = inv_of(p.s_lift);
     for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
          t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t pt = t % P;
-        const int64_t bc = t / P;
-        const int c = static_cast<int>(bc % p.C);
-        const int64_t b = bc / p.C;
-        const int dd = static_cast<int>(pt % p.Dp);
-        const int ww = static_cast<int>((pt / p.Dp) % p.Wp);
-        const int hh = static_cast<int>(pt / (static_cast<int64_t>(p.Dp) * p.Wp));
-        float v = 0.0f;
-        if (hh < p.H && ww < p.W && dd < p.D) {
-            const float* xr = p.x + (((b * p.H + hh) * p.W + ww) * p.D + dd) * p.in_ch;
-            v = __ldg(p.lift_b + c);
-            for (int k = 0; k < p.in_ch; ++k)
-                v = linear_step(v, __ldg(xr + k), __ldg(p.lift_w + c * p.in_ch + k), k >= nu);
+        const int64_t b = t >> lgP;
+        const int pt = static_cast<int>(t - (b << lgP));
+        const int dd = pt & (p.Dp - 1), ww = (pt >> lgD) & (p.Wp - 1), hh = pt >> (lgD + lgW);
+        const bool inside = hh < p.H && ww < p.W && dd < p.D;
+        const float* xr = p.x + (((b * p.H + hh) * p.W + ww) * p.D + dd) * p.in_ch;
+        for (int c = 0; c < p.C; ++c) {
+            float v = 0.0f;
+            if (inside) {
+                v = __ldg(p.lift_b + c);
+                for (int k = 0; k < p.in_ch; ++k)
+                    v = linear_step(v, __ldg(xr + k), __ldg(p.lift_w + c * p.in_ch + k), k >= nu);
+            }
+            const int64_t o = ((b * p.C + c) << lgP) + pt;
+            if (p.fp8) static_cast<uint8_t*>(p.h[0])[o] = static_cast<uint8_t>(e4m3_code(v, inv));
+            else static_cast<float*>(p.h[0])[o] = v;
         }
-        if (p.fp8) static_cast<uint8_t*>(p.h[0])[t] = static_cast<uint8_t>(e4m3_code(v, inv));
-        else static_cast<float*>(p.h[0])[t] = v;
     }
 }
 
@@ -204,6 +208,297 @@ __global__ void __launch_bounds__(256) inv3d_kernel(Fno3dPlan p) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Direct truncated DFTs of the D and W passes (fno3d_direct_dft: the FP8 variant at
+// widths 32 / 64).  Only the kept modes are formed, each output one fp32 sum over its
+// line against the correctly rounded tables of fno3d_dft_tables:
+//   forward  Y[w][kd] = sum_d x[w][d] e^{-2 pi i kd d / Dp}              (real input)
+//            A[kw][kd] = s_in * sum_w Y[w][kd] e^{-2 pi i kw w / Wp}
+//   inverse  u[w][j]  = f_j sum_kw ci[kw][j] e^{+2 pi i kw w / Wp},
+//            f_j = (j = 0 or j = Dp/2 ? 1 : 2) / (Wp Dp)   (exact powers of two)
+//            x1[w][d] = sum_j Re(u[w][j] e^{+2 pi i j d / Dp})
+// The inverse is the Hermitian D-axis Irfft of the reference (a kept mode j in
+// 1 .. Dp/2 - 1 stands for itself and its conjugate at Dp - j), so x1 is the radix-2
+// passes' result up to fp32 rounding.
+// ---------------------------------------------------------------------------
+struct DftDims {
+    int MD4, MW2;   // kept modes rounded up to 4 (kd) and 2 (kw); table columns
+    int XS, YS;     // row strides (floats): decoded plane, D-pass output
+    int TWS, TWI;   // row strides (floats) of the W table: forward, inverse
+    int UJ;         // row stride (floats) of the inverse D-pass input u
+    int NPf, NPi;   // planes per CTA pass: forward, inverse
+};
+
+constexpr int kDftThreads = 128;
+constexpr int kDftPre = 4;  // uint4 of codes a thread prefetches per forward pass
+
+DftDims dft_dims(int Wp, int Dp, int MW, int MD) {
+    DftDims g;
+    g.MD4 = (MD + 3) / 4 * 4;
+    g.MW2 = (MW + 1) / 2 * 2;
+    g.XS = Dp + 4;
+    g.YS = 2 * g.MD4 + 4;
+    g.TWS = 2 * g.MW2 + 4;
+    g.TWI = 2 * g.MW2 + 2;
+    g.UJ = 2 * g.MD4 + 2;
+    const int items_f = (Wp / 2) * (g.MD4 / 4), items_i = (Wp / 8) * (Dp / 4);
+    g.NPf = std::max(1, kDftThreads / std::max(1, items_f));
+    while (g.NPf > 1 && g.NPf * Wp * Dp > kDftPre * kDftThreads * 16) g.NPf >>= 1;
+    g.NPi = std::max(1, kDftThreads / std::max(1, items_i));
+    return g;
+}
+
+size_t dft_fwd_smem(const DftDims& g, int Wp, int Dp) {
+    return sizeof(float) * (static_cast<size_t>(2) * Dp * g.MD4 + static_cast<size_t>(Wp) * g.TWS +
+                            static_cast<size_t>(g.NPf) * Wp * (g.XS + g.YS));
+}
+
+size_t dft_inv_smem(const DftDims& g, int Wp, int Dp, int MW) {
+    return sizeof(float) * (static_cast<size_t>(2) * g.MD4 * Dp + static_cast<size_t>(Wp) * g.TWI +
+                            static_cast<size_t>(g.NPi) * (static_cast<size_t>(MW) * 2 * g.MD4 +
+                                                          static_cast<size_t>(Wp) * g.UJ));
+}
+
+// Persistent over the B * C * Hp (b, c, h) planes, NPf planes per pass.
+// smem floats: tD [Dp][MD4] float2 | tW [Wp][TWS] | x [NPf][Wp][XS] | Y [NPf][Wp][YS]
+__global__ void __launch_bounds__(kDftThreads) fwd3d_dft_kernel(Fno3dPlan p, DftDims g,
+                                                                const uint8_t* __restrict__ hin, float s_in) {
+    extern __shared__ float4 sm4[];
+    float* sm = reinterpret_cast<float*>(sm4);
+    const int T = kDftThreads, tid = threadIdx.x;
+    const int Wp = p.Wp, Dp = p.Dp, MD4 = g.MD4, NP = g.NPf, half = Wp / 2;
+    float* tD = sm;
+    float* tW = tD + 2 * Dp * MD4;
+    float* sx = tW + Wp * g.TWS;
+    float* sY = sx + NP * Wp * g.XS;
+    for (int i = tid; i < 2 * Dp * MD4; i += T) tD[i] = __ldg(p.dft + i);
+    {
+        const float* gW = p.dft + 2 * Dp * MD4;
+        const int rw = 2 * g.MW2;
+        for (int i = tid; i < Wp * rw; i += T) tW[(i / rw) * g.TWS + i % rw] = __ldg(gW + i);
+    }
+    const int64_t nplanes = static_cast<int64_t>(p.B) * p.C * p.Hp;
+    const int v16 = Wp * Dp / 16;  // uint4 of codes per plane
+    const int nv = NP * v16;
+    const int64_t npass = (nplanes + NP - 1) / NP;
+    uint4 pre[kDftPre];
+    auto fetch = [&](int64_t pass) {
+        const int64_t q0 = pass * NP;
+        const uint4* src = reinterpret_cast<const uint4*>(hin) + q0 * v16;
+        const int64_t lim = (nplanes - q0) * v16;
+#pragma unroll
+        for (int r = 0; r < kDftPre; ++r) {
+            const int i = tid + r * T;
+            pre[r] = (i < nv && i < lim) ? __ldg(src + i) : make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+    int64_t pass = blockIdx.x;
+    if (pass < npass) fetch(pass);
+    const int items1 = half * (MD4 / 4);
+    const int items2 = (g.MW2 / 2) * (MD4 / 2) * 8;
+    for (; pass < npass; pass += gridDim.x) {
+        __syncthreads();  // the previous pass is done with x and Y
+#pragma unroll
+        for (int r = 0; r < kDftPre; ++r) {
+            const int i = tid + r * T;
+            if (i < nv) {
+                const int pl = i / v16, e = (i - pl * v16) * 16;
+                const int w = e / Dp, d = e - w * Dp;
+                float* dst = sx + (pl * Wp + w) * g.XS + d;
+                const uint32_t wd[4] = {pre[r].x, pre[r].y, pre[r].z, pre[r].w};
+#pragma unroll
+                for (int m = 0; m < 4; ++m)
+                    *reinterpret_cast<float4*>(dst + 4 * m) =
+                        make_float4(e4m3_decode_fast(wd[m] & 0xFFu), e4m3_decode_fast((wd[m] >> 8) & 0xFFu),
+                                    e4m3_decode_fast((wd[m] >> 16) & 0xFFu), e4m3_decode_fast(wd[m] >> 24));
+            }
+        }
+        if (pass + gridDim.x < npass) fetch(pass + gridDim.x);
+        __syncthreads();
+        // D pass: rows rp and rp + Wp/2, kept modes 4 kq .. 4 kq + 3
+        for (int it = tid; it < NP * items1; it += T) {
+            const int pl = it / items1, r = it - pl * items1;
+            const int rp = r % half, kq = r / half;
+            const float* x0 = sx + (pl * Wp + rp) * g.XS;
+            const float* x1p = x0 + half * g.XS;
+            const float* tk = tD + 8 * kq;
+            float a0[8], a1[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) a0[k] = a1[k] = 0.0f;
+#pragma unroll 2
+            for (int d = 0; d < Dp; d += 4) {
+                const float4 u = *reinterpret_cast<const float4*>(x0 + d);
+                const float4 v = *reinterpret_cast<const float4*>(x1p + d);
+                const float uu[4] = {u.x, u.y, u.z, u.w}, vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 t0 = *reinterpret_cast<const float4*>(tk + (d + q) * 2 * MD4);
+                    const float4 t1 = *reinterpret_cast<const float4*>(tk + (d + q) * 2 * MD4 + 4);
+                    const float tt[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        a0[k] = __fmaf_rn(uu[q], tt[k], a0[k]);
+                        a1[k] = __fmaf_rn(vv[q], tt[k], a1[k]);
+                    }
+                }
+            }
+            float* y0 = sY + (pl * Wp + rp) * g.YS + 8 * kq;
+            float* y1 = y0 + half * g.YS;
+            *reinterpret_cast<float4*>(y0) = make_float4(a0[0], a0[1], a0[2], a0[3]);
+            *reinterpret_cast<float4*>(y0 + 4) = make_float4(a0[4], a0[5], a0[6], a0[7]);
+            *reinterpret_cast<float4*>(y1) = make_float4(a1[0], a1[1], a1[2], a1[3]);
+            *reinterpret_cast<float4*>(y1 + 4) = make_float4(a1[4], a1[5], a1[6], a1[7]);
+        }
+        __syncthreads();
+        // W pass: 2 x 2 output modes per thread, w split over 8 consecutive lanes
+        for (int base = 0; base < NP * items2; base += T) {
+            const int it = base + tid;
+            const bool live = it < NP * items2;
+            const int pl = live ? it / items2 : 0, r = it - pl * items2;
+            const int s = r & 7, blk = r >> 3;
+            const int kwp = blk / (MD4 / 2), kdp = blk - kwp * (MD4 / 2);
+            float o[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) o[k] = 0.0f;
+            if (live) {
+                for (int w = s; w < Wp; w += 8) {
+                    const float4 y = *reinterpret_cast<const float4*>(sY + (pl * Wp + w) * g.YS + 4 * kdp);
+                    const float4 t = *reinterpret_cast<const float4*>(tW + w * g.TWS + 4 * kwp);
+                    const float yr[2] = {y.x, y.z}, yi[2] = {y.y, y.w};
+                    const float tc[2] = {t.x, t.z}, ts[2] = {t.y, t.w};
+#pragma unroll
+                    for (int a = 0; a < 2; ++a)
+#pragma unroll
+                        for (int c = 0; c < 2; ++c) {  // kw = 2 kwp + a, kd = 2 kdp + c
+                            float& re = o[4 * a + 2 * c];
+                            float& im = o[4 * a + 2 * c + 1];
+                            re = __fmaf_rn(yr[c], tc[a], re);
+                            re = __fmaf_rn(-yi[c], ts[a], re);
+                            im = __fmaf_rn(yr[c], ts[a], im);
+                            im = __fmaf_rn(yi[c], tc[a], im);
+                        }
+                }
+            }
+#pragma unroll
+            for (int m = 1; m < 8; m <<= 1)
+#pragma unroll
+                for (int k = 0; k < 8; ++k) o[k] = __fadd_rn(o[k], __shfl_xor_sync(0xffffffffu, o[k], m));
+            const int64_t q = pass * NP + pl;
+            if (live && s == 0 && q < nplanes) {
+                float2* A = p.A + q * p.MW * p.MD;
+#pragma unroll
+                for (int a = 0; a < 2; ++a)
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        const int kw = 2 * kwp + a, kd = 2 * kdp + c;
+                        if (kw < p.MW && kd < p.MD)
+                            A[kw * p.MD + kd] =
+                                make_float2(__fmul_rn(o[4 * a + 2 * c], s_in), __fmul_rn(o[4 * a + 2 * c + 1], s_in));
+                    }
+            }
+        }
+    }
+}
+
+// Persistent over the B * C * Hp (b, o, h) planes of colinv, NPi planes per pass.
+// smem floats: iC [MD4][Dp] | iS [MD4][Dp] | tW [Wp][TWI] | ci [NPi][MW][2 MD4] | u [NPi][Wp][UJ]
+__global__ void __launch_bounds__(kDftThreads) inv3d_dft_kernel(Fno3dPlan p, DftDims g) {
+    extern __shared__ float4 sm4[];
+    float* sm = reinterpret_cast<float*>(sm4);
+    const int T = kDftThreads, tid = threadIdx.x;
+    const int Wp = p.Wp, Dp = p.Dp, MW = p.MW, MD = p.MD, MD4 = g.MD4, NP = g.NPi;
+    float* iCS = sm;
+    float* tW = iCS + 2 * MD4 * Dp;
+    float* sci = tW + Wp * g.TWI;
+    float* su = sci + NP * MW * 2 * MD4;
+    {
+        const float* gW = p.dft + 2 * Dp * MD4;
+        const float* gI = gW + 2 * Wp * g.MW2;
+        for (int i = tid; i < 2 * MD4 * Dp; i += T) iCS[i] = __ldg(gI + i);
+        const int rw = 2 * g.MW2;
+        for (int i = tid; i < Wp * rw; i += T) tW[(i / rw) * g.TWI + i % rw] = __ldg(gW + i);
+    }
+    const float* iS = iCS + MD4 * Dp;
+    const int64_t nplanes = static_cast<int64_t>(p.B) * p.C * p.Hp;
+    const int KK = MW * MD;
+    const int64_t npass = (nplanes + NP - 1) / NP;
+    const float unit = __fdiv_rn(1.0f, static_cast<float>(Wp) * static_cast<float>(Dp));
+    const int items1 = Wp * (MD4 / 2);
+    const int items2 = (Wp / 8) * (Dp / 4);
+    for (int64_t pass = blockIdx.x; pass < npass; pass += gridDim.x) {
+        const int64_t q0 = pass * NP;
+        __syncthreads();  // the previous pass is done with ci and u
+        for (int i = tid; i < NP * MW * MD4; i += T) {
+            const int pl = i / (MW * MD4), r = i - pl * (MW * MD4);
+            const int kw = r / MD4, kd = r - kw * MD4;
+            float2 v = make_float2(0.0f, 0.0f);
+            if (kd < MD && q0 + pl < nplanes) v = p.colinv[(q0 + pl) * KK + kw * MD + kd];
+            *reinterpret_cast<float2*>(sci + (pl * MW + kw) * 2 * MD4 + 2 * kd) = v;
+        }
+        __syncthreads();
+        // W inverse of the kept kd columns (two per thread), scaled by f_j
+        for (int it = tid; it < NP * items1; it += T) {
+            const int pl = it / items1, r = it - pl * items1;
+            const int w = r % Wp, jp = r / Wp;
+            float ar0 = 0.0f, ai0 = 0.0f, ar1 = 0.0f, ai1 = 0.0f;
+            for (int kw = 0; kw < MW; ++kw) {
+                const float4 c = *reinterpret_cast<const float4*>(sci + (pl * MW + kw) * 2 * MD4 + 4 * jp);
+                const float2 t = *reinterpret_cast<const float2*>(tW + w * g.TWI + 2 * kw);
+                // (cr + i ci)(tc - i ts), (tc, ts) = e^{-2 pi i kw w / Wp}
+                ar0 = __fmaf_rn(c.x, t.x, ar0);
+                ar0 = __fmaf_rn(c.y, t.y, ar0);
+                ai0 = __fmaf_rn(c.y, t.x, ai0);
+                ai0 = __fmaf_rn(-c.x, t.y, ai0);
+                ar1 = __fmaf_rn(c.z, t.x, ar1);
+                ar1 = __fmaf_rn(c.w, t.y, ar1);
+                ai1 = __fmaf_rn(c.w, t.x, ai1);
+                ai1 = __fmaf_rn(-c.z, t.y, ai1);
+            }
+            const int j0 = 2 * jp, j1 = j0 + 1;
+            const float f0 = (j0 == 0 || 2 * j0 == Dp) ? unit : __fmul_rn(2.0f, unit);
+            const float f1 = (2 * j1 == Dp) ? unit : __fmul_rn(2.0f, unit);
+            // stored as (f Re, -f Im): x1 = sum_j u.x cos + u.y sin (UJ is even, not a multiple of 4)
+            float2* ud = reinterpret_cast<float2*>(su + (pl * Wp + w) * g.UJ + 4 * jp);
+            ud[0] = make_float2(__fmul_rn(ar0, f0), -__fmul_rn(ai0, f0));
+            ud[1] = make_float2(__fmul_rn(ar1, f1), -__fmul_rn(ai1, f1));
+        }
+        __syncthreads();
+        // D inverse: 8 rows x 4 consecutive points per thread
+        for (int it = tid; it < NP * items2; it += T) {
+            const int pl = it / items2, r = it - pl * items2;
+            const int dq = r % (Dp / 4), rg = r / (Dp / 4);
+            const float* ur = su + (pl * Wp + rg * 8) * g.UJ;
+            float acc[8][4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int m = 0; m < 4; ++m) acc[i][m] = 0.0f;
+            for (int j = 0; j < MD; ++j) {
+                const float4 c4 = *reinterpret_cast<const float4*>(iCS + j * Dp + 4 * dq);
+                const float4 s4 = *reinterpret_cast<const float4*>(iS + j * Dp + 4 * dq);
+                const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float2 u = *reinterpret_cast<const float2*>(ur + i * g.UJ + 2 * j);
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        acc[i][m] = __fmaf_rn(u.x, cc[m], acc[i][m]);
+                        acc[i][m] = __fmaf_rn(u.y, ss[m], acc[i][m]);
+                    }
+                }
+            }
+            const int64_t q = q0 + pl;
+            if (q < nplanes) {
+                float* x1 = p.x1 + (q * Wp + rg * 8) * Dp + 4 * dq;
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    *reinterpret_cast<float4*>(x1 + static_cast<int64_t>(i) * Dp) =
+                        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            }
+        }
+    }
+}
+
 // local layer + epilogue, one point per thread; smem weights [C][C]
 template <int C>
 __global__ void __launch_bounds__(128) local3d_kernel(Fno3dPlan p, Fno3dLayer L, const void* hin, void* hout) {
@@ -228,7 +523,7 @@ __global__ void __launch_bounds__(128) local3d_kernel(Fno3dPlan p, Fno3dLayer L,
 #pragma unroll
             for (int o = 0; o < C; ++o) acc[o] = 0.0f;
             for (int k = 0; k < C; ++k) {
-                const float a = e4m3_decode_ref(static_cast<const uint8_t*>(hin)[base + k * P]);
+                const float a = e4m3_decode_fast(static_cast<const uint8_t*>(hin)[base + k * P]);
 #pragma unroll
                 for (int o4 = 0; o4 < C / 4; ++o4) {
                     const float4 w = sW4[k * (C / 4) + o4];
@@ -462,8 +757,9 @@ local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, c
 // projection, one unpadded point per thread
 template <int C>
 __global__ void __launch_bounds__(128) proj3d_kernel(Fno3dPlan p, const void* hin, float s_in) {
-    __shared__ float sQ[C * C];
+    __shared__ float4 sQ4[C * C / 4];  // [c][k]: 16-byte broadcast loads over k
     const float* qsrc = p.fp8 ? p.pq_q : p.pq_w;
+    float* sQ = reinterpret_cast<float*>(sQ4);
     for (int i = threadIdx.x; i < C * C; i += blockDim.x) sQ[i] = qsrc[i];
     __syncthreads();
     const int64_t Pp = static_cast<int64_t>(p.Hp) * p.Wp * p.Dp;
@@ -482,41 +778,47 @@ __global__ void __launch_bounds__(128) proj3d_kernel(Fno3dPlan p, const void* hi
         float a[C];
 #pragma unroll
         for (int k = 0; k < C; ++k) {
-            if (p.fp8) a[k] = e4m3_decode_ref(static_cast<const uint8_t*>(hin)[base + k * Pp]);
+            if (p.fp8) a[k] = e4m3_decode_fast(static_cast<const uint8_t*>(hin)[base + k * Pp]);
             else a[k] = static_cast<const float*>(hin)[base + k * Pp];
         }
-        float acc[16];
+        float qv[C];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = j < p.out_ch ? __ldg(p.po_b + j) : 0.0f;
         for (int c = 0; c < C; ++c) {
-            float q;
-            if (p.fp8) {
-                q = 0.0f;
+            float q = p.fp8 ? 0.0f : __ldg(p.pq_b + c);
 #pragma unroll
-                for (int k = 0; k < C; ++k) q = __fadd_rn(q, __fmul_rn(a[k], sQ[c * C + k]));
-                q = fp8_fake_quant(__fadd_rn(__fmul_rn(q, sc), __ldg(p.pq_b + c)), p.s_pq, inv_pq);
-            } else {
-                q = __ldg(p.pq_b + c);
+            for (int k4 = 0; k4 < C / 4; ++k4) {
+                const float4 w = sQ4[c * (C / 4) + k4];
+                const float ww4[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                for (int k = 0; k < C; ++k) q = linear_step(q, a[k], sQ[c * C + k], k >= nu);
+                for (int m = 0; m < 4; ++m) {
+                    const int k = 4 * k4 + m;
+                    q = p.fp8 ? __fadd_rn(q, __fmul_rn(a[k], ww4[m])) : linear_step(q, a[k], ww4[m], k >= nu);
+                }
             }
-            q = act_f(q, p.act);
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (j < p.out_ch)
-                    acc[j] = linear_step(acc[j], q, __ldg(p.po_w + static_cast<int64_t>(j) * C + c), c >= nu);
+            if (p.fp8) q = fp8_fake_quant(__fadd_rn(__fmul_rn(q, sc), __ldg(p.pq_b + c)), p.s_pq, inv_pq);
+            qv[c] = act_f(q, p.act);
         }
         float* yr = p.y + t * p.out_ch;
+        for (int j = 0; j < p.out_ch; ++j) {
+            float acc = __ldg(p.po_b + j);
+            const float* wj = p.po_w + static_cast<int64_t>(j) * C;
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-            if (j < p.out_ch) yr[j] = p.fp8 ? fp8_fake_quant(acc[j], p.s_po, inv_po) : acc[j];
+            for (int c = 0; c < C; ++c) acc = linear_step(acc, qv[c], __ldg(wj + c), c >= nu);
+            yr[j] = p.fp8 ? fp8_fake_quant(acc, p.s_po, inv_po) : acc;
+        }
     }
 }
 
-int mix_group(int C) {
-    for (int G = 8; G > 1; G >>= 1)
-        if (C % G == 0) return G;
-    return 1;
+// output channels per mix3d CTA: at most 8, fewer while the grid would leave SMs idle
+int mix_group(int C, int64_t B = 0, int sms = 0) {
+    int G = 1;
+    for (int g = 8; g > 1; g >>= 1)
+        if (C % g == 0) {
+            G = g;
+            break;
+        }
+    while (G > 1 && static_cast<int64_t>(C / G) * B < 2 * static_cast<int64_t>(sms)) G >>= 1;
+    return G;
 }
 
 template <int C>
@@ -530,12 +832,12 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
         if (p.timer) p.timer->end(st);
         return cudaGetLastError();
     };
-    const int64_t tl = static_cast<int64_t>(p.B) * p.C * Pp;
+    const int64_t tl = static_cast<int64_t>(p.B) * Pp;
     if ((e = timed("fno3d_lift", [&] {
-             lift3d_kernel<<<static_cast<int>(std::min<int64_t>((tl + 255) / 256, sms * 32)), 256, 0, st>>>(p);
+             lift3d_kernel<<<static_cast<int>(std::min<int64_t>((tl + 255) / 256, sms * 16)), 256, 0, st>>>(p);
          })) != cudaSuccess)
         return e;
-    const int KK = p.MW * p.MD, M = p.MH * KK, G = mix_group(p.C);
+    const int KK = p.MW * p.MD, M = p.MH * KK, G = mix_group(p.C, p.B, sms);
     const int LN = std::max(p.Wp, p.Dp);
     const size_t sa = (8 * static_cast<size_t>(p.Dp) + static_cast<size_t>(p.MD) * p.Wp) * sizeof(float2);
     const size_t sb = 8 * static_cast<size_t>(p.Hp) * sizeof(float2);
@@ -546,6 +848,26 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
         (e = set_max_dynamic_smem(reinterpret_cast<const void*>(mix3d_kernel), static_cast<int>(sx))) != cudaSuccess ||
         (e = set_max_dynamic_smem(reinterpret_cast<const void*>(inv3d_kernel), static_cast<int>(si))) != cudaSuccess)
         return e;
+    const bool direct = p.dft != nullptr;
+    const DftDims g = dft_dims(p.Wp, p.Dp, p.MW, p.MD);
+    const size_t sdf = dft_fwd_smem(g, p.Wp, p.Dp), sdi = dft_inv_smem(g, p.Wp, p.Dp, p.MW);
+    int gdf = 0, gdi = 0;
+    if (direct) {
+        if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(fwd3d_dft_kernel), static_cast<int>(sdf))) !=
+                cudaSuccess ||
+            (e = set_max_dynamic_smem(reinterpret_cast<const void*>(inv3d_dft_kernel), static_cast<int>(sdi))) !=
+                cudaSuccess)
+            return e;
+        int of = 0, oi = 0;
+        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&of, fwd3d_dft_kernel, kDftThreads, sdf)) !=
+                cudaSuccess ||
+            (e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&oi, inv3d_dft_kernel, kDftThreads, sdi)) !=
+                cudaSuccess)
+            return e;
+        const int64_t planes = static_cast<int64_t>(p.B) * p.C * p.Hp;
+        gdf = static_cast<int>(std::min<int64_t>((planes + g.NPf - 1) / g.NPf, static_cast<int64_t>(sms) * std::max(1, of)));
+        gdi = static_cast<int>(std::min<int64_t>((planes + g.NPi - 1) / g.NPi, static_cast<int64_t>(sms) * std::max(1, oi)));
+    }
     const int64_t tp = static_cast<int64_t>(p.B) * Pp;
     const int lgrid = static_cast<int>(std::min<int64_t>((tp + 127) / 128, sms * 16));
     for (int i = 0; i < p.L; ++i) {
@@ -553,7 +875,10 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
         const void* hin = p.h[i & 1];
         void* hout = p.h[(i + 1) & 1];
         if ((e = timed("fno3d_fwd", [&] {
-                 fwd3d_a_kernel<<<dim3(p.Hp, p.C, p.B), 256, sa, st>>>(p, hin, L.s_in);
+                 if (direct)
+                     fwd3d_dft_kernel<<<gdf, kDftThreads, sdf, st>>>(p, g, static_cast<const uint8_t*>(hin), L.s_in);
+                 else
+                     fwd3d_a_kernel<<<dim3(p.Hp, p.C, p.B), 256, sa, st>>>(p, hin, L.s_in);
                  fwd3d_b_kernel<<<dim3(p.C, p.B), 256, sb, st>>>(p);
              })) != cudaSuccess)
             return e;
@@ -561,7 +886,10 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
                  mix3d_kernel<<<dim3(p.C / G, p.B), 256, sx, st>>>(p, L.wr, L.wi, G);
              })) != cudaSuccess)
             return e;
-        if ((e = timed("fno3d_inv", [&] { inv3d_kernel<<<dim3(p.Hp, p.C, p.B), 256, si, st>>>(p); })) != cudaSuccess)
+        if ((e = timed("fno3d_inv", [&] {
+                 if (direct) inv3d_dft_kernel<<<gdi, kDftThreads, sdi, st>>>(p, g);
+                 else inv3d_kernel<<<dim3(p.Hp, p.C, p.B), 256, si, st>>>(p);
+             })) != cudaSuccess)
             return e;
         bool tc = false;
         if constexpr (C == 32 || C == 64) {
@@ -611,6 +939,40 @@ const char* fno3d_unsupported(int C, int Hp, int Wp, int Dp, int MH, int MW, int
         (8 * static_cast<size_t>(Dp) + static_cast<size_t>(MD) * Wp) * sizeof(float2) > 200 * 1024)
         return "FNO3d GPU executor: too many modes for the shared-memory transforms";
     return nullptr;
+}
+
+bool fno3d_direct_dft(int C, int fp8, int Wp, int Dp, int MW, int MD) {
+    if (!fp8 || (C != 32 && C != 64)) return false;
+    if (Dp % 16 != 0 || Wp % 8 != 0 || static_cast<int64_t>(Wp) * Dp > kDftPre * kDftThreads * 16) return false;
+    const DftDims g = dft_dims(Wp, Dp, MW, MD);
+    return dft_fwd_smem(g, Wp, Dp) <= 200 * 1024 && dft_inv_smem(g, Wp, Dp, MW) <= 200 * 1024;
+}
+
+std::vector<float> fno3d_dft_tables(int Wp, int Dp, int MW, int MD) {
+    const DftDims g = dft_dims(Wp, Dp, MW, MD);
+    const double two_pi = 6.283185307179586476925286766559;
+    std::vector<float> t(2 * static_cast<size_t>(Dp) * g.MD4 + 2 * static_cast<size_t>(Wp) * g.MW2 +
+                             2 * static_cast<size_t>(g.MD4) * Dp,
+                         0.0f);
+    float* fD = t.data();
+    float* fW = fD + 2 * static_cast<size_t>(Dp) * g.MD4;
+    float* iC = fW + 2 * static_cast<size_t>(Wp) * g.MW2;
+    float* iS = iC + static_cast<size_t>(g.MD4) * Dp;
+    for (int d = 0; d < Dp; ++d)
+        for (int k = 0; k < MD; ++k) {
+            const double a = two_pi * static_cast<double>((static_cast<int64_t>(k) * d) % Dp) / Dp;
+            fD[2 * (static_cast<size_t>(d) * g.MD4 + k)] = static_cast<float>(std::cos(a));
+            fD[2 * (static_cast<size_t>(d) * g.MD4 + k) + 1] = static_cast<float>(-std::sin(a));
+            iC[static_cast<size_t>(k) * Dp + d] = static_cast<float>(std::cos(a));
+            iS[static_cast<size_t>(k) * Dp + d] = static_cast<float>(std::sin(a));
+        }
+    for (int w = 0; w < Wp; ++w)
+        for (int k = 0; k < MW; ++k) {
+            const double a = two_pi * static_cast<double>((static_cast<int64_t>(k) * w) % Wp) / Wp;
+            fW[2 * (static_cast<size_t>(w) * g.MW2 + k)] = static_cast<float>(std::cos(a));
+            fW[2 * (static_cast<size_t>(w) * g.MW2 + k) + 1] = static_cast<float>(-std::sin(a));
+        }
+    return t;
 }
 
 cudaError_t fno3d_run(const Fno3dPlan& p, cudaStream_t st) {

@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <vector>
 
 #include "nfx_internal.h"
 
@@ -49,8 +50,22 @@ struct Fno3dPlan {
     float2* Xs;            // (B, C, MH, MW, MD)
     float2* colinv;        // (B, C, Hp, MW, MD) after the H inverse pass
     float* x1;             // (B, C, Hp, Wp, Dp) spectral branch output
+    const float* dft;      // direct-DFT tables (fno3d_dft_tables), or null: radix-2 passes
     KernelTimer* timer;
 };
+
+// The FP8 variant at widths 32 and 64 (whose tensor-core local layer already holds it
+// to 1e-3 relative L2 rather than bit-exactness) runs the D and W passes as direct
+// truncated DFTs on CUDA cores instead of the reference's radix-2 transforms: only
+// the kept modes are formed, every output a plain fp32 sum over one line.  The values
+// are the same transform's up to fp32 rounding.  True when that path applies.
+bool fno3d_direct_dft(int C, int fp8, int Wp, int Dp, int MW, int MD);
+// Its tables, correctly rounded from double (floats; MD4 = MD rounded up to 4, MW2 = MW
+// rounded up to 2, columns past MD / MW zero):
+//   [Dp][MD4] float2  e^{-2 pi i kd d / Dp}
+//   [Wp][MW2] float2  e^{-2 pi i kw w / Wp}
+//   [MD4][Dp]         cos(2 pi j d / Dp), then [MD4][Dp] sin(2 pi j d / Dp)
+std::vector<float> fno3d_dft_tables(int Wp, int Dp, int MW, int MD);
 
 const char* fno3d_unsupported(int C, int Hp, int Wp, int Dp, int MH, int MW, int MD, int out_ch);
 cudaError_t fno3d_run(const Fno3dPlan& plan, cudaStream_t stream);

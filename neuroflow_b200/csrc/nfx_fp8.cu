@@ -38,6 +38,22 @@ __global__ void e4m3_fake_quant_kernel(const float* __restrict__ x, float scale,
         out[i] = nfx::fp8_fake_quant(x[i], scale, inv);
 }
 
+// Every fp32 bit pattern, clamped as e4m3_code clamps, through the hardware-conversion
+// encoder and the reference one; every code through both decoders (bit patterns).
+__global__ void e4m3_selfcheck_kernel(unsigned long long* bad) {
+    unsigned long long n = 0;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < (1ull << 32); i += stride) {
+        const float v = __uint_as_float(static_cast<uint32_t>(i));
+        const float xs = v > 448.0f ? 448.0f : (v < -448.0f ? -448.0f : v);
+        if (nfx::e4m3_encode_fast(xs) != nfx::e4m3_encode_ref(xs)) ++n;
+        if (i < 256 && __float_as_uint(nfx::e4m3_decode_fast(static_cast<uint32_t>(i))) !=
+                           __float_as_uint(nfx::e4m3_decode_ref(static_cast<uint32_t>(i))))
+            ++n;
+    }
+    if (n) atomicAdd(bad, n);
+}
+
 int grid_for(int64_t n) {
     const int64_t blocks = (n + 255) / 256;
     const int cap = 8 * nfx::device_sm_count();
@@ -132,6 +148,25 @@ int nfx_fp8_e4m3_fake_quant_host(const float* x, float scale, float* y, int64_t 
     return host_call(x, y, n, [n, scale, inv](const float* dx, float* dy, cudaStream_t st) {
         e4m3_fake_quant_kernel<<<grid_for(n), 256, 0, st>>>(dx, scale, inv, dy, n);
     }, "nfx_fp8_e4m3_fake_quant_host");
+}
+
+int nfx_fp8_e4m3_selfcheck(unsigned long long* mismatches) {
+    if (!mismatches) return nfx::set_thread_error(NFX_INVALID_ARG, "nfx_fp8_e4m3_selfcheck: null output");
+    unsigned long long* d = nullptr;
+    if (cudaMalloc(&d, sizeof(*d)) != cudaSuccess)
+        return nfx::set_thread_error(NFX_INTERNAL, "nfx_fp8_e4m3_selfcheck: device allocation failed");
+    int rc = NFX_OK;
+    if (cudaMemset(d, 0, sizeof(*d)) != cudaSuccess) {
+        rc = nfx::set_thread_error(NFX_INTERNAL, "nfx_fp8_e4m3_selfcheck: memset failed");
+    } else {
+        e4m3_selfcheck_kernel<<<8 * nfx::device_sm_count(), 256>>>(d);
+        if (cudaGetLastError() != cudaSuccess)
+            rc = launch_fail("nfx_fp8_e4m3_selfcheck");
+        else if (cudaMemcpy(mismatches, d, sizeof(*d), cudaMemcpyDeviceToHost) != cudaSuccess)
+            rc = nfx::set_thread_error(NFX_INTERNAL, "nfx_fp8_e4m3_selfcheck: execution failed");
+    }
+    cudaFree(d);
+    return rc;
 }
 
 }  // extern "C"

@@ -210,6 +210,8 @@ struct nfx_runtime {
     int64_t f3_cap[6] = {};
     float2* f3_tw[6] = {};
     int f3_tw_dims[3] = {0, 0, 0};
+    float* f3_dft = nullptr;         // direct-DFT tables of the FP8 width-32/64 variant
+    int f3_dft_key[4] = {0, 0, 0, 0};
     // TokenMixer2D state
     nfx::Tm2dPlan plan_tm{};
     void* tm_bufs[13] = {};
@@ -1228,6 +1230,20 @@ int fno3d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
         }
         for (int i = 0; i < 3; ++i) rt->f3_tw_dims[i] = pd[i];
     }
+    const bool direct = nfx::fno3d_direct_dft(pl0.C, pl0.fp8, pd[1], pd[2], pl0.MW, pl0.MD);
+    const int dkey[4] = {pd[1], pd[2], pl0.MW, pl0.MD};
+    if (direct && !std::equal(dkey, dkey + 4, rt->f3_dft_key)) {
+        const std::vector<float> t = nfx::fno3d_dft_tables(pd[1], pd[2], pl0.MW, pl0.MD);
+        if (rt->f3_dft) cudaFree(rt->f3_dft);
+        rt->f3_dft = nullptr;
+        std::fill(rt->f3_dft_key, rt->f3_dft_key + 4, 0);
+        void* p = nullptr;
+        if (!cuda_ok(rt, cudaMalloc(&p, t.size() * 4), "cudaMalloc DFT tables")) return NFX_INTERNAL;
+        rt->f3_dft = static_cast<float*>(p);
+        if (!cuda_ok(rt, cudaMemcpy(p, t.data(), t.size() * 4, cudaMemcpyHostToDevice), "cudaMemcpy DFT tables"))
+            return NFX_INTERNAL;
+        std::copy(dkey, dkey + 4, rt->f3_dft_key);
+    }
     const int64_t vol = static_cast<int64_t>(B) * pl0.C * pd[0] * pd[1] * pd[2];
     const int64_t kk = static_cast<int64_t>(B) * pl0.C * pl0.MW * pl0.MD;
     const int64_t sizes[6] = {vol * 4, vol * 4, kk * pd[0] * 8, kk * pl0.MH * 8, kk * pd[0] * 8, vol * 4};
@@ -1251,6 +1267,7 @@ int fno3d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
     pl.x = dx;
     pl.y = dy;
     for (int i = 0; i < 6; ++i) pl.tw[i] = rt->f3_tw[i];
+    pl.dft = direct ? rt->f3_dft : nullptr;
     pl.h[0] = rt->f3_bufs[0];
     pl.h[1] = rt->f3_bufs[1];
     pl.A = static_cast<float2*>(rt->f3_bufs[2]);
@@ -2085,6 +2102,7 @@ void nfx_runtime_destroy(nfx_runtime* rt) {
         if (p) cudaFree(p);
     for (auto* p : rt->f3_tw)
         if (p) cudaFree(p);
+    if (rt->f3_dft) cudaFree(rt->f3_dft);
     for (auto* p : rt->f2_tw)
         if (p) cudaFree(p);
     for (auto* p : rt->f1_tw)

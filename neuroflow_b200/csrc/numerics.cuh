@@ -185,15 +185,48 @@ __device__ __forceinline__ float e4m3_decode_ref(uint32_t b) {
     return __uint_as_float((sign << 31) | ((ex + 120u) << 23) | (mt << 20));
 }
 
+// e4m3_encode_ref for v in [-448, 448] or NaN (what e4m3_code passes on), by the
+// hardware conversion.  cvt.rn.satfinite.e4m3x2.f32 rounds half-even to 3 mantissa
+// bits like the reference; the two differ only where the reference's subnormal rule
+// keeps |v| in [7.5, 8) * 2^-9 at code 7 (the conversion gives the smallest normal,
+// code 8) and on NaN (the reference gives 0x7F for either sign); both are patched.
+// nfx_fp8_e4m3_selfcheck compares the two over every fp32 bit pattern.
+__device__ __forceinline__ uint32_t e4m3_encode_fast(float v) {
+#ifdef __CUDA_ARCH__
+    unsigned short r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(v));
+    uint32_t c = r & 0xFFu;
+    c = ((c & 0x7Fu) == 8u && fabsf(v) < 0.015625f) ? c - 1u : c;
+    return v != v ? 0x7Fu : c;
+#else
+    return e4m3_encode_ref(v);
+#endif
+}
+
+// e4m3_decode_ref by the hardware conversion (E4M3 -> f16 is exact, f16 -> f32 too);
+// the NaN codes get the reference's bit pattern.
+__device__ __forceinline__ float e4m3_decode_fast(uint32_t b) {
+#ifdef __CUDA_ARCH__
+    uint32_t h2;
+    const unsigned short in = static_cast<unsigned short>(b & 0xFFu);
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(in));
+    float f;
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tcvt.f32.f16 %0, lo;\n\t}" : "=f"(f) : "r"(h2));
+    return (b & 0x7Fu) == 0x7Fu ? __uint_as_float(0x7FC00000u | ((b & 0x80u) << 24)) : f;
+#else
+    return e4m3_decode_ref(b);
+#endif
+}
+
 // fp8_e4m3.h:312-334: the E4M3 code of v under `inv` = 1/scale (scale 0 -> 1).
 __device__ __forceinline__ uint32_t e4m3_code(float v, float inv) {
     float xs = __fmul_rn(v, inv);
     xs = xs > 448.0f ? 448.0f : (xs < -448.0f ? -448.0f : xs);
-    return e4m3_encode_ref(xs);
+    return e4m3_encode_fast(xs);
 }
 // ... and the fake-quantised value
 __device__ __forceinline__ float fp8_fake_quant(float v, float scale, float inv) {
-    return __fmul_rn(e4m3_decode_ref(e4m3_code(v, inv)), scale);
+    return __fmul_rn(e4m3_decode_fast(e4m3_code(v, inv)), scale);
 }
 
 // fno.cpp:810-844 apply_fake_quant for one element: FP8 first, else INT8 per-tensor.

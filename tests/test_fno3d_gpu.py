@@ -111,6 +111,22 @@ def test_fno3d_fp8_configs3_grid():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("shape,modes", [((2, 8, 16, 16), (3, 5, 9)),    # kept D Nyquist mode
+                                         ((1, 8, 16, 32), (4, 3, 6)),
+                                         ((3, 16, 8, 16), (5, 8, 2))])
+def test_fno3d_fp8_direct_dft_geometries(tmp_path, shape, modes):
+    """FP8 at width 32 runs the D and W passes as direct truncated DFTs: non-cubic grids,
+    odd mode counts (padded table columns), the D-axis Nyquist mode kept (Dp / 2 + 1
+    modes), and plane counts that leave the last CTA pass partly empty."""
+    m, p = _model(tmp_path, "gelu", width=32, modes=modes, L=2, S=16)
+    x = np.random.default_rng(5).standard_normal(shape + (4,)).astype(np.float32)
+    want = Oracle().fno3d_forward(m, x, fp8=True)
+    got = _run(p, x, 1, fp8=True)
+    print("direct dft rel", _rel(got, want))
+    assert _rel(got, want) < 1e-3
+
+
+@pytest.mark.gpu
 def test_fno3d_errors(tmp_path):
     from neuroflow_b200.runtime import InferenceRuntime
     _, p = _model(tmp_path, width=8, modes=(2, 2, 2), L=1, S=8)

@@ -110,3 +110,16 @@ def test_fp8_helpers_known_answers_and_oracle_sweep():
         xs = np.clip(x * inv, -448.0, 448.0).astype(np.float32)
         want = (want_dec[o.fp32_to_e4m3(xs)] * scale).astype(np.float32)
         assert np.array_equal(neuroflow_cpp.fp8_e4m3_fake_quant(x, float(scale)), want)
+
+
+@pytest.mark.gpu
+def test_fp8_hardware_conversions_match_the_reference_encoder():
+    """The FP8 executors encode and decode with the hardware E4M3 conversions, patched to
+    the reference's subnormal rule ([7.5, 8) * 2^-9 stays at code 7) and NaN codes: every
+    fp32 bit pattern (clamped to +-448 as the executors clamp) and every code agree bit
+    for bit with the reference's encoder and decoder (fp8_e4m3.h:106-284)."""
+    import ctypes
+    from neuroflow_b200 import _nfx
+    n = ctypes.c_ulonglong(12345)
+    assert _nfx.lib.nfx_fp8_e4m3_selfcheck(ctypes.byref(n)) == 0
+    assert n.value == 0
