@@ -61,16 +61,80 @@ __global__ void __launch_bounds__(256) lift3d_kernel(Fno3dPlan p) {
         const int dd = pt & (p.Dp - 1), ww = (pt >> lgD) & (p.Wp - 1), hh = pt >> (lgD + lgW);
         const bool inside = hh < p.H && ww < p.W && dd < p.D;
         const float* xr = p.x + (((b * p.H + hh) * p.W + ww) * p.D + dd) * p.in_ch;
+        // the first 8 input features in registers, the rest (wider inputs) from L1
+        constexpr int kReg = 8;
+        const int nreg = p.in_ch < kReg ? p.in_ch : kReg;
+        float xv[kReg];
+#pragma unroll
+        for (int k = 0; k < kReg; ++k) xv[k] = (inside && k < nreg) ? __ldg(xr + k) : 0.0f;
+        uint8_t* h8 = static_cast<uint8_t*>(p.h[0]) + (b * p.C << lgP) + pt;
+        float* h32 = static_cast<float*>(p.h[0]) + (b * p.C << lgP) + pt;
         for (int c = 0; c < p.C; ++c) {
             float v = 0.0f;
             if (inside) {
+                const float* wc = p.lift_w + c * p.in_ch;
                 v = __ldg(p.lift_b + c);
-                for (int k = 0; k < p.in_ch; ++k)
-                    v = linear_step(v, __ldg(xr + k), __ldg(p.lift_w + c * p.in_ch + k), k >= nu);
+#pragma unroll
+                for (int k = 0; k < kReg; ++k)
+                    if (k < nreg) v = linear_step(v, xv[k], __ldg(wc + k), k >= nu);
+                for (int k = kReg; k < p.in_ch; ++k) v = linear_step(v, __ldg(xr + k), __ldg(wc + k), k >= nu);
             }
-            const int64_t o = ((b * p.C + c) << lgP) + pt;
-            if (p.fp8) static_cast<uint8_t*>(p.h[0])[o] = static_cast<uint8_t>(e4m3_code(v, inv));
-            else static_cast<float*>(p.h[0])[o] = v;
+            if (p.fp8) h8[static_cast<int64_t>(c) << lgP] = static_cast<uint8_t>(e4m3_code(v, inv));
+            else h32[static_cast<int64_t>(c) << lgP] = v;
+        }
+    }
+}
+
+// Four consecutive padded points of one D row per thread (Dp a multiple of 4, at most
+// 8 input features): each weight is read once per four points, and a channel's four
+// outputs leave in one 32-bit (E4M3 codes) or 128-bit (fp32) store.
+__global__ void __launch_bounds__(256) lift3d_x4_kernel(Fno3dPlan p) {
+    const int lgD = 31 - __clz(p.Dp), lgW = 31 - __clz(p.Wp);
+    const int lgP = lgD + lgW + (31 - __clz(p.Hp));
+    const int64_t total = static_cast<int64_t>(p.B) << (lgP - 2);
+    const int nk = p.in_ch;
+    const int nu = linear_unfused_len(nk);
+    const float inv = inv_of(p.s_lift);
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b = t >> (lgP - 2);
+        const int pt = static_cast<int>(t - (b << (lgP - 2))) << 2;
+        const int dd = pt & (p.Dp - 1), ww = (pt >> lgD) & (p.Wp - 1), hh = pt >> (lgD + lgW);
+        const bool row_in = hh < p.H && ww < p.W;
+        bool in[4];
+        float xv[4][8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            in[i] = row_in && dd + i < p.D;
+            const float* xr = p.x + ((((b * p.H + hh) * p.W + ww) * p.D) + (in[i] ? dd + i : 0)) * nk;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) xv[i][k] = (in[i] && k < nk) ? __ldg(xr + k) : 0.0f;
+        }
+        uint8_t* h8 = static_cast<uint8_t*>(p.h[0]) + (b * p.C << lgP) + pt;
+        float* h32 = static_cast<float*>(p.h[0]) + (b * p.C << lgP) + pt;
+        for (int c = 0; c < p.C; ++c) {
+            const float* wc = p.lift_w + c * nk;
+            const float bc = __ldg(p.lift_b + c);
+            float wk[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) wk[k] = k < nk ? __ldg(wc + k) : 0.0f;
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[i] = 0.0f;
+                if (in[i]) {
+                    v[i] = bc;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (k < nk) v[i] = linear_step(v[i], xv[i][k], wk[k], k >= nu);
+                }
+            }
+            if (p.fp8)
+                *reinterpret_cast<uint32_t*>(h8 + (static_cast<int64_t>(c) << lgP)) =
+                    e4m3_code(v[0], inv) | (e4m3_code(v[1], inv) << 8) | (e4m3_code(v[2], inv) << 16) |
+                    (e4m3_code(v[3], inv) << 24);
+            else
+                *reinterpret_cast<float4*>(h32 + (static_cast<int64_t>(c) << lgP)) = make_float4(v[0], v[1], v[2], v[3]);
         }
     }
 }
@@ -259,6 +323,63 @@ size_t dft_inv_smem(const DftDims& g, int Wp, int Dp, int MW) {
                                                           static_cast<size_t>(Wp) * g.UJ));
 }
 
+// W pass of the direct forward DFT for the NP planes q0 .. q0 + NP - 1 held in sY
+// ([NP][Wp][ys] floats, (re, im) per kd): A[q][kw][kd] = s_in * sum_w Y[w][kd] e^{-2 pi i
+// kw w / Wp}, 2 x 2 output modes per thread, w split over 8 consecutive lanes and
+// summed by shuffles.  Every thread of the CTA takes part (the shuffles are warp-wide).
+__device__ __forceinline__ void dft_w_pass(const Fno3dPlan& p, int MD4, int MW2, const float* sY, int ys,
+                                           const float* tW, int tws, int NP, int64_t q0, int64_t nplanes,
+                                           float s_in) {
+    const int T = blockDim.x, tid = threadIdx.x, Wp = p.Wp;
+    const int items2 = (MW2 / 2) * (MD4 / 2) * 8;
+    for (int base = 0; base < NP * items2; base += T) {
+        const int it = base + tid;
+        const bool live = it < NP * items2;
+        const int pl = live ? it / items2 : 0, r = it - pl * items2;
+        const int s = r & 7, blk = r >> 3;
+        const int kwp = blk / (MD4 / 2), kdp = blk - kwp * (MD4 / 2);
+        float o[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = 0.0f;
+        if (live) {
+            for (int w = s; w < Wp; w += 8) {
+                const float4 y = *reinterpret_cast<const float4*>(sY + (pl * Wp + w) * ys + 4 * kdp);
+                const float4 t = *reinterpret_cast<const float4*>(tW + w * tws + 4 * kwp);
+                const float yr[2] = {y.x, y.z}, yi[2] = {y.y, y.w};
+                const float tc[2] = {t.x, t.z}, ts[2] = {t.y, t.w};
+#pragma unroll
+                for (int a = 0; a < 2; ++a)
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {  // kw = 2 kwp + a, kd = 2 kdp + c
+                        float& re = o[4 * a + 2 * c];
+                        float& im = o[4 * a + 2 * c + 1];
+                        re = __fmaf_rn(yr[c], tc[a], re);
+                        re = __fmaf_rn(-yi[c], ts[a], re);
+                        im = __fmaf_rn(yr[c], ts[a], im);
+                        im = __fmaf_rn(yi[c], tc[a], im);
+                    }
+            }
+        }
+#pragma unroll
+        for (int m = 1; m < 8; m <<= 1)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) o[k] = __fadd_rn(o[k], __shfl_xor_sync(0xffffffffu, o[k], m));
+        const int64_t q = q0 + pl;
+        if (live && s == 0 && q < nplanes) {
+            float2* A = p.A + q * p.MW * p.MD;
+#pragma unroll
+            for (int a = 0; a < 2; ++a)
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const int kw = 2 * kwp + a, kd = 2 * kdp + c;
+                    if (kw < p.MW && kd < p.MD)
+                        A[kw * p.MD + kd] =
+                            make_float2(__fmul_rn(o[4 * a + 2 * c], s_in), __fmul_rn(o[4 * a + 2 * c + 1], s_in));
+                }
+        }
+    }
+}
+
 // Persistent over the B * C * Hp (b, c, h) planes, NPf planes per pass.
 // smem floats: tD [Dp][MD4] float2 | tW [Wp][TWS] | x [NPf][Wp][XS] | Y [NPf][Wp][YS]
 __global__ void __launch_bounds__(kDftThreads) fwd3d_dft_kernel(Fno3dPlan p, DftDims g,
@@ -295,7 +416,6 @@ __global__ void __launch_bounds__(kDftThreads) fwd3d_dft_kernel(Fno3dPlan p, Dft
     int64_t pass = blockIdx.x;
     if (pass < npass) fetch(pass);
     const int items1 = half * (MD4 / 4);
-    const int items2 = (g.MW2 / 2) * (MD4 / 2) * 8;
     for (; pass < npass; pass += gridDim.x) {
         __syncthreads();  // the previous pass is done with x and Y
 #pragma unroll
@@ -350,53 +470,196 @@ __global__ void __launch_bounds__(kDftThreads) fwd3d_dft_kernel(Fno3dPlan p, Dft
             *reinterpret_cast<float4*>(y1 + 4) = make_float4(a1[4], a1[5], a1[6], a1[7]);
         }
         __syncthreads();
-        // W pass: 2 x 2 output modes per thread, w split over 8 consecutive lanes
-        for (int base = 0; base < NP * items2; base += T) {
-            const int it = base + tid;
-            const bool live = it < NP * items2;
-            const int pl = live ? it / items2 : 0, r = it - pl * items2;
-            const int s = r & 7, blk = r >> 3;
-            const int kwp = blk / (MD4 / 2), kdp = blk - kwp * (MD4 / 2);
-            float o[8];
+        dft_w_pass(p, MD4, g.MW2, sY, g.YS, tW, g.TWS, NP, pass * NP, nplanes, s_in);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// fwd3d_tc: the direct forward DFT with its D pass on tensor cores (fno3d_direct_dft
+// geometries with Wp dividing 128, Dp = 64 or 128 and at most 16 kept kd modes).  A
+// tile is 128 D rows (128 / Wp planes).  E4M3 values are exact in f16
+// (cvt.rn.f16x2.e4m3x2 converts two codes per instruction), so the D pass
+//   Y[row][n] = sum_d x[row][d] T[n][d],   T[2 kd] = cos(2 pi kd d / Dp), T[2 kd + 1] = -sin
+// is one kind::f16 MMA chain (M = 128, N = 16 or 32, K = Dp, fp32 accumulation) with T
+// split into two f16 terms, hi = f16(T) and lo = f16(T - hi), whose sum holds T to
+// about 2^-22 relative (each product exact in fp32).  The W pass runs on CUDA cores
+// from shared memory (dft_w_pass).  128 threads: all convert the tile's codes into
+// the 128-byte-swizzled K-major A tile, thread 0 issues the MMAs, warp q reads TMEM
+// lanes 32 q .. 32 q + 31 (its rows of Y).
+// ---------------------------------------------------------------------------
+struct FtcDims {
+    int N;       // MMA N: 16 or 32 (2 MD4 rounded up)
+    int YS;      // sY row stride (floats)
+    int NPt;     // planes per tile (128 / Wp)
+    int offB, offY, offW, offBar, smem;  // byte offsets in the 1024-aligned dynamic smem, its size
+};
+
+bool fwd_tc_ok(int Wp, int Dp, int MD) {
+    return Wp <= 128 && 128 % Wp == 0 && (Dp == 64 || Dp == 128) && MD <= 16;
+}
+
+FtcDims ftc_dims(const DftDims& g, int Wp, int Dp) {
+    FtcDims f;
+    f.N = 2 * g.MD4 <= 16 ? 16 : 32;
+    f.YS = f.N + 4;
+    f.NPt = 128 / Wp;
+    f.offB = Dp * 256;                             // A: 128 rows x Dp f16
+    f.offY = f.offB + 2 * (Dp / 64) * f.N * 128;   // B: two f16 terms of T
+    f.offW = f.offY + 128 * f.YS * 4;
+    f.offBar = (f.offW + Wp * g.TWS * 4 + 15) & ~15;
+    f.smem = f.offBar + 16 + 1024;                 // barrier, TMEM slot, abort flag; alignment slack
+    return f;
+}
+
+// two E4M3 codes (low and high byte of v) -> f16x2 (low half from the low byte); exact
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v) {
+    uint32_t r;
+    const unsigned short in = static_cast<unsigned short>(v & 0xFFFFu);
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(in));
+    return r;
+}
+
+__device__ __forceinline__ unsigned short f16_bits_rn(float x) {
+    unsigned short r;
+    asm("cvt.rn.f16.f32 %0, %1;" : "=h"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(unsigned short h) {
+    float r;
+    asm("cvt.f32.f16 %0, %1;" : "=f"(r) : "h"(h));
+    return r;
+}
+
+__global__ void __launch_bounds__(128) fwd3d_tc_kernel(Fno3dPlan p, DftDims g, FtcDims f,
+                                                       const uint8_t* __restrict__ hin, float s_in,
+                                                       unsigned* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + f.offB;
+    float* sY = reinterpret_cast<float*>(smem + f.offY);
+    float* tW = reinterpret_cast<float*>(smem + f.offW);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + f.offBar);
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(bar + 1);
+    volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int Wp = p.Wp, Dp = p.Dp, MD4 = g.MD4, N = f.N;
+    const int nkc = Dp / 64;  // 128-byte K chunks (64 f16) of a row
+
+    {
+        // T as two f16 terms, K-major 128-byte swizzled: term t, chunk kc, row n
+        for (int i = tid; i < N * Dp; i += 128) {
+            const int n = i / Dp, d = i - n * Dp;
+            const float v = n / 2 < MD4 ? __ldg(p.dft + (d * MD4 + n / 2) * 2 + (n & 1)) : 0.0f;
+            const unsigned short hi = f16_bits_rn(v);
+            const unsigned short lo = f16_bits_rn(__fsub_rn(v, f16_bits_to_f32(hi)));
+            const uint32_t o = swz_offset(static_cast<uint32_t>(n * 128 + (d & 63) * 2), 128);
+            const int kc = d >> 6;
+            *reinterpret_cast<unsigned short*>(sB + (0 * nkc + kc) * N * 128 + o) = hi;
+            *reinterpret_cast<unsigned short*>(sB + (1 * nkc + kc) * N * 128 + o) = lo;
+        }
+        const float* gW = p.dft + 2 * Dp * MD4;
+        const int rw = 2 * g.MW2;
+        for (int i = tid; i < Wp * rw; i += 128) tW[(i / rw) * g.TWS + i % rw] = __ldg(gW + i);
+        if (tid == 0) {
+            mbar_init(bar, 1);
+            *sAbort = 0;
+            fence_mbar_init();
+        }
+        if (warp == 0) tmem_alloc(sTmem, 32);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    const uint32_t tmem = *sTmem;
+    const int64_t nplanes = static_cast<int64_t>(p.B) * p.C * p.Hp;
+    const int64_t ntiles = nplanes / f.NPt;  // B C Hp Wp rows, a multiple of 128
+    const int rv = Dp / 16;                  // uint4 of codes per row = per thread per tile
+    constexpr int kMaxPre = 8;
+    uint4 pre[kMaxPre];
+    auto fetch = [&](int64_t tile) {
+        const uint4* src = reinterpret_cast<const uint4*>(hin) + tile * 128 * rv;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) o[k] = 0.0f;
-            if (live) {
-                for (int w = s; w < Wp; w += 8) {
-                    const float4 y = *reinterpret_cast<const float4*>(sY + (pl * Wp + w) * g.YS + 4 * kdp);
-                    const float4 t = *reinterpret_cast<const float4*>(tW + w * g.TWS + 4 * kwp);
-                    const float yr[2] = {y.x, y.z}, yi[2] = {y.y, y.w};
-                    const float tc[2] = {t.x, t.z}, ts[2] = {t.y, t.w};
+        for (int r = 0; r < kMaxPre; ++r)
+            if (r < rv) pre[r] = __ldg(src + tid + r * 128);
+    };
+    const uint32_t idesc = N == 16 ? idesc_f16(16) : idesc_f16(32);
+    int64_t tile = blockIdx.x;
+    if (tile < ntiles) fetch(tile);
+    uint32_t phase = 0;
+    for (; tile < ntiles; tile += gridDim.x) {
+        // uint4 i of the tile: codes 16 (i % rv) .. + 15 of row i / rv -> two 16-byte f16 chunks
 #pragma unroll
-                    for (int a = 0; a < 2; ++a)
-#pragma unroll
-                        for (int c = 0; c < 2; ++c) {  // kw = 2 kwp + a, kd = 2 kdp + c
-                            float& re = o[4 * a + 2 * c];
-                            float& im = o[4 * a + 2 * c + 1];
-                            re = __fmaf_rn(yr[c], tc[a], re);
-                            re = __fmaf_rn(-yi[c], ts[a], re);
-                            im = __fmaf_rn(yr[c], ts[a], im);
-                            im = __fmaf_rn(yi[c], tc[a], im);
-                        }
-                }
-            }
-#pragma unroll
-            for (int m = 1; m < 8; m <<= 1)
-#pragma unroll
-                for (int k = 0; k < 8; ++k) o[k] = __fadd_rn(o[k], __shfl_xor_sync(0xffffffffu, o[k], m));
-            const int64_t q = pass * NP + pl;
-            if (live && s == 0 && q < nplanes) {
-                float2* A = p.A + q * p.MW * p.MD;
-#pragma unroll
-                for (int a = 0; a < 2; ++a)
-#pragma unroll
-                    for (int c = 0; c < 2; ++c) {
-                        const int kw = 2 * kwp + a, kd = 2 * kdp + c;
-                        if (kw < p.MW && kd < p.MD)
-                            A[kw * p.MD + kd] =
-                                make_float2(__fmul_rn(o[4 * a + 2 * c], s_in), __fmul_rn(o[4 * a + 2 * c + 1], s_in));
-                    }
+        for (int r = 0; r < kMaxPre; ++r) {
+            if (r < rv) {
+                const int i = tid + r * 128;
+                const int row = i / rv, k0 = (i - row * rv) * 16;
+                uint8_t* chunk = sA + (k0 >> 6) * (128 * 128);
+                const uint32_t o0 = swz_offset(static_cast<uint32_t>(row * 128 + (k0 & 63) * 2), 128);
+                const uint32_t o1 = swz_offset(static_cast<uint32_t>(row * 128 + (k0 & 63) * 2 + 16), 128);
+                *reinterpret_cast<uint4*>(chunk + o0) =
+                    make_uint4(e4m3x2_to_f16x2(pre[r].x), e4m3x2_to_f16x2(pre[r].x >> 16),
+                               e4m3x2_to_f16x2(pre[r].y), e4m3x2_to_f16x2(pre[r].y >> 16));
+                *reinterpret_cast<uint4*>(chunk + o1) =
+                    make_uint4(e4m3x2_to_f16x2(pre[r].z), e4m3x2_to_f16x2(pre[r].z >> 16),
+                               e4m3x2_to_f16x2(pre[r].w), e4m3x2_to_f16x2(pre[r].w >> 16));
             }
         }
+        if (tile + gridDim.x < ntiles) fetch(tile + gridDim.x);
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            for (int t = 0; t < 2; ++t)
+                for (int kc = 0; kc < nkc; ++kc)
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f16(tmem, umma_desc(smem_u32(sA) + kc * 16384 + ks * 32, 128),
+                                umma_desc(smem_u32(sB) + (t * nkc + kc) * N * 128 + ks * 32, 128), idesc,
+                                (t | kc | ks) != 0 ? 1u : 0u);
+            mma_commit(bar);
+        }
+        const bool ok = mbar_wait(bar, phase, sAbort);
+        phase ^= 1u;
+        if (!ok) {
+            *sAbort = 1;
+            atomicOr(err, kErrWaitAccFull);
+        } else {
+            tc_fence_after();
+            const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+            float* yrow = sY + (warp * 32 + lane) * f.YS;
+            if (N == 16) {
+                uint32_t v[16];
+                tmem_ld16(taddr, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                    *reinterpret_cast<uint4*>(yrow + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+                uint32_t v[32];
+                tmem_ld32(taddr, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<uint4*>(yrow + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (*sAbort) break;
+        dft_w_pass(p, MD4, g.MW2, sY, f.YS, tW, g.TWS, f.NPt, tile * f.NPt, nplanes, s_in);
+    }
+    tc_fence_before();
+    __syncthreads();
+    // an MMA chain whose completion wait gave up may still be running: let it finish
+    // before its TMEM is released
+    if (*sAbort && tid == 0 && !mbar_wait_drain(bar, phase ^ 1u)) atomicOr(err, kErrWaitDrain);
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 32);
     }
 }
 
@@ -468,23 +731,22 @@ __global__ void __launch_bounds__(kDftThreads) inv3d_dft_kernel(Fno3dPlan p, Dft
             const int pl = it / items2, r = it - pl * items2;
             const int dq = r % (Dp / 4), rg = r / (Dp / 4);
             const float* ur = su + (pl * Wp + rg * 8) * g.UJ;
-            float acc[8][4];
+            // acc[i][h] holds points 4 dq + 2 h, + 1 of row i (f32x2 lanes, each the
+            // scalar fmaf chain)
+            float2 acc[8][2];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-#pragma unroll
-                for (int m = 0; m < 4; ++m) acc[i][m] = 0.0f;
+            for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = make_float2(0.0f, 0.0f);
             for (int j = 0; j < MD; ++j) {
                 const float4 c4 = *reinterpret_cast<const float4*>(iCS + j * Dp + 4 * dq);
                 const float4 s4 = *reinterpret_cast<const float4*>(iS + j * Dp + 4 * dq);
-                const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+                const float2 c01 = make_float2(c4.x, c4.y), c23 = make_float2(c4.z, c4.w);
+                const float2 s01 = make_float2(s4.x, s4.y), s23 = make_float2(s4.z, s4.w);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const float2 u = *reinterpret_cast<const float2*>(ur + i * g.UJ + 2 * j);
-#pragma unroll
-                    for (int m = 0; m < 4; ++m) {
-                        acc[i][m] = __fmaf_rn(u.x, cc[m], acc[i][m]);
-                        acc[i][m] = __fmaf_rn(u.y, ss[m], acc[i][m]);
-                    }
+                    const float2 ux = make_float2(u.x, u.x), uy = make_float2(u.y, u.y);
+                    acc[i][0] = fma2_rn(uy, s01, fma2_rn(ux, c01, acc[i][0]));
+                    acc[i][1] = fma2_rn(uy, s23, fma2_rn(ux, c23, acc[i][1]));
                 }
             }
             const int64_t q = q0 + pl;
@@ -493,7 +755,7 @@ __global__ void __launch_bounds__(kDftThreads) inv3d_dft_kernel(Fno3dPlan p, Dft
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
                     *reinterpret_cast<float4*>(x1 + static_cast<int64_t>(i) * Dp) =
-                        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+                        make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
             }
         }
     }
@@ -587,14 +849,19 @@ struct L3Cfg {
     static constexpr int kOffA = 0;
     static constexpr int kOffW = kOffA + kStages * kABytes;
     static constexpr int kOffBias = kOffW + ((C * C + 1023) / 1024) * 1024;
-    static constexpr int kOffBars = kOffBias + C * 4;
+    static constexpr int kOffPo = kOffBias + C * 4;         // projection: proj_out (16 x C) + bias
+    static constexpr int kOffBars = kOffPo + (16 * C + 16) * 4;
     static constexpr int kNumBars = 2 * kStages + 2 * kAccStages;
     static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
 };
 
-template <int C>
+// PROJ: the same tiles and MMA for the projection (proj3d_kernel's FP8 arithmetic):
+// weights proj_q, per point q_c = fake-quant(D_c s + b_c), the activation, then
+// proj_out summed over c in order (Linear rounding) and fake-quantised into y at the
+// unpadded points.  `s_in` is the scale of the input codes.
+template <int C, bool PROJ>
 __global__ void __launch_bounds__(L3Cfg<C>::kThreads, 1)
-local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, const Fno3dLayer L,
+local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, const Fno3dLayer L, float s_in,
                   uint8_t* __restrict__ hout, unsigned* err) {
     using F = L3Cfg<C>;
     static_assert(C == 32 || C == 64, "K = C must be a multiple of 32");
@@ -622,9 +889,14 @@ local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, c
         // weights: E4M3 codes of the decoded weights, K-major rows of C bytes, swizzled
         for (int i = threadIdx.x; i < C * C; i += F::kThreads) {
             const int o = i / C, k = i % C;
-            sW[swz_offset(o * C + k, C)] = static_cast<uint8_t>(e4m3_encode_ref(L.loc_q[i]));
+            sW[swz_offset(o * C + k, C)] = static_cast<uint8_t>(e4m3_encode_ref(PROJ ? p.pq_q[i] : L.loc_q[i]));
         }
-        for (int o = threadIdx.x; o < C; o += F::kThreads) sBias[o] = L.loc_b[o];
+        for (int o = threadIdx.x; o < C; o += F::kThreads) sBias[o] = PROJ ? p.pq_b[o] : L.loc_b[o];
+        if constexpr (PROJ) {
+            float* sPo = reinterpret_cast<float*>(smem + F::kOffPo);
+            for (int i = threadIdx.x; i < p.out_ch * C; i += F::kThreads) sPo[i] = p.po_w[i];
+            for (int i = threadIdx.x; i < p.out_ch; i += F::kThreads) sPo[16 * C + i] = p.po_b[i];
+        }
         if (threadIdx.x == 0) {
             for (int s = 0; s < F::kStages; ++s) {
                 mbar_init(&full[s], 1);
@@ -705,8 +977,9 @@ local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, c
         const int ew = warp - 2;
         const int quad = warp & 3;
         const int grp = ew >> 2;
-        const float sc = __fmul_rn(L.s_in, L.s_w);
-        const float inv_out = inv_of(L.s_out);
+        const float sc = __fmul_rn(s_in, PROJ ? p.s_pq_w : L.s_w);
+        const float s_out = PROJ ? p.s_pq : L.s_out;
+        const float inv_out = inv_of(s_out);
         for (int it = grp; t_begin + it < t_end; it += F::kGroups) {
             const int tile = t_begin + it;
             const uint32_t aph = (it / F::kAccStages) & 1;
@@ -720,6 +993,56 @@ local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, c
             const int64_t pt = static_cast<int64_t>(tile - b * tiles_per_sample) * 128 + quad * 32 + lane;
             const int64_t base = static_cast<int64_t>(b) * C * Pp + pt;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + grp * C;
+            if constexpr (PROJ) {
+                const float* sPo = reinterpret_cast<const float*>(smem + F::kOffPo);
+                constexpr int nu = linear_unfused_len(C);
+                float yo[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) yo[j] = j < p.out_ch ? sPo[16 * C + j] : 0.0f;
+#pragma unroll 1
+                for (int h = 0; h < C / 32; ++h) {
+                    uint32_t acc[32];
+                    tmem_ld32(tbase + 32 * h, acc);
+                    tmem_wait_ld();
+                    if (h == C / 32 - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&accEmpty[grp]);
+                    }
+                    if (p.out_ch == 1) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int c = 32 * h + j;
+                            const float q = fp8_fake_quant(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[c]),
+                                                           s_out, inv_out);
+                            yo[0] = linear_step(yo[0], act_f(q, p.act), sPo[c], c >= nu);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int c = 32 * h + j;
+                            const float q = fp8_fake_quant(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[c]),
+                                                           s_out, inv_out);
+                            const float g = act_f(q, p.act);
+#pragma unroll
+                            for (int o = 0; o < 16; ++o)
+                                if (o < p.out_ch) yo[o] = linear_step(yo[o], g, sPo[o * C + c], c >= nu);
+                        }
+                    }
+                }
+                // the padded grid's points outside the input grid carry no output
+                const int lgD = 31 - __clz(p.Dp), lgW = 31 - __clz(p.Wp);
+                const int ip = static_cast<int>(pt);
+                const int dd = ip & (p.Dp - 1), ww = (ip >> lgD) & (p.Wp - 1), hh = ip >> (lgD + lgW);
+                if (hh < p.H && ww < p.W && dd < p.D) {
+                    const float inv_po = inv_of(p.s_po);
+                    float* yr = p.y + (((static_cast<int64_t>(b) * p.H + hh) * p.W + ww) * p.D + dd) * p.out_ch;
+#pragma unroll
+                    for (int o = 0; o < 16; ++o)
+                        if (o < p.out_ch) yr[o] = fp8_fake_quant(yo[o], p.s_po, inv_po);
+                }
+                continue;
+            }
 #pragma unroll 1
             for (int h = 0; h < C / 32; ++h) {
                 uint32_t acc[32];
@@ -738,7 +1061,7 @@ local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, c
                 for (int j = 0; j < 32; ++j) {
                     const int o = 32 * h + j;
                     const float x2 = fp8_fake_quant(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[o]),
-                                                    L.s_out, inv_out);
+                                                    s_out, inv_out);
                     const float z = act_f(__fadd_rn(x1v[j], x2), p.act);
                     hout[base + static_cast<int64_t>(o) * Pp] = static_cast<uint8_t>(e4m3_code(z, inv_out));
                 }
@@ -832,9 +1155,12 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
         if (p.timer) p.timer->end(st);
         return cudaGetLastError();
     };
-    const int64_t tl = static_cast<int64_t>(p.B) * Pp;
+    const bool lift4 = p.Dp % 4 == 0 && p.in_ch <= 8;
+    const int64_t tl = static_cast<int64_t>(p.B) * Pp / (lift4 ? 4 : 1);
     if ((e = timed("fno3d_lift", [&] {
-             lift3d_kernel<<<static_cast<int>(std::min<int64_t>((tl + 255) / 256, sms * 16)), 256, 0, st>>>(p);
+             const int grid = static_cast<int>(std::min<int64_t>((tl + 255) / 256, sms * 16));
+             if (lift4) lift3d_x4_kernel<<<grid, 256, 0, st>>>(p);
+             else lift3d_kernel<<<grid, 256, 0, st>>>(p);
          })) != cudaSuccess)
         return e;
     const int KK = p.MW * p.MD, M = p.MH * KK, G = mix_group(p.C, p.B, sms);
@@ -852,6 +1178,10 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
     const DftDims g = dft_dims(p.Wp, p.Dp, p.MW, p.MD);
     const size_t sdf = dft_fwd_smem(g, p.Wp, p.Dp), sdi = dft_inv_smem(g, p.Wp, p.Dp, p.MW);
     int gdf = 0, gdi = 0;
+    const bool ftc = direct && fwd_tc_ok(p.Wp, p.Dp, p.MD);
+    const FtcDims fd = ftc_dims(g, p.Wp, p.Dp);
+    unsigned* err = device_error_word();
+    if (ftc && !err) return cudaErrorMemoryAllocation;
     if (direct) {
         if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(fwd3d_dft_kernel), static_cast<int>(sdf))) !=
                 cudaSuccess ||
@@ -866,6 +1196,13 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
             return e;
         const int64_t planes = static_cast<int64_t>(p.B) * p.C * p.Hp;
         gdf = static_cast<int>(std::min<int64_t>((planes + g.NPf - 1) / g.NPf, static_cast<int64_t>(sms) * std::max(1, of)));
+        if (ftc) {
+            if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(fwd3d_tc_kernel), fd.smem)) != cudaSuccess)
+                return e;
+            // CTAs per SM from the shared memory (227 KB per SM; TMEM: 32 columns each)
+            const int per_sm = std::max(1, std::min(8, (227 * 1024) / (fd.smem + 1024)));
+            gdf = static_cast<int>(std::min<int64_t>(planes / fd.NPt, static_cast<int64_t>(sms) * per_sm));
+        }
         gdi = static_cast<int>(std::min<int64_t>((planes + g.NPi - 1) / g.NPi, static_cast<int64_t>(sms) * std::max(1, oi)));
     }
     const int64_t tp = static_cast<int64_t>(p.B) * Pp;
@@ -875,7 +1212,9 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
         const void* hin = p.h[i & 1];
         void* hout = p.h[(i + 1) & 1];
         if ((e = timed("fno3d_fwd", [&] {
-                 if (direct)
+                 if (ftc)
+                     fwd3d_tc_kernel<<<gdf, 128, fd.smem, st>>>(p, g, fd, static_cast<const uint8_t*>(hin), L.s_in, err);
+                 else if (direct)
                      fwd3d_dft_kernel<<<gdf, kDftThreads, sdf, st>>>(p, g, static_cast<const uint8_t*>(hin), L.s_in);
                  else
                      fwd3d_a_kernel<<<dim3(p.Hp, p.C, p.B), 256, sa, st>>>(p, hin, L.s_in);
@@ -897,18 +1236,18 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
             if (p.fp8 && Pp % 128 == 0) {
                 using F = L3Cfg<C>;
                 CUtensorMap tm;
-                unsigned* err = device_error_word();
                 if (!err) return cudaErrorMemoryAllocation;
                 if (!encode_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, hin, static_cast<uint64_t>(Pp),
                                static_cast<uint64_t>(p.B) * C, static_cast<uint64_t>(Pp), 64, C, 64))
                     return cudaErrorInvalidValue;
-                auto k = local3d_tc_kernel<C>;
+                auto k = local3d_tc_kernel<C, false>;
                 if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(k), F::kSmemBytes)) != cudaSuccess)
                     return e;
                 const int64_t tiles = static_cast<int64_t>(p.B) * (Pp / 128);
                 const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
                 if ((e = timed("fno3d_local", [&] {
-                         k<<<grid, F::kThreads, F::kSmemBytes, st>>>(tm, p, L, static_cast<uint8_t*>(hout), err);
+                         k<<<grid, F::kThreads, F::kSmemBytes, st>>>(tm, p, L, L.s_in, static_cast<uint8_t*>(hout),
+                                                                     err);
                      })) != cudaSuccess)
                     return e;
                 tc = true;
@@ -921,6 +1260,24 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
     }
     const int64_t tq = static_cast<int64_t>(p.B) * p.H * p.W * p.D;
     const float s_last = p.L > 0 ? p.layer[p.L - 1].s_out : p.s_lift;
+    if constexpr (C == 32 || C == 64) {
+        // FP8: the projection on tensor cores (the local layer's tiles and MMA)
+        if (p.fp8 && Pp % 128 == 0) {
+            using F = L3Cfg<C>;
+            CUtensorMap tm;
+            if (!err) return cudaErrorMemoryAllocation;
+            if (!encode_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.h[p.L & 1], static_cast<uint64_t>(Pp),
+                           static_cast<uint64_t>(p.B) * C, static_cast<uint64_t>(Pp), 64, C, 64))
+                return cudaErrorInvalidValue;
+            auto k = local3d_tc_kernel<C, true>;
+            if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(k), F::kSmemBytes)) != cudaSuccess) return e;
+            const int64_t tiles = static_cast<int64_t>(p.B) * (Pp / 128);
+            const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
+            return timed("fno3d_proj", [&] {
+                k<<<grid, F::kThreads, F::kSmemBytes, st>>>(tm, p, p.layer[0], s_last, nullptr, err);
+            });
+        }
+    }
     return timed("fno3d_proj", [&] {
         proj3d_kernel<C><<<static_cast<int>(std::min<int64_t>((tq + 127) / 128, sms * 16)), 128, 0, st>>>(
             p, p.h[p.L & 1], s_last);

@@ -101,7 +101,7 @@ __device__ __forceinline__ float fake_quant(float v, float s, float zp) {
 // and 0.5f*z*(1+t) as (0.5f*z)*(1+t).  tanhf is CUDA's (the reference uses glibc's;
 // the two differ by at most a couple of ulps, which the parity tolerance states).
 __device__ __forceinline__ float gelu_tanh(float z) {
-    const float c = __fsqrt_rn(__fdiv_rn(2.0f, 3.14159265358979323846f));
+    const float c = 0x1.988452p-1f;  // sqrtf(2.0f / (float)M_PI): both steps correctly rounded
     const float t = __fmul_rn(__fmul_rn(0.044715f, z), z);
     const float inner = __fmaf_rn(z, t, z);
     const float th = tanhf(__fmul_rn(c, inner));

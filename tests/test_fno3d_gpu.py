@@ -48,6 +48,7 @@ def _run(path, x, out_ch, fp8=False):
 
 
 GEOMS = [dict(width=8, modes=(3, 3, 2), L=2, S=8),
+         dict(width=8, modes=(2, 2, 2), L=1, S=8, in_ch=9),   # lift with > 8 input features
          dict(width=16, modes=(2, 4, 3), L=1, S=16, in_ch=5),
          dict(width=32, modes=(4, 4, 4), L=2, S=16)]
 
@@ -113,12 +114,17 @@ def test_fno3d_fp8_configs3_grid():
 @pytest.mark.gpu
 @pytest.mark.parametrize("shape,modes", [((2, 8, 16, 16), (3, 5, 9)),    # kept D Nyquist mode
                                          ((1, 8, 16, 32), (4, 3, 6)),
+                                         ((1, 8, 16, 64), (4, 3, 6)),    # D pass on tensor cores
+                                         ((1, 8, 8, 64), (3, 4, 16)),    # ... with N = 32
+                                         ((1, 4, 128, 128), (2, 3, 5)),  # ... Wp = Dp = 128
                                          ((3, 16, 8, 16), (5, 8, 2))])
 def test_fno3d_fp8_direct_dft_geometries(tmp_path, shape, modes):
-    """FP8 at width 32 runs the D and W passes as direct truncated DFTs: non-cubic grids,
-    odd mode counts (padded table columns), the D-axis Nyquist mode kept (Dp / 2 + 1
-    modes), and plane counts that leave the last CTA pass partly empty."""
-    m, p = _model(tmp_path, "gelu", width=32, modes=modes, L=2, S=16)
+    """FP8 at width 32 runs the D and W passes as direct truncated DFTs (the forward D
+    pass as an f16 MMA when Dp is 64 or 128): non-cubic grids, odd mode counts
+    (padded table columns), the D-axis Nyquist mode kept (Dp / 2 + 1 modes), and plane
+    counts that leave the last CTA pass partly empty."""
+    S = 16 if max(modes) <= 9 else 32     # the calibration grid holds the modes
+    m, p = _model(tmp_path, "gelu", width=32, modes=modes, L=2, S=S)
     x = np.random.default_rng(5).standard_normal(shape + (4,)).astype(np.float32)
     want = Oracle().fno3d_forward(m, x, fp8=True)
     got = _run(p, x, 1, fp8=True)
