@@ -181,7 +181,10 @@ int nfx_runtime_run_device_noalloc(nfx_runtime* rt, const float* x, const int64_
  * hold the last chunk only; use nfx_runtime_run_device for whole-batch taps.  No
  * counterpart in the reference runtime: it exposes, for layer-wise parity checks, the
  * activations between the iterations of FNO2d::Forward's layer loop
- * (cpp/src/fno.cpp:900-945) in their int8 form. */
+ * (cpp/src/fno.cpp:900-945) in their int8 form.  The FNO3d FP8 variant writes its E4M3
+ * activation codes the same way, as n_layers + 1 channel-first (batch, width, h, w, d)
+ * blocks on the padded grid (FNO3d::Forward's layer loop, cpp/src/fno.cpp:1182-1228);
+ * an FNO3d forward without FP8 fails with NFX_UNSUPPORTED_OP while taps are set. */
 int nfx_runtime_set_code_taps(nfx_runtime* rt, int8_t* device_buffer, int64_t capacity_bytes);
 
 /* Synchronise the runtime's work and report device-side errors (bounded waits that

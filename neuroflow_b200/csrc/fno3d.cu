@@ -1077,6 +1077,344 @@ local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, c
     }
 }
 
+// x = hi + lo with hi holding the upper tf32 bits (rounded half away in magnitude) and
+// lo the exact remainder, which a tf32 MMA reads to about 2^-11 of itself
+__device__ __forceinline__ void split_tf32_x3(float x, float& hi, float& lo) {
+    hi = __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+    lo = __fsub_rn(x, hi);
+}
+
+// ---------------------------------------------------------------------------
+// layer3d_tc: one whole FP8 layer after the spectral mix -- the W and D inverse
+// transforms fused into the tensor-core local layer (fno3d_fused_layer geometries:
+// widths 32 / 64, Dp = 64 or 128, at most 8 kept kw and kd modes), so the spectral
+// branch x1 never leaves the chip.  A 128-point tile is R = 128 / Dp rows w of one
+// (b, h) plane.  With
+//   U[o][r][2 kd]     =  f_kd Re s,  U[o][r][2 kd + 1] = -f_kd Im s,
+//   s = sum_kw colinv[b][o][h][kw][kd] e^{+2 pi i kw (w0 + r) / Wp},
+//   f_kd = (kd = 0 or 2 kd = Dp ? 1 : 2) / (Wp Dp),
+//   Binv[p][16 r' + 2 kd] = [r' = p / Dp] cos(2 pi kd d / Dp), ... + 1 = ... sin,
+// x1[p][o] = sum_k Binv[p][k] U[o][k] over K = 32 (16 per row slot, zeros for absent
+// rows and modes) is a kind::tf32 MMA, 3xTF32 (hi.hi + lo.hi + hi.lo, each operand
+// split into tf32 hi and the remainder lo).  It lands beside the local layer's
+// accumulator, and the epilogue reads both from TMEM.
+//   warp 0       TMA producer of the layer-input code tiles
+//   warp 1       MMA issuer: the E4M3 local GEMM and the x1 MMAs per tile
+//   warps 2..    T builders (4 threads per output channel, 2 kd modes each): U of each
+//                tile from the plane's colinv entries, held in registers while (b, h)
+//                stays the same; four U buffers
+//   then         epilogue: three groups of four warps (one per TMEM lane quadrant)
+//                take turns over the tiles; per element as local3d_tc with x1 from TMEM
+// ---------------------------------------------------------------------------
+template <int C>
+struct X3Cfg {
+    static constexpr int kTb0 = 2;
+    static constexpr int kTbWarps = C / 8;                 // 4 C threads
+    static constexpr int kEpi0 = kTb0 + kTbWarps;
+    static constexpr int kGroups = 3;
+    static constexpr int kEpiWarps = 4 * kGroups;
+    static constexpr int kThreads = 32 * (kEpi0 + kEpiWarps);
+    static constexpr int kStages = 6;
+    static constexpr int kABytes = 128 * C;               // two [C][64] boxes
+    static constexpr int kAccStages = kGroups;
+    static constexpr int kAccCols = 2 * C;                // local accumulator, then x1
+    static constexpr int kTmemCols = kAccStages * kAccCols <= 256 ? 256 : 512;
+    static constexpr int kTBufs = 4;
+    static constexpr int kBinvBlk = 128 * 128;            // [128 points][32 fp32], 128-byte swizzle
+    static constexpr int kUBlk = C * 128;                 // [C][32 fp32]
+    static constexpr int kOffA = 0;
+    static constexpr int kOffW = kOffA + kStages * kABytes;
+    static constexpr int kOffBinv = kOffW + ((C * C + 1023) / 1024) * 1024;
+    static constexpr int kOffU = kOffBinv + 2 * kBinvBlk;                 // hi, lo
+    static constexpr int kOffBias = kOffU + kTBufs * 2 * kUBlk;           // hi, lo per buffer
+    static constexpr int kOffTw = kOffBias + C * 4;                       // [Wp][8] float2 (Wp <= 128)
+    static constexpr int kOffBars = kOffTw + 128 * 8 * 8;
+    static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2 * kTBufs;
+    static constexpr int kSmemBytes = kOffBars + 8 * kNumBars + 16 + 1024;
+    static_assert(kSmemBytes <= 227 * 1024, "smem");
+};
+
+bool fno3d_fused_layer_ok(int C, int Wp, int Dp, int MW, int MD) {
+    return (C == 32 || C == 64) && (Dp == 64 || Dp == 128) && Wp <= 128 && MW <= 8 && MD <= 8;
+}
+
+template <int C>
+__global__ void __launch_bounds__(X3Cfg<C>::kThreads, 1)
+layer3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, const Fno3dLayer L, DftDims g,
+                  uint8_t* __restrict__ hout, unsigned* err) {
+    using F = X3Cfg<C>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* sA = smem + F::kOffA;
+    uint8_t* sW = smem + F::kOffW;
+    uint8_t* sBinv = smem + F::kOffBinv;
+    uint8_t* sU = smem + F::kOffU;
+    float* sBias = reinterpret_cast<float*>(smem + F::kOffBias);
+    float2* sTw = reinterpret_cast<float2*>(smem + F::kOffTw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + F::kOffBars);
+    uint64_t* empty = full + F::kStages;
+    uint64_t* accFull = empty + F::kStages;
+    uint64_t* accEmpty = accFull + F::kAccStages;
+    uint64_t* tReady = accEmpty + F::kAccStages;
+    uint64_t* tFree = tReady + F::kTBufs;
+    uint32_t* sTmem = reinterpret_cast<uint32_t*>(tFree + F::kTBufs);
+    volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int Wp = p.Wp, Dp = p.Dp, MW = p.MW, MD = p.MD;
+    const int64_t Pp = static_cast<int64_t>(p.Hp) * Wp * Dp;
+    const int tiles_per_sample = static_cast<int>(Pp / 128);
+    const int num_tiles = p.B * tiles_per_sample;
+    const int t_begin = static_cast<int>(static_cast<int64_t>(num_tiles) * blockIdx.x / gridDim.x);
+    const int t_end = static_cast<int>(static_cast<int64_t>(num_tiles) * (blockIdx.x + 1) / gridDim.x);
+
+    {
+        for (int i = threadIdx.x; i < C * C; i += F::kThreads) {
+            const int o = i / C, k = i % C;
+            sW[swz_offset(o * C + k, C)] = static_cast<uint8_t>(e4m3_encode_ref(L.loc_q[i]));
+        }
+        for (int o = threadIdx.x; o < C; o += F::kThreads) sBias[o] = L.loc_b[o];
+        // W twiddles e^{-2 pi i kw w / Wp} (the DFT table's [Wp][MW2] block), kw < 8
+        {
+            const float2* gW = reinterpret_cast<const float2*>(p.dft + 2 * Dp * g.MD4);
+            for (int i = threadIdx.x; i < Wp * 8; i += F::kThreads) {
+                const int w = i >> 3, kw = i & 7;
+                sTw[i] = kw < MW ? gW[w * g.MW2 + kw] : make_float2(0.0f, 0.0f);
+            }
+        }
+        // Binv hi / lo: point p = r' Dp + d, column 16 r' + 2 kd (+1)
+        {
+            const float* iC = p.dft + 2 * Dp * g.MD4 + 2 * Wp * g.MW2;
+            const float* iS = iC + g.MD4 * Dp;
+            for (int i = threadIdx.x; i < 128 * 32; i += F::kThreads) {
+                const int pt = i >> 5, k = i & 31;
+                const int r = k >> 4, j = k & 15, kd = j >> 1;
+                float v = 0.0f;
+                if (r == pt / Dp && kd < MD) v = (j & 1) ? iS[kd * Dp + pt % Dp] : iC[kd * Dp + pt % Dp];
+                float hi, lo;
+                split_tf32_x3(v, hi, lo);
+                const uint32_t o = swz_offset(static_cast<uint32_t>(pt * 128 + k * 4), 128);
+                *reinterpret_cast<float*>(sBinv + o) = hi;
+                *reinterpret_cast<float*>(sBinv + F::kBinvBlk + o) = lo;
+            }
+        }
+        // U buffers start zero: the builders write only present rows and modes
+        for (int i = threadIdx.x; i < F::kTBufs * 2 * F::kUBlk / 16; i += F::kThreads)
+            reinterpret_cast<uint4*>(sU)[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < F::kStages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            for (int s = 0; s < F::kAccStages; ++s) {
+                mbar_init(&accFull[s], 1);
+                mbar_init(&accEmpty[s], 4);
+            }
+            for (int b = 0; b < F::kTBufs; ++b) {
+                mbar_init(&tReady[b], F::kTbWarps * 32);
+                mbar_init(&tFree[b], 1);
+            }
+            *sAbort = 0;
+            fence_mbar_init();
+        }
+        if (warp == 1) tmem_alloc(sTmem, F::kTmemCols);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    const uint32_t tmem_base = *sTmem;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            prefetch_tmap(&tmIn);
+            int it = 0;
+            for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+                const int s = it % F::kStages;
+                const uint32_t ph = (it / F::kStages) & 1;
+                if (!mbar_wait_backoff(&empty[s], ph ^ 1, sAbort, 1024)) {
+                    *sAbort = 1;
+                    atomicOr(err, kErrWaitSlotFree);
+                    break;
+                }
+                const int b = tile / tiles_per_sample;
+                const int p0 = (tile - b * tiles_per_sample) * 128;
+                mbar_arrive_expect_tx(&full[s], F::kABytes);
+                tma_load_2d(sA + s * F::kABytes, &tmIn, &full[s], p0, b * C);
+                tma_load_2d(sA + s * F::kABytes + F::kABytes / 2, &tmIn, &full[s], p0 + 64, b * C);
+            }
+            for (int j = (it > F::kStages ? it - F::kStages : 0); j < it; ++j)
+                if (!mbar_wait_drain(&full[j % F::kStages], (j / F::kStages) & 1)) {
+                    atomicOr(err, kErrWaitDrain);
+                    break;
+                }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (elect_one()) {
+            constexpr uint32_t idesc8 = idesc_e4m3(C) | (1u << 15);  // A MN-major
+            constexpr uint32_t idesc32 = idesc_tf32(C);
+            int it = 0;
+            for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+                const int s = it % F::kStages;
+                const uint32_t ph = (it / F::kStages) & 1;
+                const int a = it % F::kAccStages;
+                const uint32_t aph = (it / F::kAccStages) & 1;
+                const int tb = it % F::kTBufs;
+                if (!mbar_wait_backoff(&accEmpty[a], aph ^ 1, sAbort, 128) ||
+                    !mbar_wait_backoff(&full[s], ph, sAbort, 128) ||
+                    !mbar_wait_backoff(&tReady[tb], (it / F::kTBufs) & 1, sAbort, 128)) {
+                    *sAbort = 1;
+                    atomicOr(err, kErrWaitTmaFull);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + a * F::kAccCols;
+                const uint32_t aBase = smem_u32(sA + s * F::kABytes);
+#pragma unroll
+                for (int kk = 0; kk < C / 32; ++kk)
+                    mma_f8(d, umma_desc_mn_sw64(aBase + kk * 2048, F::kABytes / 2, 512),
+                           umma_desc(smem_u32(sW) + kk * 32, C), idesc8, kk > 0 ? 1u : 0u);
+                const uint32_t bhi = smem_u32(sBinv), blo = bhi + F::kBinvBlk;
+                const uint32_t uhi = smem_u32(sU) + tb * 2 * F::kUBlk, ulo = uhi + F::kUBlk;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_tf32(d + C, umma_desc(bhi + kk * 32, 128), umma_desc(uhi + kk * 32, 128), idesc32,
+                             kk > 0 ? 1u : 0u);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_tf32(d + C, umma_desc(blo + kk * 32, 128), umma_desc(uhi + kk * 32, 128), idesc32, 1u);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_tf32(d + C, umma_desc(bhi + kk * 32, 128), umma_desc(ulo + kk * 32, 128), idesc32, 1u);
+                mma_commit(&empty[s]);
+                mma_commit(&accFull[a]);
+                mma_commit(&tFree[tb]);
+            }
+            if (it > 0) {
+                const int j = it - 1;
+                if (!mbar_wait_drain(&accFull[j % F::kAccStages], (j / F::kAccStages) & 1))
+                    atomicOr(err, kErrWaitDrain);
+            }
+        }
+        __syncwarp();
+    } else if (warp < F::kEpi0) {
+        // ---------------- T builders: thread (o, q) owns kd = 2q, 2q + 1 of channel o
+        const int ctid = (warp - F::kTb0) * 32 + lane;
+        const int o = ctid % C, q = ctid / C;
+        const int R = 128 / Dp;
+        const float unit = __fdiv_rn(1.0f, static_cast<float>(Wp) * static_cast<float>(Dp));
+        float f[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int kd = 2 * q + e;
+            f[e] = (kd == 0 || 2 * kd == Dp) ? unit : __fmul_rn(2.0f, unit);
+        }
+        float2 ci[8][2];
+        int cached = -1;
+        int it = 0;
+        for (int tile = t_begin; tile < t_end; ++tile, ++it) {
+            const int b = tile / tiles_per_sample;
+            const int pt0 = (tile - b * tiles_per_sample) * 128;
+            const int h = pt0 / (Wp * Dp);
+            const int w0 = (pt0 / Dp) % Wp;
+            const int plane = b * p.Hp + h;
+            if (plane != cached) {
+                const float2* src = p.colinv + ((static_cast<int64_t>(b) * C + o) * p.Hp + h) * (MW * MD);
+#pragma unroll
+                for (int kw = 0; kw < 8; ++kw)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int kd = 2 * q + e;
+                        ci[kw][e] = (kw < MW && kd < MD) ? __ldg(src + kw * MD + kd) : make_float2(0.0f, 0.0f);
+                    }
+                cached = plane;
+            }
+            const int tb = it % F::kTBufs;
+            if (!mbar_wait_backoff(&tFree[tb], ((it / F::kTBufs) & 1) ^ 1, sAbort, 256)) {
+                *sAbort = 1;
+                atomicOr(err, kErrWaitSlotFree);
+                break;
+            }
+            uint8_t* uhi = sU + tb * 2 * F::kUBlk;
+            for (int r = 0; r < R; ++r) {
+                const float2* tw = sTw + (w0 + r) * 8;
+                float sr[2] = {0.0f, 0.0f}, si[2] = {0.0f, 0.0f};
+#pragma unroll
+                for (int kw = 0; kw < 8; ++kw) {
+                    const float2 t = tw[kw];  // e^{-i theta}; e^{+i theta} = (t.x, -t.y)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        sr[e] = __fmaf_rn(ci[kw][e].x, t.x, sr[e]);
+                        sr[e] = __fmaf_rn(ci[kw][e].y, t.y, sr[e]);
+                        si[e] = __fmaf_rn(ci[kw][e].y, t.x, si[e]);
+                        si[e] = __fmaf_rn(-ci[kw][e].x, t.y, si[e]);
+                    }
+                }
+                float v[4] = {__fmul_rn(sr[0], f[0]), -__fmul_rn(si[0], f[0]), __fmul_rn(sr[1], f[1]),
+                              -__fmul_rn(si[1], f[1])};
+                float hi[4], lo[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) split_tf32_x3(v[e], hi[e], lo[e]);
+                const uint32_t off = swz_offset(static_cast<uint32_t>(o * 128 + (16 * r + 4 * q) * 4), 128);
+                *reinterpret_cast<float4*>(uhi + off) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<float4*>(uhi + F::kUBlk + off) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&tReady[tb]);
+        }
+    } else {
+        const int ew = warp - F::kEpi0;
+        const int quad = warp & 3;
+        const int grp = ew >> 2;
+        const float sc = __fmul_rn(L.s_in, L.s_w);
+        const float inv_out = inv_of(L.s_out);
+        for (int it = grp; t_begin + it < t_end; it += F::kGroups) {
+            const int tile = t_begin + it;
+            const int a = it % F::kAccStages;
+            const uint32_t aph = (it / F::kAccStages) & 1;
+            if (!mbar_wait(&accFull[a], aph, sAbort)) {
+                *sAbort = 1;
+                atomicOr(err, kErrWaitAccFull);
+                break;
+            }
+            tc_fence_after();
+            const int b = tile / tiles_per_sample;
+            const int64_t pt = static_cast<int64_t>(tile - b * tiles_per_sample) * 128 + quad * 32 + lane;
+            const int64_t base = static_cast<int64_t>(b) * C * Pp + pt;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + a * F::kAccCols;
+#pragma unroll 1
+            for (int hc = 0; hc < C / 32; ++hc) {
+                uint32_t acc[32], x1r[32];
+                tmem_ld32(tbase + 32 * hc, acc);
+                tmem_ld32(tbase + C + 32 * hc, x1r);
+                tmem_wait_ld();
+                if (hc == C / 32 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&accEmpty[a]);
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int oc = 32 * hc + j;
+                    const float x2 = fp8_fake_quant(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[oc]),
+                                                    L.s_out, inv_out);
+                    const float z = act_f(__fadd_rn(__uint_as_float(x1r[j]), x2), p.act);
+                    hout[base + static_cast<int64_t>(oc) * Pp] = static_cast<uint8_t>(e4m3_code(z, inv_out));
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, F::kTmemCols);
+    }
+}
+
 // projection, one unpadded point per thread
 template <int C>
 __global__ void __launch_bounds__(128) proj3d_kernel(Fno3dPlan p, const void* hin, float s_in) {
@@ -1179,6 +1517,7 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
     const size_t sdf = dft_fwd_smem(g, p.Wp, p.Dp), sdi = dft_inv_smem(g, p.Wp, p.Dp, p.MW);
     int gdf = 0, gdi = 0;
     const bool ftc = direct && fwd_tc_ok(p.Wp, p.Dp, p.MD);
+    const bool fused = direct && fno3d_fused_layer_ok(p.C, p.Wp, p.Dp, p.MW, p.MD);
     const FtcDims fd = ftc_dims(g, p.Wp, p.Dp);
     unsigned* err = device_error_word();
     if (ftc && !err) return cudaErrorMemoryAllocation;
@@ -1207,7 +1546,13 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
     }
     const int64_t tp = static_cast<int64_t>(p.B) * Pp;
     const int lgrid = static_cast<int>(std::min<int64_t>((tp + 127) / 128, sms * 16));
-    for (int i = 0; i < p.L; ++i) {
+    const size_t tap_bytes = static_cast<size_t>(p.B) * C * Pp;
+    for (int i = 0; i <= p.L; ++i) {
+        if (p.tap_codes && p.fp8 &&
+            (e = cudaMemcpyAsync(p.tap_codes + static_cast<size_t>(i) * tap_bytes, p.h[i & 1], tap_bytes,
+                                 cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
+            return e;
+        if (i == p.L) break;
         const Fno3dLayer& L = p.layer[i];
         const void* hin = p.h[i & 1];
         void* hout = p.h[(i + 1) & 1];
@@ -1225,12 +1570,33 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
                  mix3d_kernel<<<dim3(p.C / G, p.B), 256, sx, st>>>(p, L.wr, L.wi, G);
              })) != cudaSuccess)
             return e;
+        bool tc = false;
+        if constexpr (C == 32 || C == 64) {
+            // FP8, direct DFT geometries: inverse transforms fused into the local layer
+            if (fused) {
+                using F = X3Cfg<C>;
+                CUtensorMap tm;
+                if (!err) return cudaErrorMemoryAllocation;
+                if (!encode_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, hin, static_cast<uint64_t>(Pp),
+                               static_cast<uint64_t>(p.B) * C, static_cast<uint64_t>(Pp), 64, C, 64))
+                    return cudaErrorInvalidValue;
+                auto k = layer3d_tc_kernel<C>;
+                if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(k), F::kSmemBytes)) != cudaSuccess)
+                    return e;
+                const int64_t tiles = static_cast<int64_t>(p.B) * (Pp / 128);
+                const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
+                if ((e = timed("fno3d_local", [&] {
+                         k<<<grid, F::kThreads, F::kSmemBytes, st>>>(tm, p, L, g, static_cast<uint8_t*>(hout), err);
+                     })) != cudaSuccess)
+                    return e;
+                continue;
+            }
+        }
         if ((e = timed("fno3d_inv", [&] {
                  if (direct) inv3d_dft_kernel<<<gdi, kDftThreads, sdi, st>>>(p, g);
                  else inv3d_kernel<<<dim3(p.Hp, p.C, p.B), 256, si, st>>>(p);
              })) != cudaSuccess)
             return e;
-        bool tc = false;
         if constexpr (C == 32 || C == 64) {
             // FP8: the local layer on tensor cores when a sample is whole 128-point tiles
             if (p.fp8 && Pp % 128 == 0) {

@@ -52,6 +52,10 @@ struct Fno3dPlan {
     float* x1;             // (B, C, Hp, Wp, Dp) spectral branch output
     const float* dft;      // direct-DFT tables (fno3d_dft_tables), or null: radix-2 passes
     KernelTimer* timer;
+    // FP8 parity taps (nullptr: off): the E4M3 codes of every layer input -- the lift's
+    // output, then each layer's output -- copied as L + 1 consecutive (B, C, Hp, Wp, Dp)
+    // blocks after the kernel that wrote them
+    uint8_t* tap_codes;
 };
 
 // The FP8 variant at widths 32 and 64 (whose tensor-core local layer already holds it

@@ -1268,6 +1268,13 @@ int fno3d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
     pl.y = dy;
     for (int i = 0; i < 6; ++i) pl.tw[i] = rt->f3_tw[i];
     pl.dft = direct ? rt->f3_dft : nullptr;
+    pl.tap_codes = nullptr;
+    if (rt->tap_codes) {
+        if (!pl.fp8) return rt_fail(rt, NFX_UNSUPPORTED_OP, "FNO3d code taps exist for the FP8 variant only");
+        const int64_t need = static_cast<int64_t>(pl.L + 1) * vol;
+        if (need > rt->tap_cap) return rt_fail(rt, NFX_INVALID_ARG, "code tap buffer too small");
+        pl.tap_codes = reinterpret_cast<uint8_t*>(rt->tap_codes);
+    }
     pl.h[0] = rt->f3_bufs[0];
     pl.h[1] = rt->f3_bufs[1];
     pl.A = static_cast<float2*>(rt->f3_bufs[2]);

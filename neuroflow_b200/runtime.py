@@ -168,9 +168,10 @@ class InferenceRuntime:
             raise RuntimeError("RunTokenMixer2D failed: " + self._err())
 
     def set_code_taps(self, buf=None) -> None:
-        """FNO2d INT8 parity taps: `buf` an int8 CUDA tensor of at least
-        (n_layers + 1) * batch * h * w * width bytes receives the codes of every layer
-        input on each later device run; None turns the taps off."""
+        """Parity taps: `buf` a byte CUDA tensor of at least (n_layers + 1) * batch *
+        points * width bytes receives the codes of every layer input on each later
+        device run (FNO2d INT8: int8, channel-last; FNO3d FP8: E4M3, channel-first on
+        the padded grid); None turns the taps off."""
         if buf is None:
             rc = _lib.nfx_runtime_set_code_taps(self._h, None, 0)
         else:

@@ -132,6 +132,9 @@ class Oracle:
         L.nfo_fno2d_forward.restype = C.c_int
         L.nfo_fno2d_forward.argtypes = [C.POINTER(_FNO2d), C.c_int, _f32p, C.c_int, C.c_int,
                                         C.c_int, _f32p, C.POINTER(_Taps)]
+        L.nfo_fno3d_forward_taps.restype = C.c_int
+        L.nfo_fno3d_forward_taps.argtypes = [C.POINTER(_FNO3d), C.c_int, _f32p, C.c_int, C.c_int,
+                                             C.c_int, C.c_int, _f32p, _f32p]
         L.nfo_fno3d_forward.restype = C.c_int
         L.nfo_fno3d_forward.argtypes = [C.POINTER(_FNO3d), C.c_int, _f32p, C.c_int, C.c_int,
                                         C.c_int, C.c_int, _f32p]
@@ -357,17 +360,31 @@ class Oracle:
         self.lib.nfo_fp32_to_e4m3_array(_p(x), out.ctypes.data_as(C.c_void_p), C.c_int64(x.size))
         return out
 
-    def fno3d_forward(self, model, x, fp8: bool = False):
-        """mode 0 (fp8=False): the reference FNO3d::Forward; fp8=True: the E4M3 variant."""
+    def fno3d_forward(self, model, x, fp8: bool = False, taps: bool = False):
+        """mode 0 (fp8=False): the reference FNO3d::Forward; fp8=True: the E4M3 variant.
+        With taps (fp8 only), returns (y, t): t[i] the E4M3 values of layer i's input
+        (the lift's output, then each layer's output), channel-first on the padded grid
+        (L + 1, B, C, Hp, Wp, Dp)."""
         x = _c(x, np.float32)
         st, keep = build_fno3d_struct(model)
         y = np.empty(x.shape[:-1] + (model.config["out_channels"],), np.float32)
         B, H, W, D, _ = x.shape
-        rc = self.lib.nfo_fno3d_forward(C.byref(st), 1 if fp8 else 0, _p(x), B, H, W, D, _p(y))
+        if not taps:
+            rc = self.lib.nfo_fno3d_forward(C.byref(st), 1 if fp8 else 0, _p(x), B, H, W, D, _p(y))
+            if rc != 0:
+                raise RuntimeError(f"nfo_fno3d_forward failed: {rc}")
+            del keep
+            return y
+        if not fp8:
+            raise ValueError("FNO3d taps exist for the FP8 variant only")
+        pf = int(model.config.get("pad_factor", 0))
+        pd = [d + ((pf - d % pf) % pf if pf > 1 else 0) for d in (H, W, D)]
+        t = np.empty((model.config["n_layers"] + 1, B, model.config["width"]) + tuple(pd), np.float32)
+        rc = self.lib.nfo_fno3d_forward_taps(C.byref(st), 1, _p(x), B, H, W, D, _p(y), _p(t))
         if rc != 0:
-            raise RuntimeError(f"nfo_fno3d_forward failed: {rc}")
+            raise RuntimeError(f"nfo_fno3d_forward_taps failed: {rc}")
         del keep
-        return y
+        return y, t
 
 
 def build_fno3d_struct(model):

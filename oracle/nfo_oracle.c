@@ -1484,8 +1484,11 @@ static void fp8_linear(const float* aq, const float* wq, const float* b, int64_t
  *         locs.i.output, proj_q.output and proj_out.output are E4M3 fake-quantised
  *         like FNO2d's boundaries (fno.cpp:810-844).
  * x (b, H, W, D, in_ch) -> y (b, H, W, D, out_ch). */
-int nfo_fno3d_forward(const nfo_fno3d* m, int mode, const float* x, int bsz, int H0, int W0, int D0,
-                      float* y) {
+/* taps (mode 1, or NULL): the E4M3 values of every layer input -- the lift's output, then
+ * each layer's output -- as L + 1 consecutive channel-first padded (B, C, Hp, Wp, Dp)
+ * blocks */
+static int fno3d_forward_impl(const nfo_fno3d* m, int mode, const float* x, int bsz, int H0, int W0, int D0,
+                              float* y, float* taps) {
     const int w = m->width, mh = m->modes_h, mw = m->modes_w, md = m->modes_d, L = m->n_layers;
     const int in_ch = m->in_ch, out_ch = m->out_ch;
     if (L > NFO_MAX_LAYERS) return 1;
@@ -1546,6 +1549,7 @@ int nfo_fno3d_forward(const nfo_fno3d* m, int mode, const float* x, int bsz, int
         }
     }
     const int64_t Pp = H * W * D, Mp = (int64_t)bsz * Pp;
+    if (taps && mode == 1) memcpy(taps, xq, sizeof(float) * (size_t)(Mp * w));
     float* x1 = (float*)malloc(sizeof(float) * (size_t)(Mp * w));
     float* pin = (float*)malloc(sizeof(float) * (size_t)(Mp * w));
     float* pout = (float*)malloc(sizeof(float) * (size_t)(Mp * w));
@@ -1570,6 +1574,7 @@ int nfo_fno3d_forward(const nfo_fno3d* m, int mode, const float* x, int bsz, int
                 }
         nfo_apply_activation(hp, Mp * w, m->relu);
         if (mode == 1) fp8_codes(hp, m->s_locs[i], xq, hp, Mp * w);
+        if (taps && mode == 1) memcpy(taps + (size_t)(i + 1) * (size_t)(Mp * w), xq, sizeof(float) * (size_t)(Mp * w));
     }
     if (pad[0] || pad[1] || pad[2]) {
         const int64_t oh = H - pad[0], ow = W - pad[1], od = D - pad[2];
@@ -1624,6 +1629,16 @@ int nfo_fno3d_forward(const nfo_fno3d* m, int mode, const float* x, int bsz, int
     free(pq_w);
     free(lift_w);
     return 0;
+}
+
+int nfo_fno3d_forward(const nfo_fno3d* m, int mode, const float* x, int bsz, int H0, int W0, int D0,
+                      float* y) {
+    return fno3d_forward_impl(m, mode, x, bsz, H0, W0, D0, y, NULL);
+}
+
+int nfo_fno3d_forward_taps(const nfo_fno3d* m, int mode, const float* x, int bsz, int H0, int W0, int D0,
+                           float* y, float* taps) {
+    return fno3d_forward_impl(m, mode, x, bsz, H0, W0, D0, y, taps);
 }
 
 /* ------------------------------------------------------------------------- */

@@ -112,19 +112,22 @@ def test_fno3d_fp8_configs3_grid():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("shape,modes", [((2, 8, 16, 16), (3, 5, 9)),    # kept D Nyquist mode
-                                         ((1, 8, 16, 32), (4, 3, 6)),
-                                         ((1, 8, 16, 64), (4, 3, 6)),    # D pass on tensor cores
-                                         ((1, 8, 8, 64), (3, 4, 16)),    # ... with N = 32
-                                         ((1, 4, 128, 128), (2, 3, 5)),  # ... Wp = Dp = 128
-                                         ((3, 16, 8, 16), (5, 8, 2))])
-def test_fno3d_fp8_direct_dft_geometries(tmp_path, shape, modes):
-    """FP8 at width 32 runs the D and W passes as direct truncated DFTs (the forward D
-    pass as an f16 MMA when Dp is 64 or 128): non-cubic grids, odd mode counts
-    (padded table columns), the D-axis Nyquist mode kept (Dp / 2 + 1 modes), and plane
-    counts that leave the last CTA pass partly empty."""
+@pytest.mark.parametrize("shape,modes,width", [
+    ((2, 8, 16, 16), (3, 5, 9), 32),     # kept D Nyquist mode
+    ((1, 8, 16, 32), (4, 3, 6), 32),
+    ((1, 8, 16, 64), (4, 3, 6), 32),     # D pass on tensor cores, fused inverse + local
+    ((1, 8, 8, 64), (3, 4, 16), 32),     # ... N = 32 forward; inverse not fused (16 kd modes)
+    ((1, 4, 128, 128), (2, 3, 5), 32),   # ... Wp = Dp = 128 (one row per tile)
+    ((1, 4, 16, 64), (3, 8, 8), 64),     # width 64, fused
+    ((3, 16, 8, 16), (5, 8, 2), 32)])
+def test_fno3d_fp8_direct_dft_geometries(tmp_path, shape, modes, width):
+    """FP8 at widths 32 and 64 runs the D and W passes as direct truncated DFTs (the
+    forward D pass as an f16 MMA and the inverse fused into the tensor-core local layer
+    when Dp is 64 or 128): non-cubic grids, odd mode counts (padded table columns), the
+    D-axis Nyquist mode kept (Dp / 2 + 1 modes), and plane counts that leave the last
+    CTA pass partly empty."""
     S = 16 if max(modes) <= 9 else 32     # the calibration grid holds the modes
-    m, p = _model(tmp_path, "gelu", width=32, modes=modes, L=2, S=S)
+    m, p = _model(tmp_path, "gelu", width=width, modes=modes, L=2, S=S)
     x = np.random.default_rng(5).standard_normal(shape + (4,)).astype(np.float32)
     want = Oracle().fno3d_forward(m, x, fp8=True)
     got = _run(p, x, 1, fp8=True)
@@ -146,3 +149,42 @@ def test_fno3d_errors(tmp_path):
         rt.run(np.zeros((1, 8, 8, 8, 4), np.float32), np.zeros((1, 8, 8, 4, 1), np.float32))
     with pytest.raises(RuntimeError, match="power of two"):
         rt.run(np.zeros((1, 8, 6, 8, 4), np.float32), np.zeros((1, 8, 6, 8, 1), np.float32))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("S,modes", [(64, (8, 8, 8)), (32, (8, 8, 8))])
+def test_fno3d_fp8_layer_codes_match_oracle(tmp_path, S, modes):
+    """The FP8 variant layer by layer: the E4M3 codes of every layer input (taps) against
+    the oracle's.  The network output is fake-quantised to E4M3 and barely moves under
+    small perturbations (a 0.1 % change of a layer's spectral weights moves none of
+    65,536 outputs), so the layer codes are the sensitive check of the direct DFTs, the
+    f16 forward D pass, the fused tf32 inverse and the tensor-core local layer.  A moved
+    code is one E4M3 step from the oracle's, and few codes move."""
+    import torch
+    from neuroflow_b200.runtime import InferenceRuntime
+    m, p = _model(tmp_path, "gelu", width=32, modes=modes, L=4, S=min(S, 32))
+    x = synth.fno3d_inputs(np.random.default_rng(11), 1, S)
+    o = Oracle()
+    _, taps = o.fno3d_forward(m, x, fp8=True, taps=True)
+    rt = InferenceRuntime(p)
+    rt.enable_fp8()
+    buf = torch.zeros(taps.size, dtype=torch.uint8, device="cuda")
+    rt.set_code_taps(buf)
+    dy = torch.empty(x.shape[:-1] + (1,), dtype=torch.float32, device="cuda")
+    rt.run_device(torch.from_numpy(x).cuda(), dy)
+    torch.cuda.synchronize()
+    rt.set_code_taps(None)
+    got = buf.cpu().numpy().reshape(taps.shape)
+    dec = np.array([o.lib.nfo_e4m3_to_fp32(i) for i in range(256)], np.float32)
+    vals = dec[got]
+    for i in range(taps.shape[0]):
+        moved = vals[i] != taps[i]
+        frac = float(moved.mean())
+        print(f"S={S} layer input {i}: moved {int(moved.sum())} of {moved.size} ({frac:.2e})")
+        assert frac < 1e-5, (i, frac)
+        if moved.any():
+            # one E4M3 step: adjacent codes of one sign, or the two codes next to zero
+            gc = got[i][moved].astype(np.int32)
+            wc = o.fp32_to_e4m3(np.ascontiguousarray(taps[i][moved])).astype(np.int32)
+            ok = (np.abs(gc - wc) <= 1) | (((gc & 0x7F) <= 1) & ((wc & 0x7F) <= 1))
+            assert np.all(ok), (i, gc[~ok][:8], wc[~ok][:8])
