@@ -339,9 +339,10 @@ int nfx_fp8_e4m3_from_bits_host(const uint8_t* bits, float* y, int64_t n);
 int nfx_fp8_e4m3_fake_quant_host(const float* x, float scale, float* y, int64_t n);
 /* No reference counterpart: the FP8 executors and nfx_fp8_e4m3_fake_quant encode and
  * decode with the hardware E4M3 conversions, patched to the reference's subnormal and
- * NaN rules.  This runs every fp32 bit pattern (clamped to +-448 as the executors clamp)
- * and every code through both forms on the current device and returns the number of
- * disagreements in *mismatches (0 expected).  Synchronous. */
+ * NaN rules and relying on the conversion's saturation for the clamp to +-448.  This
+ * runs every fp32 bit pattern (the reference form clamped) and every code through both
+ * forms on the current device and returns the number of disagreements in *mismatches
+ * (0 expected).  Synchronous. */
 int nfx_fp8_e4m3_selfcheck(unsigned long long* mismatches);
 
 /* Read and clear the device error word of the current device (bit flags of waits

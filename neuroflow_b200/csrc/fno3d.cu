@@ -85,15 +85,16 @@ __global__ void __launch_bounds__(256) lift3d_kernel(Fno3dPlan p) {
     }
 }
 
-// Four consecutive padded points of one D row per thread (Dp a multiple of 4, at most
-// 8 input features): each weight is read once per four points, and a channel's four
+// Four consecutive padded points of one D row per thread (Dp a multiple of 4, IN <= 8
+// input features, a compile-time count so every Linear step is unrolled with its
+// rounding fixed): each weight is read once per four points, and a channel's four
 // outputs leave in one 32-bit (E4M3 codes) or 128-bit (fp32) store.
+template <int IN>
 __global__ void __launch_bounds__(256) lift3d_x4_kernel(Fno3dPlan p) {
     const int lgD = 31 - __clz(p.Dp), lgW = 31 - __clz(p.Wp);
     const int lgP = lgD + lgW + (31 - __clz(p.Hp));
     const int64_t total = static_cast<int64_t>(p.B) << (lgP - 2);
-    const int nk = p.in_ch;
-    const int nu = linear_unfused_len(nk);
+    constexpr int nu = linear_unfused_len(IN);
     const float inv = inv_of(p.s_lift);
     for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
          t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -102,32 +103,30 @@ __global__ void __launch_bounds__(256) lift3d_x4_kernel(Fno3dPlan p) {
         const int dd = pt & (p.Dp - 1), ww = (pt >> lgD) & (p.Wp - 1), hh = pt >> (lgD + lgW);
         const bool row_in = hh < p.H && ww < p.W;
         bool in[4];
-        float xv[4][8];
+        float xv[4][IN];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             in[i] = row_in && dd + i < p.D;
-            const float* xr = p.x + ((((b * p.H + hh) * p.W + ww) * p.D) + (in[i] ? dd + i : 0)) * nk;
+            const float* xr = p.x + ((((b * p.H + hh) * p.W + ww) * p.D) + (in[i] ? dd + i : 0)) * IN;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) xv[i][k] = (in[i] && k < nk) ? __ldg(xr + k) : 0.0f;
+            for (int k = 0; k < IN; ++k) xv[i][k] = in[i] ? __ldg(xr + k) : 0.0f;
         }
         uint8_t* h8 = static_cast<uint8_t*>(p.h[0]) + (b * p.C << lgP) + pt;
         float* h32 = static_cast<float*>(p.h[0]) + (b * p.C << lgP) + pt;
+#pragma unroll 2
         for (int c = 0; c < p.C; ++c) {
-            const float* wc = p.lift_w + c * nk;
+            const float* wc = p.lift_w + c * IN;
             const float bc = __ldg(p.lift_b + c);
-            float wk[8];
+            float wk[IN];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) wk[k] = k < nk ? __ldg(wc + k) : 0.0f;
+            for (int k = 0; k < IN; ++k) wk[k] = __ldg(wc + k);
             float v[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                v[i] = 0.0f;
-                if (in[i]) {
-                    v[i] = bc;
+                float a = bc;
 #pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        if (k < nk) v[i] = linear_step(v[i], xv[i][k], wk[k], k >= nu);
-                }
+                for (int k = 0; k < IN; ++k) a = linear_step(a, xv[i][k], wk[k], k >= nu);
+                v[i] = in[i] ? a : 0.0f;
             }
             if (p.fp8)
                 *reinterpret_cast<uint32_t*>(h8 + (static_cast<int64_t>(c) << lgP)) =
@@ -338,9 +337,12 @@ __device__ __forceinline__ void dft_w_pass(const Fno3dPlan& p, int MD4, int MW2,
         const int pl = live ? it / items2 : 0, r = it - pl * items2;
         const int s = r & 7, blk = r >> 3;
         const int kwp = blk / (MD4 / 2), kdp = blk - kwp * (MD4 / 2);
-        float o[8];
+        // (re, im) of output (kw = 2 kwp + a, kd = 2 kdp + c) at 2 a + c, each lane of the
+        // f32x2 products the scalar fmaf chain re += yr tc, re += yi (-ts); im += yr ts,
+        // im += yi tc
+        float2 o2[4];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) o[k] = 0.0f;
+        for (int k = 0; k < 4; ++k) o2[k] = make_float2(0.0f, 0.0f);
         if (live) {
             for (int w = s; w < Wp; w += 8) {
                 const float4 y = *reinterpret_cast<const float4*>(sY + (pl * Wp + w) * ys + 4 * kdp);
@@ -350,15 +352,18 @@ __device__ __forceinline__ void dft_w_pass(const Fno3dPlan& p, int MD4, int MW2,
 #pragma unroll
                 for (int a = 0; a < 2; ++a)
 #pragma unroll
-                    for (int c = 0; c < 2; ++c) {  // kw = 2 kwp + a, kd = 2 kdp + c
-                        float& re = o[4 * a + 2 * c];
-                        float& im = o[4 * a + 2 * c + 1];
-                        re = __fmaf_rn(yr[c], tc[a], re);
-                        re = __fmaf_rn(-yi[c], ts[a], re);
-                        im = __fmaf_rn(yr[c], ts[a], im);
-                        im = __fmaf_rn(yi[c], tc[a], im);
+                    for (int c = 0; c < 2; ++c) {
+                        float2& q = o2[2 * a + c];
+                        q = fma2_rn(make_float2(yr[c], yr[c]), make_float2(tc[a], ts[a]), q);
+                        q = fma2_rn(make_float2(yi[c], yi[c]), make_float2(-ts[a], tc[a]), q);
                     }
             }
+        }
+        float o[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            o[2 * k] = o2[k].x;
+            o[2 * k + 1] = o2[k].y;
         }
 #pragma unroll
         for (int m = 1; m < 8; m <<= 1)
@@ -1493,11 +1498,22 @@ cudaError_t run_c(const Fno3dPlan& p, cudaStream_t st) {
         if (p.timer) p.timer->end(st);
         return cudaGetLastError();
     };
-    const bool lift4 = p.Dp % 4 == 0 && p.in_ch <= 8;
+    const bool lift4 = p.Dp % 4 == 0 && p.in_ch >= 1 && p.in_ch <= 8;
     const int64_t tl = static_cast<int64_t>(p.B) * Pp / (lift4 ? 4 : 1);
     if ((e = timed("fno3d_lift", [&] {
              const int grid = static_cast<int>(std::min<int64_t>((tl + 255) / 256, sms * 16));
-             if (lift4) lift3d_x4_kernel<<<grid, 256, 0, st>>>(p);
+             if (lift4) {
+                 switch (p.in_ch) {
+                     case 1: lift3d_x4_kernel<1><<<grid, 256, 0, st>>>(p); break;
+                     case 2: lift3d_x4_kernel<2><<<grid, 256, 0, st>>>(p); break;
+                     case 3: lift3d_x4_kernel<3><<<grid, 256, 0, st>>>(p); break;
+                     case 4: lift3d_x4_kernel<4><<<grid, 256, 0, st>>>(p); break;
+                     case 5: lift3d_x4_kernel<5><<<grid, 256, 0, st>>>(p); break;
+                     case 6: lift3d_x4_kernel<6><<<grid, 256, 0, st>>>(p); break;
+                     case 7: lift3d_x4_kernel<7><<<grid, 256, 0, st>>>(p); break;
+                     default: lift3d_x4_kernel<8><<<grid, 256, 0, st>>>(p); break;
+                 }
+             }
              else lift3d_kernel<<<grid, 256, 0, st>>>(p);
          })) != cudaSuccess)
         return e;

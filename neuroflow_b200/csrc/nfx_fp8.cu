@@ -38,15 +38,16 @@ __global__ void e4m3_fake_quant_kernel(const float* __restrict__ x, float scale,
         out[i] = nfx::fp8_fake_quant(x[i], scale, inv);
 }
 
-// Every fp32 bit pattern, clamped as e4m3_code clamps, through the hardware-conversion
-// encoder and the reference one; every code through both decoders (bit patterns).
+// Every fp32 bit pattern through the hardware-conversion encoder (which saturates by
+// itself) and, clamped as e4m3_code clamps, through the reference one; every code
+// through both decoders (bit patterns).
 __global__ void e4m3_selfcheck_kernel(unsigned long long* bad) {
     unsigned long long n = 0;
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
     for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < (1ull << 32); i += stride) {
         const float v = __uint_as_float(static_cast<uint32_t>(i));
         const float xs = v > 448.0f ? 448.0f : (v < -448.0f ? -448.0f : v);
-        if (nfx::e4m3_encode_fast(xs) != nfx::e4m3_encode_ref(xs)) ++n;
+        if (nfx::e4m3_encode_fast(v) != nfx::e4m3_encode_ref(xs)) ++n;
         if (i < 256 && __float_as_uint(nfx::e4m3_decode_fast(static_cast<uint32_t>(i))) !=
                            __float_as_uint(nfx::e4m3_decode_ref(static_cast<uint32_t>(i))))
             ++n;

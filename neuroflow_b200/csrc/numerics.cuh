@@ -185,12 +185,13 @@ __device__ __forceinline__ float e4m3_decode_ref(uint32_t b) {
     return __uint_as_float((sign << 31) | ((ex + 120u) << 23) | (mt << 20));
 }
 
-// e4m3_encode_ref for v in [-448, 448] or NaN (what e4m3_code passes on), by the
-// hardware conversion.  cvt.rn.satfinite.e4m3x2.f32 rounds half-even to 3 mantissa
-// bits like the reference; the two differ only where the reference's subnormal rule
-// keeps |v| in [7.5, 8) * 2^-9 at code 7 (the conversion gives the smallest normal,
-// code 8) and on NaN (the reference gives 0x7F for either sign); both are patched.
-// nfx_fp8_e4m3_selfcheck compares the two over every fp32 bit pattern.
+// e4m3_encode_ref of v clamped to [-448, 448] (e4m3_code's saturation; NaN passes), by
+// the hardware conversion.  cvt.rn.satfinite.e4m3x2.f32 rounds half-even to 3 mantissa
+// bits like the reference and saturates finite values and infinities to +-448 itself;
+// the two differ only where the reference's subnormal rule keeps |v| in [7.5, 8) *
+// 2^-9 at code 7 (the conversion gives the smallest normal, code 8) and on NaN (the
+// reference gives 0x7F for either sign); both are patched.  nfx_fp8_e4m3_selfcheck
+// compares the two over every fp32 bit pattern.
 __device__ __forceinline__ uint32_t e4m3_encode_fast(float v) {
 #ifdef __CUDA_ARCH__
     unsigned short r;
@@ -220,9 +221,7 @@ __device__ __forceinline__ float e4m3_decode_fast(uint32_t b) {
 
 // fp8_e4m3.h:312-334: the E4M3 code of v under `inv` = 1/scale (scale 0 -> 1).
 __device__ __forceinline__ uint32_t e4m3_code(float v, float inv) {
-    float xs = __fmul_rn(v, inv);
-    xs = xs > 448.0f ? 448.0f : (xs < -448.0f ? -448.0f : xs);
-    return e4m3_encode_fast(xs);
+    return e4m3_encode_fast(__fmul_rn(v, inv));
 }
 // ... and the fake-quantised value
 __device__ __forceinline__ float fp8_fake_quant(float v, float scale, float inv) {

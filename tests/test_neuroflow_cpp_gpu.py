@@ -115,9 +115,10 @@ def test_fp8_helpers_known_answers_and_oracle_sweep():
 @pytest.mark.gpu
 def test_fp8_hardware_conversions_match_the_reference_encoder():
     """The FP8 executors encode and decode with the hardware E4M3 conversions, patched to
-    the reference's subnormal rule ([7.5, 8) * 2^-9 stays at code 7) and NaN codes: every
-    fp32 bit pattern (clamped to +-448 as the executors clamp) and every code agree bit
-    for bit with the reference's encoder and decoder (fp8_e4m3.h:106-284)."""
+    the reference's subnormal rule ([7.5, 8) * 2^-9 stays at code 7) and NaN codes, with
+    the conversion's own saturation standing in for the clamp to +-448: every fp32 bit
+    pattern (the reference encoder's input clamped) and every code agree bit for bit with
+    the reference's encoder and decoder (fp8_e4m3.h:106-284)."""
     import ctypes
     from neuroflow_b200 import _nfx
     n = ctypes.c_ulonglong(12345)
