@@ -819,7 +819,7 @@ __global__ void __launch_bounds__(128) local3d_kernel(Fno3dPlan p, Fno3dLayer L,
 #pragma unroll
         for (int o = 0; o < C; ++o) {
             float x2 = acc[o];
-            if (p.fp8) x2 = fp8_fake_quant(__fadd_rn(__fmul_rn(x2, sc), sB[o]), L.s_out, inv_out);
+            if (p.fp8) x2 = fp8_fake_quant_inner(__fadd_rn(__fmul_rn(x2, sc), sB[o]), L.s_out, inv_out);
             const float z = act_f(__fadd_rn(p.x1[base + o * P], x2), p.act);
             if (p.fp8) static_cast<uint8_t*>(hout)[base + o * P] = static_cast<uint8_t>(e4m3_code(z, inv_out));
             else static_cast<float*>(hout)[base + o * P] = z;
@@ -1018,7 +1018,7 @@ local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, c
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             const int c = 32 * h + j;
-                            const float q = fp8_fake_quant(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[c]),
+                            const float q = fp8_fake_quant_inner(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[c]),
                                                            s_out, inv_out);
                             yo[0] = linear_step(yo[0], act_f(q, p.act), sPo[c], c >= nu);
                         }
@@ -1026,7 +1026,7 @@ local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, c
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             const int c = 32 * h + j;
-                            const float q = fp8_fake_quant(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[c]),
+                            const float q = fp8_fake_quant_inner(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[c]),
                                                            s_out, inv_out);
                             const float g = act_f(q, p.act);
 #pragma unroll
@@ -1065,7 +1065,7 @@ local3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, c
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int o = 32 * h + j;
-                    const float x2 = fp8_fake_quant(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[o]),
+                    const float x2 = fp8_fake_quant_inner(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[o]),
                                                     s_out, inv_out);
                     const float z = act_f(__fadd_rn(x1v[j], x2), p.act);
                     hout[base + static_cast<int64_t>(o) * Pp] = static_cast<uint8_t>(e4m3_code(z, inv_out));
@@ -1403,7 +1403,7 @@ layer3d_tc_kernel(const __grid_constant__ CUtensorMap tmIn, const Fno3dPlan p, c
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int oc = 32 * hc + j;
-                    const float x2 = fp8_fake_quant(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[oc]),
+                    const float x2 = fp8_fake_quant_inner(__fadd_rn(__fmul_rn(__uint_as_float(acc[j]), sc), sBias[oc]),
                                                     L.s_out, inv_out);
                     const float z = act_f(__fadd_rn(__uint_as_float(x1r[j]), x2), p.act);
                     hout[base + static_cast<int64_t>(oc) * Pp] = static_cast<uint8_t>(e4m3_code(z, inv_out));
@@ -1461,7 +1461,7 @@ __global__ void __launch_bounds__(128) proj3d_kernel(Fno3dPlan p, const void* hi
                     q = p.fp8 ? __fadd_rn(q, __fmul_rn(a[k], ww4[m])) : linear_step(q, a[k], ww4[m], k >= nu);
                 }
             }
-            if (p.fp8) q = fp8_fake_quant(__fadd_rn(__fmul_rn(q, sc), __ldg(p.pq_b + c)), p.s_pq, inv_pq);
+            if (p.fp8) q = fp8_fake_quant_inner(__fadd_rn(__fmul_rn(q, sc), __ldg(p.pq_b + c)), p.s_pq, inv_pq);
             qv[c] = act_f(q, p.act);
         }
         float* yr = p.y + t * p.out_ch;

@@ -39,8 +39,9 @@ __global__ void e4m3_fake_quant_kernel(const float* __restrict__ x, float scale,
 }
 
 // Every fp32 bit pattern through the hardware-conversion encoder (which saturates by
-// itself) and, clamped as e4m3_code clamps, through the reference one; every code
-// through both decoders (bit patterns).
+// itself) and, clamped as e4m3_code clamps, through the reference one, and through the
+// executors' inner fake-quant against the reference round trip; every code through
+// both decoders (bit patterns).
 __global__ void e4m3_selfcheck_kernel(unsigned long long* bad) {
     unsigned long long n = 0;
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
@@ -48,6 +49,10 @@ __global__ void e4m3_selfcheck_kernel(unsigned long long* bad) {
         const float v = __uint_as_float(static_cast<uint32_t>(i));
         const float xs = v > 448.0f ? 448.0f : (v < -448.0f ? -448.0f : v);
         if (nfx::e4m3_encode_fast(v) != nfx::e4m3_encode_ref(xs)) ++n;
+        // the executors' inner fake-quant: the reference value, any NaN for a NaN
+        const float fq = nfx::fp8_fake_quant_inner(v, 1.0f, 1.0f);
+        const float fr = nfx::e4m3_decode_ref(nfx::e4m3_encode_ref(xs));
+        if (fr == fr ? __float_as_uint(fq) != __float_as_uint(fr) : fq == fq) ++n;
         if (i < 256 && __float_as_uint(nfx::e4m3_decode_fast(static_cast<uint32_t>(i))) !=
                            __float_as_uint(nfx::e4m3_decode_ref(static_cast<uint32_t>(i))))
             ++n;

@@ -219,6 +219,27 @@ __device__ __forceinline__ float e4m3_decode_fast(uint32_t b) {
 #endif
 }
 
+// fp8_fake_quant for a value whose result is only consumed on the way to another E4M3
+// code (e4m3_code patches a NaN to the reference's 0x7F there): the same value for
+// every non-NaN input, a NaN for a NaN, without the NaN bit-pattern fix-ups.
+__device__ __forceinline__ float fp8_fake_quant_inner(float v, float scale, float inv) {
+#ifdef __CUDA_ARCH__
+    const float xs = __fmul_rn(v, inv);
+    unsigned short r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(xs));
+    r = ((r & 0x7Fu) == 8u && fabsf(xs) < 0.015625f) ? static_cast<unsigned short>(r - 1u) : r;
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(r));
+    float f;
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tcvt.f32.f16 %0, lo;\n\t}" : "=f"(f) : "r"(h2));
+    return __fmul_rn(f, scale);
+#else
+    float xs = __fmul_rn(v, inv);
+    xs = xs > 448.0f ? 448.0f : (xs < -448.0f ? -448.0f : xs);
+    return __fmul_rn(e4m3_decode_ref(e4m3_encode_ref(xs)), scale);
+#endif
+}
+
 // fp8_e4m3.h:312-334: the E4M3 code of v under `inv` = 1/scale (scale 0 -> 1).
 __device__ __forceinline__ uint32_t e4m3_code(float v, float inv) {
     return e4m3_encode_fast(__fmul_rn(v, inv));
