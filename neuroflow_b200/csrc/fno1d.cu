@@ -244,6 +244,173 @@ __global__ void __launch_bounds__(256) layer1d_kernel(Layer1dArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Split layer (widths 16, 32 and 64 with the FP32 local Linear): inv1d_kernel runs the
+// contraction and the inverse transform per (b, group of R output rows), as
+// layer1d_kernel does, and writes x1 = Irfft(...) / N channel-first (b, c, p);
+// local1d_kernel then takes one point per thread and all C output channels -- the
+// local Linear (FP32 with the reference's rounding, from an input row read as 16-byte
+// vectors, the weights as [k][o] 16-byte broadcasts; the INT8 GEMM's output + bias is
+// also handled), the output fake-quant, x1 + x2, the activation -- and
+// writes the point's next activation as one contiguous run.  Every element sees the
+// operations layer1d_kernel applies, in the same order; the input row is read once per
+// point instead of once per output-channel group.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) inv1d_kernel(Layer1dArgs a, float* __restrict__ x1f) {
+    extern __shared__ float2 smem[];
+    const int G = a.G, N = a.N, C = a.C, modes = a.modes;
+    float2* sRow = smem;
+    float2* sY = sRow + static_cast<size_t>(G) * N;
+    const int b = blockIdx.y, o0 = blockIdx.x * G;
+    const Fno1dLayer& L = a.L;
+    for (int t = threadIdx.x; t < G * modes; t += blockDim.x) {
+        const int r = t / modes, m = t - (t / modes) * modes;
+        const int o = o0 + r;
+        float sr = 0.0f, si = 0.0f;
+        const float2* xb = a.Xs + static_cast<int64_t>(b) * C * modes + m;
+        for (int c = 0; c < C; ++c) {
+            const float2 hv = xb[static_cast<int64_t>(c) * modes];
+            const int64_t wi = (static_cast<int64_t>(c) * C + o) * modes + m;
+            const float wr = __ldg(L.wr + wi), wim = __ldg(L.wi + wi);
+            sr = __fadd_rn(sr, __fmaf_rn(hv.x, wr, -__fmul_rn(hv.y, wim)));
+            si = __fadd_rn(si, __fmaf_rn(hv.x, wim, __fmul_rn(hv.y, wr)));
+        }
+        sY[r * modes + m] = make_float2(sr, si);
+    }
+    __syncthreads();
+    const int half = N / 2 + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float inv_n = __fdiv_rn(1.0f, static_cast<float>(N));
+    for (int r = warp; r < G; r += blockDim.x >> 5) {
+        float2* row = sRow + static_cast<size_t>(r) * N;
+        for (int j = lane; j < N; j += 32) {
+            float2 v;
+            if (j < half) {
+                v = j < modes ? sY[r * modes + j] : make_float2(0.0f, 0.0f);
+            } else {
+                const int i = N - j;
+                const float2 u = i < modes ? sY[r * modes + i] : make_float2(0.0f, 0.0f);
+                v = make_float2(u.x, -u.y);
+            }
+            row[bit_reverse(j, a.log2N)] = v;
+        }
+        __syncwarp();
+        warp_fft_row<true>(row, N, a.tw_inv, lane);
+        float* dst = x1f + (static_cast<int64_t>(b) * C + o0 + r) * N;
+        for (int p = lane; p < N; p += 32) dst[p] = __fmul_rn(row[p].x, inv_n);
+    }
+}
+
+template <int C>
+__global__ void __launch_bounds__(128) local1d_kernel(Layer1dArgs a, const float* __restrict__ x1f,
+                                                      int64_t total) {
+    __shared__ float4 sW4[C * C / 4];  // [k][o]
+    __shared__ float sB[C];
+    float* sW = reinterpret_cast<float*>(sW4);
+    const Fno1dLayer& L = a.L;
+    const bool f32 = !L.use_int8;
+    if (f32)
+        for (int i = threadIdx.x; i < C * C; i += blockDim.x) sW[(i % C) * C + i / C] = __ldg(L.loc_w + i);
+    for (int i = threadIdx.x; i < C; i += blockDim.x) sB[i] = __ldg(L.loc_b + i);
+    __syncthreads();
+    const int N = a.N, lgN = a.log2N;
+    constexpr int nu = linear_unfused_len(C);
+    const float zpf_in = static_cast<float>(L.in_zp);
+    const float zpf_fq = static_cast<float>(L.fq_zp);
+    const float zpf_out = static_cast<float>(L.out_zp);
+    for (int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; row < total;
+         row += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b = row >> lgN;
+        const int p = static_cast<int>(row - (b << lgN));
+        float acc[C];
+        if (f32) {
+#pragma unroll
+            for (int o = 0; o < C; ++o) acc[o] = sB[o];
+#pragma unroll 1
+            for (int k16 = 0; k16 < C / 16; ++k16) {
+                float hv[16];
+                if (L.in_codes) {
+                    const uint4 q = *reinterpret_cast<const uint4*>(static_cast<const int8_t*>(a.h_in) + row * C + 16 * k16);
+                    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int8_t code = static_cast<int8_t>((w4[j >> 2] >> (8 * (j & 3))) & 0xFFu);
+                        hv[j] = __fmul_rn(__fsub_rn(static_cast<float>(code), zpf_in), L.in_s);
+                    }
+                } else {
+                    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(a.h_in) + row * C + 16 * k16);
+#pragma unroll
+                    for (int j4 = 0; j4 < 4; ++j4) {
+                        const float4 v = src[j4];
+                        hv[4 * j4] = v.x;
+                        hv[4 * j4 + 1] = v.y;
+                        hv[4 * j4 + 2] = v.z;
+                        hv[4 * j4 + 3] = v.w;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int k = 16 * k16 + j;
+                    const bool fused = k >= nu;
+#pragma unroll
+                    for (int o4 = 0; o4 < C / 4; ++o4) {
+                        const float4 w = sW4[k * (C / 4) + o4];
+                        acc[4 * o4 + 0] = linear_step(acc[4 * o4 + 0], hv[j], w.x, fused);
+                        acc[4 * o4 + 1] = linear_step(acc[4 * o4 + 1], hv[j], w.y, fused);
+                        acc[4 * o4 + 2] = linear_step(acc[4 * o4 + 2], hv[j], w.z, fused);
+                        acc[4 * o4 + 3] = linear_step(acc[4 * o4 + 3], hv[j], w.w, fused);
+                    }
+                }
+            }
+        } else {
+            const float4* xr = reinterpret_cast<const float4*>(a.x2raw + row * C);
+#pragma unroll
+            for (int o4 = 0; o4 < C / 4; ++o4) {
+                const float4 v = xr[o4];
+                acc[4 * o4 + 0] = __fadd_rn(v.x, sB[4 * o4 + 0]);
+                acc[4 * o4 + 1] = __fadd_rn(v.y, sB[4 * o4 + 1]);
+                acc[4 * o4 + 2] = __fadd_rn(v.z, sB[4 * o4 + 2]);
+                acc[4 * o4 + 3] = __fadd_rn(v.w, sB[4 * o4 + 3]);
+            }
+        }
+        const float* x1p = x1f + b * C * N + p;
+#pragma unroll
+        for (int o4 = 0; o4 < C / 4; ++o4) {
+            float out[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int o = 4 * o4 + j;
+                float v = acc[o];
+                if (L.fq_kind == 1) {
+                    v = fake_quant(v, L.fq_s, zpf_fq);
+                } else if (L.fq_kind == 2) {
+                    const int64_t qi = static_cast<int64_t>(o) * N + p;
+                    v = fake_quant(v, __ldg(L.pt_s + qi), static_cast<float>(__ldg(L.pt_zp + qi)));
+                } else if (L.fq_kind == 3) {
+                    v = fp8_log2_snap(v, L.fq_s);
+                }
+                const float z = __fadd_rn(x1p[static_cast<int64_t>(o) * N], v);
+                if (L.out_codes)
+                    out[j] = __int_as_float(L.lut_cells > 0
+                                                ? code_from_lut(z, L.code_lut, L.lut_cells, L.lut_zlo, L.lut_inv_delta)
+                                                : static_cast<int>(fq_code(act_f(z, a.act), L.out_s, zpf_out)));
+                else
+                    out[j] = act_f(z, a.act);
+            }
+            if (L.out_codes) {
+                const uint32_t pk = (static_cast<uint32_t>(__float_as_int(out[0])) & 0xFFu) |
+                                    ((static_cast<uint32_t>(__float_as_int(out[1])) & 0xFFu) << 8) |
+                                    ((static_cast<uint32_t>(__float_as_int(out[2])) & 0xFFu) << 16) |
+                                    ((static_cast<uint32_t>(__float_as_int(out[3])) & 0xFFu) << 24);
+                reinterpret_cast<uint32_t*>(static_cast<int8_t*>(a.h_out) + row * C)[o4] = pk;
+            } else {
+                reinterpret_cast<float4*>(static_cast<float*>(a.h_out) + row * C)[o4] =
+                    make_float4(out[0], out[1], out[2], out[3]);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // projection for widths up to 128, over tiles of kProjTP points (the same arithmetic as
 // proj1d_kernel below, element for element):
 //   phase 1  the tile's activation rows -> sH [TP][C], proj_q transposed -> sWt [C][C]
@@ -449,6 +616,9 @@ cudaError_t fno1d_run(const Fno1dPlan& pl, cudaStream_t st) {
             if (pl.timer) pl.timer->end(st);
             if (e != cudaSuccess) return e;
         }
+        // the FP32 local layer splits off (its per-point dot products dominate); with the
+        // INT8 GEMM the local term is a read of x2raw and the fused kernel is faster
+        const bool split = (C == 16 || C == 32 || C == 64) && !L.use_int8 && pl.x1f != nullptr;
         Layer1dArgs a;
         a.h_in = hin;
         a.h_out = hout;
@@ -462,6 +632,26 @@ cudaError_t fno1d_run(const Fno1dPlan& pl, cudaStream_t st) {
         a.G = R;
         a.modes = pl.modes;
         a.act = pl.act;
+        if (split) {
+            const size_t inv_smem = static_cast<size_t>(R) * N * sizeof(float2) +
+                                    static_cast<size_t>(R) * pl.modes * sizeof(float2);
+            if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(inv1d_kernel),
+                                          static_cast<int>(inv_smem))) != cudaSuccess)
+                return e;
+            if (pl.timer) pl.timer->begin("fno1d_inv", st);
+            inv1d_kernel<<<dim3(C / R, pl.B), 32 * R, inv_smem, st>>>(a, pl.x1f);
+            if (pl.timer) pl.timer->end(st);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            const int64_t total = static_cast<int64_t>(pl.B) * N;
+            const int grid = static_cast<int>(std::min<int64_t>((total + 127) / 128, sms * 8));
+            if (pl.timer) pl.timer->begin("fno1d_layer", st);
+            if (C == 16) local1d_kernel<16><<<grid, 128, 0, st>>>(a, pl.x1f, total);
+            else if (C == 32) local1d_kernel<32><<<grid, 128, 0, st>>>(a, pl.x1f, total);
+            else local1d_kernel<64><<<grid, 128, 0, st>>>(a, pl.x1f, total);
+            if (pl.timer) pl.timer->end(st);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            continue;
+        }
         if (pl.timer) pl.timer->begin("fno1d_layer", st);
         layer1d_kernel<<<dim3(C / R, pl.B), 256, layer_smem, st>>>(a);
         if (pl.timer) pl.timer->end(st);

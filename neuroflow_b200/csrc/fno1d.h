@@ -66,6 +66,7 @@ struct Fno1dPlan {
     void* h[2];              // ping-pong activations (B, N, C): int8 codes or fp32
     float2* Xs;              // (B, C, modes) truncated spectra
     float* x2raw;            // (B*N, C) INT8 GEMM output (dequantised, before the bias)
+    float* x1f;              // (B, C, N) spectral branch of the split layer, or null
     unsigned* err;
     KernelTimer* timer;
 };

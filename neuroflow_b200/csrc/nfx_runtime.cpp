@@ -229,7 +229,7 @@ struct nfx_runtime {
     nfx::Fno1dPlan plan1{};
     int pt_n[nfx::kFno1dMaxLayers] = {};   // per-token table sizes (locs.i.output)
     int pt_w[nfx::kFno1dMaxLayers] = {};
-    void* f1_bufs[4] = {nullptr, nullptr, nullptr, nullptr};  // h0, h1, Xs, x2raw
+    void* f1_bufs[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // h0, h1, Xs, x2raw, x1f
     int64_t f1_cap_BN = 0;                // B * N the buffers hold
     float2* f1_tw[2] = {nullptr, nullptr};
     int f1_tw_N = 0;
@@ -1071,10 +1071,10 @@ int fno1d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
             if (p) cudaFree(p);
             p = nullptr;
         }
-        const size_t sizes[4] = {static_cast<size_t>(BN) * c.width * 4, static_cast<size_t>(BN) * c.width * 4,
+        const size_t sizes[5] = {static_cast<size_t>(BN) * c.width * 4, static_cast<size_t>(BN) * c.width * 4,
                                  static_cast<size_t>(B) * c.width * (c.modes > 0 ? c.modes : 1) * sizeof(float2),
-                                 static_cast<size_t>(BN) * c.width * 4};
-        for (int i = 0; i < 4; ++i)
+                                 static_cast<size_t>(BN) * c.width * 4, static_cast<size_t>(BN) * c.width * 4};
+        for (int i = 0; i < 5; ++i)
             if (!cuda_ok(rt, cudaMalloc(&rt->f1_bufs[i], sizes[i] + 256), "cudaMalloc activations"))
                 return NFX_INTERNAL;
         rt->f1_cap_BN = BN;
@@ -1091,6 +1091,7 @@ int fno1d_launch(nfx_runtime* rt, const float* dx, const int64_t* xs, float* dy,
     pl.h[1] = rt->f1_bufs[1];
     pl.Xs = static_cast<float2*>(rt->f1_bufs[2]);
     pl.x2raw = static_cast<float*>(rt->f1_bufs[3]);
+    pl.x1f = static_cast<float*>(rt->f1_bufs[4]);
     if (c.L == 0) pl.layer[0] = nfx::Fno1dLayer{};
     pl.err = nfx::device_error_word();
     if (!pl.err) return rt_fail(rt, NFX_INTERNAL, "no device error word");
