@@ -88,4 +88,61 @@ __device__ __forceinline__ void warp_fft_row_first(float2* a, int n, const float
     }
 }
 
+// ---------------------------------------------------------------------------
+// n = 1024 in registers: the butterflies and twiddles of warp_fft_row (so the same
+// results, bit for bit), with the row held as 32 complex values per lane.  Stages with
+// half <= 16 pair entries of one 32-entry block (lane l holds entries 32 l + j), stages
+// with half >= 32 pair entries 32 apart (lane l holds entries 32 j + l); the row passes
+// through shared memory at the start, once between the two layouts and at the end,
+// instead of once per stage.  The shared-memory row is kept in the swizzled order
+// fft1024_pos(i) = i ^ ((i >> 5) & 31), under which both layouts are read and written
+// without bank conflicts; callers index the row through fft1024_pos.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int fft1024_pos(int i) { return i ^ ((i >> 5) & 31); }
+
+template <bool INV>
+__device__ __forceinline__ void fft_butterfly(float2& u, float2& x, float2 w) {
+    float2 v;
+    if (INV) {
+        v.x = __fmaf_rn(x.x, w.x, -__fmul_rn(x.y, w.y));
+        v.y = __fmaf_rn(x.x, w.y, __fmul_rn(x.y, w.x));
+    } else {
+        v.x = __fsub_rn(__fmul_rn(x.x, w.x), __fmul_rn(x.y, w.y));
+        v.y = __fadd_rn(__fmul_rn(x.y, w.x), __fmul_rn(x.x, w.y));
+    }
+    const float2 a0 = make_float2(__fadd_rn(u.x, v.x), __fadd_rn(u.y, v.y));
+    x = make_float2(__fsub_rn(u.x, v.x), __fsub_rn(u.y, v.y));
+    u = a0;
+}
+
+template <bool INV>
+__device__ __forceinline__ void warp_fft1024(float2* a, const float2* __restrict__ tw, int lane) {
+    float2 v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = a[fft1024_pos(32 * lane + j)];
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+        const int half = 1 << s;
+#pragma unroll
+        for (int j0 = 0; j0 < 32; ++j0)
+            if ((j0 & half) == 0) fft_butterfly<INV>(v[j0], v[j0 + half], __ldg(tw + (half - 1) + (j0 & (half - 1))));
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) a[fft1024_pos(32 * lane + j)] = v[j];
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = a[fft1024_pos(32 * j + lane)];
+#pragma unroll
+    for (int s = 0; s < 5; ++s) {
+        const int h = 1 << s, half = 32 << s;
+#pragma unroll
+        for (int j0 = 0; j0 < 32; ++j0)
+            if ((j0 & h) == 0)
+                fft_butterfly<INV>(v[j0], v[j0 + h], __ldg(tw + (half - 1) + 32 * (j0 & (h - 1)) + lane));
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) a[fft1024_pos(32 * j + lane)] = v[j];
+    __syncwarp();
+}
+
 }  // namespace nfx

@@ -92,11 +92,18 @@ __global__ void __launch_bounds__(256) fft1d_fwd_kernel(const void* __restrict__
     for (int t = threadIdx.x; t < N * R; t += blockDim.x) {
         const int p = t / R, r = t - (t / R) * R;
         const float v = act_value(h, (static_cast<int64_t>(b) * N + p) * C + c0 + r, codes, s, zpf);
-        sa[r * N + bit_reverse(p, log2N)] = make_float2(v, 0.0f);
+        const int q = bit_reverse(p, log2N);
+        sa[r * N + (N == 1024 ? fft1024_pos(q) : q)] = make_float2(v, 0.0f);
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float2* row = sa + warp * N;
+    if (N == 1024) {
+        warp_fft1024<false>(row, tw, lane);
+        for (int m = lane; m < modes; m += 32)
+            Xs[(static_cast<int64_t>(b) * C + c0 + warp) * modes + m] = row[fft1024_pos(m)];
+        return;
+    }
     warp_fft_row_first<false>(row, N, tw, lane, modes);
     for (int m = lane; m < modes; m += 32)
         Xs[(static_cast<int64_t>(b) * C + c0 + warp) * modes + m] = row[m];
@@ -161,10 +168,12 @@ __global__ void __launch_bounds__(256) layer1d_kernel(Layer1dArgs a) {
                 const float2 u = i < modes ? sY[r * modes + i] : make_float2(0.0f, 0.0f);
                 v = make_float2(u.x, -u.y);
             }
-            row[bit_reverse(j, a.log2N)] = v;
+            const int q = bit_reverse(j, a.log2N);
+            row[N == 1024 ? fft1024_pos(q) : q] = v;
         }
         __syncwarp();
-        warp_fft_row<true>(row, N, a.tw_inv, lane);
+        if (N == 1024) warp_fft1024<true>(row, a.tw_inv, lane);
+        else warp_fft_row<true>(row, N, a.tw_inv, lane);
     }
     __syncthreads();
 
@@ -229,7 +238,7 @@ __global__ void __launch_bounds__(256) layer1d_kernel(Layer1dArgs a) {
             } else if (L.fq_kind == 3) {
                 v = fp8_log2_snap(v, L.fq_s);
             }
-            const float x1 = __fmul_rn(sRow[static_cast<size_t>(r) * N + p].x, inv_n);
+            const float x1 = __fmul_rn(sRow[static_cast<size_t>(r) * N + (N == 1024 ? fft1024_pos(p) : p)].x, inv_n);
             const float z = __fadd_rn(x1, v);
             if (L.out_codes) {
                 const int q = L.lut_cells > 0
@@ -291,12 +300,14 @@ __global__ void __launch_bounds__(256) inv1d_kernel(Layer1dArgs a, float* __rest
                 const float2 u = i < modes ? sY[r * modes + i] : make_float2(0.0f, 0.0f);
                 v = make_float2(u.x, -u.y);
             }
-            row[bit_reverse(j, a.log2N)] = v;
+            const int q = bit_reverse(j, a.log2N);
+            row[N == 1024 ? fft1024_pos(q) : q] = v;
         }
         __syncwarp();
-        warp_fft_row<true>(row, N, a.tw_inv, lane);
+        if (N == 1024) warp_fft1024<true>(row, a.tw_inv, lane);
+        else warp_fft_row<true>(row, N, a.tw_inv, lane);
         float* dst = x1f + (static_cast<int64_t>(b) * C + o0 + r) * N;
-        for (int p = lane; p < N; p += 32) dst[p] = __fmul_rn(row[p].x, inv_n);
+        for (int p = lane; p < N; p += 32) dst[p] = __fmul_rn(row[N == 1024 ? fft1024_pos(p) : p].x, inv_n);
     }
 }
 
