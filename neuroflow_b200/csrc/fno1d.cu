@@ -336,31 +336,28 @@ __global__ void __launch_bounds__(128) local1d_kernel(Layer1dArgs a, const float
         if (f32) {
 #pragma unroll
             for (int o = 0; o < C; ++o) acc[o] = sB[o];
+            // four input features per pass (a compact loop body keeps the code in the
+            // instruction cache)
 #pragma unroll 1
-            for (int k16 = 0; k16 < C / 16; ++k16) {
-                float hv[16];
+            for (int k4 = 0; k4 < C / 4; ++k4) {
+                float hv[4];
                 if (L.in_codes) {
-                    const uint4 q = *reinterpret_cast<const uint4*>(static_cast<const int8_t*>(a.h_in) + row * C + 16 * k16);
-                    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+                    const uint32_t w4 = *reinterpret_cast<const uint32_t*>(static_cast<const int8_t*>(a.h_in) + row * C + 4 * k4);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int8_t code = static_cast<int8_t>((w4[j >> 2] >> (8 * (j & 3))) & 0xFFu);
+                    for (int j = 0; j < 4; ++j) {
+                        const int8_t code = static_cast<int8_t>((w4 >> (8 * j)) & 0xFFu);
                         hv[j] = __fmul_rn(__fsub_rn(static_cast<float>(code), zpf_in), L.in_s);
                     }
                 } else {
-                    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(a.h_in) + row * C + 16 * k16);
-#pragma unroll
-                    for (int j4 = 0; j4 < 4; ++j4) {
-                        const float4 v = src[j4];
-                        hv[4 * j4] = v.x;
-                        hv[4 * j4 + 1] = v.y;
-                        hv[4 * j4 + 2] = v.z;
-                        hv[4 * j4 + 3] = v.w;
-                    }
+                    const float4 v = *reinterpret_cast<const float4*>(static_cast<const float*>(a.h_in) + row * C + 4 * k4);
+                    hv[0] = v.x;
+                    hv[1] = v.y;
+                    hv[2] = v.z;
+                    hv[3] = v.w;
                 }
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int k = 16 * k16 + j;
+                for (int j = 0; j < 4; ++j) {
+                    const int k = 4 * k4 + j;
                     const bool fused = k >= nu;
 #pragma unroll
                     for (int o4 = 0; o4 < C / 4; ++o4) {
