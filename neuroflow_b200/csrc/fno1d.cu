@@ -124,7 +124,7 @@ struct Layer1dArgs {
     int N, log2N, C, G, modes, act;
 };
 
-__global__ void __launch_bounds__(256) layer1d_kernel(Layer1dArgs a) {
+__global__ void __launch_bounds__(256, 2) layer1d_kernel(Layer1dArgs a) {
     extern __shared__ float2 smem[];
     const int G = a.G, N = a.N, C = a.C, modes = a.modes;
     float2* sRow = smem;
@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(256) layer1d_kernel(Layer1dArgs a) {
 // operations layer1d_kernel applies, in the same order; the input row is read once per
 // point instead of once per output-channel group.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) inv1d_kernel(Layer1dArgs a, float* __restrict__ x1f) {
+__global__ void __launch_bounds__(256, 2) inv1d_kernel(Layer1dArgs a, float* __restrict__ x1f) {
     extern __shared__ float2 smem[];
     const int G = a.G, N = a.N, C = a.C, modes = a.modes;
     float2* sRow = smem;
