@@ -512,6 +512,87 @@ __global__ void __launch_bounds__(kProjThreads) proj1d_tiled_kernel(
     }
 }
 
+// The same tiled projection with the width and the output-channel count as template
+// parameters (C in {16, 32, 64, 128}, 1 <= OUT <= 4): the rows are staged one warp per
+// row (the sample index divided out once per row), the dot products' rounding split is
+// a compile-time constant, and the proj_out sums run over exactly OUT accumulators with
+// the weights in shared memory.  Element for element the arithmetic of
+// proj1d_tiled_kernel.
+template <int C, int OUT>
+__global__ void __launch_bounds__(kProjThreads) proj1d_tiled_t_kernel(
+    const float* __restrict__ h, int n, int N, int64_t total, const float* __restrict__ pq_w,
+    const float* __restrict__ pq_b, const float* __restrict__ po_w, const float* __restrict__ po_b, int act,
+    float* __restrict__ y) {
+    extern __shared__ float sh[];
+    float* sH = sh;                                 // [TP][C]
+    float* sWt = sH + kProjTP * C;                  // [C][C]: sWt[k * C + c] = pq_w[c][k]
+    float* sQ = sWt + C * C;                        // [TP][C + 1]
+    __shared__ float sPo[OUT * C];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int t = tid; t < C * C; t += kProjThreads) sWt[(t % C) * C + t / C] = __ldg(pq_w + t);
+    for (int t = tid; t < OUT * C; t += kProjThreads) sPo[t] = __ldg(po_w + t);
+    constexpr int nu = linear_unfused_len(C);
+    constexpr int G = C <= kProjThreads ? kProjThreads / C : 1;  // point groups
+    for (int64_t t0 = static_cast<int64_t>(blockIdx.x) * kProjTP; t0 < total;
+         t0 += static_cast<int64_t>(gridDim.x) * kProjTP) {
+        const int np = static_cast<int>(total - t0 < kProjTP ? total - t0 : kProjTP);
+        __syncthreads();  // the previous tile's sH / sQ are no longer read
+        for (int r = warp; r < np; r += kProjThreads / 32) {
+            const int64_t t = t0 + r;
+            const int64_t b = t / n;
+            const int pp = static_cast<int>(t - b * n);
+            const float* src = h + (b * N + pp) * C;
+#pragma unroll
+            for (int k = lane; k < C; k += 32) sH[r * C + k] = src[k];
+        }
+        __syncthreads();
+        for (int item = tid; item < C * G; item += kProjThreads) {
+            const int c = item % C, g = item / C;
+            const float bias = __ldg(pq_b + c);
+            for (int r0 = g * kProjILP; r0 < np; r0 += kProjILP * G) {
+                float q[kProjILP];
+                const float* hr[kProjILP];
+#pragma unroll
+                for (int u = 0; u < kProjILP; ++u) {
+                    q[u] = bias;
+                    hr[u] = sH + (r0 + u < np ? r0 + u : r0) * C;
+                }
+#pragma unroll 8
+                for (int k = 0; k < nu; ++k) {
+                    const float wv = sWt[k * C + c];
+#pragma unroll
+                    for (int u = 0; u < kProjILP; ++u) q[u] = __fadd_rn(q[u], __fmul_rn(hr[u][k], wv));
+                }
+#pragma unroll 8
+                for (int k = nu; k < C; ++k) {
+                    const float wv = sWt[k * C + c];
+#pragma unroll
+                    for (int u = 0; u < kProjILP; ++u) q[u] = __fmaf_rn(hr[u][k], wv, q[u]);
+                }
+#pragma unroll
+                for (int u = 0; u < kProjILP; ++u)
+                    if (r0 + u < np) sQ[(r0 + u) * (C + 1) + c] = act_f(q[u], act);
+            }
+        }
+        __syncthreads();
+        if (tid < np) {
+            const float* qr = sQ + tid * (C + 1);
+            float acc[OUT];
+#pragma unroll
+            for (int j = 0; j < OUT; ++j) acc[j] = __ldg(po_b + j);
+#pragma unroll 8
+            for (int c = 0; c < C; ++c) {
+                const float qv = qr[c];
+#pragma unroll
+                for (int j = 0; j < OUT; ++j) acc[j] = linear_step(acc[j], qv, sPo[j * C + c], c >= nu);
+            }
+            float* yr = y + (t0 + tid) * OUT;
+#pragma unroll
+            for (int j = 0; j < OUT; ++j) yr[j] = acc[j];
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // projection (fno.cpp:683-702): q = Linear(h, proj_q) -> act -> y = Linear(q, proj_out),
 // both the reference's sequential dot product from the bias (linear_step), the proj_out
@@ -674,9 +755,25 @@ cudaError_t fno1d_run(const Fno1dPlan& pl, cudaStream_t st) {
         const int per_sm = smem <= 56 * 1024 ? 4 : (smem <= 112 * 1024 ? 2 : 1);
         const int grid = static_cast<int>(std::min<int64_t>((total + kProjTP - 1) / kProjTP, sms * per_sm * 2));
         if (pl.timer) pl.timer->begin("fno1d_proj", st);
-        proj1d_tiled_kernel<<<grid, kProjThreads, smem, st>>>(static_cast<const float*>(pl.h[pl.L & 1]), pl.n, N,
-                                                              C, pl.out_ch, total, pl.pq_w, pl.pq_b, pl.po_w,
-                                                              pl.po_b, pl.act, pl.y);
+        const float* hl = static_cast<const float*>(pl.h[pl.L & 1]);
+        bool done = false;
+#define NFX_PROJ1D(CC, OO)                                                                                 \
+    if (!done && C == CC && pl.out_ch == OO) {                                                             \
+        if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(proj1d_tiled_t_kernel<CC, OO>),         \
+                                      static_cast<int>(smem))) != cudaSuccess)                             \
+            return e;                                                                                      \
+        proj1d_tiled_t_kernel<CC, OO><<<grid, kProjThreads, smem, st>>>(hl, pl.n, N, total, pl.pq_w, pl.pq_b, \
+                                                                        pl.po_w, pl.po_b, pl.act, pl.y);    \
+        done = true;                                                                                       \
+    }
+        NFX_PROJ1D(16, 1) NFX_PROJ1D(32, 1) NFX_PROJ1D(64, 1) NFX_PROJ1D(128, 1)
+        NFX_PROJ1D(16, 2) NFX_PROJ1D(32, 2) NFX_PROJ1D(64, 2) NFX_PROJ1D(128, 2)
+        NFX_PROJ1D(16, 3) NFX_PROJ1D(32, 3) NFX_PROJ1D(64, 3) NFX_PROJ1D(128, 3)
+        NFX_PROJ1D(16, 4) NFX_PROJ1D(32, 4) NFX_PROJ1D(64, 4) NFX_PROJ1D(128, 4)
+#undef NFX_PROJ1D
+        if (!done)
+            proj1d_tiled_kernel<<<grid, kProjThreads, smem, st>>>(hl, pl.n, N, C, pl.out_ch, total, pl.pq_w, pl.pq_b,
+                                                                  pl.po_w, pl.po_b, pl.act, pl.y);
         if (pl.timer) pl.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     } else {
