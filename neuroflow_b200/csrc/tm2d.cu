@@ -725,12 +725,19 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_const
                 if (cc < nk) mx4[cc & 3] = fmaxf(mx4[cc & 3], __uint_as_float(sv[cc]));
             const float m_new = fmaxf(m, fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])));
             const float alpha = m == -INFINITY ? 0.0f : exp2f((m - m_new) * c2);
+            // the exponentials of S_j first (they overlap the MMA of P_{j-1} V_{j-1})
+            float sum4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int cc = 0; cc < 64; ++cc) {
+                const float p = cc < nk ? exp2f((__uint_as_float(sv[cc]) - m_new) * c2) : 0.0f;
+                sum4[cc & 3] += p;
+                sv[cc] = __float_as_uint(p);
+            }
             // P_{j-1} has been consumed once O_{j-1} is ready: take it, then write P_j
             if (j > 0 && !take_o(j - 1)) {
                 ok = false;
                 break;
             }
-            float sum4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
             for (int blk = 0; blk < 2; ++blk) {
 #pragma unroll
@@ -738,9 +745,7 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_const
                     float ph4[4], pl4[4];
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const int cc = blk * 32 + c4 * 4 + u;
-                        const float p = cc < nk ? exp2f((__uint_as_float(sv[cc]) - m_new) * c2) : 0.0f;
-                        sum4[u] += p;
+                        const float p = __uint_as_float(sv[blk * 32 + c4 * 4 + u]);
                         ph4[u] = __uint_as_float(__float_as_uint(p) & 0xFFFFE000u);
                         pl4[u] = p - ph4[u];
                     }
