@@ -209,7 +209,9 @@ struct Layer2dArgs {
 // OBS: calibration observers compiled in; I8: the INT8 composition (int8 Linear and /
 // or the output snap) compiled in.  The plain FP32 network runs the <false, false>
 // instantiation, with neither in its loops.
-template <bool OBS, bool I8>
+// NJ = max(1, Wp / 32): the groups of 32 points a lane covers, a compile-time count so
+// the local Linear's loops carry no idle iterations.
+template <bool OBS, bool I8, int NJ>
 __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
     extern __shared__ float2 sm[];
     const int Wp = a.Wp, C = a.C, Hp = a.Hp;
@@ -239,7 +241,6 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
     }
     const float invW = __fdiv_rn(1.0f, static_cast<float>(Wp));
     const int nu = linear_unfused_len(C);
-    const int nj = Wp / 32 > 0 ? Wp / 32 : 1;
     Obs ob;
     for (int o0 = 0; o0 < C; o0 += kChunk) {
         // row pass of Irfft2 (fft.cpp:86-99) for kChunk output channels
@@ -267,45 +268,45 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
             const int r = warp * 2 + rr;
             const int o = o0 + r;
             if (o >= C) break;
-            float acc[kMaxWp / 32];
+            float acc[NJ];
             const float bias = __ldg(a.loc_b + o);
             if (i8) {
                 // exact integer dot product of codes and (w - zp_w), then the epilogue
 #pragma unroll
-                for (int j = 0; j < kMaxWp / 32; ++j) acc[j] = 0.0f;
+                for (int j = 0; j < NJ; ++j) acc[j] = 0.0f;
                 const float* wrow = a.i8.wz + static_cast<int64_t>(o) * C;
                 for (int k = 0; k < C; ++k) {
                     const float wv = __ldg(wrow + k);
                     const float* hk = sH + static_cast<size_t>(k) * Wp;
 #pragma unroll
-                    for (int j = 0; j < kMaxWp / 32; ++j)
-                        if (j < nj && lane + 32 * j < Wp) acc[j] = __fmaf_rn(hk[lane + 32 * j], wv, acc[j]);
+                    for (int j = 0; j < NJ; ++j)
+                        if (NJ > 1 || lane < Wp) acc[j] = __fmaf_rn(hk[lane + 32 * j], wv, acc[j]);
                 }
                 const int4 cc = __ldg(a.i8.cols + o);
 #pragma unroll
-                for (int j = 0; j < kMaxWp / 32; ++j)
-                    if (j < nj && lane + 32 * j < Wp) {
+                for (int j = 0; j < NJ; ++j)
+                    if (NJ > 1 || lane < Wp) {
                         const int v = __float2int_rn(acc[j]) - cc.y * __float2int_rn(sSum[lane + 32 * j]) + cc.z;
                         const float y = __fadd_rn(__fmul_rn(__int_as_float(cc.x), __int2float_rn(v)), 0.0f);
                         acc[j] = __fadd_rn(y, bias);
                     }
             } else {
 #pragma unroll
-                for (int j = 0; j < kMaxWp / 32; ++j) acc[j] = bias;
+                for (int j = 0; j < NJ; ++j) acc[j] = bias;
                 const float* wrow = a.loc_w + static_cast<int64_t>(o) * C;
                 for (int k = 0; k < C; ++k) {
                     const float wv = __ldg(wrow + k);
                     const float* hk = sH + static_cast<size_t>(k) * Wp;
 #pragma unroll
-                    for (int j = 0; j < kMaxWp / 32; ++j)
-                        if (j < nj && lane + 32 * j < Wp) acc[j] = linear_step(acc[j], hk[lane + 32 * j], wv, k >= nu);
+                    for (int j = 0; j < NJ; ++j)
+                        if (NJ > 1 || lane < Wp) acc[j] = linear_step(acc[j], hk[lane + 32 * j], wv, k >= nu);
                 }
             }
             float* dst = a.hout + ((static_cast<int64_t>(b) * C + o) * Hp + hh) * Wp;
 #pragma unroll
-            for (int j = 0; j < kMaxWp / 32; ++j) {
+            for (int j = 0; j < NJ; ++j) {
                 const int w = lane + 32 * j;
-                if (j < nj && w < Wp) {
+                if (NJ > 1 || w < Wp) {
                     if (OBS) {
                         ob.see(acc[j]);
                         if (a.obs_vals) a.obs_vals[((static_cast<int64_t>(b) * Hp + hh) * Wp + w) * C + o] = acc[j];
@@ -329,6 +330,17 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
         __syncthreads();
     }
     if (OBS) ob.flush(a.obs, a.obs_i);
+}
+
+template <bool OBS, bool I8>
+void (*layer2d_pick(int Wp))(Layer2dArgs) {
+    switch (Wp >= 32 ? Wp / 32 : 1) {
+        case 1: return layer2d_kernel<OBS, I8, 1>;
+        case 2: return layer2d_kernel<OBS, I8, 2>;
+        case 4: return layer2d_kernel<OBS, I8, 4>;
+        case 8: return layer2d_kernel<OBS, I8, 8>;
+        default: return layer2d_kernel<OBS, I8, 16>;
+    }
 }
 
 // projection (fno.cpp:966-993): one unpadded point per thread, its channel column
@@ -458,8 +470,8 @@ cudaError_t fno2d_f32_run(const Fno2dF32Plan& p, cudaStream_t st) {
     const bool obs = p.obs != nullptr;
     bool i8 = p.pq_i8.wz != nullptr || p.pq_act_table != nullptr;
     for (int i = 0; i < p.L; ++i) i8 = i8 || p.layer[i].i8.wz != nullptr || p.layer[i].snap.fq.kind != 0;
-    auto layer_k = obs ? (i8 ? layer2d_kernel<true, true> : layer2d_kernel<true, false>)
-                       : (i8 ? layer2d_kernel<false, true> : layer2d_kernel<false, false>);
+    auto layer_k = obs ? (i8 ? layer2d_pick<true, true>(p.Wp) : layer2d_pick<true, false>(p.Wp))
+                       : (i8 ? layer2d_pick<false, true>(p.Wp) : layer2d_pick<false, false>(p.Wp));
     auto proj_k = obs ? (i8 ? proj2d_f32_kernel<true, true> : proj2d_f32_kernel<true, false>)
                       : (i8 ? proj2d_f32_kernel<false, true> : proj2d_f32_kernel<false, false>);
     if ((e = set_max_dynamic_smem(reinterpret_cast<const void*>(layer_k), static_cast<int>(sl))) != cudaSuccess)
