@@ -420,6 +420,67 @@ __global__ void __launch_bounds__(128) proj2d_f32_kernel(Fno2dF32Plan p, const f
     }
 }
 
+// The plain FP32 projection (no observers, no INT8 composition) for widths 32 and 64
+// with 1 to 4 output channels: the point's C inputs in registers (coalesced channel
+// loads), proj_q rows as 16-byte broadcasts from shared memory, exactly OUT proj_out
+// sums.  Element for element proj2d_f32_kernel<false, false>'s arithmetic.
+template <int C, int OUT>
+__global__ void __launch_bounds__(128) proj2d_f32_fast_kernel(Fno2dF32Plan p, const float* __restrict__ h) {
+    __shared__ float4 sW4[C * C / 4];   // proj_q, [c][k]
+    __shared__ float sPo[OUT * C];
+    __shared__ float sB[C];
+    for (int i = threadIdx.x; i < C * C; i += blockDim.x) reinterpret_cast<float*>(sW4)[i] = __ldg(p.pq_w + i);
+    for (int i = threadIdx.x; i < OUT * C; i += blockDim.x) sPo[i] = __ldg(p.po_w + i);
+    for (int i = threadIdx.x; i < C; i += blockDim.x) sB[i] = __ldg(p.pq_b + i);
+    __syncthreads();
+    const int64_t total = static_cast<int64_t>(p.B) * p.H * p.W;
+    constexpr int nu = linear_unfused_len(C);
+    const int64_t plane = static_cast<int64_t>(p.Hp) * p.Wp;
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int ww = static_cast<int>(t % p.W);
+        const int64_t r = t / p.W;
+        const int hh = static_cast<int>(r % p.H);
+        const int64_t b = r / p.H;
+        const float* src = h + b * C * plane + static_cast<int64_t>(hh) * p.Wp + ww;
+        float x[C];
+#pragma unroll
+        for (int k = 0; k < C; ++k) x[k] = src[k * plane];
+        float acc[OUT];
+#pragma unroll
+        for (int j = 0; j < OUT; ++j) acc[j] = __ldg(p.po_b + j);
+#pragma unroll 1
+        for (int c = 0; c < C; ++c) {
+            float q = sB[c];
+#pragma unroll
+            for (int k4 = 0; k4 < C / 4; ++k4) {
+                const float4 w = sW4[c * (C / 4) + k4];
+                q = linear_step(q, x[4 * k4 + 0], w.x, 4 * k4 + 0 >= nu);
+                q = linear_step(q, x[4 * k4 + 1], w.y, 4 * k4 + 1 >= nu);
+                q = linear_step(q, x[4 * k4 + 2], w.z, 4 * k4 + 2 >= nu);
+                q = linear_step(q, x[4 * k4 + 3], w.w, 4 * k4 + 3 >= nu);
+            }
+            q = act_f(apply_fq(q, p.fq_pq), p.act);
+#pragma unroll
+            for (int j = 0; j < OUT; ++j) acc[j] = linear_step(acc[j], q, sPo[j * C + c], c >= nu);
+        }
+        float* yr = p.y + t * OUT;
+#pragma unroll
+        for (int j = 0; j < OUT; ++j) yr[j] = apply_fq(acc[j], p.fq_po);
+    }
+}
+
+template <int C>
+void (*proj2d_fast_pick(int out_ch))(Fno2dF32Plan, const float*) {
+    switch (out_ch) {
+        case 1: return proj2d_f32_fast_kernel<C, 1>;
+        case 2: return proj2d_f32_fast_kernel<C, 2>;
+        case 3: return proj2d_f32_fast_kernel<C, 3>;
+        case 4: return proj2d_f32_fast_kernel<C, 4>;
+        default: return nullptr;
+    }
+}
+
 size_t fwd_smem(int Hp, int Wp, int MW) {
     return (8 * static_cast<size_t>(Wp) + static_cast<size_t>(MW) * Hp) * sizeof(float2);
 }
@@ -520,8 +581,13 @@ cudaError_t fno2d_f32_run(const Fno2dF32Plan& p, cudaStream_t st) {
             cudaSuccess)
             return e;
         const int grid = static_cast<int>(std::min<int64_t>((total + threads - 1) / threads, sms * 8));
+        void (*fast)(Fno2dF32Plan, const float*) = nullptr;
+        if (!obs && !i8) fast = p.C == 64 ? proj2d_fast_pick<64>(p.out_ch) : p.C == 32 ? proj2d_fast_pick<32>(p.out_ch) : nullptr;
         if (p.timer) p.timer->begin("fno2d_f32_proj", st);
-        proj_k<<<grid, threads, smem, st>>>(p, p.h[p.L & 1]);
+        if (fast)
+            fast<<<grid, 128, 0, st>>>(p, p.h[p.L & 1]);
+        else
+            proj_k<<<grid, threads, smem, st>>>(p, p.h[p.L & 1]);
         if (p.timer) p.timer->end(st);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
