@@ -262,45 +262,64 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
             warp_fft_row<true>(row, Wp, a.twi_w, lane);
         }
         __syncthreads();
-        // local Linear of the row's points for this chunk: warp -> 2 output channels,
-        // lane -> points lane + 32 j
-        for (int rr = 0; rr < 2; ++rr) {
-            const int r = warp * 2 + rr;
+        // local Linear of the row's points for this chunk: warp -> R output channels,
+        // lane -> points lane + 32 j; one shared-memory load of a point's input feeds
+        // all R channels (each channel's sum keeps the k order)
+        constexpr int R = kChunk / 8;
+        float acc[R][NJ];
+        const float* wrow[R];
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+            const int o = min(o0 + warp * R + rr, C - 1);
+            wrow[rr] = (i8 ? a.i8.wz : a.loc_w) + static_cast<int64_t>(o) * C;
+            const float bias = i8 ? 0.0f : __ldg(a.loc_b + o);
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) acc[rr][j] = bias;
+        }
+        if (i8) {
+            // exact integer dot product of codes and (w - zp_w)
+            for (int k = 0; k < C; ++k) {
+                const float* hk = sH + static_cast<size_t>(k) * Wp;
+                float hv[NJ];
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) hv[j] = (NJ > 1 || lane < Wp) ? hk[lane + 32 * j] : 0.0f;
+#pragma unroll
+                for (int rr = 0; rr < R; ++rr) {
+                    const float wv = __ldg(wrow[rr] + k);
+#pragma unroll
+                    for (int j = 0; j < NJ; ++j) acc[rr][j] = __fmaf_rn(hv[j], wv, acc[rr][j]);
+                }
+            }
+        } else {
+            for (int k = 0; k < C; ++k) {
+                const float* hk = sH + static_cast<size_t>(k) * Wp;
+                float hv[NJ];
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) hv[j] = (NJ > 1 || lane < Wp) ? hk[lane + 32 * j] : 0.0f;
+#pragma unroll
+                for (int rr = 0; rr < R; ++rr) {
+                    const float wv = __ldg(wrow[rr] + k);
+#pragma unroll
+                    for (int j = 0; j < NJ; ++j) acc[rr][j] = linear_step(acc[rr][j], hv[j], wv, k >= nu);
+                }
+            }
+        }
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+            const int r = warp * R + rr;
             const int o = o0 + r;
             if (o >= C) break;
-            float acc[NJ];
-            const float bias = __ldg(a.loc_b + o);
             if (i8) {
-                // exact integer dot product of codes and (w - zp_w), then the epilogue
-#pragma unroll
-                for (int j = 0; j < NJ; ++j) acc[j] = 0.0f;
-                const float* wrow = a.i8.wz + static_cast<int64_t>(o) * C;
-                for (int k = 0; k < C; ++k) {
-                    const float wv = __ldg(wrow + k);
-                    const float* hk = sH + static_cast<size_t>(k) * Wp;
-#pragma unroll
-                    for (int j = 0; j < NJ; ++j)
-                        if (NJ > 1 || lane < Wp) acc[j] = __fmaf_rn(hk[lane + 32 * j], wv, acc[j]);
-                }
+                // the epilogue of the integer sums
+                const float bias = __ldg(a.loc_b + o);
                 const int4 cc = __ldg(a.i8.cols + o);
 #pragma unroll
                 for (int j = 0; j < NJ; ++j)
                     if (NJ > 1 || lane < Wp) {
-                        const int v = __float2int_rn(acc[j]) - cc.y * __float2int_rn(sSum[lane + 32 * j]) + cc.z;
+                        const int v = __float2int_rn(acc[rr][j]) - cc.y * __float2int_rn(sSum[lane + 32 * j]) + cc.z;
                         const float y = __fadd_rn(__fmul_rn(__int_as_float(cc.x), __int2float_rn(v)), 0.0f);
-                        acc[j] = __fadd_rn(y, bias);
+                        acc[rr][j] = __fadd_rn(y, bias);
                     }
-            } else {
-#pragma unroll
-                for (int j = 0; j < NJ; ++j) acc[j] = bias;
-                const float* wrow = a.loc_w + static_cast<int64_t>(o) * C;
-                for (int k = 0; k < C; ++k) {
-                    const float wv = __ldg(wrow + k);
-                    const float* hk = sH + static_cast<size_t>(k) * Wp;
-#pragma unroll
-                    for (int j = 0; j < NJ; ++j)
-                        if (NJ > 1 || lane < Wp) acc[j] = linear_step(acc[j], hk[lane + 32 * j], wv, k >= nu);
-                }
             }
             float* dst = a.hout + ((static_cast<int64_t>(b) * C + o) * Hp + hh) * Wp;
 #pragma unroll
@@ -308,10 +327,10 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
                 const int w = lane + 32 * j;
                 if (NJ > 1 || w < Wp) {
                     if (OBS) {
-                        ob.see(acc[j]);
-                        if (a.obs_vals) a.obs_vals[((static_cast<int64_t>(b) * Hp + hh) * Wp + w) * C + o] = acc[j];
+                        ob.see(acc[rr][j]);
+                        if (a.obs_vals) a.obs_vals[((static_cast<int64_t>(b) * Hp + hh) * Wp + w) * C + o] = acc[rr][j];
                     }
-                    const float x2 = apply_fq(acc[j], a.fq);
+                    const float x2 = apply_fq(acc[rr][j], a.fq);
                     const float x1 = __fmul_rn(sX1[static_cast<size_t>(r) * Wp + w].x, invW);
                     const float z = __fadd_rn(x1, x2);
                     if (I8 && a.snap.fq.kind == 1) {
