@@ -172,3 +172,31 @@ def test_fno2d_int8_channel_counts(tmp_path, in_ch, out_ch):
     rt.run(x, got)
     st = _stats(got, want, m.qparams["proj_out.output"].scale)
     assert st["frac_diff"] == 0, st
+
+
+@pytest.mark.gpu
+def test_fno2d_int8_integers_beyond_two_pow_22(tmp_path):
+    """Weight codes far from their zero points (all 127 against zp_w = -128) and an
+    input zero point of -50: the projection's integers sum_k (a_k - zp_in)(w_k - 2 zp_w)
+    reach the millions (up to 64 * 177 * 383), against a few thousand in the calibrated
+    models, where an error in the zero-point terms the MMA folds in would show.  Every
+    output equals the oracle's."""
+    from neuroflow_b200.ir import PerTensor
+    from neuroflow_b200.runtime import InferenceRuntime
+    m, _ = _model(tmp_path, L=2, W=128)
+    m.weights["proj_q.weight"] = np.abs(m.weights["proj_q.weight"])
+    qp = m.qparams["proj_q.weight"]
+    qp.scales = np.full_like(qp.scales, 1e-7)
+    qp.zero_points = np.full_like(qp.zero_points, -128)
+    m.qparams["locs.1.output"] = PerTensor(m.qparams["locs.1.output"].scale, -50)
+    path = os.path.join(str(tmp_path), "wide_integers.nneuroir")
+    ir.write(path, m)
+    x = synth.fno2d_inputs(np.random.default_rng(21), 2, 32, 128)
+    want = Oracle().fno2d_forward(m, x, mode=1)
+    rt = InferenceRuntime(path)
+    rt.enable_int8_gemm()
+    got = np.zeros_like(want)
+    rt.run(x, got)
+    st = _stats(got, want, m.qparams["proj_out.output"].scale)
+    print(st)
+    assert st["frac_diff"] == 0, st
