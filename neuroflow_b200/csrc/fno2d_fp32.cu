@@ -29,6 +29,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <type_traits>
 
 #include "fft_exact.cuh"
 #include "fno2d.h"
@@ -291,18 +292,24 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
                 }
             }
         } else {
-            for (int k = 0; k < C; ++k) {
-                const float* hk = sH + static_cast<size_t>(k) * Wp;
-                float hv[NJ];
+            // the reference's unfused products (k < nu) and fused tail as two loops, so
+            // neither carries the other's form
+            auto steps = [&](auto fused, int k0, int k1) {
+                for (int k = k0; k < k1; ++k) {
+                    const float* hk = sH + static_cast<size_t>(k) * Wp;
+                    float hv[NJ];
 #pragma unroll
-                for (int j = 0; j < NJ; ++j) hv[j] = (NJ > 1 || lane < Wp) ? hk[lane + 32 * j] : 0.0f;
+                    for (int j = 0; j < NJ; ++j) hv[j] = (NJ > 1 || lane < Wp) ? hk[lane + 32 * j] : 0.0f;
 #pragma unroll
-                for (int rr = 0; rr < R; ++rr) {
-                    const float wv = __ldg(wrow[rr] + k);
+                    for (int rr = 0; rr < R; ++rr) {
+                        const float wv = __ldg(wrow[rr] + k);
 #pragma unroll
-                    for (int j = 0; j < NJ; ++j) acc[rr][j] = linear_step(acc[rr][j], hv[j], wv, k >= nu);
+                        for (int j = 0; j < NJ; ++j) acc[rr][j] = linear_step(acc[rr][j], hv[j], wv, decltype(fused)::value);
+                    }
                 }
-            }
+            };
+            steps(std::false_type{}, 0, nu);
+            steps(std::true_type{}, nu, C);
         }
 #pragma unroll
         for (int rr = 0; rr < R; ++rr) {

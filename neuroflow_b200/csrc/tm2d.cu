@@ -30,6 +30,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <type_traits>
 
 #include "nfx_internal.h"
 #include "numerics.cuh"
@@ -118,18 +119,24 @@ __global__ void __launch_bounds__(256) linear_f32_kernel(LinArgs a) {
         }
         __syncthreads();
         const int kend = min(kBK, a.K - k0);
-        for (int kk = 0; kk < kend; ++kk) {
-            const bool fused = k0 + kk >= nu;
-            float av[4], wv[4];
+        // the reference's unfused products (k < nu) and fused tail as separate loops
+        auto steps = [&](auto fused, int kb, int ke) {
+            for (int kk = kb; kk < ke; ++kk) {
+                float av[4], wv[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+                for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) wv[j] = Ws[kk][tx * 4 + j];
+                for (int j = 0; j < 4; ++j) wv[j] = Ws[kk][tx * 4 + j];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+                for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = linear_step(acc[i][j], av[i], wv[j], fused);
-        }
+                    for (int j = 0; j < 4; ++j)
+                        acc[i][j] = linear_step(acc[i][j], av[i], wv[j], decltype(fused)::value);
+            }
+        };
+        const int ksplit = min(kend, max(0, nu - k0));
+        steps(std::false_type{}, 0, ksplit);
+        steps(std::true_type{}, ksplit, kend);
         __syncthreads();
     }
 #pragma unroll
