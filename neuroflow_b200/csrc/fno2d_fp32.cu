@@ -303,8 +303,20 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
 #pragma unroll
                     for (int rr = 0; rr < R; ++rr) {
                         const float wv = __ldg(wrow[rr] + k);
+                        if constexpr (!decltype(fused)::value && NJ % 2 == 0) {
+                            // two rounded products per f32x2 instruction, each sum a
+                            // scalar rounded add
 #pragma unroll
-                        for (int j = 0; j < NJ; ++j) acc[rr][j] = linear_step(acc[rr][j], hv[j], wv, decltype(fused)::value);
+                            for (int j = 0; j < NJ; j += 2) {
+                                const float2 m = mul2_rn(make_float2(hv[j], hv[j + 1]), make_float2(wv, wv));
+                                acc[rr][j] = __fadd_rn(acc[rr][j], m.x);
+                                acc[rr][j + 1] = __fadd_rn(acc[rr][j + 1], m.y);
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < NJ; ++j)
+                                acc[rr][j] = linear_step(acc[rr][j], hv[j], wv, decltype(fused)::value);
+                        }
                     }
                 }
             };

@@ -128,10 +128,21 @@ __global__ void __launch_bounds__(256) linear_f32_kernel(LinArgs a) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) wv[j] = Ws[kk][tx * 4 + j];
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
+                for (int i = 0; i < 4; ++i) {
+                    if constexpr (!decltype(fused)::value) {
+                        // two rounded products per f32x2 instruction, each sum a scalar
+                        // rounded add
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        acc[i][j] = linear_step(acc[i][j], av[i], wv[j], decltype(fused)::value);
+                        for (int j = 0; j < 4; j += 2) {
+                            const float2 m = mul2_rn(make_float2(av[i], av[i]), make_float2(wv[j], wv[j + 1]));
+                            acc[i][j] = __fadd_rn(acc[i][j], m.x);
+                            acc[i][j + 1] = __fadd_rn(acc[i][j + 1], m.y);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(av[i], wv[j], acc[i][j]);
+                    }
+                }
             }
         };
         const int ksplit = min(kend, max(0, nu - k0));
