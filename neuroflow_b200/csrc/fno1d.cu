@@ -362,10 +362,21 @@ __global__ void __launch_bounds__(128) local1d_kernel(Layer1dArgs a, const float
 #pragma unroll
                     for (int o4 = 0; o4 < C / 4; ++o4) {
                         const float4 w = sW4[k * (C / 4) + o4];
-                        acc[4 * o4 + 0] = linear_step(acc[4 * o4 + 0], hv[j], w.x, fused);
-                        acc[4 * o4 + 1] = linear_step(acc[4 * o4 + 1], hv[j], w.y, fused);
-                        acc[4 * o4 + 2] = linear_step(acc[4 * o4 + 2], hv[j], w.z, fused);
-                        acc[4 * o4 + 3] = linear_step(acc[4 * o4 + 3], hv[j], w.w, fused);
+                        if (nu >= C) {
+                            // every product unfused (C a multiple of 8): two rounded
+                            // products per f32x2 instruction, each sum a scalar add
+                            const float2 m0 = mul2_rn(make_float2(hv[j], hv[j]), make_float2(w.x, w.y));
+                            const float2 m1 = mul2_rn(make_float2(hv[j], hv[j]), make_float2(w.z, w.w));
+                            acc[4 * o4 + 0] = __fadd_rn(acc[4 * o4 + 0], m0.x);
+                            acc[4 * o4 + 1] = __fadd_rn(acc[4 * o4 + 1], m0.y);
+                            acc[4 * o4 + 2] = __fadd_rn(acc[4 * o4 + 2], m1.x);
+                            acc[4 * o4 + 3] = __fadd_rn(acc[4 * o4 + 3], m1.y);
+                        } else {
+                            acc[4 * o4 + 0] = linear_step(acc[4 * o4 + 0], hv[j], w.x, fused);
+                            acc[4 * o4 + 1] = linear_step(acc[4 * o4 + 1], hv[j], w.y, fused);
+                            acc[4 * o4 + 2] = linear_step(acc[4 * o4 + 2], hv[j], w.z, fused);
+                            acc[4 * o4 + 3] = linear_step(acc[4 * o4 + 3], hv[j], w.w, fused);
+                        }
                     }
                 }
             }

@@ -794,10 +794,13 @@ __global__ void __launch_bounds__(128) local3d_kernel(Fno3dPlan p, Fno3dLayer L,
 #pragma unroll
                 for (int o4 = 0; o4 < C / 4; ++o4) {
                     const float4 w = sW4[k * (C / 4) + o4];
-                    acc[4 * o4 + 0] = __fadd_rn(acc[4 * o4 + 0], __fmul_rn(a, w.x));
-                    acc[4 * o4 + 1] = __fadd_rn(acc[4 * o4 + 1], __fmul_rn(a, w.y));
-                    acc[4 * o4 + 2] = __fadd_rn(acc[4 * o4 + 2], __fmul_rn(a, w.z));
-                    acc[4 * o4 + 3] = __fadd_rn(acc[4 * o4 + 3], __fmul_rn(a, w.w));
+                    // two rounded products per f32x2 instruction, each sum a scalar add
+                    const float2 m0 = mul2_rn(make_float2(a, a), make_float2(w.x, w.y));
+                    const float2 m1 = mul2_rn(make_float2(a, a), make_float2(w.z, w.w));
+                    acc[4 * o4 + 0] = __fadd_rn(acc[4 * o4 + 0], m0.x);
+                    acc[4 * o4 + 1] = __fadd_rn(acc[4 * o4 + 1], m0.y);
+                    acc[4 * o4 + 2] = __fadd_rn(acc[4 * o4 + 2], m1.x);
+                    acc[4 * o4 + 3] = __fadd_rn(acc[4 * o4 + 3], m1.y);
                 }
             }
         } else {
@@ -809,10 +812,20 @@ __global__ void __launch_bounds__(128) local3d_kernel(Fno3dPlan p, Fno3dLayer L,
 #pragma unroll
                 for (int o4 = 0; o4 < C / 4; ++o4) {
                     const float4 w = sW4[k * (C / 4) + o4];
-                    acc[4 * o4 + 0] = linear_step(acc[4 * o4 + 0], a, w.x, fused);
-                    acc[4 * o4 + 1] = linear_step(acc[4 * o4 + 1], a, w.y, fused);
-                    acc[4 * o4 + 2] = linear_step(acc[4 * o4 + 2], a, w.z, fused);
-                    acc[4 * o4 + 3] = linear_step(acc[4 * o4 + 3], a, w.w, fused);
+                    if (nu >= C) {
+                        // every product unfused: two per f32x2 instruction
+                        const float2 m0 = mul2_rn(make_float2(a, a), make_float2(w.x, w.y));
+                        const float2 m1 = mul2_rn(make_float2(a, a), make_float2(w.z, w.w));
+                        acc[4 * o4 + 0] = __fadd_rn(acc[4 * o4 + 0], m0.x);
+                        acc[4 * o4 + 1] = __fadd_rn(acc[4 * o4 + 1], m0.y);
+                        acc[4 * o4 + 2] = __fadd_rn(acc[4 * o4 + 2], m1.x);
+                        acc[4 * o4 + 3] = __fadd_rn(acc[4 * o4 + 3], m1.y);
+                    } else {
+                        acc[4 * o4 + 0] = linear_step(acc[4 * o4 + 0], a, w.x, fused);
+                        acc[4 * o4 + 1] = linear_step(acc[4 * o4 + 1], a, w.y, fused);
+                        acc[4 * o4 + 2] = linear_step(acc[4 * o4 + 2], a, w.z, fused);
+                        acc[4 * o4 + 3] = linear_step(acc[4 * o4 + 3], a, w.w, fused);
+                    }
                 }
             }
         }
