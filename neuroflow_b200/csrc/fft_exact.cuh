@@ -145,4 +145,57 @@ __device__ __forceinline__ void warp_fft1024(float2* a, const float2* __restrict
     __syncwarp();
 }
 
+// ---------------------------------------------------------------------------
+// n = 128 in registers, four complex values per lane: the butterflies and twiddles of
+// warp_fft_row (bit for bit).  In: v[m] = a[4 lane + m] of the bit-reversed row, so the
+// stages with half <= 2 pair a lane's own entries and those with half = 4, 8, 16 pair
+// entry m of lanes l and l ^ (half / 4) (exchanged by shuffles; both lanes evaluate the
+// butterfly and keep their output).  One pass through `scratch` (128 float2, the warp's
+// own; swizzled by fft128_pos so that neither layout has bank conflicts) turns the row
+// into v[j] = a[lane + 32 j] for the stages with half = 32 and 64.  Out: v[j] = the
+// transform's entry lane + 32 j.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int fft128_pos(int i) { return i ^ ((i >> 4) & 3); }
+
+// entry of the natural-order row that lands at bit-reversed position 4 lane + m
+__device__ __forceinline__ int fft128_src(int lane, int m) {
+    return static_cast<int>(__brev(static_cast<unsigned>(lane)) >> 27) + 32 * (((m & 1) << 1) | (m >> 1));
+}
+
+template <bool INV>
+__device__ __forceinline__ void warp_fft128_regs(float2 (&v)[4], float2* scratch, const float2* __restrict__ tw,
+                                                 int lane) {
+    const float2 w0 = __ldg(tw);
+    fft_butterfly<INV>(v[0], v[1], w0);
+    fft_butterfly<INV>(v[2], v[3], w0);
+    fft_butterfly<INV>(v[0], v[2], __ldg(tw + 1));
+    fft_butterfly<INV>(v[1], v[3], __ldg(tw + 2));
+#pragma unroll
+    for (int s = 1; s <= 4; s <<= 1) {
+        const int half = 4 * s;
+        const bool hi = (lane & s) != 0;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const float2 w = __ldg(tw + (half - 1) + ((4 * lane + m) & (half - 1)));
+            const float2 p = make_float2(__shfl_xor_sync(0xffffffffu, v[m].x, s),
+                                         __shfl_xor_sync(0xffffffffu, v[m].y, s));
+            float2 u = hi ? p : v[m];
+            float2 x = hi ? v[m] : p;
+            fft_butterfly<INV>(u, x, w);
+            v[m] = hi ? x : u;
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) scratch[fft128_pos(4 * lane + m)] = v[m];
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = scratch[fft128_pos(lane + 32 * j)];
+    __syncwarp();
+    const float2 w32 = __ldg(tw + 31 + lane);
+    fft_butterfly<INV>(v[0], v[1], w32);
+    fft_butterfly<INV>(v[2], v[3], w32);
+    fft_butterfly<INV>(v[0], v[2], __ldg(tw + 63 + lane));
+    fft_butterfly<INV>(v[1], v[3], __ldg(tw + 95 + lane));
+}
+
 }  // namespace nfx

@@ -126,13 +126,29 @@ __global__ void __launch_bounds__(256) fwd2d_kernel(const float* __restrict__ hi
     float2* row = sm + warp * Wp;
     float2* col = sm + 8 * Wp;
     const float* plane = hin + (static_cast<int64_t>(b) * C + c) * Hp * Wp;
-    for (int r = warp; r < Hp; r += 8) {
-        for (int j = lane; j < Wp; j += 32) row[bit_reverse(j, lgW)] = make_float2(plane[static_cast<int64_t>(r) * Wp + j], 0.0f);
-        __syncwarp();
-        warp_fft_row_first<false>(row, Wp, twf_w, lane, MW);
-        const int rr = bit_reverse(r, lgH);
-        for (int kw = lane; kw < MW; kw += 32) col[kw * Hp + rr] = row[kw];
-        __syncwarp();
+    if (Wp == 128) {
+        // rows in registers (warp_fft128_regs); the kept modes kw < MW are entries
+        // lane + 32 j of the result
+        for (int r = warp; r < Hp; r += 8) {
+            const float* src = plane + static_cast<int64_t>(r) * 128;
+            float2 v[4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) v[m] = make_float2(src[fft128_src(lane, m)], 0.0f);
+            warp_fft128_regs<false>(v, row, twf_w, lane);
+            const int rr = bit_reverse(r, lgH);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (lane + 32 * j < MW) col[(lane + 32 * j) * Hp + rr] = v[j];
+        }
+    } else {
+        for (int r = warp; r < Hp; r += 8) {
+            for (int j = lane; j < Wp; j += 32) row[bit_reverse(j, lgW)] = make_float2(plane[static_cast<int64_t>(r) * Wp + j], 0.0f);
+            __syncwarp();
+            warp_fft_row_first<false>(row, Wp, twf_w, lane, MW);
+            const int rr = bit_reverse(r, lgH);
+            for (int kw = lane; kw < MW; kw += 32) col[kw * Hp + rr] = row[kw];
+            __syncwarp();
+        }
     }
     __syncthreads();
     for (int kw = warp; kw < MW; kw += 8) {
@@ -243,30 +259,61 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
     const float invW = __fdiv_rn(1.0f, static_cast<float>(Wp));
     const int nu = linear_unfused_len(C);
     Obs ob;
+    constexpr int R = kChunk / 8;
+    // at Wp = 128 no chunk-wide barrier follows the row pass: the layer input (and
+    // sSum) must be visible before the first local Linear
+    if constexpr (NJ == 4) __syncthreads();
     for (int o0 = 0; o0 < C; o0 += kChunk) {
-        // row pass of Irfft2 (fft.cpp:86-99) for kChunk output channels
-        for (int r = warp; r < kChunk && o0 + r < C; r += 8) {
-            float2* row = sX1 + static_cast<size_t>(r) * Wp;
-            const float2* ci = a.colinv + ((static_cast<int64_t>(b) * C + o0 + r) * Hp + hh) * a.MW;
-            for (int j = lane; j < Wp; j += 32) {
-                float2 v;
-                if (j < half) {
-                    v = j < a.MW ? ci[j] : make_float2(0.0f, 0.0f);
-                } else {
-                    const int i = Wp - j;
-                    const float2 u = i < a.MW ? ci[i] : make_float2(0.0f, 0.0f);
-                    v = make_float2(u.x, -u.y);
+        // row pass of Irfft2 (fft.cpp:86-99) for kChunk output channels.  At Wp = 128
+        // (NJ = 4) each warp transforms the rows of its own R output channels in
+        // registers: entry lane + 32 j of the result is the x1 of point lane + 32 j,
+        // the point this lane takes in the local Linear below.
+        float x1v[R][NJ];
+        if constexpr (NJ == 4) {
+#pragma unroll
+            for (int rr = 0; rr < R; ++rr) {
+                const int r = warp * R + rr;
+                if (o0 + r >= C) break;
+                const float2* ci = a.colinv + ((static_cast<int64_t>(b) * C + o0 + r) * Hp + hh) * a.MW;
+                float2 v[4];
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    const int j = fft128_src(lane, m);
+                    if (j < half) {
+                        v[m] = j < a.MW ? ci[j] : make_float2(0.0f, 0.0f);
+                    } else {
+                        const int i = 128 - j;
+                        const float2 u = i < a.MW ? ci[i] : make_float2(0.0f, 0.0f);
+                        v[m] = make_float2(u.x, -u.y);
+                    }
                 }
-                row[bit_reverse(j, lgW)] = v;
+                warp_fft128_regs<true>(v, sX1 + static_cast<size_t>(warp) * 128, a.twi_w, lane);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) x1v[rr][j] = v[j].x;
             }
-            __syncwarp();
-            warp_fft_row<true>(row, Wp, a.twi_w, lane);
+        } else {
+            for (int r = warp; r < kChunk && o0 + r < C; r += 8) {
+                float2* row = sX1 + static_cast<size_t>(r) * Wp;
+                const float2* ci = a.colinv + ((static_cast<int64_t>(b) * C + o0 + r) * Hp + hh) * a.MW;
+                for (int j = lane; j < Wp; j += 32) {
+                    float2 v;
+                    if (j < half) {
+                        v = j < a.MW ? ci[j] : make_float2(0.0f, 0.0f);
+                    } else {
+                        const int i = Wp - j;
+                        const float2 u = i < a.MW ? ci[i] : make_float2(0.0f, 0.0f);
+                        v = make_float2(u.x, -u.y);
+                    }
+                    row[bit_reverse(j, lgW)] = v;
+                }
+                __syncwarp();
+                warp_fft_row<true>(row, Wp, a.twi_w, lane);
+            }
+            __syncthreads();
         }
-        __syncthreads();
         // local Linear of the row's points for this chunk: warp -> R output channels,
         // lane -> points lane + 32 j; one shared-memory load of a point's input feeds
         // all R channels (each channel's sum keeps the k order)
-        constexpr int R = kChunk / 8;
         float acc[R][NJ];
         const float* wrow[R];
 #pragma unroll
@@ -350,7 +397,7 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
                         if (a.obs_vals) a.obs_vals[((static_cast<int64_t>(b) * Hp + hh) * Wp + w) * C + o] = acc[rr][j];
                     }
                     const float x2 = apply_fq(acc[rr][j], a.fq);
-                    const float x1 = __fmul_rn(sX1[static_cast<size_t>(r) * Wp + w].x, invW);
+                    const float x1 = __fmul_rn(NJ == 4 ? x1v[rr][j] : sX1[static_cast<size_t>(r) * Wp + w].x, invW);
                     const float z = __fadd_rn(x1, x2);
                     if (I8 && a.snap.fq.kind == 1) {
                         const float zpo = static_cast<float>(a.snap.fq.zp);
@@ -365,7 +412,9 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
                 }
             }
         }
-        __syncthreads();
+        // the next chunk's row pass rewrites sX1 (at Wp = 128 each warp only its own
+        // scratch row)
+        if constexpr (NJ != 4) __syncthreads();
     }
     if (OBS) ob.flush(a.obs, a.obs_i);
 }
