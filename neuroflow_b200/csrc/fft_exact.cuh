@@ -198,4 +198,43 @@ __device__ __forceinline__ void warp_fft128_regs(float2 (&v)[4], float2* scratch
     fft_butterfly<INV>(v[1], v[3], __ldg(tw + 95 + lane));
 }
 
+// n = 64 in registers, two complex values per lane, in the manner of warp_fft128_regs:
+// in v[m] = a[2 lane + m] of the bit-reversed row (half = 1 within the lane, half = 2 ..
+// 16 by shuffles with lane l ^ (half / 2)), one swizzled pass through `scratch` (64
+// float2), half = 32 on v[j] = a[lane + 32 j].  Out: v[j] = the entry lane + 32 j.
+__device__ __forceinline__ int fft64_pos(int i) { return i ^ ((i >> 4) & 1); }
+
+// entry of the natural-order row that lands at bit-reversed position 2 lane + m
+__device__ __forceinline__ int fft64_src(int lane, int m) {
+    return static_cast<int>(__brev(static_cast<unsigned>(lane)) >> 27) + 32 * m;
+}
+
+template <bool INV>
+__device__ __forceinline__ void warp_fft64_regs(float2 (&v)[2], float2* scratch, const float2* __restrict__ tw,
+                                                int lane) {
+    fft_butterfly<INV>(v[0], v[1], __ldg(tw));
+#pragma unroll
+    for (int s = 1; s <= 8; s <<= 1) {
+        const int half = 2 * s;
+        const bool hi = (lane & s) != 0;
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+            const float2 w = __ldg(tw + (half - 1) + ((2 * lane + m) & (half - 1)));
+            const float2 p = make_float2(__shfl_xor_sync(0xffffffffu, v[m].x, s),
+                                         __shfl_xor_sync(0xffffffffu, v[m].y, s));
+            float2 u = hi ? p : v[m];
+            float2 x = hi ? v[m] : p;
+            fft_butterfly<INV>(u, x, w);
+            v[m] = hi ? x : u;
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < 2; ++m) scratch[fft64_pos(2 * lane + m)] = v[m];
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 2; ++j) v[j] = scratch[fft64_pos(lane + 32 * j)];
+    __syncwarp();
+    fft_butterfly<INV>(v[0], v[1], __ldg(tw + 31 + lane));
+}
+
 }  // namespace nfx

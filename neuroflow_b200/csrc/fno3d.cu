@@ -147,14 +147,29 @@ __global__ void __launch_bounds__(256) fwd3d_a_kernel(Fno3dPlan p, const void* h
     float2* row = sm + warp * p.Dp;
     float2* col = sm + 8 * p.Dp;
     const int64_t base = ((static_cast<int64_t>(b) * p.C + c) * p.Hp + hh) * p.Wp * p.Dp;
-    for (int w = warp; w < p.Wp; w += 8) {
-        for (int d = lane; d < p.Dp; d += 32)
-            row[bit_reverse(d, lgD)] = make_float2(value_at(hin, base + static_cast<int64_t>(w) * p.Dp + d, p.fp8, s_in), 0.0f);
-        __syncwarp();
-        warp_fft_row<false>(row, p.Dp, p.tw[4], lane);
-        const int wr = bit_reverse(w, lgW);
-        for (int kd = lane; kd < p.MD; kd += 32) col[kd * p.Wp + wr] = row[kd];
-        __syncwarp();
+    if (p.Dp == 64) {
+        // D rows in registers (warp_fft64_regs): mode kd is entry lane + 32 j
+        for (int w = warp; w < p.Wp; w += 8) {
+            float2 v[2];
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+                v[m] = make_float2(value_at(hin, base + static_cast<int64_t>(w) * 64 + fft64_src(lane, m), p.fp8, s_in), 0.0f);
+            warp_fft64_regs<false>(v, row, p.tw[4], lane);
+            const int wr = bit_reverse(w, lgW);
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                if (lane + 32 * j < p.MD) col[(lane + 32 * j) * p.Wp + wr] = v[j];
+        }
+    } else {
+        for (int w = warp; w < p.Wp; w += 8) {
+            for (int d = lane; d < p.Dp; d += 32)
+                row[bit_reverse(d, lgD)] = make_float2(value_at(hin, base + static_cast<int64_t>(w) * p.Dp + d, p.fp8, s_in), 0.0f);
+            __syncwarp();
+            warp_fft_row<false>(row, p.Dp, p.tw[4], lane);
+            const int wr = bit_reverse(w, lgW);
+            for (int kd = lane; kd < p.MD; kd += 32) col[kd * p.Wp + wr] = row[kd];
+            __syncwarp();
+        }
     }
     __syncthreads();
     float2* A = p.A + ((static_cast<int64_t>(b) * p.C + c) * p.Hp + hh) * p.MW * p.MD;
@@ -252,6 +267,27 @@ __global__ void __launch_bounds__(256) inv3d_kernel(Fno3dPlan p) {
     const int half = p.Dp / 2 + 1;
     const float invD = __fdiv_rn(1.0f, static_cast<float>(p.Dp));
     float* x1 = p.x1 + ((static_cast<int64_t>(b) * p.C + o) * p.Hp + hh) * p.Wp * p.Dp;
+    if (p.Dp == 64) {
+        // D lines in registers (warp_fft64_regs): point d is entry lane + 32 j
+        for (int w = warp; w < p.Wp; w += 8) {
+            float2 v[2];
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const int j = fft64_src(lane, m);
+                if (j < half) {
+                    v[m] = j < p.MD ? tmp[j * p.Wp + w] : make_float2(0.0f, 0.0f);
+                } else {
+                    const int i = 64 - j;
+                    const float2 u = i < p.MD ? tmp[i * p.Wp + w] : make_float2(0.0f, 0.0f);
+                    v[m] = make_float2(u.x, -u.y);
+                }
+            }
+            warp_fft64_regs<true>(v, line, p.tw[5], lane);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) x1[static_cast<int64_t>(w) * 64 + lane + 32 * j] = __fmul_rn(v[j].x, invD);
+        }
+        return;
+    }
     for (int w = warp; w < p.Wp; w += 8) {
         for (int j = lane; j < p.Dp; j += 32) {
             float2 v;
