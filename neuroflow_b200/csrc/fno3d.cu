@@ -173,6 +173,18 @@ __global__ void __launch_bounds__(256) fwd3d_a_kernel(Fno3dPlan p, const void* h
     }
     __syncthreads();
     float2* A = p.A + ((static_cast<int64_t>(b) * p.C + c) * p.Hp + hh) * p.MW * p.MD;
+    if (p.Wp == 64 && p.Dp >= 64) {  // the warp's row buffer (Dp entries) is the scratch
+        for (int kd = warp; kd < p.MD; kd += 8) {
+            float2 v[2];
+#pragma unroll
+            for (int m = 0; m < 2; ++m) v[m] = col[kd * 64 + 2 * lane + m];  // bit-reversed row
+            warp_fft64_regs<false>(v, row, p.tw[2], lane);
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                if (lane + 32 * j < p.MW) A[(lane + 32 * j) * p.MD + kd] = v[j];
+        }
+        return;
+    }
     for (int kd = warp; kd < p.MD; kd += 8) {
         warp_fft_row<false>(col + kd * p.Wp, p.Wp, p.tw[2], lane);
         for (int kw = lane; kw < p.MW; kw += 32) A[kw * p.MD + kd] = col[kd * p.Wp + kw];
@@ -189,6 +201,18 @@ __global__ void __launch_bounds__(256) fwd3d_b_kernel(Fno3dPlan p) {
     float2* line = sm + warp * p.Hp;
     const float2* A = p.A + (static_cast<int64_t>(b) * p.C + c) * p.Hp * KK;
     float2* X = p.Xs + (static_cast<int64_t>(b) * p.C + c) * p.MH * KK;
+    if (p.Hp == 64) {
+        for (int q = warp; q < KK; q += 8) {
+            float2 v[2];
+#pragma unroll
+            for (int m = 0; m < 2; ++m) v[m] = A[static_cast<int64_t>(fft64_src(lane, m)) * KK + q];
+            warp_fft64_regs<false>(v, line, p.tw[0], lane);
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                if (lane + 32 * j < p.MH) X[(lane + 32 * j) * KK + q] = v[j];
+        }
+        return;
+    }
     for (int q = warp; q < KK; q += 8) {
         for (int h = lane; h < p.Hp; h += 32) line[bit_reverse(h, lgH)] = A[static_cast<int64_t>(h) * KK + q];
         __syncwarp();
@@ -225,6 +249,24 @@ __global__ void __launch_bounds__(256) mix3d_kernel(Fno3dPlan p, const float* __
     const int lgH = 31 - __clz(p.Hp);
     const float invH = __fdiv_rn(1.0f, static_cast<float>(p.Hp));
     float2* line = lines + warp * p.Hp;
+    if (p.Hp == 64) {
+        for (int q = warp; q < G * KK; q += 8) {
+            const int r = q / KK, kk = q - (q / KK) * KK;
+            float2 v[2];
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const int h = fft64_src(lane, m);
+                v[m] = h < p.MH ? sY[r * M + h * KK + kk] : make_float2(0.0f, 0.0f);
+            }
+            warp_fft64_regs<true>(v, line, p.tw[1], lane);
+            float2* dst = p.colinv + (static_cast<int64_t>(b) * C + o0 + r) * p.Hp * KK + kk;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                dst[static_cast<int64_t>(lane + 32 * j) * KK] =
+                    make_float2(__fmul_rn(v[j].x, invH), __fmul_rn(v[j].y, invH));
+        }
+        return;
+    }
     for (int q = warp; q < G * KK; q += 8) {
         const int r = q / KK, kk = q - (q / KK) * KK;
         for (int h = lane; h < p.Hp; h += 32)
@@ -252,16 +294,31 @@ __global__ void __launch_bounds__(256) inv3d_kernel(Fno3dPlan p) {
     float2* line = sm + p.MD * p.Wp + warp * LN;
     const float2* ci = p.colinv + ((static_cast<int64_t>(b) * p.C + o) * p.Hp + hh) * KK;
     const float invW = __fdiv_rn(1.0f, static_cast<float>(p.Wp));
-    for (int kd = warp; kd < p.MD; kd += 8) {
-        for (int w = lane; w < p.Wp; w += 32)
-            line[bit_reverse(w, lgW)] = w < p.MW ? ci[w * p.MD + kd] : make_float2(0.0f, 0.0f);
-        __syncwarp();
-        warp_fft_row<true>(line, p.Wp, p.tw[3], lane);
-        for (int w = lane; w < p.Wp; w += 32) {
-            const float2 v = line[w];
-            tmp[kd * p.Wp + w] = make_float2(__fmul_rn(v.x, invW), __fmul_rn(v.y, invW));
+    if (p.Wp == 64) {
+        for (int kd = warp; kd < p.MD; kd += 8) {
+            float2 v[2];
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const int w = fft64_src(lane, m);
+                v[m] = w < p.MW ? ci[w * p.MD + kd] : make_float2(0.0f, 0.0f);
+            }
+            warp_fft64_regs<true>(v, line, p.tw[3], lane);
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                tmp[kd * 64 + lane + 32 * j] = make_float2(__fmul_rn(v[j].x, invW), __fmul_rn(v[j].y, invW));
         }
-        __syncwarp();
+    } else {
+        for (int kd = warp; kd < p.MD; kd += 8) {
+            for (int w = lane; w < p.Wp; w += 32)
+                line[bit_reverse(w, lgW)] = w < p.MW ? ci[w * p.MD + kd] : make_float2(0.0f, 0.0f);
+            __syncwarp();
+            warp_fft_row<true>(line, p.Wp, p.tw[3], lane);
+            for (int w = lane; w < p.Wp; w += 32) {
+                const float2 v = line[w];
+                tmp[kd * p.Wp + w] = make_float2(__fmul_rn(v.x, invW), __fmul_rn(v.y, invW));
+            }
+            __syncwarp();
+        }
     }
     __syncthreads();
     const int half = p.Dp / 2 + 1;

@@ -69,12 +69,15 @@ def test_fno3d_relu_bit_exact(tmp_path, kw, fp8):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("width,fp8", [(8, False), (8, True), (32, False)])
-def test_fno3d_relu_bit_exact_d64(tmp_path, width, fp8):
-    """D = 64 lines, where the forward and inverse D passes transform each line in
-    registers, on a non-cubic grid with ReLU: bit-identical to the oracle."""
+@pytest.mark.parametrize("width,fp8,shape", [(8, False, (2, 8, 16, 64)), (8, True, (2, 8, 16, 64)),
+                                              (32, False, (2, 8, 16, 64)), (8, False, (1, 64, 64, 16)),
+                                              (8, False, (1, 16, 64, 64))])
+def test_fno3d_relu_bit_exact_d64(tmp_path, width, fp8, shape):
+    """64-point lines, which the forward and inverse passes transform in registers (D,
+    W and H axes; the W pass only where D >= 64), on non-cubic grids with ReLU:
+    bit-identical to the oracle."""
     m, p = _model(tmp_path, "relu", width=width, modes=(3, 4, 6), L=2, S=16)
-    x = np.random.default_rng(7).standard_normal((2, 8, 16, 64, 4)).astype(np.float32)
+    x = np.random.default_rng(7).standard_normal(shape + (4,)).astype(np.float32)
     want = Oracle().fno3d_forward(m, x, fp8=fp8)
     got = _run(p, x, 1, fp8)
     assert np.array_equal(_bits(got), _bits(want)), float(np.abs(got - want).max())
