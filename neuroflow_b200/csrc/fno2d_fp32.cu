@@ -151,6 +151,18 @@ __global__ void __launch_bounds__(256) fwd2d_kernel(const float* __restrict__ hi
         }
     }
     __syncthreads();
+    if (Hp == 128 && Wp >= 128) {  // the warp's row buffer (Wp entries) is the scratch
+        for (int kw = warp; kw < MW; kw += 8) {
+            float2 v[4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) v[m] = col[kw * 128 + 4 * lane + m];  // bit-reversed column
+            warp_fft128_regs<false>(v, row, twf_h, lane);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (lane + 32 * j < MH) Xs[((static_cast<int64_t>(b) * C + c) * MH + lane + 32 * j) * MW + kw] = v[j];
+        }
+        return;
+    }
     for (int kw = warp; kw < MW; kw += 8) {
         warp_fft_row_first<false>(col + kw * Hp, Hp, twf_h, lane, MH);
         for (int kh = lane; kh < MH; kh += 32)
@@ -190,6 +202,24 @@ __global__ void __launch_bounds__(256) mix2d_kernel(const float2* __restrict__ X
     const int lgH = 31 - __clz(Hp);
     const float invH = __fdiv_rn(1.0f, static_cast<float>(Hp));
     float2* cb = colb + warp * Hp;
+    if (Hp == 128) {
+        for (int q = warp; q < G * MW; q += 8) {
+            const int r = q / MW, kw = q - (q / MW) * MW;
+            float2 v[4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int i = fft128_src(lane, m);
+                v[m] = i < MH ? sY[r * M + i * MW + kw] : make_float2(0.0f, 0.0f);
+            }
+            warp_fft128_regs<true>(v, cb, twi_h, lane);
+            float2* dst = colinv + ((static_cast<int64_t>(b) * C + o0 + r) * Hp) * MW + kw;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                dst[static_cast<int64_t>(lane + 32 * j) * MW] =
+                    make_float2(__fmul_rn(v[j].x, invH), __fmul_rn(v[j].y, invH));
+        }
+        return;
+    }
     for (int q = warp; q < G * MW; q += 8) {
         const int r = q / MW, kw = q - (q / MW) * MW;
         for (int i = lane; i < Hp; i += 32)

@@ -45,7 +45,7 @@ def _model(tmp_path, act, quant, in_ch=5, width=20, mh=5, mw=4, L=3, H=16, W=32,
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("quant", [True, False])
-@pytest.mark.parametrize("geom", [(16, 32, 1), (32, 16, 1), (16, 8, 32)])
+@pytest.mark.parametrize("geom", [(16, 32, 1), (32, 16, 1), (16, 8, 32), (128, 128, 1), (128, 64, 1)])
 def test_fno2d_fp32_relu_bit_exact(tmp_path, quant, geom):
     H, W, pad = geom
     m, p = _model(tmp_path, "relu", quant, H=H, W=W, pad=pad)
