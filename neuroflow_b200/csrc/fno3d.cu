@@ -899,25 +899,35 @@ __global__ void __launch_bounds__(128) local3d_kernel(Fno3dPlan p, Fno3dLayer L,
         } else {
 #pragma unroll
             for (int o = 0; o < C; ++o) acc[o] = sB[o];
-            for (int k = 0; k < C; ++k) {
-                const float a = static_cast<const float*>(hin)[base + k * P];
-                const bool fused = k >= nu;
+            // the inputs of eight channels loaded before their products (the loads of
+            // a group are in flight together)
+            constexpr int KB = C % 8 == 0 ? 8 : 1;
+            for (int k0 = 0; k0 < C; k0 += KB) {
+                float av[KB];
 #pragma unroll
-                for (int o4 = 0; o4 < C / 4; ++o4) {
-                    const float4 w = sW4[k * (C / 4) + o4];
-                    if (nu >= C) {
-                        // every product unfused: two per f32x2 instruction
-                        const float2 m0 = mul2_rn(make_float2(a, a), make_float2(w.x, w.y));
-                        const float2 m1 = mul2_rn(make_float2(a, a), make_float2(w.z, w.w));
-                        acc[4 * o4 + 0] = __fadd_rn(acc[4 * o4 + 0], m0.x);
-                        acc[4 * o4 + 1] = __fadd_rn(acc[4 * o4 + 1], m0.y);
-                        acc[4 * o4 + 2] = __fadd_rn(acc[4 * o4 + 2], m1.x);
-                        acc[4 * o4 + 3] = __fadd_rn(acc[4 * o4 + 3], m1.y);
-                    } else {
-                        acc[4 * o4 + 0] = linear_step(acc[4 * o4 + 0], a, w.x, fused);
-                        acc[4 * o4 + 1] = linear_step(acc[4 * o4 + 1], a, w.y, fused);
-                        acc[4 * o4 + 2] = linear_step(acc[4 * o4 + 2], a, w.z, fused);
-                        acc[4 * o4 + 3] = linear_step(acc[4 * o4 + 3], a, w.w, fused);
+                for (int kk = 0; kk < KB; ++kk) av[kk] = static_cast<const float*>(hin)[base + (k0 + kk) * P];
+#pragma unroll
+                for (int kk = 0; kk < KB; ++kk) {
+                    const int k = k0 + kk;
+                    const float a = av[kk];
+                    const bool fused = k >= nu;
+#pragma unroll
+                    for (int o4 = 0; o4 < C / 4; ++o4) {
+                        const float4 w = sW4[k * (C / 4) + o4];
+                        if (nu >= C) {
+                            // every product unfused: two per f32x2 instruction
+                            const float2 m0 = mul2_rn(make_float2(a, a), make_float2(w.x, w.y));
+                            const float2 m1 = mul2_rn(make_float2(a, a), make_float2(w.z, w.w));
+                            acc[4 * o4 + 0] = __fadd_rn(acc[4 * o4 + 0], m0.x);
+                            acc[4 * o4 + 1] = __fadd_rn(acc[4 * o4 + 1], m0.y);
+                            acc[4 * o4 + 2] = __fadd_rn(acc[4 * o4 + 2], m1.x);
+                            acc[4 * o4 + 3] = __fadd_rn(acc[4 * o4 + 3], m1.y);
+                        } else {
+                            acc[4 * o4 + 0] = linear_step(acc[4 * o4 + 0], a, w.x, fused);
+                            acc[4 * o4 + 1] = linear_step(acc[4 * o4 + 1], a, w.y, fused);
+                            acc[4 * o4 + 2] = linear_step(acc[4 * o4 + 2], a, w.z, fused);
+                            acc[4 * o4 + 3] = linear_step(acc[4 * o4 + 3], a, w.w, fused);
+                        }
                     }
                 }
             }
