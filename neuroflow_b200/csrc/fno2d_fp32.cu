@@ -271,11 +271,25 @@ __global__ void __launch_bounds__(256) layer2d_kernel(Layer2dArgs a) {
     const int half = Wp / 2 + 1;
     const bool i8 = I8 && a.i8.wz != nullptr;
     const float zp_in = static_cast<float>(a.i8.zp_in);
-    for (int t = threadIdx.x; t < C * Wp; t += blockDim.x) {
-        const int k = t / Wp, w = t - (t / Wp) * Wp;
-        const float v = a.hin[((static_cast<int64_t>(b) * C + k) * Hp + hh) * Wp + w];
-        // INT8: QuantiseActivation's code (int8_gemm.cpp:507-520) of the snapped input
-        sH[t] = i8 ? fq_code(v, a.i8.s_in, zp_in) : v;
+    if (Wp % 4 == 0) {
+        // 16-byte loads, four in flight per thread
+#pragma unroll 4
+        for (int t4 = threadIdx.x; t4 < C * Wp / 4; t4 += blockDim.x) {
+            const int t = 4 * t4;
+            const int k = t / Wp, w = t - (t / Wp) * Wp;
+            const float4 v = *reinterpret_cast<const float4*>(a.hin + ((static_cast<int64_t>(b) * C + k) * Hp + hh) * Wp + w);
+            // INT8: QuantiseActivation's code (int8_gemm.cpp:507-520) of the snapped input
+            *reinterpret_cast<float4*>(sH + t) =
+                i8 ? make_float4(fq_code(v.x, a.i8.s_in, zp_in), fq_code(v.y, a.i8.s_in, zp_in),
+                                 fq_code(v.z, a.i8.s_in, zp_in), fq_code(v.w, a.i8.s_in, zp_in))
+                   : v;
+        }
+    } else {
+        for (int t = threadIdx.x; t < C * Wp; t += blockDim.x) {
+            const int k = t / Wp, w = t - (t / Wp) * Wp;
+            const float v = a.hin[((static_cast<int64_t>(b) * C + k) * Hp + hh) * Wp + w];
+            sH[t] = i8 ? fq_code(v, a.i8.s_in, zp_in) : v;
+        }
     }
     if (i8) {
         // sum_a of each point (exact: |sum| <= 128 C)
