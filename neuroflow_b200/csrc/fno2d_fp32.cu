@@ -85,14 +85,24 @@ __global__ void __launch_bounds__(256) lift2d_f32_kernel(Fno2dF32Plan p) {
     const int64_t total = static_cast<int64_t>(p.B) * p.C * p.Hp * p.Wp;
     const int nu = linear_unfused_len(p.in_ch);
     Obs ob;
+    // Hp and Wp are powers of two (radix-2 transforms): the point's coordinates by
+    // shifts and masks, and one 32-bit division by C
+    const int lgW = 31 - __clz(p.Wp), lgH = 31 - __clz(p.Hp);
     for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
          t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int ww = static_cast<int>(t % p.Wp);
-        int64_t r = t / p.Wp;
-        const int hh = static_cast<int>(r % p.Hp);
-        r /= p.Hp;
-        const int c = static_cast<int>(r % p.C);
-        const int64_t b = r / p.C;
+        const int ww = static_cast<int>(t & (p.Wp - 1));
+        const int hh = static_cast<int>((t >> lgW) & (p.Hp - 1));
+        const int64_t bc = t >> (lgW + lgH);
+        int c;
+        int64_t b;
+        if (bc <= 0x7fffffff) {
+            const unsigned q = static_cast<unsigned>(bc) / static_cast<unsigned>(p.C);
+            b = q;
+            c = static_cast<int>(static_cast<unsigned>(bc) - q * static_cast<unsigned>(p.C));
+        } else {
+            b = bc / p.C;
+            c = static_cast<int>(bc - b * p.C);
+        }
         float v = 0.0f;
         if (hh < p.H && ww < p.W) {
             const float* xr = p.x + ((b * p.H + hh) * p.W + ww) * p.in_ch;
